@@ -1,0 +1,383 @@
+#!/usr/bin/env python
+"""Benchmark of the DeepSeek-V3/R1 MoE block on B200 (libmoe_cuda.so).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
+
+One JSON line on rank 0.  A "step" is one decode step of one MoE layer over
+one batch of synthetic tokens.  Workloads:
+  decode_b64_zipf  (default) config 3: 64 tokens, router skewed by a Zipf(1.1)
+                   per-expert bias, 256 experts sharded over N GPUs
+  decode_b1        config 2: one token on one GPU
+Weights are random-init N(0, 0.02) quantized to Q4_K gate/up and Q6_K down on
+the device; inputs N(0, 1) from a fixed seed.  Between timed steps a 256 MiB
+buffer is written to flush the 126 MB L2.
+
+--impl reference times the reference's own CPU path (quant.c dequant + fp32
+dots + route(), built in place under oracle/_ref) on this host's cores, on a
+bounded sample of tokens of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import glob
+import json
+import os
+import re
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "MoE decode tokens/s at 1/2/4/8 B200; expert matvec HBM GB/s vs 8 TB/s peak"
+H, I, E, K = 7168, 2048, 256, 8
+Q4_ROW = H // 256 * 144
+GATE_BYTES = I * Q4_ROW                      # 8,257,536
+DOWN_Q6_BYTES = H * (I // 256) * 210         # 12,042,240
+EXPERT_BYTES = 2 * GATE_BYTES + DOWN_Q6_BYTES
+ROUTER_BYTES = E * H * 4 + E * 4
+WORKLOADS = {
+    "decode_b64_zipf": dict(B=64, zipf=True, name="config3_decode_b64_zipf"),
+    "decode_b1": dict(B=1, zipf=False, name="config2_decode_b1"),
+}
+
+
+def zipf_bias(n=256, s=1.1, seed=0):
+    """Zipf(s) expert-load skew: a seeded rank permutation pi and
+    bias_e = log(n * p_pi(e)), p_r proportional to r^-s."""
+    rng = np.random.default_rng(seed)
+    p = np.arange(1, n + 1, dtype=np.float64) ** -s
+    p /= p.sum()
+    return np.log(n * p[rng.permutation(n)]).astype(np.float32)
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def traffic_from_profiles(kernel: str, workload: str):
+    """Per-launch DRAM bytes from a committed ncu summary, if there is one."""
+    for p in sorted(glob.glob(os.path.join(ROOT, "profiles", f"{kernel}__{workload}*.txt"))):
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(p).read())
+        if m:
+            return float(m.group(1))
+    return None
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed
+    region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu, self.proc, self.lines = gpu, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------- CPU path
+def cpu_reference(workload: str, steps: int, warmup: int, seconds: float = 20.0):
+    """The reference's CPU expert path (oracle/_ref: quant.c + route() of the
+    reference, plain-C dots in place of Accelerate) on sampled tokens."""
+    import ctypes as C
+    from oracle import oracle as O
+    W = WORKLOADS[workload]
+    threads = len(os.sched_getaffinity(0))
+    if not O.ref_available():
+        O.build()
+    R = O.ref()
+    router = O.normal(0, O.stream(0, 0, O.KIND_ROUTER), E * H, 0.006, threads=threads).reshape(E, H)
+    bias = O.normal(0, O.stream(0, 0, O.KIND_BIAS), E, 0.01, threads=threads)
+    if W["zipf"]:
+        bias = (bias + zipf_bias()).astype(np.float32)
+    rng = np.random.default_rng(1234)
+    n_tok = max(1, steps + warmup)
+    xs = rng.standard_normal((n_tok, H)).astype(np.float32)
+    need = set()
+    for t in range(n_tok):
+        lg = (router.astype(np.float64) @ xs[t].astype(np.float64)).astype(np.float32)
+        idx, _ = O.ref_route(lg, bias, K=8)
+        need |= set(idx.tolist())
+    blobs = {e: O.gen_expert(0, 0, e, H, I, O.TYPE_Q6_K, threads=threads) for e in sorted(need)}
+    blobs[E] = O.gen_expert(0, 0, E, H, I, O.TYPE_Q6_K, threads=threads)
+    dummy = np.zeros(EXPERT_BYTES, np.uint8)
+    table = (C.c_void_p * (E + 1))()
+    for e in range(E + 1):
+        table[e] = (blobs.get(e, dummy)).ctypes.data
+    out = np.empty(H, np.float32)
+    times = []
+    for t in range(n_tok):
+        t0 = time.perf_counter()
+        rc = R.ref_moe_token_cpu(table, 1, router, bias, xs[t], 8, out, None, None, threads)
+        dt = time.perf_counter() - t0
+        if rc != 0:
+            raise RuntimeError(f"ref_moe_token_cpu failed ({rc})")
+        if t >= warmup:
+            times.append(dt)
+        if sum(times) > seconds and len(times) >= 2:
+            break
+    tok_s = len(times) / sum(times)
+    return dict(value=tok_s, unit="tokens/s", cores=threads, kind="reference",
+                sample=f"{len(times)} tokens of {W['name']}, one at a time as infer.m decodes "
+                       f"(quant.c dequant of 8 routed + 1 shared expert, fp32 dots, route())")
+
+
+# ----------------------------------------------------------------- GPU path
+def run_ours(args):
+    import torch
+    import flash_deepseek_b200 as F
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
+        pg = dist
+    W = WORKLOADS[args.workload]
+    B = W["B"]
+    if world > 1 and B % world:
+        raise SystemExit("global batch must divide over the GPUs")
+    b_loc = max(1, B // world)
+    uid = None
+    if world > 1:
+        obj = [F.get_unique_id() if rank == 0 else None]
+        pg.broadcast_object_list(obj, src=0)
+        uid = obj[0]
+    cfg = F.MoeConfig(n_layers=1, max_tokens=b_loc)
+    moe = F.MoE(cfg, device=local, rank=rank, world_size=world, unique_id=uid)
+    moe.init_layer_synthetic(0, seed=0, down_type=F.TYPE_Q6_K)
+    if W["zipf"]:
+        moe.add_router_bias(0, zipf_bias())
+
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.ExternalStream(moe.stream, device=dev)
+    n_pool = 4
+    g = torch.Generator(device="cpu").manual_seed(1234)
+    pool_h = [torch.randn(B, H, generator=g, dtype=torch.float32) for _ in range(n_pool)]
+    pool = [p[rank * b_loc:(rank + 1) * b_loc].contiguous().to(dev) for p in pool_h]
+    out = torch.empty(b_loc, H, device=dev)
+    steps_total = args.warmup + args.steps
+    idx_all = torch.empty(steps_total, b_loc, K, dtype=torch.int32, device=dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    moe.set_timing(True)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if not pg:
+            return v
+        t = torch.tensor([v], dtype=torch.float64)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t[0])
+
+    # ---- device-resident leg (value)
+    for s in range(args.warmup):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+        moe.forward_device(0, pool[s % n_pool], b_loc, out, d_idx=idx_all[s])
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    phases = []
+    barrier()
+    launches0 = moe.kernel_launches
+    with Clocks(local) as clk:
+        for s in range(args.steps):
+            with torch.cuda.stream(stream):
+                flush.zero_()
+            ev[s][0].record(stream)
+            moe.forward_device(0, pool[(args.warmup + s) % n_pool], b_loc, out, d_idx=idx_all[args.warmup + s])
+            ev[s][1].record(stream)
+            phases.append(moe.timing())
+        barrier()
+    launches = moe.kernel_launches - launches0
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    total_ms = max_over_ranks(sum(step_ms))
+    value = B * args.steps / (total_ms / 1e3)
+
+    # ---- roofline of the dominant kernel (gate/up GEMV) on this rank
+    idx_h = idx_all[args.warmup:].cpu().numpy()
+    e_lo, e_hi = rank * (E // world), (rank + 1) * (E // world)
+    gu_bytes, dn_bytes, active = [], [], []
+    for s in range(args.steps):
+        # experts this rank computes: routed experts it owns hit by any token
+        # of the global batch (idx of the local slice is what we see here;
+        # with world > 1 the owner side is summed in run_ep)
+        hit = set(int(e) for e in np.unique(idx_h[s]) if e_lo <= e < e_hi)
+        n_act = len(hit) + 1
+        active.append(n_act)
+        gu_bytes.append(n_act * 2 * GATE_BYTES + b_loc * H * 4 + (b_loc * K + b_loc) * I * 4)
+        dn_bytes.append(n_act * DOWN_Q6_BYTES + (b_loc * K + b_loc) * (I * 4 + H * 4))
+    gu_ms = float(np.mean([p["gateup"] for p in phases]))
+    dn_ms = float(np.mean([p["down"] for p in phases]))
+    peak, peak_kind = peaks()
+    ach = float(np.mean(gu_bytes)) / (gu_ms / 1e3) / 1e9
+    ach_dn = float(np.mean(dn_bytes)) / (dn_ms / 1e3) / 1e9
+    step_bytes = float(np.mean([a * EXPERT_BYTES for a in active])) + ROUTER_BYTES
+    traffic = traffic_from_profiles("k_gateup", args.workload)
+
+    # ---- end-to-end leg through the C ABI with host buffers
+    h_pin = [p[rank * b_loc:(rank + 1) * b_loc].contiguous().pin_memory() for p in pool_h]
+    o_pin = torch.empty(b_loc, H, dtype=torch.float32).pin_memory()
+    h_np = [p.numpy() for p in h_pin]
+    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    idx_np = np.empty((b_loc, K), np.int32)
+    w_np = np.empty((b_loc, K), np.float32)
+    lib = moe.lib
+    o_np = o_pin.numpy()
+    for s in range(args.warmup):
+        lib.moe_forward(moe.ctx, 0, h_np[s % n_pool].ctypes.data, b_loc, o_np.ctypes.data, idx_np.ctypes.data,
+                        w_np.ctypes.data)
+    barrier()
+    for s in range(args.steps):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+        ev2[s][0].record(stream)
+        rc = lib.moe_forward(moe.ctx, 0, h_np[(args.warmup + s) % n_pool].ctypes.data, b_loc, o_np.ctypes.data,
+                             idx_np.ctypes.data, w_np.ctypes.data)
+        ev2[s][1].record(stream)
+        if rc != 0:
+            raise RuntimeError(moe.lib.moe_last_error(moe.ctx))
+    barrier()
+    e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in ev2))
+    e2e = B * args.steps / (e2e_ms / 1e3)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_reference(args.workload, steps=4, warmup=1, seconds=15.0)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "fp32 (Q4_K/Q6_K weights decoded exactly to fp16 integers, fp32 accumulation)",
+            "data": "synthetic: random-init N(0,0.02) weights quantized on device, N(0,1) tokens",
+            "config": {"workload": W["name"], "global_batch": B, "tokens_per_gpu": b_loc, "hidden": H,
+                       "intermediate": I, "experts": E, "top_k": K, "gate_up": "Q4_K", "down": "Q6_K",
+                       "router_skew": "zipf(1.1) bias" if W["zipf"] else "none",
+                       "parallelism": f"ep{world}", "l2": "flushed: 256 MiB write between timed steps"},
+            "roofline": {"bound": "hbm", "kernel": "k_gateup (grouped Q4_K gate/up GEMV + SwiGLU)",
+                         "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(ach / peak, 4), "peak_source": peak_kind,
+                         "frac_of_8TBs": round(ach / 8000.0, 4),
+                         "traffic": traffic,
+                         "algorithmic_bytes_per_launch": round(float(np.mean(gu_bytes))),
+                         "launch_ms": round(gu_ms, 5)},
+            "roofline_down": {"kernel": "k_down (grouped Q6_K down GEMV)", "achieved": round(ach_dn, 1),
+                              "frac": round(ach_dn / peak, 4), "launch_ms": round(dn_ms, 5)},
+            "step_hbm": {"weight_bytes_per_step": round(step_bytes),
+                         "achieved_gbs": round(step_bytes / (total_ms / args.steps / 1e3) / 1e9, 1),
+                         "active_experts_per_step": round(float(np.mean(active)), 2)},
+            "phase_ms": {k: round(float(np.mean([p[k] for p in phases])), 5) for k in phases[0]},
+            "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": B * H * 4,
+                    "d2h_bytes_per_step": B * H * 4 + B * K * 8},
+            "gpu_launches": int(launches),
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    moe.close()
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    W = WORKLOADS[args.workload]
+    cpu = cpu_reference(args.workload, steps=args.steps, warmup=args.warmup, seconds=60.0)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(cpu["value"], 4), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 / cpu["value"], 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "fp32", "data": "synthetic (same generator and seed as the GPU arm)",
+        "config": {"workload": W["name"], "global_batch": W["B"], "hidden": H, "intermediate": I, "experts": E,
+                   "top_k": K, "gate_up": "Q4_K", "down": "Q6_K"},
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(cpu["value"], 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="decode_b64_zipf", choices=sorted(WORKLOADS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

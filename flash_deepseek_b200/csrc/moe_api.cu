@@ -1,0 +1,690 @@
+// moe_api.cu -- context, weight residency and the C ABI of libmoe_cuda.so
+// (include/moe_cuda.h).  One context per GPU; expert-parallel contexts talk
+// over NCCL (dispatch / combine) with fixed-capacity buffers so that a forward
+// step needs no host synchronisation.
+#include <nccl.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/moe_cuda.h"
+#include "moe_common.cuh"
+#include "moe_internal.h"
+
+struct moe_ctx {
+    moe_config cfg;
+    MoeDims d;
+    int device = 0, rank = 0, world = 1;
+    cudaStream_t stream = nullptr;
+    ncclComm_t comm = nullptr;
+    int e0 = 0, n_local = 0;
+    int max_tok = 0;   // tokens of one call on this rank
+    int max_rows = 0;  // activation rows the expert kernels may see (world * max_tok)
+    int max_pairs = 0;
+    int n_split = 0;
+    std::vector<MoeLayerDev> layers;
+    std::vector<size_t> layer_down_bytes;
+    // workspace
+    float *part = nullptr, *d_in = nullptr, *d_out = nullptr, *h_post = nullptr;
+    int *idx = nullptr, *idx_given = nullptr;
+    float *wts = nullptr, *w_given = nullptr, *bias_tmp = nullptr;
+    __half *xop = nullptr;
+    float *x_inv = nullptr;
+    MoePlan plan{};
+    int *counter = nullptr;
+    float *act = nullptr, *dcf = nullptr, *d_inv = nullptr, *eo = nullptr;
+    __half *dop = nullptr;
+    size_t dop_stride = 0;
+    int *h_counts = nullptr;  // pinned [4]
+    // expert-parallel buffers
+    float *send_x = nullptr, *recv_x = nullptr, *send_y = nullptr, *recv_y = nullptr;
+    int *send_meta = nullptr, *recv_meta = nullptr;
+    float *rows_partial = nullptr;
+    std::string err;
+    bool timing = false;
+    cudaEvent_t ev[MOE_N_PHASES + 1] = {};
+    bool ev_valid[MOE_N_PHASES + 1] = {};
+    uint64_t launches = 0;
+    uint64_t last_bytes = 0;
+    int last_layer = -1;
+};
+
+static thread_local std::string g_create_err;
+
+static int fail(moe_ctx *c, int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    if (c) c->err = buf;
+    fprintf(stderr, "[moe_cuda] ERROR: %s\n", buf);
+    return code;
+}
+
+#define CK(call)                                                                                     \
+    do {                                                                                             \
+        cudaError_t e_ = (call);                                                                     \
+        if (e_ != cudaSuccess) return fail(c, MOE_ERR_CUDA, "%s: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                                           __FILE__, __LINE__);                                     \
+    } while (0)
+#define NK(call)                                                                                     \
+    do {                                                                                             \
+        ncclResult_t r_ = (call);                                                                    \
+        if (r_ != ncclSuccess) return fail(c, MOE_ERR_NCCL, "%s: %s", #call, ncclGetErrorString(r_)); \
+    } while (0)
+
+template <typename T>
+static cudaError_t dmalloc(T **p, size_t n) {
+    return cudaMalloc((void **)p, n * sizeof(T) + 256);
+}
+
+static size_t row_bytes(int type, int cols) {
+    return (size_t)(cols / MOE_QK) * (type == MOE_TYPE_Q6_K ? MOE_Q6K_BYTES : MOE_Q4K_BYTES);
+}
+
+extern "C" {
+
+int moe_get_unique_id(void *out) {
+    ncclUniqueId id;
+    if (ncclGetUniqueId(&id) != ncclSuccess) return MOE_ERR_NCCL;
+    memcpy(out, &id, sizeof(id));
+    return MOE_OK;
+}
+
+static int ctx_alloc(moe_ctx *c) {
+    const int T = c->max_tok, R = c->max_rows, H = c->d.H, I = c->d.I, E = c->d.E, K = c->d.K;
+    c->max_pairs = R * K + T;
+    c->n_split = H / MOE_QK;
+    CK(dmalloc(&c->part, (size_t)c->n_split * T * E));
+    CK(dmalloc(&c->d_in, (size_t)T * H));
+    CK(dmalloc(&c->d_out, (size_t)T * H));
+    CK(dmalloc(&c->h_post, (size_t)T * H));
+    CK(dmalloc(&c->idx, (size_t)R * K));
+    CK(dmalloc(&c->wts, (size_t)R * K));
+    CK(dmalloc(&c->idx_given, (size_t)R * K));
+    CK(dmalloc(&c->w_given, (size_t)R * K));
+    CK(dmalloc(&c->bias_tmp, (size_t)E));
+    CK(dmalloc(&c->xop, (size_t)R * q4op_halves(H)));
+    CK(dmalloc(&c->x_inv, (size_t)R));
+    const int P = c->max_pairs;
+    CK(dmalloc(&c->plan.counts, 4));
+    CK(dmalloc(&c->plan.pair_expert, P));
+    CK(dmalloc(&c->plan.pair_token, P));
+    CK(dmalloc(&c->plan.pair_w, P));
+    CK(dmalloc(&c->plan.chunk_expert, P));
+    CK(dmalloc(&c->plan.chunk_pair0, P));
+    CK(dmalloc(&c->plan.chunk_ntok, P));
+    CK(dmalloc(&c->plan.slot_pair, (size_t)R * (K + 1)));
+    CK(dmalloc(&c->plan.error, 1));
+    CK(cudaMemset(c->plan.error, 0, sizeof(int)));
+    CK(cudaMemset(c->plan.counts, 0, 4 * sizeof(int)));
+    CK(dmalloc(&c->counter, 1));
+    CK(cudaMemset(c->counter, 0, sizeof(int)));
+    CK(dmalloc(&c->act, (size_t)P * I));
+    c->dop_stride = q4op_halves(I) > q6op_halves(I) ? q4op_halves(I) : q6op_halves(I);
+    CK(dmalloc(&c->dop, (size_t)P * c->dop_stride));
+    CK(dmalloc(&c->dcf, (size_t)P * (I / MOE_QK) * 16));
+    CK(dmalloc(&c->d_inv, (size_t)P));
+    CK(dmalloc(&c->eo, (size_t)P * H));
+    CK(cudaMallocHost((void **)&c->h_counts, 4 * sizeof(int)));
+    if (c->world > 1) {
+        const size_t rows = (size_t)c->world * T;
+        CK(dmalloc(&c->send_x, rows * H));
+        CK(dmalloc(&c->recv_x, rows * H));
+        CK(dmalloc(&c->send_y, rows * H));
+        CK(dmalloc(&c->recv_y, rows * H));
+        CK(dmalloc(&c->send_meta, rows * (2 * K + 2)));
+        CK(dmalloc(&c->recv_meta, rows * (2 * K + 2)));
+        CK(dmalloc(&c->rows_partial, rows * H));
+    }
+    return MOE_OK;
+}
+
+moe_ctx *moe_create(const moe_config *cfg, int device, int rank, int world_size, const void *uid) {
+    if (!cfg) return nullptr;
+    moe_ctx *c = new moe_ctx();
+    c->cfg = *cfg;
+    c->d = MoeDims{cfg->hidden, cfg->intermediate, cfg->n_experts, cfg->n_group, cfg->topk_group, cfg->top_k,
+                   cfg->routed_scale};
+    c->device = device;
+    c->rank = rank;
+    c->world = world_size;
+    const moe_config &k = *cfg;
+    const char *bad = nullptr;
+    if (k.hidden <= 0 || k.hidden % 256) bad = "hidden must be a positive multiple of 256";
+    else if (k.intermediate <= 0 || k.intermediate % 256) bad = "intermediate must be a positive multiple of 256";
+    else if (k.n_experts <= 0 || k.n_experts > 1024) bad = "n_experts must be in 1..1024";
+    else if (k.n_group <= 0 || k.n_group > 64 || k.n_experts % k.n_group) bad = "n_group must divide n_experts (<= 64)";
+    else if (k.topk_group <= 0 || k.topk_group > k.n_group) bad = "topk_group must be in 1..n_group";
+    else if (k.top_k <= 0 || k.top_k > MOE_MAX_K) bad = "top_k must be in 1..16";
+    else if (k.top_k > k.topk_group * (k.n_experts / k.n_group)) bad = "top_k exceeds the experts of the selected groups";
+    else if (k.n_layers <= 0) bad = "n_layers must be positive";
+    else if (k.max_tokens <= 0 || k.max_tokens > 64) bad = "max_tokens must be in 1..64";
+    else if (world_size <= 0 || rank < 0 || rank >= world_size) bad = "bad rank / world_size";
+    else if (k.n_experts % world_size) bad = "world_size must divide n_experts";
+    else if (world_size > 1 && (size_t)world_size * k.max_tokens > 1024) bad = "world_size * max_tokens exceeds 1024";
+    if (bad) {
+        fprintf(stderr, "[moe_cuda] ERROR: moe_create: %s\n", bad);
+        delete c;
+        return nullptr;
+    }
+    if (cudaSetDevice(device) != cudaSuccess) {
+        fprintf(stderr, "[moe_cuda] ERROR: moe_create: cudaSetDevice(%d) failed\n", device);
+        delete c;
+        return nullptr;
+    }
+    c->n_local = k.n_experts / world_size;
+    c->e0 = rank * c->n_local;
+    c->max_tok = k.max_tokens;
+    c->max_rows = world_size * k.max_tokens;
+    c->layers.assign(k.n_layers, MoeLayerDev{});
+    c->layer_down_bytes.assign(k.n_layers, 0);
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess || ctx_alloc(c) != MOE_OK) {
+        fprintf(stderr, "[moe_cuda] ERROR: moe_create: allocation failed: %s\n", c->err.c_str());
+        moe_destroy(c);
+        return nullptr;
+    }
+    if (world_size > 1) {
+        if (!uid) {
+            fprintf(stderr, "[moe_cuda] ERROR: moe_create: world_size > 1 needs a unique id\n");
+            moe_destroy(c);
+            return nullptr;
+        }
+        ncclUniqueId id;
+        memcpy(&id, uid, sizeof(id));
+        if (ncclCommInitRank(&c->comm, world_size, id, rank) != ncclSuccess) {
+            fprintf(stderr, "[moe_cuda] ERROR: moe_create: ncclCommInitRank failed\n");
+            c->comm = nullptr;
+            moe_destroy(c);
+            return nullptr;
+        }
+    }
+    return c;
+}
+
+void moe_destroy(moe_ctx *c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    if (c->comm) ncclCommDestroy(c->comm);
+    for (int p = 0; p <= MOE_N_PHASES; p++)
+        if (c->ev[p]) cudaEventDestroy(c->ev[p]);
+    for (auto &L : c->layers) {
+        cudaFree(L.experts);
+        cudaFree(L.router);
+        cudaFree(L.bias);
+        cudaFree(L.norm);
+    }
+    void *bufs[] = {c->part, c->d_in, c->d_out, c->h_post, c->idx, c->wts, c->idx_given, c->w_given, c->bias_tmp, c->xop, c->x_inv, c->plan.counts,
+                    c->plan.pair_expert, c->plan.pair_token, c->plan.pair_w, c->plan.chunk_expert,
+                    c->plan.chunk_pair0, c->plan.chunk_ntok, c->plan.slot_pair, c->plan.error, c->counter, c->act,
+                    c->dop, c->dcf, c->d_inv, c->eo, c->send_x, c->recv_x, c->send_y, c->recv_y, c->send_meta,
+                    c->recv_meta, c->rows_partial};
+    for (void *b : bufs) cudaFree(b);
+    if (c->h_counts) cudaFreeHost(c->h_counts);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+const char *moe_last_error(const moe_ctx *c) { return c ? c->err.c_str() : "null context"; }
+void *moe_stream(moe_ctx *c) { return c ? (void *)c->stream : nullptr; }
+int moe_rank(const moe_ctx *c) { return c ? c->rank : -1; }
+int moe_world_size(const moe_ctx *c) { return c ? c->world : -1; }
+uint64_t moe_kernel_launches(const moe_ctx *c) { return c ? c->launches : 0; }
+void moe_reset_kernel_launches(moe_ctx *c) {
+    if (c) c->launches = 0;
+}
+
+// ------------------------------------------------------------------ weights
+static int layer_alloc(moe_ctx *c, int layer, int down_type, int sh_down_type) {
+    if (layer < 0 || layer >= (int)c->layers.size()) return fail(c, MOE_ERR_ARG, "layer %d out of range", layer);
+    if ((down_type != MOE_TYPE_Q4_K && down_type != MOE_TYPE_Q6_K) ||
+        (sh_down_type != MOE_TYPE_Q4_K && sh_down_type != MOE_TYPE_Q6_K))
+        return fail(c, MOE_ERR_ARG, "down types must be Q4_K (12) or Q6_K (14)");
+    if ((down_type == MOE_TYPE_Q6_K || sh_down_type == MOE_TYPE_Q6_K) && (c->d.I / MOE_QK) % 8)
+        return fail(c, MOE_ERR_ARG, "Q6_K down needs intermediate %% 2048 == 0");
+    CK(cudaSetDevice(c->device));
+    MoeLayerDev &L = c->layers[layer];
+    const int H = c->d.H, I = c->d.I, E = c->d.E;
+    L.gate_bytes = row_bytes(MOE_TYPE_Q4_K, H) * I;
+    const size_t db = row_bytes(down_type, I) * H, sdb = row_bytes(sh_down_type, I) * H;
+    const size_t stride = (2 * L.gate_bytes + (db > sdb ? db : sdb) + 255) & ~(size_t)255;
+    if (!L.experts || L.expert_stride != stride) {
+        cudaFree(L.experts);
+        L.experts = nullptr;
+        CK(cudaMalloc((void **)&L.experts, stride * (c->n_local + 1)));
+    }
+    L.expert_stride = stride;
+    L.down_type = down_type;
+    L.sh_down_type = sh_down_type;
+    L.e0 = c->e0;
+    L.n_local = c->n_local;
+    if (!L.router) CK(cudaMalloc((void **)&L.router, sizeof(float) * (size_t)E * H));
+    if (!L.bias) CK(cudaMalloc((void **)&L.bias, sizeof(float) * E));
+    c->layer_down_bytes[layer] = db;
+    return MOE_OK;
+}
+
+// copies one down matrix (GGUF bytes, device or host) into its slot
+static int put_down(moe_ctx *c, uint8_t *dst, const void *src, int type, bool src_host, uint8_t *tmp) {
+    const int H = c->d.H, I = c->d.I;
+    const size_t bytes = row_bytes(type, I) * H;
+    if (type == MOE_TYPE_Q4_K) {
+        CK(cudaMemcpyAsync(dst, src, bytes, src_host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice,
+                           c->stream));
+        return MOE_OK;
+    }
+    const uint8_t *s = (const uint8_t *)src;
+    if (src_host) {
+        CK(cudaMemcpyAsync(tmp, src, bytes, cudaMemcpyHostToDevice, c->stream));
+        s = tmp;
+    }
+    moe_launch_q6_repack(s, dst, H, I / MOE_QK, 0, c->stream, &c->launches);
+    CK(cudaGetLastError());
+    return MOE_OK;
+}
+
+int moe_load_layer(moe_ctx *c, int layer, const void *gate_exps, const void *up_exps, const void *down_exps,
+                   int down_type, const float *router_w, const float *bias, const void *sh_gate, const void *sh_up,
+                   const void *sh_down, int sh_down_type) {
+    if (!c) return MOE_ERR_ARG;
+    if (!gate_exps || !up_exps || !down_exps || !router_w || !sh_gate || !sh_up || !sh_down)
+        return fail(c, MOE_ERR_ARG, "moe_load_layer: null weight pointer");
+    int rc = layer_alloc(c, layer, down_type, sh_down_type);
+    if (rc) return rc;
+    MoeLayerDev &L = c->layers[layer];
+    const int H = c->d.H, I = c->d.I, E = c->d.E;
+    const size_t gb = L.gate_bytes, db = row_bytes(down_type, I) * H;
+    uint8_t *tmp = nullptr;
+    CK(cudaMalloc((void **)&tmp, row_bytes(MOE_TYPE_Q6_K, I) * H));
+    for (int j = 0; j <= c->n_local; j++) {
+        uint8_t *dst = L.experts + (size_t)j * L.expert_stride;
+        const bool sh = j == c->n_local;
+        const int e = c->e0 + j;
+        const uint8_t *g = sh ? (const uint8_t *)sh_gate : (const uint8_t *)gate_exps + (size_t)e * gb;
+        const uint8_t *u = sh ? (const uint8_t *)sh_up : (const uint8_t *)up_exps + (size_t)e * gb;
+        const uint8_t *dn = sh ? (const uint8_t *)sh_down : (const uint8_t *)down_exps + (size_t)e * db;
+        cudaError_t e1 = cudaMemcpyAsync(dst, g, gb, cudaMemcpyHostToDevice, c->stream);
+        cudaError_t e2 = cudaMemcpyAsync(dst + gb, u, gb, cudaMemcpyHostToDevice, c->stream);
+        if (e1 != cudaSuccess || e2 != cudaSuccess) { cudaFree(tmp); return fail(c, MOE_ERR_CUDA, "weight copy failed"); }
+        rc = put_down(c, dst + 2 * gb, dn, sh ? sh_down_type : down_type, true, tmp);
+        if (rc) { cudaFree(tmp); return rc; }
+        cudaStreamSynchronize(c->stream);  // tmp is reused by the next expert
+    }
+    cudaFree(tmp);
+    CK(cudaMemcpyAsync(L.router, router_w, sizeof(float) * (size_t)E * H, cudaMemcpyHostToDevice, c->stream));
+    if (bias) CK(cudaMemcpyAsync(L.bias, bias, sizeof(float) * E, cudaMemcpyHostToDevice, c->stream));
+    else CK(cudaMemsetAsync(L.bias, 0, sizeof(float) * E, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    return MOE_OK;
+}
+
+int moe_load_layer_packed(moe_ctx *c, int layer, const void *blob, size_t expert_size, const float *router_w,
+                          const float *bias, const void *sh_gate, const void *sh_up, const void *sh_down,
+                          int sh_down_type) {
+    if (!c || !blob) return MOE_ERR_ARG;
+    const int H = c->d.H, I = c->d.I;
+    const size_t gb = row_bytes(MOE_TYPE_Q4_K, H) * I;
+    int down_type;
+    // down type inferred from the per-expert size (infer.m:1814-1821)
+    if (expert_size == 2 * gb + row_bytes(MOE_TYPE_Q6_K, I) * H) down_type = MOE_TYPE_Q6_K;
+    else if (expert_size == 2 * gb + row_bytes(MOE_TYPE_Q4_K, I) * H) down_type = MOE_TYPE_Q4_K;
+    else return fail(c, MOE_ERR_ARG, "packed expert size %zu matches neither Q4_K nor Q6_K down", expert_size);
+    int rc = layer_alloc(c, layer, down_type, sh_down_type);
+    if (rc) return rc;
+    MoeLayerDev &L = c->layers[layer];
+    uint8_t *tmp = nullptr;
+    CK(cudaMalloc((void **)&tmp, row_bytes(MOE_TYPE_Q6_K, I) * H));
+    for (int j = 0; j <= c->n_local; j++) {
+        uint8_t *dst = L.experts + (size_t)j * L.expert_stride;
+        const bool sh = j == c->n_local;
+        const uint8_t *src = (const uint8_t *)blob + (size_t)(c->e0 + j) * expert_size;
+        cudaError_t e1 = cudaMemcpyAsync(dst, sh ? sh_gate : src, gb, cudaMemcpyHostToDevice, c->stream);
+        cudaError_t e2 = cudaMemcpyAsync(dst + gb, sh ? sh_up : src + gb, gb, cudaMemcpyHostToDevice, c->stream);
+        if (e1 != cudaSuccess || e2 != cudaSuccess) { cudaFree(tmp); return fail(c, MOE_ERR_CUDA, "weight copy failed"); }
+        rc = put_down(c, dst + 2 * gb, sh ? sh_down : src + 2 * gb, sh ? sh_down_type : down_type, true, tmp);
+        if (rc) { cudaFree(tmp); return rc; }
+        cudaStreamSynchronize(c->stream);
+    }
+    cudaFree(tmp);
+    CK(cudaMemcpyAsync(L.router, router_w, sizeof(float) * (size_t)c->d.E * H, cudaMemcpyHostToDevice, c->stream));
+    if (bias) CK(cudaMemcpyAsync(L.bias, bias, sizeof(float) * c->d.E, cudaMemcpyHostToDevice, c->stream));
+    else CK(cudaMemsetAsync(L.bias, 0, sizeof(float) * c->d.E, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    return MOE_OK;
+}
+
+int moe_init_layer_synthetic(moe_ctx *c, int layer, uint64_t seed, int down_type, float w_sigma, float router_sigma,
+                             float bias_sigma) {
+    if (!c) return MOE_ERR_ARG;
+    int rc = layer_alloc(c, layer, down_type, down_type);
+    if (rc) return rc;
+    MoeLayerDev &L = c->layers[layer];
+    const int H = c->d.H, I = c->d.I, E = c->d.E;
+    uint8_t *tmp = nullptr;
+    if (down_type == MOE_TYPE_Q6_K) CK(cudaMalloc((void **)&tmp, row_bytes(MOE_TYPE_Q6_K, I) * H));
+    for (int j = 0; j <= c->n_local; j++) {
+        uint8_t *dst = L.experts + (size_t)j * L.expert_stride;
+        const int e = (j == c->n_local) ? E : c->e0 + j;
+        moe_launch_synth_quant(MOE_TYPE_Q4_K, seed, synth_stream(layer, e, SYN_GATE), I, H, w_sigma, dst, c->stream,
+                               &c->launches);
+        moe_launch_synth_quant(MOE_TYPE_Q4_K, seed, synth_stream(layer, e, SYN_UP), I, H, w_sigma,
+                               dst + L.gate_bytes, c->stream, &c->launches);
+        if (down_type == MOE_TYPE_Q6_K) {
+            moe_launch_synth_quant(MOE_TYPE_Q6_K, seed, synth_stream(layer, e, SYN_DOWN), H, I, w_sigma, tmp,
+                                   c->stream, &c->launches);
+            moe_launch_q6_repack(tmp, dst + 2 * L.gate_bytes, H, I / MOE_QK, 0, c->stream, &c->launches);
+        } else {
+            moe_launch_synth_quant(MOE_TYPE_Q4_K, seed, synth_stream(layer, e, SYN_DOWN), H, I, w_sigma,
+                                   dst + 2 * L.gate_bytes, c->stream, &c->launches);
+        }
+    }
+    moe_launch_synth_f32(seed, synth_stream(layer, 0, SYN_ROUTER), (size_t)E * H, router_sigma, L.router, c->stream,
+                         &c->launches);
+    moe_launch_synth_f32(seed, synth_stream(layer, 0, SYN_BIAS), (size_t)E, bias_sigma, L.bias, c->stream,
+                         &c->launches);
+    CK(cudaGetLastError());
+    CK(cudaStreamSynchronize(c->stream));
+    if (tmp) cudaFree(tmp);
+    return MOE_OK;
+}
+
+int moe_add_router_bias(moe_ctx *c, int layer, const float *extra) {
+    if (!c || !extra) return MOE_ERR_ARG;
+    if (layer < 0 || layer >= (int)c->layers.size() || !c->layers[layer].bias)
+        return fail(c, MOE_ERR_STATE, "layer %d not loaded", layer);
+    std::vector<float> b(c->d.E);
+    CK(cudaMemcpy(b.data(), c->layers[layer].bias, sizeof(float) * c->d.E, cudaMemcpyDeviceToHost));
+    for (int e = 0; e < c->d.E; e++) b[e] += extra[e];
+    CK(cudaMemcpy(c->layers[layer].bias, b.data(), sizeof(float) * c->d.E, cudaMemcpyHostToDevice));
+    return MOE_OK;
+}
+
+int moe_set_norm_weight(moe_ctx *c, int layer, const float *w) {
+    if (!c || !w) return MOE_ERR_ARG;
+    if (layer < 0 || layer >= (int)c->layers.size()) return fail(c, MOE_ERR_ARG, "layer %d out of range", layer);
+    CK(cudaSetDevice(c->device));
+    MoeLayerDev &L = c->layers[layer];
+    if (!L.norm) CK(cudaMalloc((void **)&L.norm, sizeof(float) * c->d.H));
+    CK(cudaMemcpy(L.norm, w, sizeof(float) * c->d.H, cudaMemcpyHostToDevice));
+    return MOE_OK;
+}
+
+size_t moe_expert_bytes(const moe_ctx *c, int layer) {
+    if (!c || layer < 0 || layer >= (int)c->layers.size() || !c->layers[layer].experts) return 0;
+    return 2 * c->layers[layer].gate_bytes + c->layer_down_bytes[layer];
+}
+
+int moe_read_expert(moe_ctx *c, int layer, int expert, void *dst, size_t dst_size) {
+    if (!c || !dst) return MOE_ERR_ARG;
+    if (layer < 0 || layer >= (int)c->layers.size() || !c->layers[layer].experts)
+        return fail(c, MOE_ERR_STATE, "layer %d not loaded", layer);
+    MoeLayerDev &L = c->layers[layer];
+    int j;
+    if (expert == c->d.E) j = c->n_local;
+    else if (expert >= c->e0 && expert < c->e0 + c->n_local) j = expert - c->e0;
+    else return fail(c, MOE_ERR_ARG, "expert %d not held by rank %d", expert, c->rank);
+    const int ty = expert == c->d.E ? L.sh_down_type : L.down_type;
+    const size_t db = row_bytes(ty, c->d.I) * c->d.H;
+    if (dst_size < 2 * L.gate_bytes + db) return fail(c, MOE_ERR_ARG, "moe_read_expert: buffer too small");
+    CK(cudaSetDevice(c->device));
+    const uint8_t *src = L.experts + (size_t)j * L.expert_stride;
+    CK(cudaMemcpy(dst, src, 2 * L.gate_bytes, cudaMemcpyDeviceToHost));
+    if (ty == MOE_TYPE_Q4_K) {
+        CK(cudaMemcpy((uint8_t *)dst + 2 * L.gate_bytes, src + 2 * L.gate_bytes, db, cudaMemcpyDeviceToHost));
+    } else {
+        uint8_t *tmp = nullptr;
+        CK(cudaMalloc((void **)&tmp, db));
+        moe_launch_q6_repack(src + 2 * L.gate_bytes, tmp, c->d.H, c->d.I / MOE_QK, 1, c->stream, &c->launches);
+        cudaError_t e1 = cudaStreamSynchronize(c->stream);
+        cudaError_t e2 = cudaMemcpy((uint8_t *)dst + 2 * L.gate_bytes, tmp, db, cudaMemcpyDeviceToHost);
+        cudaFree(tmp);
+        if (e1 != cudaSuccess || e2 != cudaSuccess) return fail(c, MOE_ERR_CUDA, "moe_read_expert: unpack failed");
+    }
+    return MOE_OK;
+}
+
+// ------------------------------------------------------------------ forward
+// records the boundary before phase `ph` (MOE_N_PHASES = end of the step)
+static void mark(moe_ctx *c, int ph, cudaStream_t s) {
+    if (!c->timing) return;
+    cudaEventRecord(c->ev[ph], s);
+    c->ev_valid[ph] = true;
+}
+
+static int check_layer(moe_ctx *c, int layer) {
+    if (layer < 0 || layer >= (int)c->layers.size() || !c->layers[layer].experts)
+        return fail(c, MOE_ERR_STATE, "layer %d not loaded", layer);
+    return MOE_OK;
+}
+
+// experts + combine over the activation rows in `x` (rows = tokens on one GPU)
+static int run_local(moe_ctx *c, int layer, const float *x, int T, const int *idx_in, const float *w_in,
+                     int routed, int with_shared, const float *residual, float *out, cudaStream_t s) {
+    MoeLayerDev &L = c->layers[layer];
+    const MoeDims &d = c->d;
+    const int mode = !routed ? 2 : (idx_in ? 1 : 0);
+    for (int p = 0; p <= MOE_N_PHASES; p++) c->ev_valid[p] = false;
+    mark(c, MOE_PHASE_ROUTER, s);
+    if (mode == 0) moe_launch_router_logits(L.router, x, T, d.H, d.E, c->part, c->n_split, s, &c->launches);
+    mark(c, MOE_PHASE_ROUTE, s);
+    moe_launch_route_and_plan(d, c->part, c->n_split, nullptr, L.bias, mode, idx_in, w_in, T, c->idx, c->wts, x,
+                              c->xop, c->x_inv, with_shared, 1, c->plan, c->counter, s, &c->launches);
+    const int max_chunks = (T * d.K + T + MOE_TC - 1) / MOE_TC + d.E + 1;
+    mark(c, MOE_PHASE_GATEUP, s);
+    moe_launch_gateup(d, L, c->plan, c->xop, c->x_inv, c->act, max_chunks * (d.I / MOE_ROWS_GU), s, &c->launches);
+    mark(c, MOE_PHASE_PREP, s);
+    moe_launch_prep_down(d, L, c->plan, c->act, c->dop, c->dcf, c->d_inv, T * d.K + T, s, &c->launches);
+    mark(c, MOE_PHASE_DOWN, s);
+    moe_launch_down(d, L, c->plan, c->dop, c->dcf, c->d_inv, c->eo, max_chunks * (d.H / 16), s, &c->launches);
+    mark(c, MOE_PHASE_OUTPUT, s);
+    moe_launch_combine(d, c->plan, c->eo, T, routed, with_shared, residual, out, s, &c->launches);
+    mark(c, MOE_N_PHASES, s);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(c, MOE_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+    c->last_layer = layer;
+    return MOE_OK;
+}
+
+int moe_forward_device(moe_ctx *c, int layer, const float *d_h, int T, float *d_out, int *d_idx, float *d_w,
+                       void *stream) {
+    if (!c || !d_h || !d_out) return MOE_ERR_ARG;
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
+    if (c->world > 1) return fail(c, MOE_ERR_STATE, "expert-parallel forward not available in this build");
+    if (T == 0) return MOE_OK;
+    cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    rc = run_local(c, layer, d_h, T, nullptr, nullptr, 1, 1, nullptr, d_out, s);
+    if (rc) return rc;
+    if (d_idx) CK(cudaMemcpyAsync(d_idx, c->idx, sizeof(int) * T * c->d.K, cudaMemcpyDeviceToDevice, s));
+    if (d_w) CK(cudaMemcpyAsync(d_w, c->wts, sizeof(float) * T * c->d.K, cudaMemcpyDeviceToDevice, s));
+    return MOE_OK;
+}
+
+static int finish_sync(moe_ctx *c) {
+    CK(cudaStreamSynchronize(c->stream));
+    int errflag = 0;
+    CK(cudaMemcpy(&errflag, c->plan.error, sizeof(int), cudaMemcpyDeviceToHost));
+    if (errflag) {
+        cudaMemset(c->plan.error, 0, sizeof(int));
+        return fail(c, MOE_ERR_ARG, "expert index out of range in routing");
+    }
+    return MOE_OK;
+}
+
+int moe_forward(moe_ctx *c, int layer, const float *h, int T, float *out, int *idx_out, float *w_out) {
+    if (!c || !h || !out) return MOE_ERR_ARG;
+    if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
+    CK(cudaSetDevice(c->device));
+    const size_t n = (size_t)T * c->d.H;
+    CK(cudaMemcpyAsync(c->d_in, h, n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    int rc = moe_forward_device(c, layer, c->d_in, T, c->d_out, nullptr, nullptr, nullptr);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(out, c->d_out, n * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    if (idx_out) CK(cudaMemcpyAsync(idx_out, c->idx, sizeof(int) * T * c->d.K, cudaMemcpyDeviceToHost, c->stream));
+    if (w_out) CK(cudaMemcpyAsync(w_out, c->wts, sizeof(float) * T * c->d.K, cudaMemcpyDeviceToHost, c->stream));
+    return finish_sync(c);
+}
+
+int moe_experts_forward_device(moe_ctx *c, int layer, const float *d_h, int T, const int *d_idx, const float *d_w,
+                               int K, float *d_out, void *stream) {
+    if (!c || !d_h || !d_idx || !d_w || !d_out) return MOE_ERR_ARG;
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    if (K != c->d.K) return fail(c, MOE_ERR_ARG, "K %d differs from the context's top_k %d", K, c->d.K);
+    if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
+    if (c->world > 1) return fail(c, MOE_ERR_STATE, "expert-parallel forward not available in this build");
+    if (T == 0) return MOE_OK;
+    cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    return run_local(c, layer, d_h, T, d_idx, d_w, 1, 0, nullptr, d_out, s);
+}
+
+int moe_experts_forward(moe_ctx *c, int layer, const float *h, int T, const int *idx, const float *w, int K,
+                        float *out) {
+    if (!c || !h || !idx || !w || !out) return MOE_ERR_ARG;
+    if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
+    if (K != c->d.K) return fail(c, MOE_ERR_ARG, "K %d differs from the context's top_k %d", K, c->d.K);
+    for (int i = 0; i < T * K; i++)
+        if (idx[i] < 0 || idx[i] >= c->d.E) return fail(c, MOE_ERR_ARG, "expert index %d out of range", idx[i]);
+    CK(cudaSetDevice(c->device));
+    const size_t n = (size_t)T * c->d.H;
+    CK(cudaMemcpyAsync(c->d_in, h, n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->idx_given, idx, sizeof(int) * T * K, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->w_given, w, sizeof(float) * T * K, cudaMemcpyHostToDevice, c->stream));
+    int rc = moe_experts_forward_device(c, layer, c->d_in, T, c->idx_given, c->w_given, K, c->d_out, nullptr);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(out, c->d_out, n * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    return finish_sync(c);
+}
+
+int moe_shared_forward(moe_ctx *c, int layer, const float *h, int T, float *sd) {
+    if (!c || !h || !sd) return MOE_ERR_ARG;
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
+    if (T == 0) return MOE_OK;
+    CK(cudaSetDevice(c->device));
+    const size_t n = (size_t)T * c->d.H;
+    CK(cudaMemcpyAsync(c->d_in, h, n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    // shared only: routed slots are empty (routing given as "none")
+    rc = run_local(c, layer, c->d_in, T, nullptr, nullptr, 0, 1, nullptr, c->d_out, c->stream);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(sd, c->d_out, n * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    return finish_sync(c);
+}
+
+int moe_route(moe_ctx *c, const float *logits, const float *bias, int T, int *idx, float *w) {
+    if (!c || !logits || !idx || !w) return MOE_ERR_ARG;
+    if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
+    if (T == 0) return MOE_OK;
+    CK(cudaSetDevice(c->device));
+    const int E = c->d.E, K = c->d.K;
+    float *d_lg = c->part, *d_b = nullptr;
+    CK(cudaMemcpyAsync(d_lg, logits, sizeof(float) * T * E, cudaMemcpyHostToDevice, c->stream));
+    if (bias) {
+        d_b = c->bias_tmp;
+        CK(cudaMemcpyAsync(d_b, bias, sizeof(float) * E, cudaMemcpyHostToDevice, c->stream));
+    }
+    moe_launch_route_and_plan(c->d, nullptr, 0, d_lg, d_b, 0, nullptr, nullptr, T, c->idx, c->wts, nullptr,
+                              nullptr, nullptr, 0, 0, c->plan, c->counter, c->stream, &c->launches);
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(idx, c->idx, sizeof(int) * T * K, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaMemcpyAsync(w, c->wts, sizeof(float) * T * K, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    return MOE_OK;
+}
+
+int moe_forward_stack_device(moe_ctx *c, int first, int n_layers, float *d_hidden, int T, void *stream) {
+    if (!c || !d_hidden) return MOE_ERR_ARG;
+    if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
+    if (c->world > 1) return fail(c, MOE_ERR_STATE, "expert-parallel forward not available in this build");
+    cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    for (int l = first; l < first + n_layers; l++) {
+        int rc = check_layer(c, l);
+        if (rc) return rc;
+        moe_launch_rmsnorm(d_hidden, c->layers[l].norm, c->h_post, T, c->d.H, c->cfg.rms_eps, s, &c->launches);
+        rc = run_local(c, l, c->h_post, T, nullptr, nullptr, 1, 1, d_hidden, d_hidden, s);
+        if (rc) return rc;
+    }
+    return MOE_OK;
+}
+
+int moe_forward_stack(moe_ctx *c, int first, int n_layers, float *hidden, int T) {
+    if (!c || !hidden) return MOE_ERR_ARG;
+    if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
+    CK(cudaSetDevice(c->device));
+    const size_t n = (size_t)T * c->d.H;
+    CK(cudaMemcpyAsync(c->d_in, hidden, n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    int rc = moe_forward_stack_device(c, first, n_layers, c->d_in, T, nullptr);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(hidden, c->d_in, n * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    return finish_sync(c);
+}
+
+int moe_set_timing(moe_ctx *c, int enable) {
+    if (!c) return MOE_ERR_ARG;
+    CK(cudaSetDevice(c->device));
+    if (enable && !c->ev[0])
+        for (int p = 0; p <= MOE_N_PHASES; p++) CK(cudaEventCreate(&c->ev[p]));
+    c->timing = enable != 0;
+    return MOE_OK;
+}
+
+int moe_get_timing(moe_ctx *c, float *ms, int n) {
+    if (!c || !ms) return MOE_ERR_ARG;
+    if (!c->timing) return fail(c, MOE_ERR_STATE, "timing is not enabled");
+    for (int p = MOE_N_PHASES; p >= 0; p--)
+        if (c->ev_valid[p]) { CK(cudaEventSynchronize(c->ev[p])); break; }
+    for (int p = 0; p < n && p < MOE_N_PHASES; p++) {
+        ms[p] = 0.0f;
+        if (!c->ev_valid[p]) continue;
+        int q = p + 1;
+        while (q <= MOE_N_PHASES && !c->ev_valid[q]) q++;
+        if (q > MOE_N_PHASES) continue;
+        CK(cudaEventElapsedTime(&ms[p], c->ev[p], c->ev[q]));
+    }
+    return MOE_OK;
+}
+
+uint64_t moe_last_weight_bytes(const moe_ctx *cc) {
+    moe_ctx *c = const_cast<moe_ctx *>(cc);
+    if (!c || c->last_layer < 0) return 0;
+    if (cudaStreamSynchronize(c->stream) != cudaSuccess) return 0;
+    int counts[4] = {0, 0, 0, 0};
+    if (cudaMemcpy(counts, c->plan.counts, sizeof(counts), cudaMemcpyDeviceToHost) != cudaSuccess) return 0;
+    const MoeLayerDev &L = c->layers[c->last_layer];
+    const size_t eb = 2 * L.gate_bytes + c->layer_down_bytes[c->last_layer];
+    const size_t sb = 2 * L.gate_bytes + row_bytes(L.sh_down_type, c->d.I) * c->d.H;
+    return (uint64_t)counts[2] * eb + sb + sizeof(float) * ((size_t)c->d.E * c->d.H + c->d.E);
+}
+
+// ------------------------------------------------------------------ codec
+static int dequant_host(int type, const void *src, float *dst, size_t n) {
+    moe_ctx *c = nullptr;
+    if (!src || !dst || n % MOE_QK) return fail(c, MOE_ERR_ARG, "dequantize: n must be a multiple of 256");
+    const size_t nb = n / MOE_QK, bytes = nb * (type == MOE_TYPE_Q6_K ? MOE_Q6K_BYTES : MOE_Q4K_BYTES);
+    uint8_t *ds = nullptr;
+    float *dd = nullptr;
+    CK(cudaMalloc((void **)&ds, bytes + 16));
+    if (cudaMalloc((void **)&dd, n * sizeof(float)) != cudaSuccess) { cudaFree(ds); return MOE_ERR_CUDA; }
+    int rc = MOE_OK;
+    if (cudaMemcpy(ds, src, bytes, cudaMemcpyHostToDevice) != cudaSuccess) rc = MOE_ERR_CUDA;
+    if (!rc) {
+        moe_launch_dequant(type, ds, dd, n, 0, nullptr);
+        if (cudaGetLastError() != cudaSuccess || cudaMemcpy(dst, dd, n * sizeof(float), cudaMemcpyDeviceToHost) !=
+                                                     cudaSuccess)
+            rc = MOE_ERR_CUDA;
+    }
+    cudaFree(ds);
+    cudaFree(dd);
+    return rc;
+}
+int moe_dequantize_row_q4_K(const void *src, float *dst, size_t n) { return dequant_host(MOE_TYPE_Q4_K, src, dst, n); }
+int moe_dequantize_row_q6_K(const void *src, float *dst, size_t n) { return dequant_host(MOE_TYPE_Q6_K, src, dst, n); }
+
+}  // extern "C"

@@ -1,0 +1,74 @@
+// moe_internal.h -- host-side view of the device pipeline of libmoe_cuda.so.
+#pragma once
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+// Dispatch plan of one forward step on one GPU: (token, expert) pairs grouped
+// by expert, and chunks of at most `tc` tokens of one expert (the unit of
+// work of the expert kernels).
+struct MoePlan {
+    int *counts;        // [4]: n_pairs, n_chunks, routed experts hit, spare
+    int *pair_expert;   // [max_pairs]  global expert id (n_experts = shared)
+    int *pair_token;    // [max_pairs]  row of the activation operand
+    float *pair_w;      // [max_pairs]  routing weight (1 for the shared expert)
+    int *chunk_expert;  // [max_pairs]
+    int *chunk_pair0;   // [max_pairs]
+    int *chunk_ntok;    // [max_pairs]
+    int *slot_pair;     // [max_tokens][K+1] pair of (token, slot); slot K = shared
+    int *error;         // [1] set to a non-zero code by device-side checks
+};
+
+// Where the expert weights of one layer live on this GPU.
+struct MoeLayerDev {
+    uint8_t *experts;       // [n_local + 1][expert_stride]; slot n_local = shared
+    size_t expert_stride;
+    size_t gate_bytes;      // one Q4_K [I x H] matrix
+    int down_type, sh_down_type;  // 12 / 14
+    int e0, n_local;        // global id of slot 0, number of routed experts here
+    float *router;          // [E][H]
+    float *bias;            // [E] or nullptr
+    float *norm;            // [H] or nullptr
+};
+
+struct MoeDims {
+    int H, I, E, n_group, topk_group, K;
+    float scale;
+};
+
+#define MOE_TC 8  // tokens per chunk (two 8-column MMA tiles: 4 tokens x {hi, lo} each)
+
+// ---- launchers (moe_kernels.cu); every one counts its kernel launches ------
+extern "C++" {
+void moe_launch_router_logits(const float *Wr, const float *x, int T, int H, int E, float *part, int n_split,
+                              cudaStream_t s, uint64_t *launches);
+// mode: 0 route from logits / partial logits, 1 routing given (idx_in, w_in),
+// 2 shared expert only
+void moe_launch_route_and_plan(const MoeDims &d, const float *part, int n_split, const float *logits,
+                               const float *bias, int mode, const int *idx_in, const float *w_in, int T,
+                               int *idx_out, float *w_out, const float *x, __half *xop, float *x_inv,
+                               int include_shared, int build_plan, const MoePlan &plan, int *counter,
+                               cudaStream_t s, uint64_t *launches);
+void moe_launch_gateup(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const __half *xop,
+                       const float *x_inv, float *act, int max_items, cudaStream_t s, uint64_t *launches);
+void moe_launch_prep_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const float *act,
+                          __half *dop, float *dcf, float *d_inv, int max_pairs, cudaStream_t s,
+                          uint64_t *launches);
+void moe_launch_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const __half *dop,
+                     const float *dcf, const float *d_inv, float *eo, int max_items, cudaStream_t s,
+                     uint64_t *launches);
+void moe_launch_combine(const MoeDims &d, const MoePlan &plan, const float *eo, int T, int include_routed,
+                        int include_shared, const float *residual, float *out, cudaStream_t s, uint64_t *launches);
+void moe_launch_rmsnorm(const float *x, const float *w, float *y, int T, int H, float eps, cudaStream_t s,
+                        uint64_t *launches);
+void moe_launch_dequant(int type, const uint8_t *src, float *dst, size_t n, cudaStream_t s, uint64_t *launches);
+void moe_launch_q6_repack(const uint8_t *src, uint8_t *dst, int rows, int nb, int inverse, cudaStream_t s,
+                          uint64_t *launches);
+void moe_launch_synth_quant(int type, uint64_t seed, uint64_t stream, int rows, int cols, double sigma,
+                            uint8_t *dst, cudaStream_t s, uint64_t *launches);
+void moe_launch_synth_f32(uint64_t seed, uint64_t stream, size_t n, double sigma, float *dst, cudaStream_t s,
+                          uint64_t *launches);
+size_t moe_q4op_halves(int K);   // Q4_K activation operand, halves per vector
+size_t moe_q6op_halves(int K);   // Q6_K activation operand, halves per vector
+}

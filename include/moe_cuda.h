@@ -1,0 +1,203 @@
+/*
+ * moe_cuda.h -- C ABI of libmoe_cuda.so: the DeepSeek-V3/R1 mixture-of-experts
+ * block (sigmoid router, grouped top-k, dispatch, Q4_K/Q6_K SwiGLU experts,
+ * shared expert, weighted combine) on NVIDIA B200 (sm_100a).
+ *
+ * Drop-in boundary.  The reference engine (JohnnyNg6/flash_deepseek) runs this
+ * block inside layer_forward (infer.m:1878-1922) through four seams, each of
+ * which has an entry point here:
+ *
+ *   route(logits, bias, K, exp_idx, exp_w)            infer.m:920-991
+ *       -> moe_route()
+ *   metal_moe_forward(L, h_post, exp_idx, exp_w, K, moe_out)
+ *                                                     infer.m:1604-1700
+ *       -> moe_experts_forward()
+ *   shared_expert_worker(SharedJob *)                 infer.m:1099-1114
+ *       -> moe_shared_forward()
+ *   the whole MoE half of layer_forward (logits mv + route + shared + routed
+ *   experts + combine, infer.m:1878-1922 without the residual)
+ *       -> moe_forward()
+ *   the codec dequantize_row_q4_K / dequantize_row_q6_K    quant.h:11-12
+ *       -> moe_dequantize_row_q4_K() / moe_dequantize_row_q6_K()
+ *
+ * Weights enter as the raw GGUF block bytes the reference reads with
+ * gguf_tensor_pread (gguf.h:192): the stacked blk.L.ffn_{gate,up,down}_exps
+ * tensors (repack_experts.c:126-128) with type ids GGML_TYPE_Q4_K = 12 and
+ * GGML_TYPE_Q6_K = 14 (gguf.h:59,61), or the reference's packed per-layer
+ * expert file (infer.m:1802-1823).
+ *
+ * Conventions follow gguf.h: plain pointers and sizes, int return 0 = ok,
+ * < 0 = error with the message available from moe_last_error().  All calls on
+ * one context come from one host thread.  Host-pointer calls are synchronous;
+ * the *_device calls are asynchronous on the stream given (NULL = the
+ * context's stream).
+ */
+#ifndef MOE_CUDA_H
+#define MOE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MOE_TYPE_Q4_K 12 /* GGML_TYPE_Q4_K, gguf.h:59 */
+#define MOE_TYPE_Q6_K 14 /* GGML_TYPE_Q6_K, gguf.h:61 */
+
+#define MOE_OK 0
+#define MOE_ERR_ARG (-1)      /* bad argument / shape */
+#define MOE_ERR_CUDA (-2)     /* CUDA runtime error */
+#define MOE_ERR_NCCL (-3)     /* NCCL error or timeout */
+#define MOE_ERR_STATE (-4)    /* layer not loaded, wrong call order */
+#define MOE_ERR_TIMEOUT (-5)  /* a bounded device wait gave up */
+
+/* Model constants of infer.m:43-80 made run-time parameters. */
+typedef struct moe_config {
+    int hidden;         /* H: 7168 (HIDDEN_DIM) */
+    int intermediate;   /* I: 2048 (MOE_INTERMEDIATE, also the shared expert) */
+    int n_experts;      /* E: 256 (NUM_EXPERTS) */
+    int n_group;        /* 8 (N_GROUP) */
+    int topk_group;     /* 4 (TOPK_GROUP) */
+    int top_k;          /* K: 8 (--k, infer.m:2042); at most 16 (MAX_K) */
+    float routed_scale; /* 2.5 (ROUTED_SCALE) */
+    float rms_eps;      /* 1e-6 (RMS_NORM_EPS), used by moe_forward_stack */
+    int n_layers;       /* number of layer slots in this context */
+    int max_tokens;     /* largest token batch of one forward call */
+} moe_config;
+
+typedef struct moe_ctx moe_ctx;
+
+/* ------------------------------------------------------------------ setup */
+/* Fills 128 bytes with a fresh NCCL unique id (rank 0 only, then broadcast
+ * to the other ranks by the caller). */
+int moe_get_unique_id(void *out_id128);
+
+/* Creates a context on CUDA device `device`.  world_size == 1 needs no id.
+ * For world_size > 1 (expert parallel, one process per GPU) routed expert e
+ * lives on rank e / (n_experts / world_size); router and shared expert are
+ * replicated.  Returns NULL on error (message on stderr). */
+moe_ctx *moe_create(const moe_config *cfg, int device, int rank, int world_size,
+                    const void *unique_id128);
+void moe_destroy(moe_ctx *ctx);
+const char *moe_last_error(const moe_ctx *ctx);
+/* cudaStream_t of the context, for callers that time or chain work. */
+void *moe_stream(moe_ctx *ctx);
+int moe_rank(const moe_ctx *ctx);
+int moe_world_size(const moe_ctx *ctx);
+
+/* ---------------------------------------------------------------- weights */
+/* Loads one MoE layer from the GGUF tensors of layer L (host pointers):
+ *   gate_exps / up_exps : blk.L.ffn_{gate,up}_exps.weight, Q4_K, E experts of
+ *                         [I rows x H cols] stacked expert-major;
+ *   down_exps           : blk.L.ffn_down_exps.weight, [H x I] per expert,
+ *                         down_type MOE_TYPE_Q4_K or MOE_TYPE_Q6_K;
+ *   router_w            : blk.L.ffn_gate_inp.weight as fp32 [E x H];
+ *   bias                : blk.L.exp_probs_b.bias fp32 [E] (may be NULL);
+ *   sh_gate/sh_up/sh_down: blk.L.ffn_{gate,up,down}_shexp.weight.
+ * Each rank copies only its own experts.  Q6_K matrices are repacked on the
+ * device into an aligned layout (lossless; moe_read_expert returns the GGUF
+ * bytes again). */
+int moe_load_layer(moe_ctx *ctx, int layer, const void *gate_exps, const void *up_exps,
+                   const void *down_exps, int down_type, const float *router_w,
+                   const float *bias, const void *sh_gate, const void *sh_up,
+                   const void *sh_down, int sh_down_type);
+
+/* Same, from the reference's packed expert file layout (packed_experts/
+ * layer_XX.bin: expert e at e*expert_size = [gate][up][down],
+ * repack_experts.c:157-238, infer.m:1802-1823); the down type is inferred
+ * from expert_size as infer.m:1814-1821 does. */
+int moe_load_layer_packed(moe_ctx *ctx, int layer, const void *layer_blob, size_t expert_size,
+                          const float *router_w, const float *bias, const void *sh_gate,
+                          const void *sh_up, const void *sh_down, int sh_down_type);
+
+/* Synthetic layer generated on the device (no host transfer): every weight
+ * N(0, w_sigma) from a counter-based generator keyed by (seed, layer, expert,
+ * matrix, element), quantized to Q4_K / down_type; router N(0, router_sigma),
+ * bias N(0, bias_sigma).  Bit-identical to the host generator of the test
+ * oracle. */
+int moe_init_layer_synthetic(moe_ctx *ctx, int layer, uint64_t seed, int down_type,
+                             float w_sigma, float router_sigma, float bias_sigma);
+
+/* Adds a per-expert bias to the router bias of a loaded layer (used to skew
+ * expert load, e.g. a Zipf profile). */
+int moe_add_router_bias(moe_ctx *ctx, int layer, const float *extra_bias);
+
+/* RMSNorm weight (fp32 [H]) applied before layer L in moe_forward_stack. */
+int moe_set_norm_weight(moe_ctx *ctx, int layer, const float *w);
+
+/* Copies expert `expert` (n_experts = shared) of layer L back in the GGUF
+ * byte layout [gate][up][down]; only experts this rank holds.  dst_size must
+ * be at least moe_expert_bytes(). */
+int moe_read_expert(moe_ctx *ctx, int layer, int expert, void *dst, size_t dst_size);
+size_t moe_expert_bytes(const moe_ctx *ctx, int layer);
+
+/* ---------------------------------------------------------------- forward */
+/* The full MoE block for n_tokens tokens held by this rank (host buffers):
+ * out[t] = sum_k w_k E_{idx_k}(h[t]) + shared(h[t]), fp32 [n_tokens x H].
+ * idx_out / w_out (optional, [n_tokens x K]) return the routing in the
+ * reference's slot order. */
+int moe_forward(moe_ctx *ctx, int layer, const float *h_post, int n_tokens, float *out,
+                int *idx_out, float *w_out);
+/* Same on device buffers, asynchronous on `stream` (NULL = context stream). */
+int moe_forward_device(moe_ctx *ctx, int layer, const float *d_h_post, int n_tokens,
+                       float *d_out, int *d_idx_out, float *d_w_out, void *stream);
+
+/* Routed experts only, with the routing given (metal_moe_forward,
+ * infer.m:1604): moe_out[t] = sum_k exp_w[t,k] E_{exp_idx[t,k]}(h[t]). */
+int moe_experts_forward(moe_ctx *ctx, int layer, const float *h_post, int n_tokens,
+                        const int *exp_idx, const float *exp_w, int K, float *moe_out);
+int moe_experts_forward_device(moe_ctx *ctx, int layer, const float *d_h_post, int n_tokens,
+                               const int *d_exp_idx, const float *d_exp_w, int K,
+                               float *d_moe_out, void *stream);
+
+/* Shared expert only (shared_expert_worker, infer.m:1099): sd = shared(h). */
+int moe_shared_forward(moe_ctx *ctx, int layer, const float *h_post, int n_tokens, float *sd);
+
+/* Routing only (route, infer.m:920-991) for n_tokens rows of logits, with the
+ * context's group/top-k constants. */
+int moe_route(moe_ctx *ctx, const float *logits, const float *bias, int n_tokens, int *exp_idx,
+              float *exp_w);
+
+/* Stack of layers [first, first + n_layers): per layer
+ *   h_post = RMSNorm(hidden) * norm_w;  hidden = hidden + MoE(h_post)
+ * (infer.m:1850, 1922 with attention as identity).  hidden is updated in
+ * place, device buffer [n_tokens x H]. */
+int moe_forward_stack_device(moe_ctx *ctx, int first_layer, int n_layers, float *d_hidden,
+                             int n_tokens, void *stream);
+int moe_forward_stack(moe_ctx *ctx, int first_layer, int n_layers, float *hidden, int n_tokens);
+
+/* ------------------------------------------------------------------ codec */
+/* Device twins of quant.h:11-12 (host buffers in and out). */
+int moe_dequantize_row_q4_K(const void *src, float *dst, size_t n);
+int moe_dequantize_row_q6_K(const void *src, float *dst, size_t n);
+
+/* ------------------------------------------------------------- statistics */
+/* Per-phase device timing of the last forward call (the B200 counterpart of
+ * the reference's moe_prof_t phase records, infer.m:177-261): when enabled,
+ * CUDA events are recorded on the context stream between the phases below and
+ * moe_get_timing() returns their durations in milliseconds. */
+#define MOE_PHASE_ROUTER 0   /* router logits GEMV */
+#define MOE_PHASE_ROUTE 1    /* sigmoid + grouped top-k + plan + operand */
+#define MOE_PHASE_DISPATCH 2 /* expert-parallel dispatch (0 on one GPU) */
+#define MOE_PHASE_GATEUP 3   /* gate/up GEMV + SwiGLU */
+#define MOE_PHASE_PREP 4     /* down-operand preparation */
+#define MOE_PHASE_DOWN 5     /* down GEMV */
+#define MOE_PHASE_COMBINE 6  /* combine all-to-all (0 on one GPU) */
+#define MOE_PHASE_OUTPUT 7   /* weighted combine + shared (+ residual) */
+#define MOE_N_PHASES 8
+int moe_set_timing(moe_ctx *ctx, int enable);
+int moe_get_timing(moe_ctx *ctx, float *ms, int n);
+
+/* Number of kernels this library launched on the context's device since
+ * creation (or the last reset). */
+uint64_t moe_kernel_launches(const moe_ctx *ctx);
+void moe_reset_kernel_launches(moe_ctx *ctx);
+/* Weight bytes the last forward call had to read on this rank (routed experts
+ * actually hit + shared + router), for roofline accounting. */
+uint64_t moe_last_weight_bytes(const moe_ctx *ctx);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MOE_CUDA_H */

@@ -1,0 +1,102 @@
+/*
+ * oracle.h -- CPU restatement of the DeepSeek-V3/R1 MoE block of the reference
+ * engine (JohnnyNg6/flash_deepseek), used ONLY as test infrastructure: the
+ * checker for the CUDA library in tests/, __graft_entry__.smoke() and the
+ * cpu_baseline leg of bench.py.  Nothing in the product links or calls it.
+ *
+ * Parity pins (how this restatement is itself checked):
+ *   - Q4_K/Q6_K/fp16 decode: bit-exact against the reference's own quant.c
+ *     (compiled in place into oracle/_ref/ by oracle/Makefile) and against
+ *     gguf-py 0.19.0 dequantize() golden vectors in tests/golden/.
+ *   - route / sigmoid / silu_mul / rms_norm: against the reference's own
+ *     functions extracted from infer.m at build time (oracle/_ref/), and the
+ *     golden vectors they produced (tests/golden/route_golden.npz).
+ *   - The expert / layer composition (dequant + dot in place of Accelerate's
+ *     cblas_sgemv, which does not exist on Linux) is a restatement of
+ *     infer.m:1069-1114 and 1915-1922 built from the pinned pieces.
+ *   - The quantizer and the counter-based RNG have no counterpart in the
+ *     reference (it ships neither); they define the synthetic inputs.
+ */
+#ifndef MOE_ORACLE_H
+#define MOE_ORACLE_H
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define OR_QK 256
+#define OR_Q4K_BYTES 144
+#define OR_Q6K_BYTES 210
+#define OR_TYPE_Q4_K 12
+#define OR_TYPE_Q6_K 14
+
+/* ---- fp16 codec (quant.c:4-24) and the quantizer's fp32->fp16 (RNE) ---- */
+float    or_fp16_to_fp32(uint16_t h);
+uint16_t or_fp32_to_fp16(float f);
+
+/* ---- block dequant (quant.c:26-92) ---- */
+void or_dequant_q4k(const void *src, float *dst, size_t n);
+void or_dequant_q6k(const void *src, float *dst, size_t n);
+size_t or_row_bytes(int type, size_t n_cols);
+
+/* ---- quantizer (new; the reference has none) ---- */
+void or_quantize_q4k(const float *x, void *dst, size_t n);
+void or_quantize_q6k(const float *x, void *dst, size_t n);
+
+/* ---- counter-based N(0, sigma) generator (new) ---- */
+uint64_t or_splitmix64(uint64_t x);
+uint64_t or_stream(int layer, int expert, int kind);
+double   or_det_log(double s);
+double   or_normal(uint64_t seed, uint64_t stream, uint64_t index);
+void     or_fill_normal(uint64_t seed, uint64_t stream, uint64_t first,
+                        size_t n, double sigma, float *dst, int n_threads);
+/* Generate + quantize one [rows x cols] matrix of a synthetic tensor. */
+void     or_gen_matrix(uint64_t seed, uint64_t stream, int type, int rows,
+                       int cols, double sigma, void *dst, int n_threads);
+
+/* ---- routing pieces (infer.m:369-383, 920-991) ---- */
+float or_sigmoidf(float x);
+void  or_silu_mul(const float *g, const float *u, float *o, int d);
+void  or_rms_norm(const float *x, const float *w, float *o, int d, float eps);
+void  or_route(const float *logits, const float *bias, int n_experts,
+               int n_group, int topk_group, int K, float routed_scale,
+               int *exp_idx, float *exp_w);
+
+/* ---- dense pieces ---- */
+/* y[r] = sum_k W[r,k] x[k] over quantized rows; acc_double selects fp64
+ * accumulation (tight golden) or a left-to-right fp32 loop (order-only). */
+void or_qmatvec(const void *W, int type, int rows, int cols, const float *x,
+                float *y, int acc_double, int n_threads);
+void or_router_logits(const float *Wr, const float *x, int n_experts, int H,
+                      float *logits, int acc_double);
+/* One SwiGLU expert (infer.m:1069-1091): eo = Wd (silu(Wg x) * (Wu x)). */
+void or_expert_forward(const void *gate, const void *up, const void *down,
+                       int down_type, const float *x, int H, int I,
+                       float *eo, int acc_double, int n_threads);
+
+/* ---- one MoE layer for B tokens (infer.m:1878-1922, attention = identity) --
+ * experts: pointer table of (n_experts + 1) expert blobs; entry n_experts is
+ * the shared expert.  Each blob is [gate Q4_K][up Q4_K][down Q4_K|Q6_K].
+ * force_idx/force_w (may be NULL) replace the oracle's own routing, so the
+ * expert math can be compared on the GPU's routing after a near-tie.
+ * out[b] = sum_k w_k eo_k (slot order) + shared.  idx/w outputs optional. */
+typedef struct {
+    int H, I, n_experts, n_group, topk_group, K;
+    float routed_scale;
+    int down_type;       /* 12 (Q4_K) or 14 (Q6_K) */
+} or_layer_cfg;
+
+void or_moe_layer(const or_layer_cfg *cfg, const void *const *experts,
+                  const float *router_w, const float *bias, const float *x,
+                  int B, const int *force_idx, const float *force_w,
+                  float *out, int *idx_out, float *w_out, float *logits_out,
+                  int acc_double, int n_threads);
+
+size_t or_expert_bytes(int H, int I, int down_type);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,231 @@
+"""ctypes bindings for the CPU checker (oracle/liboracle.so) and for the
+reference's own code built in place (oracle/_ref/libref_moe.so).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and the
+cpu_baseline leg of bench.py, never by the product package.
+"""
+from __future__ import annotations
+
+import ctypes as C  # noqa: N812
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+REF_PATH = os.path.join(HERE, "_ref", "libref_moe.so")
+
+TYPE_Q4_K = 12
+TYPE_Q6_K = 14
+QK = 256
+BLOCK_BYTES = {TYPE_Q4_K: 144, TYPE_Q6_K: 210}
+# synthetic tensor kinds (stream ids), shared with the CUDA library's generator
+KIND_GATE, KIND_UP, KIND_DOWN, KIND_ROUTER, KIND_BIAS, KIND_NORM, KIND_ACT = range(7)
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_u8p = np.ctypeslib.ndpointer(np.uint8, flags="C_CONTIGUOUS")
+
+
+def build():
+    """Compile the checker (and the reference, when its sources are present)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+class LayerCfg(C.Structure):
+    _fields_ = [("H", C.c_int), ("I", C.c_int), ("n_experts", C.c_int), ("n_group", C.c_int),
+                ("topk_group", C.c_int), ("K", C.c_int), ("routed_scale", C.c_float),
+                ("down_type", C.c_int)]
+
+
+_lib = None
+_ref = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = C.CDLL(LIB_PATH)
+        L.or_fp16_to_fp32.restype = C.c_float
+        L.or_fp16_to_fp32.argtypes = [C.c_uint16]
+        L.or_fp32_to_fp16.restype = C.c_uint16
+        L.or_fp32_to_fp16.argtypes = [C.c_float]
+        for fn in (L.or_dequant_q4k, L.or_dequant_q6k):
+            fn.restype = None
+            fn.argtypes = [_u8p, _f32p, C.c_size_t]
+        L.or_quantize_q4k.argtypes = [_f32p, _u8p, C.c_size_t]
+        L.or_quantize_q6k.argtypes = [_f32p, _u8p, C.c_size_t]
+        L.or_splitmix64.restype = C.c_uint64
+        L.or_splitmix64.argtypes = [C.c_uint64]
+        L.or_stream.restype = C.c_uint64
+        L.or_stream.argtypes = [C.c_int, C.c_int, C.c_int]
+        L.or_det_log.restype = C.c_double
+        L.or_det_log.argtypes = [C.c_double]
+        L.or_normal.restype = C.c_double
+        L.or_normal.argtypes = [C.c_uint64, C.c_uint64, C.c_uint64]
+        L.or_fill_normal.argtypes = [C.c_uint64, C.c_uint64, C.c_uint64, C.c_size_t, C.c_double, _f32p, C.c_int]
+        L.or_gen_matrix.argtypes = [C.c_uint64, C.c_uint64, C.c_int, C.c_int, C.c_int, C.c_double, _u8p, C.c_int]
+        L.or_sigmoidf.restype = C.c_float
+        L.or_sigmoidf.argtypes = [C.c_float]
+        L.or_silu_mul.argtypes = [_f32p, _f32p, _f32p, C.c_int]
+        L.or_rms_norm.argtypes = [_f32p, C.c_void_p, _f32p, C.c_int, C.c_float]
+        L.or_route.argtypes = [_f32p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, _i32p, _f32p]
+        L.or_qmatvec.argtypes = [_u8p, C.c_int, C.c_int, C.c_int, _f32p, _f32p, C.c_int, C.c_int]
+        L.or_router_logits.argtypes = [_f32p, _f32p, C.c_int, C.c_int, _f32p, C.c_int]
+        L.or_expert_forward.argtypes = [_u8p, _u8p, _u8p, C.c_int, _f32p, C.c_int, C.c_int, _f32p, C.c_int, C.c_int]
+        L.or_expert_bytes.restype = C.c_size_t
+        L.or_expert_bytes.argtypes = [C.c_int, C.c_int, C.c_int]
+        L.or_moe_layer.argtypes = [C.POINTER(LayerCfg), C.POINTER(C.c_void_p), _f32p, C.c_void_p, _f32p, C.c_int,
+                                   C.c_void_p, C.c_void_p, _f32p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                   C.c_int, C.c_int]
+        _lib = L
+    return _lib
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_PATH)
+
+
+def ref():
+    """The reference's own quant.c / route() / silu_mul / rms_norm."""
+    global _ref
+    if _ref is None:
+        R = C.CDLL(REF_PATH)
+        R.fp16_to_fp32.restype = C.c_float
+        R.fp16_to_fp32.argtypes = [C.c_uint16]
+        R.dequantize_row_q4_K.argtypes = [_u8p, _f32p, C.c_size_t]
+        R.dequantize_row_q6_K.argtypes = [_u8p, _f32p, C.c_size_t]
+        R.ref_sigmoidf.restype = C.c_float
+        R.ref_sigmoidf.argtypes = [C.c_float]
+        R.ref_silu_mul.argtypes = [_f32p, _f32p, _f32p, C.c_int]
+        R.ref_rms_norm.argtypes = [_f32p, C.c_void_p, _f32p, C.c_int]
+        R.ref_route.argtypes = [_f32p, C.c_void_p, C.c_int, _i32p, _f32p]
+        R.ref_moe_token_cpu.restype = C.c_int
+        R.ref_moe_token_cpu.argtypes = [C.POINTER(C.c_void_p), C.c_int, _f32p, _f32p, _f32p, C.c_int, _f32p,
+                                        C.c_void_p, C.c_void_p, C.c_int]
+        _ref = R
+    return _ref
+
+
+def _ptr(a):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+# ---------------------------------------------------------------- wrappers
+def row_bytes(qtype: int, cols: int) -> int:
+    return cols // QK * BLOCK_BYTES[qtype]
+
+
+def dequant(blob: np.ndarray, qtype: int, n: int) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    b = np.ascontiguousarray(blob, dtype=np.uint8)
+    (lib().or_dequant_q6k if qtype == TYPE_Q6_K else lib().or_dequant_q4k)(b, out, n)
+    return out
+
+
+def ref_dequant(blob: np.ndarray, qtype: int, n: int) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    b = np.ascontiguousarray(blob, dtype=np.uint8)
+    (ref().dequantize_row_q6_K if qtype == TYPE_Q6_K else ref().dequantize_row_q4_K)(b, out, n)
+    return out
+
+
+def quantize(x: np.ndarray, qtype: int) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1)
+    out = np.empty(x.size // QK * BLOCK_BYTES[qtype], np.uint8)
+    (lib().or_quantize_q6k if qtype == TYPE_Q6_K else lib().or_quantize_q4k)(x, out, x.size)
+    return out
+
+
+def stream(layer: int, expert: int, kind: int) -> int:
+    return lib().or_stream(layer, expert, kind)
+
+
+def normal(seed: int, strm: int, n: int, sigma: float = 1.0, first: int = 0, threads: int = 8) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    lib().or_fill_normal(seed, strm, first, n, sigma, out, threads)
+    return out
+
+
+def gen_matrix(seed: int, strm: int, qtype: int, rows: int, cols: int, sigma: float, threads: int = 8):
+    out = np.empty(rows * row_bytes(qtype, cols), np.uint8)
+    lib().or_gen_matrix(seed, strm, qtype, rows, cols, sigma, out, threads)
+    return out
+
+
+def gen_expert(seed: int, layer: int, expert: int, H: int, I: int, down_type: int, sigma: float = 0.02,
+               threads: int = 8) -> np.ndarray:
+    """[gate Q4_K][up Q4_K][down] blob of one synthetic expert."""
+    g = gen_matrix(seed, stream(layer, expert, KIND_GATE), TYPE_Q4_K, I, H, sigma, threads)
+    u = gen_matrix(seed, stream(layer, expert, KIND_UP), TYPE_Q4_K, I, H, sigma, threads)
+    d = gen_matrix(seed, stream(layer, expert, KIND_DOWN), down_type, H, I, sigma, threads)
+    return np.concatenate([g, u, d])
+
+
+def expert_bytes(H: int, I: int, down_type: int) -> int:
+    return lib().or_expert_bytes(H, I, down_type)
+
+
+def route(logits, bias, n_group=8, topk_group=4, K=8, scale=2.5):
+    logits = np.ascontiguousarray(logits, np.float32)
+    E = logits.size
+    idx = np.zeros(K, np.int32)
+    w = np.zeros(K, np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    lib().or_route(logits, _ptr(b), E, n_group, topk_group, K, scale, idx, w)
+    return idx, w
+
+
+def ref_route(logits, bias, K=8):
+    logits = np.ascontiguousarray(logits, np.float32)
+    idx = np.zeros(K, np.int32)
+    w = np.zeros(K, np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    ref().ref_route(logits, _ptr(b), K, idx, w)
+    return idx, w
+
+
+def qmatvec(W, qtype, rows, cols, x, acc_double=True, threads=8):
+    y = np.empty(rows, np.float32)
+    lib().or_qmatvec(np.ascontiguousarray(W, np.uint8), qtype, rows, cols,
+                     np.ascontiguousarray(x, np.float32), y, int(acc_double), threads)
+    return y
+
+
+def expert_forward(blob, H, I, down_type, x, acc_double=True, threads=8):
+    gb = row_bytes(TYPE_Q4_K, H) * I
+    blob = np.ascontiguousarray(blob, np.uint8)
+    eo = np.empty(H, np.float32)
+    lib().or_expert_forward(blob[:gb], blob[gb:2 * gb], blob[2 * gb:], down_type,
+                            np.ascontiguousarray(x, np.float32), H, I, eo, int(acc_double), threads)
+    return eo
+
+
+def moe_layer(cfg: dict, experts: dict, router_w, bias, x, force_idx=None, force_w=None,
+              acc_double=True, threads=8):
+    """experts: {expert_id: blob}; only the ids the routing touches (and the
+    shared expert, id n_experts) need to be present."""
+    E = cfg["n_experts"]
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, cfg["H"])
+    B = x.shape[0]
+    c = LayerCfg(cfg["H"], cfg["I"], E, cfg["n_group"], cfg["topk_group"], cfg["K"],
+                 cfg["routed_scale"], cfg["down_type"])
+    table = (C.c_void_p * (E + 1))()
+    keep = []
+    for e, blob in experts.items():
+        blob = np.ascontiguousarray(blob, np.uint8)
+        keep.append(blob)
+        table[e] = blob.ctypes.data
+    out = np.empty((B, cfg["H"]), np.float32)
+    idx = np.empty((B, cfg["K"]), np.int32)
+    w = np.empty((B, cfg["K"]), np.float32)
+    logits = np.empty((B, E), np.float32)
+    fi = None if force_idx is None else np.ascontiguousarray(force_idx, np.int32)
+    fw = None if force_w is None else np.ascontiguousarray(force_w, np.float32)
+    lib().or_moe_layer(C.byref(c), table, np.ascontiguousarray(router_w, np.float32),
+                       _ptr(None if bias is None else np.ascontiguousarray(bias, np.float32)), x, B,
+                       _ptr(fi), _ptr(fw), out, _ptr(idx), _ptr(w), _ptr(logits), int(acc_double), threads)
+    return out, idx, w, logits

@@ -1,0 +1,284 @@
+"""GPU parity of the MoE block against the oracle (pinned to the reference's
+quant.c and route()), through the C ABI of libmoe_cuda.so.
+
+Tolerances (north star): routing index sets identical except for swaps whose
+choice scores lie within 1e-6 of the selection boundary; expert / layer
+outputs within normwise relative error 2e-3 = max|gpu - ref| / max|ref|.  A
+second, much tighter bound (1e-4) guards against regressions: the kernels
+use exact products and fp32 accumulation, so only summation order differs.
+"""
+import numpy as np
+import pytest
+
+TOL = 2e-3
+GUARD = 1e-4
+
+
+def rel_err(a, b):
+    return float(np.max(np.abs(a - b)) / max(np.max(np.abs(b)), 1e-30))
+
+
+def small_cfg(**kw):
+    from flash_deepseek_b200 import MoeConfig
+    base = dict(hidden=1024, intermediate=2048, n_experts=16, n_group=4, topk_group=2, top_k=4, n_layers=3,
+                max_tokens=16)
+    base.update(kw)
+    return MoeConfig(**base)
+
+
+def oracle_cfg(cfg, down_type):
+    return dict(H=cfg.hidden, I=cfg.intermediate, n_experts=cfg.n_experts, n_group=cfg.n_group,
+                topk_group=cfg.topk_group, K=cfg.top_k, routed_scale=cfg.routed_scale, down_type=down_type)
+
+
+def router_of(oracle, seed, layer, cfg, sigma=0.006, bsigma=0.01):
+    O = oracle
+    W = O.normal(seed, O.stream(layer, 0, O.KIND_ROUTER), cfg.n_experts * cfg.hidden, sigma).reshape(
+        cfg.n_experts, cfg.hidden)
+    b = O.normal(seed, O.stream(layer, 0, O.KIND_BIAS), cfg.n_experts, bsigma)
+    return W, b
+
+
+def check_routing(oracle, cfg, logits, bias, idx_gpu, w_gpu):
+    """Index sets equal up to near ties (1e-6); weights equal by index."""
+    for t in range(len(idx_gpu)):
+        idx_o, w_o = oracle.route(logits[t], bias, cfg.n_group, cfg.topk_group, cfg.top_k, cfg.routed_scale)
+        sg, so = set(idx_gpu[t].tolist()), set(idx_o.tolist())
+        if sg != so:
+            choice = 1.0 / (1.0 + np.exp(-logits[t].astype(np.float64))) + bias
+            kth = np.sort(choice[list(so)])[0]
+            for e in sg ^ so:
+                assert abs(choice[e] - kth) < 1e-6, (t, sorted(sg), sorted(so))
+            continue
+        wo = dict(zip(idx_o.tolist(), w_o.tolist()))
+        for e, w in zip(idx_gpu[t].tolist(), w_gpu[t].tolist()):
+            assert abs(w - wo[e]) <= 1e-6 * max(1.0, abs(wo[e])), (t, e)
+
+
+def oracle_layer(oracle, m, cfg, layer, down_type, h, idx, w, router, bias):
+    needed = sorted(set(np.asarray(idx).reshape(-1).tolist()))
+    experts = {e: m.read_expert(layer, e) for e in needed}
+    experts[cfg.n_experts] = m.read_expert(layer, cfg.n_experts)
+    out, _, _, _ = oracle.moe_layer(oracle_cfg(cfg, down_type), experts, router, bias, h, force_idx=idx,
+                                    force_w=w)
+    return out
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("down_type", [12, 14])
+@pytest.mark.parametrize("T", [1, 5, 16])
+def test_small_layer_parity(cuda_lib, oracle, down_type, T):
+    cfg = small_cfg(intermediate=2048 if down_type == 14 else 512)
+    m = cuda_lib.MoE(cfg)
+    m.init_layer_synthetic(0, seed=11, down_type=down_type)
+    router, bias = router_of(oracle, 11, 0, cfg)
+    h = oracle.normal(3, oracle.stream(0, 0, oracle.KIND_ACT), T * cfg.hidden, 1.0).reshape(T, cfg.hidden)
+    out, idx, w = m.forward(0, h)
+    logits = np.stack([router.astype(np.float64) @ h[t].astype(np.float64) for t in range(T)]).astype(np.float32)
+    check_routing(oracle, cfg, logits, bias, idx, w)
+    ref = oracle_layer(oracle, m, cfg, 0, down_type, h, idx, w, router, bias)
+    e = rel_err(out, ref)
+    assert e < TOL and e < GUARD, e
+    m.close()
+
+
+@pytest.mark.gpu
+def test_loaded_bytes_match_synthetic(cuda_lib, oracle):
+    """moe_load_layer (host GGUF bytes) and moe_init_layer_synthetic give the
+    same outputs for the same weights."""
+    cfg = small_cfg()
+    H, I, E = cfg.hidden, cfg.intermediate, cfg.n_experts
+    O = oracle
+    blobs = [O.gen_expert(2, 0, e, H, I, 14) for e in range(E + 1)]
+    gb, db = O.row_bytes(12, H) * I, O.row_bytes(14, I) * H
+    gate = np.concatenate([b[:gb] for b in blobs[:E]])
+    up = np.concatenate([b[gb:2 * gb] for b in blobs[:E]])
+    down = np.concatenate([b[2 * gb:] for b in blobs[:E]])
+    router, bias = router_of(O, 2, 0, cfg)
+    a = cuda_lib.MoE(cfg)
+    a.load_layer(0, gate, up, down, 14, router, bias, blobs[E][:gb], blobs[E][gb:2 * gb], blobs[E][2 * gb:], 14)
+    b = cuda_lib.MoE(cfg)
+    b.init_layer_synthetic(0, seed=2, down_type=14)
+    h = O.normal(9, O.stream(0, 1, O.KIND_ACT), 4 * H, 1.0).reshape(4, H)
+    oa, ia, wa = a.forward(0, h)
+    ob, ib, wb = b.forward(0, h)
+    assert np.array_equal(ia, ib) and np.array_equal(oa.view(np.uint32), ob.view(np.uint32))
+    # packed per-layer file format (packed_experts/layer_XX.bin)
+    c = cuda_lib.MoE(cfg)
+    packed = np.concatenate(blobs[:E])
+    c.load_layer_packed(0, packed, 2 * gb + db, router, bias, blobs[E][:gb], blobs[E][gb:2 * gb], blobs[E][2 * gb:],
+                        14)
+    oc, ic, _ = c.forward(0, h)
+    assert np.array_equal(ic, ia) and np.array_equal(oc.view(np.uint32), oa.view(np.uint32))
+    for x in (a, b, c):
+        x.close()
+
+
+@pytest.mark.gpu
+def test_experts_and_shared_entry_points(cuda_lib, oracle):
+    cfg = small_cfg()
+    m = cuda_lib.MoE(cfg)
+    m.init_layer_synthetic(0, seed=4, down_type=14)
+    H, I = cfg.hidden, cfg.intermediate
+    h = oracle.normal(4, oracle.stream(0, 2, oracle.KIND_ACT), 3 * H, 1.0).reshape(3, H)
+    idx = np.array([[0, 5, 9, 15], [1, 2, 3, 4], [15, 14, 13, 12]], np.int32)
+    w = np.array([[0.5, 0.25, 1.0, 0.75]] * 3, np.float32)
+    moe_out = m.experts_forward(0, h, idx, w)
+    sd = m.shared_forward(0, h)
+    for t in range(3):
+        ref = np.zeros(H, np.float32)
+        for k in range(4):
+            ref += w[t, k] * oracle.expert_forward(m.read_expert(0, int(idx[t, k])), H, I, 14, h[t])
+        assert rel_err(moe_out[t], ref) < GUARD
+        rs = oracle.expert_forward(m.read_expert(0, cfg.n_experts), H, I, 14, h[t])
+        assert rel_err(sd[t], rs) < GUARD
+    m.close()
+
+
+@pytest.mark.gpu
+def test_route_entry_point_golden(cuda_lib):
+    """moe_route reproduces the reference route() (golden vectors produced by
+    the reference itself), slot order included; near-tie cases may differ
+    only by swaps within 1e-6."""
+    import os
+    from flash_deepseek_b200 import MoeConfig
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "route_golden.npz"))
+    m = cuda_lib.MoE(MoeConfig(max_tokens=1, n_layers=1, intermediate=256, hidden=256))
+    L, B, I, W = g["logits"], g["bias"], g["idx"], g["w"]
+    exact = 0
+    for i in range(len(L)):
+        idx, w = m.route(L[i][None], B[i])
+        if np.array_equal(idx[0], I[i]):
+            exact += 1
+            assert np.allclose(w[0], W[i], rtol=1e-6, atol=0)
+        else:
+            choice = 1.0 / (1.0 + np.exp(-L[i].astype(np.float64))) + B[i]
+            kth = np.sort(choice[I[i]])[0]
+            for e in set(idx[0].tolist()) ^ set(I[i].tolist()):
+                assert abs(choice[e] - kth) < 1e-6, i
+    assert exact >= len(L) - 20
+    m.close()
+
+
+@pytest.mark.gpu
+def test_config1_single_expert_full_size(cuda_lib, oracle):
+    """Config 1: one Q4_K expert SwiGLU, hidden 7168, intermediate 2048, one
+    token, against quant.c dequant + dot (through the oracle)."""
+    from flash_deepseek_b200 import MoeConfig
+    cfg = MoeConfig(n_layers=1, max_tokens=1, top_k=1, topk_group=1)
+    m = cuda_lib.MoE(cfg)
+    m.init_layer_synthetic(0, seed=0, down_type=12)
+    x = oracle.normal(0, oracle.stream(0, 0, oracle.KIND_ACT), 7168, 1.0)
+    for e in (0, 255):
+        out = m.experts_forward(0, x[None], np.array([[e]], np.int32), np.array([[1.0]], np.float32))[0]
+        ref = oracle.expert_forward(m.read_expert(0, e), 7168, 2048, 12, x)
+        ref32 = oracle.expert_forward(m.read_expert(0, e), 7168, 2048, 12, x, acc_double=False)
+        err = rel_err(out, ref)
+        assert err < TOL and err < GUARD, err
+        assert rel_err(ref32, ref) < GUARD
+    m.close()
+
+
+@pytest.mark.gpu
+def test_config2_layer_b1(cuda_lib, oracle):
+    """Config 2: one DeepSeek-V3 layer, decode batch 1, Q4_K gate/up, Q6_K
+    down, 256 + 1 experts."""
+    from flash_deepseek_b200 import MoeConfig
+    cfg = MoeConfig(n_layers=1, max_tokens=1)
+    m = cuda_lib.MoE(cfg)
+    m.init_layer_synthetic(0, seed=0, down_type=14)
+    router, bias = router_of(oracle, 0, 0, cfg)
+    h = oracle.normal(0, oracle.stream(0, 0, oracle.KIND_ACT), 7168, 1.0)[None]
+    out, idx, w = m.forward(0, h)
+    logits = (router.astype(np.float64) @ h[0].astype(np.float64)).astype(np.float32)[None]
+    check_routing(oracle, cfg, logits, bias, idx, w)
+    ref = oracle_layer(oracle, m, cfg, 0, 14, h, idx, w, router, bias)
+    err = rel_err(out, ref)
+    assert err < TOL and err < GUARD, err
+    assert m.last_weight_bytes() == 8 * 28557312 + 28557312 + 256 * 7168 * 4 + 256 * 4
+    m.close()
+
+
+def zipf_bias(n=256, s=1.1, seed=0):
+    """Zipf(s) expert-load skew: a seeded rank permutation pi and
+    bias_e = log(n * p_pi(e)), p_r proportional to r^-s."""
+    rng = np.random.default_rng(seed)
+    p = np.arange(1, n + 1, dtype=np.float64) ** -s
+    p /= p.sum()
+    return np.log(n * p[rng.permutation(n)]).astype(np.float32)
+
+
+@pytest.mark.gpu
+def test_config3_shape_b64_zipf(cuda_lib, oracle):
+    """Config 3 on one GPU: decode batch 64, Zipf-skewed router; routing of all
+    64 tokens and outputs of a sample of tokens against the oracle."""
+    from flash_deepseek_b200 import MoeConfig
+    cfg = MoeConfig(n_layers=1, max_tokens=64)
+    m = cuda_lib.MoE(cfg)
+    m.init_layer_synthetic(0, seed=0, down_type=14)
+    zb = zipf_bias()
+    m.add_router_bias(0, zb)
+    router, bias = router_of(oracle, 0, 0, cfg)
+    bias = bias + zb
+    h = oracle.normal(0, oracle.stream(0, 0, oracle.KIND_ACT), 64 * 7168, 1.0).reshape(64, 7168)
+    out, idx, w = m.forward(0, h)
+    logits = (h.astype(np.float64) @ router.astype(np.float64).T).astype(np.float32)
+    check_routing(oracle, cfg, logits, bias, idx, w)
+    counts = np.bincount(idx.reshape(-1), minlength=256)
+    assert counts.max() >= 8  # skew reaches multi-chunk experts
+    sample = [0, 17, 42, 63]
+    ref = oracle_layer(oracle, m, cfg, 0, 14, h[sample], idx[sample], w[sample], router, bias)
+    err = rel_err(out[sample], ref)
+    assert err < TOL and err < GUARD, err
+    # token independence: a token's output does not depend on its batch mates
+    o1, i1, _ = m.forward(0, h[17:18])
+    assert np.array_equal(i1[0], idx[17]) and rel_err(o1[0], out[17]) < 1e-6
+    m.close()
+
+
+@pytest.mark.gpu
+def test_stack_chaining(cuda_lib, oracle):
+    """Config 4 chaining on a small shape: per layer RMSNorm (eps 1e-6) then
+    hidden += MoE(h_post), attention = identity."""
+    cfg = small_cfg(n_layers=3)
+    m = cuda_lib.MoE(cfg)
+    H = cfg.hidden
+    norms = []
+    for L in range(3):
+        m.init_layer_synthetic(L, seed=5, down_type=14 if L % 2 == 0 else 12)
+        nw = (1.0 + 0.1 * oracle.normal(5, oracle.stream(L, 0, oracle.KIND_NORM), H, 1.0)).astype(np.float32)
+        m.set_norm_weight(L, nw)
+        norms.append(nw)
+    h0 = oracle.normal(6, oracle.stream(0, 0, oracle.KIND_ACT), 2 * H, 1.0).reshape(2, H)
+    got = m.forward_stack(0, 3, h0)
+    hid = h0.copy()
+    for L in range(3):
+        post = np.empty_like(hid)
+        for t in range(2):
+            r = np.empty(H, np.float32)
+            oracle.lib().or_rms_norm(np.ascontiguousarray(hid[t]), norms[L].ctypes.data, r, H, 1e-6)
+            post[t] = r
+        _, idx, w = m.forward(L, post)
+        router, bias = router_of(oracle, 5, L, cfg)
+        moe = oracle_layer(oracle, m, cfg, L, 14 if L % 2 == 0 else 12, post, idx, w, router, bias)
+        hid = hid + moe
+    assert rel_err(got, hid) < GUARD
+    m.close()
+
+
+@pytest.mark.gpu
+def test_errors_are_reported(cuda_lib):
+    cfg = small_cfg()
+    m = cuda_lib.MoE(cfg)
+    with pytest.raises(cuda_lib.MoeError):
+        m.forward(0, np.zeros((1, cfg.hidden), np.float32))  # layer not loaded
+    m.init_layer_synthetic(0, seed=1, down_type=14)
+    with pytest.raises(cuda_lib.MoeError):
+        m.forward(0, np.zeros((cfg.max_tokens + 1, cfg.hidden), np.float32))
+    with pytest.raises(cuda_lib.MoeError):
+        m.experts_forward(0, np.zeros((1, cfg.hidden), np.float32), np.array([[99, 0, 1, 2]], np.int32),
+                          np.ones((1, 4), np.float32))
+    # the context stays usable after an error
+    out, _, _ = m.forward(0, np.ones((1, cfg.hidden), np.float32))
+    assert np.all(np.isfinite(out))
+    m.close()

@@ -1,0 +1,133 @@
+"""CPU: pins the oracle (the checker) against the reference's own outputs --
+golden fixtures made by tests/golden/make_golden.py from gguf-py and from the
+reference's quant.c / route() built in place -- and, where the reference
+build is present, against it directly."""
+import os
+
+import numpy as np
+import pytest
+
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+
+
+def gold(name):
+    return np.load(os.path.join(GOLD, name))
+
+
+def test_fp16_all_patterns(oracle):
+    t = gold("fp16_table.npz")["bits"]
+    L = oracle.lib()
+    mine = np.array([L.or_fp16_to_fp32(h) for h in range(65536)], np.float32).view(np.uint32)
+    assert np.array_equal(mine, t)
+
+
+@pytest.mark.parametrize("name,qtype", [("dequant_q4k.npz", 12), ("dequant_q6k.npz", 14)])
+def test_dequant_golden(oracle, name, qtype):
+    g = gold(name)
+    blocks, exp = g["blocks"], g["expected"]
+    got = oracle.dequant(blocks.reshape(-1), qtype, exp.size).reshape(exp.shape)
+    assert np.array_equal(got.view(np.uint32), exp.view(np.uint32))
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(os.path.dirname(GOLD), "..", "oracle", "_ref", "libref_moe.so")),
+                    reason="reference build not present")
+@pytest.mark.parametrize("qtype,bsz", [(12, 144), (14, 210)])
+def test_dequant_vs_reference_random(oracle, qtype, bsz):
+    rng = np.random.default_rng(qtype)
+    b = rng.integers(0, 256, size=(4096, bsz), dtype=np.uint8)
+    off = 0 if qtype == 12 else 208
+    b[:, off:off + 2] = (rng.standard_normal(4096) * 1e-2).astype(np.float16).view(np.uint8).reshape(-1, 2)
+    a = oracle.dequant(b.reshape(-1), qtype, 4096 * 256)
+    r = oracle.ref_dequant(b.reshape(-1), qtype, 4096 * 256)
+    assert np.array_equal(a.view(np.uint32), r.view(np.uint32))
+
+
+def test_route_golden(oracle):
+    g = gold("route_golden.npz")
+    for i in range(len(g["logits"])):
+        idx, w = oracle.route(g["logits"][i], g["bias"][i])
+        assert np.array_equal(idx, g["idx"][i]), i
+        assert np.array_equal(w.view(np.uint32), g["w"][i].view(np.uint32)), i
+
+
+@pytest.mark.skipif(not os.path.exists(os.path.join(os.path.dirname(GOLD), "..", "oracle", "_ref", "libref_moe.so")),
+                    reason="reference build not present")
+def test_route_vs_reference_random(oracle):
+    rng = np.random.default_rng(7)
+    for _ in range(500):
+        lg = (rng.standard_normal(256) * rng.uniform(0.1, 4)).astype(np.float32)
+        b = (rng.standard_normal(256) * 0.01).astype(np.float32)
+        i1, w1 = oracle.route(lg, b)
+        i2, w2 = oracle.ref_route(lg, b)
+        assert np.array_equal(i1, i2) and np.array_equal(w1.view(np.uint32), w2.view(np.uint32))
+
+
+def test_activation_golden(oracle):
+    g = gold("act_golden.npz")
+    L = oracle.lib()
+    o = np.empty_like(g["g"])
+    L.or_silu_mul(g["g"], g["u"], o, o.size)
+    assert np.array_equal(o.view(np.uint32), g["silu"].view(np.uint32))
+    x, nw = g["x"], g["norm_w"]
+    r = np.empty_like(x)
+    L.or_rms_norm(x, nw.ctypes.data, r, r.size, 1e-6)
+    assert np.array_equal(r.view(np.uint32), g["rms"].view(np.uint32))
+    s = np.array([L.or_sigmoidf(float(v)) for v in g["sig_in"]], np.float32)
+    assert np.array_equal(s.view(np.uint32), g["sig"].view(np.uint32))
+
+
+def test_synth_golden(oracle):
+    g = gold("synth_golden.npz")
+    O = oracle
+    assert np.array_equal(O.gen_matrix(0, O.stream(0, 0, O.KIND_GATE), O.TYPE_Q4_K, 1, 1024, 0.02), g["gate_q4k"])
+    assert np.array_equal(O.gen_matrix(0, O.stream(0, 0, O.KIND_DOWN), O.TYPE_Q6_K, 1, 1024, 0.02), g["down_q6k"])
+    assert np.array_equal(O.normal(0, O.stream(0, 0, O.KIND_ROUTER), 64, 0.006).view(np.uint32),
+                          g["router"].view(np.uint32))
+
+
+def test_generator_statistics(oracle):
+    x = oracle.normal(0, oracle.stream(1, 2, 3), 400000, 0.02)
+    assert abs(x.mean()) < 2e-4 and abs(x.std() - 0.02) < 2e-4
+    y = oracle.normal(0, oracle.stream(1, 2, 4), 400000, 0.02)
+    assert abs(np.corrcoef(x, y)[0, 1]) < 0.01
+    z = oracle.normal(1, oracle.stream(1, 2, 3), 400000, 0.02)
+    assert not np.array_equal(x, z)
+    # deterministic and position-addressable
+    part = oracle.normal(0, oracle.stream(1, 2, 3), 1000, 0.02, first=5000)
+    assert np.array_equal(part, x[5000:6000])
+
+
+def test_det_log(oracle):
+    L = oracle.lib()
+    for s in np.concatenate([np.linspace(1e-12, 1.0, 997), [2.0 ** -62, 0.5, 0.7071067811865476]]):
+        assert abs(L.or_det_log(float(s)) - np.log(s)) <= 4e-16 * max(1.0, abs(np.log(s)))
+
+
+@pytest.mark.parametrize("qtype", [12, 14])
+def test_quantizer_roundtrip(oracle, qtype):
+    rng = np.random.default_rng(3)
+    x = (rng.standard_normal(256 * 512) * 0.02).astype(np.float32)
+    x[:256] = 0.0                      # all-zero super-block
+    x[256:512] = np.abs(x[256:512])    # all positive (min clamps to 0)
+    q = oracle.quantize(x, qtype)
+    y = oracle.dequant(q, qtype, x.size)
+    assert np.all(y[:256] == 0.0)
+    rel = np.sqrt(np.mean((y - x) ** 2)) / np.sqrt(np.mean(x ** 2))
+    assert rel < (0.1 if qtype == 12 else 0.03), rel
+    # every reconstructed value is within one quantization step of the input
+    blocks = x.reshape(-1, 256)
+    err = np.abs(y - x).reshape(-1, 256).max(axis=1)
+    span = blocks.max(axis=1) - np.minimum(blocks.min(axis=1), 0)
+    assert np.all(err <= span / 4 + 1e-6)
+
+
+def test_expert_forward_precision_variants(oracle):
+    """fp32 and fp64 accumulation of the oracle agree far inside the 2e-3
+    tolerance: the tolerance covers summation order only."""
+    H, I = 512, 512
+    O = oracle
+    blob = O.gen_expert(0, 0, 0, H, I, O.TYPE_Q4_K)
+    x = O.normal(0, O.stream(0, 0, O.KIND_ACT), H, 1.0)
+    a = O.expert_forward(blob, H, I, O.TYPE_Q4_K, x, acc_double=True)
+    b = O.expert_forward(blob, H, I, O.TYPE_Q4_K, x, acc_double=False)
+    assert np.max(np.abs(a - b)) / np.max(np.abs(a)) < 1e-5
