@@ -33,6 +33,8 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
+from flash_deepseek_b200.workloads import zipf_logit_bias  # noqa: E402
+
 METRIC = "MoE decode tokens/s at 1/2/4/8 B200; expert matvec HBM GB/s vs 8 TB/s peak"
 H, I, E, K = 7168, 2048, 256, 8
 Q4_ROW = H // 256 * 144
@@ -44,15 +46,6 @@ WORKLOADS = {
     "decode_b64_zipf": dict(B=64, zipf=True, name="config3_decode_b64_zipf"),
     "decode_b1": dict(B=1, zipf=False, name="config2_decode_b1"),
 }
-
-
-def zipf_bias(n=256, s=1.1, seed=0):
-    """Zipf(s) expert-load skew: a seeded rank permutation pi and
-    bias_e = log(n * p_pi(e)), p_r proportional to r^-s."""
-    rng = np.random.default_rng(seed)
-    p = np.arange(1, n + 1, dtype=np.float64) ** -s
-    p /= p.sum()
-    return np.log(n * p[rng.permutation(n)]).astype(np.float32)
 
 
 def peaks():
@@ -138,14 +131,13 @@ def cpu_reference(workload: str, steps: int, warmup: int, seconds: float = 20.0)
     R = O.ref()
     router = O.normal(0, O.stream(0, 0, O.KIND_ROUTER), E * H, 0.006, threads=threads).reshape(E, H)
     bias = O.normal(0, O.stream(0, 0, O.KIND_BIAS), E, 0.01, threads=threads)
-    if W["zipf"]:
-        bias = (bias + zipf_bias()).astype(np.float32)
+    lbias = zipf_logit_bias() if W["zipf"] else np.zeros(E, np.float32)
     rng = np.random.default_rng(1234)
     n_tok = max(1, steps + warmup)
     xs = rng.standard_normal((n_tok, H)).astype(np.float32)
     need = set()
     for t in range(n_tok):
-        lg = (router.astype(np.float64) @ xs[t].astype(np.float64)).astype(np.float32)
+        lg = (router.astype(np.float64) @ xs[t].astype(np.float64) + lbias).astype(np.float32)
         idx, _ = O.ref_route(lg, bias, K=8)
         need |= set(idx.tolist())
     blobs = {e: O.gen_expert(0, 0, e, H, I, O.TYPE_Q6_K, threads=threads) for e in sorted(need)}
@@ -158,7 +150,7 @@ def cpu_reference(workload: str, steps: int, warmup: int, seconds: float = 20.0)
     times = []
     for t in range(n_tok):
         t0 = time.perf_counter()
-        rc = R.ref_moe_token_cpu(table, 1, router, bias, xs[t], 8, out, None, None, threads)
+        rc = R.ref_moe_token_cpu(table, 1, router, lbias, bias, xs[t], 8, out, None, None, threads)
         dt = time.perf_counter() - t0
         if rc != 0:
             raise RuntimeError(f"ref_moe_token_cpu failed ({rc})")
@@ -191,31 +183,34 @@ def run_ours(args):
         pg = dist
     W = WORKLOADS[args.workload]
     B = W["B"]
-    if world > 1 and B % world:
+    if world > 1 and B > world and B % world:
         raise SystemExit("global batch must divide over the GPUs")
-    b_loc = max(1, B // world)
+    # tokens of this rank: an even share, or (batch < GPUs) one token on the
+    # first B ranks and none elsewhere
+    b_loc = B // world if B >= world else (1 if rank < B else 0)
+    t0_loc = rank * b_loc if B >= world else min(rank, B)
     uid = None
     if world > 1:
         obj = [F.get_unique_id() if rank == 0 else None]
         pg.broadcast_object_list(obj, src=0)
         uid = obj[0]
-    cfg = F.MoeConfig(n_layers=1, max_tokens=b_loc)
+    cfg = F.MoeConfig(n_layers=1, max_tokens=max(1, b_loc), n_experts=args.experts)
     moe = F.MoE(cfg, device=local, rank=rank, world_size=world, unique_id=uid)
     moe.init_layer_synthetic(0, seed=0, down_type=F.TYPE_Q6_K)
     if W["zipf"]:
-        moe.add_router_bias(0, zipf_bias())
+        moe.set_logit_bias(0, zipf_logit_bias(n=args.experts))
 
     dev = torch.device("cuda", local)
     stream = torch.cuda.ExternalStream(moe.stream, device=dev)
     n_pool = 4
     g = torch.Generator(device="cpu").manual_seed(1234)
     pool_h = [torch.randn(B, H, generator=g, dtype=torch.float32) for _ in range(n_pool)]
-    pool = [p[rank * b_loc:(rank + 1) * b_loc].contiguous().to(dev) for p in pool_h]
-    out = torch.empty(b_loc, H, device=dev)
+    pool = [p[t0_loc:t0_loc + b_loc].contiguous().to(dev) for p in pool_h]
+    out = torch.empty(max(1, b_loc), H, device=dev)
     steps_total = args.warmup + args.steps
-    idx_all = torch.empty(steps_total, b_loc, K, dtype=torch.int32, device=dev)
+    idx_all = torch.empty(steps_total, max(1, b_loc), K, dtype=torch.int32, device=dev)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
-    moe.set_timing(True)
+    moe.set_timing(args.steps)
 
     def barrier():
         torch.cuda.synchronize()
@@ -230,6 +225,10 @@ def run_ours(args):
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         return float(t[0])
 
+    clk = Clocks(local).__enter__()
+    t_wait = time.time()
+    while not clk.lines and time.time() - t_wait < 5.0:
+        time.sleep(0.05)
     # ---- device-resident leg (value)
     for s in range(args.warmup):
         with torch.cuda.stream(stream):
@@ -239,48 +238,57 @@ def run_ours(args):
     phases = []
     barrier()
     launches0 = moe.kernel_launches
-    with Clocks(local) as clk:
-        for s in range(args.steps):
-            with torch.cuda.stream(stream):
-                flush.zero_()
-            ev[s][0].record(stream)
-            moe.forward_device(0, pool[(args.warmup + s) % n_pool], b_loc, out, d_idx=idx_all[args.warmup + s])
-            ev[s][1].record(stream)
-            phases.append(moe.timing())
-        barrier()
+    n_clk0 = len(clk.lines)
+    for s in range(args.steps):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+        ev[s][0].record(stream)
+        moe.forward_device(0, pool[(args.warmup + s) % n_pool], b_loc, out, d_idx=idx_all[args.warmup + s])
+        ev[s][1].record(stream)
+    barrier()
+    phases = [moe.timing(back) for back in range(args.steps)]
+    clk_lines_timed = clk.lines[n_clk0:]
     launches = moe.kernel_launches - launches0
     step_ms = [a.elapsed_time(b) for a, b in ev]
     total_ms = max_over_ranks(sum(step_ms))
     value = B * args.steps / (total_ms / 1e3)
 
-    # ---- roofline of the dominant kernel (gate/up GEMV) on this rank
-    idx_h = idx_all[args.warmup:].cpu().numpy()
-    e_lo, e_hi = rank * (E // world), (rank + 1) * (E // world)
+    # ---- roofline of the dominant kernel (gate/up GEMV) on this rank: the
+    # experts it holds that any token of the global batch routes to
+    idx_loc = idx_all[args.warmup:, :b_loc].cpu()
+    if pg:
+        sizes = [None] * world
+        pg.all_gather_object(sizes, idx_loc.numpy())
+        idx_g = np.concatenate([x for x in sizes if x.size], axis=1)
+    else:
+        idx_g = idx_loc.numpy()
+    NE = args.experts
+    e_lo, e_hi = rank * (NE // world), (rank + 1) * (NE // world)
     gu_bytes, dn_bytes, active = [], [], []
     for s in range(args.steps):
-        # experts this rank computes: routed experts it owns hit by any token
-        # of the global batch (idx of the local slice is what we see here;
-        # with world > 1 the owner side is summed in run_ep)
-        hit = set(int(e) for e in np.unique(idx_h[s]) if e_lo <= e < e_hi)
+        mine = (idx_g[s] >= e_lo) & (idx_g[s] < e_hi)
+        hit = set(int(e) for e in np.unique(idx_g[s][mine]))
         n_act = len(hit) + 1
+        rows = int(mine.any(axis=1).sum()) + b_loc
+        pairs = int(mine.sum()) + b_loc
         active.append(n_act)
-        gu_bytes.append(n_act * 2 * GATE_BYTES + b_loc * H * 4 + (b_loc * K + b_loc) * I * 4)
-        dn_bytes.append(n_act * DOWN_Q6_BYTES + (b_loc * K + b_loc) * (I * 4 + H * 4))
+        gu_bytes.append(n_act * 2 * GATE_BYTES + rows * H * 4 + pairs * I * 4)
+        dn_bytes.append(n_act * DOWN_Q6_BYTES + pairs * (I * 4 + H * 4))
     gu_ms = float(np.mean([p["gateup"] for p in phases]))
     dn_ms = float(np.mean([p["down"] for p in phases]))
     peak, peak_kind = peaks()
     ach = float(np.mean(gu_bytes)) / (gu_ms / 1e3) / 1e9
     ach_dn = float(np.mean(dn_bytes)) / (dn_ms / 1e3) / 1e9
-    step_bytes = float(np.mean([a * EXPERT_BYTES for a in active])) + ROUTER_BYTES
+    step_bytes = float(np.mean([a * EXPERT_BYTES for a in active])) + NE * H * 4 + NE * 4
     traffic = traffic_from_profiles("k_gateup", args.workload)
 
     # ---- end-to-end leg through the C ABI with host buffers
-    h_pin = [p[rank * b_loc:(rank + 1) * b_loc].contiguous().pin_memory() for p in pool_h]
-    o_pin = torch.empty(b_loc, H, dtype=torch.float32).pin_memory()
+    h_pin = [p[t0_loc:t0_loc + max(1, b_loc)].contiguous().pin_memory() for p in pool_h]
+    o_pin = torch.empty(max(1, b_loc), H, dtype=torch.float32).pin_memory()
     h_np = [p.numpy() for p in h_pin]
     ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    idx_np = np.empty((b_loc, K), np.int32)
-    w_np = np.empty((b_loc, K), np.float32)
+    idx_np = np.empty((max(1, b_loc), K), np.int32)
+    w_np = np.empty((max(1, b_loc), K), np.float32)
     lib = moe.lib
     o_np = o_pin.numpy()
     for s in range(args.warmup):
@@ -298,6 +306,10 @@ def run_ours(args):
             raise RuntimeError(moe.lib.moe_last_error(moe.ctx))
     barrier()
     e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in ev2))
+    clk.__exit__(None, None, None)
+    if len(clk_lines_timed) < 3:   # timed region shorter than the sampling period
+        clk_lines_timed = clk.lines
+    clk.lines = clk_lines_timed
     e2e = B * args.steps / (e2e_ms / 1e3)
 
     cpu = None
@@ -312,8 +324,8 @@ def run_ours(args):
             "dtype": "fp32 (Q4_K/Q6_K weights decoded exactly to fp16 integers, fp32 accumulation)",
             "data": "synthetic: random-init N(0,0.02) weights quantized on device, N(0,1) tokens",
             "config": {"workload": W["name"], "global_batch": B, "tokens_per_gpu": b_loc, "hidden": H,
-                       "intermediate": I, "experts": E, "top_k": K, "gate_up": "Q4_K", "down": "Q6_K",
-                       "router_skew": "zipf(1.1) bias" if W["zipf"] else "none",
+                       "intermediate": I, "experts": NE, "top_k": K, "gate_up": "Q4_K", "down": "Q6_K",
+                       "router_skew": "zipf(1.1) logit bias" if W["zipf"] else "none",
                        "parallelism": f"ep{world}", "l2": "flushed: 256 MiB write between timed steps"},
             "roofline": {"bound": "hbm", "kernel": "k_gateup (grouped Q4_K gate/up GEMV + SwiGLU)",
                          "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
@@ -365,11 +377,13 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--workload", default="decode_b64_zipf", choices=sorted(WORKLOADS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--experts", type=int, default=E,
+                    help="routed experts (default 256); smaller values only to keep ncu captures small")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3

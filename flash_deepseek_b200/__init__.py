@@ -132,14 +132,17 @@ class MoE:
     def last_weight_bytes(self) -> int:
         return int(self.lib.moe_last_weight_bytes(self.ctx))
 
-    def set_timing(self, enable: bool = True):
-        self._check(self.lib.moe_set_timing(self.ctx, int(enable)), "moe_set_timing")
+    def set_timing(self, ring_steps: int = 1):
+        """Record per-phase CUDA events for the last `ring_steps` forward calls
+        (0 turns timing off)."""
+        self._check(self.lib.moe_set_timing(self.ctx, int(ring_steps)), "moe_set_timing")
 
-    def timing(self) -> dict:
-        """Per-phase device milliseconds of the last forward call."""
+    def timing(self, back: int = 0) -> dict:
+        """Per-phase device milliseconds of the `back`-th most recent call."""
         from ._lib import PHASES
         ms = (C.c_float * len(PHASES))()
-        self._check(self.lib.moe_get_timing(self.ctx, C.cast(ms, C.c_void_p), len(PHASES)), "moe_get_timing")
+        self._check(self.lib.moe_get_timing_at(self.ctx, back, C.cast(ms, C.c_void_p), len(PHASES)),
+                    "moe_get_timing_at")
         return dict(zip(PHASES, list(ms)))
 
     # --------------------------------------------------------------- weights
@@ -170,6 +173,12 @@ class MoE:
     def add_router_bias(self, layer: int, extra_bias):
         eb = _f32(extra_bias)
         self._check(self.lib.moe_add_router_bias(self.ctx, layer, _ptr(eb)), "moe_add_router_bias")
+
+    def set_logit_bias(self, layer: int, logit_bias):
+        """Per-expert term added to the router logits before the sigmoid (None
+        clears it)."""
+        lb = None if logit_bias is None else _f32(logit_bias)
+        self._check(self.lib.moe_set_logit_bias(self.ctx, layer, _ptr(lb)), "moe_set_logit_bias")
 
     def set_norm_weight(self, layer: int, w):
         w = _f32(w)

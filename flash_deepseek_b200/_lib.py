@@ -33,8 +33,10 @@ SIGNATURES = {
     "moe_world_size": (C.c_int, [_vp]),
     "moe_load_layer": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, C.c_int, _vp, _vp, _vp, _vp, _vp, C.c_int]),
     "moe_load_layer_packed": (C.c_int, [_vp, C.c_int, _vp, C.c_size_t, _vp, _vp, _vp, _vp, _vp, C.c_int]),
-    "moe_init_layer_synthetic": (C.c_int, [_vp, C.c_int, C.c_uint64, C.c_int, C.c_float, C.c_float, C.c_float]),
+    "moe_init_layer_synthetic": (C.c_int, [_vp, C.c_int, C.c_uint64, C.c_int, C.c_double, C.c_double,
+                                           C.c_double]),
     "moe_add_router_bias": (C.c_int, [_vp, C.c_int, _vp]),
+    "moe_set_logit_bias": (C.c_int, [_vp, C.c_int, _vp]),
     "moe_set_norm_weight": (C.c_int, [_vp, C.c_int, _vp]),
     "moe_read_expert": (C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_size_t]),
     "moe_expert_bytes": (C.c_size_t, [_vp, C.c_int]),
@@ -53,6 +55,7 @@ SIGNATURES = {
     "moe_last_weight_bytes": (C.c_uint64, [_vp]),
     "moe_set_timing": (C.c_int, [_vp, C.c_int]),
     "moe_get_timing": (C.c_int, [_vp, _vp, C.c_int]),
+    "moe_get_timing_at": (C.c_int, [_vp, C.c_int, _vp, C.c_int]),
 }
 
 PHASES = ["router", "route", "dispatch", "gateup", "prep", "down", "combine_a2a", "output"]

@@ -35,18 +35,20 @@ struct moe_ctx {
     float *x_inv = nullptr;
     MoePlan plan{};
     int *counter = nullptr;
-    float *act = nullptr, *dcf = nullptr, *d_inv = nullptr, *eo = nullptr;
-    __half *dop = nullptr;
-    size_t dop_stride = 0;
+    float *act = nullptr, *d_inv = nullptr, *eo = nullptr;
+    uint8_t *dop = nullptr;   // down operand, dop_bytes(I) per pair
+    uint8_t *zop = nullptr;   // zeroed operand stream for empty MMA columns
     int *h_counts = nullptr;  // pinned [4]
     // expert-parallel buffers
     float *send_x = nullptr, *recv_x = nullptr, *send_y = nullptr, *recv_y = nullptr;
     int *send_meta = nullptr, *recv_meta = nullptr;
     float *rows_partial = nullptr;
+    int *tok_slot = nullptr;
     std::string err;
     bool timing = false;
-    cudaEvent_t ev[MOE_N_PHASES + 1] = {};
-    bool ev_valid[MOE_N_PHASES + 1] = {};
+    int ring = 0, ring_pos = 0, ring_used = 0;  // per-step phase events
+    std::vector<cudaEvent_t> ev;                // [ring][MOE_N_PHASES + 1]
+    std::vector<uint8_t> ev_valid;
     uint64_t launches = 0;
     uint64_t last_bytes = 0;
     int last_layer = -1;
@@ -108,8 +110,9 @@ static int ctx_alloc(moe_ctx *c) {
     CK(dmalloc(&c->idx_given, (size_t)R * K));
     CK(dmalloc(&c->w_given, (size_t)R * K));
     CK(dmalloc(&c->bias_tmp, (size_t)E));
-    CK(dmalloc(&c->xop, (size_t)R * q4op_halves(H)));
-    CK(dmalloc(&c->x_inv, (size_t)R));
+    const int RT = (c->world > 1 ? R + T : R);  // EP: received rows + local rows
+    CK(dmalloc(&c->xop, (size_t)RT * q4op_halves(H)));
+    CK(dmalloc(&c->x_inv, (size_t)RT));
     const int P = c->max_pairs;
     CK(dmalloc(&c->plan.counts, 4));
     CK(dmalloc(&c->plan.pair_expert, P));
@@ -118,16 +121,19 @@ static int ctx_alloc(moe_ctx *c) {
     CK(dmalloc(&c->plan.chunk_expert, P));
     CK(dmalloc(&c->plan.chunk_pair0, P));
     CK(dmalloc(&c->plan.chunk_ntok, P));
-    CK(dmalloc(&c->plan.slot_pair, (size_t)R * (K + 1)));
+    CK(dmalloc(&c->plan.slot_pair, (size_t)RT * (K + 1)));
     CK(dmalloc(&c->plan.error, 1));
     CK(cudaMemset(c->plan.error, 0, sizeof(int)));
     CK(cudaMemset(c->plan.counts, 0, 4 * sizeof(int)));
     CK(dmalloc(&c->counter, 1));
     CK(cudaMemset(c->counter, 0, sizeof(int)));
     CK(dmalloc(&c->act, (size_t)P * I));
-    c->dop_stride = q4op_halves(I) > q6op_halves(I) ? q4op_halves(I) : q6op_halves(I);
-    CK(dmalloc(&c->dop, (size_t)P * c->dop_stride));
-    CK(dmalloc(&c->dcf, (size_t)P * (I / MOE_QK) * 16));
+    CK(dmalloc(&c->dop, (size_t)P * dop_bytes(I)));
+    {
+        const size_t zb = (dop_bytes(I) > q4op_halves(H) * 2 ? dop_bytes(I) : q4op_halves(H) * 2) + 4096;
+        CK(cudaMalloc((void **)&c->zop, zb));
+        CK(cudaMemset(c->zop, 0, zb));
+    }
     CK(dmalloc(&c->d_inv, (size_t)P));
     CK(dmalloc(&c->eo, (size_t)P * H));
     CK(cudaMallocHost((void **)&c->h_counts, 4 * sizeof(int)));
@@ -140,6 +146,7 @@ static int ctx_alloc(moe_ctx *c) {
         CK(dmalloc(&c->send_meta, rows * (2 * K + 2)));
         CK(dmalloc(&c->recv_meta, rows * (2 * K + 2)));
         CK(dmalloc(&c->rows_partial, rows * H));
+        CK(dmalloc(&c->tok_slot, (size_t)T * c->world));
     }
     return MOE_OK;
 }
@@ -155,8 +162,9 @@ moe_ctx *moe_create(const moe_config *cfg, int device, int rank, int world_size,
     c->world = world_size;
     const moe_config &k = *cfg;
     const char *bad = nullptr;
-    if (k.hidden <= 0 || k.hidden % 256) bad = "hidden must be a positive multiple of 256";
-    else if (k.intermediate <= 0 || k.intermediate % 256) bad = "intermediate must be a positive multiple of 256";
+    if (k.hidden <= 0 || k.hidden % 256 || k.hidden > 32768) bad = "hidden must be a multiple of 256 in 256..32768";
+    else if (k.intermediate <= 0 || k.intermediate % 256 || k.intermediate > 32768)
+        bad = "intermediate must be a multiple of 256 in 256..32768";
     else if (k.n_experts <= 0 || k.n_experts > 1024) bad = "n_experts must be in 1..1024";
     else if (k.n_group <= 0 || k.n_group > 64 || k.n_experts % k.n_group) bad = "n_group must divide n_experts (<= 64)";
     else if (k.topk_group <= 0 || k.topk_group > k.n_group) bad = "topk_group must be in 1..n_group";
@@ -211,19 +219,19 @@ void moe_destroy(moe_ctx *c) {
     cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->comm) ncclCommDestroy(c->comm);
-    for (int p = 0; p <= MOE_N_PHASES; p++)
-        if (c->ev[p]) cudaEventDestroy(c->ev[p]);
+    for (cudaEvent_t e : c->ev) cudaEventDestroy(e);
     for (auto &L : c->layers) {
         cudaFree(L.experts);
         cudaFree(L.router);
         cudaFree(L.bias);
+        cudaFree(L.logit_bias);
         cudaFree(L.norm);
     }
     void *bufs[] = {c->part, c->d_in, c->d_out, c->h_post, c->idx, c->wts, c->idx_given, c->w_given, c->bias_tmp, c->xop, c->x_inv, c->plan.counts,
                     c->plan.pair_expert, c->plan.pair_token, c->plan.pair_w, c->plan.chunk_expert,
                     c->plan.chunk_pair0, c->plan.chunk_ntok, c->plan.slot_pair, c->plan.error, c->counter, c->act,
-                    c->dop, c->dcf, c->d_inv, c->eo, c->send_x, c->recv_x, c->send_y, c->recv_y, c->send_meta,
-                    c->recv_meta, c->rows_partial};
+                    c->dop, c->zop, c->d_inv, c->eo, c->send_x, c->recv_x, c->send_y, c->recv_y, c->send_meta,
+                    c->recv_meta, c->rows_partial, c->tok_slot};
     for (void *b : bufs) cudaFree(b);
     if (c->h_counts) cudaFreeHost(c->h_counts);
     if (c->stream) cudaStreamDestroy(c->stream);
@@ -358,8 +366,8 @@ int moe_load_layer_packed(moe_ctx *c, int layer, const void *blob, size_t expert
     return MOE_OK;
 }
 
-int moe_init_layer_synthetic(moe_ctx *c, int layer, uint64_t seed, int down_type, float w_sigma, float router_sigma,
-                             float bias_sigma) {
+int moe_init_layer_synthetic(moe_ctx *c, int layer, uint64_t seed, int down_type, double w_sigma,
+                             double router_sigma, double bias_sigma) {
     if (!c) return MOE_ERR_ARG;
     int rc = layer_alloc(c, layer, down_type, down_type);
     if (rc) return rc;
@@ -401,6 +409,22 @@ int moe_add_router_bias(moe_ctx *c, int layer, const float *extra) {
     CK(cudaMemcpy(b.data(), c->layers[layer].bias, sizeof(float) * c->d.E, cudaMemcpyDeviceToHost));
     for (int e = 0; e < c->d.E; e++) b[e] += extra[e];
     CK(cudaMemcpy(c->layers[layer].bias, b.data(), sizeof(float) * c->d.E, cudaMemcpyHostToDevice));
+    return MOE_OK;
+}
+
+int moe_set_logit_bias(moe_ctx *c, int layer, const float *lb) {
+    if (!c) return MOE_ERR_ARG;
+    if (layer < 0 || layer >= (int)c->layers.size() || !c->layers[layer].router)
+        return fail(c, MOE_ERR_STATE, "layer %d not loaded", layer);
+    CK(cudaSetDevice(c->device));
+    MoeLayerDev &L = c->layers[layer];
+    if (!lb) {
+        cudaFree(L.logit_bias);
+        L.logit_bias = nullptr;
+        return MOE_OK;
+    }
+    if (!L.logit_bias) CK(cudaMalloc((void **)&L.logit_bias, sizeof(float) * c->d.E));
+    CK(cudaMemcpy(L.logit_bias, lb, sizeof(float) * c->d.E, cudaMemcpyHostToDevice));
     return MOE_OK;
 }
 
@@ -452,8 +476,15 @@ int moe_read_expert(moe_ctx *c, int layer, int expert, void *dst, size_t dst_siz
 // records the boundary before phase `ph` (MOE_N_PHASES = end of the step)
 static void mark(moe_ctx *c, int ph, cudaStream_t s) {
     if (!c->timing) return;
-    cudaEventRecord(c->ev[ph], s);
-    c->ev_valid[ph] = true;
+    const size_t i = (size_t)c->ring_pos * (MOE_N_PHASES + 1) + ph;
+    cudaEventRecord(c->ev[i], s);
+    c->ev_valid[i] = 1;
+}
+static void mark_begin(moe_ctx *c) {
+    if (!c->timing) return;
+    c->ring_pos = (c->ring_pos + 1) % c->ring;
+    if (c->ring_used < c->ring) c->ring_used++;
+    for (int p = 0; p <= MOE_N_PHASES; p++) c->ev_valid[(size_t)c->ring_pos * (MOE_N_PHASES + 1) + p] = 0;
 }
 
 static int check_layer(moe_ctx *c, int layer) {
@@ -468,21 +499,79 @@ static int run_local(moe_ctx *c, int layer, const float *x, int T, const int *id
     MoeLayerDev &L = c->layers[layer];
     const MoeDims &d = c->d;
     const int mode = !routed ? 2 : (idx_in ? 1 : 0);
-    for (int p = 0; p <= MOE_N_PHASES; p++) c->ev_valid[p] = false;
+    mark_begin(c);
     mark(c, MOE_PHASE_ROUTER, s);
     if (mode == 0) moe_launch_router_logits(L.router, x, T, d.H, d.E, c->part, c->n_split, s, &c->launches);
     mark(c, MOE_PHASE_ROUTE, s);
-    moe_launch_route_and_plan(d, c->part, c->n_split, nullptr, L.bias, mode, idx_in, w_in, T, c->idx, c->wts, x,
-                              c->xop, c->x_inv, with_shared, 1, c->plan, c->counter, s, &c->launches);
+    moe_launch_route_and_plan(d, c->part, c->n_split, nullptr, L.bias, L.logit_bias, mode, idx_in, w_in, T, c->idx,
+                              c->wts, x, c->xop, c->x_inv, with_shared, 1, c->plan, c->counter, s, &c->launches);
     const int max_chunks = (T * d.K + T + MOE_TC - 1) / MOE_TC + d.E + 1;
     mark(c, MOE_PHASE_GATEUP, s);
-    moe_launch_gateup(d, L, c->plan, c->xop, c->x_inv, c->act, max_chunks * (d.I / MOE_ROWS_GU), s, &c->launches);
+    moe_launch_gateup(d, L, c->plan, c->xop, reinterpret_cast<const __half *>(c->zop), c->x_inv, c->act,
+                      max_chunks * (d.I / MOE_ROWS_GU), s, &c->launches);
     mark(c, MOE_PHASE_PREP, s);
-    moe_launch_prep_down(d, L, c->plan, c->act, c->dop, c->dcf, c->d_inv, T * d.K + T, s, &c->launches);
+    moe_launch_prep_down(d, L, c->plan, c->act, c->dop, c->d_inv, T * d.K + T, s, &c->launches);
     mark(c, MOE_PHASE_DOWN, s);
-    moe_launch_down(d, L, c->plan, c->dop, c->dcf, c->d_inv, c->eo, max_chunks * (d.H / 16), s, &c->launches);
+    moe_launch_down(d, L, c->plan, c->dop, c->zop, c->d_inv, c->eo, max_chunks * (d.H / 16), s, &c->launches);
     mark(c, MOE_PHASE_OUTPUT, s);
     moe_launch_combine(d, c->plan, c->eo, T, routed, with_shared, residual, out, s, &c->launches);
+    mark(c, MOE_N_PHASES, s);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(c, MOE_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+    c->last_layer = layer;
+    return MOE_OK;
+}
+
+// Expert-parallel step: route local tokens, dispatch rows to the ranks that
+// own their experts, run the local experts on received rows (+ shared expert
+// on local rows), pre-combine per row, return the partials, sum them in rank
+// order.
+static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_in, const float *w_in,
+                  const float *residual, float *out, cudaStream_t s) {
+    MoeLayerDev &L = c->layers[layer];
+    const MoeDims &d = c->d;
+    const int N = c->world, cap = c->max_tok, R = N * cap, mw = 2 + 2 * d.K;
+    const int mode = idx_in ? 1 : 0;
+    mark_begin(c);
+    mark(c, MOE_PHASE_ROUTER, s);
+    if (mode == 0 && T > 0) moe_launch_router_logits(L.router, x, T, d.H, d.E, c->part, c->n_split, s, &c->launches);
+    mark(c, MOE_PHASE_ROUTE, s);
+    if (T > 0)
+        moe_launch_route_and_plan(d, c->part, c->n_split, nullptr, L.bias, L.logit_bias, mode, idx_in, w_in, T,
+                                  c->idx, c->wts, x, nullptr, nullptr, 0, 0, c->plan, c->counter, s, &c->launches);
+    mark(c, MOE_PHASE_DISPATCH, s);
+    moe_launch_ep_pack(x, c->idx, c->wts, T, d.K, d.H, N, c->n_local, cap, c->send_x, c->send_meta, c->tok_slot, s,
+                       &c->launches);
+    NK(ncclGroupStart());
+    for (int p = 0; p < N; p++) {
+        NK(ncclSend(c->send_x + (size_t)p * cap * d.H, (size_t)cap * d.H, ncclFloat32, p, c->comm, s));
+        NK(ncclRecv(c->recv_x + (size_t)p * cap * d.H, (size_t)cap * d.H, ncclFloat32, p, c->comm, s));
+        NK(ncclSend(c->send_meta + (size_t)p * cap * mw, (size_t)cap * mw, ncclInt32, p, c->comm, s));
+        NK(ncclRecv(c->recv_meta + (size_t)p * cap * mw, (size_t)cap * mw, ncclInt32, p, c->comm, s));
+    }
+    NK(ncclGroupEnd());
+    moe_launch_ep_plan(d, c->recv_meta, N, cap, T, c->e0, c->n_local, c->plan, s, &c->launches);
+    moe_launch_prep_rows(c->recv_x, c->recv_meta, mw, R, x, T, d.H, c->xop, c->x_inv, s, &c->launches);
+    const int P = R * d.K + T;
+    const int max_chunks = (P + MOE_TC - 1) / MOE_TC + d.E + 1;
+    mark(c, MOE_PHASE_GATEUP, s);
+    moe_launch_gateup(d, L, c->plan, c->xop, reinterpret_cast<const __half *>(c->zop), c->x_inv, c->act,
+                      max_chunks * (d.I / MOE_ROWS_GU), s, &c->launches);
+    mark(c, MOE_PHASE_PREP, s);
+    moe_launch_prep_down(d, L, c->plan, c->act, c->dop, c->d_inv, P, s, &c->launches);
+    mark(c, MOE_PHASE_DOWN, s);
+    moe_launch_down(d, L, c->plan, c->dop, c->zop, c->d_inv, c->eo, max_chunks * (d.H / 16), s, &c->launches);
+    mark(c, MOE_PHASE_COMBINE, s);
+    moe_launch_ep_partial(d, c->plan, c->recv_meta, c->eo, R, c->send_y, s, &c->launches);
+    NK(ncclGroupStart());
+    for (int p = 0; p < N; p++) {
+        NK(ncclSend(c->send_y + (size_t)p * cap * d.H, (size_t)cap * d.H, ncclFloat32, p, c->comm, s));
+        NK(ncclRecv(c->recv_y + (size_t)p * cap * d.H, (size_t)cap * d.H, ncclFloat32, p, c->comm, s));
+    }
+    NK(ncclGroupEnd());
+    mark(c, MOE_PHASE_OUTPUT, s);
+    if (T > 0)
+        moe_launch_ep_final(d, c->plan, c->recv_y, c->tok_slot, N, cap, T, c->eo, residual, out, s, &c->launches);
     mark(c, MOE_N_PHASES, s);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(c, MOE_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
@@ -496,10 +585,13 @@ int moe_forward_device(moe_ctx *c, int layer, const float *d_h, int T, float *d_
     int rc = check_layer(c, layer);
     if (rc) return rc;
     if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
-    if (c->world > 1) return fail(c, MOE_ERR_STATE, "expert-parallel forward not available in this build");
-    if (T == 0) return MOE_OK;
     cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
-    rc = run_local(c, layer, d_h, T, nullptr, nullptr, 1, 1, nullptr, d_out, s);
+    if (c->world > 1) {
+        rc = run_ep(c, layer, d_h, T, nullptr, nullptr, nullptr, d_out, s);  // every rank joins, even with T == 0
+    } else {
+        if (T == 0) return MOE_OK;
+        rc = run_local(c, layer, d_h, T, nullptr, nullptr, 1, 1, nullptr, d_out, s);
+    }
     if (rc) return rc;
     if (d_idx) CK(cudaMemcpyAsync(d_idx, c->idx, sizeof(int) * T * c->d.K, cudaMemcpyDeviceToDevice, s));
     if (d_w) CK(cudaMemcpyAsync(d_w, c->wts, sizeof(float) * T * c->d.K, cudaMemcpyDeviceToDevice, s));
@@ -538,9 +630,10 @@ int moe_experts_forward_device(moe_ctx *c, int layer, const float *d_h, int T, c
     if (rc) return rc;
     if (K != c->d.K) return fail(c, MOE_ERR_ARG, "K %d differs from the context's top_k %d", K, c->d.K);
     if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
-    if (c->world > 1) return fail(c, MOE_ERR_STATE, "expert-parallel forward not available in this build");
-    if (T == 0) return MOE_OK;
     cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    if (c->world > 1) return fail(c, MOE_ERR_STATE, "moe_experts_forward is single-GPU (the shared expert is "
+                                                     "always added on the expert-parallel path)");
+    if (T == 0) return MOE_OK;
     return run_local(c, layer, d_h, T, d_idx, d_w, 1, 0, nullptr, d_out, s);
 }
 
@@ -590,7 +683,7 @@ int moe_route(moe_ctx *c, const float *logits, const float *bias, int T, int *id
         d_b = c->bias_tmp;
         CK(cudaMemcpyAsync(d_b, bias, sizeof(float) * E, cudaMemcpyHostToDevice, c->stream));
     }
-    moe_launch_route_and_plan(c->d, nullptr, 0, d_lg, d_b, 0, nullptr, nullptr, T, c->idx, c->wts, nullptr,
+    moe_launch_route_and_plan(c->d, nullptr, 0, d_lg, d_b, nullptr, 0, nullptr, nullptr, T, c->idx, c->wts, nullptr,
                               nullptr, nullptr, 0, 0, c->plan, c->counter, c->stream, &c->launches);
     CK(cudaGetLastError());
     CK(cudaMemcpyAsync(idx, c->idx, sizeof(int) * T * K, cudaMemcpyDeviceToHost, c->stream));
@@ -602,13 +695,14 @@ int moe_route(moe_ctx *c, const float *logits, const float *bias, int T, int *id
 int moe_forward_stack_device(moe_ctx *c, int first, int n_layers, float *d_hidden, int T, void *stream) {
     if (!c || !d_hidden) return MOE_ERR_ARG;
     if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
-    if (c->world > 1) return fail(c, MOE_ERR_STATE, "expert-parallel forward not available in this build");
     cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
     for (int l = first; l < first + n_layers; l++) {
         int rc = check_layer(c, l);
         if (rc) return rc;
-        moe_launch_rmsnorm(d_hidden, c->layers[l].norm, c->h_post, T, c->d.H, c->cfg.rms_eps, s, &c->launches);
-        rc = run_local(c, l, c->h_post, T, nullptr, nullptr, 1, 1, d_hidden, d_hidden, s);
+        if (T > 0) moe_launch_rmsnorm(d_hidden, c->layers[l].norm, c->h_post, T, c->d.H, c->cfg.rms_eps, s,
+                                      &c->launches);
+        if (c->world > 1) rc = run_ep(c, l, c->h_post, T, nullptr, nullptr, d_hidden, d_hidden, s);
+        else if (T > 0) rc = run_local(c, l, c->h_post, T, nullptr, nullptr, 1, 1, d_hidden, d_hidden, s);
         if (rc) return rc;
     }
     return MOE_OK;
@@ -627,29 +721,42 @@ int moe_forward_stack(moe_ctx *c, int first, int n_layers, float *hidden, int T)
 }
 
 int moe_set_timing(moe_ctx *c, int enable) {
-    if (!c) return MOE_ERR_ARG;
+    if (!c || enable < 0) return MOE_ERR_ARG;
     CK(cudaSetDevice(c->device));
-    if (enable && !c->ev[0])
-        for (int p = 0; p <= MOE_N_PHASES; p++) CK(cudaEventCreate(&c->ev[p]));
-    c->timing = enable != 0;
+    if (enable > 0 && enable != c->ring) {
+        for (cudaEvent_t e : c->ev) cudaEventDestroy(e);
+        c->ev.assign((size_t)enable * (MOE_N_PHASES + 1), nullptr);
+        c->ev_valid.assign(c->ev.size(), 0);
+        for (auto &e : c->ev) CK(cudaEventCreate(&e));
+        c->ring = enable;
+        c->ring_pos = enable - 1;
+        c->ring_used = 0;
+    }
+    c->timing = enable > 0;
     return MOE_OK;
 }
 
-int moe_get_timing(moe_ctx *c, float *ms, int n) {
+int moe_get_timing_at(moe_ctx *c, int back, float *ms, int n) {
     if (!c || !ms) return MOE_ERR_ARG;
-    if (!c->timing) return fail(c, MOE_ERR_STATE, "timing is not enabled");
+    if (!c->timing || c->ring == 0) return fail(c, MOE_ERR_STATE, "timing is not enabled");
+    if (back < 0 || back >= c->ring_used) return fail(c, MOE_ERR_ARG, "step %d is not in the timing ring", back);
+    const int slot = ((c->ring_pos - back) % c->ring + c->ring) % c->ring;
+    cudaEvent_t *ev = &c->ev[(size_t)slot * (MOE_N_PHASES + 1)];
+    const uint8_t *valid = &c->ev_valid[(size_t)slot * (MOE_N_PHASES + 1)];
     for (int p = MOE_N_PHASES; p >= 0; p--)
-        if (c->ev_valid[p]) { CK(cudaEventSynchronize(c->ev[p])); break; }
+        if (valid[p]) { CK(cudaEventSynchronize(ev[p])); break; }
     for (int p = 0; p < n && p < MOE_N_PHASES; p++) {
         ms[p] = 0.0f;
-        if (!c->ev_valid[p]) continue;
+        if (!valid[p]) continue;
         int q = p + 1;
-        while (q <= MOE_N_PHASES && !c->ev_valid[q]) q++;
+        while (q <= MOE_N_PHASES && !valid[q]) q++;
         if (q > MOE_N_PHASES) continue;
-        CK(cudaEventElapsedTime(&ms[p], c->ev[p], c->ev[q]));
+        CK(cudaEventElapsedTime(&ms[p], ev[p], ev[q]));
     }
     return MOE_OK;
 }
+
+int moe_get_timing(moe_ctx *c, float *ms, int n) { return moe_get_timing_at(c, 0, ms, n); }
 
 uint64_t moe_last_weight_bytes(const moe_ctx *cc) {
     moe_ctx *c = const_cast<moe_ctx *>(cc);

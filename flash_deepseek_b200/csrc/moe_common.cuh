@@ -16,27 +16,33 @@
 
 // ---------------------------------------------------------------------------
 // Activation-operand layouts.  The decode GEMVs use the tensor core as an
-// exact reducer: weights are decoded in registers to small integers in fp16
-// (exact), activations are split x*s = hi + lo (two fp16, s a power of two per
-// vector) and the MMA accumulates in fp32.  The K order inside an MMA is free,
-// so the activation operand is stored pre-permuted to match the order in
-// which each thread naturally decodes its weight bytes.
+// exact reducer: the K order inside an MMA is free, so each activation
+// operand is stored pre-permuted to match the order in which a lane naturally
+// decodes its weight bytes, and laid out so that a lane reads its fragments
+// with 16-byte vector loads.
 //
-// Q4_K operand, per vector and per super-block (256 weights): 17 groups
-// (16 MMA steps + 1 step for the min term) x 2 parts (hi, lo) x 4 quad lanes
-// x 4 halves = 544 halves.
-//   step m < 16, lane t, slot j:  weight index q4k_k(m, t, j)
-//   step 16: (X_a, X_b, 0, 0) with X the sub-block sums of x*s for the two
-//   sub-blocks q4k_min_sub(t), q4k_min_sub(t)+1.
-// Q6_K operand, per vector and super-block: 16 steps (one per 16-weight
-// sub-block) x 2 parts x 4 lanes x 4 halves = 512 halves, weight index
-// 16*s + 4*t + {0,2,1,3}[j]; plus a float per sub-block (the C-fold term).
+// Q4_K operand (fp16 MMA; gate/up and Q4_K down).  x*s = hi + lo (two fp16,
+// s a power of two per vector).  Per vector and super-block (256 weights):
+//   [part (hi, lo)][lane t][step 0..17][4 halves]      = 576 halves
+//   step m < 16, slot j: weight q4k_k(m, t, j)
+//   step 16: (X_a, X_b, 0, 0), X = sub-block sums of x*s for sub-blocks
+//            q4k_min_sub(t), q4k_min_sub(t)+1;  step 17: zero padding
+// Q6_K operand (int8 MMA; Q6_K down).  x*2^e rounded to a 21-bit integer
+// split into three int8 planes x = p0 + 2^7 p1 + 2^14 p2 (p0, p1 in [0,127],
+// p2 signed).  Per vector: [plane][super-block][lane t][step 0..15][4 bytes]
+// = 3 * 256 bytes per super-block; step s, byte i: weight 16 s + 4 t + i.
 // ---------------------------------------------------------------------------
-#define Q4OP_STEPS 17
-#define Q4OP_HALVES_PER_SB (Q4OP_STEPS * 2 * 4 * 4)
-#define Q6OP_HALVES_PER_SB (16 * 2 * 4 * 4)
+#define Q4OP_STEPS 18
+#define Q4OP_LANE_HALVES (Q4OP_STEPS * 4)            // 72 halves = 144 B per lane
+#define Q4OP_HALVES_PER_SB (2 * 4 * Q4OP_LANE_HALVES) // 576
+#define Q6I_BYTES_PER_SB 256                          // per plane
 __host__ __device__ __forceinline__ size_t q4op_halves(int K) { return (size_t)(K / 256) * Q4OP_HALVES_PER_SB; }
-__host__ __device__ __forceinline__ size_t q6op_halves(int K) { return (size_t)(K / 256) * Q6OP_HALVES_PER_SB; }
+__host__ __device__ __forceinline__ size_t q6i_bytes(int K) { return (size_t)3 * (K / 256) * Q6I_BYTES_PER_SB; }
+// bytes reserved per vector in a buffer that may hold either operand
+__host__ __device__ __forceinline__ size_t dop_bytes(int K) {
+    const size_t a = q4op_halves(K) * 2, b = q6i_bytes(K);
+    return a > b ? a : b;
+}
 
 __host__ __device__ __forceinline__ int perm_j(int j) { return (j == 1) ? 2 : ((j == 2) ? 1 : j); }
 
@@ -53,8 +59,8 @@ __host__ __device__ __forceinline__ int q4k_k(int m, int t, int j) {
 __host__ __device__ __forceinline__ int q4k_min_sub(int t) { return 2 * (t >> 1) + 4 * (t & 1); }
 
 // Weight index inside a Q6_K super-block for sub-block step s (0..15), lane t,
-// slot j.
-__host__ __device__ __forceinline__ int q6k_k(int s, int t, int j) { return 16 * s + 4 * t + perm_j(j); }
+// byte i of the lane's int8 fragment.
+__host__ __device__ __forceinline__ int q6k_k(int s, int t, int i) { return 16 * s + 4 * t + i; }
 
 // ---------------------------------------------------------------------------
 // Repacked Q6_K matrix (lossless permutation of the GGUF bytes, done once at
@@ -124,6 +130,27 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c0), "f"(c1), "f"(c2), "f"(c3));
 }
 
+// Integer tensor-core step: D = A(16x16 u8 / s8, row) * B(16x8 s8, col) + C (s32).
+__device__ __forceinline__ void mma_u8s8_16816(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0, int c0, int c1,
+                                               int c2, int c3) {
+    asm("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%8,%9,%10};\n"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(b0), "r"(c0), "r"(c1), "r"(c2), "r"(c3));
+}
+__device__ __forceinline__ void mma_s8s8_16816(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0, int c0, int c1,
+                                               int c2, int c3) {
+    asm("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%8,%9,%10};\n"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(b0), "r"(c0), "r"(c1), "r"(c2), "r"(c3));
+}
+// sign-extended byte `i` (compile-time) of w
+template <int I>
+__device__ __forceinline__ int sext_byte(uint32_t w) {
+    int r;
+    asm("prmt.b32 %0, %1, 0, %2;\n" : "=r"(r) : "r"(w), "n"(I | ((8 | I) << 4) | ((8 | I) << 8) | ((8 | I) << 12)));
+    return r;
+}
+
 __device__ __forceinline__ uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 __device__ __forceinline__ __half2 u32_as_h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
 
@@ -136,12 +163,28 @@ __device__ __forceinline__ uint4 ldg_stream16(const void *p) {
                  : "l"(p));
     return r;
 }
-// Activation-operand load (8 bytes, cached: shared by many warps).
-__device__ __forceinline__ uint2 ldg_op8(const void *p) {
-    uint2 r;
-    asm("ld.global.nc.v2.u32 {%0,%1}, [%2];\n" : "=r"(r.x), "=r"(r.y) : "l"(p));
+// Activation-operand load (16 bytes, cached in L1: shared by many warps).
+__device__ __forceinline__ uint4 ldg_op16(const void *p) {
+    uint4 r;
+    asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];\n" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
     return r;
 }
+
+// Asynchronous 16-byte global -> shared copy (L2 only), completed with
+// cp.async.wait_group.  Each lane later reads back only what it copied, so
+// no barrier is needed between the copy and its use.
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+#define MOE_STAGES 3        // per-warp weight pipeline depth
+#define MOE_Q4_WORDS 6      // 16-byte words per lane per Q4_K super-block (2 rows)
+#define MOE_Q6_WORDS 8      // 16-byte words per lane per Q6_K super-block (2 rows)
 
 // ---------------------------------------------------------------------------
 // Counter-based N(0, sigma) generator, bit-identical to the test oracle:

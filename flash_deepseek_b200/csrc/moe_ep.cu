@@ -1,0 +1,253 @@
+// moe_ep.cu -- expert-parallel dispatch / combine kernels (one process per GPU,
+// experts sharded n_experts / world per rank, router and shared expert
+// replicated).  The all-to-all itself is NCCL send/recv with fixed-capacity
+// buffers (moe_api.cu), so a step needs no host synchronisation.
+//
+// Row space of the expert kernels on rank r (world N, capacity cap = max
+// tokens per rank):
+//   rows [p*cap, p*cap + cap)   activations received from rank p
+//   rows [N*cap, N*cap + T)     this rank's own tokens (shared expert)
+// Metadata of a dispatched row: [valid, src_token, idx[K], w_bits[K]].
+#include <stdio.h>
+
+#include "moe_common.cuh"
+#include "moe_internal.h"
+
+#define LAUNCH_COUNT(p) \
+    do {                \
+        if (p) (*(p))++; \
+    } while (0)
+
+// Per-peer masks of the local tokens that route to at least one expert of
+// that peer (T <= 64).
+__device__ __forceinline__ unsigned long long peer_mask(const int *__restrict__ idx, int T, int K, int n_local,
+                                                        int p) {
+    unsigned long long m = 0ull;
+    for (int t = 0; t < T; t++)
+        for (int k = 0; k < K; k++)
+            if (idx[t * K + k] / n_local == p) { m |= 1ull << t; break; }
+    return m;
+}
+
+// grid = T blocks (+1 block that clears the unused slots' valid flags)
+__global__ void k_ep_pack(const float *__restrict__ x, const int *__restrict__ idx, const float *__restrict__ w,
+                          int T, int K, int H, int world, int n_local, int cap, float *__restrict__ send_x,
+                          int *__restrict__ send_meta, int *__restrict__ tok_slot) {
+    __shared__ unsigned long long pm[64];
+    const int meta_w = 2 + 2 * K;
+    for (int p = threadIdx.x; p < world; p += blockDim.x) pm[p] = peer_mask(idx, T, K, n_local, p);
+    __syncthreads();
+    if (blockIdx.x == T) {  // clear the valid flag of unused slots
+        for (int s = threadIdx.x; s < world * cap; s += blockDim.x) {
+            const int p = s / cap, i = s % cap;
+            if (i >= __popcll(pm[p])) send_meta[(size_t)s * meta_w] = 0;
+        }
+        return;
+    }
+    const int t = blockIdx.x;
+    for (int p = 0; p < world; p++) {
+        const bool hit = (pm[p] >> t) & 1ull;
+        const int slot = hit ? __popcll(pm[p] & ((1ull << t) - 1ull)) : -1;
+        if (threadIdx.x == 0) tok_slot[t * world + p] = slot;
+        if (!hit) continue;
+        const size_t row = (size_t)p * cap + slot;
+        const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)t * H);
+        float4 *dst = reinterpret_cast<float4 *>(send_x + row * H);
+        for (int i = threadIdx.x; i < H / 4; i += blockDim.x) dst[i] = src[i];
+        int *m = send_meta + row * meta_w;
+        if (threadIdx.x == 0) { m[0] = 1; m[1] = t; }
+        for (int k = threadIdx.x; k < K; k += blockDim.x) {
+            m[2 + k] = idx[t * K + k];
+            m[2 + K + k] = __float_as_int(w[t * K + k]);
+        }
+    }
+}
+
+// Plan over the received rows (experts this rank owns) + the shared expert on
+// the local rows.  One block; dynamic smem = (E+1) * MW * 8 bytes of masks.
+__global__ void __launch_bounds__(512) k_ep_plan(MoeDims d, const int *__restrict__ recv_meta, int world, int cap,
+                                                 int T, int e0, int n_local, MoePlan plan) {
+    extern __shared__ unsigned long long mask[];  // [E+1][MW]
+    __shared__ int cnt[1025], off[1026], coff[1026];
+    __shared__ int wsum[3][32], carry[3];
+    const int E = d.E, K = d.K, NE = E + 1;
+    const int R = world * cap, RT = R + T;
+    const int MW = (RT + 63) / 64;
+    const int meta_w = 2 + 2 * K;
+    for (int e = threadIdx.x; e < NE; e += blockDim.x) cnt[e] = 0;
+    for (int i = threadIdx.x; i < NE * MW; i += blockDim.x) mask[i] = 0ull;
+    __syncthreads();
+    for (int p = threadIdx.x; p < R * K; p += blockDim.x) {
+        const int r = p / K, k = p % K;
+        const int *m = recv_meta + (size_t)r * meta_w;
+        if (!m[0]) continue;
+        const int e = m[2 + k];
+        if (e < 0 || e >= E) { atomicExch(plan.error, 1); continue; }
+        if (e < e0 || e >= e0 + n_local) continue;
+        atomicAdd(&cnt[e], 1);
+        atomicOr(&mask[(size_t)e * MW + (r >> 6)], 1ull << (r & 63));
+    }
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
+        const int r = R + t;
+        atomicOr(&mask[(size_t)E * MW + (r >> 6)], 1ull << (r & 63));
+    }
+    if (threadIdx.x == 0) cnt[E] = T;
+    if (threadIdx.x == 0) carry[0] = carry[1] = carry[2] = 0;
+    __syncthreads();
+    // exclusive scans (pairs, chunks, routed experts hit)
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
+    for (int base = 0; base < NE; base += blockDim.x) {
+        const int e = base + threadIdx.x;
+        int v[3] = {0, 0, 0};
+        if (e < NE) {
+            v[0] = cnt[e];
+            v[1] = (cnt[e] + MOE_TC - 1) / MOE_TC;
+            v[2] = (e < E && cnt[e] > 0) ? 1 : 0;
+        }
+        int inc[3];
+#pragma unroll
+        for (int q = 0; q < 3; q++) {
+            int xv = v[q];
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, xv, o);
+                if (lane >= o) xv += y;
+            }
+            inc[q] = xv;
+            if (lane == 31) wsum[q][wid] = xv;
+        }
+        __syncthreads();
+        if (threadIdx.x < 32) {
+#pragma unroll
+            for (int q = 0; q < 3; q++) {
+                int xv = threadIdx.x < nwarp ? wsum[q][threadIdx.x] : 0;
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int y = __shfl_up_sync(0xffffffffu, xv, o);
+                    if (threadIdx.x >= o) xv += y;
+                }
+                if (threadIdx.x < nwarp) wsum[q][threadIdx.x] = xv;
+            }
+        }
+        __syncthreads();
+        int excl[3];
+#pragma unroll
+        for (int q = 0; q < 3; q++) excl[q] = carry[q] + (wid ? wsum[q][wid - 1] : 0) + inc[q] - v[q];
+        if (e < NE) { off[e] = excl[0]; coff[e] = excl[1]; }
+        __syncthreads();
+        if (threadIdx.x == blockDim.x - 1) {
+#pragma unroll
+            for (int q = 0; q < 3; q++) carry[q] = excl[q] + v[q];
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        plan.counts[0] = carry[0];
+        plan.counts[1] = carry[1];
+        plan.counts[2] = carry[2];
+    }
+    __syncthreads();
+    // pairs: position = offset of the expert + earlier rows of that expert
+    for (int p = threadIdx.x; p < R * K; p += blockDim.x) {
+        const int r = p / K, k = p % K;
+        const int *m = recv_meta + (size_t)r * meta_w;
+        int pos = -1;
+        const int e = m[0] ? m[2 + k] : -1;
+        if (m[0] && e >= e0 && e < e0 + n_local && e < E) {
+            const unsigned long long *me = mask + (size_t)e * MW;
+            int before = 0;
+            for (int wv = 0; wv < (r >> 6); wv++) before += __popcll(me[wv]);
+            before += __popcll(me[r >> 6] & ((1ull << (r & 63)) - 1ull));
+            pos = off[e] + before;
+            plan.pair_expert[pos] = e;
+            plan.pair_token[pos] = r;
+            plan.pair_w[pos] = __int_as_float(m[2 + K + k]);
+        }
+        plan.slot_pair[(size_t)r * (K + 1) + k] = pos;
+    }
+    for (int t = threadIdx.x; t < T; t += blockDim.x) {
+        const int pos = off[E] + t, r = R + t;
+        plan.pair_expert[pos] = E;
+        plan.pair_token[pos] = r;
+        plan.pair_w[pos] = 1.0f;
+        plan.slot_pair[(size_t)r * (K + 1) + K] = pos;
+    }
+    for (int e = threadIdx.x; e < NE; e += blockDim.x) {
+        const int n = cnt[e];
+        for (int c = 0; c * MOE_TC < n; c++) {
+            const int ci = coff[e] + c;
+            plan.chunk_expert[ci] = e;
+            plan.chunk_pair0[ci] = off[e] + c * MOE_TC;
+            plan.chunk_ntok[ci] = min(MOE_TC, n - c * MOE_TC);
+        }
+    }
+}
+
+// Pre-combine on the expert side: partial[r] = sum over the slots of received
+// row r whose expert lives here, in slot order, of w_k * eo.
+__global__ void k_ep_partial(MoeDims d, MoePlan plan, const int *__restrict__ recv_meta, const float *__restrict__ eo,
+                             int rows, float *__restrict__ out) {
+    const int r = blockIdx.y;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r >= rows || i >= d.H) return;
+    const int K = d.K;
+    if (!recv_meta[(size_t)r * (2 + 2 * K)]) return;
+    float acc = 0.0f;
+    for (int k = 0; k < K; k++) {
+        const int p = plan.slot_pair[(size_t)r * (K + 1) + k];
+        if (p < 0) continue;
+        acc = fmaf(plan.pair_w[p], eo[(size_t)p * d.H + i], acc);
+    }
+    out[(size_t)r * d.H + i] = acc;
+}
+
+// Owner side: out[t] = sum over ranks (rank order) of the returned partials +
+// shared expert (+ residual).
+__global__ void k_ep_final(MoeDims d, MoePlan plan, const float *__restrict__ recv_y, const int *__restrict__ tok_slot,
+                           int world, int cap, int T, const float *__restrict__ eo, const float *__restrict__ residual,
+                           float *__restrict__ out) {
+    const int t = blockIdx.y;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= d.H) return;
+    float acc = 0.0f;
+    for (int p = 0; p < world; p++) {
+        const int s = tok_slot[t * world + p];
+        if (s >= 0) acc = acc + recv_y[((size_t)p * cap + s) * d.H + i];
+    }
+    const int sp = plan.slot_pair[(size_t)(world * cap + t) * (d.K + 1) + d.K];
+    acc = acc + eo[(size_t)sp * d.H + i];
+    if (residual) acc = residual[(size_t)t * d.H + i] + acc;
+    out[(size_t)t * d.H + i] = acc;
+}
+
+void moe_launch_ep_pack(const float *x, const int *idx, const float *w, int T, int K, int H, int world, int n_local,
+                        int cap, float *send_x, int *send_meta, int *tok_slot, cudaStream_t s, uint64_t *launches) {
+    k_ep_pack<<<T + 1, 256, 0, s>>>(x, idx, w, T, K, H, world, n_local, cap, send_x, send_meta, tok_slot);
+    LAUNCH_COUNT(launches);
+}
+
+void moe_launch_ep_plan(const MoeDims &d, const int *recv_meta, int world, int cap, int T, int e0, int n_local,
+                        const MoePlan &plan, cudaStream_t s, uint64_t *launches) {
+    const int MW = (world * cap + T + 63) / 64;
+    const size_t smem = sizeof(unsigned long long) * (size_t)(d.E + 1) * MW;
+    static size_t attr = 0;
+    if (smem > 48 * 1024 && smem > attr) {
+        cudaFuncSetAttribute(k_ep_plan, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attr = smem;
+    }
+    k_ep_plan<<<1, 512, smem, s>>>(d, recv_meta, world, cap, T, e0, n_local, plan);
+    LAUNCH_COUNT(launches);
+}
+
+void moe_launch_ep_partial(const MoeDims &d, const MoePlan &plan, const int *recv_meta, const float *eo, int rows,
+                           float *out, cudaStream_t s, uint64_t *launches) {
+    dim3 grid((d.H + 255) / 256, rows);
+    k_ep_partial<<<grid, 256, 0, s>>>(d, plan, recv_meta, eo, rows, out);
+    LAUNCH_COUNT(launches);
+}
+
+void moe_launch_ep_final(const MoeDims &d, const MoePlan &plan, const float *recv_y, const int *tok_slot, int world,
+                         int cap, int T, const float *eo, const float *residual, float *out, cudaStream_t s,
+                         uint64_t *launches) {
+    dim3 grid((d.H + 255) / 256, T);
+    k_ep_final<<<grid, 256, 0, s>>>(d, plan, recv_y, tok_slot, world, cap, T, eo, residual, out);
+    LAUNCH_COUNT(launches);
+}

@@ -28,7 +28,8 @@ struct MoeLayerDev {
     int down_type, sh_down_type;  // 12 / 14
     int e0, n_local;        // global id of slot 0, number of routed experts here
     float *router;          // [E][H]
-    float *bias;            // [E] or nullptr
+    float *bias;            // [E] selection bias (exp_probs_b)
+    float *logit_bias;      // [E] added to the logits before the sigmoid, or nullptr
     float *norm;            // [H] or nullptr
 };
 
@@ -46,17 +47,18 @@ void moe_launch_router_logits(const float *Wr, const float *x, int T, int H, int
 // mode: 0 route from logits / partial logits, 1 routing given (idx_in, w_in),
 // 2 shared expert only
 void moe_launch_route_and_plan(const MoeDims &d, const float *part, int n_split, const float *logits,
-                               const float *bias, int mode, const int *idx_in, const float *w_in, int T,
+                               const float *bias, const float *logit_bias, int mode, const int *idx_in, const float *w_in, int T,
                                int *idx_out, float *w_out, const float *x, __half *xop, float *x_inv,
                                int include_shared, int build_plan, const MoePlan &plan, int *counter,
                                cudaStream_t s, uint64_t *launches);
+// zop: zeroed operand stream used for empty MMA columns
 void moe_launch_gateup(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const __half *xop,
-                       const float *x_inv, float *act, int max_items, cudaStream_t s, uint64_t *launches);
+                       const __half *zop, const float *x_inv, float *act, int max_items, cudaStream_t s,
+                       uint64_t *launches);
 void moe_launch_prep_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const float *act,
-                          __half *dop, float *dcf, float *d_inv, int max_pairs, cudaStream_t s,
-                          uint64_t *launches);
-void moe_launch_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const __half *dop,
-                     const float *dcf, const float *d_inv, float *eo, int max_items, cudaStream_t s,
+                          uint8_t *dop, float *d_inv, int max_pairs, cudaStream_t s, uint64_t *launches);
+void moe_launch_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const uint8_t *dop,
+                     const uint8_t *zop, const float *d_inv, float *eo, int max_items, cudaStream_t s,
                      uint64_t *launches);
 void moe_launch_combine(const MoeDims &d, const MoePlan &plan, const float *eo, int T, int include_routed,
                         int include_shared, const float *residual, float *out, cudaStream_t s, uint64_t *launches);
@@ -69,6 +71,18 @@ void moe_launch_synth_quant(int type, uint64_t seed, uint64_t stream, int rows, 
                             uint8_t *dst, cudaStream_t s, uint64_t *launches);
 void moe_launch_synth_f32(uint64_t seed, uint64_t stream, size_t n, double sigma, float *dst, cudaStream_t s,
                           uint64_t *launches);
+void moe_launch_prep_rows(const float *recv, const int *meta, int meta_w, int R, const float *local, int T, int H,
+                          __half *xop, float *x_inv, cudaStream_t s, uint64_t *launches);
+// expert parallel (moe_ep.cu)
+void moe_launch_ep_pack(const float *x, const int *idx, const float *w, int T, int K, int H, int world, int n_local,
+                        int cap, float *send_x, int *send_meta, int *tok_slot, cudaStream_t s, uint64_t *launches);
+void moe_launch_ep_plan(const MoeDims &d, const int *recv_meta, int world, int cap, int T, int e0, int n_local,
+                        const MoePlan &plan, cudaStream_t s, uint64_t *launches);
+void moe_launch_ep_partial(const MoeDims &d, const MoePlan &plan, const int *recv_meta, const float *eo, int rows,
+                           float *out, cudaStream_t s, uint64_t *launches);
+void moe_launch_ep_final(const MoeDims &d, const MoePlan &plan, const float *recv_y, const int *tok_slot, int world,
+                         int cap, int T, const float *eo, const float *residual, float *out, cudaStream_t s,
+                         uint64_t *launches);
 size_t moe_q4op_halves(int K);   // Q4_K activation operand, halves per vector
-size_t moe_q6op_halves(int K);   // Q6_K activation operand, halves per vector
+size_t moe_dop_bytes(int K);     // bytes per vector of the down operand buffer
 }

@@ -31,7 +31,7 @@ static int num_sms() {
 }
 
 size_t moe_q4op_halves(int K) { return q4op_halves(K); }
-size_t moe_q6op_halves(int K) { return q6op_halves(K); }
+size_t moe_dop_bytes(int K) { return dop_bytes(K); }
 
 // ===========================================================================
 // codec: device twins of quant.c (bit exact; explicit _rn ops, no contraction)
@@ -296,26 +296,24 @@ void moe_launch_synth_f32(uint64_t seed, uint64_t stream, size_t n, double sigma
 // CTA = 32 experts x 256 k x all T tokens; thread = 4 experts x 2 tokens.
 // ===========================================================================
 #define RL_KS 256
-#define RL_WPAD 36
+#define RL_WPAD (RL_KS + 4)
 __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__ Wr, const float *__restrict__ x,
                                                        int T, int H, int E, float *__restrict__ part) {
     extern __shared__ float sm[];
-    float *Wt = sm;                       // [RL_KS][RL_WPAD]
-    float *xt = sm + RL_KS * RL_WPAD;     // [RL_KS][64]
+    float *Ws = sm;                       // [32 experts][RL_WPAD] row-major (k contiguous)
+    float *xt = sm + 32 * RL_WPAD;        // [RL_KS][64] (tokens contiguous)
     const int e0 = blockIdx.x * 32, split = blockIdx.y, k0 = split * RL_KS;
     const int tid = threadIdx.x;
-    // W tile: 32 rows x 256 floats, coalesced float4 loads, transposed store
+    // W tile: coalesced float4 loads, conflict-free float4 stores
     for (int i = tid; i < 32 * (RL_KS / 4); i += 256) {
         const int r = i / (RL_KS / 4), c4 = i % (RL_KS / 4);
         float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
         if (e0 + r < E) w = __ldg(reinterpret_cast<const float4 *>(Wr + (size_t)(e0 + r) * H + k0) + c4);
-        Wt[(4 * c4 + 0) * RL_WPAD + r] = w.x;
-        Wt[(4 * c4 + 1) * RL_WPAD + r] = w.y;
-        Wt[(4 * c4 + 2) * RL_WPAD + r] = w.z;
-        Wt[(4 * c4 + 3) * RL_WPAD + r] = w.w;
+        *reinterpret_cast<float4 *>(Ws + r * RL_WPAD + 4 * c4) = w;
     }
+    // x tile transposed: consecutive threads take consecutive tokens
     for (int i = tid; i < T * (RL_KS / 4); i += 256) {
-        const int t = i / (RL_KS / 4), c4 = i % (RL_KS / 4);
+        const int c4 = i / T, t = i % T;
         const float4 v = __ldg(reinterpret_cast<const float4 *>(x + (size_t)t * H + k0) + c4);
         xt[(4 * c4 + 0) * 64 + t] = v.x;
         xt[(4 * c4 + 1) * 64 + t] = v.y;
@@ -323,18 +321,26 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
         xt[(4 * c4 + 3) * 64 + t] = v.w;
     }
     __syncthreads();
-    const int eg = tid >> 5, tg = tid & 31;
+    const int eg = tid >> 5, tg = tid & 31;  // warp = 4 experts, lane = tokens tg, tg+32
     const bool t0ok = tg < T, t1ok = tg + 32 < T;
     if (!t0ok) return;
     float acc[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
-#pragma unroll 4
-    for (int k = 0; k < RL_KS; k++) {
-        const float4 w = *reinterpret_cast<const float4 *>(Wt + k * RL_WPAD + 4 * eg);
-        const float xa = xt[k * 64 + tg], xb = t1ok ? xt[k * 64 + tg + 32] : 0.f;
-        acc[0][0] = fmaf(w.x, xa, acc[0][0]); acc[0][1] = fmaf(w.x, xb, acc[0][1]);
-        acc[1][0] = fmaf(w.y, xa, acc[1][0]); acc[1][1] = fmaf(w.y, xb, acc[1][1]);
-        acc[2][0] = fmaf(w.z, xa, acc[2][0]); acc[2][1] = fmaf(w.z, xb, acc[2][1]);
-        acc[3][0] = fmaf(w.w, xa, acc[3][0]); acc[3][1] = fmaf(w.w, xb, acc[3][1]);
+    const float *w0 = Ws + (4 * eg) * RL_WPAD;
+#pragma unroll 2
+    for (int k = 0; k < RL_KS; k += 4) {
+        float4 w[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) w[u] = *reinterpret_cast<const float4 *>(w0 + u * RL_WPAD + k);  // broadcast
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const float xa = xt[(k + j) * 64 + tg], xb = t1ok ? xt[(k + j) * 64 + tg + 32] : 0.f;
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const float wv = j == 0 ? w[u].x : j == 1 ? w[u].y : j == 2 ? w[u].z : w[u].w;
+                acc[u][0] = fmaf(wv, xa, acc[u][0]);
+                acc[u][1] = fmaf(wv, xb, acc[u][1]);
+            }
+        }
     }
 #pragma unroll
     for (int u = 0; u < 4; u++) {
@@ -348,7 +354,7 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
 void moe_launch_router_logits(const float *Wr, const float *x, int T, int H, int E, float *part, int n_split,
                               cudaStream_t s, uint64_t *launches) {
     dim3 grid((E + 31) / 32, n_split);
-    const size_t smem = sizeof(float) * (RL_KS * RL_WPAD + RL_KS * 64);
+    const size_t smem = sizeof(float) * (32 * RL_WPAD + RL_KS * 64);
     static bool attr = false;
     if (!attr) {
         cudaFuncSetAttribute(k_router_logits, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -379,12 +385,14 @@ __device__ __forceinline__ float block_max_abs(const float *x, int n, float *red
     return r;
 }
 
-// power-of-two scale s with max|x| * s in (2^9, 2^10]; returns s, sets *inv.
-__device__ __forceinline__ float op_scale(float amax, float *inv) {
+// power-of-two scale s with max|x| * s in [2^(top-1), 2^top); returns s, sets
+// *inv = 1/s.  top = 10 for the fp16 operand (sub-block sums stay below
+// 65504), 20 for the int8-plane operand (|x * s| < 2^20).
+__device__ __forceinline__ float op_scale(float amax, float *inv, int top = 10) {
     if (!(amax > 0.0f) || !isfinite(amax)) { *inv = 1.0f; return 1.0f; }
     int ex;
     frexpf(amax, &ex);  // amax = m 2^ex, m in [0.5, 1)
-    int e = 10 - ex;
+    int e = top - ex;
     if (e > 120) e = 120;
     if (e < -120) e = -120;
     *inv = ldexpf(1.0f, -e);
@@ -396,12 +404,26 @@ __device__ __forceinline__ void split_hl(float v, __half &hi, __half &lo) {
     lo = __float2half_rn(__fsub_rn(v, __half2float(hi)));
 }
 
-// Q4_K operand of one K-vector (all threads of the block).
-__device__ void build_q4op(const float *__restrict__ x, int K, float s, __half *__restrict__ op) {
+// Q4_K operand of one K-vector (all threads of the block).  xsum: smem
+// scratch of K/32 floats for the sub-block sums.
+__device__ void build_q4op(const float *__restrict__ x, int K, float s, __half *__restrict__ op,
+                           float *__restrict__ xsum) {
     const int NB = K / MOE_QK;
-    for (int ent = threadIdx.x; ent < NB * Q4OP_STEPS * 4; ent += blockDim.x) {
-        const int sb = ent / (Q4OP_STEPS * 4), m = (ent / 4) % Q4OP_STEPS, t = ent % 4;
-        __half *o = op + ((size_t)sb * Q4OP_STEPS + m) * 32 + t * 4;
+    for (int sub = threadIdx.x; sub < K / 32; sub += blockDim.x) {
+        float acc = 0.0f;
+        for (int i = 0; i < 32; i++) {
+            __half hi, lo;
+            split_hl(__fmul_rn(x[32 * sub + i], s), hi, lo);
+            acc = __fadd_rn(acc, __fadd_rn(__half2float(hi), __half2float(lo)));
+        }
+        xsum[sub] = acc;
+    }
+    __syncthreads();
+    const __half z = __float2half_rn(0.0f);
+    for (int ent = threadIdx.x; ent < NB * 4 * Q4OP_STEPS; ent += blockDim.x) {
+        const int sb = ent / (4 * Q4OP_STEPS), t = (ent / Q4OP_STEPS) % 4, m = ent % Q4OP_STEPS;
+        __half *o = op + (size_t)sb * Q4OP_HALVES_PER_SB + t * Q4OP_LANE_HALVES + m * 4;  // part 0 (hi)
+        __half *o1 = o + 4 * Q4OP_LANE_HALVES;                                                // part 1 (lo)
         const float *xb = x + sb * MOE_QK;
         if (m < 16) {
 #pragma unroll
@@ -409,56 +431,35 @@ __device__ void build_q4op(const float *__restrict__ x, int K, float s, __half *
                 __half hi, lo;
                 split_hl(__fmul_rn(xb[q4k_k(m, t, j)], s), hi, lo);
                 o[j] = hi;
-                o[16 + j] = lo;
+                o1[j] = lo;
             }
-        } else {
+        } else if (m == 16) {
             const int sa = q4k_min_sub(t);
 #pragma unroll
             for (int u = 0; u < 2; u++) {
-                float acc = 0.0f;
-                for (int i = 0; i < 32; i++) {
-                    __half hi, lo;
-                    split_hl(__fmul_rn(xb[32 * (sa + u) + i], s), hi, lo);
-                    acc = __fadd_rn(acc, __fadd_rn(__half2float(hi), __half2float(lo)));
-                }
                 __half hi, lo;
-                split_hl(acc, hi, lo);
+                split_hl(xsum[sb * 8 + sa + u], hi, lo);
                 o[u] = hi;
-                o[16 + u] = lo;
+                o1[u] = lo;
             }
-            o[2] = o[3] = o[18] = o[19] = __float2half_rn(0.0f);
+            o[2] = o[3] = o1[2] = o1[3] = z;
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; j++) o[j] = o1[j] = z;
         }
     }
 }
 
-// Q6_K operand of one K-vector plus the C-fold term per 16-weight sub-block.
-__device__ void build_q6op(const float *__restrict__ x, int K, float s, __half *__restrict__ op,
-                           float *__restrict__ cf) {
+// Q6_K operand: 21-bit fixed point x * 2^e split into three int8 planes.
+__device__ void build_q6i(const float *__restrict__ x, int K, float s, int8_t *__restrict__ op) {
     const int NB = K / MOE_QK;
-    for (int ent = threadIdx.x; ent < NB * 16 * 4; ent += blockDim.x) {
-        const int sb = ent / 64, st = (ent / 4) % 16, t = ent % 4;
-        __half *o = op + ((size_t)sb * 16 + st) * 32 + t * 4;
-        const float *xb = x + sb * MOE_QK;
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            __half hi, lo;
-            split_hl(__fmul_rn(xb[q6k_k(st, t, j)], s), hi, lo);
-            o[j] = hi;
-            o[16 + j] = lo;
-        }
-    }
-    for (int e = threadIdx.x; e < NB * 16; e += blockDim.x) {
-        const int sb = e / 16, st = e % 16;
-        const float *xb = x + sb * MOE_QK + 16 * st;
-        float acc = 0.0f;
-        for (int i = 0; i < 16; i++) {
-            __half hi, lo;
-            split_hl(__fmul_rn(xb[i], s), hi, lo);
-            acc = __fadd_rn(acc, __fadd_rn(__half2float(hi), __half2float(lo)));
-        }
-        // low sub-blocks (s' < 4) decode to 1024 + q6, high ones to 1024 + 16 q6
-        const float off = ((st & 7) < 4) ? -1056.0f : -1536.0f;
-        cf[e] = __fmul_rn(off, acc);
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        const int v = __float2int_rn(__fmul_rn(x[k], s));  // |v| <= 2^20
+        const int sb = k / MOE_QK, w = k % MOE_QK, st = w / 16, t = (w / 4) % 4, i = w % 4;
+        const size_t off = ((size_t)sb * 4 + t) * 64 + st * 4 + i;
+        op[off] = (int8_t)(v & 127);
+        op[(size_t)NB * Q6I_BYTES_PER_SB + off] = (int8_t)((v >> 7) & 127);
+        op[(size_t)2 * NB * Q6I_BYTES_PER_SB + off] = (int8_t)(v >> 14);
     }
 }
 
@@ -470,6 +471,7 @@ struct RouteArgs {
     const float *part;  int n_split;   // partial logits or nullptr
     const float *logits;               // full logits [T][E] or nullptr
     const float *bias;
+    const float *logit_bias;               // added to the logits before the sigmoid (or nullptr)
     const int *idx_in; const float *w_in;  // given routing (mode 1)
     int mode;                              // 0 route, 1 routing given, 2 shared expert only
     int T;
@@ -501,18 +503,60 @@ __device__ void build_plan_block(const RouteArgs &a) {
         mask[E] = (T >= 64) ? ~0ull : ((1ull << T) - 1ull);
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        int o = 0, c = 0, act = 0;
-        for (int e = 0; e < NE; e++) {
-            off[e] = o; coff[e] = c;
-            o += cnt[e];
-            c += (cnt[e] + MOE_TC - 1) / MOE_TC;
-            if (e < E && cnt[e] > 0) act++;
+    // exclusive scans of the pair counts and chunk counts over experts
+    __shared__ int wsum[3][32], carry[3];
+    if (threadIdx.x == 0) carry[0] = carry[1] = carry[2] = 0;
+    __syncthreads();
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
+    for (int base = 0; base < NE; base += blockDim.x) {
+        const int e = base + threadIdx.x;
+        int v[3] = {0, 0, 0};
+        if (e < NE) {
+            v[0] = cnt[e];
+            v[1] = (cnt[e] + MOE_TC - 1) / MOE_TC;
+            v[2] = (e < E && cnt[e] > 0) ? 1 : 0;
         }
-        off[NE] = o; coff[NE] = c;
-        a.plan.counts[0] = o;
-        a.plan.counts[1] = c;
-        a.plan.counts[2] = act;
+        int inc[3];
+#pragma unroll
+        for (int q = 0; q < 3; q++) {
+            int x = v[q];
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, x, o);
+                if (lane >= o) x += y;
+            }
+            inc[q] = x;
+            if (lane == 31) wsum[q][wid] = x;
+        }
+        __syncthreads();
+        if (threadIdx.x < 32) {
+#pragma unroll
+            for (int q = 0; q < 3; q++) {
+                int x = threadIdx.x < nwarp ? wsum[q][threadIdx.x] : 0;
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int y = __shfl_up_sync(0xffffffffu, x, o);
+                    if (threadIdx.x >= o) x += y;
+                }
+                if (threadIdx.x < nwarp) wsum[q][threadIdx.x] = x;  // inclusive warp totals
+            }
+        }
+        __syncthreads();
+        int excl[3];
+#pragma unroll
+        for (int q = 0; q < 3; q++) excl[q] = carry[q] + (wid ? wsum[q][wid - 1] : 0) + inc[q] - v[q];
+        if (e < NE) { off[e] = excl[0]; coff[e] = excl[1]; }
+        __syncthreads();
+        if (threadIdx.x == blockDim.x - 1) {
+#pragma unroll
+            for (int q = 0; q < 3; q++) carry[q] = excl[q] + v[q];
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        off[NE] = carry[0];
+        coff[NE] = carry[1];
+        a.plan.counts[0] = carry[0];
+        a.plan.counts[1] = carry[1];
+        a.plan.counts[2] = carry[2];
     }
     __syncthreads();
     for (int p = threadIdx.x; p < n_routed; p += blockDim.x) {
@@ -552,6 +596,7 @@ __global__ void __launch_bounds__(256) k_route_plan(RouteArgs a) {
     __shared__ float score[1024], choice[1024];
     __shared__ float gs[64];
     __shared__ float red[32];
+    __shared__ float xsum[1024];  // sub-block sums of the operand (H <= 32768)
     __shared__ int is_last;
     const int t = blockIdx.x;
     const int E = a.d.E, K = a.d.K, G = a.d.n_group, TG = a.d.topk_group;
@@ -564,6 +609,7 @@ __global__ void __launch_bounds__(256) k_route_plan(RouteArgs a) {
                 lg = 0.0f;
                 for (int s = 0; s < a.n_split; s++) lg += a.part[((size_t)s * a.T + t) * E + e];
             }
+            if (a.logit_bias) lg += a.logit_bias[e];
             const float sc = 1.0f / (1.0f + expf(-lg));  // sigmoidf, infer.m:376
             score[e] = sc;
             choice[e] = sc + (a.bias ? a.bias[e] : 0.0f);
@@ -591,10 +637,12 @@ __global__ void __launch_bounds__(256) k_route_plan(RouteArgs a) {
                 if (best >= 0) taken |= 1ull << best;
             }
             // top-K in slot order (infer.m:966-980): scan experts ascending,
-            // replace the first minimum slot when strictly greater.
+            // replace the first minimum slot when strictly greater.  The K
+            // slots stay in registers (fully unrolled over MOE_MAX_K).
             float key[MOE_MAX_K];
             int idx[MOE_MAX_K];
-            for (int k = 0; k < K; k++) { key[k] = -1e30f; idx[k] = 0; }
+#pragma unroll
+            for (int k = 0; k < MOE_MAX_K; k++) { key[k] = -1e30f; idx[k] = 0; }
             int mk = 0;
             float mkey = -1e30f;
             for (int g = 0; g < G; g++) {
@@ -602,25 +650,28 @@ __global__ void __launch_bounds__(256) k_route_plan(RouteArgs a) {
                 for (int e = g * per; e < (g + 1) * per; e++) {
                     const float c = choice[e];
                     if (c > mkey) {
-                        key[mk] = c;
-                        idx[mk] = e;
+#pragma unroll
+                        for (int k = 0; k < MOE_MAX_K; k++)
+                            if (k == mk) { key[k] = c; idx[k] = e; }
                         mk = 0;
                         mkey = key[0];
-                        for (int k = 1; k < K; k++)
-                            if (key[k] < mkey) { mkey = key[k]; mk = k; }
+#pragma unroll
+                        for (int k = 1; k < MOE_MAX_K; k++)
+                            if (k < K && key[k] < mkey) { mkey = key[k]; mk = k; }
                     }
                 }
             }
             float w[MOE_MAX_K], s = 0.0f;
-            for (int k = 0; k < K; k++) { w[k] = score[idx[k]]; s += w[k]; }
-            if (s > 0.0f) {
-                const float f = a.d.scale / s;
-                for (int k = 0; k < K; k++) w[k] *= f;
-            }
-            for (int k = 0; k < K; k++) {
-                a.idx_out[t * K + k] = idx[k];
-                a.w_out[t * K + k] = w[k];
-            }
+#pragma unroll
+            for (int k = 0; k < MOE_MAX_K; k++)
+                if (k < K) { w[k] = score[idx[k]]; s += w[k]; }
+            const float f = s > 0.0f ? a.d.scale / s : 1.0f;
+#pragma unroll
+            for (int k = 0; k < MOE_MAX_K; k++)
+                if (k < K) {
+                    a.idx_out[t * K + k] = idx[k];
+                    a.w_out[t * K + k] = s > 0.0f ? w[k] * f : w[k];
+                }
         }
     } else if (a.mode == 1 && threadIdx.x < K) {
         a.idx_out[t * K + threadIdx.x] = a.idx_in[t * K + threadIdx.x];
@@ -633,7 +684,7 @@ __global__ void __launch_bounds__(256) k_route_plan(RouteArgs a) {
         const float amax = block_max_abs(xr, a.d.H, red);
         float inv;
         const float s = op_scale(amax, &inv);
-        build_q4op(xr, a.d.H, s, a.xop + (size_t)t * q4op_halves(a.d.H));
+        build_q4op(xr, a.d.H, s, a.xop + (size_t)t * q4op_halves(a.d.H), xsum);
         if (threadIdx.x == 0) a.x_inv[t] = inv;
     }
     if (!a.build_plan) return;
@@ -649,12 +700,12 @@ __global__ void __launch_bounds__(256) k_route_plan(RouteArgs a) {
 }
 
 void moe_launch_route_and_plan(const MoeDims &d, const float *part, int n_split, const float *logits,
-                               const float *bias, int mode, const int *idx_in, const float *w_in, int T,
+                               const float *bias, const float *logit_bias, int mode, const int *idx_in, const float *w_in, int T,
                                int *idx_out, float *w_out, const float *x, __half *xop, float *x_inv,
                                int include_shared, int build_plan, const MoePlan &plan, int *counter,
                                cudaStream_t s, uint64_t *launches) {
     RouteArgs a;
-    a.d = d; a.part = part; a.n_split = n_split; a.logits = logits; a.bias = bias;
+    a.d = d; a.part = part; a.n_split = n_split; a.logits = logits; a.bias = bias; a.logit_bias = logit_bias;
     a.idx_in = idx_in; a.w_in = w_in; a.mode = mode; a.T = T; a.idx_out = idx_out; a.w_out = w_out;
     a.x = x; a.xop = xop; a.x_inv = x_inv; a.include_shared = include_shared; a.build_plan = build_plan;
     a.plan = plan; a.counter = counter;
@@ -677,6 +728,10 @@ struct Q4Hdr {
     float d, dmin;
 };
 
+// Scales of the four sub-blocks lane t decodes (u = 2r + hi -> sub-block
+// 4r + 2(t/2) + hi, quant.c:26-34) as half2 pairs, with the magic offsets of
+// the low-nibble (1024) and high-nibble (64) decodes; m2 = the two minimums
+// lane t supplies to the min-term MMA.
 __device__ __forceinline__ void q4_decode_hdr(const uint4 h, int t, Q4Hdr &o) {
     const int q = t >> 1;
     o.d = h2f_bits((uint16_t)(h.x & 0xFFFFu));
@@ -685,147 +740,277 @@ __device__ __forceinline__ void q4_decode_hdr(const uint4 h, int t, Q4Hdr &o) {
     const uint32_t sc_lo = a0 & 0x3F3Fu, m_lo = a1 & 0x3F3Fu;
     const uint32_t sc_hi = (a2 & 0x0F0Fu) | ((a0 >> 2) & 0x3030u);
     const uint32_t m_hi = ((a2 >> 4) & 0x0F0Fu) | ((a1 >> 2) & 0x3030u);
-    const __half2 k1024 = __float2half2_rn(1024.0f), km1024 = __float2half2_rn(-1024.0f);
+    const __half2 k1024 = __float2half2_rn(1024.0f), km1024 = __float2half2_rn(-1024.0f),
+                  km64 = __float2half2_rn(-64.0f);
     o.sc[0] = __hsub2(u32_as_h2(__byte_perm(sc_lo, 0x6464u, 0x4040u)), k1024);
     o.sc[1] = __hsub2(u32_as_h2(__byte_perm(sc_lo, 0x6464u, 0x4141u)), k1024);
     o.sc[2] = __hsub2(u32_as_h2(__byte_perm(sc_hi, 0x6464u, 0x4040u)), k1024);
     o.sc[3] = __hsub2(u32_as_h2(__byte_perm(sc_hi, 0x6464u, 0x4141u)), k1024);
-#pragma unroll
-    for (int u = 0; u < 4; u++) o.nsc[u] = __hmul2(o.sc[u], km1024);
+    o.nsc[0] = __hmul2(o.sc[0], km1024);
+    o.nsc[1] = __hmul2(o.sc[1], km64);
+    o.nsc[2] = __hmul2(o.sc[2], km1024);
+    o.nsc[3] = __hmul2(o.sc[3], km64);
     const uint32_t mw = (t & 1) ? m_hi : m_lo;
     o.m2 = h2_as_u32(__hsub2(u32_as_h2(__byte_perm(mw, 0x6464u, 0x4140u)), k1024));
 }
 
-// sc*q for the two nibbles at bits [0,4) and [16,20) of w (exact fp16)
-__device__ __forceinline__ uint32_t q4_dq(uint32_t w, __half2 sc, __half2 nsc) {
-    const uint32_t h = (w & 0x000F000Fu) | 0x64006400u;
-    return h2_as_u32(__hfma2(u32_as_h2(h), sc, nsc));
+// sc*q (exact fp16) of the low nibbles at bits [0,4) and [16,20) of w: the
+// half with bits 0x6400 | q is 1024 + q.
+__device__ __forceinline__ uint32_t q4_dq_lo(uint32_t w, __half2 sc, __half2 nsc1024) {
+    return h2_as_u32(__hfma2(u32_as_h2((w & 0x000F000Fu) | 0x64006400u), sc, nsc1024));
+}
+// ... of the high nibbles at bits [4,8) and [20,24) without a shift: the
+// half with bits 0x5400 | (q << 4) is 64 + q.
+__device__ __forceinline__ uint32_t q4_dq_hi(uint32_t w, __half2 sc, __half2 nsc64) {
+    return h2_as_u32(__hfma2(u32_as_h2((w & 0x00F000F0u) | 0x54005400u), sc, nsc64));
+}
+
+// raw bytes of one Q4_K super-block for rows g and g+8 of one lane
+struct Q4Raw {
+    uint4 hg, hg8, qg[2], qg8[2];
+};
+
+// ring slot of a lane: word k of stage `slot` at wsm[(slot * W + k) * 32 + lane]
+__device__ __forceinline__ void q4_issue(uint4 *wsm, int slot, int lane, const uint8_t *__restrict__ rg,
+                                         const uint8_t *__restrict__ rg8, int sb, int t) {
+    const uint8_t *bg = rg + (size_t)sb * MOE_Q4K_BYTES, *bg8 = rg8 + (size_t)sb * MOE_Q4K_BYTES;
+    uint4 *w = wsm + slot * MOE_Q4_WORDS * 32 + lane;
+    cp_async16(w + 0 * 32, bg);
+    cp_async16(w + 1 * 32, bg8);
+    cp_async16(w + 2 * 32, bg + 16 + 16 * t);
+    cp_async16(w + 3 * 32, bg + 80 + 16 * t);
+    cp_async16(w + 4 * 32, bg8 + 16 + 16 * t);
+    cp_async16(w + 5 * 32, bg8 + 80 + 16 * t);
+}
+
+__device__ __forceinline__ void q4_read(Q4Raw &r, const uint4 *wsm, int slot, int lane) {
+    const uint4 *w = wsm + slot * MOE_Q4_WORDS * 32 + lane;
+    r.hg = w[0];
+    r.hg8 = w[32];
+    r.qg[0] = w[64];
+    r.qg[1] = w[96];
+    r.qg8[0] = w[128];
+    r.qg8[1] = w[160];
+}
+
+__device__ __forceinline__ uint32_t u4c(const uint4 &v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+
+// One Q4_K super-block of rows (g, g+8) against NT 8-column tiles (4 vectors
+// x {hi, lo}).  opb[n] points at this lane's fragment stream of tile n (a
+// zero stream for empty columns).
+template <int NT>
+__device__ __forceinline__ void q4_compute(const Q4Raw &R, int sb, const __half *const (&opb)[NT],
+                                           float (&acc)[NT][2], int t) {
+    Q4Hdr Hg, Hg8;
+    q4_decode_hdr(R.hg, t, Hg);
+    q4_decode_hdr(R.hg8, t, Hg8);
+    float p1[NT][4], p2[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; n++)
+#pragma unroll
+        for (int c = 0; c < 4; c++) p1[n][c] = 0.0f;
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        uint4 B[NT][4];  // steps 8r .. 8r+7 of this lane: 64 bytes
+#pragma unroll
+        for (int n = 0; n < NT; n++) {
+            const uint4 *bp = reinterpret_cast<const uint4 *>(opb[n] + (size_t)sb * Q4OP_HALVES_PER_SB + r * 32);
+#pragma unroll
+            for (int q = 0; q < 4; q++) B[n][q] = ldg_op16(bp + q);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const uint32_t wg = u4c(R.qg[r], i), wg8 = u4c(R.qg8[r], i);
+            const uint32_t wg_s = wg >> 8, wg8_s = wg8 >> 8;
+            const int ul = 2 * r, uh = 2 * r + 1;
+            // low nibbles (step 2i) then high nibbles (step 2i + 1)
+            const uint32_t l0 = q4_dq_lo(wg, Hg.sc[ul], Hg.nsc[ul]), l2 = q4_dq_lo(wg_s, Hg.sc[ul], Hg.nsc[ul]);
+            const uint32_t l1 = q4_dq_lo(wg8, Hg8.sc[ul], Hg8.nsc[ul]), l3 = q4_dq_lo(wg8_s, Hg8.sc[ul], Hg8.nsc[ul]);
+            const uint32_t h0 = q4_dq_hi(wg, Hg.sc[uh], Hg.nsc[uh]), h2 = q4_dq_hi(wg_s, Hg.sc[uh], Hg.nsc[uh]);
+            const uint32_t h1 = q4_dq_hi(wg8, Hg8.sc[uh], Hg8.nsc[uh]), h3 = q4_dq_hi(wg8_s, Hg8.sc[uh], Hg8.nsc[uh]);
+#pragma unroll
+            for (int n = 0; n < NT; n++) {
+                const uint4 &b = B[n][i];
+                mma_f16_16816(p1[n], l0, l1, l2, l3, b.x, b.y, p1[n][0], p1[n][1], p1[n][2], p1[n][3]);
+                mma_f16_16816(p1[n], h0, h1, h2, h3, b.z, b.w, p1[n][0], p1[n][1], p1[n][2], p1[n][3]);
+            }
+        }
+    }
+#pragma unroll
+    for (int n = 0; n < NT; n++) {
+        const uint4 b = ldg_op16(opb[n] + (size_t)sb * Q4OP_HALVES_PER_SB + 64);  // steps 16 (min) and 17 (pad)
+        mma_f16_16816(p2[n], Hg.m2, Hg8.m2, 0u, 0u, b.x, b.y, 0.f, 0.f, 0.f, 0.f);
+        acc[n][0] = fmaf(Hg.d, p1[n][0] + p1[n][1], fmaf(-Hg.dmin, p2[n][0] + p2[n][1], acc[n][0]));
+        acc[n][1] = fmaf(Hg8.d, p1[n][2] + p1[n][3], fmaf(-Hg8.dmin, p2[n][2] + p2[n][3], acc[n][1]));
+    }
+}
+
+// Per-lane cp.async pipeline: MOE_STAGES - 1 super-blocks in flight while
+// the current one is decoded.  wsm = this warp's ring [MOE_STAGES][6][32].
+template <int NT>
+__device__ __forceinline__ void q4k_warp_rows(const uint8_t *__restrict__ rg, const uint8_t *__restrict__ rg8,
+                                              int sb0, int sb1, const __half *const (&opb)[NT],
+                                              float (&acc)[NT][2], int t, int lane, uint4 *wsm) {
+#pragma unroll
+    for (int s = 0; s < MOE_STAGES - 1; s++) {
+        if (sb0 + s < sb1) q4_issue(wsm, s, lane, rg, rg8, sb0 + s, t);
+        cp_async_commit();
+    }
+    int slot = 0, nslot = MOE_STAGES - 1;
+#pragma unroll 1
+    for (int sb = sb0; sb < sb1; ++sb) {
+        if (sb + MOE_STAGES - 1 < sb1) q4_issue(wsm, nslot, lane, rg, rg8, sb + MOE_STAGES - 1, t);
+        cp_async_commit();
+        cp_async_wait<MOE_STAGES - 1>();
+        Q4Raw R;
+        q4_read(R, wsm, slot, lane);
+        q4_compute<NT>(R, sb, opb, acc, t);
+        slot = (slot + 1 == MOE_STAGES) ? 0 : slot + 1;
+        nslot = (nslot + 1 == MOE_STAGES) ? 0 : nslot + 1;
+    }
+    cp_async_wait<0>();
+}
+
+// ---------------------------------------------------------------------------
+// Q6_K (repacked planes) against the int8-plane operand.  Per 16-weight
+// sub-block s: A = q6 as u8 (nibble | 2 high bits << 4, exact), one u8 x s8
+// MMA for sum q6*x and one s8 x s8 MMA with A = -32 everywhere for -32*sum x,
+// both into the same int32 tile; flushed as acc += sc_s * D (exact int32).
+// At the end of each super-block acc_f += d * acc (fp32).
+// ---------------------------------------------------------------------------
+struct Q6Raw {
+    uint4 ug[3], ug8[3], sg, sg8;
+};
+
+__device__ __forceinline__ void q6_issue(uint4 *wsm, int slot, int lane, const uint8_t *__restrict__ qpl,
+                                         const uint8_t *__restrict__ spl, int nb, int row_g, int sb, int t) {
+    const uint8_t *qg = qpl + ((size_t)row_g * nb + sb) * 192 + 48 * t;
+    const uint8_t *qg8 = qpl + ((size_t)(row_g + 8) * nb + sb) * 192 + 48 * t;
+    uint4 *w = wsm + slot * MOE_Q6_WORDS * 32 + lane;
+#pragma unroll
+    for (int v = 0; v < 3; v++) {
+        cp_async16(w + v * 32, qg + 16 * v);
+        cp_async16(w + (3 + v) * 32, qg8 + 16 * v);
+    }
+    cp_async16(w + 6 * 32, spl + ((size_t)row_g * nb + sb) * 16);
+    cp_async16(w + 7 * 32, spl + ((size_t)(row_g + 8) * nb + sb) * 16);
+}
+
+__device__ __forceinline__ void q6_read(Q6Raw &r, const uint4 *wsm, int slot, int lane) {
+    const uint4 *w = wsm + slot * MOE_Q6_WORDS * 32 + lane;
+#pragma unroll
+    for (int v = 0; v < 3; v++) {
+        r.ug[v] = w[v * 32];
+        r.ug8[v] = w[(3 + v) * 32];
+    }
+    r.sg = w[6 * 32];
+    r.sg8 = w[7 * 32];
+}
+
+// u8 q6 values (one byte per weight) of sub-block sp of a half: nibble word W,
+// qh word Hw (bit pair sp/2 of every byte)
+template <int SP>
+__device__ __forceinline__ uint32_t q6_a(uint32_t W, uint32_t Hw) {
+    const uint32_t nib = SP < 4 ? (W & 0x0F0F0F0Fu) : ((W >> 4) & 0x0F0F0F0Fu);
+    const int f = SP >> 1;
+    const uint32_t hs = f == 0 ? (Hw << 4) : f == 1 ? (Hw << 2) : f == 2 ? Hw : (Hw >> 2);
+    return nib | (hs & 0x30303030u);
 }
 
 template <int NT>
-__device__ __forceinline__ void q4k_warp_rows(const uint8_t *__restrict__ rg, const uint8_t *__restrict__ rg8,
-                                              int sb0, int sb1, const __half *const (&opb)[NT], const bool (&bok)[NT],
-                                              float (&acc)[NT][2], int t) {
-#pragma unroll 1
-    for (int sb = sb0; sb < sb1; ++sb) {
-        const uint8_t *bg = rg + (size_t)sb * MOE_Q4K_BYTES, *bg8 = rg8 + (size_t)sb * MOE_Q4K_BYTES;
-        const uint4 hg = ldg_stream16(bg), hg8 = ldg_stream16(bg8);
-        uint4 qg[2], qg8[2];
-        qg[0] = ldg_stream16(bg + 16 + 16 * t);
-        qg[1] = ldg_stream16(bg + 80 + 16 * t);
-        qg8[0] = ldg_stream16(bg8 + 16 + 16 * t);
-        qg8[1] = ldg_stream16(bg8 + 80 + 16 * t);
-        Q4Hdr Hg, Hg8;
-        q4_decode_hdr(hg, t, Hg);
-        q4_decode_hdr(hg8, t, Hg8);
-        float p1[NT][4], p2[NT][4];
+__device__ __forceinline__ void q6i_compute(const Q6Raw &R, int sb, const int8_t *const (&opb)[NT],
+                                            int (&acc)[NT][4]) {
+    const uint32_t wg[2][6] = {{R.ug[0].x, R.ug[0].y, R.ug[0].z, R.ug[0].w, R.ug[1].x, R.ug[1].y},
+                               {R.ug[1].z, R.ug[1].w, R.ug[2].x, R.ug[2].y, R.ug[2].z, R.ug[2].w}};
+    const uint32_t wg8[2][6] = {{R.ug8[0].x, R.ug8[0].y, R.ug8[0].z, R.ug8[0].w, R.ug8[1].x, R.ug8[1].y},
+                                {R.ug8[1].z, R.ug8[1].w, R.ug8[2].x, R.ug8[2].y, R.ug8[2].z, R.ug8[2].w}};
+    const uint32_t sgw[4] = {R.sg.x, R.sg.y, R.sg.z, R.sg.w}, sg8w[4] = {R.sg8.x, R.sg8.y, R.sg8.z, R.sg8.w};
+    const uint32_t NEG32 = 0xE0E0E0E0u;
 #pragma unroll
-        for (int n = 0; n < NT; n++)
+    for (int h = 0; h < 2; h++) {
 #pragma unroll
-            for (int c = 0; c < 4; c++) p1[n][c] = 0.0f;
-        const __half *opsb[NT];
+        for (int qd = 0; qd < 2; qd++) {  // quarter: steps 8h + 4qd .. +3
+            uint4 B[NT];
 #pragma unroll
-        for (int n = 0; n < NT; n++) opsb[n] = opb[n] + (size_t)sb * Q4OP_HALVES_PER_SB;
+            for (int n = 0; n < NT; n++) B[n] = ldg_op16(opb[n] + (size_t)sb * Q6I_BYTES_PER_SB + h * 32 + qd * 16);
 #pragma unroll
-        for (int r = 0; r < 2; r++) {
+            for (int j = 0; j < 4; j++) {
+                const int sp = 4 * qd + j, s = 8 * h + sp;
+                uint32_t a0, a1;
+#define Q6A(SPV)                                                   \
+    a0 = q6_a<SPV>(wg[h][(SPV)&3], wg[h][4 + ((SPV)&1)]);          \
+    a1 = q6_a<SPV>(wg8[h][(SPV)&3], wg8[h][4 + ((SPV)&1)]);
+                switch (sp) {
+                    case 0: Q6A(0) break;
+                    case 1: Q6A(1) break;
+                    case 2: Q6A(2) break;
+                    case 3: Q6A(3) break;
+                    case 4: Q6A(4) break;
+                    case 5: Q6A(5) break;
+                    case 6: Q6A(6) break;
+                    default: Q6A(7) break;
+                }
+#undef Q6A
+                int scg, scg8;
+                switch (s & 3) {
+                    case 0: scg = sext_byte<0>(sgw[s >> 2]); scg8 = sext_byte<0>(sg8w[s >> 2]); break;
+                    case 1: scg = sext_byte<1>(sgw[s >> 2]); scg8 = sext_byte<1>(sg8w[s >> 2]); break;
+                    case 2: scg = sext_byte<2>(sgw[s >> 2]); scg8 = sext_byte<2>(sg8w[s >> 2]); break;
+                    default: scg = sext_byte<3>(sgw[s >> 2]); scg8 = sext_byte<3>(sg8w[s >> 2]); break;
+                }
 #pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const uint32_t wg = (i == 0) ? qg[r].x : (i == 1) ? qg[r].y : (i == 2) ? qg[r].z : qg[r].w;
-                const uint32_t wg8 = (i == 0) ? qg8[r].x : (i == 1) ? qg8[r].y : (i == 2) ? qg8[r].z : qg8[r].w;
-#pragma unroll
-                for (int hi = 0; hi < 2; hi++) {
-                    const int m = 8 * r + 2 * i + hi, u = 2 * r + hi;
-                    const uint32_t a0 = q4_dq(wg >> (4 * hi), Hg.sc[u], Hg.nsc[u]);
-                    const uint32_t a2 = q4_dq(wg >> (8 + 4 * hi), Hg.sc[u], Hg.nsc[u]);
-                    const uint32_t a1 = q4_dq(wg8 >> (4 * hi), Hg8.sc[u], Hg8.nsc[u]);
-                    const uint32_t a3 = q4_dq(wg8 >> (8 + 4 * hi), Hg8.sc[u], Hg8.nsc[u]);
-#pragma unroll
-                    for (int n = 0; n < NT; n++) {
-                        uint2 b = make_uint2(0u, 0u);
-                        if (bok[n]) b = ldg_op8(opsb[n] + m * 32);
-                        mma_f16_16816(p1[n], a0, a1, a2, a3, b.x, b.y, p1[n][0], p1[n][1], p1[n][2], p1[n][3]);
-                    }
+                for (int n = 0; n < NT; n++) {
+                    const uint32_t b = u4c(B[n], j);
+                    int dd[4];
+                    mma_u8s8_16816(dd, a0, a1, b, 0, 0, 0, 0);
+                    mma_s8s8_16816(dd, NEG32, NEG32, b, dd[0], dd[1], dd[2], dd[3]);
+                    acc[n][0] += scg * dd[0];
+                    acc[n][1] += scg * dd[1];
+                    acc[n][2] += scg8 * dd[2];
+                    acc[n][3] += scg8 * dd[3];
                 }
             }
-        }
-#pragma unroll
-        for (int n = 0; n < NT; n++) {
-            uint2 b = make_uint2(0u, 0u);
-            if (bok[n]) b = ldg_op8(opsb[n] + 16 * 32);
-            mma_f16_16816(p2[n], Hg.m2, Hg8.m2, 0u, 0u, b.x, b.y, 0.f, 0.f, 0.f, 0.f);
-            acc[n][0] = fmaf(Hg.d, p1[n][0] + p1[n][1], fmaf(-Hg.dmin, p2[n][0] + p2[n][1], acc[n][0]));
-            acc[n][1] = fmaf(Hg8.d, p1[n][2] + p1[n][3], fmaf(-Hg8.dmin, p2[n][2] + p2[n][3], acc[n][1]));
         }
     }
 }
 
-// ===========================================================================
-// Q6_K warp tile (repacked layout): one MMA per 16-weight sub-block with the
-// -32 offset and the decode magic folded into the C operand, flushed as
-// acc += d*sc*D (quant.c:63-92 algebra, fp32).
-// ===========================================================================
 template <int NT>
 __device__ __forceinline__ void q6k_warp_rows(const uint8_t *__restrict__ W, int rows, int nb, int row_g,
-                                              const __half *const (&opb)[NT], const bool (&bok)[NT],
-                                              const float *const (&cfb)[NT], const bool (&cok)[NT],
-                                              float (&acc)[NT][2], int t) {
-    const int row_g8 = row_g + 8;
+                                              const int8_t *const (&opb)[NT], float (&accf)[NT][4], int t,
+                                              int lane, uint4 *wsm) {
     const int nbp = q6r_nb_pad(nb);
     const uint8_t *qpl = W, *spl = W + q6r_plane_s_off(rows, nb);
     const uint16_t *dpl = reinterpret_cast<const uint16_t *>(W + q6r_plane_d_off(rows, nb));
+#pragma unroll
+    for (int s = 0; s < MOE_STAGES - 1; s++) {
+        if (s < nb) q6_issue(wsm, s, lane, qpl, spl, nb, row_g, s, t);
+        cp_async_commit();
+    }
+    int slot = 0, nslot = MOE_STAGES - 1;
 #pragma unroll 1
     for (int sb = 0; sb < nb; ++sb) {
-        const uint8_t *qg = qpl + ((size_t)row_g * nb + sb) * 192 + 48 * t;
-        const uint8_t *qg8 = qpl + ((size_t)row_g8 * nb + sb) * 192 + 48 * t;
-        uint4 ug[3], ug8[3];
-#pragma unroll
-        for (int v = 0; v < 3; v++) {
-            ug[v] = ldg_stream16(qg + 16 * v);
-            ug8[v] = ldg_stream16(qg8 + 16 * v);
-        }
-        const uint4 sg = ldg_stream16(spl + ((size_t)row_g * nb + sb) * 16);
-        const uint4 sg8 = ldg_stream16(spl + ((size_t)row_g8 * nb + sb) * 16);
+        if (sb + MOE_STAGES - 1 < nb) q6_issue(wsm, nslot, lane, qpl, spl, nb, row_g, sb + MOE_STAGES - 1, t);
+        cp_async_commit();
         const float dg = h2f_bits(__ldg(dpl + (size_t)row_g * nbp + sb));
-        const float dg8 = h2f_bits(__ldg(dpl + (size_t)row_g8 * nbp + sb));
-        // words [h][0..3] = ql, [h][4..5] = qh
-        const uint32_t wg[2][6] = {{ug[0].x, ug[0].y, ug[0].z, ug[0].w, ug[1].x, ug[1].y},
-                                   {ug[1].z, ug[1].w, ug[2].x, ug[2].y, ug[2].z, ug[2].w}};
-        const uint32_t wg8[2][6] = {{ug8[0].x, ug8[0].y, ug8[0].z, ug8[0].w, ug8[1].x, ug8[1].y},
-                                    {ug8[1].z, ug8[1].w, ug8[2].x, ug8[2].y, ug8[2].z, ug8[2].w}};
-        const uint32_t sgw[4] = {sg.x, sg.y, sg.z, sg.w}, sg8w[4] = {sg8.x, sg8.y, sg8.z, sg8.w};
-        const size_t sbo = (size_t)sb * Q6OP_HALVES_PER_SB;
+        const float dg8 = h2f_bits(__ldg(dpl + (size_t)(row_g + 8) * nbp + sb));
+        cp_async_wait<MOE_STAGES - 1>();
+        Q6Raw R;
+        q6_read(R, wsm, slot, lane);
+        int acc[NT][4];
 #pragma unroll
-        for (int h = 0; h < 2; h++) {
+        for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0;
+        q6i_compute<NT>(R, sb, opb, acc);
 #pragma unroll
-            for (int sp = 0; sp < 8; sp++) {
-                const int s = 8 * h + sp;
-                const bool hiT = sp >= 4;
-                const int f = sp >> 1;
-                const uint32_t M1 = hiT ? 0x00F000F0u : 0x000F000Fu;
-                const uint32_t M2 = hiT ? 0x03000300u : 0x00300030u;
-                const int she = (f & 1) ? 2 : 4, sho = (f & 1) ? 6 : 4;
-                const uint32_t Wg = wg[h][sp & 3], Hg = wg[h][4 + (sp & 1)];
-                const uint32_t Wg8 = wg8[h][sp & 3], Hg8 = wg8[h][4 + (sp & 1)];
-                const uint32_t a0 = (Wg & M1) | ((Hg << she) & M2) | 0x64006400u;
-                const uint32_t a2 = ((Wg >> 8) & M1) | ((Hg >> sho) & M2) | 0x64006400u;
-                const uint32_t a1 = (Wg8 & M1) | ((Hg8 << she) & M2) | 0x64006400u;
-                const uint32_t a3 = ((Wg8 >> 8) & M1) | ((Hg8 >> sho) & M2) | 0x64006400u;
-                const float fs = hiT ? 0.0625f : 1.0f;
-                const float dsg = dg * fs * (float)(int8_t)(sgw[s >> 2] >> (8 * (s & 3)));
-                const float dsg8 = dg8 * fs * (float)(int8_t)(sg8w[s >> 2] >> (8 * (s & 3)));
-#pragma unroll
-                for (int n = 0; n < NT; n++) {
-                    uint2 b = make_uint2(0u, 0u);
-                    if (bok[n]) b = ldg_op8(opb[n] + sbo + s * 32);
-                    const float cf = cok[n] ? __ldg(cfb[n] + sb * 16 + s) : 0.0f;
-                    float dd[4];
-                    mma_f16_16816(dd, a0, a1, a2, a3, b.x, b.y, cf, 0.f, cf, 0.f);
-                    acc[n][0] = fmaf(dsg, dd[0] + dd[1], acc[n][0]);
-                    acc[n][1] = fmaf(dsg8, dd[2] + dd[3], acc[n][1]);
-                }
-            }
+        for (int n = 0; n < NT; n++) {
+            accf[n][0] = fmaf(dg, (float)acc[n][0], accf[n][0]);
+            accf[n][1] = fmaf(dg, (float)acc[n][1], accf[n][1]);
+            accf[n][2] = fmaf(dg8, (float)acc[n][2], accf[n][2]);
+            accf[n][3] = fmaf(dg8, (float)acc[n][3], accf[n][3]);
         }
+        slot = (slot + 1 == MOE_STAGES) ? 0 : slot + 1;
+        nslot = (nslot + 1 == MOE_STAGES) ? 0 : nslot + 1;
     }
+    cp_async_wait<0>();
 }
 
 __device__ __forceinline__ int expert_slot(const MoeLayerDev &L, int E, int e) {
@@ -836,48 +1021,58 @@ __device__ __forceinline__ int expert_slot(const MoeLayerDev &L, int E, int e) {
 // gate/up: CTA item = (chunk, 64 rows); warp w: row tile w&3, K half w>>2.
 // act[pair][row] = silu(gate) * up  (infer.m:378-383)
 // ===========================================================================
-#define GU_NT 2
-__global__ void __launch_bounds__(256, 2) k_gateup(MoeDims d, MoeLayerDev L, MoePlan plan,
-                                                   const __half *__restrict__ xop, const float *__restrict__ x_inv,
-                                                   float *__restrict__ act) {
-    __shared__ float red[2][2][MOE_ROWS_GU][MOE_TC + 1];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int rt = warp & 3, kh = warp >> 2;
-    const int n_chunks = plan.counts[1];
-    const int n_rg = d.I / MOE_ROWS_GU;
-    const int n_items = n_chunks * n_rg;
+// one (chunk, row group) item: warp (rt, kh) runs gate then up for its 16
+// rows over its K half and leaves partial sums in `red`
+template <int NT>
+__device__ __forceinline__ void gateup_item(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan,
+                                            const __half *__restrict__ xop, const __half *__restrict__ zop, int e,
+                                            int p0, int ntok, int rgi, int rt, int kh, int g, int t, int lane,
+                                            uint4 *wsm, float (*red)[2][MOE_ROWS_GU][MOE_TC + 1]) {
     const int NB = d.H / MOE_QK, nbh = NB / 2;
     const int sb0 = kh ? nbh : 0, sb1 = kh ? NB : nbh;
     const size_t rowb = (size_t)NB * MOE_Q4K_BYTES;
     const size_t opstride = q4op_halves(d.H);
+    const uint8_t *ex = L.experts + (size_t)expert_slot(L, d.E, e) * L.expert_stride;
+    const int r0 = rgi * MOE_ROWS_GU + rt * 16;
+    const int lane_off = (g & 1) * 4 * Q4OP_LANE_HALVES + t * Q4OP_LANE_HALVES;
+    const __half *opb[NT];
+#pragma unroll
+    for (int n = 0; n < NT; n++) {
+        const int tk = 4 * n + (g >> 1);
+        opb[n] = (tk < ntok ? xop + (size_t)plan.pair_token[p0 + tk] * opstride : zop) + lane_off;
+    }
+#pragma unroll 1
+    for (int mat = 0; mat < 2; mat++) {
+        const uint8_t *Wm = ex + (size_t)mat * L.gate_bytes;
+        float acc[NT][2];
+#pragma unroll
+        for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = 0.0f;
+        q4k_warp_rows<NT>(Wm + (size_t)(r0 + g) * rowb, Wm + (size_t)(r0 + g + 8) * rowb, sb0, sb1, opb, acc, t,
+                          lane, wsm);
+#pragma unroll
+        for (int n = 0; n < NT; n++) {
+            red[kh][mat][rt * 16 + g][4 * n + t] = acc[n][0];
+            red[kh][mat][rt * 16 + g + 8][4 * n + t] = acc[n][1];
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256, 2) k_gateup(MoeDims d, MoeLayerDev L, MoePlan plan,
+                                                   const __half *__restrict__ xop, const __half *__restrict__ zop,
+                                                   const float *__restrict__ x_inv, float *__restrict__ act) {
+    __shared__ float red[2][2][MOE_ROWS_GU][MOE_TC + 1];
+    extern __shared__ uint4 ring[];  // [8 warps][MOE_STAGES][6][32]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    uint4 *wsm = ring + (size_t)warp * MOE_STAGES * MOE_Q4_WORDS * 32;
+    const int rt = warp & 3, kh = warp >> 2;
+    const int n_chunks = plan.counts[1];
+    const int n_rg = d.I / MOE_ROWS_GU;
+    const int n_items = n_chunks * n_rg;
     for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
         const int rgi = item / n_chunks, c = item % n_chunks;
         const int e = plan.chunk_expert[c], p0 = plan.chunk_pair0[c], ntok = plan.chunk_ntok[c];
-        const uint8_t *ex = L.experts + (size_t)expert_slot(L, d.E, e) * L.expert_stride;
-        const int r0 = rgi * MOE_ROWS_GU + rt * 16;
-        const __half *opb[GU_NT];
-        bool bok[GU_NT];
-#pragma unroll
-        for (int n = 0; n < GU_NT; n++) {
-            const int tk = 4 * n + (g >> 1);
-            bok[n] = tk < ntok;
-            const int tok = bok[n] ? plan.pair_token[p0 + tk] : 0;
-            opb[n] = xop + (size_t)tok * opstride + (g & 1) * 16 + t * 4;
-        }
-#pragma unroll 1
-        for (int mat = 0; mat < 2; mat++) {
-            const uint8_t *Wm = ex + (size_t)mat * L.gate_bytes;
-            float acc[GU_NT][2];
-#pragma unroll
-            for (int n = 0; n < GU_NT; n++) acc[n][0] = acc[n][1] = 0.0f;
-            q4k_warp_rows<GU_NT>(Wm + (size_t)(r0 + g) * rowb, Wm + (size_t)(r0 + g + 8) * rowb, sb0, sb1, opb, bok,
-                                 acc, t);
-#pragma unroll
-            for (int n = 0; n < GU_NT; n++) {
-                red[kh][mat][rt * 16 + g][4 * n + t] = acc[n][0];
-                red[kh][mat][rt * 16 + g + 8][4 * n + t] = acc[n][1];
-            }
-        }
+        if (ntok <= 4) gateup_item<1>(d, L, plan, xop, zop, e, p0, ntok, rgi, rt, kh, g, t, lane, wsm, red);
+        else gateup_item<2>(d, L, plan, xop, zop, e, p0, ntok, rgi, rt, kh, g, t, lane, wsm, red);
         __syncthreads();
         for (int i = threadIdx.x; i < MOE_ROWS_GU * ntok; i += blockDim.x) {
             const int row = i / ntok, tk = i % ntok;
@@ -892,110 +1087,217 @@ __global__ void __launch_bounds__(256, 2) k_gateup(MoeDims d, MoeLayerDev L, Moe
 }
 
 void moe_launch_gateup(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const __half *xop,
-                       const float *x_inv, float *act, int max_items, cudaStream_t s, uint64_t *launches) {
+                       const __half *zop, const float *x_inv, float *act, int max_items, cudaStream_t s,
+                       uint64_t *launches) {
     int grid = num_sms() * 2;
     if (grid > max_items) grid = max_items;
     if (grid < 1) grid = 1;
-    k_gateup<<<grid, 256, 0, s>>>(d, L, plan, xop, x_inv, act);
+    const size_t smem = sizeof(uint4) * 8 * MOE_STAGES * MOE_Q4_WORDS * 32;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(k_gateup, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attr = true;
+    }
+    k_gateup<<<grid, 256, smem, s>>>(d, L, plan, xop, zop, x_inv, act);
     LAUNCH_COUNT(launches);
 }
 
 // ===========================================================================
-// down operand: per pair, scale + hi/lo split of act into the layout of the
-// expert's down type.
+// down operand: per pair, scale + operand of the expert's down type
 // ===========================================================================
 __global__ void __launch_bounds__(256) k_prep_down(MoeDims d, MoeLayerDev L, MoePlan plan,
-                                                   const float *__restrict__ act, __half *__restrict__ dop,
-                                                   float *__restrict__ dcf, float *__restrict__ d_inv) {
+                                                   const float *__restrict__ act, uint8_t *__restrict__ dop,
+                                                   float *__restrict__ d_inv) {
     __shared__ float red[32];
+    __shared__ float xsum[1024];
     const int n_pairs = plan.counts[0];
-    const size_t opst = q4op_halves(d.I) > q6op_halves(d.I) ? q4op_halves(d.I) : q6op_halves(d.I);
+    const size_t opst = dop_bytes(d.I);
     for (int p = blockIdx.x; p < n_pairs; p += gridDim.x) {
         const float *a = act + (size_t)p * d.I;
         const float amax = block_max_abs(a, d.I, red);
-        float inv;
-        const float s = op_scale(amax, &inv);
         const int e = plan.pair_expert[p];
         const int ty = (e == d.E) ? L.sh_down_type : L.down_type;
-        if (ty == 14) build_q6op(a, d.I, s, dop + (size_t)p * opst, dcf + (size_t)p * (d.I / MOE_QK) * 16);
-        else build_q4op(a, d.I, s, dop + (size_t)p * opst);
+        float inv;
+        if (ty == 14) {
+            const float s = op_scale(amax, &inv, 20);
+            build_q6i(a, d.I, s, reinterpret_cast<int8_t *>(dop + (size_t)p * opst));
+        } else {
+            const float s = op_scale(amax, &inv);
+            build_q4op(a, d.I, s, reinterpret_cast<__half *>(dop + (size_t)p * opst), xsum);
+        }
         if (threadIdx.x == 0) d_inv[p] = inv;
         __syncthreads();
     }
 }
 
+// Q4_K operand of activation rows: rows [0, R) come from `recv` (skipped when
+// their metadata says the slot is empty), rows [R, R + T) from `local`.
+__global__ void __launch_bounds__(256) k_prep_rows(const float *__restrict__ recv, const int *__restrict__ meta,
+                                                   int meta_w, int R, const float *__restrict__ local, int H,
+                                                   __half *__restrict__ xop, float *__restrict__ x_inv) {
+    __shared__ float red[32];
+    __shared__ float xsum[1024];
+    const int r = blockIdx.x;
+    if (r < R && !meta[(size_t)r * meta_w]) return;
+    const float *x = r < R ? recv + (size_t)r * H : local + (size_t)(r - R) * H;
+    const float amax = block_max_abs(x, H, red);
+    float inv;
+    const float s = op_scale(amax, &inv);
+    build_q4op(x, H, s, xop + (size_t)r * q4op_halves(H), xsum);
+    if (threadIdx.x == 0) x_inv[r] = inv;
+}
+
+void moe_launch_prep_rows(const float *recv, const int *meta, int meta_w, int R, const float *local, int T, int H,
+                          __half *xop, float *x_inv, cudaStream_t s, uint64_t *launches) {
+    k_prep_rows<<<R + T, 256, 0, s>>>(recv, meta, meta_w, R, local, H, xop, x_inv);
+    LAUNCH_COUNT(launches);
+}
+
 void moe_launch_prep_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const float *act,
-                          __half *dop, float *dcf, float *d_inv, int max_pairs, cudaStream_t s,
-                          uint64_t *launches) {
+                          uint8_t *dop, float *d_inv, int max_pairs, cudaStream_t s, uint64_t *launches) {
     int grid = max_pairs;
     if (grid > num_sms() * 4) grid = num_sms() * 4;
     if (grid < 1) grid = 1;
-    k_prep_down<<<grid, 256, 0, s>>>(d, L, plan, act, dop, dcf, d_inv);
+    k_prep_down<<<grid, 256, 0, s>>>(d, L, plan, act, dop, d_inv);
     LAUNCH_COUNT(launches);
 }
 
 // ===========================================================================
 // down: warp task = (chunk, 16 rows of H); eo[pair][row]
 // ===========================================================================
-#define DN_NT 2
-__global__ void __launch_bounds__(256, 2) k_down(MoeDims d, MoeLayerDev L, MoePlan plan,
-                                                 const __half *__restrict__ dop, const float *__restrict__ dcf,
-                                                 const float *__restrict__ d_inv, float *__restrict__ eo) {
-    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int nw = gridDim.x * (blockDim.x >> 5);
-    const int n_chunks = plan.counts[1];
-    const int n_rt = d.H / 16;
-    const int n_tasks = n_chunks * n_rt;
+// Q6_K: n-tile n holds vectors 2n, 2n+1, three planes each (columns 0-2,
+// 3-5; columns 6, 7 empty).  NT = ceil(ntok / 2).
+template <int NT>
+__device__ __forceinline__ void down_task_q6(const MoeDims &d, const MoeLayerDev &L, const uint8_t *__restrict__ dop,
+                                             const uint8_t *__restrict__ zop, const float *__restrict__ d_inv,
+                                             float *__restrict__ eo, int e, int p0, int ntok, int rt, int g, int t,
+                                             int lane, uint4 *wsm) {
     const int NB = d.I / MOE_QK;
-    const size_t opst = q4op_halves(d.I) > q6op_halves(d.I) ? q4op_halves(d.I) : q6op_halves(d.I);
-    for (int task = gw; task < n_tasks; task += nw) {
-        const int rt = task / n_chunks, c = task % n_chunks;
-        const int e = plan.chunk_expert[c], p0 = plan.chunk_pair0[c], ntok = plan.chunk_ntok[c];
-        const uint8_t *Wd = L.experts + (size_t)expert_slot(L, d.E, e) * L.expert_stride + 2 * L.gate_bytes;
-        const int ty = (e == d.E) ? L.sh_down_type : L.down_type;
-        const int r0 = rt * 16;
-        const __half *opb[DN_NT];
-        const float *cfb[DN_NT];
-        bool bok[DN_NT], cok[DN_NT];
+    const size_t opst = dop_bytes(d.I);
+    const uint8_t *Wd = L.experts + (size_t)expert_slot(L, d.E, e) * L.expert_stride + 2 * L.gate_bytes;
+    const int r0 = rt * 16;
+    const int8_t *opb[NT];
 #pragma unroll
-        for (int n = 0; n < DN_NT; n++) {
-            const int tb = 4 * n + (g >> 1), tc = 4 * n + t;
-            bok[n] = tb < ntok;
-            cok[n] = tc < ntok;
-            opb[n] = dop + (size_t)(p0 + (bok[n] ? tb : 0)) * opst + (g & 1) * 16 + t * 4;
-            cfb[n] = dcf + (size_t)(p0 + (cok[n] ? tc : 0)) * NB * 16;
+    for (int n = 0; n < NT; n++) {
+        const int tk = 2 * n + (g >= 3 ? 1 : 0), plane = g % 3;
+        const bool ok = g < 6 && tk < ntok;
+        const uint8_t *base = ok ? dop + (size_t)(p0 + tk) * opst : zop;
+        opb[n] = reinterpret_cast<const int8_t *>(base + (size_t)(ok ? plane : 0) * NB * Q6I_BYTES_PER_SB + t * 64);
+    }
+    float accf[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; n++) accf[n][0] = accf[n][1] = accf[n][2] = accf[n][3] = 0.0f;
+    q6k_warp_rows<NT>(Wd, d.H, NB, r0 + g, opb, accf, t, lane, wsm);
+    // combine the planes: column c of tile n = vector 2n + c/3, plane c%3
+#pragma unroll
+    for (int n = 0; n < NT; n++) {
+        float va[2], vb[2];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {  // rows g (h=0) and g+8 (h=1)
+            const float c0 = accf[n][2 * h], c1 = accf[n][2 * h + 1];
+            va[h] = t == 0 ? c0 + 128.0f * c1 : (t == 1 ? 16384.0f * c0 : 0.0f);
+            vb[h] = t == 1 ? c1 : (t == 2 ? 128.0f * c0 + 16384.0f * c1 : 0.0f);
+#pragma unroll
+            for (int o = 1; o < 4; o <<= 1) {
+                va[h] += __shfl_xor_sync(0xffffffffu, va[h], o);
+                vb[h] += __shfl_xor_sync(0xffffffffu, vb[h], o);
+            }
         }
-        float acc[DN_NT][2];
-#pragma unroll
-        for (int n = 0; n < DN_NT; n++) acc[n][0] = acc[n][1] = 0.0f;
-        if (ty == 14) {
-            q6k_warp_rows<DN_NT>(Wd, d.H, NB, r0 + g, opb, bok, cfb, cok, acc, t);
-        } else {
-            const size_t rowb = (size_t)NB * MOE_Q4K_BYTES;
-            q4k_warp_rows<DN_NT>(Wd + (size_t)(r0 + g) * rowb, Wd + (size_t)(r0 + g + 8) * rowb, 0, NB, opb, bok,
-                                 acc, t);
-        }
-#pragma unroll
-        for (int n = 0; n < DN_NT; n++) {
-            if (!cok[n]) continue;
-            const int pair = p0 + 4 * n + t;
-            const float inv = d_inv[pair];
-            eo[(size_t)pair * d.H + r0 + g] = acc[n][0] * inv;
-            eo[(size_t)pair * d.H + r0 + g + 8] = acc[n][1] * inv;
+        if (t < 2) {
+            const int tk = 2 * n + t;
+            if (tk < ntok) {
+                const int pair = p0 + tk;
+                const float inv = d_inv[pair];
+                eo[(size_t)pair * d.H + r0 + g] = (t == 0 ? va[0] : vb[0]) * inv;
+                eo[(size_t)pair * d.H + r0 + g + 8] = (t == 0 ? va[1] : vb[1]) * inv;
+            }
         }
     }
 }
 
-void moe_launch_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const __half *dop,
-                     const float *dcf, const float *d_inv, float *eo, int max_items, cudaStream_t s,
+template <int NT>
+__device__ __forceinline__ void down_task_q4(const MoeDims &d, const MoeLayerDev &L, const uint8_t *__restrict__ dop,
+                                             const uint8_t *__restrict__ zop, const float *__restrict__ d_inv,
+                                             float *__restrict__ eo, int e, int p0, int ntok, int rt, int g, int t,
+                                             int lane, uint4 *wsm) {
+    const int NB = d.I / MOE_QK;
+    const size_t opst = dop_bytes(d.I);
+    const uint8_t *Wd = L.experts + (size_t)expert_slot(L, d.E, e) * L.expert_stride + 2 * L.gate_bytes;
+    const int r0 = rt * 16;
+    const int lane_off = (g & 1) * 4 * Q4OP_LANE_HALVES + t * Q4OP_LANE_HALVES;
+    const __half *opb[NT];
+#pragma unroll
+    for (int n = 0; n < NT; n++) {
+        const int tb = 4 * n + (g >> 1);
+        opb[n] = reinterpret_cast<const __half *>(tb < ntok ? dop + (size_t)(p0 + tb) * opst : zop) + lane_off;
+    }
+    float acc[NT][2];
+#pragma unroll
+    for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = 0.0f;
+    const size_t rowb = (size_t)NB * MOE_Q4K_BYTES;
+    q4k_warp_rows<NT>(Wd + (size_t)(r0 + g) * rowb, Wd + (size_t)(r0 + g + 8) * rowb, 0, NB, opb, acc, t, lane, wsm);
+#pragma unroll
+    for (int n = 0; n < NT; n++) {
+        const int tc = 4 * n + t;
+        if (tc >= ntok) continue;
+        const int pair = p0 + tc;
+        const float inv = d_inv[pair];
+        eo[(size_t)pair * d.H + r0 + g] = acc[n][0] * inv;
+        eo[(size_t)pair * d.H + r0 + g + 8] = acc[n][1] * inv;
+    }
+}
+
+// One instance per down type; chunks of the other type are skipped.
+template <int TY>
+__global__ void __launch_bounds__(256, 2) k_down(MoeDims d, MoeLayerDev L, MoePlan plan,
+                                                 const uint8_t *__restrict__ dop, const uint8_t *__restrict__ zop,
+                                                 const float *__restrict__ d_inv, float *__restrict__ eo) {
+    extern __shared__ uint4 ring[];  // [8 warps][MOE_STAGES][words][32]
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+    uint4 *wsm = ring + (size_t)(threadIdx.x >> 5) * MOE_STAGES * (TY == 14 ? MOE_Q6_WORDS : MOE_Q4_WORDS) * 32;
+    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int nw = gridDim.x * (blockDim.x >> 5);
+    const int n_chunks = plan.counts[1];
+    const int n_tasks = n_chunks * (d.H / 16);
+    for (int task = gw; task < n_tasks; task += nw) {
+        const int rt = task / n_chunks, c = task % n_chunks;
+        const int e = plan.chunk_expert[c], p0 = plan.chunk_pair0[c], ntok = plan.chunk_ntok[c];
+        if (((e == d.E) ? L.sh_down_type : L.down_type) != TY) continue;
+        if (TY == 14) {
+            if (ntok <= 2) down_task_q6<1>(d, L, dop, zop, d_inv, eo, e, p0, ntok, rt, g, t, lane, wsm);
+            else if (ntok <= 4) down_task_q6<2>(d, L, dop, zop, d_inv, eo, e, p0, ntok, rt, g, t, lane, wsm);
+            else if (ntok <= 6) down_task_q6<3>(d, L, dop, zop, d_inv, eo, e, p0, ntok, rt, g, t, lane, wsm);
+            else down_task_q6<4>(d, L, dop, zop, d_inv, eo, e, p0, ntok, rt, g, t, lane, wsm);
+        } else {
+            if (ntok <= 4) down_task_q4<1>(d, L, dop, zop, d_inv, eo, e, p0, ntok, rt, g, t, lane, wsm);
+            else down_task_q4<2>(d, L, dop, zop, d_inv, eo, e, p0, ntok, rt, g, t, lane, wsm);
+        }
+    }
+}
+
+void moe_launch_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const uint8_t *dop,
+                     const uint8_t *zop, const float *d_inv, float *eo, int max_items, cudaStream_t s,
                      uint64_t *launches) {
     int grid = num_sms() * 2;
     const int need = (max_items + 7) / 8;
     if (grid > need) grid = need;
     if (grid < 1) grid = 1;
-    k_down<<<grid, 256, 0, s>>>(d, L, plan, dop, dcf, d_inv, eo);
-    LAUNCH_COUNT(launches);
+    const size_t sm6 = sizeof(uint4) * 8 * MOE_STAGES * MOE_Q6_WORDS * 32;
+    const size_t sm4 = sizeof(uint4) * 8 * MOE_STAGES * MOE_Q4_WORDS * 32;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(k_down<14>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm6);
+        cudaFuncSetAttribute(k_down<12>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm4);
+        attr = true;
+    }
+    if (L.down_type == 14 || L.sh_down_type == 14) {
+        k_down<14><<<grid, 256, sm6, s>>>(d, L, plan, dop, zop, d_inv, eo);
+        LAUNCH_COUNT(launches);
+    }
+    if (L.down_type == 12 || L.sh_down_type == 12) {
+        k_down<12><<<grid, 256, sm4, s>>>(d, L, plan, dop, zop, d_inv, eo);
+        LAUNCH_COUNT(launches);
+    }
 }
 
 // ===========================================================================

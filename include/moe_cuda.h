@@ -117,11 +117,16 @@ int moe_load_layer_packed(moe_ctx *ctx, int layer, const void *layer_blob, size_
  * bias N(0, bias_sigma).  Bit-identical to the host generator of the test
  * oracle. */
 int moe_init_layer_synthetic(moe_ctx *ctx, int layer, uint64_t seed, int down_type,
-                             float w_sigma, float router_sigma, float bias_sigma);
+                             double w_sigma, double router_sigma, double bias_sigma);
 
-/* Adds a per-expert bias to the router bias of a loaded layer (used to skew
- * expert load, e.g. a Zipf profile). */
+/* Adds a per-expert term to the selection bias (exp_probs_b) of a loaded
+ * layer. */
 int moe_add_router_bias(moe_ctx *ctx, int layer, const float *extra_bias);
+
+/* Sets a per-expert term added to the router logits before the sigmoid
+ * (logits = W_r h + logit_bias; NULL clears it).  Used to skew expert load,
+ * e.g. by a Zipf profile. */
+int moe_set_logit_bias(moe_ctx *ctx, int layer, const float *logit_bias);
 
 /* RMSNorm weight (fp32 [H]) applied before layer L in moe_forward_stack. */
 int moe_set_norm_weight(moe_ctx *ctx, int layer, const float *w);
@@ -186,8 +191,14 @@ int moe_dequantize_row_q6_K(const void *src, float *dst, size_t n);
 #define MOE_PHASE_COMBINE 6  /* combine all-to-all (0 on one GPU) */
 #define MOE_PHASE_OUTPUT 7   /* weighted combine + shared (+ residual) */
 #define MOE_N_PHASES 8
+/* enable > 0 turns timing on with a ring of `enable` steps (each forward call
+ * records into the next slot), 0 turns it off. */
 int moe_set_timing(moe_ctx *ctx, int enable);
+/* Durations of the last forward call (n <= MOE_N_PHASES floats). */
 int moe_get_timing(moe_ctx *ctx, float *ms, int n);
+/* Durations of the `back`-th most recent call (0 = last), while it is still
+ * in the ring. */
+int moe_get_timing_at(moe_ctx *ctx, int back, float *ms, int n);
 
 /* Number of kernels this library launched on the context's device since
  * creation (or the last reset). */

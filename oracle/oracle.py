@@ -104,8 +104,8 @@ def ref():
         R.ref_rms_norm.argtypes = [_f32p, C.c_void_p, _f32p, C.c_int]
         R.ref_route.argtypes = [_f32p, C.c_void_p, C.c_int, _i32p, _f32p]
         R.ref_moe_token_cpu.restype = C.c_int
-        R.ref_moe_token_cpu.argtypes = [C.POINTER(C.c_void_p), C.c_int, _f32p, _f32p, _f32p, C.c_int, _f32p,
-                                        C.c_void_p, C.c_void_p, C.c_int]
+        R.ref_moe_token_cpu.argtypes = [C.POINTER(C.c_void_p), C.c_int, _f32p, _f32p, _f32p, _f32p, C.c_int,
+                                        _f32p, C.c_void_p, C.c_void_p, C.c_int]
         _ref = R
     return _ref
 

@@ -122,9 +122,11 @@ static float *g_scr = NULL;
 static int g_scr_k = 0;
 
 /* experts: NUM_EXPERTS + 1 blobs ([gate][up][down]); entry NUM_EXPERTS is the
- * shared expert.  out = (sum_k w_k eo_k, slot order) + shared. */
-int ref_moe_token_cpu(const void *const *experts, int down_is_q6, const float *router_w, const float *bias,
-                      const float *h_post, int K, float *out, int *idx_out, float *w_out, int n_threads) {
+ * shared expert.  logit_bias (may be NULL) is added to the router logits (the
+ * synthetic load skew).  out = (sum_k w_k eo_k, slot order) + shared. */
+int ref_moe_token_cpu(const void *const *experts, int down_is_q6, const float *router_w, const float *logit_bias,
+                      const float *bias, const float *h_post, int K, float *out, int *idx_out, float *w_out,
+                      int n_threads) {
     if (K < 1 || K > MAX_K) return -1;
     const size_t big = (size_t)MOE_INTERMEDIATE * HIDDEN_DIM;
     const size_t per_ex = 3 * big + 3 * MOE_INTERMEDIATE + HIDDEN_DIM;
@@ -136,7 +138,7 @@ int ref_moe_token_cpu(const void *const *experts, int down_is_q6, const float *r
     }
     float logits[NUM_EXPERTS];
     for (int e = 0; e < NUM_EXPERTS; e++) {
-        logits[e] = dot_f32(router_w + (size_t)e * HIDDEN_DIM, h_post, HIDDEN_DIM);
+        logits[e] = dot_f32(router_w + (size_t)e * HIDDEN_DIM, h_post, HIDDEN_DIM) + (logit_bias ? logit_bias[e] : 0.0f);
     }
     int idx[MAX_K]; float wts[MAX_K];
     route(logits, bias, K, idx, wts);
