@@ -28,7 +28,8 @@ struct moe_ctx {
     std::vector<MoeLayerDev> layers;
     std::vector<size_t> layer_down_bytes;
     // workspace
-    float *part = nullptr, *d_in = nullptr, *d_out = nullptr, *h_post = nullptr;
+    float *part = nullptr, *logits = nullptr, *d_in = nullptr, *d_out = nullptr, *h_post = nullptr;
+    int *rl_counters = nullptr;
     int *idx = nullptr, *idx_given = nullptr;
     float *wts = nullptr, *w_given = nullptr, *bias_tmp = nullptr;
     __half *xop = nullptr;
@@ -102,6 +103,9 @@ static int ctx_alloc(moe_ctx *c) {
     c->max_pairs = R * K + T;
     c->n_split = H / MOE_QK;
     CK(dmalloc(&c->part, (size_t)c->n_split * T * E));
+    CK(dmalloc(&c->logits, (size_t)T * E));
+    CK(dmalloc(&c->rl_counters, (size_t)(E + 31) / 32));
+    CK(cudaMemset(c->rl_counters, 0, sizeof(int) * ((E + 31) / 32 + 64)));
     CK(dmalloc(&c->d_in, (size_t)T * H));
     CK(dmalloc(&c->d_out, (size_t)T * H));
     CK(dmalloc(&c->h_post, (size_t)T * H));
@@ -227,7 +231,7 @@ void moe_destroy(moe_ctx *c) {
         cudaFree(L.logit_bias);
         cudaFree(L.norm);
     }
-    void *bufs[] = {c->part, c->d_in, c->d_out, c->h_post, c->idx, c->wts, c->idx_given, c->w_given, c->bias_tmp, c->xop, c->x_inv, c->plan.counts,
+    void *bufs[] = {c->part, c->logits, c->rl_counters, c->d_in, c->d_out, c->h_post, c->idx, c->wts, c->idx_given, c->w_given, c->bias_tmp, c->xop, c->x_inv, c->plan.counts,
                     c->plan.pair_expert, c->plan.pair_token, c->plan.pair_w, c->plan.chunk_expert,
                     c->plan.chunk_pair0, c->plan.chunk_ntok, c->plan.slot_pair, c->plan.error, c->counter, c->act,
                     c->dop, c->zop, c->d_inv, c->eo, c->send_x, c->recv_x, c->send_y, c->recv_y, c->send_meta,
@@ -501,10 +505,12 @@ static int run_local(moe_ctx *c, int layer, const float *x, int T, const int *id
     const int mode = !routed ? 2 : (idx_in ? 1 : 0);
     mark_begin(c);
     mark(c, MOE_PHASE_ROUTER, s);
-    if (mode == 0) moe_launch_router_logits(L.router, x, T, d.H, d.E, c->part, c->n_split, s, &c->launches);
+    if (mode == 0)
+        moe_launch_router_logits(L.router, x, T, d.H, d.E, c->part, c->n_split, c->logits, c->rl_counters, s,
+                                 &c->launches);
     mark(c, MOE_PHASE_ROUTE, s);
-    moe_launch_route_and_plan(d, c->part, c->n_split, nullptr, L.bias, L.logit_bias, mode, idx_in, w_in, T, c->idx,
-                              c->wts, x, c->xop, c->x_inv, with_shared, 1, c->plan, c->counter, s, &c->launches);
+    moe_launch_route_and_plan(d, nullptr, 0, c->logits, L.bias, L.logit_bias, mode, idx_in, w_in, T, c->idx, c->wts,
+                              x, c->xop, c->x_inv, with_shared, 1, c->plan, c->counter, s, &c->launches);
     const int max_chunks = (T * d.K + T + MOE_TC - 1) / MOE_TC + d.E + 1;
     mark(c, MOE_PHASE_GATEUP, s);
     moe_launch_gateup(d, L, c->plan, c->xop, reinterpret_cast<const __half *>(c->zop), c->x_inv, c->act,
@@ -534,11 +540,13 @@ static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_i
     const int mode = idx_in ? 1 : 0;
     mark_begin(c);
     mark(c, MOE_PHASE_ROUTER, s);
-    if (mode == 0 && T > 0) moe_launch_router_logits(L.router, x, T, d.H, d.E, c->part, c->n_split, s, &c->launches);
+    if (mode == 0 && T > 0)
+        moe_launch_router_logits(L.router, x, T, d.H, d.E, c->part, c->n_split, c->logits, c->rl_counters, s,
+                                 &c->launches);
     mark(c, MOE_PHASE_ROUTE, s);
     if (T > 0)
-        moe_launch_route_and_plan(d, c->part, c->n_split, nullptr, L.bias, L.logit_bias, mode, idx_in, w_in, T,
-                                  c->idx, c->wts, x, nullptr, nullptr, 0, 0, c->plan, c->counter, s, &c->launches);
+        moe_launch_route_and_plan(d, nullptr, 0, c->logits, L.bias, L.logit_bias, mode, idx_in, w_in, T, c->idx,
+                                  c->wts, x, nullptr, nullptr, 0, 0, c->plan, c->counter, s, &c->launches);
     mark(c, MOE_PHASE_DISPATCH, s);
     moe_launch_ep_pack(x, c->idx, c->wts, T, d.K, d.H, N, c->n_local, cap, c->send_x, c->send_meta, c->tok_slot, s,
                        &c->launches);

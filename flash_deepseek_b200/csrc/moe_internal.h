@@ -42,8 +42,10 @@ struct MoeDims {
 
 // ---- launchers (moe_kernels.cu); every one counts its kernel launches ------
 extern "C++" {
+// logits[T][E] = x Wr^T; part: [n_split][T][E] scratch; counters: [E/32]
+// zeroed ints (reset by the kernel)
 void moe_launch_router_logits(const float *Wr, const float *x, int T, int H, int E, float *part, int n_split,
-                              cudaStream_t s, uint64_t *launches);
+                              float *logits, int *counters, cudaStream_t s, uint64_t *launches);
 // mode: 0 route from logits / partial logits, 1 routing given (idx_in, w_in),
 // 2 shared expert only
 void moe_launch_route_and_plan(const MoeDims &d, const float *part, int n_split, const float *logits,

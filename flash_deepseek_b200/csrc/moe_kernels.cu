@@ -298,7 +298,8 @@ void moe_launch_synth_f32(uint64_t seed, uint64_t stream, size_t n, double sigma
 #define RL_KS 256
 #define RL_WPAD (RL_KS + 4)
 __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__ Wr, const float *__restrict__ x,
-                                                       int T, int H, int E, float *__restrict__ part) {
+                                                       int T, int H, int E, float *__restrict__ part,
+                                                       float *__restrict__ logits, int *__restrict__ counters) {
     extern __shared__ float sm[];
     float *Ws = sm;                       // [32 experts][RL_WPAD] row-major (k contiguous)
     float *xt = sm + 32 * RL_WPAD;        // [RL_KS][64] (tokens contiguous)
@@ -323,7 +324,6 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
     __syncthreads();
     const int eg = tid >> 5, tg = tid & 31;  // warp = 4 experts, lane = tokens tg, tg+32
     const bool t0ok = tg < T, t1ok = tg + 32 < T;
-    if (!t0ok) return;
     float acc[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
     const float *w0 = Ws + (4 * eg) * RL_WPAD;
 #pragma unroll 2
@@ -346,13 +346,32 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
     for (int u = 0; u < 4; u++) {
         const int e = e0 + 4 * eg + u;
         if (e >= E) continue;
-        part[((size_t)split * T + tg) * E + e] = acc[u][0];
+        if (t0ok) part[((size_t)split * T + tg) * E + e] = acc[u][0];
         if (t1ok) part[((size_t)split * T + tg + 32) * E + e] = acc[u][1];
     }
+    // The last split CTA of this expert group sums the partials in split
+    // order (deterministic) into the final logits.
+    __shared__ int last;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last = atomicAdd(&counters[blockIdx.x], 1) == (int)gridDim.y - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    const int ns = gridDim.y;
+    for (int i = tid; i < T * 32; i += 256) {
+        const int t = i / 32, e = e0 + i % 32;
+        if (e >= E) continue;
+        float v = 0.0f;
+#pragma unroll 4
+        for (int sp = 0; sp < ns; sp++) v += __ldcg(part + ((size_t)sp * T + t) * E + e);
+        logits[(size_t)t * E + e] = v;
+    }
+    if (tid == 0) counters[blockIdx.x] = 0;
 }
 
 void moe_launch_router_logits(const float *Wr, const float *x, int T, int H, int E, float *part, int n_split,
-                              cudaStream_t s, uint64_t *launches) {
+                              float *logits, int *counters, cudaStream_t s, uint64_t *launches) {
     dim3 grid((E + 31) / 32, n_split);
     const size_t smem = sizeof(float) * (32 * RL_WPAD + RL_KS * 64);
     static bool attr = false;
@@ -360,7 +379,7 @@ void moe_launch_router_logits(const float *Wr, const float *x, int T, int H, int
         cudaFuncSetAttribute(k_router_logits, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         attr = true;
     }
-    k_router_logits<<<grid, 256, smem, s>>>(Wr, x, T, H, E, part);
+    k_router_logits<<<grid, 256, smem, s>>>(Wr, x, T, H, E, part, logits, counters);
     LAUNCH_COUNT(launches);
 }
 
