@@ -13,8 +13,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 ROOT = os.path.dirname(HERE)
 OUT = os.path.join(HERE, "libmoe_cuda.so")
-SOURCES = ["moe_kernels.cu", "moe_ep.cu", "moe_api.cu"]
-HEADERS = ["moe_common.cuh", "moe_internal.h"]
+SOURCES = ["moe_kernels.cu", "moe_ep.cu", "moe_api.cu", "moe_noalloc.cu"]
+HEADERS = ["moe_common.cuh", "moe_internal.h", "moe_nccl.h"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
@@ -49,7 +49,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
 
     with ThreadPoolExecutor(len(SOURCES)) as ex:
         list(ex.map(compile_one, SOURCES))
-    link = [NVCC, *ARCH, "-shared", "-o", OUT + ".tmp", *[_obj(s) for s in SOURCES], "-lnccl",
+    link = [NVCC, *ARCH, "-shared", "-o", OUT + ".tmp", *[_obj(s) for s in SOURCES], "-ldl",
             "-Xlinker", "-rpath,$ORIGIN"]
     r = subprocess.run(link, capture_output=True, text=True)
     if r.returncode != 0:

@@ -2,8 +2,9 @@
 // (include/moe_cuda.h).  One context per GPU; expert-parallel contexts talk
 // over NCCL (dispatch / combine) with fixed-capacity buffers so that a forward
 // step needs no host synchronisation.
-#include <nccl.h>
+#include <dlfcn.h>
 #include <stdarg.h>
+#include <stdlib.h>
 #include <stdio.h>
 #include <string.h>
 
@@ -13,6 +14,44 @@
 #include "../../include/moe_cuda.h"
 #include "moe_common.cuh"
 #include "moe_internal.h"
+#include "moe_nccl.h"
+
+const MoeNccl *moe_nccl() {
+    static MoeNccl api;
+    static int state = 0;  // 0 unknown, 1 ok, -1 unavailable
+    if (state) return state > 0 ? &api : nullptr;
+    const char *env = getenv("MOE_NCCL_LIB");
+    void *h = nullptr;
+    if (env && *env) h = dlopen(env, RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);  // already in the process
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+        fprintf(stderr, "[moe_cuda] ERROR: cannot load libnccl (set MOE_NCCL_LIB): %s\n", dlerror());
+        state = -1;
+        return nullptr;
+    }
+#define MOE_NCCL_SYM(field, name)                                                        \
+    api.field = reinterpret_cast<decltype(api.field)>(dlsym(h, name));                   \
+    if (!api.field) {                                                                    \
+        fprintf(stderr, "[moe_cuda] ERROR: libnccl lacks %s\n", name);                   \
+        state = -1;                                                                      \
+        return nullptr;                                                                  \
+    }
+    MOE_NCCL_SYM(GetUniqueId, "ncclGetUniqueId")
+    MOE_NCCL_SYM(CommInitRank, "ncclCommInitRank")
+    MOE_NCCL_SYM(CommDestroy, "ncclCommDestroy")
+    MOE_NCCL_SYM(CommAbort, "ncclCommAbort")
+    MOE_NCCL_SYM(CommGetAsyncError, "ncclCommGetAsyncError")
+    MOE_NCCL_SYM(GroupStart, "ncclGroupStart")
+    MOE_NCCL_SYM(GroupEnd, "ncclGroupEnd")
+    MOE_NCCL_SYM(Send, "ncclSend")
+    MOE_NCCL_SYM(Recv, "ncclRecv")
+    MOE_NCCL_SYM(GetErrorString, "ncclGetErrorString")
+#undef MOE_NCCL_SYM
+    state = 1;
+    return &api;
+}
 
 struct moe_ctx {
     moe_config cfg;
@@ -77,7 +116,7 @@ static int fail(moe_ctx *c, int code, const char *fmt, ...) {
 #define NK(call)                                                                                     \
     do {                                                                                             \
         ncclResult_t r_ = (call);                                                                    \
-        if (r_ != ncclSuccess) return fail(c, MOE_ERR_NCCL, "%s: %s", #call, ncclGetErrorString(r_)); \
+        if (r_ != ncclSuccess) return fail(c, MOE_ERR_NCCL, "%s: %s", #call, moe_nccl()->GetErrorString(r_)); \
     } while (0)
 
 template <typename T>
@@ -92,8 +131,10 @@ static size_t row_bytes(int type, int cols) {
 extern "C" {
 
 int moe_get_unique_id(void *out) {
+    const MoeNccl *nc = moe_nccl();
+    if (!nc) return MOE_ERR_NCCL;
     ncclUniqueId id;
-    if (ncclGetUniqueId(&id) != ncclSuccess) return MOE_ERR_NCCL;
+    if (nc->GetUniqueId(&id) != ncclSuccess) return MOE_ERR_NCCL;
     memcpy(out, &id, sizeof(id));
     return MOE_OK;
 }
@@ -208,7 +249,8 @@ moe_ctx *moe_create(const moe_config *cfg, int device, int rank, int world_size,
         }
         ncclUniqueId id;
         memcpy(&id, uid, sizeof(id));
-        if (ncclCommInitRank(&c->comm, world_size, id, rank) != ncclSuccess) {
+        const MoeNccl *nc = moe_nccl();
+        if (!nc || nc->CommInitRank(&c->comm, world_size, id, rank) != ncclSuccess) {
             fprintf(stderr, "[moe_cuda] ERROR: moe_create: ncclCommInitRank failed\n");
             c->comm = nullptr;
             moe_destroy(c);
@@ -222,7 +264,7 @@ void moe_destroy(moe_ctx *c) {
     if (!c) return;
     cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
-    if (c->comm) ncclCommDestroy(c->comm);
+    if (c->comm) moe_nccl()->CommDestroy(c->comm);
     for (cudaEvent_t e : c->ev) cudaEventDestroy(e);
     for (auto &L : c->layers) {
         cudaFree(L.experts);
@@ -550,14 +592,14 @@ static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_i
     mark(c, MOE_PHASE_DISPATCH, s);
     moe_launch_ep_pack(x, c->idx, c->wts, T, d.K, d.H, N, c->n_local, cap, c->send_x, c->send_meta, c->tok_slot, s,
                        &c->launches);
-    NK(ncclGroupStart());
+    NK(moe_nccl()->GroupStart());
     for (int p = 0; p < N; p++) {
-        NK(ncclSend(c->send_x + (size_t)p * cap * d.H, (size_t)cap * d.H, ncclFloat32, p, c->comm, s));
-        NK(ncclRecv(c->recv_x + (size_t)p * cap * d.H, (size_t)cap * d.H, ncclFloat32, p, c->comm, s));
-        NK(ncclSend(c->send_meta + (size_t)p * cap * mw, (size_t)cap * mw, ncclInt32, p, c->comm, s));
-        NK(ncclRecv(c->recv_meta + (size_t)p * cap * mw, (size_t)cap * mw, ncclInt32, p, c->comm, s));
+        NK(moe_nccl()->Send(c->send_x + (size_t)p * cap * d.H, (size_t)cap * d.H, ncclFloat32, p, c->comm, s));
+        NK(moe_nccl()->Recv(c->recv_x + (size_t)p * cap * d.H, (size_t)cap * d.H, ncclFloat32, p, c->comm, s));
+        NK(moe_nccl()->Send(c->send_meta + (size_t)p * cap * mw, (size_t)cap * mw, ncclInt32, p, c->comm, s));
+        NK(moe_nccl()->Recv(c->recv_meta + (size_t)p * cap * mw, (size_t)cap * mw, ncclInt32, p, c->comm, s));
     }
-    NK(ncclGroupEnd());
+    NK(moe_nccl()->GroupEnd());
     moe_launch_ep_plan(d, c->recv_meta, N, cap, T, c->e0, c->n_local, c->plan, s, &c->launches);
     moe_launch_prep_rows(c->recv_x, c->recv_meta, mw, R, x, T, d.H, c->xop, c->x_inv, s, &c->launches);
     const int P = R * d.K + T;
@@ -571,12 +613,12 @@ static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_i
     moe_launch_down(d, L, c->plan, c->dop, c->zop, c->d_inv, c->eo, max_chunks * (d.H / 16), s, &c->launches);
     mark(c, MOE_PHASE_COMBINE, s);
     moe_launch_ep_partial(d, c->plan, c->recv_meta, c->eo, R, c->send_y, s, &c->launches);
-    NK(ncclGroupStart());
+    NK(moe_nccl()->GroupStart());
     for (int p = 0; p < N; p++) {
-        NK(ncclSend(c->send_y + (size_t)p * cap * d.H, (size_t)cap * d.H, ncclFloat32, p, c->comm, s));
-        NK(ncclRecv(c->recv_y + (size_t)p * cap * d.H, (size_t)cap * d.H, ncclFloat32, p, c->comm, s));
+        NK(moe_nccl()->Send(c->send_y + (size_t)p * cap * d.H, (size_t)cap * d.H, ncclFloat32, p, c->comm, s));
+        NK(moe_nccl()->Recv(c->recv_y + (size_t)p * cap * d.H, (size_t)cap * d.H, ncclFloat32, p, c->comm, s));
     }
-    NK(ncclGroupEnd());
+    NK(moe_nccl()->GroupEnd());
     mark(c, MOE_PHASE_OUTPUT, s);
     if (T > 0)
         moe_launch_ep_final(d, c->plan, c->recv_y, c->tok_slot, N, cap, T, c->eo, residual, out, s, &c->launches);
