@@ -46,6 +46,7 @@ SIGNATURES = {
     "moe_experts_forward_device": (C.c_int, [_vp, C.c_int, _vp, C.c_int, _vp, _vp, C.c_int, _vp, _vp]),
     "moe_shared_forward": (C.c_int, [_vp, C.c_int, _vp, C.c_int, _vp]),
     "moe_route": (C.c_int, [_vp, _vp, _vp, C.c_int, _vp, _vp]),
+    "moe_route_hidden_noalloc": (C.c_int, [C.POINTER(MoeConfigC), _vp, _vp, _vp, C.c_int, _vp, _vp, _vp]),
     "moe_forward_stack_device": (C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_int, _vp]),
     "moe_forward_stack": (C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_int]),
     "moe_dequantize_row_q4_K": (C.c_int, [_vp, _vp, C.c_size_t]),

@@ -172,6 +172,22 @@ int moe_forward_stack_device(moe_ctx *ctx, int first_layer, int n_layers, float 
                              int n_tokens, void *stream);
 int moe_forward_stack(moe_ctx *ctx, int first_layer, int n_layers, float *hidden, int n_tokens);
 
+/* Routing from hidden states with no allocation: router logits
+ * (d_h x d_router_w^T, fp32) then the grouped top-k of moe_route(), writing
+ * d_idx / d_w [n_tokens x top_k] -- the same kernels and arithmetic as the
+ * routing inside moe_forward().  For callers that cannot call cudaMalloc (a
+ * fixed memory pool, or a latency-critical decode loop where an allocation
+ * may synchronize the device): all scratch lives in a fixed array inside the
+ * library (1.25 MiB per GPU, held until exit).  Limits: n_tokens <= 64,
+ * (hidden/256) * n_tokens * n_experts <= 262144, n_tokens * n_experts <=
+ * 65536.  All pointers are device pointers; the call is asynchronous on
+ * `stream` (NULL = default stream).  The first call on a device looks up the
+ * array's device address; make it before any stream capture.  Every call
+ * shares the one array, so calls that overlap on the GPU (other streams,
+ * other threads) race.  No counterpart in the reference. */
+int moe_route_hidden_noalloc(const moe_config *cfg, const float *d_router_w, const float *d_bias,
+                             const float *d_h, int n_tokens, int *d_idx, float *d_w, void *stream);
+
 /* ------------------------------------------------------------------ codec */
 /* Device twins of quant.h:11-12 (host buffers in and out). */
 int moe_dequantize_row_q4_K(const void *src, float *dst, size_t n);
