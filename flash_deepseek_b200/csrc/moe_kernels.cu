@@ -305,13 +305,60 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
     float *xt = sm + 32 * RL_WPAD;        // [RL_KS][64] (tokens contiguous)
     const int e0 = blockIdx.x * 32, split = blockIdx.y, k0 = split * RL_KS;
     const int tid = threadIdx.x;
-    // W tile: coalesced float4 loads, conflict-free float4 stores
-    for (int i = tid; i < 32 * (RL_KS / 4); i += 256) {
-        const int r = i / (RL_KS / 4), c4 = i % (RL_KS / 4);
-        float4 w = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (e0 + r < E) w = __ldg(reinterpret_cast<const float4 *>(Wr + (size_t)(e0 + r) * H + k0) + c4);
-        *reinterpret_cast<float4 *>(Ws + r * RL_WPAD + 4 * c4) = w;
+    // W tile: 8 coalesced float4 loads in flight per thread, then float4 stores
+    {
+        float4 wv[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int i = tid + 256 * u, r = i / (RL_KS / 4), c4 = i % (RL_KS / 4);
+            wv[u] = e0 + r < E ? __ldg(reinterpret_cast<const float4 *>(Wr + (size_t)(e0 + r) * H + k0) + c4)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int i = tid + 256 * u, r = i / (RL_KS / 4), c4 = i % (RL_KS / 4);
+            *reinterpret_cast<float4 *>(Ws + r * RL_WPAD + 4 * c4) = wv[u];
+        }
     }
+    const int eg = tid >> 5, tg = tid & 31;
+    const bool small = T <= 4;
+    if (small) {
+        // few tokens: x row-major, lane = 8 consecutive k, warp-reduced
+        for (int i = tid; i < T * (RL_KS / 4); i += 256) {
+            const int t = i / (RL_KS / 4), c4 = i % (RL_KS / 4);
+            *reinterpret_cast<float4 *>(xt + t * RL_KS + 4 * c4) =
+                __ldg(reinterpret_cast<const float4 *>(x + (size_t)t * H + k0) + c4);
+        }
+        __syncthreads();
+        float accs[4][4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const float4 w0 = *reinterpret_cast<const float4 *>(Ws + (4 * eg + u) * RL_WPAD + 8 * tg);
+            const float4 w1 = *reinterpret_cast<const float4 *>(Ws + (4 * eg + u) * RL_WPAD + 8 * tg + 4);
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                float v = 0.0f;
+                if (t < T) {
+                    const float4 x0 = *reinterpret_cast<const float4 *>(xt + t * RL_KS + 8 * tg);
+                    const float4 x1 = *reinterpret_cast<const float4 *>(xt + t * RL_KS + 8 * tg + 4);
+                    v = w0.x * x0.x + w0.y * x0.y + w0.z * x0.z + w0.w * x0.w + w1.x * x1.x + w1.y * x1.y +
+                        w1.z * x1.z + w1.w * x1.w;
+                    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+                }
+                accs[u][t] = v;
+            }
+        }
+        if (tg == 0) {
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int e = e0 + 4 * eg + u;
+                if (e >= E) continue;
+#pragma unroll
+                for (int t = 0; t < 4; t++)
+                    if (t < T) part[((size_t)split * T + t) * E + e] = accs[u][t];
+            }
+        }
+    } else {
     // x tile transposed: consecutive threads take consecutive tokens
     for (int i = tid; i < T * (RL_KS / 4); i += 256) {
         const int c4 = i / T, t = i % T;
@@ -322,7 +369,7 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
         xt[(4 * c4 + 3) * 64 + t] = v.w;
     }
     __syncthreads();
-    const int eg = tid >> 5, tg = tid & 31;  // warp = 4 experts, lane = tokens tg, tg+32
+    // warp = 4 experts, lane = tokens tg, tg+32
     const bool t0ok = tg < T, t1ok = tg + 32 < T;
     float acc[4][2] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
     const float *w0 = Ws + (4 * eg) * RL_WPAD;
@@ -348,6 +395,7 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
         if (e >= E) continue;
         if (t0ok) part[((size_t)split * T + tg) * E + e] = acc[u][0];
         if (t1ok) part[((size_t)split * T + tg + 32) * E + e] = acc[u][1];
+    }
     }
     // The last split CTA of this expert group sums the partials in split
     // order (deterministic) into the final logits.
@@ -386,6 +434,28 @@ void moe_launch_router_logits(const float *Wr, const float *x, int T, int H, int
 // ===========================================================================
 // Activation operands
 // ===========================================================================
+// Copies a row of n floats (n % 4 == 0, 16-byte aligned) to shared memory
+// with up to 8 float4 loads in flight per thread, then syncs the block.
+__device__ __forceinline__ void stage_row(const float *__restrict__ x, int n, float *__restrict__ xs) {
+    const float4 *src = reinterpret_cast<const float4 *>(x);
+    float4 *dst = reinterpret_cast<float4 *>(xs);
+    const int n4 = n / 4, step = blockDim.x;
+    for (int base = 0; base < n4; base += 8 * step) {
+        float4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int i = base + u * step + threadIdx.x;
+            if (i < n4) v[u] = __ldg(src + i);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int i = base + u * step + threadIdx.x;
+            if (i < n4) dst[i] = v[u];
+        }
+    }
+    __syncthreads();
+}
+
 __device__ __forceinline__ float block_max_abs(const float *x, int n, float *red /*[32]*/) {
     float m = 0.0f;
     for (int i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, fabsf(x[i]));
@@ -699,7 +769,9 @@ __global__ void __launch_bounds__(256) k_route_plan(RouteArgs a) {
 
     // activation operand of this token for the gate/up GEMV
     if (a.xop) {
-        const float *xr = a.x + (size_t)t * a.d.H;
+        extern __shared__ float xrow[];  // [H]
+        stage_row(a.x + (size_t)t * a.d.H, a.d.H, xrow);
+        const float *xr = xrow;
         const float amax = block_max_abs(xr, a.d.H, red);
         float inv;
         const float s = op_scale(amax, &inv);
@@ -728,7 +800,13 @@ void moe_launch_route_and_plan(const MoeDims &d, const float *part, int n_split,
     a.idx_in = idx_in; a.w_in = w_in; a.mode = mode; a.T = T; a.idx_out = idx_out; a.w_out = w_out;
     a.x = x; a.xop = xop; a.x_inv = x_inv; a.include_shared = include_shared; a.build_plan = build_plan;
     a.plan = plan; a.counter = counter;
-    k_route_plan<<<T, 256, 0, s>>>(a);
+    const size_t smem = xop ? sizeof(float) * (size_t)d.H : 0;
+    static size_t attr = 0;
+    if (smem > attr) {
+        cudaFuncSetAttribute(k_route_plan, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attr = smem;
+    }
+    k_route_plan<<<T, 256, smem, s>>>(a);
     LAUNCH_COUNT(launches);
 }
 
@@ -945,13 +1023,19 @@ __device__ __forceinline__ void q6i_compute(const Q6Raw &R, int sb, const int8_t
                                 {R.ug8[1].z, R.ug8[1].w, R.ug8[2].x, R.ug8[2].y, R.ug8[2].z, R.ug8[2].w}};
     const uint32_t sgw[4] = {R.sg.x, R.sg.y, R.sg.z, R.sg.w}, sg8w[4] = {R.sg8.x, R.sg8.y, R.sg8.z, R.sg8.w};
     const uint32_t NEG32 = 0xE0E0E0E0u;
+    uint4 Bq[NT];  // fragments of the current quarter; the next quarter's are loaded one quarter ahead
+#pragma unroll
+    for (int n = 0; n < NT; n++) Bq[n] = ldg_op16(opb[n] + (size_t)sb * Q6I_BYTES_PER_SB);
 #pragma unroll
     for (int h = 0; h < 2; h++) {
 #pragma unroll
         for (int qd = 0; qd < 2; qd++) {  // quarter: steps 8h + 4qd .. +3
-            uint4 B[NT];
+            uint4 B[NT], Bn[NT];
 #pragma unroll
-            for (int n = 0; n < NT; n++) B[n] = ldg_op16(opb[n] + (size_t)sb * Q6I_BYTES_PER_SB + h * 32 + qd * 16);
+            for (int n = 0; n < NT; n++) {
+                B[n] = Bq[n];
+                if (2 * h + qd < 3) Bn[n] = ldg_op16(opb[n] + (size_t)sb * Q6I_BYTES_PER_SB + (2 * h + qd + 1) * 16);
+            }
 #pragma unroll
             for (int j = 0; j < 4; j++) {
                 const int sp = 4 * qd + j, s = 8 * h + sp;
@@ -989,6 +1073,9 @@ __device__ __forceinline__ void q6i_compute(const Q6Raw &R, int sb, const int8_t
                     acc[n][3] += scg8 * dd[3];
                 }
             }
+#pragma unroll
+            for (int n = 0; n < NT; n++)
+                if (2 * h + qd < 3) Bq[n] = Bn[n];
         }
     }
 }
@@ -1005,13 +1092,23 @@ __device__ __forceinline__ void q6k_warp_rows(const uint8_t *__restrict__ W, int
         if (s < nb) q6_issue(wsm, s, lane, qpl, spl, nb, row_g, s, t);
         cp_async_commit();
     }
+    // d of the first 8 super-blocks of both rows in one 16-byte load each
+    const uint4 dv = __ldg(reinterpret_cast<const uint4 *>(dpl + (size_t)row_g * nbp));
+    const uint4 dv8 = __ldg(reinterpret_cast<const uint4 *>(dpl + (size_t)(row_g + 8) * nbp));
     int slot = 0, nslot = MOE_STAGES - 1;
 #pragma unroll 1
     for (int sb = 0; sb < nb; ++sb) {
         if (sb + MOE_STAGES - 1 < nb) q6_issue(wsm, nslot, lane, qpl, spl, nb, row_g, sb + MOE_STAGES - 1, t);
         cp_async_commit();
-        const float dg = h2f_bits(__ldg(dpl + (size_t)row_g * nbp + sb));
-        const float dg8 = h2f_bits(__ldg(dpl + (size_t)(row_g + 8) * nbp + sb));
+        float dg, dg8;
+        if (sb < 8) {
+            const uint32_t w = u4c(dv, sb >> 1), w8 = u4c(dv8, sb >> 1);
+            dg = h2f_bits((uint16_t)((sb & 1) ? (w >> 16) : (w & 0xFFFFu)));
+            dg8 = h2f_bits((uint16_t)((sb & 1) ? (w8 >> 16) : (w8 & 0xFFFFu)));
+        } else {
+            dg = h2f_bits(__ldg(dpl + (size_t)row_g * nbp + sb));
+            dg8 = h2f_bits(__ldg(dpl + (size_t)(row_g + 8) * nbp + sb));
+        }
         cp_async_wait<MOE_STAGES - 1>();
         Q6Raw R;
         q6_read(R, wsm, slot, lane);
@@ -1040,8 +1137,6 @@ __device__ __forceinline__ int expert_slot(const MoeLayerDev &L, int E, int e) {
 // gate/up: CTA item = (chunk, 64 rows); warp w: row tile w&3, K half w>>2.
 // act[pair][row] = silu(gate) * up  (infer.m:378-383)
 // ===========================================================================
-// one (chunk, row group) item: warp (rt, kh) runs gate then up for its 16
-// rows over its K half and leaves partial sums in `red`
 template <int NT>
 __device__ __forceinline__ void gateup_item(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan,
                                             const __half *__restrict__ xop, const __half *__restrict__ zop, int e,
@@ -1131,8 +1226,10 @@ __global__ void __launch_bounds__(256) k_prep_down(MoeDims d, MoeLayerDev L, Moe
     __shared__ float xsum[1024];
     const int n_pairs = plan.counts[0];
     const size_t opst = dop_bytes(d.I);
+    extern __shared__ float arow[];  // [I]
     for (int p = blockIdx.x; p < n_pairs; p += gridDim.x) {
-        const float *a = act + (size_t)p * d.I;
+        stage_row(act + (size_t)p * d.I, d.I, arow);
+        const float *a = arow;
         const float amax = block_max_abs(a, d.I, red);
         const int e = plan.pair_expert[p];
         const int ty = (e == d.E) ? L.sh_down_type : L.down_type;
@@ -1158,7 +1255,9 @@ __global__ void __launch_bounds__(256) k_prep_rows(const float *__restrict__ rec
     __shared__ float xsum[1024];
     const int r = blockIdx.x;
     if (r < R && !meta[(size_t)r * meta_w]) return;
-    const float *x = r < R ? recv + (size_t)r * H : local + (size_t)(r - R) * H;
+    extern __shared__ float xrow[];  // [H]
+    stage_row(r < R ? recv + (size_t)r * H : local + (size_t)(r - R) * H, H, xrow);
+    const float *x = xrow;
     const float amax = block_max_abs(x, H, red);
     float inv;
     const float s = op_scale(amax, &inv);
@@ -1168,7 +1267,13 @@ __global__ void __launch_bounds__(256) k_prep_rows(const float *__restrict__ rec
 
 void moe_launch_prep_rows(const float *recv, const int *meta, int meta_w, int R, const float *local, int T, int H,
                           __half *xop, float *x_inv, cudaStream_t s, uint64_t *launches) {
-    k_prep_rows<<<R + T, 256, 0, s>>>(recv, meta, meta_w, R, local, H, xop, x_inv);
+    const size_t smem = sizeof(float) * (size_t)H;
+    static size_t attr = 0;
+    if (smem > attr) {
+        cudaFuncSetAttribute(k_prep_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attr = smem;
+    }
+    k_prep_rows<<<R + T, 256, smem, s>>>(recv, meta, meta_w, R, local, H, xop, x_inv);
     LAUNCH_COUNT(launches);
 }
 
@@ -1177,7 +1282,13 @@ void moe_launch_prep_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan 
     int grid = max_pairs;
     if (grid > num_sms() * 4) grid = num_sms() * 4;
     if (grid < 1) grid = 1;
-    k_prep_down<<<grid, 256, 0, s>>>(d, L, plan, act, dop, d_inv);
+    const size_t smem = sizeof(float) * (size_t)d.I;
+    static size_t attr = 0;
+    if (smem > attr) {
+        cudaFuncSetAttribute(k_prep_down, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attr = smem;
+    }
+    k_prep_down<<<grid, 256, smem, s>>>(d, L, plan, act, dop, d_inv);
     LAUNCH_COUNT(launches);
 }
 
@@ -1283,10 +1394,13 @@ __global__ void __launch_bounds__(256, 2) k_down(MoeDims d, MoeLayerDev L, MoePl
         const int e = plan.chunk_expert[c], p0 = plan.chunk_pair0[c], ntok = plan.chunk_ntok[c];
         if (((e == d.E) ? L.sh_down_type : L.down_type) != TY) continue;
         if (TY == 14) {
-            if (ntok <= 2) down_task_q6<1>(d, L, dop, zop, d_inv, eo, e, p0, ntok, rt, g, t, lane, wsm);
-            else if (ntok <= 4) down_task_q6<2>(d, L, dop, zop, d_inv, eo, e, p0, ntok, rt, g, t, lane, wsm);
-            else if (ntok <= 6) down_task_q6<3>(d, L, dop, zop, d_inv, eo, e, p0, ntok, rt, g, t, lane, wsm);
-            else down_task_q6<4>(d, L, dop, zop, d_inv, eo, e, p0, ntok, rt, g, t, lane, wsm);
+            // at most 4 vectors per pass (two 8-column tiles); a chunk of more
+            // runs a second pass over the same rows (weights then come from L2)
+            for (int q0 = 0; q0 < ntok; q0 += 4) {
+                const int nq = min(4, ntok - q0);
+                if (nq <= 2) down_task_q6<1>(d, L, dop, zop, d_inv, eo, e, p0 + q0, nq, rt, g, t, lane, wsm);
+                else down_task_q6<2>(d, L, dop, zop, d_inv, eo, e, p0 + q0, nq, rt, g, t, lane, wsm);
+            }
         } else {
             if (ntok <= 4) down_task_q4<1>(d, L, dop, zop, d_inv, eo, e, p0, ntok, rt, g, t, lane, wsm);
             else down_task_q4<2>(d, L, dop, zop, d_inv, eo, e, p0, ntok, rt, g, t, lane, wsm);
