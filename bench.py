@@ -168,6 +168,7 @@ def cpu_reference(workload: str, steps: int, warmup: int, seconds: float = 20.0)
 def run_ours(args):
     import torch
     import flash_deepseek_b200 as F
+    from flash_deepseek_b200 import ep
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -183,17 +184,10 @@ def run_ours(args):
         pg = dist
     W = WORKLOADS[args.workload]
     B = W["B"]
-    if world > 1 and B > world and B % world:
-        raise SystemExit("global batch must divide over the GPUs")
     # tokens of this rank: an even share, or (batch < GPUs) one token on the
     # first B ranks and none elsewhere
-    b_loc = B // world if B >= world else (1 if rank < B else 0)
-    t0_loc = rank * b_loc if B >= world else min(rank, B)
-    uid = None
-    if world > 1:
-        obj = [F.get_unique_id() if rank == 0 else None]
-        pg.broadcast_object_list(obj, src=0)
-        uid = obj[0]
+    t0_loc, b_loc = ep.local_tokens(B, world, rank)
+    uid = ep.share_unique_id(pg, rank, F.get_unique_id) if world > 1 else None
     cfg = F.MoeConfig(n_layers=1, max_tokens=max(1, b_loc), n_experts=args.experts)
     moe = F.MoE(cfg, device=local, rank=rank, world_size=world, unique_id=uid)
     moe.init_layer_synthetic(0, seed=0, down_type=F.TYPE_Q6_K)
@@ -263,12 +257,10 @@ def run_ours(args):
     else:
         idx_g = idx_loc.numpy()
     NE = args.experts
-    e_lo, e_hi = rank * (NE // world), (rank + 1) * (NE // world)
     gu_bytes, dn_bytes, active = [], [], []
     for s in range(args.steps):
-        mine = (idx_g[s] >= e_lo) & (idx_g[s] < e_hi)
-        hit = set(int(e) for e in np.unique(idx_g[s][mine]))
-        n_act = len(hit) + 1
+        mine = ep.expert_owner(idx_g[s], NE, world) == rank
+        n_act = len(ep.experts_hit(idx_g[s], NE, world, rank)) + 1
         rows = int(mine.any(axis=1).sum()) + b_loc
         pairs = int(mine.sum()) + b_loc
         active.append(n_act)

@@ -64,6 +64,23 @@ PHASES = ["router", "route", "dispatch", "gateup", "prep", "down", "combine_a2a"
 _lib = None
 
 
+def _bundled_nccl() -> str | None:
+    """libnccl.so.2 of the nvidia-nccl wheel that torch links against.  The
+    library dlopens NCCL on first expert-parallel use; pointing it at this
+    copy keeps a later `import torch` in the same process working (both
+    resolve the soname libnccl.so.2 to the same, newer, file)."""
+    try:
+        import importlib.util
+        spec = importlib.util.find_spec("nvidia.nccl")
+        for d in (spec.submodule_search_locations or []) if spec else []:
+            p = os.path.join(d, "lib", "libnccl.so.2")
+            if os.path.exists(p):
+                return p
+    except (ImportError, ValueError):
+        pass
+    return None
+
+
 def load(build_if_missing: bool = False) -> C.CDLL:
     """Returns the loaded CUDA library; raises if it is not there."""
     global _lib
@@ -76,6 +93,10 @@ def load(build_if_missing: bool = False) -> C.CDLL:
         else:
             raise ImportError(f"libmoe_cuda.so not found at {LIB_PATH}: run `python -m flash_deepseek_b200.build` "
                               "(there is no CPU fallback)")
+    if "MOE_NCCL_LIB" not in os.environ:
+        nccl = _bundled_nccl()
+        if nccl:
+            os.environ["MOE_NCCL_LIB"] = nccl
     lib = C.CDLL(LIB_PATH)
     for name, (res, args) in SIGNATURES.items():
         fn = getattr(lib, name)

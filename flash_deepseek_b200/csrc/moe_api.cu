@@ -631,7 +631,8 @@ static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_i
 
 int moe_forward_device(moe_ctx *c, int layer, const float *d_h, int T, float *d_out, int *d_idx, float *d_w,
                        void *stream) {
-    if (!c || !d_h || !d_out) return MOE_ERR_ARG;
+    if (!c) return MOE_ERR_ARG;
+    if (T > 0 && (!d_h || !d_out)) return fail(c, MOE_ERR_ARG, "moe_forward_device: null input or output");
     int rc = check_layer(c, layer);
     if (rc) return rc;
     if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
@@ -660,13 +661,15 @@ static int finish_sync(moe_ctx *c) {
 }
 
 int moe_forward(moe_ctx *c, int layer, const float *h, int T, float *out, int *idx_out, float *w_out) {
-    if (!c || !h || !out) return MOE_ERR_ARG;
+    if (!c) return MOE_ERR_ARG;
+    if (T > 0 && (!h || !out)) return fail(c, MOE_ERR_ARG, "moe_forward: null input or output");
     if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
     CK(cudaSetDevice(c->device));
     const size_t n = (size_t)T * c->d.H;
-    CK(cudaMemcpyAsync(c->d_in, h, n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    if (n) CK(cudaMemcpyAsync(c->d_in, h, n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
     int rc = moe_forward_device(c, layer, c->d_in, T, c->d_out, nullptr, nullptr, nullptr);
     if (rc) return rc;
+    if (n == 0) return finish_sync(c);
     CK(cudaMemcpyAsync(out, c->d_out, n * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
     if (idx_out) CK(cudaMemcpyAsync(idx_out, c->idx, sizeof(int) * T * c->d.K, cudaMemcpyDeviceToHost, c->stream));
     if (w_out) CK(cudaMemcpyAsync(w_out, c->wts, sizeof(float) * T * c->d.K, cudaMemcpyDeviceToHost, c->stream));
@@ -675,7 +678,9 @@ int moe_forward(moe_ctx *c, int layer, const float *h, int T, float *out, int *i
 
 int moe_experts_forward_device(moe_ctx *c, int layer, const float *d_h, int T, const int *d_idx, const float *d_w,
                                int K, float *d_out, void *stream) {
-    if (!c || !d_h || !d_idx || !d_w || !d_out) return MOE_ERR_ARG;
+    if (!c) return MOE_ERR_ARG;
+    if (T > 0 && (!d_h || !d_idx || !d_w || !d_out))
+        return fail(c, MOE_ERR_ARG, "moe_experts_forward_device: null pointer");
     int rc = check_layer(c, layer);
     if (rc) return rc;
     if (K != c->d.K) return fail(c, MOE_ERR_ARG, "K %d differs from the context's top_k %d", K, c->d.K);
@@ -689,7 +694,8 @@ int moe_experts_forward_device(moe_ctx *c, int layer, const float *d_h, int T, c
 
 int moe_experts_forward(moe_ctx *c, int layer, const float *h, int T, const int *idx, const float *w, int K,
                         float *out) {
-    if (!c || !h || !idx || !w || !out) return MOE_ERR_ARG;
+    if (!c) return MOE_ERR_ARG;
+    if (T > 0 && (!h || !idx || !w || !out)) return fail(c, MOE_ERR_ARG, "moe_experts_forward: null pointer");
     if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
     if (K != c->d.K) return fail(c, MOE_ERR_ARG, "K %d differs from the context's top_k %d", K, c->d.K);
     for (int i = 0; i < T * K; i++)
@@ -706,7 +712,8 @@ int moe_experts_forward(moe_ctx *c, int layer, const float *h, int T, const int 
 }
 
 int moe_shared_forward(moe_ctx *c, int layer, const float *h, int T, float *sd) {
-    if (!c || !h || !sd) return MOE_ERR_ARG;
+    if (!c) return MOE_ERR_ARG;
+    if (T > 0 && (!h || !sd)) return fail(c, MOE_ERR_ARG, "moe_shared_forward: null pointer");
     int rc = check_layer(c, layer);
     if (rc) return rc;
     if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
@@ -722,7 +729,8 @@ int moe_shared_forward(moe_ctx *c, int layer, const float *h, int T, float *sd) 
 }
 
 int moe_route(moe_ctx *c, const float *logits, const float *bias, int T, int *idx, float *w) {
-    if (!c || !logits || !idx || !w) return MOE_ERR_ARG;
+    if (!c) return MOE_ERR_ARG;
+    if (T > 0 && (!logits || !idx || !w)) return fail(c, MOE_ERR_ARG, "moe_route: null pointer");
     if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
     if (T == 0) return MOE_OK;
     CK(cudaSetDevice(c->device));
@@ -743,7 +751,8 @@ int moe_route(moe_ctx *c, const float *logits, const float *bias, int T, int *id
 }
 
 int moe_forward_stack_device(moe_ctx *c, int first, int n_layers, float *d_hidden, int T, void *stream) {
-    if (!c || !d_hidden) return MOE_ERR_ARG;
+    if (!c) return MOE_ERR_ARG;
+    if (T > 0 && !d_hidden) return fail(c, MOE_ERR_ARG, "moe_forward_stack_device: null hidden");
     if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
     cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
     for (int l = first; l < first + n_layers; l++) {
@@ -759,14 +768,15 @@ int moe_forward_stack_device(moe_ctx *c, int first, int n_layers, float *d_hidde
 }
 
 int moe_forward_stack(moe_ctx *c, int first, int n_layers, float *hidden, int T) {
-    if (!c || !hidden) return MOE_ERR_ARG;
+    if (!c) return MOE_ERR_ARG;
+    if (T > 0 && !hidden) return fail(c, MOE_ERR_ARG, "moe_forward_stack: null hidden");
     if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
     CK(cudaSetDevice(c->device));
     const size_t n = (size_t)T * c->d.H;
-    CK(cudaMemcpyAsync(c->d_in, hidden, n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    if (n) CK(cudaMemcpyAsync(c->d_in, hidden, n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
     int rc = moe_forward_stack_device(c, first, n_layers, c->d_in, T, nullptr);
     if (rc) return rc;
-    CK(cudaMemcpyAsync(hidden, c->d_in, n * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    if (n) CK(cudaMemcpyAsync(hidden, c->d_in, n * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
     return finish_sync(c);
 }
 

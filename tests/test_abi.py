@@ -3,6 +3,8 @@ include/moe_cuda.h declares (no compute call: there may be no GPU)."""
 import ctypes
 import os
 import re
+import subprocess
+import sys
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
@@ -37,3 +39,15 @@ def test_create_rejects_bad_config(cuda_lib):
     assert not lib.moe_create(ctypes.byref(bad), 0, 0, 1, None)
     bad = MoeConfig(top_k=17).c()
     assert not lib.moe_create(ctypes.byref(bad), 0, 0, 1, None)
+
+
+def test_nccl_then_torch_import_in_one_process():
+    """The library dlopens NCCL on first use; a later `import torch` in the
+    same process must still find the NCCL it was built against."""
+    code = ("import flash_deepseek_b200 as F\n"
+            "assert len(F.get_unique_id()) == 128\n"
+            "import torch\n"
+            "print('ok')\n")
+    env = {k: v for k, v in os.environ.items() if k != "MOE_NCCL_LIB"}
+    r = subprocess.run([sys.executable, "-c", code], cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and "ok" in r.stdout, r.stderr[-2000:]
