@@ -57,12 +57,16 @@ def peaks():
         return 6650.0, "fallback"
 
 
-def traffic_from_profiles(kernel: str, workload: str):
-    """Per-launch DRAM bytes from a committed ncu summary, if there is one."""
+def traffic_from_profiles(kernel: str, workload: str, alg_bytes: float):
+    """Per-launch DRAM bytes from a committed ncu summary, if there is one.
+    The captures run a smaller case of the same kernel (fewer experts); their
+    traffic is scaled to this launch by the algorithmic bytes of both."""
     for p in sorted(glob.glob(os.path.join(ROOT, "profiles", f"{kernel}__{workload}*.txt"))):
-        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", open(p).read())
-        if m:
-            return float(m.group(1))
+        txt = open(p).read()
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", txt)
+        a = re.search(r"algorithmic_bytes_per_launch:\s*([0-9.eE+]+)", txt)
+        if m and a:
+            return float(m.group(1)) * alg_bytes / float(a.group(1))
     return None
 
 
@@ -272,7 +276,7 @@ def run_ours(args):
     ach = float(np.mean(gu_bytes)) / (gu_ms / 1e3) / 1e9
     ach_dn = float(np.mean(dn_bytes)) / (dn_ms / 1e3) / 1e9
     step_bytes = float(np.mean([a * EXPERT_BYTES for a in active])) + NE * H * 4 + NE * 4
-    traffic = traffic_from_profiles("k_gateup", args.workload)
+    traffic = traffic_from_profiles("k_gateup", args.workload, float(np.mean(gu_bytes)))
 
     # ---- end-to-end leg through the C ABI with host buffers
     h_pin = [p[t0_loc:t0_loc + max(1, b_loc)].contiguous().pin_memory() for p in pool_h]
