@@ -71,13 +71,12 @@ struct moe_ctx {
     int *rl_counters = nullptr;
     int *idx = nullptr, *idx_given = nullptr;
     float *wts = nullptr, *w_given = nullptr, *bias_tmp = nullptr;
-    __half *xop = nullptr;
+    uint8_t *xop = nullptr;   // int8-plane operand rows, op_bytes(H) each
     float *x_inv = nullptr;
     MoePlan plan{};
     int *counter = nullptr;
     float *act = nullptr, *d_inv = nullptr, *eo = nullptr;
-    uint8_t *dop = nullptr;   // down operand, dop_bytes(I) per pair
-    uint8_t *zop = nullptr;   // zeroed operand stream for empty MMA columns
+    uint8_t *dop = nullptr;   // down operand, op_bytes(I) per pair
     int *h_counts = nullptr;  // pinned [4]
     // expert-parallel buffers
     float *send_x = nullptr, *recv_x = nullptr, *send_y = nullptr, *recv_y = nullptr;
@@ -156,7 +155,8 @@ static int ctx_alloc(moe_ctx *c) {
     CK(dmalloc(&c->w_given, (size_t)R * K));
     CK(dmalloc(&c->bias_tmp, (size_t)E));
     const int RT = (c->world > 1 ? R + T : R);  // EP: received rows + local rows
-    CK(dmalloc(&c->xop, (size_t)RT * q4op_halves(H)));
+    CK(dmalloc(&c->xop, (size_t)RT * op_bytes(H)));
+    CK(cudaMemset(c->xop, 0, (size_t)RT * op_bytes(H)));
     CK(dmalloc(&c->x_inv, (size_t)RT));
     const int P = c->max_pairs;
     CK(dmalloc(&c->plan.counts, 4));
@@ -173,12 +173,8 @@ static int ctx_alloc(moe_ctx *c) {
     CK(dmalloc(&c->counter, 1));
     CK(cudaMemset(c->counter, 0, sizeof(int)));
     CK(dmalloc(&c->act, (size_t)P * I));
-    CK(dmalloc(&c->dop, (size_t)P * dop_bytes(I)));
-    {
-        const size_t zb = (dop_bytes(I) > q4op_halves(H) * 2 ? dop_bytes(I) : q4op_halves(H) * 2) + 4096;
-        CK(cudaMalloc((void **)&c->zop, zb));
-        CK(cudaMemset(c->zop, 0, zb));
-    }
+    CK(dmalloc(&c->dop, (size_t)P * op_bytes(I)));
+    CK(cudaMemset(c->dop, 0, (size_t)P * op_bytes(I)));
     CK(dmalloc(&c->d_inv, (size_t)P));
     CK(dmalloc(&c->eo, (size_t)P * H));
     CK(cudaMallocHost((void **)&c->h_counts, 4 * sizeof(int)));
@@ -276,7 +272,7 @@ void moe_destroy(moe_ctx *c) {
     void *bufs[] = {c->part, c->logits, c->rl_counters, c->d_in, c->d_out, c->h_post, c->idx, c->wts, c->idx_given, c->w_given, c->bias_tmp, c->xop, c->x_inv, c->plan.counts,
                     c->plan.pair_expert, c->plan.pair_token, c->plan.pair_w, c->plan.chunk_expert,
                     c->plan.chunk_pair0, c->plan.chunk_ntok, c->plan.slot_pair, c->plan.error, c->counter, c->act,
-                    c->dop, c->zop, c->d_inv, c->eo, c->send_x, c->recv_x, c->send_y, c->recv_y, c->send_meta,
+                    c->dop, c->d_inv, c->eo, c->send_x, c->recv_x, c->send_y, c->recv_y, c->send_meta,
                     c->recv_meta, c->rows_partial, c->tok_slot};
     for (void *b : bufs) cudaFree(b);
     if (c->h_counts) cudaFreeHost(c->h_counts);
@@ -320,6 +316,8 @@ static int layer_alloc(moe_ctx *c, int layer, int down_type, int sh_down_type) {
     if (!L.router) CK(cudaMalloc((void **)&L.router, sizeof(float) * (size_t)E * H));
     if (!L.bias) CK(cudaMalloc((void **)&L.bias, sizeof(float) * E));
     c->layer_down_bytes[layer] = db;
+    const int mrc = moe_make_layer_maps(L, c->d);
+    if (mrc) return fail(c, MOE_ERR_CUDA, "TMA tensor map of layer %d failed (%d)", layer, mrc);
     return MOE_OK;
 }
 
@@ -330,6 +328,8 @@ static int put_down(moe_ctx *c, uint8_t *dst, const void *src, int type, bool sr
     if (type == MOE_TYPE_Q4_K) {
         CK(cudaMemcpyAsync(dst, src, bytes, src_host ? cudaMemcpyHostToDevice : cudaMemcpyDeviceToDevice,
                            c->stream));
+        moe_launch_q4_repack(dst, (size_t)H * (I / MOE_QK), c->stream, &c->launches);
+        CK(cudaGetLastError());
         return MOE_OK;
     }
     const uint8_t *s = (const uint8_t *)src;
@@ -365,6 +365,7 @@ int moe_load_layer(moe_ctx *c, int layer, const void *gate_exps, const void *up_
         cudaError_t e1 = cudaMemcpyAsync(dst, g, gb, cudaMemcpyHostToDevice, c->stream);
         cudaError_t e2 = cudaMemcpyAsync(dst + gb, u, gb, cudaMemcpyHostToDevice, c->stream);
         if (e1 != cudaSuccess || e2 != cudaSuccess) { cudaFree(tmp); return fail(c, MOE_ERR_CUDA, "weight copy failed"); }
+        moe_launch_q4_repack(dst, 2 * (size_t)c->d.I * (c->d.H / MOE_QK), c->stream, &c->launches);
         rc = put_down(c, dst + 2 * gb, dn, sh ? sh_down_type : down_type, true, tmp);
         if (rc) { cudaFree(tmp); return rc; }
         cudaStreamSynchronize(c->stream);  // tmp is reused by the next expert
@@ -400,6 +401,7 @@ int moe_load_layer_packed(moe_ctx *c, int layer, const void *blob, size_t expert
         cudaError_t e1 = cudaMemcpyAsync(dst, sh ? sh_gate : src, gb, cudaMemcpyHostToDevice, c->stream);
         cudaError_t e2 = cudaMemcpyAsync(dst + gb, sh ? sh_up : src + gb, gb, cudaMemcpyHostToDevice, c->stream);
         if (e1 != cudaSuccess || e2 != cudaSuccess) { cudaFree(tmp); return fail(c, MOE_ERR_CUDA, "weight copy failed"); }
+        moe_launch_q4_repack(dst, 2 * (size_t)c->d.I * (c->d.H / MOE_QK), c->stream, &c->launches);
         rc = put_down(c, dst + 2 * gb, sh ? sh_down : src + 2 * gb, sh ? sh_down_type : down_type, true, tmp);
         if (rc) { cudaFree(tmp); return rc; }
         cudaStreamSynchronize(c->stream);
@@ -428,6 +430,7 @@ int moe_init_layer_synthetic(moe_ctx *c, int layer, uint64_t seed, int down_type
                                &c->launches);
         moe_launch_synth_quant(MOE_TYPE_Q4_K, seed, synth_stream(layer, e, SYN_UP), I, H, w_sigma,
                                dst + L.gate_bytes, c->stream, &c->launches);
+        moe_launch_q4_repack(dst, 2 * (size_t)I * (H / MOE_QK), c->stream, &c->launches);
         if (down_type == MOE_TYPE_Q6_K) {
             moe_launch_synth_quant(MOE_TYPE_Q6_K, seed, synth_stream(layer, e, SYN_DOWN), H, I, w_sigma, tmp,
                                    c->stream, &c->launches);
@@ -435,6 +438,7 @@ int moe_init_layer_synthetic(moe_ctx *c, int layer, uint64_t seed, int down_type
         } else {
             moe_launch_synth_quant(MOE_TYPE_Q4_K, seed, synth_stream(layer, e, SYN_DOWN), H, I, w_sigma,
                                    dst + 2 * L.gate_bytes, c->stream, &c->launches);
+            moe_launch_q4_repack(dst + 2 * L.gate_bytes, (size_t)H * (I / MOE_QK), c->stream, &c->launches);
         }
     }
     moe_launch_synth_f32(seed, synth_stream(layer, 0, SYN_ROUTER), (size_t)E * H, router_sigma, L.router, c->stream,
@@ -503,18 +507,27 @@ int moe_read_expert(moe_ctx *c, int layer, int expert, void *dst, size_t dst_siz
     if (dst_size < 2 * L.gate_bytes + db) return fail(c, MOE_ERR_ARG, "moe_read_expert: buffer too small");
     CK(cudaSetDevice(c->device));
     const uint8_t *src = L.experts + (size_t)j * L.expert_stride;
-    CK(cudaMemcpy(dst, src, 2 * L.gate_bytes, cudaMemcpyDeviceToHost));
+    // undo the load-time repacks in a device copy: Q4_K qs transpose (its
+    // own inverse) of gate, up and a Q4_K down; Q6_K planes -> GGUF blocks
+    uint8_t *tmp = nullptr;
+    const size_t total = 2 * L.gate_bytes + db;
+    CK(cudaMalloc((void **)&tmp, total));
+    cudaError_t e1 = cudaMemcpyAsync(tmp, src, 2 * L.gate_bytes, cudaMemcpyDeviceToDevice, c->stream);
+    moe_launch_q4_repack(tmp, 2 * (size_t)c->d.I * (c->d.H / MOE_QK), c->stream, &c->launches);
     if (ty == MOE_TYPE_Q4_K) {
-        CK(cudaMemcpy((uint8_t *)dst + 2 * L.gate_bytes, src + 2 * L.gate_bytes, db, cudaMemcpyDeviceToHost));
+        if (e1 == cudaSuccess)
+            e1 = cudaMemcpyAsync(tmp + 2 * L.gate_bytes, src + 2 * L.gate_bytes, db, cudaMemcpyDeviceToDevice,
+                                 c->stream);
+        moe_launch_q4_repack(tmp + 2 * L.gate_bytes, (size_t)c->d.H * (c->d.I / MOE_QK), c->stream, &c->launches);
     } else {
-        uint8_t *tmp = nullptr;
-        CK(cudaMalloc((void **)&tmp, db));
-        moe_launch_q6_repack(src + 2 * L.gate_bytes, tmp, c->d.H, c->d.I / MOE_QK, 1, c->stream, &c->launches);
-        cudaError_t e1 = cudaStreamSynchronize(c->stream);
-        cudaError_t e2 = cudaMemcpy((uint8_t *)dst + 2 * L.gate_bytes, tmp, db, cudaMemcpyDeviceToHost);
-        cudaFree(tmp);
-        if (e1 != cudaSuccess || e2 != cudaSuccess) return fail(c, MOE_ERR_CUDA, "moe_read_expert: unpack failed");
+        moe_launch_q6_repack(src + 2 * L.gate_bytes, tmp + 2 * L.gate_bytes, c->d.H, c->d.I / MOE_QK, 1, c->stream,
+                             &c->launches);
     }
+    cudaError_t e2 = cudaStreamSynchronize(c->stream);
+    cudaError_t e3 = cudaMemcpy(dst, tmp, total, cudaMemcpyDeviceToHost);
+    cudaFree(tmp);
+    if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess)
+        return fail(c, MOE_ERR_CUDA, "moe_read_expert: unpack failed");
     return MOE_OK;
 }
 
@@ -555,12 +568,12 @@ static int run_local(moe_ctx *c, int layer, const float *x, int T, const int *id
                               x, c->xop, c->x_inv, with_shared, 1, c->plan, c->counter, s, &c->launches);
     const int max_chunks = (T * d.K + T + MOE_TC - 1) / MOE_TC + d.E + 1;
     mark(c, MOE_PHASE_GATEUP, s);
-    moe_launch_gateup(d, L, c->plan, c->xop, reinterpret_cast<const __half *>(c->zop), c->x_inv, c->act,
-                      max_chunks * (d.I / MOE_ROWS_GU), s, &c->launches);
+    moe_launch_gateup(d, L, c->plan, c->xop, c->x_inv, c->act,
+                      max_chunks, s, &c->launches);
     mark(c, MOE_PHASE_PREP, s);
     moe_launch_prep_down(d, L, c->plan, c->act, c->dop, c->d_inv, T * d.K + T, s, &c->launches);
     mark(c, MOE_PHASE_DOWN, s);
-    moe_launch_down(d, L, c->plan, c->dop, c->zop, c->d_inv, c->eo, max_chunks * (d.H / 16), s, &c->launches);
+    moe_launch_down(d, L, c->plan, c->dop, c->d_inv, c->eo, max_chunks, s, &c->launches);
     mark(c, MOE_PHASE_OUTPUT, s);
     moe_launch_combine(d, c->plan, c->eo, T, routed, with_shared, residual, out, s, &c->launches);
     mark(c, MOE_N_PHASES, s);
@@ -605,12 +618,12 @@ static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_i
     const int P = R * d.K + T;
     const int max_chunks = (P + MOE_TC - 1) / MOE_TC + d.E + 1;
     mark(c, MOE_PHASE_GATEUP, s);
-    moe_launch_gateup(d, L, c->plan, c->xop, reinterpret_cast<const __half *>(c->zop), c->x_inv, c->act,
-                      max_chunks * (d.I / MOE_ROWS_GU), s, &c->launches);
+    moe_launch_gateup(d, L, c->plan, c->xop, c->x_inv, c->act,
+                      max_chunks, s, &c->launches);
     mark(c, MOE_PHASE_PREP, s);
     moe_launch_prep_down(d, L, c->plan, c->act, c->dop, c->d_inv, P, s, &c->launches);
     mark(c, MOE_PHASE_DOWN, s);
-    moe_launch_down(d, L, c->plan, c->dop, c->zop, c->d_inv, c->eo, max_chunks * (d.H / 16), s, &c->launches);
+    moe_launch_down(d, L, c->plan, c->dop, c->d_inv, c->eo, max_chunks, s, &c->launches);
     mark(c, MOE_PHASE_COMBINE, s);
     moe_launch_ep_partial(d, c->plan, c->recv_meta, c->eo, R, c->send_y, s, &c->launches);
     NK(moe_nccl()->GroupStart());
@@ -655,6 +668,7 @@ static int finish_sync(moe_ctx *c) {
     CK(cudaMemcpy(&errflag, c->plan.error, sizeof(int), cudaMemcpyDeviceToHost));
     if (errflag) {
         cudaMemset(c->plan.error, 0, sizeof(int));
+        if (errflag == 0x7100) return fail(c, MOE_ERR_CUDA, "expert pipeline wait timed out");
         return fail(c, MOE_ERR_ARG, "expert index out of range in routing");
     }
     return MOE_OK;

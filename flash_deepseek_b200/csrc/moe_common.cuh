@@ -15,48 +15,54 @@
 #define MOE_WARPS_DN 8     // down CTA: 8 independent warps
 
 // ---------------------------------------------------------------------------
-// Activation-operand layouts.  The decode GEMVs use the tensor core as an
-// exact reducer: the K order inside an MMA is free, so each activation
-// operand is stored pre-permuted to match the order in which a lane naturally
-// decodes its weight bytes, and laid out so that a lane reads its fragments
-// with 16-byte vector loads.
-//
-// Q4_K operand (fp16 MMA; gate/up and Q4_K down).  x*s = hi + lo (two fp16,
-// s a power of two per vector).  Per vector and super-block (256 weights):
-//   [part (hi, lo)][lane t][step 0..17][4 halves]      = 576 halves
-//   step m < 16, slot j: weight q4k_k(m, t, j)
-//   step 16: (X_a, X_b, 0, 0), X = sub-block sums of x*s for sub-blocks
-//            q4k_min_sub(t), q4k_min_sub(t)+1;  step 17: zero padding
-// Q6_K operand (int8 MMA; Q6_K down).  x*2^e rounded to a 21-bit integer
-// split into three int8 planes x = p0 + 2^7 p1 + 2^14 p2 (p0, p1 in [0,127],
-// p2 signed).  Per vector: [plane][super-block][lane t][step 0..15][4 bytes]
-// = 3 * 256 bytes per super-block; step s, byte i: weight 16 s + 4 t + i.
+// Activation operand (int8 planes).  The decode GEMVs use the tensor core as
+// an exact reducer: x * s (s a power of two per vector) is rounded to an
+// integer v with |v| <= 2^20 and split into three int8 planes
+//     v = p0 + 2^7 p1 + 2^14 p2,   p0, p1 in [0, 127], p2 in [-64, 64],
+// so that every product with a weight is exact in int32.  The K order inside
+// one MMA is free, so the planes are stored pre-permuted to the order in
+// which a lane naturally decodes its weight bytes.  Per vector and 256-weight
+// super-block, OPB_SB = 960 bytes: three plane blocks of 320 bytes
+//   [0, 256)   int8 values in lane order (style Q4 or Q6, below)
+//   [256, 288) style Q4 only: fp16 sums of 16 consecutive plane values,
+//              lane t: sums 2t, 2t+1, 2t+8, 2t+9 (exact: |sum| <= 2032)
+//   [288, 320) zero padding: plane blocks 80 words apart keep the 16-byte
+//              fragment loads of one quarter-warp on distinct banks
+// Style Q4 (Q4_K weights, m16n8k32 u8 x s8): weight k = 32 s + 8 t + i of
+// sub-block s = 2 j + h sits at 64 j + 16 t + 8 h + i.
+// Style Q6 (Q6_K weights, m16n8k16 s8 x s8): weight k = 16 s + 4 t + i of
+// sub-block s = 4 q + u sits at 64 q + 16 t + 4 u + i.
 // ---------------------------------------------------------------------------
-#define Q4OP_STEPS 18
-#define Q4OP_LANE_HALVES (Q4OP_STEPS * 4)            // 72 halves = 144 B per lane
-#define Q4OP_HALVES_PER_SB (2 * 4 * Q4OP_LANE_HALVES) // 576
-#define Q6I_BYTES_PER_SB 256                          // per plane
-__host__ __device__ __forceinline__ size_t q4op_halves(int K) { return (size_t)(K / 256) * Q4OP_HALVES_PER_SB; }
-__host__ __device__ __forceinline__ size_t q6i_bytes(int K) { return (size_t)3 * (K / 256) * Q6I_BYTES_PER_SB; }
-// bytes reserved per vector in a buffer that may hold either operand
-__host__ __device__ __forceinline__ size_t dop_bytes(int K) {
-    const size_t a = q4op_halves(K) * 2, b = q6i_bytes(K);
-    return a > b ? a : b;
+#define OPB_PLANE 320
+#define OPB_SB (3 * OPB_PLANE)
+#define OPB_XSUM 256
+__host__ __device__ __forceinline__ size_t op_bytes(int K) { return (size_t)(K / 256) * OPB_SB; }
+__host__ __device__ __forceinline__ int opq4_off(int k) {
+    const int s = k >> 5, t = (k >> 3) & 3, i = k & 7;
+    return 64 * (s >> 1) + 16 * t + 8 * (s & 1) + i;
+}
+__host__ __device__ __forceinline__ int opq6_off(int k) {
+    const int s = k >> 4, t = (k >> 2) & 3, i = k & 3;
+    return 64 * (s >> 2) + 16 * t + 4 * (s & 3) + i;
+}
+// byte offset (inside a plane block) of the fp16 sum of plane values
+// [16 jj, 16 jj + 16) of a super-block
+__host__ __device__ __forceinline__ int opq4_xsum_off(int jj) {
+    const int t = (jj & 7) >> 1, u = 2 * (jj >> 3) + (jj & 1);
+    return OPB_XSUM + 8 * t + 2 * u;
 }
 
-__host__ __device__ __forceinline__ int perm_j(int j) { return (j == 1) ? 2 : ((j == 2) ? 1 : j); }
-
-// Weight index (0..255) inside a Q4_K super-block for MMA step m, lane t, slot
-// j.  Lane t loads qs bytes [64r + 16t, +16) (r = m/8); word i = (m/2)%4 of
-// that load; m odd = high nibbles.  Low nibble of qs byte b of chunk c is
-// weight 64c + b, the high nibble weight 64c + 32 + b (quant.c:49-58).
-__host__ __device__ __forceinline__ int q4k_k(int m, int t, int j) {
-    const int r = m >> 3, i = (m >> 1) & 3, hi = m & 1;
-    const int c = 2 * r + (t >> 1);
-    return 64 * c + 32 * hi + 16 * (t & 1) + 4 * i + perm_j(j);
+// ---------------------------------------------------------------------------
+// Repacked Q4_K block (lossless, done once at load): the 16-byte header
+// (d, dmin, 12 scale bytes) stays, the 128 qs bytes are transposed as a 4x4
+// grid of 8-byte chunks, new chunk 4 t + j = old chunk 4 j + t, so that lane
+// t of an MMA finds its 32 bytes (old bytes 32 j + 8 t + [0, 8), j = 0..3)
+// contiguous.  The transpose is its own inverse.
+// ---------------------------------------------------------------------------
+__host__ __device__ __forceinline__ int q4r_src_qs(int p) {
+    const int c = p >> 3, i = p & 7;
+    return 8 * (4 * (c & 3) + (c >> 2)) + i;
 }
-// First of the two sub-blocks whose min-term lane t supplies (0, 4, 2, 6).
-__host__ __device__ __forceinline__ int q4k_min_sub(int t) { return 2 * (t >> 1) + 4 * (t & 1); }
 
 // Weight index inside a Q6_K super-block for sub-block step s (0..15), lane t,
 // byte i of the lane's int8 fragment.

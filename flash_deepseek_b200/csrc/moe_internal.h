@@ -1,5 +1,6 @@
 // moe_internal.h -- host-side view of the device pipeline of libmoe_cuda.so.
 #pragma once
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
@@ -31,6 +32,12 @@ struct MoeLayerDev {
     float *bias;            // [E] selection bias (exp_probs_b)
     float *logit_bias;      // [E] added to the logits before the sigmoid, or nullptr
     float *norm;            // [H] or nullptr
+    // TMA maps over [slot][row][byte] of this layer's weights (moe_experts.cu)
+    CUtensorMap tm_gu;      // gate and up rows (2 I) of repacked Q4_K, box 144 B x 64 rows
+    CUtensorMap tm_d4;      // Q4_K down rows (H), box 144 B x 128 rows
+    CUtensorMap tm_d6q;     // Q6_K down, Q plane, box 192 B x 128 rows
+    CUtensorMap tm_d6s;     // Q6_K down, S plane, box 16 B x 128 rows
+    CUtensorMap tm_d6d;     // Q6_K down, D plane, box 2 nb_pad B x 128 rows
 };
 
 struct MoeDims {
@@ -38,7 +45,7 @@ struct MoeDims {
     float scale;
 };
 
-#define MOE_TC 8  // tokens per chunk (two 8-column MMA tiles: 4 tokens x {hi, lo} each)
+#define MOE_TC 8  // tokens per chunk (four 8-column MMA tiles of 2 tokens x 3 planes)
 
 // ---- launchers (moe_kernels.cu); every one counts its kernel launches ------
 extern "C++" {
@@ -50,18 +57,19 @@ void moe_launch_router_logits(const float *Wr, const float *x, int T, int H, int
 // 2 shared expert only
 void moe_launch_route_and_plan(const MoeDims &d, const float *part, int n_split, const float *logits,
                                const float *bias, const float *logit_bias, int mode, const int *idx_in, const float *w_in, int T,
-                               int *idx_out, float *w_out, const float *x, __half *xop, float *x_inv,
+                               int *idx_out, float *w_out, const float *x, uint8_t *xop, float *x_inv,
                                int include_shared, int build_plan, const MoePlan &plan, int *counter,
                                cudaStream_t s, uint64_t *launches);
-// zop: zeroed operand stream used for empty MMA columns
-void moe_launch_gateup(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const __half *xop,
-                       const __half *zop, const float *x_inv, float *act, int max_items, cudaStream_t s,
-                       uint64_t *launches);
+// xop: int8-plane operand rows (op_bytes(H) each) indexed by pair_token;
+// max_chunks bounds the chunk count of the plan (grid size)
+void moe_launch_gateup(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const uint8_t *xop,
+                       const float *x_inv, float *act, int max_chunks, cudaStream_t s, uint64_t *launches);
 void moe_launch_prep_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const float *act,
                           uint8_t *dop, float *d_inv, int max_pairs, cudaStream_t s, uint64_t *launches);
 void moe_launch_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const uint8_t *dop,
-                     const uint8_t *zop, const float *d_inv, float *eo, int max_items, cudaStream_t s,
-                     uint64_t *launches);
+                     const float *d_inv, float *eo, int max_chunks, cudaStream_t s, uint64_t *launches);
+// TMA maps of a layer (after its weights are allocated); 0 = ok
+int moe_make_layer_maps(MoeLayerDev &L, const MoeDims &d);
 void moe_launch_combine(const MoeDims &d, const MoePlan &plan, const float *eo, int T, int include_routed,
                         int include_shared, const float *residual, float *out, cudaStream_t s, uint64_t *launches);
 void moe_launch_rmsnorm(const float *x, const float *w, float *y, int T, int H, float eps, cudaStream_t s,
@@ -69,12 +77,14 @@ void moe_launch_rmsnorm(const float *x, const float *w, float *y, int T, int H, 
 void moe_launch_dequant(int type, const uint8_t *src, float *dst, size_t n, cudaStream_t s, uint64_t *launches);
 void moe_launch_q6_repack(const uint8_t *src, uint8_t *dst, int rows, int nb, int inverse, cudaStream_t s,
                           uint64_t *launches);
+// in-place Q4_K qs transpose (its own inverse) of nblocks 144-byte blocks
+void moe_launch_q4_repack(uint8_t *buf, size_t nblocks, cudaStream_t s, uint64_t *launches);
 void moe_launch_synth_quant(int type, uint64_t seed, uint64_t stream, int rows, int cols, double sigma,
                             uint8_t *dst, cudaStream_t s, uint64_t *launches);
 void moe_launch_synth_f32(uint64_t seed, uint64_t stream, size_t n, double sigma, float *dst, cudaStream_t s,
                           uint64_t *launches);
 void moe_launch_prep_rows(const float *recv, const int *meta, int meta_w, int R, const float *local, int T, int H,
-                          __half *xop, float *x_inv, cudaStream_t s, uint64_t *launches);
+                          uint8_t *xop, float *x_inv, cudaStream_t s, uint64_t *launches);
 // expert parallel (moe_ep.cu)
 void moe_launch_ep_pack(const float *x, const int *idx, const float *w, int T, int K, int H, int world, int n_local,
                         int cap, float *send_x, int *send_meta, int *tok_slot, cudaStream_t s, uint64_t *launches);
@@ -85,6 +95,4 @@ void moe_launch_ep_partial(const MoeDims &d, const MoePlan &plan, const int *rec
 void moe_launch_ep_final(const MoeDims &d, const MoePlan &plan, const float *recv_y, const int *tok_slot, int world,
                          int cap, int T, const float *eo, const float *residual, float *out, cudaStream_t s,
                          uint64_t *launches);
-size_t moe_q4op_halves(int K);   // Q4_K activation operand, halves per vector
-size_t moe_dop_bytes(int K);     // bytes per vector of the down operand buffer
 }

@@ -30,8 +30,6 @@ static int num_sms() {
     return g_num_sms;
 }
 
-size_t moe_q4op_halves(int K) { return q4op_halves(K); }
-size_t moe_dop_bytes(int K) { return dop_bytes(K); }
 
 // ===========================================================================
 // codec: device twins of quant.c (bit exact; explicit _rn ops, no contraction)
@@ -118,7 +116,11 @@ __global__ void k_q6_repack(const uint8_t *__restrict__ src, uint8_t *__restrict
         uint8_t *g = (inverse ? dst : (uint8_t *)src) + b * MOE_Q6K_BYTES;
         for (int p = lane; p < 192; p += 32) {
             const int sbyte = q6r_src_byte(p);
-            if (inverse) g[sbyte] = rq[p]; else rq[p] = g[sbyte];
+            // qh bytes are stored with the high bit of every 2-bit pair
+            // inverted: the kernels then decode 4 (q ^ 32), i.e. 4 (q - 32)
+            // as int8, with no separate offset term
+            const uint8_t flip = sbyte >= 128 ? 0xAA : 0x00;
+            if (inverse) g[sbyte] = rq[p] ^ flip; else rq[p] = g[sbyte] ^ flip;
         }
         if (lane < 16) {
             if (inverse) g[192 + lane] = rs[lane]; else rs[lane] = g[192 + lane];
@@ -128,6 +130,30 @@ __global__ void k_q6_repack(const uint8_t *__restrict__ src, uint8_t *__restrict
         // pad entries of the d plane (nb not a multiple of 8) stay zero: the
         // destination is cleared by the caller.
     }
+}
+
+// Q4_K: transpose the 4x4 grid of 8-byte qs chunks of every block (its own
+// inverse; layout in moe_common.cuh).
+__global__ void k_q4_repack(uint8_t *__restrict__ buf, size_t nblocks) {
+    for (size_t b = (size_t)blockIdx.x * blockDim.x + threadIdx.x; b < nblocks; b += (size_t)gridDim.x * blockDim.x) {
+        uint2 *qs = reinterpret_cast<uint2 *>(buf + b * MOE_Q4K_BYTES + 16);
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+#pragma unroll
+            for (int t = j + 1; t < 4; t++) {
+                const uint2 x = qs[4 * j + t];
+                qs[4 * j + t] = qs[4 * t + j];
+                qs[4 * t + j] = x;
+            }
+    }
+}
+
+void moe_launch_q4_repack(uint8_t *buf, size_t nblocks, cudaStream_t s, uint64_t *launches) {
+    if (!nblocks) return;
+    size_t grid = (nblocks + 255) / 256;
+    if (grid > (size_t)num_sms() * 16) grid = (size_t)num_sms() * 16;
+    k_q4_repack<<<(int)grid, 256, 0, s>>>(buf, nblocks);
+    LAUNCH_COUNT(launches);
 }
 
 void moe_launch_q6_repack(const uint8_t *src, uint8_t *dst, int rows, int nb, int inverse, cudaStream_t s,
@@ -475,9 +501,8 @@ __device__ __forceinline__ float block_max_abs(const float *x, int n, float *red
 }
 
 // power-of-two scale s with max|x| * s in [2^(top-1), 2^top); returns s, sets
-// *inv = 1/s.  top = 10 for the fp16 operand (sub-block sums stay below
-// 65504), 20 for the int8-plane operand (|x * s| < 2^20).
-__device__ __forceinline__ float op_scale(float amax, float *inv, int top = 10) {
+// *inv = 1/s.  The int8-plane operand uses top = 20 (|rint(x * s)| <= 2^20).
+__device__ __forceinline__ float op_scale(float amax, float *inv, int top) {
     if (!(amax > 0.0f) || !isfinite(amax)) { *inv = 1.0f; return 1.0f; }
     int ex;
     frexpf(amax, &ex);  // amax = m 2^ex, m in [0.5, 1)
@@ -488,67 +513,36 @@ __device__ __forceinline__ float op_scale(float amax, float *inv, int top = 10) 
     return ldexpf(1.0f, e);
 }
 
-__device__ __forceinline__ void split_hl(float v, __half &hi, __half &lo) {
-    hi = __float2half_rn(v);
-    lo = __float2half_rn(__fsub_rn(v, __half2float(hi)));
-}
-
-// Q4_K operand of one K-vector (all threads of the block).  xsum: smem
-// scratch of K/32 floats for the sub-block sums.
-__device__ void build_q4op(const float *__restrict__ x, int K, float s, __half *__restrict__ op,
-                           float *__restrict__ xsum) {
-    const int NB = K / MOE_QK;
-    for (int sub = threadIdx.x; sub < K / 32; sub += blockDim.x) {
-        float acc = 0.0f;
-        for (int i = 0; i < 32; i++) {
-            __half hi, lo;
-            split_hl(__fmul_rn(x[32 * sub + i], s), hi, lo);
-            acc = __fadd_rn(acc, __fadd_rn(__half2float(hi), __half2float(lo)));
+// int8-plane operand of one K-vector (all threads of the block; x in shared
+// memory): v = rint(x * s), |v| <= 2^20, v = p0 + 2^7 p1 + 2^14 p2, stored
+// in the lane order of `style` (4: Q4_K weights, with the fp16 sums of 16
+// consecutive plane values; 6: Q6_K weights).  Layout in moe_common.cuh.
+__device__ void build_op(const float *__restrict__ x, int K, float s, uint8_t *__restrict__ op, int style) {
+    for (int m = threadIdx.x; m < K / 4; m += blockDim.x) {
+        const int k = 4 * m, kk = k & 255;
+        uint32_t w0 = 0, w1 = 0, w2 = 0;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int v = __float2int_rn(__fmul_rn(x[k + i], s));
+            w0 |= (uint32_t)(v & 127) << (8 * i);
+            w1 |= (uint32_t)((v >> 7) & 127) << (8 * i);
+            w2 |= (uint32_t)((v >> 14) & 255) << (8 * i);
         }
-        xsum[sub] = acc;
+        uint8_t *b = op + (size_t)(k >> 8) * OPB_SB + (style == 4 ? opq4_off(kk) : opq6_off(kk));
+        *reinterpret_cast<uint32_t *>(b) = w0;
+        *reinterpret_cast<uint32_t *>(b + OPB_PLANE) = w1;
+        *reinterpret_cast<uint32_t *>(b + 2 * OPB_PLANE) = w2;
     }
-    __syncthreads();
-    const __half z = __float2half_rn(0.0f);
-    for (int ent = threadIdx.x; ent < NB * 4 * Q4OP_STEPS; ent += blockDim.x) {
-        const int sb = ent / (4 * Q4OP_STEPS), t = (ent / Q4OP_STEPS) % 4, m = ent % Q4OP_STEPS;
-        __half *o = op + (size_t)sb * Q4OP_HALVES_PER_SB + t * Q4OP_LANE_HALVES + m * 4;  // part 0 (hi)
-        __half *o1 = o + 4 * Q4OP_LANE_HALVES;                                                // part 1 (lo)
-        const float *xb = x + sb * MOE_QK;
-        if (m < 16) {
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                __half hi, lo;
-                split_hl(__fmul_rn(xb[q4k_k(m, t, j)], s), hi, lo);
-                o[j] = hi;
-                o1[j] = lo;
-            }
-        } else if (m == 16) {
-            const int sa = q4k_min_sub(t);
-#pragma unroll
-            for (int u = 0; u < 2; u++) {
-                __half hi, lo;
-                split_hl(xsum[sb * 8 + sa + u], hi, lo);
-                o[u] = hi;
-                o1[u] = lo;
-            }
-            o[2] = o[3] = o1[2] = o1[3] = z;
-        } else {
-#pragma unroll
-            for (int j = 0; j < 4; j++) o[j] = o1[j] = z;
+    if (style != 4) return;
+    for (int q = threadIdx.x; q < (K / 16) * 3; q += blockDim.x) {
+        const int grp = q / 3, pl = q % 3, k0 = 16 * grp;
+        int acc = 0;
+        for (int i = 0; i < 16; i++) {
+            const int v = __float2int_rn(__fmul_rn(x[k0 + i], s));
+            acc += pl == 0 ? (v & 127) : (pl == 1 ? ((v >> 7) & 127) : (v >> 14));
         }
-    }
-}
-
-// Q6_K operand: 21-bit fixed point x * 2^e split into three int8 planes.
-__device__ void build_q6i(const float *__restrict__ x, int K, float s, int8_t *__restrict__ op) {
-    const int NB = K / MOE_QK;
-    for (int k = threadIdx.x; k < K; k += blockDim.x) {
-        const int v = __float2int_rn(__fmul_rn(x[k], s));  // |v| <= 2^20
-        const int sb = k / MOE_QK, w = k % MOE_QK, st = w / 16, t = (w / 4) % 4, i = w % 4;
-        const size_t off = ((size_t)sb * 4 + t) * 64 + st * 4 + i;
-        op[off] = (int8_t)(v & 127);
-        op[(size_t)NB * Q6I_BYTES_PER_SB + off] = (int8_t)((v >> 7) & 127);
-        op[(size_t)2 * NB * Q6I_BYTES_PER_SB + off] = (int8_t)(v >> 14);
+        *reinterpret_cast<__half *>(op + (size_t)(k0 >> 8) * OPB_SB + pl * OPB_PLANE +
+                                    opq4_xsum_off((k0 & 255) >> 4)) = __int2half_rn(acc);
     }
 }
 
@@ -565,7 +559,7 @@ struct RouteArgs {
     int mode;                              // 0 route, 1 routing given, 2 shared expert only
     int T;
     int *idx_out; float *w_out;
-    const float *x; __half *xop; float *x_inv;   // x operand (may be nullptr)
+    const float *x; uint8_t *xop; float *x_inv;  // x operand (may be nullptr)
     int include_shared, build_plan;
     MoePlan plan;
     int *counter;
@@ -685,7 +679,6 @@ __global__ void __launch_bounds__(256) k_route_plan(RouteArgs a) {
     __shared__ float score[1024], choice[1024];
     __shared__ float gs[64];
     __shared__ float red[32];
-    __shared__ float xsum[1024];  // sub-block sums of the operand (H <= 32768)
     __shared__ int is_last;
     const int t = blockIdx.x;
     const int E = a.d.E, K = a.d.K, G = a.d.n_group, TG = a.d.topk_group;
@@ -774,8 +767,8 @@ __global__ void __launch_bounds__(256) k_route_plan(RouteArgs a) {
         const float *xr = xrow;
         const float amax = block_max_abs(xr, a.d.H, red);
         float inv;
-        const float s = op_scale(amax, &inv);
-        build_q4op(xr, a.d.H, s, a.xop + (size_t)t * q4op_halves(a.d.H), xsum);
+        const float s = op_scale(amax, &inv, 20);
+        build_op(xr, a.d.H, s, a.xop + (size_t)t * op_bytes(a.d.H), 4);
         if (threadIdx.x == 0) a.x_inv[t] = inv;
     }
     if (!a.build_plan) return;
@@ -792,7 +785,7 @@ __global__ void __launch_bounds__(256) k_route_plan(RouteArgs a) {
 
 void moe_launch_route_and_plan(const MoeDims &d, const float *part, int n_split, const float *logits,
                                const float *bias, const float *logit_bias, int mode, const int *idx_in, const float *w_in, int T,
-                               int *idx_out, float *w_out, const float *x, __half *xop, float *x_inv,
+                               int *idx_out, float *w_out, const float *x, uint8_t *xop, float *x_inv,
                                int include_shared, int build_plan, const MoePlan &plan, int *counter,
                                cudaStream_t s, uint64_t *launches) {
     RouteArgs a;
@@ -819,413 +812,14 @@ void moe_launch_route_and_plan(const MoeDims &d, const float *part, int n_split,
 // P1 = sum sc*q*x and P2 = sum m*X (min term) on the tensor core and flushes
 // acc += d*P1 - dmin*P2 (quant.c:36-61 algebra, fp32).
 // ===========================================================================
-struct Q4Hdr {
-    __half2 sc[4], nsc[4];
-    uint32_t m2;
-    float d, dmin;
-};
-
-// Scales of the four sub-blocks lane t decodes (u = 2r + hi -> sub-block
-// 4r + 2(t/2) + hi, quant.c:26-34) as half2 pairs, with the magic offsets of
-// the low-nibble (1024) and high-nibble (64) decodes; m2 = the two minimums
-// lane t supplies to the min-term MMA.
-__device__ __forceinline__ void q4_decode_hdr(const uint4 h, int t, Q4Hdr &o) {
-    const int q = t >> 1;
-    o.d = h2f_bits((uint16_t)(h.x & 0xFFFFu));
-    o.dmin = h2f_bits((uint16_t)(h.x >> 16));
-    const uint32_t a0 = h.y >> (16 * q), a1 = h.z >> (16 * q), a2 = h.w >> (16 * q);
-    const uint32_t sc_lo = a0 & 0x3F3Fu, m_lo = a1 & 0x3F3Fu;
-    const uint32_t sc_hi = (a2 & 0x0F0Fu) | ((a0 >> 2) & 0x3030u);
-    const uint32_t m_hi = ((a2 >> 4) & 0x0F0Fu) | ((a1 >> 2) & 0x3030u);
-    const __half2 k1024 = __float2half2_rn(1024.0f), km1024 = __float2half2_rn(-1024.0f),
-                  km64 = __float2half2_rn(-64.0f);
-    o.sc[0] = __hsub2(u32_as_h2(__byte_perm(sc_lo, 0x6464u, 0x4040u)), k1024);
-    o.sc[1] = __hsub2(u32_as_h2(__byte_perm(sc_lo, 0x6464u, 0x4141u)), k1024);
-    o.sc[2] = __hsub2(u32_as_h2(__byte_perm(sc_hi, 0x6464u, 0x4040u)), k1024);
-    o.sc[3] = __hsub2(u32_as_h2(__byte_perm(sc_hi, 0x6464u, 0x4141u)), k1024);
-    o.nsc[0] = __hmul2(o.sc[0], km1024);
-    o.nsc[1] = __hmul2(o.sc[1], km64);
-    o.nsc[2] = __hmul2(o.sc[2], km1024);
-    o.nsc[3] = __hmul2(o.sc[3], km64);
-    const uint32_t mw = (t & 1) ? m_hi : m_lo;
-    o.m2 = h2_as_u32(__hsub2(u32_as_h2(__byte_perm(mw, 0x6464u, 0x4140u)), k1024));
-}
-
-// sc*q (exact fp16) of the low nibbles at bits [0,4) and [16,20) of w: the
-// half with bits 0x6400 | q is 1024 + q.
-__device__ __forceinline__ uint32_t q4_dq_lo(uint32_t w, __half2 sc, __half2 nsc1024) {
-    return h2_as_u32(__hfma2(u32_as_h2((w & 0x000F000Fu) | 0x64006400u), sc, nsc1024));
-}
-// ... of the high nibbles at bits [4,8) and [20,24) without a shift: the
-// half with bits 0x5400 | (q << 4) is 64 + q.
-__device__ __forceinline__ uint32_t q4_dq_hi(uint32_t w, __half2 sc, __half2 nsc64) {
-    return h2_as_u32(__hfma2(u32_as_h2((w & 0x00F000F0u) | 0x54005400u), sc, nsc64));
-}
-
-// raw bytes of one Q4_K super-block for rows g and g+8 of one lane
-struct Q4Raw {
-    uint4 hg, hg8, qg[2], qg8[2];
-};
-
-// ring slot of a lane: word k of stage `slot` at wsm[(slot * W + k) * 32 + lane]
-__device__ __forceinline__ void q4_issue(uint4 *wsm, int slot, int lane, const uint8_t *__restrict__ rg,
-                                         const uint8_t *__restrict__ rg8, int sb, int t) {
-    const uint8_t *bg = rg + (size_t)sb * MOE_Q4K_BYTES, *bg8 = rg8 + (size_t)sb * MOE_Q4K_BYTES;
-    uint4 *w = wsm + slot * MOE_Q4_WORDS * 32 + lane;
-    cp_async16(w + 0 * 32, bg);
-    cp_async16(w + 1 * 32, bg8);
-    cp_async16(w + 2 * 32, bg + 16 + 16 * t);
-    cp_async16(w + 3 * 32, bg + 80 + 16 * t);
-    cp_async16(w + 4 * 32, bg8 + 16 + 16 * t);
-    cp_async16(w + 5 * 32, bg8 + 80 + 16 * t);
-}
-
-__device__ __forceinline__ void q4_read(Q4Raw &r, const uint4 *wsm, int slot, int lane) {
-    const uint4 *w = wsm + slot * MOE_Q4_WORDS * 32 + lane;
-    r.hg = w[0];
-    r.hg8 = w[32];
-    r.qg[0] = w[64];
-    r.qg[1] = w[96];
-    r.qg8[0] = w[128];
-    r.qg8[1] = w[160];
-}
-
-__device__ __forceinline__ uint32_t u4c(const uint4 &v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
-
-// One Q4_K super-block of rows (g, g+8) against NT 8-column tiles (4 vectors
-// x {hi, lo}).  opb[n] points at this lane's fragment stream of tile n (a
-// zero stream for empty columns).
-template <int NT>
-__device__ __forceinline__ void q4_compute(const Q4Raw &R, int sb, const __half *const (&opb)[NT],
-                                           float (&acc)[NT][2], int t) {
-    Q4Hdr Hg, Hg8;
-    q4_decode_hdr(R.hg, t, Hg);
-    q4_decode_hdr(R.hg8, t, Hg8);
-    float p1[NT][4], p2[NT][4];
-#pragma unroll
-    for (int n = 0; n < NT; n++)
-#pragma unroll
-        for (int c = 0; c < 4; c++) p1[n][c] = 0.0f;
-#pragma unroll
-    for (int r = 0; r < 2; r++) {
-        uint4 B[NT][4];  // steps 8r .. 8r+7 of this lane: 64 bytes
-#pragma unroll
-        for (int n = 0; n < NT; n++) {
-            const uint4 *bp = reinterpret_cast<const uint4 *>(opb[n] + (size_t)sb * Q4OP_HALVES_PER_SB + r * 32);
-#pragma unroll
-            for (int q = 0; q < 4; q++) B[n][q] = ldg_op16(bp + q);
-        }
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const uint32_t wg = u4c(R.qg[r], i), wg8 = u4c(R.qg8[r], i);
-            const uint32_t wg_s = wg >> 8, wg8_s = wg8 >> 8;
-            const int ul = 2 * r, uh = 2 * r + 1;
-            // low nibbles (step 2i) then high nibbles (step 2i + 1)
-            const uint32_t l0 = q4_dq_lo(wg, Hg.sc[ul], Hg.nsc[ul]), l2 = q4_dq_lo(wg_s, Hg.sc[ul], Hg.nsc[ul]);
-            const uint32_t l1 = q4_dq_lo(wg8, Hg8.sc[ul], Hg8.nsc[ul]), l3 = q4_dq_lo(wg8_s, Hg8.sc[ul], Hg8.nsc[ul]);
-            const uint32_t h0 = q4_dq_hi(wg, Hg.sc[uh], Hg.nsc[uh]), h2 = q4_dq_hi(wg_s, Hg.sc[uh], Hg.nsc[uh]);
-            const uint32_t h1 = q4_dq_hi(wg8, Hg8.sc[uh], Hg8.nsc[uh]), h3 = q4_dq_hi(wg8_s, Hg8.sc[uh], Hg8.nsc[uh]);
-#pragma unroll
-            for (int n = 0; n < NT; n++) {
-                const uint4 &b = B[n][i];
-                mma_f16_16816(p1[n], l0, l1, l2, l3, b.x, b.y, p1[n][0], p1[n][1], p1[n][2], p1[n][3]);
-                mma_f16_16816(p1[n], h0, h1, h2, h3, b.z, b.w, p1[n][0], p1[n][1], p1[n][2], p1[n][3]);
-            }
-        }
-    }
-#pragma unroll
-    for (int n = 0; n < NT; n++) {
-        const uint4 b = ldg_op16(opb[n] + (size_t)sb * Q4OP_HALVES_PER_SB + 64);  // steps 16 (min) and 17 (pad)
-        mma_f16_16816(p2[n], Hg.m2, Hg8.m2, 0u, 0u, b.x, b.y, 0.f, 0.f, 0.f, 0.f);
-        acc[n][0] = fmaf(Hg.d, p1[n][0] + p1[n][1], fmaf(-Hg.dmin, p2[n][0] + p2[n][1], acc[n][0]));
-        acc[n][1] = fmaf(Hg8.d, p1[n][2] + p1[n][3], fmaf(-Hg8.dmin, p2[n][2] + p2[n][3], acc[n][1]));
-    }
-}
-
-// Per-lane cp.async pipeline: MOE_STAGES - 1 super-blocks in flight while
-// the current one is decoded.  wsm = this warp's ring [MOE_STAGES][6][32].
-template <int NT>
-__device__ __forceinline__ void q4k_warp_rows(const uint8_t *__restrict__ rg, const uint8_t *__restrict__ rg8,
-                                              int sb0, int sb1, const __half *const (&opb)[NT],
-                                              float (&acc)[NT][2], int t, int lane, uint4 *wsm) {
-#pragma unroll
-    for (int s = 0; s < MOE_STAGES - 1; s++) {
-        if (sb0 + s < sb1) q4_issue(wsm, s, lane, rg, rg8, sb0 + s, t);
-        cp_async_commit();
-    }
-    int slot = 0, nslot = MOE_STAGES - 1;
-#pragma unroll 1
-    for (int sb = sb0; sb < sb1; ++sb) {
-        if (sb + MOE_STAGES - 1 < sb1) q4_issue(wsm, nslot, lane, rg, rg8, sb + MOE_STAGES - 1, t);
-        cp_async_commit();
-        cp_async_wait<MOE_STAGES - 1>();
-        Q4Raw R;
-        q4_read(R, wsm, slot, lane);
-        q4_compute<NT>(R, sb, opb, acc, t);
-        slot = (slot + 1 == MOE_STAGES) ? 0 : slot + 1;
-        nslot = (nslot + 1 == MOE_STAGES) ? 0 : nslot + 1;
-    }
-    cp_async_wait<0>();
-}
-
-// ---------------------------------------------------------------------------
-// Q6_K (repacked planes) against the int8-plane operand.  Per 16-weight
-// sub-block s: A = q6 as u8 (nibble | 2 high bits << 4, exact), one u8 x s8
-// MMA for sum q6*x and one s8 x s8 MMA with A = -32 everywhere for -32*sum x,
-// both into the same int32 tile; flushed as acc += sc_s * D (exact int32).
-// At the end of each super-block acc_f += d * acc (fp32).
-// ---------------------------------------------------------------------------
-struct Q6Raw {
-    uint4 ug[3], ug8[3], sg, sg8;
-};
-
-__device__ __forceinline__ void q6_issue(uint4 *wsm, int slot, int lane, const uint8_t *__restrict__ qpl,
-                                         const uint8_t *__restrict__ spl, int nb, int row_g, int sb, int t) {
-    const uint8_t *qg = qpl + ((size_t)row_g * nb + sb) * 192 + 48 * t;
-    const uint8_t *qg8 = qpl + ((size_t)(row_g + 8) * nb + sb) * 192 + 48 * t;
-    uint4 *w = wsm + slot * MOE_Q6_WORDS * 32 + lane;
-#pragma unroll
-    for (int v = 0; v < 3; v++) {
-        cp_async16(w + v * 32, qg + 16 * v);
-        cp_async16(w + (3 + v) * 32, qg8 + 16 * v);
-    }
-    cp_async16(w + 6 * 32, spl + ((size_t)row_g * nb + sb) * 16);
-    cp_async16(w + 7 * 32, spl + ((size_t)(row_g + 8) * nb + sb) * 16);
-}
-
-__device__ __forceinline__ void q6_read(Q6Raw &r, const uint4 *wsm, int slot, int lane) {
-    const uint4 *w = wsm + slot * MOE_Q6_WORDS * 32 + lane;
-#pragma unroll
-    for (int v = 0; v < 3; v++) {
-        r.ug[v] = w[v * 32];
-        r.ug8[v] = w[(3 + v) * 32];
-    }
-    r.sg = w[6 * 32];
-    r.sg8 = w[7 * 32];
-}
-
-// u8 q6 values (one byte per weight) of sub-block sp of a half: nibble word W,
-// qh word Hw (bit pair sp/2 of every byte)
-template <int SP>
-__device__ __forceinline__ uint32_t q6_a(uint32_t W, uint32_t Hw) {
-    const uint32_t nib = SP < 4 ? (W & 0x0F0F0F0Fu) : ((W >> 4) & 0x0F0F0F0Fu);
-    const int f = SP >> 1;
-    const uint32_t hs = f == 0 ? (Hw << 4) : f == 1 ? (Hw << 2) : f == 2 ? Hw : (Hw >> 2);
-    return nib | (hs & 0x30303030u);
-}
-
-template <int NT>
-__device__ __forceinline__ void q6i_compute(const Q6Raw &R, int sb, const int8_t *const (&opb)[NT],
-                                            int (&acc)[NT][4]) {
-    const uint32_t wg[2][6] = {{R.ug[0].x, R.ug[0].y, R.ug[0].z, R.ug[0].w, R.ug[1].x, R.ug[1].y},
-                               {R.ug[1].z, R.ug[1].w, R.ug[2].x, R.ug[2].y, R.ug[2].z, R.ug[2].w}};
-    const uint32_t wg8[2][6] = {{R.ug8[0].x, R.ug8[0].y, R.ug8[0].z, R.ug8[0].w, R.ug8[1].x, R.ug8[1].y},
-                                {R.ug8[1].z, R.ug8[1].w, R.ug8[2].x, R.ug8[2].y, R.ug8[2].z, R.ug8[2].w}};
-    const uint32_t sgw[4] = {R.sg.x, R.sg.y, R.sg.z, R.sg.w}, sg8w[4] = {R.sg8.x, R.sg8.y, R.sg8.z, R.sg8.w};
-    const uint32_t NEG32 = 0xE0E0E0E0u;
-    uint4 Bq[NT];  // fragments of the current quarter; the next quarter's are loaded one quarter ahead
-#pragma unroll
-    for (int n = 0; n < NT; n++) Bq[n] = ldg_op16(opb[n] + (size_t)sb * Q6I_BYTES_PER_SB);
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-#pragma unroll
-        for (int qd = 0; qd < 2; qd++) {  // quarter: steps 8h + 4qd .. +3
-            uint4 B[NT], Bn[NT];
-#pragma unroll
-            for (int n = 0; n < NT; n++) {
-                B[n] = Bq[n];
-                if (2 * h + qd < 3) Bn[n] = ldg_op16(opb[n] + (size_t)sb * Q6I_BYTES_PER_SB + (2 * h + qd + 1) * 16);
-            }
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const int sp = 4 * qd + j, s = 8 * h + sp;
-                uint32_t a0, a1;
-#define Q6A(SPV)                                                   \
-    a0 = q6_a<SPV>(wg[h][(SPV)&3], wg[h][4 + ((SPV)&1)]);          \
-    a1 = q6_a<SPV>(wg8[h][(SPV)&3], wg8[h][4 + ((SPV)&1)]);
-                switch (sp) {
-                    case 0: Q6A(0) break;
-                    case 1: Q6A(1) break;
-                    case 2: Q6A(2) break;
-                    case 3: Q6A(3) break;
-                    case 4: Q6A(4) break;
-                    case 5: Q6A(5) break;
-                    case 6: Q6A(6) break;
-                    default: Q6A(7) break;
-                }
-#undef Q6A
-                int scg, scg8;
-                switch (s & 3) {
-                    case 0: scg = sext_byte<0>(sgw[s >> 2]); scg8 = sext_byte<0>(sg8w[s >> 2]); break;
-                    case 1: scg = sext_byte<1>(sgw[s >> 2]); scg8 = sext_byte<1>(sg8w[s >> 2]); break;
-                    case 2: scg = sext_byte<2>(sgw[s >> 2]); scg8 = sext_byte<2>(sg8w[s >> 2]); break;
-                    default: scg = sext_byte<3>(sgw[s >> 2]); scg8 = sext_byte<3>(sg8w[s >> 2]); break;
-                }
-#pragma unroll
-                for (int n = 0; n < NT; n++) {
-                    const uint32_t b = u4c(B[n], j);
-                    int dd[4];
-                    mma_u8s8_16816(dd, a0, a1, b, 0, 0, 0, 0);
-                    mma_s8s8_16816(dd, NEG32, NEG32, b, dd[0], dd[1], dd[2], dd[3]);
-                    acc[n][0] += scg * dd[0];
-                    acc[n][1] += scg * dd[1];
-                    acc[n][2] += scg8 * dd[2];
-                    acc[n][3] += scg8 * dd[3];
-                }
-            }
-#pragma unroll
-            for (int n = 0; n < NT; n++)
-                if (2 * h + qd < 3) Bq[n] = Bn[n];
-        }
-    }
-}
-
-template <int NT>
-__device__ __forceinline__ void q6k_warp_rows(const uint8_t *__restrict__ W, int rows, int nb, int row_g,
-                                              const int8_t *const (&opb)[NT], float (&accf)[NT][4], int t,
-                                              int lane, uint4 *wsm) {
-    const int nbp = q6r_nb_pad(nb);
-    const uint8_t *qpl = W, *spl = W + q6r_plane_s_off(rows, nb);
-    const uint16_t *dpl = reinterpret_cast<const uint16_t *>(W + q6r_plane_d_off(rows, nb));
-#pragma unroll
-    for (int s = 0; s < MOE_STAGES - 1; s++) {
-        if (s < nb) q6_issue(wsm, s, lane, qpl, spl, nb, row_g, s, t);
-        cp_async_commit();
-    }
-    // d of the first 8 super-blocks of both rows in one 16-byte load each
-    const uint4 dv = __ldg(reinterpret_cast<const uint4 *>(dpl + (size_t)row_g * nbp));
-    const uint4 dv8 = __ldg(reinterpret_cast<const uint4 *>(dpl + (size_t)(row_g + 8) * nbp));
-    int slot = 0, nslot = MOE_STAGES - 1;
-#pragma unroll 1
-    for (int sb = 0; sb < nb; ++sb) {
-        if (sb + MOE_STAGES - 1 < nb) q6_issue(wsm, nslot, lane, qpl, spl, nb, row_g, sb + MOE_STAGES - 1, t);
-        cp_async_commit();
-        float dg, dg8;
-        if (sb < 8) {
-            const uint32_t w = u4c(dv, sb >> 1), w8 = u4c(dv8, sb >> 1);
-            dg = h2f_bits((uint16_t)((sb & 1) ? (w >> 16) : (w & 0xFFFFu)));
-            dg8 = h2f_bits((uint16_t)((sb & 1) ? (w8 >> 16) : (w8 & 0xFFFFu)));
-        } else {
-            dg = h2f_bits(__ldg(dpl + (size_t)row_g * nbp + sb));
-            dg8 = h2f_bits(__ldg(dpl + (size_t)(row_g + 8) * nbp + sb));
-        }
-        cp_async_wait<MOE_STAGES - 1>();
-        Q6Raw R;
-        q6_read(R, wsm, slot, lane);
-        int acc[NT][4];
-#pragma unroll
-        for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0;
-        q6i_compute<NT>(R, sb, opb, acc);
-#pragma unroll
-        for (int n = 0; n < NT; n++) {
-            accf[n][0] = fmaf(dg, (float)acc[n][0], accf[n][0]);
-            accf[n][1] = fmaf(dg, (float)acc[n][1], accf[n][1]);
-            accf[n][2] = fmaf(dg8, (float)acc[n][2], accf[n][2]);
-            accf[n][3] = fmaf(dg8, (float)acc[n][3], accf[n][3]);
-        }
-        slot = (slot + 1 == MOE_STAGES) ? 0 : slot + 1;
-        nslot = (nslot + 1 == MOE_STAGES) ? 0 : nslot + 1;
-    }
-    cp_async_wait<0>();
-}
-
-__device__ __forceinline__ int expert_slot(const MoeLayerDev &L, int E, int e) {
-    return e == E ? L.n_local : e - L.e0;
-}
-
-// ===========================================================================
-// gate/up: CTA item = (chunk, 64 rows); warp w: row tile w&3, K half w>>2.
-// act[pair][row] = silu(gate) * up  (infer.m:378-383)
-// ===========================================================================
-template <int NT>
-__device__ __forceinline__ void gateup_item(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan,
-                                            const __half *__restrict__ xop, const __half *__restrict__ zop, int e,
-                                            int p0, int ntok, int rgi, int rt, int kh, int g, int t, int lane,
-                                            uint4 *wsm, float (*red)[2][MOE_ROWS_GU][MOE_TC + 1]) {
-    const int NB = d.H / MOE_QK, nbh = NB / 2;
-    const int sb0 = kh ? nbh : 0, sb1 = kh ? NB : nbh;
-    const size_t rowb = (size_t)NB * MOE_Q4K_BYTES;
-    const size_t opstride = q4op_halves(d.H);
-    const uint8_t *ex = L.experts + (size_t)expert_slot(L, d.E, e) * L.expert_stride;
-    const int r0 = rgi * MOE_ROWS_GU + rt * 16;
-    const int lane_off = (g & 1) * 4 * Q4OP_LANE_HALVES + t * Q4OP_LANE_HALVES;
-    const __half *opb[NT];
-#pragma unroll
-    for (int n = 0; n < NT; n++) {
-        const int tk = 4 * n + (g >> 1);
-        opb[n] = (tk < ntok ? xop + (size_t)plan.pair_token[p0 + tk] * opstride : zop) + lane_off;
-    }
-#pragma unroll 1
-    for (int mat = 0; mat < 2; mat++) {
-        const uint8_t *Wm = ex + (size_t)mat * L.gate_bytes;
-        float acc[NT][2];
-#pragma unroll
-        for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = 0.0f;
-        q4k_warp_rows<NT>(Wm + (size_t)(r0 + g) * rowb, Wm + (size_t)(r0 + g + 8) * rowb, sb0, sb1, opb, acc, t,
-                          lane, wsm);
-#pragma unroll
-        for (int n = 0; n < NT; n++) {
-            red[kh][mat][rt * 16 + g][4 * n + t] = acc[n][0];
-            red[kh][mat][rt * 16 + g + 8][4 * n + t] = acc[n][1];
-        }
-    }
-}
-
-__global__ void __launch_bounds__(256, 2) k_gateup(MoeDims d, MoeLayerDev L, MoePlan plan,
-                                                   const __half *__restrict__ xop, const __half *__restrict__ zop,
-                                                   const float *__restrict__ x_inv, float *__restrict__ act) {
-    __shared__ float red[2][2][MOE_ROWS_GU][MOE_TC + 1];
-    extern __shared__ uint4 ring[];  // [8 warps][MOE_STAGES][6][32]
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    uint4 *wsm = ring + (size_t)warp * MOE_STAGES * MOE_Q4_WORDS * 32;
-    const int rt = warp & 3, kh = warp >> 2;
-    const int n_chunks = plan.counts[1];
-    const int n_rg = d.I / MOE_ROWS_GU;
-    const int n_items = n_chunks * n_rg;
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
-        const int rgi = item / n_chunks, c = item % n_chunks;
-        const int e = plan.chunk_expert[c], p0 = plan.chunk_pair0[c], ntok = plan.chunk_ntok[c];
-        if (ntok <= 4) gateup_item<1>(d, L, plan, xop, zop, e, p0, ntok, rgi, rt, kh, g, t, lane, wsm, red);
-        else gateup_item<2>(d, L, plan, xop, zop, e, p0, ntok, rgi, rt, kh, g, t, lane, wsm, red);
-        __syncthreads();
-        for (int i = threadIdx.x; i < MOE_ROWS_GU * ntok; i += blockDim.x) {
-            const int row = i / ntok, tk = i % ntok;
-            const int pair = p0 + tk;
-            const float inv = x_inv[plan.pair_token[pair]];
-            const float gv = (red[0][0][row][tk] + red[1][0][row][tk]) * inv;
-            const float uv = (red[0][1][row][tk] + red[1][1][row][tk]) * inv;
-            act[(size_t)pair * d.I + rgi * MOE_ROWS_GU + row] = (gv / (1.0f + expf(-gv))) * uv;
-        }
-        __syncthreads();
-    }
-}
-
-void moe_launch_gateup(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const __half *xop,
-                       const __half *zop, const float *x_inv, float *act, int max_items, cudaStream_t s,
-                       uint64_t *launches) {
-    int grid = num_sms() * 2;
-    if (grid > max_items) grid = max_items;
-    if (grid < 1) grid = 1;
-    const size_t smem = sizeof(uint4) * 8 * MOE_STAGES * MOE_Q4_WORDS * 32;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(k_gateup, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr = true;
-    }
-    k_gateup<<<grid, 256, smem, s>>>(d, L, plan, xop, zop, x_inv, act);
-    LAUNCH_COUNT(launches);
-}
-
-// ===========================================================================
 // down operand: per pair, scale + operand of the expert's down type
 // ===========================================================================
 __global__ void __launch_bounds__(256) k_prep_down(MoeDims d, MoeLayerDev L, MoePlan plan,
                                                    const float *__restrict__ act, uint8_t *__restrict__ dop,
                                                    float *__restrict__ d_inv) {
     __shared__ float red[32];
-    __shared__ float xsum[1024];
     const int n_pairs = plan.counts[0];
-    const size_t opst = dop_bytes(d.I);
+    const size_t opst = op_bytes(d.I);
     extern __shared__ float arow[];  // [I]
     for (int p = blockIdx.x; p < n_pairs; p += gridDim.x) {
         stage_row(act + (size_t)p * d.I, d.I, arow);
@@ -1234,13 +828,8 @@ __global__ void __launch_bounds__(256) k_prep_down(MoeDims d, MoeLayerDev L, Moe
         const int e = plan.pair_expert[p];
         const int ty = (e == d.E) ? L.sh_down_type : L.down_type;
         float inv;
-        if (ty == 14) {
-            const float s = op_scale(amax, &inv, 20);
-            build_q6i(a, d.I, s, reinterpret_cast<int8_t *>(dop + (size_t)p * opst));
-        } else {
-            const float s = op_scale(amax, &inv);
-            build_q4op(a, d.I, s, reinterpret_cast<__half *>(dop + (size_t)p * opst), xsum);
-        }
+        const float s = op_scale(amax, &inv, 20);
+        build_op(a, d.I, s, dop + (size_t)p * opst, ty == 14 ? 6 : 4);
         if (threadIdx.x == 0) d_inv[p] = inv;
         __syncthreads();
     }
@@ -1250,9 +839,8 @@ __global__ void __launch_bounds__(256) k_prep_down(MoeDims d, MoeLayerDev L, Moe
 // their metadata says the slot is empty), rows [R, R + T) from `local`.
 __global__ void __launch_bounds__(256) k_prep_rows(const float *__restrict__ recv, const int *__restrict__ meta,
                                                    int meta_w, int R, const float *__restrict__ local, int H,
-                                                   __half *__restrict__ xop, float *__restrict__ x_inv) {
+                                                   uint8_t *__restrict__ xop, float *__restrict__ x_inv) {
     __shared__ float red[32];
-    __shared__ float xsum[1024];
     const int r = blockIdx.x;
     if (r < R && !meta[(size_t)r * meta_w]) return;
     extern __shared__ float xrow[];  // [H]
@@ -1260,13 +848,13 @@ __global__ void __launch_bounds__(256) k_prep_rows(const float *__restrict__ rec
     const float *x = xrow;
     const float amax = block_max_abs(x, H, red);
     float inv;
-    const float s = op_scale(amax, &inv);
-    build_q4op(x, H, s, xop + (size_t)r * q4op_halves(H), xsum);
+    const float s = op_scale(amax, &inv, 20);
+    build_op(x, H, s, xop + (size_t)r * op_bytes(H), 4);
     if (threadIdx.x == 0) x_inv[r] = inv;
 }
 
 void moe_launch_prep_rows(const float *recv, const int *meta, int meta_w, int R, const float *local, int T, int H,
-                          __half *xop, float *x_inv, cudaStream_t s, uint64_t *launches) {
+                          uint8_t *xop, float *x_inv, cudaStream_t s, uint64_t *launches) {
     const size_t smem = sizeof(float) * (size_t)H;
     static size_t attr = 0;
     if (smem > attr) {
@@ -1290,147 +878,6 @@ void moe_launch_prep_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan 
     }
     k_prep_down<<<grid, 256, smem, s>>>(d, L, plan, act, dop, d_inv);
     LAUNCH_COUNT(launches);
-}
-
-// ===========================================================================
-// down: warp task = (chunk, 16 rows of H); eo[pair][row]
-// ===========================================================================
-// Q6_K: n-tile n holds vectors 2n, 2n+1, three planes each (columns 0-2,
-// 3-5; columns 6, 7 empty).  NT = ceil(ntok / 2).
-template <int NT>
-__device__ __forceinline__ void down_task_q6(const MoeDims &d, const MoeLayerDev &L, const uint8_t *__restrict__ dop,
-                                             const uint8_t *__restrict__ zop, const float *__restrict__ d_inv,
-                                             float *__restrict__ eo, int e, int p0, int ntok, int rt, int g, int t,
-                                             int lane, uint4 *wsm) {
-    const int NB = d.I / MOE_QK;
-    const size_t opst = dop_bytes(d.I);
-    const uint8_t *Wd = L.experts + (size_t)expert_slot(L, d.E, e) * L.expert_stride + 2 * L.gate_bytes;
-    const int r0 = rt * 16;
-    const int8_t *opb[NT];
-#pragma unroll
-    for (int n = 0; n < NT; n++) {
-        const int tk = 2 * n + (g >= 3 ? 1 : 0), plane = g % 3;
-        const bool ok = g < 6 && tk < ntok;
-        const uint8_t *base = ok ? dop + (size_t)(p0 + tk) * opst : zop;
-        opb[n] = reinterpret_cast<const int8_t *>(base + (size_t)(ok ? plane : 0) * NB * Q6I_BYTES_PER_SB + t * 64);
-    }
-    float accf[NT][4];
-#pragma unroll
-    for (int n = 0; n < NT; n++) accf[n][0] = accf[n][1] = accf[n][2] = accf[n][3] = 0.0f;
-    q6k_warp_rows<NT>(Wd, d.H, NB, r0 + g, opb, accf, t, lane, wsm);
-    // combine the planes: column c of tile n = vector 2n + c/3, plane c%3
-#pragma unroll
-    for (int n = 0; n < NT; n++) {
-        float va[2], vb[2];
-#pragma unroll
-        for (int h = 0; h < 2; h++) {  // rows g (h=0) and g+8 (h=1)
-            const float c0 = accf[n][2 * h], c1 = accf[n][2 * h + 1];
-            va[h] = t == 0 ? c0 + 128.0f * c1 : (t == 1 ? 16384.0f * c0 : 0.0f);
-            vb[h] = t == 1 ? c1 : (t == 2 ? 128.0f * c0 + 16384.0f * c1 : 0.0f);
-#pragma unroll
-            for (int o = 1; o < 4; o <<= 1) {
-                va[h] += __shfl_xor_sync(0xffffffffu, va[h], o);
-                vb[h] += __shfl_xor_sync(0xffffffffu, vb[h], o);
-            }
-        }
-        if (t < 2) {
-            const int tk = 2 * n + t;
-            if (tk < ntok) {
-                const int pair = p0 + tk;
-                const float inv = d_inv[pair];
-                eo[(size_t)pair * d.H + r0 + g] = (t == 0 ? va[0] : vb[0]) * inv;
-                eo[(size_t)pair * d.H + r0 + g + 8] = (t == 0 ? va[1] : vb[1]) * inv;
-            }
-        }
-    }
-}
-
-template <int NT>
-__device__ __forceinline__ void down_task_q4(const MoeDims &d, const MoeLayerDev &L, const uint8_t *__restrict__ dop,
-                                             const uint8_t *__restrict__ zop, const float *__restrict__ d_inv,
-                                             float *__restrict__ eo, int e, int p0, int ntok, int rt, int g, int t,
-                                             int lane, uint4 *wsm) {
-    const int NB = d.I / MOE_QK;
-    const size_t opst = dop_bytes(d.I);
-    const uint8_t *Wd = L.experts + (size_t)expert_slot(L, d.E, e) * L.expert_stride + 2 * L.gate_bytes;
-    const int r0 = rt * 16;
-    const int lane_off = (g & 1) * 4 * Q4OP_LANE_HALVES + t * Q4OP_LANE_HALVES;
-    const __half *opb[NT];
-#pragma unroll
-    for (int n = 0; n < NT; n++) {
-        const int tb = 4 * n + (g >> 1);
-        opb[n] = reinterpret_cast<const __half *>(tb < ntok ? dop + (size_t)(p0 + tb) * opst : zop) + lane_off;
-    }
-    float acc[NT][2];
-#pragma unroll
-    for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = 0.0f;
-    const size_t rowb = (size_t)NB * MOE_Q4K_BYTES;
-    q4k_warp_rows<NT>(Wd + (size_t)(r0 + g) * rowb, Wd + (size_t)(r0 + g + 8) * rowb, 0, NB, opb, acc, t, lane, wsm);
-#pragma unroll
-    for (int n = 0; n < NT; n++) {
-        const int tc = 4 * n + t;
-        if (tc >= ntok) continue;
-        const int pair = p0 + tc;
-        const float inv = d_inv[pair];
-        eo[(size_t)pair * d.H + r0 + g] = acc[n][0] * inv;
-        eo[(size_t)pair * d.H + r0 + g + 8] = acc[n][1] * inv;
-    }
-}
-
-// One instance per down type; chunks of the other type are skipped.
-template <int TY>
-__global__ void __launch_bounds__(256, 2) k_down(MoeDims d, MoeLayerDev L, MoePlan plan,
-                                                 const uint8_t *__restrict__ dop, const uint8_t *__restrict__ zop,
-                                                 const float *__restrict__ d_inv, float *__restrict__ eo) {
-    extern __shared__ uint4 ring[];  // [8 warps][MOE_STAGES][words][32]
-    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-    uint4 *wsm = ring + (size_t)(threadIdx.x >> 5) * MOE_STAGES * (TY == 14 ? MOE_Q6_WORDS : MOE_Q4_WORDS) * 32;
-    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int nw = gridDim.x * (blockDim.x >> 5);
-    const int n_chunks = plan.counts[1];
-    const int n_tasks = n_chunks * (d.H / 16);
-    for (int task = gw; task < n_tasks; task += nw) {
-        const int rt = task / n_chunks, c = task % n_chunks;
-        const int e = plan.chunk_expert[c], p0 = plan.chunk_pair0[c], ntok = plan.chunk_ntok[c];
-        if (((e == d.E) ? L.sh_down_type : L.down_type) != TY) continue;
-        if (TY == 14) {
-            // at most 4 vectors per pass (two 8-column tiles); a chunk of more
-            // runs a second pass over the same rows (weights then come from L2)
-            for (int q0 = 0; q0 < ntok; q0 += 4) {
-                const int nq = min(4, ntok - q0);
-                if (nq <= 2) down_task_q6<1>(d, L, dop, zop, d_inv, eo, e, p0 + q0, nq, rt, g, t, lane, wsm);
-                else down_task_q6<2>(d, L, dop, zop, d_inv, eo, e, p0 + q0, nq, rt, g, t, lane, wsm);
-            }
-        } else {
-            if (ntok <= 4) down_task_q4<1>(d, L, dop, zop, d_inv, eo, e, p0, ntok, rt, g, t, lane, wsm);
-            else down_task_q4<2>(d, L, dop, zop, d_inv, eo, e, p0, ntok, rt, g, t, lane, wsm);
-        }
-    }
-}
-
-void moe_launch_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const uint8_t *dop,
-                     const uint8_t *zop, const float *d_inv, float *eo, int max_items, cudaStream_t s,
-                     uint64_t *launches) {
-    int grid = num_sms() * 2;
-    const int need = (max_items + 7) / 8;
-    if (grid > need) grid = need;
-    if (grid < 1) grid = 1;
-    const size_t sm6 = sizeof(uint4) * 8 * MOE_STAGES * MOE_Q6_WORDS * 32;
-    const size_t sm4 = sizeof(uint4) * 8 * MOE_STAGES * MOE_Q4_WORDS * 32;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(k_down<14>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm6);
-        cudaFuncSetAttribute(k_down<12>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm4);
-        attr = true;
-    }
-    if (L.down_type == 14 || L.sh_down_type == 14) {
-        k_down<14><<<grid, 256, sm6, s>>>(d, L, plan, dop, zop, d_inv, eo);
-        LAUNCH_COUNT(launches);
-    }
-    if (L.down_type == 12 || L.sh_down_type == 12) {
-        k_down<12><<<grid, 256, sm4, s>>>(d, L, plan, dop, zop, d_inv, eo);
-        LAUNCH_COUNT(launches);
-    }
 }
 
 // ===========================================================================

@@ -1,6 +1,9 @@
-"""CPU: the weight-byte -> MMA-slot maps and the lossless Q6_K repack used by
-the CUDA kernels (moe_common.cuh) are bijections that match the GGUF block
-layouts of quant.c, checked on a host build of the same header."""
+"""CPU: the operand and repack maps of moe_common.cuh, and a lane-by-lane
+emulation of the tensor-core arithmetic of the expert kernels
+(moe_experts.cu: q4_stage, q6_stage, planes_to_vector) against the
+quant.c dequantization, so that a fragment-layout or decode error shows up
+without a GPU.  The maps come from a host build of the same header; the MMA
+fragment layouts are those of the PTX ISA for mma.m16n8k32 / m16n8k16."""
 import os
 import subprocess
 import tempfile
@@ -23,9 +26,7 @@ def tables():
         if not line:
             continue
         f = line.split()
-        if f[0] in ("q4k", "q6k"):
-            t[f[0]][tuple(map(int, f[1:4]))] = int(f[4])
-        elif f[0] in ("q4min", "q6r"):
+        if f[0] in ("opq4", "opq6", "xsum", "q4r", "q6r"):
             t[f[0]][int(f[1])] = int(f[2])
         elif f[0] == "sizes":
             t["sizes"] = tuple(map(int, f[1:]))
@@ -36,49 +37,47 @@ def tables():
     return t
 
 
-def test_q4k_map_is_bijection(tables):
-    ks = sorted(tables["q4k"].values())
-    assert ks == list(range(256))
+# ------------------------------------------------------------------ maps
+def test_operand_maps_are_bijections(tables):
+    assert sorted(tables["opq4"].values()) == list(range(256))
+    assert sorted(tables["opq6"].values()) == list(range(256))
+    xs = sorted(tables["xsum"].values())
+    assert xs == [256 + 2 * i for i in range(16)]
+    H, ob, op2, sb, plane = 7168, *tables["sizes"][1:]
+    assert (sb, plane) == (960, 320) and ob == 28 * 960 and op2 == 8 * 960
+    assert plane % 128 == 64  # plane blocks 80 words apart: quarter-warp loads hit distinct banks
 
 
-def test_q4k_map_matches_nibble_layout(tables):
-    # lane t of MMA step m reads qs bytes [64r+16t, +16), word i = (m/2)%4;
-    # slots (0,1) = bytes (0,2) of the word, (2,3) = bytes (1,3); m odd = high
-    # nibble.  quant.c:49-58: low nibble of qs byte b (chunk c = b/32) is
-    # weight 64c + b%32, the high nibble weight 64c + 32 + b%32.
-    for (m, t, j), k in tables["q4k"].items():
-        r, i, hi = m // 8, (m // 2) % 4, m % 2
-        byte = 64 * r + 16 * t + 4 * i + [0, 2, 1, 3][j]
-        c, l = byte // 32, byte % 32
-        assert k == 64 * c + 32 * hi + l
+def test_q4_operand_matches_weight_lanes(tables):
+    # weight side: lane t holds repacked qs chunk j = old bytes 32j + 8t + i;
+    # low nibble -> weight 32(2j) + 8t + i, high -> 32(2j+1) + 8t + i (quant.c:49-58).
+    # operand side: lane t's 16-byte load j = [8 B of sub-block 2j][8 B of 2j+1].
+    for j in range(4):
+        for t in range(4):
+            for i in range(8):
+                for h in range(2):
+                    k = 32 * (2 * j + h) + 8 * t + i
+                    assert tables["opq4"][k] == 64 * j + 16 * t + 8 * h + i
 
 
-def test_q4k_min_subblocks(tables):
-    # the four lanes supply the 8 min slots once each
-    subs = sorted(s + u for s in tables["q4min"].values() for u in (0, 1))
-    assert subs == list(range(8))
-    # and lane t owns the scales of those sub-blocks (its nibbles live there)
-    for t, s in tables["q4min"].items():
-        own = {tables["q4k"][(m, t, 0)] // 32 for m in range(16)}
-        assert {s, s + 1} <= own
+def test_q4_repack_is_transpose(tables):
+    src = tables["q4r"]
+    assert sorted(src.values()) == list(range(128))
+    for p, s in src.items():
+        assert src[s] == p  # its own inverse
+        c, i = p // 8, p % 8
+        t, j = c // 4, c % 4
+        assert s == 32 * j + 8 * t + i
 
 
-def test_q6k_map(tables):
-    ks = sorted(tables["q6k"].values())
-    assert ks == list(range(256))
-    for (s, t, j), k in tables["q6k"].items():
-        assert k // 16 == s  # one MMA step = one 16-weight sub-block
-
-
-def test_q6_repack_is_permutation(tables):
+def test_q6_operand_and_repack(tables):
+    for s in range(16):
+        for t in range(4):
+            for i in range(4):
+                assert tables["opq6"][16 * s + 4 * t + i] == 64 * (s // 4) + 16 * t + 4 * (s % 4) + i
     src = sorted(tables["q6r"].values())
-    assert src == list(range(192))  # every ql/qh byte exactly once
-    n = tables["sizes"]
-    assert n[0] == 7168 * 8 * 210   # repacked matrix has the GGUF size
-
-
-def test_q6_repack_lane_bytes(tables):
-    # lane t of block half h reads ql bytes 4t+16w (w<4) and qh bytes 4t+16w'
+    assert src == list(range(192))
+    assert tables["sizes"][0] == 7168 * 8 * 210   # repacked matrix has the GGUF size
     for p, sb in tables["q6r"].items():
         t, rem = p // 48, p % 48
         h, w, b = rem // 24, (rem % 24) // 4, rem % 4
@@ -95,3 +94,216 @@ def test_f2h_matches_numpy(tables):
 
 def test_splitmix_matches_oracle(tables, oracle):
     assert tables["split"] == oracle.lib().or_splitmix64(12345)
+
+
+# ------------------------------------------------------- MMA emulation
+def w32(buf, off):
+    return int.from_bytes(bytes(buf[off:off + 4]), "little")
+
+
+def bytes_of(w, signed):
+    b = [(w >> (8 * i)) & 0xFF for i in range(4)]
+    return [x - 256 if signed and x > 127 else x for x in b]
+
+
+def halves_of(w):
+    return list(np.array([w & 0xFFFF, w >> 16], np.uint16).view(np.float16).astype(np.float64))
+
+
+def mma(a, b, k, kind):
+    """a[lane] = A registers, b[lane] = B registers of one warp; returns
+    d[lane] = (D[g][2t], D[g][2t+1], D[g+8][2t], D[g+8][2t+1])."""
+    A = np.zeros((16, k))
+    B = np.zeros((k, 8))
+    for lane in range(32):
+        g, t = lane >> 2, lane & 3
+        if kind == "k32":      # u8 x s8, m16n8k32
+            for r, (row, k0) in enumerate([(g, 4 * t), (g + 8, 4 * t), (g, 16 + 4 * t), (g + 8, 16 + 4 * t)]):
+                A[row, k0:k0 + 4] = bytes_of(a[lane][r], False)
+            B[4 * t:4 * t + 4, g] = bytes_of(b[lane][0], True)
+            B[16 + 4 * t:20 + 4 * t, g] = bytes_of(b[lane][1], True)
+        elif kind == "k16s8":  # s8 x s8, m16n8k16
+            A[g, 4 * t:4 * t + 4] = bytes_of(a[lane][0], True)
+            A[g + 8, 4 * t:4 * t + 4] = bytes_of(a[lane][1], True)
+            B[4 * t:4 * t + 4, g] = bytes_of(b[lane][0], True)
+        else:                  # f16 m16n8k16
+            for r, (row, k0) in enumerate([(g, 2 * t), (g + 8, 2 * t), (g, 2 * t + 8), (g + 8, 2 * t + 8)]):
+                A[row, k0:k0 + 2] = halves_of(a[lane][r])
+            B[2 * t:2 * t + 2, g] = halves_of(b[lane][0])
+            B[2 * t + 8:2 * t + 10, g] = halves_of(b[lane][1])
+    D = A @ B
+    return [(D[l >> 2, 2 * (l & 3)], D[l >> 2, 2 * (l & 3) + 1], D[(l >> 2) + 8, 2 * (l & 3)],
+             D[(l >> 2) + 8, 2 * (l & 3) + 1]) for l in range(32)]
+
+
+def build_operand(tables, x, style):
+    """Operand bytes of one super-block of each vector, as build_op writes them."""
+    s = 2.0 ** (20 - np.frexp(np.max(np.abs(x)))[1])
+    v = np.rint(x.astype(np.float64) * s).astype(np.int64)
+    ops = []
+    for vec in v:
+        op = np.zeros(960, np.uint8)
+        planes = [vec & 127, (vec >> 7) & 127, (vec >> 14) & 255]
+        for p in range(3):
+            for k in range(256):
+                off = tables["opq4" if style == 4 else "opq6"][k]
+                op[320 * p + off] = planes[p][k]
+            if style == 4:
+                pv = [vec & 127, (vec >> 7) & 127, vec >> 14][p]
+                for jj in range(16):
+                    h = np.float16(int(pv[16 * jj:16 * jj + 16].sum()))
+                    op[320 * p + tables["xsum"][jj]:320 * p + tables["xsum"][jj] + 2] = \
+                        np.frombuffer(h.tobytes(), np.uint8)
+        ops.append(op)
+    return np.concatenate(ops), v, 1.0 / s
+
+
+def planes_to_vector(c0, c1, t_list):
+    """planes_to_vector over a quad: c0[t], c1[t] for t = 0..3 -> (vector 2n, 2n+1)."""
+    va = [c0[0] + 128 * c1[0], 16384 * c0[1], 0, 0]
+    vb = [0, c1[1], 128 * c0[2] + 16384 * c1[2], 0]
+    return sum(va), sum(vb)
+
+
+def header_words(block):
+    """q4_stage's word-level unpack of the 12 scale bytes (4 values per word)."""
+    y, z, w = w32(block, 4), w32(block, 8), w32(block, 12)
+    sc_lo, sc_hi = y & 0x3F3F3F3F, (w & 0x0F0F0F0F) | ((y >> 2) & 0x30303030)
+    mn_lo, mn_hi = z & 0x3F3F3F3F, ((w >> 4) & 0x0F0F0F0F) | ((z >> 2) & 0x30303030)
+    return sc_lo, sc_hi, mn_lo, mn_hi
+
+
+def sc_pair(block, j):
+    """(16 sc of sub-block 2j, sc of sub-block 2j + 1) as q4_stage extracts them."""
+    sc_lo, sc_hi = header_words(block)[:2]
+    sw, bl = (sc_lo if j < 2 else sc_hi), 2 * (j & 1)
+    return ((sw >> (8 * bl)) & 0x3F) << 4, (sw >> (8 * bl + 8)) & 0x3F
+
+
+def mins_words(block):
+    mn_lo, mn_hi = header_words(block)[2:]
+    return [(mn_lo >> (8 * s)) & 0xFF for s in range(4)] + [(mn_hi >> (8 * s)) & 0xFF for s in range(4)]
+
+
+def test_q4_header_unpack_matches_quant_c():
+    # get_scale_min_k4 (quant.c:26-34) on random scale bytes
+    rng = np.random.default_rng(3)
+    for _ in range(200):
+        blk = rng.integers(0, 256, 144, dtype=np.uint8)
+        q = blk[4:16].astype(int)
+        sc = [(q[s] & 63) if s < 4 else ((q[s + 4] & 0xF) | ((q[s - 4] >> 6) << 4)) for s in range(8)]
+        mn = [(q[s + 4] & 63) if s < 4 else ((q[s + 4] >> 4) | ((q[s] >> 6) << 4)) for s in range(8)]
+        for j in range(4):
+            assert sc_pair(blk, j) == (16 * sc[2 * j], sc[2 * j + 1])
+        assert mins_words(blk) == mn
+
+
+def test_q4_stage_emulation(tables, oracle):
+    rng = np.random.default_rng(7)
+    W = (rng.standard_normal((16, 256)) * 0.02).astype(np.float32)
+    blocks = oracle.quantize(W.reshape(-1), oracle.TYPE_Q4_K).reshape(16, 144)
+    wdq = oracle.dequant(blocks.reshape(-1), oracle.TYPE_Q4_K, 16 * 256).reshape(16, 256).astype(np.float64)
+    rep = blocks.copy()
+    for p, sidx in tables["q4r"].items():
+        rep[:, 16 + p] = blocks[:, 16 + sidx]
+    x = rng.standard_normal((2, 256)).astype(np.float32)
+    opnd, v, inv = build_operand(tables, x, 4)
+    acc = [[0, 0, 0, 0] for _ in range(32)]
+    a_l, a_h, b_l, b_h = {}, {}, {}, {}
+    for j in range(4):
+        for lane in range(32):
+            g, t = lane >> 2, lane & 3
+            wg = [w32(rep[g], 16 + 32 * t + 8 * j), w32(rep[g], 20 + 32 * t + 8 * j)]
+            w8 = [w32(rep[g + 8], 16 + 32 * t + 8 * j), w32(rep[g + 8], 20 + 32 * t + 8 * j)]
+            a_l[lane] = [wg[0] & 0x0F0F0F0F, w8[0] & 0x0F0F0F0F, wg[1] & 0x0F0F0F0F, w8[1] & 0x0F0F0F0F]
+            a_h[lane] = [wg[0] & 0xF0F0F0F0, w8[0] & 0xF0F0F0F0, wg[1] & 0xF0F0F0F0, w8[1] & 0xF0F0F0F0]
+            tsel, plane = (1 if g >= 3 else 0), g % 3
+            ok = g < 6 and tsel < 2
+            base = tsel * 960 + plane * 320 + 16 * t + 64 * j
+            wv = [w32(opnd, base + 4 * q) if ok else 0 for q in range(4)]
+            b_l[lane], b_h[lane] = wv[0:2], wv[2:4]
+        dl, dh = mma(a_l, b_l, 32, "k32"), mma(a_h, b_h, 32, "k32")
+        for lane in range(32):
+            g = lane >> 2
+            slg, shg = sc_pair(rep[g], j)
+            sl8, sh8 = sc_pair(rep[g + 8], j)
+            acc[lane][0] += slg * dl[lane][0] + shg * dh[lane][0]
+            acc[lane][1] += slg * dl[lane][1] + shg * dh[lane][1]
+            acc[lane][2] += sl8 * dl[lane][2] + sh8 * dh[lane][2]
+            acc[lane][3] += sl8 * dl[lane][3] + sh8 * dh[lane][3]
+    assert max(abs(a) for l in acc for a in l) < 2 ** 31
+    am, bm = {}, {}
+    for lane in range(32):
+        g, t = lane >> 2, lane & 3
+
+        mg, m8 = mins_words(rep[g]), mins_words(rep[g + 8])
+        h2 = lambda m: int(np.array([m, m], np.float16).view(np.uint32)[0])
+        am[lane] = [h2(mg[t]), h2(m8[t]), h2(mg[t + 4]), h2(m8[t + 4])]
+        tsel, plane = (1 if g >= 3 else 0), g % 3
+        base = tsel * 960 + plane * 320 + 256 + 8 * t
+        bm[lane] = [w32(opnd, base), w32(opnd, base + 4)] if g < 6 else [0, 0]
+    mt = mma(am, bm, 16, "f16")
+    out = np.zeros((16, 2))
+    for lane in range(32):
+        g, t = lane >> 2, lane & 3
+        hg, h8 = rep[g][:4].view(np.float16).astype(np.float64), rep[g + 8][:4].view(np.float16).astype(np.float64)
+        lane_f = [hg[0] / 16 * acc[lane][0] - hg[1] * mt[lane][0], hg[0] / 16 * acc[lane][1] - hg[1] * mt[lane][1],
+                  h8[0] / 16 * acc[lane][2] - h8[1] * mt[lane][2], h8[0] / 16 * acc[lane][3] - h8[1] * mt[lane][3]]
+        acc[lane] = lane_f
+    for g in range(8):
+        quad = [acc[4 * g + t] for t in range(4)]
+        for half, row in ((0, g), (2, g + 8)):
+            va, vb = planes_to_vector([q[half] for q in quad], [q[half + 1] for q in quad], None)
+            out[row] = (va, vb)
+    ref = np.stack([wdq @ v[0].astype(np.float64), wdq @ v[1].astype(np.float64)], axis=1)
+    err = np.max(np.abs(out - ref)) / np.max(np.abs(ref))
+    assert err < 1e-12, err
+
+
+def test_q6_stage_emulation(tables, oracle):
+    rng = np.random.default_rng(8)
+    W = (rng.standard_normal((16, 256)) * 0.02).astype(np.float32)
+    blocks = oracle.quantize(W.reshape(-1), oracle.TYPE_Q6_K).reshape(16, 210)
+    wdq = oracle.dequant(blocks.reshape(-1), oracle.TYPE_Q6_K, 16 * 256).reshape(16, 256).astype(np.float64)
+    Q = np.zeros((16, 192), np.uint8)
+    for p, sidx in tables["q6r"].items():
+        Q[:, p] = blocks[:, sidx] ^ (0xAA if sidx >= 128 else 0)
+    S = blocks[:, 192:208].view(np.int8)
+    D = blocks[:, 208:210].copy().view(np.float16).astype(np.float64)[:, 0]
+    x = rng.standard_normal((2, 256)).astype(np.float32)
+    opnd, v, inv = build_operand(tables, x, 6)
+
+    def q6_a4(sp, W_, Hw):
+        nib = ((W_ << 2) & 0x3C3C3C3C) if sp < 4 else ((W_ >> 2) & 0x3C3C3C3C)
+        f = sp >> 1
+        hs = [(Hw << 6), (Hw << 4), (Hw << 2), Hw][f] & 0xFFFFFFFF
+        return (nib | (hs & 0xC0C0C0C0)) & 0xFFFFFFFF
+    acc = [[0, 0, 0, 0] for _ in range(32)]
+    for s in range(16):
+        h, sp = s // 8, s % 8
+        a, b = {}, {}
+        for lane in range(32):
+            g, t = lane >> 2, lane & 3
+            wg = [w32(Q[g], 48 * t + 24 * h + 4 * i) for i in range(6)]
+            w8 = [w32(Q[g + 8], 48 * t + 24 * h + 4 * i) for i in range(6)]
+            a[lane] = [q6_a4(sp, wg[sp & 3], wg[4 + (sp & 1)]), q6_a4(sp, w8[sp & 3], w8[4 + (sp & 1)])]
+            tsel, plane = (1 if g >= 3 else 0), g % 3
+            base = tsel * 960 + plane * 320 + 16 * t + 64 * (s // 4) + 4 * (s % 4)
+            b[lane] = [w32(opnd, base) if g < 6 else 0]
+        dd = mma(a, b, 16, "k16s8")
+        for lane in range(32):
+            g = lane >> 2
+            acc[lane][0] += int(S[g, s]) * dd[lane][0]
+            acc[lane][1] += int(S[g, s]) * dd[lane][1]
+            acc[lane][2] += int(S[g + 8, s]) * dd[lane][2]
+            acc[lane][3] += int(S[g + 8, s]) * dd[lane][3]
+    assert max(abs(a_) for l in acc for a_ in l) < 2 ** 31
+    out = np.zeros((16, 2))
+    for g in range(8):
+        quad = [acc[4 * g + t] for t in range(4)]
+        for half, row in ((0, g), (2, g + 8)):
+            va, vb = planes_to_vector([q[half] for q in quad], [q[half + 1] for q in quad], None)
+            out[row] = (D[row] * 0.25 * va, D[row] * 0.25 * vb)
+    ref = np.stack([wdq @ v[0].astype(np.float64), wdq @ v[1].astype(np.float64)], axis=1)
+    err = np.max(np.abs(out - ref)) / np.max(np.abs(ref))
+    assert err < 1e-12, err
