@@ -208,7 +208,6 @@ def run_ours(args):
     steps_total = args.warmup + args.steps
     idx_all = torch.empty(steps_total, max(1, b_loc), K, dtype=torch.int32, device=dev)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
-    moe.set_timing(args.steps)
 
     def barrier():
         torch.cuda.synchronize()
@@ -227,7 +226,11 @@ def run_ours(args):
     t_wait = time.time()
     while not clk.lines and time.time() - t_wait < 5.0:
         time.sleep(0.05)
-    # ---- device-resident leg (value)
+    # ---- device-resident leg (value).  The library replays each call
+    # signature as a CUDA graph from its second call on; two untimed passes
+    # over the input pool capture them before the warm-up proper.
+    for s in range(2 * n_pool):
+        moe.forward_device(0, pool[s % n_pool], b_loc, out)
     for s in range(args.warmup):
         with torch.cuda.stream(stream):
             flush.zero_()
@@ -244,12 +247,23 @@ def run_ours(args):
         moe.forward_device(0, pool[(args.warmup + s) % n_pool], b_loc, out, d_idx=idx_all[args.warmup + s])
         ev[s][1].record(stream)
     barrier()
-    phases = [moe.timing(back) for back in range(args.steps)]
     clk_lines_timed = clk.lines[n_clk0:]
     launches = moe.kernel_launches - launches0
     step_ms = [a.elapsed_time(b) for a, b in ev]
     total_ms = max_over_ranks(sum(step_ms))
     value = B * args.steps / (total_ms / 1e3)
+
+    # ---- per-kernel durations: a separate pass with CUDA events between the
+    # kernels (direct launches, no graph), same inputs and L2 flush
+    n_ph = min(args.steps, 50)
+    moe.set_timing(n_ph)
+    for s in range(n_ph):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+        moe.forward_device(0, pool[(args.warmup + s) % n_pool], b_loc, out)
+    barrier()
+    phases = [moe.timing(back) for back in range(n_ph)]
+    moe.set_timing(0)
 
     # ---- roofline of the dominant kernel (gate/up GEMV) on this rank: the
     # experts it holds that any token of the global batch routes to

@@ -9,6 +9,7 @@
 #include <string.h>
 
 #include <string>
+#include <array>
 #include <vector>
 
 #include "../../include/moe_cuda.h"
@@ -72,10 +73,9 @@ struct moe_ctx {
     int *idx = nullptr, *idx_given = nullptr;
     float *wts = nullptr, *w_given = nullptr, *bias_tmp = nullptr;
     uint8_t *xop = nullptr;   // int8-plane operand rows, op_bytes(H) each
-    float *x_inv = nullptr;
     MoePlan plan{};
     int *counter = nullptr;
-    float *act = nullptr, *d_inv = nullptr, *eo = nullptr;
+    float *act = nullptr, *eo = nullptr;
     uint8_t *dop = nullptr;   // down operand, op_bytes(I) per pair
     int *h_counts = nullptr;  // pinned [4]
     // expert-parallel buffers
@@ -89,6 +89,18 @@ struct moe_ctx {
     std::vector<cudaEvent_t> ev;                // [ring][MOE_N_PHASES + 1]
     std::vector<uint8_t> ev_valid;
     uint64_t launches = 0;
+    // replayable CUDA graphs of the 1-GPU forward, one per call signature
+    struct Graph {
+        int layer, T;
+        const void *h, *out, *idx, *w;
+        cudaStream_t s;
+        cudaGraphExec_t exec;
+        uint64_t kernels, last_use;
+    };
+    std::vector<Graph> graphs;
+    std::vector<std::array<const void *, 5>> seen;  // signatures run once eagerly (attributes set)
+    bool use_graphs = true;
+    uint64_t clock = 0;
     uint64_t last_bytes = 0;
     int last_layer = -1;
 };
@@ -138,6 +150,12 @@ int moe_get_unique_id(void *out) {
     return MOE_OK;
 }
 
+static void drop_graphs(moe_ctx *c) {
+    for (auto &g : c->graphs) cudaGraphExecDestroy(g.exec);
+    c->graphs.clear();
+    c->seen.clear();
+}
+
 static int ctx_alloc(moe_ctx *c) {
     const int T = c->max_tok, R = c->max_rows, H = c->d.H, I = c->d.I, E = c->d.E, K = c->d.K;
     c->max_pairs = R * K + T;
@@ -157,7 +175,6 @@ static int ctx_alloc(moe_ctx *c) {
     const int RT = (c->world > 1 ? R + T : R);  // EP: received rows + local rows
     CK(dmalloc(&c->xop, (size_t)RT * op_bytes(H)));
     CK(cudaMemset(c->xop, 0, (size_t)RT * op_bytes(H)));
-    CK(dmalloc(&c->x_inv, (size_t)RT));
     const int P = c->max_pairs;
     CK(dmalloc(&c->plan.counts, 4));
     CK(dmalloc(&c->plan.pair_expert, P));
@@ -175,7 +192,6 @@ static int ctx_alloc(moe_ctx *c) {
     CK(dmalloc(&c->act, (size_t)P * I));
     CK(dmalloc(&c->dop, (size_t)P * op_bytes(I)));
     CK(cudaMemset(c->dop, 0, (size_t)P * op_bytes(I)));
-    CK(dmalloc(&c->d_inv, (size_t)P));
     CK(dmalloc(&c->eo, (size_t)P * H));
     CK(cudaMallocHost((void **)&c->h_counts, 4 * sizeof(int)));
     if (c->world > 1) {
@@ -196,6 +212,7 @@ moe_ctx *moe_create(const moe_config *cfg, int device, int rank, int world_size,
     if (!cfg) return nullptr;
     moe_ctx *c = new moe_ctx();
     c->cfg = *cfg;
+    c->use_graphs = getenv("MOE_NO_GRAPHS") == nullptr;
     c->d = MoeDims{cfg->hidden, cfg->intermediate, cfg->n_experts, cfg->n_group, cfg->topk_group, cfg->top_k,
                    cfg->routed_scale};
     c->device = device;
@@ -262,6 +279,7 @@ void moe_destroy(moe_ctx *c) {
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->comm) moe_nccl()->CommDestroy(c->comm);
     for (cudaEvent_t e : c->ev) cudaEventDestroy(e);
+    for (auto &g : c->graphs) cudaGraphExecDestroy(g.exec);
     for (auto &L : c->layers) {
         cudaFree(L.experts);
         cudaFree(L.router);
@@ -269,10 +287,10 @@ void moe_destroy(moe_ctx *c) {
         cudaFree(L.logit_bias);
         cudaFree(L.norm);
     }
-    void *bufs[] = {c->part, c->logits, c->rl_counters, c->d_in, c->d_out, c->h_post, c->idx, c->wts, c->idx_given, c->w_given, c->bias_tmp, c->xop, c->x_inv, c->plan.counts,
+    void *bufs[] = {c->part, c->logits, c->rl_counters, c->d_in, c->d_out, c->h_post, c->idx, c->wts, c->idx_given, c->w_given, c->bias_tmp, c->xop, c->plan.counts,
                     c->plan.pair_expert, c->plan.pair_token, c->plan.pair_w, c->plan.chunk_expert,
                     c->plan.chunk_pair0, c->plan.chunk_ntok, c->plan.slot_pair, c->plan.error, c->counter, c->act,
-                    c->dop, c->d_inv, c->eo, c->send_x, c->recv_x, c->send_y, c->recv_y, c->send_meta,
+                    c->dop, c->eo, c->send_x, c->recv_x, c->send_y, c->recv_y, c->send_meta,
                     c->recv_meta, c->rows_partial, c->tok_slot};
     for (void *b : bufs) cudaFree(b);
     if (c->h_counts) cudaFreeHost(c->h_counts);
@@ -316,6 +334,7 @@ static int layer_alloc(moe_ctx *c, int layer, int down_type, int sh_down_type) {
     if (!L.router) CK(cudaMalloc((void **)&L.router, sizeof(float) * (size_t)E * H));
     if (!L.bias) CK(cudaMalloc((void **)&L.bias, sizeof(float) * E));
     c->layer_down_bytes[layer] = db;
+    drop_graphs(c);
     const int mrc = moe_make_layer_maps(L, c->d);
     if (mrc) return fail(c, MOE_ERR_CUDA, "TMA tensor map of layer %d failed (%d)", layer, mrc);
     return MOE_OK;
@@ -464,6 +483,7 @@ int moe_add_router_bias(moe_ctx *c, int layer, const float *extra) {
 
 int moe_set_logit_bias(moe_ctx *c, int layer, const float *lb) {
     if (!c) return MOE_ERR_ARG;
+    drop_graphs(c);  // the kernels take this layer's pointers by value
     if (layer < 0 || layer >= (int)c->layers.size() || !c->layers[layer].router)
         return fail(c, MOE_ERR_STATE, "layer %d not loaded", layer);
     CK(cudaSetDevice(c->device));
@@ -480,6 +500,7 @@ int moe_set_logit_bias(moe_ctx *c, int layer, const float *lb) {
 
 int moe_set_norm_weight(moe_ctx *c, int layer, const float *w) {
     if (!c || !w) return MOE_ERR_ARG;
+    drop_graphs(c);  // the kernels take this layer's pointers by value
     if (layer < 0 || layer >= (int)c->layers.size()) return fail(c, MOE_ERR_ARG, "layer %d out of range", layer);
     CK(cudaSetDevice(c->device));
     MoeLayerDev &L = c->layers[layer];
@@ -565,15 +586,15 @@ static int run_local(moe_ctx *c, int layer, const float *x, int T, const int *id
                                  &c->launches);
     mark(c, MOE_PHASE_ROUTE, s);
     moe_launch_route_and_plan(d, nullptr, 0, c->logits, L.bias, L.logit_bias, mode, idx_in, w_in, T, c->idx, c->wts,
-                              x, c->xop, c->x_inv, with_shared, 1, c->plan, c->counter, s, &c->launches);
+                              x, c->xop, with_shared, 1, c->plan, c->counter, s, &c->launches);
     const int max_chunks = (T * d.K + T + MOE_TC - 1) / MOE_TC + d.E + 1;
     mark(c, MOE_PHASE_GATEUP, s);
-    moe_launch_gateup(d, L, c->plan, c->xop, c->x_inv, c->act,
+    moe_launch_gateup(d, L, c->plan, c->xop, c->act,
                       max_chunks, s, &c->launches);
     mark(c, MOE_PHASE_PREP, s);
-    moe_launch_prep_down(d, L, c->plan, c->act, c->dop, c->d_inv, T * d.K + T, s, &c->launches);
+    moe_launch_prep_down(d, L, c->plan, c->act, c->dop, T * d.K + T, s, &c->launches);
     mark(c, MOE_PHASE_DOWN, s);
-    moe_launch_down(d, L, c->plan, c->dop, c->d_inv, c->eo, max_chunks, s, &c->launches);
+    moe_launch_down(d, L, c->plan, c->dop, c->eo, max_chunks, s, &c->launches);
     mark(c, MOE_PHASE_OUTPUT, s);
     moe_launch_combine(d, c->plan, c->eo, T, routed, with_shared, residual, out, s, &c->launches);
     mark(c, MOE_N_PHASES, s);
@@ -601,7 +622,7 @@ static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_i
     mark(c, MOE_PHASE_ROUTE, s);
     if (T > 0)
         moe_launch_route_and_plan(d, nullptr, 0, c->logits, L.bias, L.logit_bias, mode, idx_in, w_in, T, c->idx,
-                                  c->wts, x, nullptr, nullptr, 0, 0, c->plan, c->counter, s, &c->launches);
+                                  c->wts, x, nullptr, 0, 0, c->plan, c->counter, s, &c->launches);
     mark(c, MOE_PHASE_DISPATCH, s);
     moe_launch_ep_pack(x, c->idx, c->wts, T, d.K, d.H, N, c->n_local, cap, c->send_x, c->send_meta, c->tok_slot, s,
                        &c->launches);
@@ -614,16 +635,16 @@ static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_i
     }
     NK(moe_nccl()->GroupEnd());
     moe_launch_ep_plan(d, c->recv_meta, N, cap, T, c->e0, c->n_local, c->plan, s, &c->launches);
-    moe_launch_prep_rows(c->recv_x, c->recv_meta, mw, R, x, T, d.H, c->xop, c->x_inv, s, &c->launches);
+    moe_launch_prep_rows(c->recv_x, c->recv_meta, mw, R, x, T, d.H, c->xop, s, &c->launches);
     const int P = R * d.K + T;
     const int max_chunks = (P + MOE_TC - 1) / MOE_TC + d.E + 1;
     mark(c, MOE_PHASE_GATEUP, s);
-    moe_launch_gateup(d, L, c->plan, c->xop, c->x_inv, c->act,
+    moe_launch_gateup(d, L, c->plan, c->xop, c->act,
                       max_chunks, s, &c->launches);
     mark(c, MOE_PHASE_PREP, s);
-    moe_launch_prep_down(d, L, c->plan, c->act, c->dop, c->d_inv, P, s, &c->launches);
+    moe_launch_prep_down(d, L, c->plan, c->act, c->dop, P, s, &c->launches);
     mark(c, MOE_PHASE_DOWN, s);
-    moe_launch_down(d, L, c->plan, c->dop, c->d_inv, c->eo, max_chunks, s, &c->launches);
+    moe_launch_down(d, L, c->plan, c->dop, c->eo, max_chunks, s, &c->launches);
     mark(c, MOE_PHASE_COMBINE, s);
     moe_launch_ep_partial(d, c->plan, c->recv_meta, c->eo, R, c->send_y, s, &c->launches);
     NK(moe_nccl()->GroupStart());
@@ -642,6 +663,63 @@ static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_i
     return MOE_OK;
 }
 
+// One forward on one GPU: the kernel sequence of run_local plus the routing
+// copies.  A signature (layer, T, buffers, stream) seen before is replayed
+// as a CUDA graph (captured on its second call, when every kernel attribute
+// is already set); the per-phase timing ring and a stream that is already
+// being captured by the caller run the kernels directly.
+static int forward_local_once(moe_ctx *c, int layer, const float *d_h, int T, float *d_out, cudaStream_t s) {
+    return run_local(c, layer, d_h, T, nullptr, nullptr, 1, 1, nullptr, d_out, s);
+}
+
+static int forward_local_kernels(moe_ctx *c, int layer, const float *d_h, int T, float *d_out, cudaStream_t s) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (!c->use_graphs || c->timing || cudaStreamIsCapturing(s, &cs) != cudaSuccess ||
+        cs != cudaStreamCaptureStatusNone)
+        return forward_local_once(c, layer, d_h, T, d_out, s);
+    c->clock++;
+    for (auto &g : c->graphs)
+        if (g.layer == layer && g.T == T && g.h == d_h && g.out == d_out && g.s == s) {
+            g.last_use = c->clock;
+            CK(cudaGraphLaunch(g.exec, s));
+            c->launches += g.kernels;
+            return MOE_OK;
+        }
+    const std::array<const void *, 5> sig = {(const void *)(intptr_t)(layer * 4096 + T), d_h, d_out, nullptr,
+                                             (const void *)s};
+    bool seen = false;
+    for (auto &x : c->seen) seen = seen || x == sig;
+    if (!seen) {  // first call: run directly (sets kernel attributes)
+        if (c->seen.size() > 64) c->seen.erase(c->seen.begin());
+        c->seen.push_back(sig);
+        return forward_local_once(c, layer, d_h, T, d_out, s);
+    }
+    const uint64_t k0 = c->launches;
+    CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+    const int rc = forward_local_once(c, layer, d_h, T, d_out, s);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t ec = cudaStreamEndCapture(s, &graph);
+    if (rc) {
+        if (graph) cudaGraphDestroy(graph);
+        return rc;
+    }
+    if (ec != cudaSuccess || !graph) return fail(c, MOE_ERR_CUDA, "graph capture: %s", cudaGetErrorString(ec));
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t ei = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ei != cudaSuccess) return fail(c, MOE_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(ei));
+    if (c->graphs.size() >= 32) {  // drop the least recently used
+        size_t lru = 0;
+        for (size_t i = 1; i < c->graphs.size(); i++)
+            if (c->graphs[i].last_use < c->graphs[lru].last_use) lru = i;
+        cudaGraphExecDestroy(c->graphs[lru].exec);
+        c->graphs.erase(c->graphs.begin() + lru);
+    }
+    c->graphs.push_back({layer, T, d_h, d_out, nullptr, nullptr, s, exec, c->launches - k0, c->clock});
+    CK(cudaGraphLaunch(exec, s));
+    return MOE_OK;
+}
+
 int moe_forward_device(moe_ctx *c, int layer, const float *d_h, int T, float *d_out, int *d_idx, float *d_w,
                        void *stream) {
     if (!c) return MOE_ERR_ARG;
@@ -652,11 +730,12 @@ int moe_forward_device(moe_ctx *c, int layer, const float *d_h, int T, float *d_
     cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
     if (c->world > 1) {
         rc = run_ep(c, layer, d_h, T, nullptr, nullptr, nullptr, d_out, s);  // every rank joins, even with T == 0
+        if (rc) return rc;
     } else {
         if (T == 0) return MOE_OK;
-        rc = run_local(c, layer, d_h, T, nullptr, nullptr, 1, 1, nullptr, d_out, s);
+        rc = forward_local_kernels(c, layer, d_h, T, d_out, s);
+        if (rc) return rc;
     }
-    if (rc) return rc;
     if (d_idx) CK(cudaMemcpyAsync(d_idx, c->idx, sizeof(int) * T * c->d.K, cudaMemcpyDeviceToDevice, s));
     if (d_w) CK(cudaMemcpyAsync(d_w, c->wts, sizeof(float) * T * c->d.K, cudaMemcpyDeviceToDevice, s));
     return MOE_OK;
@@ -756,7 +835,7 @@ int moe_route(moe_ctx *c, const float *logits, const float *bias, int T, int *id
         CK(cudaMemcpyAsync(d_b, bias, sizeof(float) * E, cudaMemcpyHostToDevice, c->stream));
     }
     moe_launch_route_and_plan(c->d, nullptr, 0, d_lg, d_b, nullptr, 0, nullptr, nullptr, T, c->idx, c->wts, nullptr,
-                              nullptr, nullptr, 0, 0, c->plan, c->counter, c->stream, &c->launches);
+                              nullptr, 0, 0, c->plan, c->counter, c->stream, &c->launches);
     CK(cudaGetLastError());
     CK(cudaMemcpyAsync(idx, c->idx, sizeof(int) * T * K, cudaMemcpyDeviceToHost, c->stream));
     CK(cudaMemcpyAsync(w, c->wts, sizeof(float) * T * K, cudaMemcpyDeviceToHost, c->stream));
@@ -796,6 +875,7 @@ int moe_forward_stack(moe_ctx *c, int first, int n_layers, float *hidden, int T)
 
 int moe_set_timing(moe_ctx *c, int enable) {
     if (!c || enable < 0) return MOE_ERR_ARG;
+    drop_graphs(c);
     CK(cudaSetDevice(c->device));
     if (enable > 0 && enable != c->ring) {
         for (cudaEvent_t e : c->ev) cudaEventDestroy(e);

@@ -16,7 +16,7 @@
 
 // ---------------------------------------------------------------------------
 // Activation operand (int8 planes).  The decode GEMVs use the tensor core as
-// an exact reducer: x * s (s a power of two per vector) is rounded to an
+// an exact reducer: x * s (s a power of two per super-block) is rounded to an
 // integer v with |v| <= 2^20 and split into three int8 planes
 //     v = p0 + 2^7 p1 + 2^14 p2,   p0, p1 in [0, 127], p2 in [-64, 64],
 // so that every product with a weight is exact in int32.  The K order inside
@@ -26,7 +26,10 @@
 //   [0, 256)   int8 values in lane order (style Q4 or Q6, below)
 //   [256, 288) style Q4 only: fp16 sums of 16 consecutive plane values,
 //              lane t: sums 2t, 2t+1, 2t+8, 2t+9 (exact: |sum| <= 2032)
-//   [288, 320) zero padding: plane blocks 80 words apart keep the 16-byte
+//   [288, 292) plane 0 only: 1/s of this super-block (fp32); s is a power
+//              of two per vector and super-block, from the super-block's
+//              max |x|
+//   [292, 320) padding: plane blocks 80 words apart keep the 16-byte
 //              fragment loads of one quarter-warp on distinct banks
 // Style Q4 (Q4_K weights, m16n8k32 u8 x s8): weight k = 32 s + 8 t + i of
 // sub-block s = 2 j + h sits at 64 j + 16 t + 8 h + i.
@@ -36,6 +39,7 @@
 #define OPB_PLANE 320
 #define OPB_SB (3 * OPB_PLANE)
 #define OPB_XSUM 256
+#define OPB_SCALE 288
 __host__ __device__ __forceinline__ size_t op_bytes(int K) { return (size_t)(K / 256) * OPB_SB; }
 __host__ __device__ __forceinline__ int opq4_off(int k) {
     const int s = k >> 5, t = (k >> 3) & 3, i = k & 7;

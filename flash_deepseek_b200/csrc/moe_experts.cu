@@ -148,6 +148,16 @@ __device__ __forceinline__ void ex_item(const MoePlan &plan, const MoeLayerDev &
     it.slot = it.e == E ? L.n_local : it.e - L.e0;
 }
 
+// 1/s of the two vectors of an operand tile (2n, 2n + 1) for the lane's two
+// columns 2t, 2t + 1 (columns 0-2: vector 2n, 3-5: vector 2n + 1; columns 6,
+// 7 carry no vector and their results are discarded)
+__device__ __forceinline__ void tile_scales(const uint8_t *tile, int t, float &i0, float &i1) {
+    const float a = *reinterpret_cast<const float *>(tile + OPB_SCALE);
+    const float b = *reinterpret_cast<const float *>(tile + OPB_SB + OPB_SCALE);
+    i0 = t >= 2 ? b : a;
+    i1 = t >= 1 ? b : a;
+}
+
 // ===========================================================================
 // Q4_K super-block of two rows (A rows g, g+8) against NT operand tiles.
 // A Q4_K weight is d sc q - dmin m (quant.c:36-61).  Per sub-block pair j the
@@ -170,10 +180,11 @@ __device__ __forceinline__ void q4_stage(const uint8_t *rowg, const uint8_t *row
         sc8_lo = h8.y & 0x3F3F3F3Fu;
         sc8_hi = (h8.w & 0x0F0F0F0Fu) | ((h8.y >> 2) & 0x30303030u);
     }
-    // this lane's operand column: vector 2n + tsel, plane g % 3 (g < 6)
+    // this lane's operand column: vector 2n + tsel, plane g % 3.  Columns
+    // without a vector (g >= 6, or 2n + tsel >= ntok) read another slot of
+    // the stage; only their own output columns see it, and those are dropped.
     const int tsel = g >= 3 ? 1 : 0;
     const uint8_t *bp = opnd + tsel * OPB_SB + (g % 3) * OPB_PLANE + 16 * t;
-    const int nval = g < 6 ? (ntok - tsel + 1) >> 1 : 0;  // tiles n < nval hold this column
     int acc[NT][4];
 #pragma unroll
     for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0;
@@ -196,7 +207,7 @@ __device__ __forceinline__ void q4_stage(const uint8_t *rowg, const uint8_t *row
         const uint32_t a1h = w80 & 0xF0F0F0F0u, a3h = w81 & 0xF0F0F0F0u;
 #pragma unroll
         for (int n = 0; n < NT; n++) {
-            const uint4 b = n < nval ? lds128(bp + 2 * n * OPB_SB + 64 * j) : make_uint4(0u, 0u, 0u, 0u);
+            const uint4 b = lds128(bp + 2 * n * OPB_SB + 64 * j);
             int dl[4], dh[4];
             mma_u8s8_16832(dl, a0l, a1l, a2l, a3l, b.x, b.y);
             mma_u8s8_16832(dh, a0h, a1h, a2h, a3h, b.z, b.w);
@@ -220,13 +231,16 @@ __device__ __forceinline__ void q4_stage(const uint8_t *rowg, const uint8_t *row
     const float d8 = h2f_bits((uint16_t)(h8.x & 0xFFFFu)) * 0.0625f, dm8 = h2f_bits((uint16_t)(h8.x >> 16));
 #pragma unroll
     for (int n = 0; n < NT; n++) {
-        const uint2 xs = n < nval ? lds64(bp + 2 * n * OPB_SB - 8 * t + OPB_XSUM) : make_uint2(0u, 0u);
+        const uint2 xs = lds64(bp + 2 * n * OPB_SB - 8 * t + OPB_XSUM);
         float mt[4];
         mma_f16_16816(mt, ma, mb, mc, md, xs.x, xs.y, 0.f, 0.f, 0.f, 0.f);
-        accf[n][0] = fmaf(dg, (float)acc[n][0], fmaf(-dmg, mt[0], accf[n][0]));
-        accf[n][1] = fmaf(dg, (float)acc[n][1], fmaf(-dmg, mt[1], accf[n][1]));
-        accf[n][2] = fmaf(d8, (float)acc[n][2], fmaf(-dm8, mt[2], accf[n][2]));
-        accf[n][3] = fmaf(d8, (float)acc[n][3], fmaf(-dm8, mt[3], accf[n][3]));
+        // 1/s of this super-block for the vector of each of the lane's columns
+        float i0, i1;
+        tile_scales(opnd + 2 * n * OPB_SB, t, i0, i1);
+        accf[n][0] = fmaf(dg * i0, (float)acc[n][0], fmaf(-dmg * i0, mt[0], accf[n][0]));
+        accf[n][1] = fmaf(dg * i1, (float)acc[n][1], fmaf(-dmg * i1, mt[1], accf[n][1]));
+        accf[n][2] = fmaf(d8 * i0, (float)acc[n][2], fmaf(-dm8 * i0, mt[2], accf[n][2]));
+        accf[n][3] = fmaf(d8 * i1, (float)acc[n][3], fmaf(-dm8 * i1, mt[3], accf[n][3]));
     }
 }
 
@@ -255,10 +269,11 @@ __device__ __forceinline__ void q6_stage(const uint8_t *qg, const uint8_t *q8, c
     const uint32_t w8[2][6] = {{v0.x, v0.y, v0.z, v0.w, v1.x, v1.y}, {v1.z, v1.w, v2.x, v2.y, v2.z, v2.w}};
     const uint4 sgv = lds128(sg_p), s8v = lds128(s8_p);
     const uint32_t sgw[4] = {sgv.x, sgv.y, sgv.z, sgv.w}, s8w[4] = {s8v.x, s8v.y, s8v.z, s8v.w};
-    // this lane's operand column: vector 2n + tsel, plane g % 3 (g < 6)
+    // this lane's operand column: vector 2n + tsel, plane g % 3.  Columns
+    // without a vector (g >= 6, or 2n + tsel >= ntok) read another slot of
+    // the stage; only their own output columns see it, and those are dropped.
     const int tsel = g >= 3 ? 1 : 0;
     const uint8_t *bp = opnd + tsel * OPB_SB + (g % 3) * OPB_PLANE + 16 * t;
-    const int nval = g < 6 ? (ntok - tsel + 1) >> 1 : 0;  // tiles n < nval hold this column
     int acc[NT][4];
 #pragma unroll
     for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0;
@@ -268,8 +283,7 @@ __device__ __forceinline__ void q6_stage(const uint8_t *qg, const uint8_t *q8, c
         for (int q = 0; q < 2; q++) {
             uint4 B[NT];
 #pragma unroll
-            for (int n = 0; n < NT; n++)
-                B[n] = n < nval ? lds128(bp + 2 * n * OPB_SB + 64 * (2 * h + q)) : make_uint4(0u, 0u, 0u, 0u);
+            for (int n = 0; n < NT; n++) B[n] = lds128(bp + 2 * n * OPB_SB + 64 * (2 * h + q));
 #pragma unroll
             for (int u = 0; u < 4; u++) {
                 const int sp = 4 * q + u, s = 8 * h + sp;
@@ -310,10 +324,12 @@ __device__ __forceinline__ void q6_stage(const uint8_t *qg, const uint8_t *q8, c
     const float fg = dg * 0.25f, f8 = d8 * 0.25f;
 #pragma unroll
     for (int n = 0; n < NT; n++) {
-        accf[n][0] = fmaf(fg, (float)acc[n][0], accf[n][0]);
-        accf[n][1] = fmaf(fg, (float)acc[n][1], accf[n][1]);
-        accf[n][2] = fmaf(f8, (float)acc[n][2], accf[n][2]);
-        accf[n][3] = fmaf(f8, (float)acc[n][3], accf[n][3]);
+        float i0, i1;
+        tile_scales(opnd + 2 * n * OPB_SB, t, i0, i1);
+        accf[n][0] = fmaf(fg * i0, (float)acc[n][0], accf[n][0]);
+        accf[n][1] = fmaf(fg * i1, (float)acc[n][1], accf[n][1]);
+        accf[n][2] = fmaf(f8 * i0, (float)acc[n][2], accf[n][2]);
+        accf[n][3] = fmaf(f8 * i1, (float)acc[n][3], accf[n][3]);
     }
 }
 
@@ -335,8 +351,7 @@ __device__ __forceinline__ float planes_to_vector(float c0, float c1, int t) {
 // gate/up
 // ===========================================================================
 template <int NT>
-__device__ __forceinline__ bool gu_item(const MoeDims &d, const MoePlan &plan, const float *__restrict__ x_inv,
-                                        float *__restrict__ act, const ExItem &it, int NB, uint8_t *sm,
+__device__ __forceinline__ bool gu_item(const MoeDims &d, const MoePlan &plan, float *__restrict__ act, const ExItem &it, int NB, uint8_t *sm,
                                         uint64_t *full, uint64_t *empty, uint32_t &seq, int w, int lane) {
     const int g = lane >> 2, t = lane & 3;
     float accf[NT][4];
@@ -357,12 +372,7 @@ __device__ __forceinline__ bool gu_item(const MoeDims &d, const MoePlan &plan, c
         const float gv = planes_to_vector(accf[n][0], accf[n][1], t);
         const float uv = planes_to_vector(accf[n][2], accf[n][3], t);
         const int tk = 2 * n + t;
-        if (t < 2 && tk < it.ntok) {
-            const int pair = it.p0 + tk;
-            const float inv = x_inv[plan.pair_token[pair]];
-            const float gs = gv * inv, us = uv * inv;
-            act[(size_t)pair * d.I + row] = (gs / (1.0f + expf(-gs))) * us;
-        }
+        if (t < 2 && tk < it.ntok) act[(size_t)(it.p0 + tk) * d.I + row] = (gv / (1.0f + expf(-gv))) * uv;
     }
     return true;
 }
@@ -373,13 +383,12 @@ __device__ __forceinline__ uint8_t *align128(uint8_t *p) {
 
 __global__ void __launch_bounds__(EX_THREADS, 2)
     k_gateup(MoeDims d, const __grid_constant__ MoeLayerDev L, MoePlan plan, const uint8_t *__restrict__ xop,
-             const float *__restrict__ x_inv, float *__restrict__ act) {
+             float *__restrict__ act) {
     extern __shared__ uint8_t ex_raw[];
     __shared__ __align__(8) uint64_t full[GU_NS], empty[GU_NS];
     uint8_t *sm = align128(ex_raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n_chunks = plan.counts[1], NB = d.H / MOE_QK;
-    const int n_items = n_chunks * (d.I / GU_ROWS);
+    const int NB = d.H / MOE_QK;
     if (threadIdx.x == 0) {
         for (int s = 0; s < GU_NS; s++) {
             mbar_init(&full[s], 1);
@@ -388,6 +397,10 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
         fence_barrier_init();
     }
     __syncthreads();
+    moe_pdl_wait();  // the plan and the operand come from the previous kernels
+    moe_pdl_trigger();
+    const int n_chunks = plan.counts[1];
+    const int n_items = n_chunks * (d.I / GU_ROWS);
     uint32_t seq = 0;
     if (warp == EX_CONSUMERS) {  // producer
         const size_t opst = op_bytes(d.H);
@@ -423,10 +436,10 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
         ex_item(plan, L, d.E, n_chunks, item, it);
         bool ok;
         switch ((it.ntok + 1) >> 1) {
-            case 1: ok = gu_item<1>(d, plan, x_inv, act, it, NB, sm, full, empty, seq, warp, lane); break;
-            case 2: ok = gu_item<2>(d, plan, x_inv, act, it, NB, sm, full, empty, seq, warp, lane); break;
-            case 3: ok = gu_item<3>(d, plan, x_inv, act, it, NB, sm, full, empty, seq, warp, lane); break;
-            default: ok = gu_item<4>(d, plan, x_inv, act, it, NB, sm, full, empty, seq, warp, lane); break;
+            case 1: ok = gu_item<1>(d, plan, act, it, NB, sm, full, empty, seq, warp, lane); break;
+            case 2: ok = gu_item<2>(d, plan, act, it, NB, sm, full, empty, seq, warp, lane); break;
+            case 3: ok = gu_item<3>(d, plan, act, it, NB, sm, full, empty, seq, warp, lane); break;
+            default: ok = gu_item<4>(d, plan, act, it, NB, sm, full, empty, seq, warp, lane); break;
         }
         if (!ok) {
             if (lane == 0) atomicExch(plan.error, EX_ERR_TIMEOUT);
@@ -439,7 +452,7 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
 // down
 // ===========================================================================
 template <int NT, int TY>
-__device__ __forceinline__ bool dn_item(const MoeDims &d, const float *__restrict__ d_inv, float *__restrict__ eo,
+__device__ __forceinline__ bool dn_item(const MoeDims &d, float *__restrict__ eo,
                                         const ExItem &it, int NB, int nbp, uint8_t *sm, const uint8_t *dbuf,
                                         uint64_t *full, uint64_t *empty, uint32_t &seq, int w, int lane) {
     const int g = lane >> 2, t = lane & 3;
@@ -473,10 +486,8 @@ __device__ __forceinline__ bool dn_item(const MoeDims &d, const float *__restric
         const float v8 = planes_to_vector(accf[n][2], accf[n][3], t);
         const int tk = 2 * n + t;
         if (t < 2 && tk < it.ntok) {
-            const int pair = it.p0 + tk;
-            const float inv = d_inv[pair];
-            eo[(size_t)pair * d.H + row] = vg * inv;
-            eo[(size_t)pair * d.H + row + 8] = v8 * inv;
+            eo[(size_t)(it.p0 + tk) * d.H + row] = vg;
+            eo[(size_t)(it.p0 + tk) * d.H + row + 8] = v8;
         }
     }
     return true;
@@ -486,7 +497,7 @@ __device__ __forceinline__ bool dn_item(const MoeDims &d, const float *__restric
 template <int TY>
 __global__ void __launch_bounds__(EX_THREADS, 2)
     k_down(MoeDims d, const __grid_constant__ MoeLayerDev L, MoePlan plan, const uint8_t *__restrict__ dop,
-           const float *__restrict__ d_inv, float *__restrict__ eo) {
+           float *__restrict__ eo) {
     constexpr int NS = TY == MOE_TYPE_Q6_K ? DN6_NS : DN4_NS;
     constexpr int STAGE = TY == MOE_TYPE_Q6_K ? DN6_STAGE : DN4_STAGE;
     extern __shared__ uint8_t ex_raw[];
@@ -496,8 +507,6 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
     const int dbytes = DN_ROWS * 2 * nbp;  // per item (Q6_K d plane)
     uint8_t *dbuf0 = sm + (size_t)NS * STAGE;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n_chunks = plan.counts[1];
-    const int n_items = n_chunks * (d.H / DN_ROWS);
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; s++) {
             mbar_init(&full[s], 1);
@@ -506,6 +515,10 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
         fence_barrier_init();
     }
     __syncthreads();
+    moe_pdl_wait();
+    moe_pdl_trigger();
+    const int n_chunks = plan.counts[1];
+    const int n_items = n_chunks * (d.H / DN_ROWS);
     uint32_t seq = 0, nitem = 0;
     if (warp == EX_CONSUMERS) {  // producer
         const size_t opst = op_bytes(d.I);
@@ -552,10 +565,10 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
         nitem++;
         bool ok;
         switch ((it.ntok + 1) >> 1) {
-            case 1: ok = dn_item<1, TY>(d, d_inv, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
-            case 2: ok = dn_item<2, TY>(d, d_inv, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
-            case 3: ok = dn_item<3, TY>(d, d_inv, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
-            default: ok = dn_item<4, TY>(d, d_inv, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
+            case 1: ok = dn_item<1, TY>(d, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
+            case 2: ok = dn_item<2, TY>(d, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
+            case 3: ok = dn_item<3, TY>(d, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
+            default: ok = dn_item<4, TY>(d, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
         }
         if (!ok) {
             if (lane == 0) atomicExch(plan.error, EX_ERR_TIMEOUT);
@@ -568,7 +581,7 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
 // host side
 // ===========================================================================
 void moe_launch_gateup(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const uint8_t *xop,
-                       const float *x_inv, float *act, int max_chunks, cudaStream_t s, uint64_t *launches) {
+                       float *act, int max_chunks, cudaStream_t s, uint64_t *launches) {
     const int max_items = max_chunks * (d.I / GU_ROWS);
     int grid = 2 * ex_num_sms();
     if (grid > max_items) grid = max_items;
@@ -579,12 +592,12 @@ void moe_launch_gateup(const MoeDims &d, const MoeLayerDev &L, const MoePlan &pl
         cudaFuncSetAttribute(k_gateup, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         attr = true;
     }
-    k_gateup<<<grid, EX_THREADS, smem, s>>>(d, L, plan, xop, x_inv, act);
+    moe_launch_pdl(k_gateup, dim3(grid), dim3(EX_THREADS), smem, s, d, L, plan, xop, act);
     LAUNCH_COUNT(launches);
 }
 
-void moe_launch_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const uint8_t *dop,
-                     const float *d_inv, float *eo, int max_chunks, cudaStream_t s, uint64_t *launches) {
+void moe_launch_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const uint8_t *dop, float *eo,
+                     int max_chunks, cudaStream_t s, uint64_t *launches) {
     const int max_items = max_chunks * (d.H / DN_ROWS);
     int grid = 2 * ex_num_sms();
     if (grid > max_items) grid = max_items;
@@ -603,11 +616,11 @@ void moe_launch_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan
         attr4 = true;
     }
     if (L.down_type == MOE_TYPE_Q6_K || L.sh_down_type == MOE_TYPE_Q6_K) {
-        k_down<MOE_TYPE_Q6_K><<<grid, EX_THREADS, sm6, s>>>(d, L, plan, dop, d_inv, eo);
+        moe_launch_pdl(k_down<MOE_TYPE_Q6_K>, dim3(grid), dim3(EX_THREADS), sm6, s, d, L, plan, dop, eo);
         LAUNCH_COUNT(launches);
     }
     if (L.down_type == MOE_TYPE_Q4_K || L.sh_down_type == MOE_TYPE_Q4_K) {
-        k_down<MOE_TYPE_Q4_K><<<grid, EX_THREADS, sm4, s>>>(d, L, plan, dop, d_inv, eo);
+        moe_launch_pdl(k_down<MOE_TYPE_Q4_K>, dim3(grid), dim3(EX_THREADS), sm4, s, d, L, plan, dop, eo);
         LAUNCH_COUNT(launches);
     }
 }

@@ -45,6 +45,29 @@ struct MoeDims {
     float scale;
 };
 
+// Programmatic dependent launch: a forward-path kernel may start while its
+// predecessor on the stream finishes; it runs only prologue work that reads
+// no earlier output before moe_pdl_wait(), and lets its own successor start
+// early with moe_pdl_trigger().  Without the launch attribute both are no-ops.
+#define moe_pdl_wait() asm volatile("griddepcontrol.wait;\n" ::: "memory")
+#define moe_pdl_trigger() asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory")
+
+template <typename... KArgs, typename... Args>
+static inline cudaError_t moe_launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                         cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 #define MOE_TC 8  // tokens per chunk (four 8-column MMA tiles of 2 tokens x 3 planes)
 
 // ---- launchers (moe_kernels.cu); every one counts its kernel launches ------
@@ -57,17 +80,17 @@ void moe_launch_router_logits(const float *Wr, const float *x, int T, int H, int
 // 2 shared expert only
 void moe_launch_route_and_plan(const MoeDims &d, const float *part, int n_split, const float *logits,
                                const float *bias, const float *logit_bias, int mode, const int *idx_in, const float *w_in, int T,
-                               int *idx_out, float *w_out, const float *x, uint8_t *xop, float *x_inv,
+                               int *idx_out, float *w_out, const float *x, uint8_t *xop,
                                int include_shared, int build_plan, const MoePlan &plan, int *counter,
                                cudaStream_t s, uint64_t *launches);
 // xop: int8-plane operand rows (op_bytes(H) each) indexed by pair_token;
 // max_chunks bounds the chunk count of the plan (grid size)
 void moe_launch_gateup(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const uint8_t *xop,
-                       const float *x_inv, float *act, int max_chunks, cudaStream_t s, uint64_t *launches);
+                       float *act, int max_chunks, cudaStream_t s, uint64_t *launches);
 void moe_launch_prep_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const float *act,
-                          uint8_t *dop, float *d_inv, int max_pairs, cudaStream_t s, uint64_t *launches);
-void moe_launch_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const uint8_t *dop,
-                     const float *d_inv, float *eo, int max_chunks, cudaStream_t s, uint64_t *launches);
+                          uint8_t *dop, int max_pairs, cudaStream_t s, uint64_t *launches);
+void moe_launch_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const uint8_t *dop, float *eo,
+                     int max_chunks, cudaStream_t s, uint64_t *launches);
 // TMA maps of a layer (after its weights are allocated); 0 = ok
 int moe_make_layer_maps(MoeLayerDev &L, const MoeDims &d);
 void moe_launch_combine(const MoeDims &d, const MoePlan &plan, const float *eo, int T, int include_routed,
@@ -84,7 +107,7 @@ void moe_launch_synth_quant(int type, uint64_t seed, uint64_t stream, int rows, 
 void moe_launch_synth_f32(uint64_t seed, uint64_t stream, size_t n, double sigma, float *dst, cudaStream_t s,
                           uint64_t *launches);
 void moe_launch_prep_rows(const float *recv, const int *meta, int meta_w, int R, const float *local, int T, int H,
-                          uint8_t *xop, float *x_inv, cudaStream_t s, uint64_t *launches);
+                          uint8_t *xop, cudaStream_t s, uint64_t *launches);
 // expert parallel (moe_ep.cu)
 void moe_launch_ep_pack(const float *x, const int *idx, const float *w, int T, int K, int H, int world, int n_local,
                         int cap, float *send_x, int *send_meta, int *tok_slot, cudaStream_t s, uint64_t *launches);

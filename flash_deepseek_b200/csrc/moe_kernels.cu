@@ -323,6 +323,7 @@ void moe_launch_synth_f32(uint64_t seed, uint64_t stream, size_t n, double sigma
 // ===========================================================================
 #define RL_KS 256
 #define RL_WPAD (RL_KS + 4)
+#define RL_MAX_SPLIT 32  // partial sums loaded together by the reducing CTA
 __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__ Wr, const float *__restrict__ x,
                                                        int T, int H, int E, float *__restrict__ part,
                                                        float *__restrict__ logits, int *__restrict__ counters) {
@@ -346,6 +347,9 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
             *reinterpret_cast<float4 *>(Ws + r * RL_WPAD + 4 * c4) = wv[u];
         }
     }
+    // the weight tile above is constant; x comes from the previous kernel
+    moe_pdl_wait();
+    moe_pdl_trigger();
     const int eg = tid >> 5, tg = tid & 31;
     const bool small = T <= 4;
     if (small) {
@@ -436,9 +440,16 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
     for (int i = tid; i < T * 32; i += 256) {
         const int t = i / 32, e = e0 + i % 32;
         if (e >= E) continue;
+        // all partials in flight at once, then summed in split order
+        float pv[RL_MAX_SPLIT];
+#pragma unroll
+        for (int sp = 0; sp < RL_MAX_SPLIT; sp++)
+            pv[sp] = sp < ns ? __ldcg(part + ((size_t)sp * T + t) * E + e) : 0.0f;
         float v = 0.0f;
-#pragma unroll 4
-        for (int sp = 0; sp < ns; sp++) v += __ldcg(part + ((size_t)sp * T + t) * E + e);
+#pragma unroll
+        for (int sp = 0; sp < RL_MAX_SPLIT; sp++)
+            if (sp < ns) v += pv[sp];
+        for (int sp = RL_MAX_SPLIT; sp < ns; sp++) v += __ldcg(part + ((size_t)sp * T + t) * E + e);
         logits[(size_t)t * E + e] = v;
     }
     if (tid == 0) counters[blockIdx.x] = 0;
@@ -453,51 +464,8 @@ void moe_launch_router_logits(const float *Wr, const float *x, int T, int H, int
         cudaFuncSetAttribute(k_router_logits, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         attr = true;
     }
-    k_router_logits<<<grid, 256, smem, s>>>(Wr, x, T, H, E, part, logits, counters);
+    moe_launch_pdl(k_router_logits, grid, dim3(256), smem, s, Wr, x, T, H, E, part, logits, counters);
     LAUNCH_COUNT(launches);
-}
-
-// ===========================================================================
-// Activation operands
-// ===========================================================================
-// Copies a row of n floats (n % 4 == 0, 16-byte aligned) to shared memory
-// with up to 8 float4 loads in flight per thread, then syncs the block.
-__device__ __forceinline__ void stage_row(const float *__restrict__ x, int n, float *__restrict__ xs) {
-    const float4 *src = reinterpret_cast<const float4 *>(x);
-    float4 *dst = reinterpret_cast<float4 *>(xs);
-    const int n4 = n / 4, step = blockDim.x;
-    for (int base = 0; base < n4; base += 8 * step) {
-        float4 v[8];
-#pragma unroll
-        for (int u = 0; u < 8; u++) {
-            const int i = base + u * step + threadIdx.x;
-            if (i < n4) v[u] = __ldg(src + i);
-        }
-#pragma unroll
-        for (int u = 0; u < 8; u++) {
-            const int i = base + u * step + threadIdx.x;
-            if (i < n4) dst[i] = v[u];
-        }
-    }
-    __syncthreads();
-}
-
-__device__ __forceinline__ float block_max_abs(const float *x, int n, float *red /*[32]*/) {
-    float m = 0.0f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, fabsf(x[i]));
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    __syncthreads();
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0f;
-        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-        if (threadIdx.x == 0) red[0] = v;
-    }
-    __syncthreads();
-    const float r = red[0];
-    __syncthreads();
-    return r;
 }
 
 // power-of-two scale s with max|x| * s in [2^(top-1), 2^top); returns s, sets
@@ -513,37 +481,62 @@ __device__ __forceinline__ float op_scale(float amax, float *inv, int top) {
     return ldexpf(1.0f, e);
 }
 
-// int8-plane operand of one K-vector (all threads of the block; x in shared
-// memory): v = rint(x * s), |v| <= 2^20, v = p0 + 2^7 p1 + 2^14 p2, stored
-// in the lane order of `style` (4: Q4_K weights, with the fp16 sums of 16
-// consecutive plane values; 6: Q6_K weights).  Layout in moe_common.cuh.
-__device__ void build_op(const float *__restrict__ x, int K, float s, uint8_t *__restrict__ op, int style) {
-    for (int m = threadIdx.x; m < K / 4; m += blockDim.x) {
-        const int k = 4 * m, kk = k & 255;
-        uint32_t w0 = 0, w1 = 0, w2 = 0;
+// One 256-weight super-block of one vector, built by one warp: s = power of
+// two from the super-block's max |x| (|rint(x s)| <= 2^20), int8 planes in
+// the lane order of `style` (4: Q4_K weights, with the fp16 sums of 16
+// consecutive plane values; 6: Q6_K weights) and 1/s.  Layout in
+// moe_common.cuh.  x must be 16-byte aligned.
+__device__ __forceinline__ void build_op_sb(const float *__restrict__ x, uint8_t *__restrict__ op, int style,
+                                            int lane) {
+    const float4 a = __ldg(reinterpret_cast<const float4 *>(x) + 2 * lane);
+    const float4 b = __ldg(reinterpret_cast<const float4 *>(x) + 2 * lane + 1);
+    const float v8[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    float m = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int v = __float2int_rn(__fmul_rn(x[k + i], s));
-            w0 |= (uint32_t)(v & 127) << (8 * i);
-            w1 |= (uint32_t)((v >> 7) & 127) << (8 * i);
-            w2 |= (uint32_t)((v >> 14) & 255) << (8 * i);
-        }
-        uint8_t *b = op + (size_t)(k >> 8) * OPB_SB + (style == 4 ? opq4_off(kk) : opq6_off(kk));
-        *reinterpret_cast<uint32_t *>(b) = w0;
-        *reinterpret_cast<uint32_t *>(b + OPB_PLANE) = w1;
-        *reinterpret_cast<uint32_t *>(b + 2 * OPB_PLANE) = w2;
+    for (int i = 0; i < 8; i++) m = fmaxf(m, fabsf(v8[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float inv;
+    const float s = op_scale(m, &inv, 20);
+    uint32_t w[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};
+    int ps[3] = {0, 0, 0};
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int v = __float2int_rn(__fmul_rn(v8[i], s));
+        const int p0 = v & 127, p1 = (v >> 7) & 127, p2 = v >> 14;
+        w[0][i >> 2] |= (uint32_t)p0 << (8 * (i & 3));
+        w[1][i >> 2] |= (uint32_t)p1 << (8 * (i & 3));
+        w[2][i >> 2] |= (uint32_t)(p2 & 255) << (8 * (i & 3));
+        ps[0] += p0;
+        ps[1] += p1;
+        ps[2] += p2;
     }
-    if (style != 4) return;
-    for (int q = threadIdx.x; q < (K / 16) * 3; q += blockDim.x) {
-        const int grp = q / 3, pl = q % 3, k0 = 16 * grp;
-        int acc = 0;
-        for (int i = 0; i < 16; i++) {
-            const int v = __float2int_rn(__fmul_rn(x[k0 + i], s));
-            acc += pl == 0 ? (v & 127) : (pl == 1 ? ((v >> 7) & 127) : (v >> 14));
-        }
-        *reinterpret_cast<__half *>(op + (size_t)(k0 >> 8) * OPB_SB + pl * OPB_PLANE +
-                                    opq4_xsum_off((k0 & 255) >> 4)) = __int2half_rn(acc);
+    const int k = 8 * lane;
+    const int off0 = style == 4 ? opq4_off(k) : opq6_off(k), off1 = style == 4 ? opq4_off(k + 4) : opq6_off(k + 4);
+#pragma unroll
+    for (int p = 0; p < 3; p++) {
+        *reinterpret_cast<uint32_t *>(op + p * OPB_PLANE + off0) = w[p][0];
+        *reinterpret_cast<uint32_t *>(op + p * OPB_PLANE + off1) = w[p][1];
     }
+    if (style == 4) {  // lanes 2j, 2j + 1 hold the 16 values [16 j, 16 j + 16)
+        int tot[3];
+#pragma unroll
+        for (int p = 0; p < 3; p++) tot[p] = ps[p] + __shfl_xor_sync(0xffffffffu, ps[p], 1);
+        if ((lane & 1) == 0) {
+#pragma unroll
+            for (int p = 0; p < 3; p++)
+                *reinterpret_cast<__half *>(op + p * OPB_PLANE + opq4_xsum_off(lane >> 1)) = __int2half_rn(tot[p]);
+        }
+    }
+    if (lane == 0) *reinterpret_cast<float *>(op + OPB_SCALE) = inv;
+}
+
+// Operand of a K-vector by the warps of the block, one super-block per warp.
+__device__ __forceinline__ void build_op_rows(const float *__restrict__ x, int K, uint8_t *__restrict__ op,
+                                              int style) {
+    const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int sb = threadIdx.x >> 5; sb < K / MOE_QK; sb += nw)
+        build_op_sb(x + (size_t)sb * MOE_QK, op + (size_t)sb * OPB_SB, style, lane);
 }
 
 // ===========================================================================
@@ -559,7 +552,7 @@ struct RouteArgs {
     int mode;                              // 0 route, 1 routing given, 2 shared expert only
     int T;
     int *idx_out; float *w_out;
-    const float *x; uint8_t *xop; float *x_inv;  // x operand (may be nullptr)
+    const float *x; uint8_t *xop;  // x operand (may be nullptr)
     int include_shared, build_plan;
     MoePlan plan;
     int *counter;
@@ -678,8 +671,9 @@ __device__ void build_plan_block(const RouteArgs &a) {
 __global__ void __launch_bounds__(256) k_route_plan(RouteArgs a) {
     __shared__ float score[1024], choice[1024];
     __shared__ float gs[64];
-    __shared__ float red[32];
     __shared__ int is_last;
+    moe_pdl_wait();
+    moe_pdl_trigger();
     const int t = blockIdx.x;
     const int E = a.d.E, K = a.d.K, G = a.d.n_group, TG = a.d.topk_group;
     const int per = E / G;
@@ -697,15 +691,33 @@ __global__ void __launch_bounds__(256) k_route_plan(RouteArgs a) {
             choice[e] = sc + (a.bias ? a.bias[e] : 0.0f);
         }
         __syncthreads();
-        // group score = top1 + top2 (strict '>', infer.m:931-941)
-        for (int g = threadIdx.x; g < G; g += blockDim.x) {
-            float t1 = -1e30f, t2 = -1e30f;
-            for (int e = 0; e < per; e++) {
-                const float s = choice[g * per + e];
-                if (s > t1) { t2 = t1; t1 = s; }
-                else if (s > t2) t2 = s;
+        // group score = top1 + top2 (strict '>', infer.m:931-941): the sum of
+        // the two largest values of the group, counted with multiplicity
+        if (per <= 32) {
+            const int lane = threadIdx.x & 31;
+            for (int g = threadIdx.x >> 5; g < G; g += blockDim.x >> 5) {
+                const float v = lane < per ? choice[g * per + lane] : -1e30f;
+                float m1 = v;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+                const unsigned at = __ballot_sync(0xffffffffu, v == m1);
+                float m2 = (__popc(at) > 1 || lane != __ffs(at) - 1) ? v : -1e30f;
+                if (__popc(at) > 1) m2 = m1;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) m2 = fmaxf(m2, __shfl_xor_sync(0xffffffffu, m2, o));
+                if (per < 2) m2 = -1e30f;
+                if (lane == 0) gs[g] = m1 + m2;
             }
-            gs[g] = t1 + t2;
+        } else {
+            for (int g = threadIdx.x; g < G; g += blockDim.x) {
+                float t1 = -1e30f, t2 = -1e30f;
+                for (int e = 0; e < per; e++) {
+                    const float s = choice[g * per + e];
+                    if (s > t1) { t2 = t1; t1 = s; }
+                    else if (s > t2) t2 = s;
+                }
+                gs[g] = t1 + t2;
+            }
         }
         __syncthreads();
         if (threadIdx.x == 0) {
@@ -761,16 +773,7 @@ __global__ void __launch_bounds__(256) k_route_plan(RouteArgs a) {
     }
 
     // activation operand of this token for the gate/up GEMV
-    if (a.xop) {
-        extern __shared__ float xrow[];  // [H]
-        stage_row(a.x + (size_t)t * a.d.H, a.d.H, xrow);
-        const float *xr = xrow;
-        const float amax = block_max_abs(xr, a.d.H, red);
-        float inv;
-        const float s = op_scale(amax, &inv, 20);
-        build_op(xr, a.d.H, s, a.xop + (size_t)t * op_bytes(a.d.H), 4);
-        if (threadIdx.x == 0) a.x_inv[t] = inv;
-    }
+    if (a.xop) build_op_rows(a.x + (size_t)t * a.d.H, a.d.H, a.xop + (size_t)t * op_bytes(a.d.H), 4);
     if (!a.build_plan) return;
     // last block to finish builds the plan for all tokens
     __threadfence();
@@ -785,53 +788,31 @@ __global__ void __launch_bounds__(256) k_route_plan(RouteArgs a) {
 
 void moe_launch_route_and_plan(const MoeDims &d, const float *part, int n_split, const float *logits,
                                const float *bias, const float *logit_bias, int mode, const int *idx_in, const float *w_in, int T,
-                               int *idx_out, float *w_out, const float *x, uint8_t *xop, float *x_inv,
+                               int *idx_out, float *w_out, const float *x, uint8_t *xop,
                                int include_shared, int build_plan, const MoePlan &plan, int *counter,
                                cudaStream_t s, uint64_t *launches) {
     RouteArgs a;
     a.d = d; a.part = part; a.n_split = n_split; a.logits = logits; a.bias = bias; a.logit_bias = logit_bias;
     a.idx_in = idx_in; a.w_in = w_in; a.mode = mode; a.T = T; a.idx_out = idx_out; a.w_out = w_out;
-    a.x = x; a.xop = xop; a.x_inv = x_inv; a.include_shared = include_shared; a.build_plan = build_plan;
+    a.x = x; a.xop = xop; a.include_shared = include_shared; a.build_plan = build_plan;
     a.plan = plan; a.counter = counter;
-    const size_t smem = xop ? sizeof(float) * (size_t)d.H : 0;
-    static size_t attr = 0;
-    if (smem > attr) {
-        cudaFuncSetAttribute(k_route_plan, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr = smem;
-    }
-    k_route_plan<<<T, 256, smem, s>>>(a);
+    moe_launch_pdl(k_route_plan, dim3(T), dim3(256), 0, s, a);
     LAUNCH_COUNT(launches);
 }
 
 // ===========================================================================
-// Q4_K warp tile: rows (r0+g, r0+g+8) of one matrix over super-blocks
-// [sb0, sb1) against up to 4*NT activation vectors.  Lane (g = lane/4,
-// t = lane%4).  For each super-block the lane loads 2 x 16 B of nibbles per
-// row plus the 16-byte header, decodes the weights of each MMA step to
-// sc*q in fp16 (exact: HFMA2 of the 1024+q magic), accumulates
-// P1 = sum sc*q*x and P2 = sum m*X (min term) on the tensor core and flushes
-// acc += d*P1 - dmin*P2 (quant.c:36-61 algebra, fp32).
-// ===========================================================================
 // down operand: per pair, scale + operand of the expert's down type
 // ===========================================================================
 __global__ void __launch_bounds__(256) k_prep_down(MoeDims d, MoeLayerDev L, MoePlan plan,
-                                                   const float *__restrict__ act, uint8_t *__restrict__ dop,
-                                                   float *__restrict__ d_inv) {
-    __shared__ float red[32];
+                                                   const float *__restrict__ act, uint8_t *__restrict__ dop) {
+    moe_pdl_wait();
+    moe_pdl_trigger();
     const int n_pairs = plan.counts[0];
     const size_t opst = op_bytes(d.I);
-    extern __shared__ float arow[];  // [I]
     for (int p = blockIdx.x; p < n_pairs; p += gridDim.x) {
-        stage_row(act + (size_t)p * d.I, d.I, arow);
-        const float *a = arow;
-        const float amax = block_max_abs(a, d.I, red);
         const int e = plan.pair_expert[p];
         const int ty = (e == d.E) ? L.sh_down_type : L.down_type;
-        float inv;
-        const float s = op_scale(amax, &inv, 20);
-        build_op(a, d.I, s, dop + (size_t)p * opst, ty == 14 ? 6 : 4);
-        if (threadIdx.x == 0) d_inv[p] = inv;
-        __syncthreads();
+        build_op_rows(act + (size_t)p * d.I, d.I, dop + (size_t)p * opst, ty == 14 ? 6 : 4);
     }
 }
 
@@ -839,44 +820,24 @@ __global__ void __launch_bounds__(256) k_prep_down(MoeDims d, MoeLayerDev L, Moe
 // their metadata says the slot is empty), rows [R, R + T) from `local`.
 __global__ void __launch_bounds__(256) k_prep_rows(const float *__restrict__ recv, const int *__restrict__ meta,
                                                    int meta_w, int R, const float *__restrict__ local, int H,
-                                                   uint8_t *__restrict__ xop, float *__restrict__ x_inv) {
-    __shared__ float red[32];
+                                                   uint8_t *__restrict__ xop) {
     const int r = blockIdx.x;
     if (r < R && !meta[(size_t)r * meta_w]) return;
-    extern __shared__ float xrow[];  // [H]
-    stage_row(r < R ? recv + (size_t)r * H : local + (size_t)(r - R) * H, H, xrow);
-    const float *x = xrow;
-    const float amax = block_max_abs(x, H, red);
-    float inv;
-    const float s = op_scale(amax, &inv, 20);
-    build_op(x, H, s, xop + (size_t)r * op_bytes(H), 4);
-    if (threadIdx.x == 0) x_inv[r] = inv;
+    build_op_rows(r < R ? recv + (size_t)r * H : local + (size_t)(r - R) * H, H, xop + (size_t)r * op_bytes(H), 4);
 }
 
 void moe_launch_prep_rows(const float *recv, const int *meta, int meta_w, int R, const float *local, int T, int H,
-                          uint8_t *xop, float *x_inv, cudaStream_t s, uint64_t *launches) {
-    const size_t smem = sizeof(float) * (size_t)H;
-    static size_t attr = 0;
-    if (smem > attr) {
-        cudaFuncSetAttribute(k_prep_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr = smem;
-    }
-    k_prep_rows<<<R + T, 256, smem, s>>>(recv, meta, meta_w, R, local, H, xop, x_inv);
+                          uint8_t *xop, cudaStream_t s, uint64_t *launches) {
+    k_prep_rows<<<R + T, 256, 0, s>>>(recv, meta, meta_w, R, local, H, xop);
     LAUNCH_COUNT(launches);
 }
 
 void moe_launch_prep_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const float *act,
-                          uint8_t *dop, float *d_inv, int max_pairs, cudaStream_t s, uint64_t *launches) {
+                          uint8_t *dop, int max_pairs, cudaStream_t s, uint64_t *launches) {
     int grid = max_pairs;
     if (grid > num_sms() * 4) grid = num_sms() * 4;
     if (grid < 1) grid = 1;
-    const size_t smem = sizeof(float) * (size_t)d.I;
-    static size_t attr = 0;
-    if (smem > attr) {
-        cudaFuncSetAttribute(k_prep_down, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr = smem;
-    }
-    k_prep_down<<<grid, 256, smem, s>>>(d, L, plan, act, dop, d_inv);
+    moe_launch_pdl(k_prep_down, dim3(grid), dim3(256), 0, s, d, L, plan, act, dop);
     LAUNCH_COUNT(launches);
 }
 
@@ -885,6 +846,8 @@ void moe_launch_prep_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan 
 // ===========================================================================
 __global__ void k_combine(MoeDims d, MoePlan plan, const float *__restrict__ eo, int T, int include_routed,
                           int include_shared, const float *__restrict__ residual, float *__restrict__ out) {
+    moe_pdl_wait();
+    moe_pdl_trigger();
     const int t = blockIdx.y;
     const int K = d.K, KR = include_routed ? d.K : 0;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -903,7 +866,7 @@ __global__ void k_combine(MoeDims d, MoePlan plan, const float *__restrict__ eo,
 void moe_launch_combine(const MoeDims &d, const MoePlan &plan, const float *eo, int T, int include_routed,
                         int include_shared, const float *residual, float *out, cudaStream_t s, uint64_t *launches) {
     dim3 grid((d.H + 255) / 256, T);
-    k_combine<<<grid, 256, 0, s>>>(d, plan, eo, T, include_routed, include_shared, residual, out);
+    moe_launch_pdl(k_combine, grid, dim3(256), 0, s, d, plan, eo, T, include_routed, include_shared, residual, out);
     LAUNCH_COUNT(launches);
 }
 
@@ -912,6 +875,8 @@ void moe_launch_combine(const MoeDims &d, const MoePlan &plan, const float *eo, 
 // ===========================================================================
 __global__ void k_rmsnorm(const float *__restrict__ x, const float *__restrict__ w, float *__restrict__ y, int H,
                           float eps) {
+    moe_pdl_wait();
+    moe_pdl_trigger();
     __shared__ float red[32];
     const float *xr = x + (size_t)blockIdx.x * H;
     float ss = 0.0f;
@@ -934,6 +899,6 @@ __global__ void k_rmsnorm(const float *__restrict__ x, const float *__restrict__
 
 void moe_launch_rmsnorm(const float *x, const float *w, float *y, int T, int H, float eps, cudaStream_t s,
                         uint64_t *launches) {
-    k_rmsnorm<<<T, 256, 0, s>>>(x, w, y, H, eps);
+    moe_launch_pdl(k_rmsnorm, dim3(T), dim3(256), 0, s, x, w, y, H, eps);
     LAUNCH_COUNT(launches);
 }

@@ -76,7 +76,7 @@ extern "C" int moe_route_hidden_noalloc(const moe_config *cfg, const float *d_ro
     moe_launch_router_logits(d_router_w, d_h, T, H, E, part, n_split, logits, counters, s, nullptr);
     MoePlan none{};
     moe_launch_route_and_plan(d, nullptr, 0, logits, d_bias, nullptr, 0, nullptr, nullptr, T, d_idx, d_w, nullptr,
-                              nullptr, nullptr, 0, 0, none, nullptr, s, nullptr);
+                              nullptr, 0, 0, none, nullptr, s, nullptr);
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         fprintf(stderr, "[moe_cuda] ERROR: moe_route_hidden_noalloc: %s\n", cudaGetErrorString(e));

@@ -274,3 +274,32 @@ def test_errors_are_reported(cuda_lib):
     out, _, _ = m.forward(0, np.ones((1, cfg.hidden), np.float32))
     assert np.all(np.isfinite(out))
     m.close()
+
+
+@pytest.mark.gpu
+def test_graph_replay_matches_direct_launch(cuda_lib, oracle, monkeypatch):
+    """The 1-GPU forward is replayed as a CUDA graph from the second call of a
+    signature on; replays are bit-identical to direct launches (a context
+    created with MOE_NO_GRAPHS) and to each other."""
+    import torch
+    cfg = small_cfg()
+    h = oracle.normal(5, oracle.stream(0, 0, oracle.KIND_ACT), 6 * cfg.hidden, 1.0).reshape(6, cfg.hidden)
+    outs = {}
+    for mode in ("graphs", "direct"):
+        if mode == "direct":
+            monkeypatch.setenv("MOE_NO_GRAPHS", "1")
+        m = cuda_lib.MoE(cfg)
+        m.init_layer_synthetic(0, seed=11, down_type=14)
+        d_h = torch.from_numpy(h).cuda()
+        d_out = torch.empty_like(d_h)
+        res = []
+        for _ in range(4):
+            m.forward_device(0, d_h, 6, d_out)
+            torch.cuda.synchronize()
+            res.append(d_out.cpu().numpy().copy())
+        for r in res[1:]:
+            assert np.array_equal(r.view(np.uint32), res[0].view(np.uint32))
+        outs[mode] = res[0]
+        m.close()
+        monkeypatch.delenv("MOE_NO_GRAPHS", raising=False)
+    assert np.array_equal(outs["graphs"].view(np.uint32), outs["direct"].view(np.uint32))
