@@ -668,12 +668,115 @@ __device__ void build_plan_block(const RouteArgs &a) {
     }
 }
 
+// Top groups by repeated argmax, the lowest index winning ties and only
+// scores above -1e30 counting (infer.m:944-954), with one warp: lane l holds
+// groups l and l + 32.
+__device__ __forceinline__ unsigned long long top_groups_warp(const float *gs, int G, int TG, int lane) {
+    unsigned long long taken = 0ull;
+    const float v0 = lane < G ? gs[lane] : -3.0e38f, v1 = lane + 32 < G ? gs[lane + 32] : -3.0e38f;
+    for (int k = 0; k < TG; k++) {
+        float bv = -1e30f;
+        int bi = -1;
+        if (lane < G && !((taken >> lane) & 1ull) && v0 > bv) { bv = v0; bi = lane; }
+        if (lane + 32 < G && !((taken >> (lane + 32)) & 1ull) && v1 > bv) { bv = v1; bi = lane + 32; }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (oi >= 0 && (ov > bv || (ov == bv && (bi < 0 || oi < bi)))) { bv = ov; bi = oi; }
+        }
+        if (bi >= 0) taken |= 1ull << bi;
+    }
+    return taken;
+}
+
+// Slot-order top-K of infer.m:966-980 over the experts of the taken groups in
+// ascending order: a candidate strictly greater than the current minimum
+// replaces the first (lowest) slot holding that minimum.  One warp; every
+// lane keeps the same KK slots (K <= KK used) in registers.  Candidates are
+// tested 32 at a time with a ballot; only the first one above the minimum is
+// inserted before the rest of the batch is tested again against the new
+// minimum (the minimum only grows, so earlier lanes stay out).
+template <int KK>
+__device__ __forceinline__ void topk_slots_warp(const float *choice, unsigned long long taken, int G, int per, int K,
+                                                int lane, float (&key)[MOE_MAX_K], int (&idx)[MOE_MAX_K]) {
+    float kv[KK];
+    int iv[KK];
+#pragma unroll
+    for (int k = 0; k < KK; k++) {
+        kv[k] = k < K ? -1e30f : 3.0e38f;  // unused slots are never the minimum
+        iv[k] = 0;
+    }
+    int mk = 0;
+    float mkey = -1e30f;
+    for (int g = 0; g < G; g++) {
+        if (!((taken >> g) & 1ull)) continue;
+        for (int e0 = g * per; e0 < (g + 1) * per; e0 += 32) {
+            const float c = e0 + lane < (g + 1) * per ? choice[e0 + lane] : -1e30f;
+            unsigned rem = 0xffffffffu;
+            for (;;) {
+                const unsigned bal = __ballot_sync(0xffffffffu, c > mkey) & rem;
+                if (!bal) break;
+                const int f = __ffs(bal) - 1;
+                const float cf = __shfl_sync(0xffffffffu, c, f);
+#pragma unroll
+                for (int k = 0; k < KK; k++)
+                    if (k == mk) { kv[k] = cf; iv[k] = e0 + f; }
+                float tv[KK];
+                int ti[KK];
+#pragma unroll
+                for (int k = 0; k < KK; k++) { tv[k] = kv[k]; ti[k] = k; }
+#pragma unroll
+                for (int w = 1; w < KK; w <<= 1)
+#pragma unroll
+                    for (int k = 0; k + w < KK; k += 2 * w)
+                        if (tv[k + w] < tv[k]) { tv[k] = tv[k + w]; ti[k] = ti[k + w]; }
+                mkey = tv[0];
+                mk = ti[0];
+                rem = f == 31 ? 0u : (0xffffffffu << (f + 1));
+            }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < MOE_MAX_K; k++) {
+        key[k] = k < KK ? kv[k < KK ? k : 0] : -1e30f;
+        idx[k] = k < KK ? iv[k < KK ? k : 0] : 0;
+    }
+}
+
+// The last block of the grid to finish builds the plan for all tokens.
+__device__ __forceinline__ void route_plan_finish(const RouteArgs &a, int &is_last) {
+    if (!a.build_plan) return;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) is_last = (atomicAdd(a.counter, 1) == (int)gridDim.x - 1);
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    build_plan_block(a);
+    if (threadIdx.x == 0) *a.counter = 0;
+}
+
+// Grid: T routing blocks (one per token), then the operand blocks (one
+// super-block of one token per warp).  The last block to finish builds the
+// plan.
 __global__ void __launch_bounds__(256) k_route_plan(RouteArgs a) {
     __shared__ float score[1024], choice[1024];
     __shared__ float gs[64];
     __shared__ int is_last;
     moe_pdl_wait();
     moe_pdl_trigger();
+    if ((int)blockIdx.x >= a.T) {
+        const int nbh = a.d.H / MOE_QK;
+        const int item = ((int)blockIdx.x - a.T) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+        if (item < a.T * nbh) {
+            const int tk = item / nbh, sb = item % nbh;
+            build_op_sb(a.x + (size_t)tk * a.d.H + (size_t)sb * MOE_QK,
+                        a.xop + (size_t)tk * op_bytes(a.d.H) + (size_t)sb * OPB_SB, 4, threadIdx.x & 31);
+        }
+        route_plan_finish(a, is_last);
+        return;
+    }
     const int t = blockIdx.x;
     const int E = a.d.E, K = a.d.K, G = a.d.n_group, TG = a.d.topk_group;
     const int per = E / G;
@@ -720,41 +823,16 @@ __global__ void __launch_bounds__(256) k_route_plan(RouteArgs a) {
             }
         }
         __syncthreads();
-        if (threadIdx.x == 0) {
-            // top groups by repeated argmax, lowest index wins (infer.m:944-954)
-            unsigned long long taken = 0ull;
-            for (int k = 0; k < TG; k++) {
-                int best = -1;
-                float bs = -1e30f;
-                for (int g = 0; g < G; g++)
-                    if (!((taken >> g) & 1ull) && gs[g] > bs) { bs = gs[g]; best = g; }
-                if (best >= 0) taken |= 1ull << best;
-            }
-            // top-K in slot order (infer.m:966-980): scan experts ascending,
-            // replace the first minimum slot when strictly greater.  The K
-            // slots stay in registers (fully unrolled over MOE_MAX_K).
+        if (threadIdx.x < 32) {
+            // top groups, then the slot-order top-K, by warp 0 (all lanes end
+            // with the same slots)
+            const int lane = threadIdx.x;
+            const unsigned long long taken = top_groups_warp(gs, G, TG, lane);
             float key[MOE_MAX_K];
             int idx[MOE_MAX_K];
-#pragma unroll
-            for (int k = 0; k < MOE_MAX_K; k++) { key[k] = -1e30f; idx[k] = 0; }
-            int mk = 0;
-            float mkey = -1e30f;
-            for (int g = 0; g < G; g++) {
-                if (!((taken >> g) & 1ull)) continue;
-                for (int e = g * per; e < (g + 1) * per; e++) {
-                    const float c = choice[e];
-                    if (c > mkey) {
-#pragma unroll
-                        for (int k = 0; k < MOE_MAX_K; k++)
-                            if (k == mk) { key[k] = c; idx[k] = e; }
-                        mk = 0;
-                        mkey = key[0];
-#pragma unroll
-                        for (int k = 1; k < MOE_MAX_K; k++)
-                            if (k < K && key[k] < mkey) { mkey = key[k]; mk = k; }
-                    }
-                }
-            }
+            if (K <= 8) topk_slots_warp<8>(choice, taken, G, per, K, lane, key, idx);
+            else topk_slots_warp<MOE_MAX_K>(choice, taken, G, per, K, lane, key, idx);
+            if (lane != 0) goto routed;
             float w[MOE_MAX_K], s = 0.0f;
 #pragma unroll
             for (int k = 0; k < MOE_MAX_K; k++)
@@ -767,23 +845,13 @@ __global__ void __launch_bounds__(256) k_route_plan(RouteArgs a) {
                     a.w_out[t * K + k] = s > 0.0f ? w[k] * f : w[k];
                 }
         }
+    routed:;
     } else if (a.mode == 1 && threadIdx.x < K) {
         a.idx_out[t * K + threadIdx.x] = a.idx_in[t * K + threadIdx.x];
         a.w_out[t * K + threadIdx.x] = a.w_in[t * K + threadIdx.x];
     }
 
-    // activation operand of this token for the gate/up GEMV
-    if (a.xop) build_op_rows(a.x + (size_t)t * a.d.H, a.d.H, a.xop + (size_t)t * op_bytes(a.d.H), 4);
-    if (!a.build_plan) return;
-    // last block to finish builds the plan for all tokens
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) is_last = (atomicAdd(a.counter, 1) == a.T - 1);
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-    build_plan_block(a);
-    if (threadIdx.x == 0) *a.counter = 0;
+    route_plan_finish(a, is_last);
 }
 
 void moe_launch_route_and_plan(const MoeDims &d, const float *part, int n_split, const float *logits,
@@ -796,7 +864,8 @@ void moe_launch_route_and_plan(const MoeDims &d, const float *part, int n_split,
     a.idx_in = idx_in; a.w_in = w_in; a.mode = mode; a.T = T; a.idx_out = idx_out; a.w_out = w_out;
     a.x = x; a.xop = xop; a.include_shared = include_shared; a.build_plan = build_plan;
     a.plan = plan; a.counter = counter;
-    moe_launch_pdl(k_route_plan, dim3(T), dim3(256), 0, s, a);
+    const int n_op = xop ? (T * (d.H / MOE_QK) + 7) / 8 : 0;
+    moe_launch_pdl(k_route_plan, dim3(T + n_op), dim3(256), 0, s, a);
     LAUNCH_COUNT(launches);
 }
 
