@@ -46,6 +46,14 @@ WORKLOADS = {
     "decode_b64_zipf": dict(B=64, zipf=True, name="config3_decode_b64_zipf"),
     "decode_b1": dict(B=1, zipf=False, name="config2_decode_b1"),
 }
+# further BASELINE configs, measured on one GPU by run_extra()
+EXTRA = {
+    "expert1": dict(B=1, name="config1_single_q4k_expert"),
+    "stack_b1": dict(B=1, name="config4_stack58_b1_1gpu"),
+    "stack_b8": dict(B=8, name="config4_stack58_b8_1gpu"),
+    "prefill4096": dict(B=4096, name="config5_prefill4096_1layer"),
+}
+Q4_DOWN_BYTES = H * (I // 256) * 144         # 8,257,536
 
 
 def peaks():
@@ -363,6 +371,176 @@ def run_ours(args):
         pg.destroy_process_group()
 
 
+def run_extra(args):
+    """Configs 1, 4 and 5 on one GPU (informational lines; the default bench
+    line is config 3).
+      expert1      one Q4_K expert (gate/up/down Q4_K) per call, routing given
+                   (moe_experts_forward_device, K = 1), 256 distinct experts in
+                   turn so that no call finds its weights in L2
+      stack_b*     the 58-layer stack (RMSNorm + MoE + residual per layer,
+                   down Q6_K / Q4_K alternating) through moe_forward_stack_device:
+                   20 layers are resident (about 137 GB) and a step runs them
+                   20 + 20 + 18 times; every layer's weights exceed L2, so the
+                   re-use changes nothing but the memory needed
+      prefill4096  4096 tokens through one layer in 64-token calls of
+                   moe_forward_device (the decode kernels; no tcgen05 path yet)"""
+    import torch
+    import flash_deepseek_b200 as F
+    W = EXTRA[args.workload]
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    g = torch.Generator(device="cpu").manual_seed(1234)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    peak, peak_kind = peaks()
+    clk = Clocks(0).__enter__()
+    extra = {}
+    if args.workload == "expert1":
+        cfg = F.MoeConfig(n_layers=1, max_tokens=1, top_k=1)
+        moe = F.MoE(cfg)
+        moe.init_layer_synthetic(0, seed=0, down_type=F.TYPE_Q4_K)
+        x = torch.randn(1, H, generator=g).to(dev)
+        out = torch.empty_like(x)
+        idx = torch.arange(E, dtype=torch.int32, device=dev).reshape(E, 1)
+        w1 = torch.ones(E, 1, dtype=torch.float32, device=dev)
+        stream = torch.cuda.ExternalStream(moe.stream, device=dev)
+        for e in range(args.warmup):
+            moe.experts_forward_device(0, x, 1, idx[e % E], w1[e % E], 1, out)
+        n = args.steps
+        torch.cuda.synchronize()
+        l0 = moe.kernel_launches
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for e in range(n):
+            moe.experts_forward_device(0, x, 1, idx[e % E], w1[e % E], 1, out)
+        b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b)
+        launches = moe.kernel_launches - l0
+        per_call = ms / n
+        bytes_call = 3 * GATE_BYTES + H * 4 + I * 4 * 2 + H * 4
+        value = n / (ms / 1e3)
+        roof = {"bound": "hbm", "kernel": "whole call (route given, gate/up, prep, down, combine)",
+                "achieved": round(bytes_call / (per_call / 1e3) / 1e9, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(bytes_call / (per_call / 1e3) / 1e9 / peak, 4), "peak_source": peak_kind,
+                "algorithmic_bytes_per_launch": bytes_call, "traffic": None}
+        unit, ms_step = "expert calls/s", per_call
+        e2e = None
+    elif args.workload.startswith("stack"):
+        B = W["B"]
+        n_res, seq = 20, [(0, 20), (0, 20), (0, 18)]
+        cfg = F.MoeConfig(n_layers=n_res, max_tokens=B)
+        moe = F.MoE(cfg)
+        for l in range(n_res):
+            moe.init_layer_synthetic(l, seed=0, down_type=F.TYPE_Q6_K if l % 2 == 0 else F.TYPE_Q4_K)
+        hs = [torch.randn(B, H, generator=g).to(dev) for _ in range(4)]
+        hid = torch.empty(B, H, device=dev)
+        stream = torch.cuda.ExternalStream(moe.stream, device=dev)
+
+        def step(i):
+            hid.copy_(hs[i % 4])
+            for f0, nl in seq:
+                moe.forward_stack_device(f0, nl, hid, B, stream=moe.stream)
+        with torch.cuda.stream(stream):
+            for i in range(args.warmup):
+                step(i)
+        torch.cuda.synchronize()
+        l0 = moe.kernel_launches
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        with torch.cuda.stream(stream):
+            for i in range(args.steps):
+                ev[i][0].record(stream)
+                step(i)
+                ev[i][1].record(stream)
+        torch.cuda.synchronize()
+        ms = sum(x.elapsed_time(y) for x, y in ev)
+        launches = moe.kernel_launches - l0
+        ms_step = ms / args.steps
+        value = B * args.steps / (ms / 1e3)
+        unit = "tokens/s"
+        # B = 1: every layer reads the router and exactly K + 1 = 9 distinct experts
+        layer_b = [ROUTER_BYTES + (K + 1) * (2 * GATE_BYTES + (DOWN_Q6_BYTES if l % 2 == 0 else Q4_DOWN_BYTES))
+                   for l in range(n_res)]
+        step_b = sum(sum(layer_b[f0:f0 + nl]) for f0, nl in seq)
+        roof = None
+        if B == 1:
+            roof = {"bound": "hbm", "kernel": "whole 58-layer step", "achieved": round(step_b / (ms_step / 1e3) / 1e9, 1),
+                    "peak": peak, "unit": "GB/s", "frac": round(step_b / (ms_step / 1e3) / 1e9 / peak, 4),
+                    "peak_source": peak_kind, "algorithmic_bytes_per_step": step_b, "traffic": None}
+        h_pin = hs[0].cpu().pin_memory().numpy()
+        lib = moe.lib
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        buf = h_pin.copy()
+        lib.moe_forward_stack(moe.ctx, 0, 20, buf.ctypes.data, B)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        n_e2e = max(2, args.steps // 4)
+        for i in range(n_e2e):
+            buf[:] = h_pin
+            for f0, nl in seq:
+                rc = lib.moe_forward_stack(moe.ctx, f0, nl, buf.ctypes.data, B)
+                if rc != 0:
+                    raise RuntimeError(lib.moe_last_error(moe.ctx))
+        e2e_s = time.perf_counter() - t0
+        e2e = {"value": round(B * n_e2e / e2e_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 3 * B * H * 4,
+               "d2h_bytes_per_step": 3 * B * H * 4, "timer": "host wall clock (synchronous calls)"}
+        extra = {"layers_resident": n_res, "layer_calls_per_step": 58}
+    else:  # prefill4096
+        B, chunk = 4096, 64
+        cfg = F.MoeConfig(n_layers=1, max_tokens=chunk)
+        moe = F.MoE(cfg)
+        moe.init_layer_synthetic(0, seed=0, down_type=F.TYPE_Q6_K)
+        xs = torch.randn(B, H, generator=g).to(dev)
+        out = torch.empty(B, H, device=dev)
+        stage_in = torch.empty(chunk, H, device=dev)
+        stage_out = torch.empty(chunk, H, device=dev)
+        idx = torch.empty(B, K, dtype=torch.int32, device=dev)
+        stream = torch.cuda.ExternalStream(moe.stream, device=dev)
+
+        def step(record_idx=False):
+            for c in range(B // chunk):
+                stage_in.copy_(xs[c * chunk:(c + 1) * chunk])
+                moe.forward_device(0, stage_in, chunk, stage_out,
+                                   d_idx=idx[c * chunk:(c + 1) * chunk] if record_idx else None, stream=moe.stream)
+                out[c * chunk:(c + 1) * chunk].copy_(stage_out)
+        with torch.cuda.stream(stream):
+            step(record_idx=True)
+            for i in range(max(1, args.warmup)):
+                step()
+        torch.cuda.synchronize()
+        n = max(1, min(args.steps, 5))
+        l0 = moe.kernel_launches
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            a.record(stream)
+            for i in range(n):
+                step()
+            b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b)
+        launches = moe.kernel_launches - l0
+        ms_step = ms / n
+        value = B * n / (ms / 1e3)
+        unit = "tokens/s"
+        flops = 2.0 * B * (K + 1) * (3 * H * I) + 2.0 * B * E * H
+        tf = flops / (ms_step / 1e3) / 1e12
+        roof = {"bound": "tensor", "kernel": "whole step (int8 mma.sync decode kernels, 64-token calls)",
+                "achieved": round(tf, 2), "peak": 1642.1, "unit": "TFLOP/s", "frac": round(tf / 1642.1, 5),
+                "peak_source": "measured bf16 burst (MEASURED_PEAKS.json)", "flops_per_step": flops,
+                "traffic": None}
+        e2e = None
+        extra = {"tokens_per_call": chunk, "calls_per_step": B // chunk}
+    clk.__exit__(None, None, None)
+    line = {"metric": METRIC, "value": round(value, 2), "unit": unit, "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "fp32 accumulation over exact int8 products",
+            "data": "synthetic: random-init N(0,0.02) weights quantized on device, N(0,1) tokens",
+            "config": dict({"workload": W["name"], "global_batch": W["B"], "hidden": H, "intermediate": I,
+                            "experts": E, "parallelism": "ep1"}, **extra),
+            "roofline": roof, "e2e": e2e, "gpu_launches": int(launches), "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+    moe.close()
+
+
 def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -389,7 +567,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--workload", default="decode_b64_zipf", choices=sorted(WORKLOADS))
+    ap.add_argument("--workload", default="decode_b64_zipf", choices=sorted(WORKLOADS) + sorted(EXTRA))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--experts", type=int, default=E,
@@ -397,7 +575,12 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
-    if args.impl == "reference":
+    if args.workload in EXTRA:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference arm times configs 2 and 3"}))
+            return
+        run_extra(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
