@@ -243,6 +243,20 @@ class MoE:
         self._check(self.lib.moe_route(self.ctx, _ptr(lg), _ptr(b), T, _ptr(idx), _ptr(w)), "moe_route")
         return idx, w
 
+    def prefill(self, layer: int, h_post):
+        """Many tokens through one layer on the tensor-core path: (out, idx, w)."""
+        h = _f32(h_post).reshape(-1, self.cfg.hidden)
+        T = h.shape[0]
+        out = np.empty_like(h)
+        idx = np.empty((T, self.cfg.top_k), np.int32)
+        w = np.empty((T, self.cfg.top_k), np.float32)
+        self._check(self.lib.moe_prefill(self.ctx, layer, _ptr(h), T, _ptr(out), _ptr(idx), _ptr(w)), "moe_prefill")
+        return out, idx, w
+
+    def prefill_device(self, layer: int, d_h, n_tokens: int, d_out, d_idx=None, d_w=None, stream=None):
+        self._check(self.lib.moe_prefill_device(self.ctx, layer, _ptr(d_h), n_tokens, _ptr(d_out), _ptr(d_idx),
+                                                _ptr(d_w), _ptr(stream)), "moe_prefill_device")
+
     def forward_stack(self, first_layer: int, n_layers: int, hidden):
         h = _f32(hidden).reshape(-1, self.cfg.hidden).copy()
         self._check(self.lib.moe_forward_stack(self.ctx, first_layer, n_layers, _ptr(h), h.shape[0]),

@@ -49,6 +49,8 @@ SIGNATURES = {
     "moe_route_hidden_noalloc": (C.c_int, [C.POINTER(MoeConfigC), _vp, _vp, _vp, C.c_int, _vp, _vp, _vp]),
     "moe_forward_stack_device": (C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_int, _vp]),
     "moe_forward_stack": (C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_int]),
+    "moe_prefill_device": (C.c_int, [_vp, C.c_int, _vp, C.c_int, _vp, _vp, _vp, _vp]),
+    "moe_prefill": (C.c_int, [_vp, C.c_int, _vp, C.c_int, _vp, _vp, _vp]),
     "moe_dequantize_row_q4_K": (C.c_int, [_vp, _vp, C.c_size_t]),
     "moe_dequantize_row_q6_K": (C.c_int, [_vp, _vp, C.c_size_t]),
     "moe_kernel_launches": (C.c_uint64, [_vp]),

@@ -98,6 +98,7 @@ struct moe_ctx {
         uint64_t kernels, last_use;
     };
     std::vector<Graph> graphs;
+    MoePrefillWs pf;  // prefill workspace, allocated on first use
     std::vector<std::array<const void *, 5>> seen;  // signatures run once eagerly (attributes set)
     bool use_graphs = true;
     uint64_t clock = 0;
@@ -280,6 +281,7 @@ void moe_destroy(moe_ctx *c) {
     if (c->comm) moe_nccl()->CommDestroy(c->comm);
     for (cudaEvent_t e : c->ev) cudaEventDestroy(e);
     for (auto &g : c->graphs) cudaGraphExecDestroy(g.exec);
+    moe_prefill_free(c->pf);
     for (auto &L : c->layers) {
         cudaFree(L.experts);
         cudaFree(L.router);
@@ -840,6 +842,64 @@ int moe_route(moe_ctx *c, const float *logits, const float *bias, int T, int *id
     CK(cudaMemcpyAsync(idx, c->idx, sizeof(int) * T * K, cudaMemcpyDeviceToHost, c->stream));
     CK(cudaMemcpyAsync(w, c->wts, sizeof(float) * T * K, cudaMemcpyDeviceToHost, c->stream));
     CK(cudaStreamSynchronize(c->stream));
+    return MOE_OK;
+}
+
+int moe_prefill_device(moe_ctx *c, int layer, const float *d_h, int T, float *d_out, int *d_idx, float *d_w,
+                       void *stream) {
+    if (!c) return MOE_ERR_ARG;
+    if (T <= 0 || !d_h || !d_out) return fail(c, MOE_ERR_ARG, "moe_prefill_device: need n_tokens >= 1 and buffers");
+    int rc = check_layer(c, layer);
+    if (rc) return rc;
+    if (c->world > 1) return fail(c, MOE_ERR_STATE, "moe_prefill runs on one GPU (world_size 1)");
+    CK(cudaSetDevice(c->device));
+    if (moe_prefill_alloc(c->pf, c->d, T))
+        return fail(c, MOE_ERR_CUDA, "prefill workspace for %d tokens could not be allocated", T);
+    cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    MoeLayerDev &L = c->layers[layer];
+    const MoeDims &d = c->d;
+    moe_launch_router_logits(L.router, d_h, T, d.H, d.E, c->pf.part, d.H / MOE_QK, c->pf.logits, c->pf.counters, s,
+                             &c->launches);
+    moe_launch_route_and_plan(d, nullptr, 0, c->pf.logits, L.bias, L.logit_bias, 0, nullptr, nullptr, T, c->pf.idx,
+                              c->pf.w, d_h, nullptr, 1, 0, c->pf.plan, c->counter, s, &c->launches);
+    moe_launch_prefill_experts(d, L, c->pf, d_h, T, d_out, s, &c->launches);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(c, MOE_ERR_CUDA, "prefill launch: %s", cudaGetErrorString(e));
+    if (d_idx) CK(cudaMemcpyAsync(d_idx, c->pf.idx, sizeof(int) * T * d.K, cudaMemcpyDeviceToDevice, s));
+    if (d_w) CK(cudaMemcpyAsync(d_w, c->pf.w, sizeof(float) * T * d.K, cudaMemcpyDeviceToDevice, s));
+    return MOE_OK;
+}
+
+int moe_prefill(moe_ctx *c, int layer, const float *h, int T, float *out, int *idx_out, float *w_out) {
+    if (!c) return MOE_ERR_ARG;
+    if (T <= 0 || !h || !out) return fail(c, MOE_ERR_ARG, "moe_prefill: need n_tokens >= 1 and buffers");
+    CK(cudaSetDevice(c->device));
+    const size_t n = (size_t)T * c->d.H;
+    float *dh = nullptr, *dout = nullptr;
+    CK(cudaMalloc((void **)&dh, n * sizeof(float)));
+    if (cudaMalloc((void **)&dout, n * sizeof(float)) != cudaSuccess) {
+        cudaFree(dh);
+        return fail(c, MOE_ERR_CUDA, "moe_prefill: out of memory");
+    }
+    int rc = MOE_OK;
+    if (cudaMemcpyAsync(dh, h, n * sizeof(float), cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
+        rc = fail(c, MOE_ERR_CUDA, "moe_prefill: copy in");
+    if (!rc) rc = moe_prefill_device(c, layer, dh, T, dout, nullptr, nullptr, nullptr);
+    if (!rc && cudaMemcpyAsync(out, dout, n * sizeof(float), cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
+        rc = fail(c, MOE_ERR_CUDA, "moe_prefill: copy out");
+    if (!rc && idx_out)
+        cudaMemcpyAsync(idx_out, c->pf.idx, sizeof(int) * T * c->d.K, cudaMemcpyDeviceToHost, c->stream);
+    if (!rc && w_out) cudaMemcpyAsync(w_out, c->pf.w, sizeof(float) * T * c->d.K, cudaMemcpyDeviceToHost, c->stream);
+    cudaStreamSynchronize(c->stream);
+    cudaFree(dh);
+    cudaFree(dout);
+    if (rc) return rc;
+    int errflag = 0;
+    CK(cudaMemcpy(&errflag, c->pf.plan.error, sizeof(int), cudaMemcpyDeviceToHost));
+    if (errflag) {
+        cudaMemset(c->pf.plan.error, 0, sizeof(int));
+        return fail(c, errflag == 1 ? MOE_ERR_ARG : MOE_ERR_CUDA, "prefill error code 0x%x", errflag);
+    }
     return MOE_OK;
 }
 

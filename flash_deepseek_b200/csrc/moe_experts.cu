@@ -658,6 +658,20 @@ static int map3(CUtensorMap *m, const void *base, uint64_t row_bytes, uint64_t r
     return r == CUDA_SUCCESS ? 0 : -(int)r - 100;
 }
 
+int moe_make_map_f16_sw128(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, uint32_t box_cols,
+                           uint32_t box_rows) {
+    moe_encode_tiled_fn fn = encode_fn();
+    if (!fn) return -1;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, es,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : -(int)r - 100;
+}
+
 int moe_make_layer_maps(MoeLayerDev &L, const MoeDims &d) {
     const int H = d.H, I = d.I, NBh = H / MOE_QK, NBi = I / MOE_QK;
     const uint64_t slots = (uint64_t)L.n_local + 1;

@@ -93,6 +93,25 @@ void moe_launch_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan
                      int max_chunks, cudaStream_t s, uint64_t *launches);
 // TMA maps of a layer (after its weights are allocated); 0 = ok
 int moe_make_layer_maps(MoeLayerDev &L, const MoeDims &d);
+// 2-D map over a row-major fp16 matrix [rows][cols] with 128-byte swizzle
+int moe_make_map_f16_sw128(CUtensorMap *m, const void *base, uint64_t cols, uint64_t rows, uint32_t box_cols,
+                           uint32_t box_rows);
+
+// ---- prefill (moe_prefill.cu) ----------------------------------------------
+struct MoePrefillWs {
+    int cap = 0;                 // tokens
+    float *part = nullptr, *logits = nullptr, *w = nullptr, *eo = nullptr;
+    int *idx = nullptr, *counters = nullptr;
+    __half *xg = nullptr, *act = nullptr;
+    MoePlan plan{};
+    CUtensorMap tm_xg, tm_act;
+};
+int moe_prefill_alloc(MoePrefillWs &ws, const MoeDims &d, int T);
+void moe_prefill_free(MoePrefillWs &ws);
+// plan + gather + the two tcgen05 GEMMs + combine, after ws.idx / ws.w hold
+// the routing of T tokens
+void moe_launch_prefill_experts(const MoeDims &d, const MoeLayerDev &L, MoePrefillWs &ws, const float *x, int T,
+                                float *out, cudaStream_t s, uint64_t *launches);
 void moe_launch_combine(const MoeDims &d, const MoePlan &plan, const float *eo, int T, int include_routed,
                         int include_shared, const float *residual, float *out, cudaStream_t s, uint64_t *launches);
 void moe_launch_rmsnorm(const float *x, const float *w, float *y, int T, int H, float eps, cudaStream_t s,

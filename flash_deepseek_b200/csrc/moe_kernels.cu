@@ -325,12 +325,15 @@ void moe_launch_synth_f32(uint64_t seed, uint64_t stream, size_t n, double sigma
 #define RL_WPAD (RL_KS + 4)
 #define RL_MAX_SPLIT 32  // partial sums loaded together by the reducing CTA
 __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__ Wr, const float *__restrict__ x,
-                                                       int T, int H, int E, float *__restrict__ part,
+                                                       int T_all, int H, int E, float *__restrict__ part,
                                                        float *__restrict__ logits, int *__restrict__ counters) {
     extern __shared__ float sm[];
     float *Ws = sm;                       // [32 experts][RL_WPAD] row-major (k contiguous)
     float *xt = sm + 32 * RL_WPAD;        // [RL_KS][64] (tokens contiguous)
     const int e0 = blockIdx.x * 32, split = blockIdx.y, k0 = split * RL_KS;
+    // token chunk z: tokens [64 z, 64 z + T) of T_all
+    const int tz0 = blockIdx.z * 64, T = min(64, T_all - tz0);
+    x += (size_t)tz0 * H;
     const int tid = threadIdx.x;
     // W tile: 8 coalesced float4 loads in flight per thread, then float4 stores
     {
@@ -385,7 +388,7 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
                 if (e >= E) continue;
 #pragma unroll
                 for (int t = 0; t < 4; t++)
-                    if (t < T) part[((size_t)split * T + t) * E + e] = accs[u][t];
+                    if (t < T) part[((size_t)split * T_all + tz0 + t) * E + e] = accs[u][t];
             }
         }
     } else {
@@ -423,8 +426,8 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
     for (int u = 0; u < 4; u++) {
         const int e = e0 + 4 * eg + u;
         if (e >= E) continue;
-        if (t0ok) part[((size_t)split * T + tg) * E + e] = acc[u][0];
-        if (t1ok) part[((size_t)split * T + tg + 32) * E + e] = acc[u][1];
+        if (t0ok) part[((size_t)split * T_all + tz0 + tg) * E + e] = acc[u][0];
+        if (t1ok) part[((size_t)split * T_all + tz0 + tg + 32) * E + e] = acc[u][1];
     }
     }
     // The last split CTA of this expert group sums the partials in split
@@ -432,7 +435,7 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
     __shared__ int last;
     __threadfence();
     __syncthreads();
-    if (tid == 0) last = atomicAdd(&counters[blockIdx.x], 1) == (int)gridDim.y - 1;
+    if (tid == 0) last = atomicAdd(&counters[blockIdx.z * gridDim.x + blockIdx.x], 1) == (int)gridDim.y - 1;
     __syncthreads();
     if (!last) return;
     __threadfence();
@@ -444,20 +447,20 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
         float pv[RL_MAX_SPLIT];
 #pragma unroll
         for (int sp = 0; sp < RL_MAX_SPLIT; sp++)
-            pv[sp] = sp < ns ? __ldcg(part + ((size_t)sp * T + t) * E + e) : 0.0f;
+            pv[sp] = sp < ns ? __ldcg(part + ((size_t)sp * T_all + tz0 + t) * E + e) : 0.0f;
         float v = 0.0f;
 #pragma unroll
         for (int sp = 0; sp < RL_MAX_SPLIT; sp++)
             if (sp < ns) v += pv[sp];
-        for (int sp = RL_MAX_SPLIT; sp < ns; sp++) v += __ldcg(part + ((size_t)sp * T + t) * E + e);
-        logits[(size_t)t * E + e] = v;
+        for (int sp = RL_MAX_SPLIT; sp < ns; sp++) v += __ldcg(part + ((size_t)sp * T_all + tz0 + t) * E + e);
+        logits[(size_t)(tz0 + t) * E + e] = v;
     }
-    if (tid == 0) counters[blockIdx.x] = 0;
+    if (tid == 0) counters[blockIdx.z * gridDim.x + blockIdx.x] = 0;
 }
 
 void moe_launch_router_logits(const float *Wr, const float *x, int T, int H, int E, float *part, int n_split,
                               float *logits, int *counters, cudaStream_t s, uint64_t *launches) {
-    dim3 grid((E + 31) / 32, n_split);
+    dim3 grid((E + 31) / 32, n_split, (T + 63) / 64);
     const size_t smem = sizeof(float) * (32 * RL_WPAD + RL_KS * 64);
     static bool attr = false;
     if (!attr) {

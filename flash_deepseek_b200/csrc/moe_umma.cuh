@@ -1,0 +1,98 @@
+// moe_umma.cuh -- the fifth-generation tensor-core (tcgen05) pieces used by
+// the prefill GEMMs: tensor-memory allocation, shared-memory matrix
+// descriptors for K-major 128-byte-swizzled tiles, the instruction
+// descriptor of kind::f16, the MMA, its commit to an mbarrier, and the
+// tensor-memory loads of the epilogue.  Field layouts follow the PTX ISA for
+// sm_100a (the same encodings CUTLASS writes in cute/arch/mma_sm100_desc.hpp).
+#pragma once
+#include <stdint.h>
+
+// ---------------------------------------------------------------------------
+// Shared-memory tiles.  A K-major operand tile of R rows x 64 fp16 (one
+// 128-byte line per row) is stored as R/8 atoms of 8 rows x 128 B (1024 B
+// apart); inside an atom the 16-byte chunk c of row r sits at chunk
+// c ^ (r % 8) (the 128-byte swizzle, which TMA's SWIZZLE_128B writes too).
+// Tiles start on a 1024-byte boundary.
+// ---------------------------------------------------------------------------
+__host__ __device__ __forceinline__ uint32_t sw128_offset(int row, int k) {
+    const int chunk = (k >> 3) ^ (row & 7);
+    return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + chunk * 16 + (k & 7) * 2);
+}
+
+// Matrix descriptor: start address >> 4 in [0,14), leading byte offset >> 4
+// in [16,30) (unused by swizzled K-major tiles: 1), stride byte offset >> 4
+// in [32,46) (1024 B between 8-row atoms), version 1 in [46,48), layout type
+// in [61,64) (2 = 128-byte swizzle).
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
+    uint64_t d = (uint64_t)((smem_addr >> 4) & 0x3FFFu);
+    d |= (uint64_t)1u << 16;
+    d |= (uint64_t)(1024u >> 4) << 32;
+    d |= (uint64_t)1u << 46;
+    d |= (uint64_t)2u << 61;
+    return d;
+}
+
+// Instruction descriptor of kind::f16: D fp32 (bits 4-5 = 1), A and B fp16
+// (formats 0), both K-major, N >> 3 in [17,23), M >> 4 in [24,29).
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int M, int N) {
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ uint32_t umma_smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, one elected thread.
+__device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t desc_a, uint64_t desc_b, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}\n" ::"r"(tmem_d),
+        "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate), "r"(0u)
+        : "memory");
+}
+
+// Arrives on `bar` once every MMA issued so far by this thread has completed.
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
+                     umma_smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+}
+__device__ __forceinline__ void tmem_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+}
+
+// Whole warp: allocate / free `ncols` tensor-memory columns (power of two,
+// >= 32); the base address is written to *dst (shared memory).
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(umma_smem_u32(dst)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void tmem_free(uint32_t base, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(base), "r"(ncols) : "memory");
+}
+
+// 16 consecutive fp32 columns of this thread's lane (warp w reads lanes
+// 32 (w % 4) .. + 31; addr = base + (lane0 << 16) + column).
+__device__ __forceinline__ void tmem_ld16(uint32_t addr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(addr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy reads (the tensor core reading an operand tile).
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
