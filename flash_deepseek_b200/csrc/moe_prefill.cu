@@ -15,13 +15,15 @@
 // Differences from the reference's fp32 dot: weights and activations are
 // rounded to fp16 (11-bit significands) before the fp32-accumulated product.
 //
-// GEMM CTA: warp 0 issues TMA copies (raw Q4_K / Q6_K tiles of one
-// super-block, and the pairs' 64-column activation slices with the 128-byte
-// swizzle), warp 1 owns tensor memory and issues the MMAs from one thread,
-// warps 2-5 dequantize one weight row each into the swizzled A tile and,
-// after the last k step, run the epilogue from tensor memory.  All hand-offs
-// are mbarriers; every wait gives up after about a second and records an
-// error instead of hanging.
+// GEMM CTA: warp 0 streams the raw Q4_K / Q6_K tiles, one super-block per
+// stage, several stages ahead; warp 2 streams the pairs' 64-column
+// activation slices (TMA with the 128-byte swizzle); warp 1 owns tensor
+// memory and issues the MMAs from one thread; 16 warps dequantize (four
+// lanes per weight row) into the swizzled A tile and, after the last k step,
+// run the epilogue from tensor memory.  All hand-offs are mbarriers; every
+// wait gives up after about a second and records an error instead of
+// hanging, and a producer that gives up first waits (bounded) for the copies
+// it issued.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <stdio.h>
@@ -31,14 +33,21 @@
 #include "moe_internal.h"
 #include "moe_umma.cuh"
 
-#define PF_TILE 128                // pairs per tile (MMA N) and weight rows per tile (MMA M)
-#define PF_NS 4                    // k-atom stages (64 columns of K each)
-#define PF_ATOM 16384              // 128 rows x 128 B
-#define PF_RAW_NS 2                // raw super-block stages
+#define PF_TILE 128                // weight rows per tile (MMA M)
+#define PF_TILE_N 256              // pairs per tile (MMA N <= 256)
+#define PF_NS 3                    // k-atom stages (64 columns of K each)
+#define PF_BATOM (PF_TILE_N * 128) // B atom: 256 pair rows x 128 B
+#define PF_ATOM 16384              // A atom: 128 rows x 128 B
+#define PF_RAW_NS_Q4 3             // raw super-block stages (Q4_K tiles)
+#define PF_RAW_NS_Q6 2             // (Q6_K tiles)
+#define PF_RAW_NS_MAX 3
 #define PF_RAW_Q4 (128 * 144)      // 128 Q4_K rows of one super-block
 #define PF_RAW_Q6 (128 * 192 + 128 * 16)
-#define PF_THREADS 192
+#define PF_DQ_WARPS 16                              // dequantize + epilogue (warps 2 ..)
+#define PF_DQ_WARP0 3                               // warps 0-2: weight TMA, MMA, activation TMA
+#define PF_THREADS (32 * (PF_DQ_WARP0 + PF_DQ_WARPS))
 #define PF_WAIT_CYCLES (1ll << 31)
+#define PF_SUSPEND_NS 1000000u    // a waiting thread sleeps up to 1 ms per try (woken when the phase completes)
 #define PF_ERR_TIMEOUT 0x7200
 
 #define LAUNCH_COUNT(p) \
@@ -61,13 +70,23 @@ __device__ __forceinline__ bool pf_wait(uint64_t *b, uint32_t parity) {
     for (;;) {
         uint32_t ok;
         asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+            " selp.u32 %0, 1, 0, p;\n}\n"
             : "=r"(ok)
-            : "r"(umma_smem_u32(b)), "r"(parity)
+            : "r"(umma_smem_u32(b)), "r"(parity), "r"(PF_SUSPEND_NS)
             : "memory");
         if (ok) return true;
         if (clock64() - t0 > PF_WAIT_CYCLES) return false;
     }
+}
+// after a producer gave up: wait (bounded) for the copies it issued into
+// the last `ns` stages of a ring, so that none lands after the CTA exits
+__device__ __forceinline__ void pf_drain(uint64_t *full, int issued, int ns) {
+    for (int k = issued > ns ? issued - ns : 0; k < issued; k++) pf_wait(&full[k % ns], (k / ns) & 1);
+}
+// the same, agreed by the whole warp (a lane that gave up fails them all)
+__device__ __forceinline__ bool pf_wait_warp(uint64_t *b, uint32_t parity) {
+    return __all_sync(0xffffffffu, pf_wait(b, parity));
 }
 __device__ __forceinline__ void pf_tma3(void *dst, const CUtensorMap *m, int x, int y, int z, uint64_t *bar) {
     asm volatile(
@@ -114,7 +133,7 @@ __global__ void __launch_bounds__(1024) k_prefill_plan(MoeDims d, const int *__r
             off[e] = a;
             toff[e] = b;
             a += cnt[e];
-            b += (cnt[e] + PF_TILE - 1) / PF_TILE;
+            b += (cnt[e] + PF_TILE_N - 1) / PF_TILE_N;
         }
         off[NE] = a;
         toff[NE] = b;
@@ -123,10 +142,10 @@ __global__ void __launch_bounds__(1024) k_prefill_plan(MoeDims d, const int *__r
     }
     __syncthreads();
     for (int e = threadIdx.x; e < NE; e += blockDim.x)
-        for (int c = 0; c * PF_TILE < cnt[e]; c++) {
+        for (int c = 0; c * PF_TILE_N < cnt[e]; c++) {
             plan.chunk_expert[toff[e] + c] = e;
-            plan.chunk_pair0[toff[e] + c] = off[e] + c * PF_TILE;
-            plan.chunk_ntok[toff[e] + c] = min(PF_TILE, cnt[e] - c * PF_TILE);
+            plan.chunk_pair0[toff[e] + c] = off[e] + c * PF_TILE_N;
+            plan.chunk_ntok[toff[e] + c] = min(PF_TILE_N, cnt[e] - c * PF_TILE_N);
         }
     for (int p = threadIdx.x; p < T * K; p += blockDim.x) {
         const int t = p / K, k = p % K, e = idx[p];
@@ -161,95 +180,155 @@ __global__ void __launch_bounds__(256) k_prefill_gather(const float *__restrict_
 }
 
 // ===========================================================================
-// dequantization of one weight row into one 64-column A atom (thread = row)
+// dequantization into one 64-column A atom, in fp16 arithmetic with exact
+// intermediate steps.  Four lanes share a weight row: lane t holds, for a
+// whole super-block, the bytes the repacked layouts give MMA lane t and
+// writes 16 of the row's 64 fp16 values per atom.
+//   - A byte permute puts two weight bytes under the fp16 exponent of 1024
+//     (0x64 high bytes); masking keeps the low nibble (1024 + q) or the high
+//     nibble in place (1024 + 16 q), exact.
+//   - Q4_K, w = d*sc*q - dmin*m: p = fma(1024 + q, sc, -1024 sc) = q*sc
+//     exactly (<= 945; the high nibble uses sc/16 and -64 sc); then
+//     fma(d, p, -dm_hi) - dm_lo with dmin*m = dm_hi + dm_lo split into two
+//     fp16 values (exact), so the result is rounded on the scale of w itself.
+//   - Q6_K, w = d*sc*(q - 32): (1024 + q) - 1056 = q - 32 exactly; then
+//     fma(q - 32, fs_hi, (q - 32) * fs_lo) with d*sc = fs_hi + fs_lo.
+// The per-sub-block constants of an atom (8 fp16 pairs) are computed once
+// per super-block by the quad lane that owns the atom and read back from
+// shared memory by the whole quad.
+// A warp's lanes cover rows 8w + brev3(0..7) (bit-reversed), so the two rows
+// of a quarter-warp differ in row bit 2 and the four of a half-warp in row
+// bits 1-2: the 16-byte (Q4_K) and 8-byte (Q6_K) stores into the 128-byte
+// swizzled atom then hit distinct banks.
 // ===========================================================================
-// Q4_K, repacked block (header + transposed qs): atom a = weights
-// [64 a, 64 a + 64) of the super-block: low nibbles of old bytes 32 a + l
-// (sub-block 2a) and high nibbles (sub-block 2a + 1); old byte 32 a + 8 t + i
-// sits at 16 + 32 t + 8 a + i.
-__device__ __forceinline__ void pf_deq_q4(const uint8_t *blk, int a, uint8_t *atom, int row) {
-    const uint4 hd = *reinterpret_cast<const uint4 *>(blk);
-    const float d = __half2float(__ushort_as_half((uint16_t)(hd.x & 0xFFFFu)));
-    const float dmin = __half2float(__ushort_as_half((uint16_t)(hd.x >> 16)));
-    const uint8_t *q = blk + 4;  // 12 scale bytes (get_scale_min_k4, quant.c:26-34)
-    int sc0, m0, sc1, m1;
-    {
-        const int j0 = 2 * a, j1 = 2 * a + 1;
-        if (j0 < 4) { sc0 = q[j0] & 63; m0 = q[j0 + 4] & 63; }
-        else { sc0 = (q[j0 + 4] & 0xF) | ((q[j0 - 4] >> 6) << 4); m0 = (q[j0 + 4] >> 4) | ((q[j0] >> 6) << 4); }
-        if (j1 < 4) { sc1 = q[j1] & 63; m1 = q[j1 + 4] & 63; }
-        else { sc1 = (q[j1 + 4] & 0xF) | ((q[j1 - 4] >> 6) << 4); m1 = (q[j1 + 4] >> 4) | ((q[j1] >> 6) << 4); }
-    }
-    const float ds0 = d * (float)sc0, dm0 = dmin * (float)m0, ds1 = d * (float)sc1, dm1 = dmin * (float)m1;
-#pragma unroll
-    for (int t = 0; t < 4; t++) {
-        const uint2 wv = *reinterpret_cast<const uint2 *>(blk + 16 + 32 * t + 8 * a);
-        const uint32_t wd[2] = {wv.x, wv.y};
-        uint32_t lo[4], hi[4];
-#pragma unroll
-        for (int h = 0; h < 2; h++)
-#pragma unroll
-            for (int b = 0; b < 4; b += 2) {
-                const uint32_t q0 = (wd[h] >> (8 * b)) & 0xFFu, q1 = (wd[h] >> (8 * b + 8)) & 0xFFu;
-                lo[2 * h + b / 2] = pf_h2(fmaf(pf_i2f(q0 & 0xFu), ds0, -dm0), fmaf(pf_i2f(q1 & 0xFu), ds0, -dm0));
-                hi[2 * h + b / 2] = pf_h2(fmaf(pf_i2f(q0 >> 4), ds1, -dm1), fmaf(pf_i2f(q1 >> 4), ds1, -dm1));
-            }
-        *reinterpret_cast<uint4 *>(atom + sw128_offset(row, 8 * t)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-        *reinterpret_cast<uint4 *>(atom + sw128_offset(row, 32 + 8 * t)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-    }
+#define PF_CONST_ROW 144  // bytes per quad: 4 atoms x 32 B + 16 B padding (distinct banks for two quads)
+
+__device__ __forceinline__ uint32_t pf_h2u(__half2 h) { return *reinterpret_cast<const uint32_t *>(&h); }
+__device__ __forceinline__ __half2 pf_u2h(uint32_t u) { return *reinterpret_cast<const __half2 *>(&u); }
+__device__ __forceinline__ uint32_t pf_dup(float x) { return pf_h2u(__float2half2_rn(x)); }
+// (hi, lo) fp16 pair of an fp32 value with <= 22 significant bits: hi + lo == x
+__device__ __forceinline__ void pf_split(float x, uint32_t &hi, uint32_t &lo) {
+    const float h = __half2float(__float2half_rn(x));
+    hi = pf_dup(h);
+    lo = pf_dup(x - h);
 }
 
-// Q6_K, repacked planes: rq = this row's 192-byte Q part of the super-block
-// (lane chunk t: per half h, ql words w at 24 h + 4 w, qh words at
-// 24 h + 16 + 4 w', high bit of every qh pair stored inverted), sc = its 16
-// scales, d = its fp16 d.  Atom a covers weights [64 a, 64 a + 64).
-__device__ __forceinline__ void pf_deq_q6(const uint8_t *rq, const int8_t *sc, float d, int a, uint8_t *atom,
-                                          int row) {
-    const int h = a >> 1, wp = a & 1;
+// scale and min of sub-block J of a Q4_K block (get_scale_min_k4,
+// quant.c:26-34); h.y, h.z, h.w = the 12 scale bytes
+template <int J>
+__device__ __forceinline__ void q4_scale_min(uint4 h, int &sc, int &m) {
+    const uint32_t s[3] = {h.y, h.z, h.w};
+#define PF_B(k) ((int)((s[(k) >> 2] >> (8 * ((k) & 3))) & 0xFFu))
+    if (J < 4) {
+        sc = PF_B(J) & 63;
+        m = PF_B(J + 4) & 63;
+    } else {
+        sc = (PF_B(J + 4) & 0xF) | ((PF_B(J - 4) >> 6) << 4);
+        m = (PF_B(J + 4) >> 4) | ((PF_B(J) >> 6) << 4);
+    }
+#undef PF_B
+}
+
+// the constants of Q4_K atom t (sub-blocks 2t, 2t + 1):
+// {sc0, -1024 sc0, -dm0_hi, -dm0_lo, sc1/16, -64 sc1, -dm1_hi, -dm1_lo}
+__device__ __forceinline__ void pf_q4_consts(uint4 h, int t, uint32_t (&c)[8]) {
+    const float dmin = __half2float(__ushort_as_half((uint16_t)(h.x >> 16)));
+    int sc0 = 0, m0 = 0, sc1 = 0, m1 = 0;
+    if (t == 0) { q4_scale_min<0>(h, sc0, m0); q4_scale_min<1>(h, sc1, m1); }
+    else if (t == 1) { q4_scale_min<2>(h, sc0, m0); q4_scale_min<3>(h, sc1, m1); }
+    else if (t == 2) { q4_scale_min<4>(h, sc0, m0); q4_scale_min<5>(h, sc1, m1); }
+    else { q4_scale_min<6>(h, sc0, m0); q4_scale_min<7>(h, sc1, m1); }
+    c[0] = pf_dup((float)sc0);
+    c[1] = pf_dup(-1024.0f * (float)sc0);
+    pf_split(-dmin * (float)m0, c[2], c[3]);
+    c[4] = pf_dup(0.0625f * (float)sc1);
+    c[5] = pf_dup(-64.0f * (float)sc1);
+    pf_split(-dmin * (float)m1, c[6], c[7]);
+}
+
+// two weights: fp16 pair (1024 + v) or (1024 + 16 v) -> d * sc * v - dm
+__device__ __forceinline__ uint32_t pf_q4_pair(uint32_t x, __half2 d2, const uint32_t *c) {
+    const __half2 p = __hfma2(pf_u2h(x), pf_u2h(c[0]), pf_u2h(c[1]));  // v * sc, exact
+    return pf_h2u(__hadd2(__hfma2(p, d2, pf_u2h(c[2])), pf_u2h(c[3])));
+}
+
+// Q4_K atom a: low nibbles of old bytes 32 a + l (sub-block 2a) and high
+// nibbles (2a + 1); the lane's words w0, w1 hold old bytes 32 a + 8 t + i,
+// i.e. k = 64 a + 8 t + i (atom chunk t, byte offset oL) and
+// 64 a + 32 + 8 t + i (chunk 4 + t, oH).
+__device__ __forceinline__ void pf_deq_q4(uint32_t w0, uint32_t w1, __half2 d2, const uint32_t (&c)[8], uint8_t *atom,
+                                          uint32_t oL, uint32_t oH) {
+    const uint32_t wd[2] = {w0, w1};
+    uint32_t lo[4], hi[4];
 #pragma unroll
-    for (int t = 0; t < 4; t++)
+    for (int h = 0; h < 2; h++) {
+        const uint32_t x01 = __byte_perm(wd[h], 0x64u, 0x4140u);  // bytes 0, 1 under 0x64
+        const uint32_t x23 = __byte_perm(wd[h], 0x64u, 0x4342u);
+        lo[2 * h] = pf_q4_pair(x01 & 0xFF0FFF0Fu, d2, c);
+        lo[2 * h + 1] = pf_q4_pair(x23 & 0xFF0FFF0Fu, d2, c);
+        hi[2 * h] = pf_q4_pair(x01 & 0xFFF0FFF0u, d2, c + 4);
+        hi[2 * h + 1] = pf_q4_pair(x23 & 0xFFF0FFF0u, d2, c + 4);
+    }
+    *reinterpret_cast<uint4 *>(atom + oL) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    *reinterpret_cast<uint4 *>(atom + oH) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+}
+
+// the constants of Q6_K atom t (sub-blocks 4t .. 4t + 3): {fs_hi, fs_lo} x 4
+// with fs = d * sc (exact in fp32)
+__device__ __forceinline__ void pf_q6_consts(float d6, uint32_t sc4, uint32_t (&c)[8]) {
 #pragma unroll
-        for (int g = 0; g < 2; g++) {
-            const uint32_t hq = *reinterpret_cast<const uint32_t *>(rq + 48 * t + 24 * h + 16 + 4 * g) ^ 0xAAAAAAAAu;
+    for (int u = 0; u < 4; u++) pf_split(d6 * (float)(int8_t)(sc4 >> (8 * u)), c[2 * u], c[2 * u + 1]);
+}
+
+// Q6_K atom A (sub-blocks 4A .. 4A + 3): q = this lane's 12 words of the row
+// (per half h: ql words at 6h + w, qh words at 6h + 4 + w', the high bit of
+// every qh pair stored inverted); it holds k = 16 s + 4 t + i of sub-block s.
+// With the inverted bit the 6-bit field nib | qh2 << 4 is q ^ 32; one more
+// xor restores q.  o[s4] = byte offset of k = 16 s4 + 4 t in the atom.
+template <int A>
+__device__ __forceinline__ void pf_deq_q6(const uint32_t (&q)[12], const uint32_t (&c)[8], uint8_t *atom,
+                                          const uint32_t (&o)[4]) {
+    constexpr int h = A >> 1;
+    const __half2 off = pf_u2h(0x64206420u);  // 1056 = 1024 + 32
 #pragma unroll
-            for (int u = 0; u < 2; u++) {
-                const uint32_t W = *reinterpret_cast<const uint32_t *>(rq + 48 * t + 24 * h + 8 * u + 4 * g);
-                const int which = 2 * wp + u;
-                const float f = d * (float)sc[8 * h + 2 * which + g];
-                float v[4];
-#pragma unroll
-                for (int bb = 0; bb < 4; bb++) {
-                    const uint32_t q6 = ((W >> (8 * bb + 4 * wp)) & 0xFu) | (((hq >> (8 * bb + 2 * which)) & 3u) << 4);
-                    v[bb] = f * (pf_i2f(q6) - 32.0f);
-                }
-                const int c = 4 * u + 2 * g + (t >> 1);
-                *reinterpret_cast<uint2 *>(atom + sw128_offset(row, 8 * c) + 8 * (t & 1)) =
-                    make_uint2(pf_h2(v[0], v[1]), pf_h2(v[2], v[3]));
-            }
-        }
+    for (int s4 = 0; s4 < 4; s4++) {
+        const int sp = 4 * (A & 1) + s4, f = sp >> 1;
+        const uint32_t W = q[6 * h + s4];
+        const uint32_t Hq = q[6 * h + 4 + (s4 & 1)];
+        const uint32_t nib = (sp < 4 ? W : W >> 4) & 0x0F0F0F0Fu;
+        const uint32_t hb = (2 * f <= 4 ? Hq << (4 - 2 * f) : Hq >> (2 * f - 4)) & 0x30303030u;
+        const uint32_t q6 = nib | (hb ^ 0x20202020u);  // four values q in bytes
+        const __half2 fh = pf_u2h(c[2 * s4]), fl = pf_u2h(c[2 * s4 + 1]);
+        const __half2 v01 = __hsub2(pf_u2h(__byte_perm(q6, 0x64u, 0x4140u)), off);  // q - 32, exact
+        const __half2 v23 = __hsub2(pf_u2h(__byte_perm(q6, 0x64u, 0x4342u)), off);
+        *reinterpret_cast<uint2 *>(atom + o[s4]) = make_uint2(pf_h2u(__hfma2(v01, fh, __hmul2(v01, fl))),
+                                                              pf_h2u(__hfma2(v23, fh, __hmul2(v23, fl))));
+    }
 }
 
 // ===========================================================================
 // GEMM.  MODE 0: gate/up (Q4_K) -> act (fp16, SwiGLU); 1: down Q4_K -> eo;
-// 2: down Q6_K -> eo.  blockIdx.x = tile (expert, <= 128 pairs), blockIdx.y
-// = row block.
+// 2: down Q6_K -> eo.  blockIdx.x = row block, blockIdx.y = tile (expert,
+// <= 256 pairs): the CTAs resident at one time work on a few tiles, so each
+// tile's activation slices are read from DRAM once and then hit in L2.
 // ===========================================================================
 template <int MODE>
 __global__ void __launch_bounds__(PF_THREADS, 1)
     k_prefill_gemm(MoeDims d, const __grid_constant__ MoeLayerDev L, MoePlan plan,
                    const __grid_constant__ CUtensorMap tmB, __half *__restrict__ act, float *__restrict__ eo) {
     constexpr int RAW = MODE == 2 ? PF_RAW_Q6 : PF_RAW_Q4;
+    constexpr int PF_RAW_NS = MODE == 2 ? PF_RAW_NS_Q6 : PF_RAW_NS_Q4;
     extern __shared__ uint8_t pf_raw[];
     uint8_t *sm = pf_raw + ((1024u - (umma_smem_u32(pf_raw) & 1023u)) & 1023u);
-    uint8_t *sa = sm, *sb = sm + PF_NS * PF_ATOM, *sr = sm + 2 * PF_NS * PF_ATOM;
+    uint8_t *sa = sm, *sb = sm + PF_NS * PF_ATOM, *sr = sb + PF_NS * PF_BATOM;
     uint8_t *sd = sr + PF_RAW_NS * RAW;  // Q6_K d plane of the tile (rows x 2 nb_pad bytes)
-    __shared__ __align__(8) uint64_t raw_full[PF_RAW_NS], raw_empty[PF_RAW_NS], a_full[PF_NS], b_full[PF_NS],
+    __shared__ __align__(8) uint64_t raw_full[PF_RAW_NS_MAX], raw_empty[PF_RAW_NS_MAX], a_full[PF_NS], b_full[PF_NS],
         ab_empty[PF_NS], acc_full;
     __shared__ uint32_t tmem_base;
     __shared__ int s_skip;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int tile = blockIdx.x, rb = blockIdx.y;
+    const int tile = blockIdx.y, rb = blockIdx.x;
     if (tid == 0) {
         int skip = tile >= plan.counts[1];
         if (!skip && MODE > 0) {
@@ -264,10 +343,11 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     const int slot = e == d.E ? L.n_local : e - L.e0;
     const int K = MODE == 0 ? d.H : d.I, NB = K / MOE_QK, n_atoms = 4 * NB;
     const int nbp = q6r_nb_pad(NB);
+    uint8_t *sk = sd + (MODE == 2 ? 128 * 2 * nbp : 0);  // per-quad atom constants (one quad per row)
     if (tid == 0) {
-        for (int i = 0; i < PF_RAW_NS; i++) { pf_mbar_init(&raw_full[i], 1); pf_mbar_init(&raw_empty[i], 4); }
+        for (int i = 0; i < PF_RAW_NS; i++) { pf_mbar_init(&raw_full[i], 1); pf_mbar_init(&raw_empty[i], PF_DQ_WARPS); }
         for (int i = 0; i < PF_NS; i++) {
-            pf_mbar_init(&a_full[i], 4);
+            pf_mbar_init(&a_full[i], PF_DQ_WARPS);
             pf_mbar_init(&b_full[i], 1);
             pf_mbar_init(&ab_empty[i], 1);
         }
@@ -275,7 +355,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
     }
-    if (warp == 1) tmem_alloc(&tmem_base, PF_TILE);
+    if (warp == 1) tmem_alloc(&tmem_base, PF_TILE_N);
     tmem_fence_before();
     __syncthreads();
     tmem_fence_after();
@@ -283,7 +363,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     bool ok = true;
 
     if (warp == 0) {
+        // weight producer: the raw tiles of each super-block, PF_RAW_NS ahead
         if (lane == 0) {
+            int issued = 0;
             for (int sbk = 0; sbk < NB && ok; sbk++) {
                 const int rs = sbk % PF_RAW_NS;
                 if (!pf_wait(&raw_empty[rs], ((sbk / PF_RAW_NS) & 1) ^ 1)) { ok = false; break; }
@@ -301,70 +383,130 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
                     pf_tma3(r + 128 * 192, &L.tm_d6s, sbk * 16, rb * 128, slot, &raw_full[rs]);
                     if (sbk == 0) pf_tma3(sd, &L.tm_d6d, 0, rb * 128, slot, &raw_full[rs]);
                 }
-                for (int a = 0; a < 4; a++) {
-                    const int i = 4 * sbk + a, st = i % PF_NS;
-                    if (!pf_wait(&ab_empty[st], ((i / PF_NS) & 1) ^ 1)) { ok = false; break; }
-                    pf_expect(&b_full[st], PF_ATOM);
-                    pf_tma2(sb + st * PF_ATOM, &tmB, sbk * MOE_QK + 64 * a, p0, &b_full[st]);
-                }
+                issued = sbk + 1;
             }
-            if (!ok) atomicExch(plan.error, PF_ERR_TIMEOUT);
+            if (!ok) {
+                atomicExch(plan.error, PF_ERR_TIMEOUT);
+                pf_drain(raw_full, issued, PF_RAW_NS);
+            }
+        }
+    } else if (warp == 2) {
+        // activation producer: the pairs' 64-column slices, PF_NS atoms ahead
+        if (lane == 0) {
+            int issued = 0;
+            for (int i = 0; i < n_atoms && ok; i++) {
+                const int st = i % PF_NS;
+                if (!pf_wait(&ab_empty[st], ((i / PF_NS) & 1) ^ 1)) { ok = false; break; }
+                // one 128-row box, or two for a tile of more than 128 pairs
+                pf_expect(&b_full[st], ntile > 128 ? 2 * PF_ATOM : PF_ATOM);
+                pf_tma2(sb + st * PF_BATOM, &tmB, 64 * i, p0, &b_full[st]);
+                if (ntile > 128) pf_tma2(sb + st * PF_BATOM + PF_ATOM, &tmB, 64 * i, p0 + 128, &b_full[st]);
+                issued = i + 1;
+            }
+            if (!ok) {
+                atomicExch(plan.error, PF_ERR_TIMEOUT);
+                pf_drain(b_full, issued, PF_NS);
+            }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t idesc = umma_idesc_f16(PF_TILE, PF_TILE);
+            // N = the tile's pairs rounded up to 16 (M = 128 takes N = 16 .. 256 in steps of 16)
+            const uint32_t idesc = umma_idesc_f16(PF_TILE, (ntile + 15) & ~15);
             for (int i = 0; i < n_atoms && ok; i++) {
                 const int st = i % PF_NS;
                 const uint32_t ph = (i / PF_NS) & 1;
                 if (!pf_wait(&a_full[st], ph) || !pf_wait(&b_full[st], ph)) { ok = false; break; }
                 tmem_fence_after();
-                const uint32_t a0 = umma_smem_u32(sa + st * PF_ATOM), b0 = umma_smem_u32(sb + st * PF_ATOM);
+                const uint32_t a0 = umma_smem_u32(sa + st * PF_ATOM), b0 = umma_smem_u32(sb + st * PF_BATOM);
 #pragma unroll
                 for (int kk = 0; kk < 4; kk++)
                     umma_f16(tmem, umma_desc_sw128(a0 + 32 * kk), umma_desc_sw128(b0 + 32 * kk), idesc,
                              (i | kk) != 0);
                 umma_commit(&ab_empty[st]);
             }
-            if (ok) umma_commit(&acc_full);
-            else atomicExch(plan.error, PF_ERR_TIMEOUT);
+            umma_commit(&acc_full);
+            if (!ok) {
+                // the MMAs already issued finish before tensor memory is freed
+                atomicExch(plan.error, PF_ERR_TIMEOUT);
+                pf_wait(&acc_full, 0);
+            }
         }
     } else {
-        // dequantization: thread = A row
-        const int row = tid - 64;
-        int rraw;  // raw tile row holding A row `row`
+        // dequantization: lane quad (j / 4) of the 16 warps owns one A row
+        static_assert(4 * PF_TILE == 32 * PF_DQ_WARPS, "one weight row per lane quad");
+        const int j = tid - 32 * PF_DQ_WARP0, t = j & 3, ri = (j >> 2) & 7;
+        const int row = (j & ~31) / 4 + (((ri & 1) << 2) | (ri & 2) | (ri >> 2));  // 8 w + brev3(ri)
+        int rraw = row;  // raw tile row holding A row `row`
         if (MODE == 0) {
             const int q = row >> 5, h = (row >> 4) & 1, i = row & 15;  // row = 32 q + 16 h + i
             rraw = h * 64 + 16 * q + i;                                // gate rows first, then up rows
-        } else {
-            rraw = row;
         }
+        // byte offsets of this lane's stores inside an atom
+        const uint32_t rbase = (uint32_t)((row >> 3) * 1024 + (row & 7) * 128), rx = (uint32_t)(row & 7);
+        const uint32_t oL = rbase + (((uint32_t)t ^ rx) << 4), oH = rbase + (((uint32_t)(4 + t) ^ rx) << 4);
+        uint32_t o6[4];
+#pragma unroll
+        for (int s4 = 0; s4 < 4; s4++) o6[s4] = rbase + (((uint32_t)(2 * s4 + (t >> 1)) ^ rx) << 4) + 8 * (t & 1);
+        uint8_t *kq = sk + (size_t)(j >> 2) * PF_CONST_ROW;  // this quad's constants
         for (int sbk = 0; sbk < NB && ok; sbk++) {
             const int rs = sbk % PF_RAW_NS;
-            if (!pf_wait(&raw_full[rs], (sbk / PF_RAW_NS) & 1)) { ok = false; break; }
+            if (!pf_wait_warp(&raw_full[rs], (sbk / PF_RAW_NS) & 1)) { ok = false; break; }
             const uint8_t *r = sr + rs * RAW;
-            float d6 = 0.0f;
-            if (MODE == 2) d6 = __half2float(reinterpret_cast<const __half *>(sd)[rraw * nbp + sbk]);
+            // the lane's bytes of its row for the whole super-block; the
+            // constants of atom t go to the quad's table
+            uint32_t qw[12], c[8];
+            __half2 d2 = __float2half2_rn(0.0f);
+            if (MODE == 2) {
+                const uint4 *src = reinterpret_cast<const uint4 *>(r + rraw * 192 + 48 * t);
+#pragma unroll
+                for (int v = 0; v < 3; v++) {
+                    const uint4 x = src[v];
+                    qw[4 * v] = x.x; qw[4 * v + 1] = x.y; qw[4 * v + 2] = x.z; qw[4 * v + 3] = x.w;
+                }
+                const uint32_t sc4 = reinterpret_cast<const uint32_t *>(r + 128 * 192 + rraw * 16)[t];
+                pf_q6_consts(__half2float(reinterpret_cast<const __half *>(sd)[rraw * nbp + sbk]), sc4, c);
+            } else {
+                const uint8_t *blk = r + rraw * MOE_Q4K_BYTES;
+                const uint4 hd = *reinterpret_cast<const uint4 *>(blk);
+                const uint4 x = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * t);
+                const uint4 y = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * t);
+                qw[0] = x.x; qw[1] = x.y; qw[2] = x.z; qw[3] = x.w;
+                qw[4] = y.x; qw[5] = y.y; qw[6] = y.z; qw[7] = y.w;
+                d2 = pf_u2h(__byte_perm(hd.x, 0, 0x1010));  // (d, d)
+                pf_q4_consts(hd, t, c);
+            }
+            __syncwarp();  // the previous super-block's constants are no longer read
+            *reinterpret_cast<uint4 *>(kq + 32 * t) = make_uint4(c[0], c[1], c[2], c[3]);
+            *reinterpret_cast<uint4 *>(kq + 32 * t + 16) = make_uint4(c[4], c[5], c[6], c[7]);
+            __syncwarp();
+            if (lane == 0) pf_arrive(&raw_empty[rs]);  // everything needed is in registers
+#pragma unroll
             for (int a = 0; a < 4; a++) {
                 const int i = 4 * sbk + a, st = i % PF_NS;
-                if (!pf_wait(&ab_empty[st], ((i / PF_NS) & 1) ^ 1)) { ok = false; break; }
+                if (!pf_wait_warp(&ab_empty[st], ((i / PF_NS) & 1) ^ 1)) { ok = false; break; }
                 uint8_t *atom = sa + st * PF_ATOM;
-                if (MODE == 2)
-                    pf_deq_q6(r + rraw * 192, reinterpret_cast<const int8_t *>(r + 128 * 192 + rraw * 16), d6, a,
-                              atom, row);
-                else
-                    pf_deq_q4(r + rraw * MOE_Q4K_BYTES, a, atom, row);
+                const uint4 k0 = *reinterpret_cast<const uint4 *>(kq + 32 * a);
+                const uint4 k1 = *reinterpret_cast<const uint4 *>(kq + 32 * a + 16);
+                const uint32_t ka[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
+                if (MODE == 2) {
+                    if (a == 0) pf_deq_q6<0>(qw, ka, atom, o6);
+                    else if (a == 1) pf_deq_q6<1>(qw, ka, atom, o6);
+                    else if (a == 2) pf_deq_q6<2>(qw, ka, atom, o6);
+                    else pf_deq_q6<3>(qw, ka, atom, o6);
+                } else {
+                    pf_deq_q4(qw[2 * a], qw[2 * a + 1], d2, ka, atom, oL, oH);
+                }
                 fence_async_smem();
                 __syncwarp();
                 if (lane == 0) pf_arrive(&a_full[st]);
             }
-            __syncwarp();
-            if (lane == 0) pf_arrive(&raw_empty[rs]);
         }
         // epilogue: this warp reads tensor-memory lanes 32 (warp % 4) .. + 31
-        if (ok && pf_wait(&acc_full, 0)) {
+        if (ok && pf_wait_warp(&acc_full, 0)) {
             tmem_fence_after();
-            const int q = warp & 3;
-            for (int c = 0; c < PF_TILE; c += 16) {
+            // PF_DQ_WARPS / 4 warps per lane quarter: column chunks alternate between them
+            const int q = warp & 3, sub = (warp - PF_DQ_WARP0) >> 2;
+            for (int c = 16 * sub; c < PF_TILE_N; c += 16 * (PF_DQ_WARPS / 4)) {
                 if (c >= ntile) break;
                 float v[16];
                 tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + c, v);
@@ -390,7 +532,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     }
     tmem_fence_before();
     __syncthreads();
-    if (warp == 1) tmem_free(tmem, PF_TILE);
+    if (warp == 1) tmem_free(tmem, PF_TILE_N);
 }
 
 // ===========================================================================
@@ -398,7 +540,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 // ===========================================================================
 static size_t pf_smem(int mode, int nbp) {
     const size_t raw = mode == 2 ? PF_RAW_Q6 : PF_RAW_Q4;
-    return 1024 + 2 * (size_t)PF_NS * PF_ATOM + PF_RAW_NS * raw + (mode == 2 ? 128 * 2 * (size_t)nbp : 0);
+    const size_t ns = mode == 2 ? PF_RAW_NS_Q6 : PF_RAW_NS_Q4;
+    return 1024 + (size_t)PF_NS * (PF_ATOM + PF_BATOM) + ns * raw + (mode == 2 ? 128 * 2 * (size_t)nbp : 0) +
+           (size_t)PF_TILE * PF_CONST_ROW;
 }
 
 template <int MODE>
@@ -410,7 +554,7 @@ static void pf_launch(const MoeDims &d, const MoeLayerDev &L, const MoePlan &pla
         cudaFuncSetAttribute(k_prefill_gemm<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         attr = smem;
     }
-    k_prefill_gemm<MODE><<<dim3(max_tiles, row_blocks), PF_THREADS, smem, s>>>(d, L, plan, tmB, act, eo);
+    k_prefill_gemm<MODE><<<dim3(row_blocks, max_tiles), PF_THREADS, smem, s>>>(d, L, plan, tmB, act, eo);
     LAUNCH_COUNT(launches);
 }
 
@@ -426,8 +570,8 @@ int moe_prefill_alloc(MoePrefillWs &ws, const MoeDims &d, int T) {
     if (ws.cap >= T) return 0;
     moe_prefill_free(ws);
     const int cap = (T + 255) & ~255;
-    const size_t P = (size_t)cap * (d.K + 1) + PF_TILE;  // pairs (+ slack rows for the last TMA box)
-    const size_t tiles = (size_t)d.E + 1 + P / PF_TILE + 1;
+    const size_t P = (size_t)cap * (d.K + 1) + PF_TILE_N;  // pairs (+ slack rows for the last TMA box)
+    const size_t tiles = (size_t)d.E + 1 + P / PF_TILE_N + 1;
     const int nsplit = d.H / MOE_QK;
     cudaError_t e = cudaSuccess;
 #define PFA(ptr, bytes) \
@@ -474,7 +618,7 @@ void moe_launch_prefill_experts(const MoeDims &d, const MoeLayerDev &L, MoePrefi
     const int P = T * (d.K + 1);
     k_prefill_gather<<<P < 148 * 8 ? P : 148 * 8, 256, 0, s>>>(x, d.H, ws.plan, ws.xg);
     LAUNCH_COUNT(launches);
-    const int max_tiles = d.E + 1 + P / PF_TILE + 1;
+    const int max_tiles = d.E + 1 + P / PF_TILE_N + 1;
     pf_launch<0>(d, L, ws.plan, ws.tm_xg, ws.act, nullptr, max_tiles, d.I / 64, s, launches);
     if (L.down_type == MOE_TYPE_Q6_K || L.sh_down_type == MOE_TYPE_Q6_K)
         pf_launch<2>(d, L, ws.plan, ws.tm_act, nullptr, ws.eo, max_tiles, d.H / 128, s, launches);
