@@ -692,6 +692,10 @@ int moe_make_layer_maps(MoeLayerDev &L, const MoeDims &d) {
         if (!rc)
             rc = map3(&L.tm_d6d, down + q6r_plane_d_off(H, NBi), (uint64_t)nbp * 2, H, slots, L.expert_stride,
                       (uint32_t)nbp * 2, DN_ROWS);
+        // the prefill copies 208 bytes per row (the super-block plus 16 bytes it
+        // ignores), so that rows land 208 B apart: eight consecutive rows on
+        // distinct 16-byte bank groups
+        if (!rc) rc = map3(&L.tm_pf6q, down, (uint64_t)NBi * 192, H, slots, L.expert_stride, 208, DN_ROWS);
         if (rc) return rc;
     }
     return 0;

@@ -38,6 +38,7 @@ struct MoeLayerDev {
     CUtensorMap tm_d6q;     // Q6_K down, Q plane, box 192 B x 128 rows
     CUtensorMap tm_d6s;     // Q6_K down, S plane, box 16 B x 128 rows
     CUtensorMap tm_d6d;     // Q6_K down, D plane, box 2 nb_pad B x 128 rows
+    CUtensorMap tm_pf6q;    // Q6_K down, Q plane, box 208 B x 128 rows (prefill: rows 208 B apart in shared memory)
 };
 
 struct MoeDims {

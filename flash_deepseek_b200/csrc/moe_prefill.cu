@@ -3,27 +3,29 @@
 //
 // With ~128 tokens per expert the expert products are real matrix products
 // (C = W X^T, M = weight rows, N = tokens, K = hidden or intermediate), so
-// the weights are dequantized once per tile into fp16 shared-memory tiles
-// that feed tcgen05.mma, with the fp32 accumulator in tensor memory:
+// the weights are dequantized once per tile into fp16 tiles that feed
+// tcgen05.mma, with the fp32 accumulator in tensor memory:
 //   plan     counting sort of the (token, slot) pairs by expert, tiles of
-//            <= 128 pairs per expert
+//            <= 256 pairs per expert
 //   gather   fp16 copy of each pair's token row, pairs grouped by expert
-//   gemm1    gate/up rows (64 + 64 per tile) x 128 pairs, SwiGLU in the
+//   gemm1    gate/up rows (64 + 64 per tile) x <= 256 pairs, SwiGLU in the
 //            epilogue (infer.m:378-383), act in fp16
-//   gemm2    down rows (128 per tile) x 128 pairs, fp32 expert outputs
+//   gemm2    down rows (128 per tile) x <= 256 pairs, fp32 expert outputs
 //   combine  slot order, then the shared expert (infer.m:1915-1922)
 // Differences from the reference's fp32 dot: weights and activations are
 // rounded to fp16 (11-bit significands) before the fp32-accumulated product.
 //
-// GEMM CTA: warp 0 streams the raw Q4_K / Q6_K tiles, one super-block per
-// stage, several stages ahead; warp 2 streams the pairs' 64-column
-// activation slices (TMA with the 128-byte swizzle); warp 1 owns tensor
-// memory and issues the MMAs from one thread; 16 warps dequantize (four
-// lanes per weight row) into the swizzled A tile and, after the last k step,
-// run the epilogue from tensor memory.  All hand-offs are mbarriers; every
-// wait gives up after about a second and records an error instead of
-// hanging, and a producer that gives up first waits (bounded) for the copies
-// it issued.
+// GEMM CTA (one per SM): warp 0 streams the raw Q4_K / Q6_K tiles, one
+// super-block per stage; warp 2 streams the pairs' 64-column activation
+// slices (TMA, 128-byte swizzle) into a ring of 16 KB or 32 KB stages; warp
+// 1 owns tensor memory and issues the MMAs from one thread.  16 warps
+// dequantize: warp (q, g) writes atom g of every super-block for tensor-
+// memory lanes 32q .. 32q + 31 straight into tensor memory (tcgen05.st), so
+// the A operand never touches shared memory, and the MMA reads A from tensor
+// memory and B from shared memory; the same warps run the epilogue.  All
+// hand-offs are mbarriers; every wait gives up after about a second and
+// records an error instead of hanging, and a producer that gives up first
+// waits (bounded) for the copies it issued.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <stdio.h>
@@ -35,15 +37,16 @@
 
 #define PF_TILE 128                // weight rows per tile (MMA M)
 #define PF_TILE_N 256              // pairs per tile (MMA N <= 256)
-#define PF_NS 3                    // k-atom stages (64 columns of K each)
-#define PF_BATOM (PF_TILE_N * 128) // B atom: 256 pair rows x 128 B
-#define PF_ATOM 16384              // A atom: 128 rows x 128 B
-#define PF_RAW_NS_Q4 3             // raw super-block stages (Q4_K tiles)
-#define PF_RAW_NS_Q6 2             // (Q6_K tiles)
-#define PF_RAW_NS_MAX 3
+#define PF_ATOM 16384              // one 128-row x 128-byte activation box (64 columns of K)
+#define PF_NSA 8                   // A stages in tensor memory (32 columns each, after the accumulator)
+#define PF_BRING_Q4 (160 * 1024)   // activation ring: 10 stages of <= 128 pairs or 5 of <= 256
+#define PF_BRING_Q6 (128 * 1024)   // 8 or 4
+#define PF_NSB_MAX 10
 #define PF_RAW_Q4 (128 * 144)      // 128 Q4_K rows of one super-block
-#define PF_RAW_Q6 (128 * 192 + 128 * 16)
-#define PF_DQ_WARPS 16                              // dequantize + epilogue (warps 2 ..)
+#define PF_Q6_ROW 208              // Q6_K Q-plane row stride in shared memory (192 B used)
+#define PF_RAW_Q6 (128 * PF_Q6_ROW + 128 * 16)
+#define PF_RAW_NS 3                // raw super-block stages
+#define PF_DQ_WARPS 16                              // dequantize + epilogue (warps 3 ..)
 #define PF_DQ_WARP0 3                               // warps 0-2: weight TMA, MMA, activation TMA
 #define PF_THREADS (32 * (PF_DQ_WARP0 + PF_DQ_WARPS))
 #define PF_WAIT_CYCLES (1ll << 31)
@@ -180,29 +183,19 @@ __global__ void __launch_bounds__(256) k_prefill_gather(const float *__restrict_
 }
 
 // ===========================================================================
-// dequantization into one 64-column A atom, in fp16 arithmetic with exact
-// intermediate steps.  Four lanes share a weight row: lane t holds, for a
-// whole super-block, the bytes the repacked layouts give MMA lane t and
-// writes 16 of the row's 64 fp16 values per atom.
-//   - A byte permute puts two weight bytes under the fp16 exponent of 1024
+// dequantization of one 64-column A atom of one weight row into 32 registers
+// (fp16 pairs, k = 2c and 2c + 1 in register c), written to tensor memory by
+// the caller.  fp16 arithmetic with exact intermediate steps:
+//   - a byte permute puts two weight bytes under the fp16 exponent of 1024
 //     (0x64 high bytes); masking keeps the low nibble (1024 + q) or the high
-//     nibble in place (1024 + 16 q), exact.
+//     nibble in place (1024 + 16 q), exact;
 //   - Q4_K, w = d*sc*q - dmin*m: p = fma(1024 + q, sc, -1024 sc) = q*sc
 //     exactly (<= 945; the high nibble uses sc/16 and -64 sc); then
 //     fma(d, p, -dm_hi) - dm_lo with dmin*m = dm_hi + dm_lo split into two
-//     fp16 values (exact), so the result is rounded on the scale of w itself.
+//     fp16 values (exact), so the result is rounded on the scale of w itself;
 //   - Q6_K, w = d*sc*(q - 32): (1024 + q) - 1056 = q - 32 exactly; then
 //     fma(q - 32, fs_hi, (q - 32) * fs_lo) with d*sc = fs_hi + fs_lo.
-// The per-sub-block constants of an atom (8 fp16 pairs) are computed once
-// per super-block by the quad lane that owns the atom and read back from
-// shared memory by the whole quad.
-// A warp's lanes cover rows 8w + brev3(0..7) (bit-reversed), so the two rows
-// of a quarter-warp differ in row bit 2 and the four of a half-warp in row
-// bits 1-2: the 16-byte (Q4_K) and 8-byte (Q6_K) stores into the 128-byte
-// swizzled atom then hit distinct banks.
 // ===========================================================================
-#define PF_CONST_ROW 144  // bytes per quad: 4 atoms x 32 B + 16 B padding (distinct banks for two quads)
-
 __device__ __forceinline__ uint32_t pf_h2u(__half2 h) { return *reinterpret_cast<const uint32_t *>(&h); }
 __device__ __forceinline__ __half2 pf_u2h(uint32_t u) { return *reinterpret_cast<const __half2 *>(&u); }
 __device__ __forceinline__ uint32_t pf_dup(float x) { return pf_h2u(__float2half2_rn(x)); }
@@ -229,14 +222,14 @@ __device__ __forceinline__ void q4_scale_min(uint4 h, int &sc, int &m) {
 #undef PF_B
 }
 
-// the constants of Q4_K atom t (sub-blocks 2t, 2t + 1):
+// the constants of Q4_K atom g (sub-blocks 2g, 2g + 1):
 // {sc0, -1024 sc0, -dm0_hi, -dm0_lo, sc1/16, -64 sc1, -dm1_hi, -dm1_lo}
-__device__ __forceinline__ void pf_q4_consts(uint4 h, int t, uint32_t (&c)[8]) {
+__device__ __forceinline__ void pf_q4_consts(uint4 h, int g, uint32_t (&c)[8]) {
     const float dmin = __half2float(__ushort_as_half((uint16_t)(h.x >> 16)));
     int sc0 = 0, m0 = 0, sc1 = 0, m1 = 0;
-    if (t == 0) { q4_scale_min<0>(h, sc0, m0); q4_scale_min<1>(h, sc1, m1); }
-    else if (t == 1) { q4_scale_min<2>(h, sc0, m0); q4_scale_min<3>(h, sc1, m1); }
-    else if (t == 2) { q4_scale_min<4>(h, sc0, m0); q4_scale_min<5>(h, sc1, m1); }
+    if (g == 0) { q4_scale_min<0>(h, sc0, m0); q4_scale_min<1>(h, sc1, m1); }
+    else if (g == 1) { q4_scale_min<2>(h, sc0, m0); q4_scale_min<3>(h, sc1, m1); }
+    else if (g == 2) { q4_scale_min<4>(h, sc0, m0); q4_scale_min<5>(h, sc1, m1); }
     else { q4_scale_min<6>(h, sc0, m0); q4_scale_min<7>(h, sc1, m1); }
     c[0] = pf_dup((float)sc0);
     c[1] = pf_dup(-1024.0f * (float)sc0);
@@ -252,58 +245,55 @@ __device__ __forceinline__ uint32_t pf_q4_pair(uint32_t x, __half2 d2, const uin
     return pf_h2u(__hadd2(__hfma2(p, d2, pf_u2h(c[2])), pf_u2h(c[3])));
 }
 
-// Q4_K atom a: low nibbles of old bytes 32 a + l (sub-block 2a) and high
-// nibbles (2a + 1); the lane's words w0, w1 hold old bytes 32 a + 8 t + i,
-// i.e. k = 64 a + 8 t + i (atom chunk t, byte offset oL) and
-// 64 a + 32 + 8 t + i (chunk 4 + t, oH).
-__device__ __forceinline__ void pf_deq_q4(uint32_t w0, uint32_t w1, __half2 d2, const uint32_t (&c)[8], uint8_t *atom,
-                                          uint32_t oL, uint32_t oH) {
-    const uint32_t wd[2] = {w0, w1};
-    uint32_t lo[4], hi[4];
+// Q4_K atom g of one row: w[2t], w[2t + 1] = old qs bytes 32 g + 8 t .. + 7
+// (at 16 + 32 t + 8 g of the repacked block); low nibbles are k = 8 t + i
+// (registers 4t ..), high nibbles k = 32 + 8 t + i (registers 16 + 4t ..).
+__device__ __forceinline__ void pf_deq_q4(const uint32_t (&w)[8], __half2 d2, const uint32_t (&c)[8],
+                                          uint32_t (&v)[32]) {
 #pragma unroll
-    for (int h = 0; h < 2; h++) {
-        const uint32_t x01 = __byte_perm(wd[h], 0x64u, 0x4140u);  // bytes 0, 1 under 0x64
-        const uint32_t x23 = __byte_perm(wd[h], 0x64u, 0x4342u);
-        lo[2 * h] = pf_q4_pair(x01 & 0xFF0FFF0Fu, d2, c);
-        lo[2 * h + 1] = pf_q4_pair(x23 & 0xFF0FFF0Fu, d2, c);
-        hi[2 * h] = pf_q4_pair(x01 & 0xFFF0FFF0u, d2, c + 4);
-        hi[2 * h + 1] = pf_q4_pair(x23 & 0xFFF0FFF0u, d2, c + 4);
-    }
-    *reinterpret_cast<uint4 *>(atom + oL) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-    *reinterpret_cast<uint4 *>(atom + oH) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    for (int t = 0; t < 4; t++)
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const uint32_t x01 = __byte_perm(w[2 * t + h], 0x64u, 0x4140u);  // bytes 0, 1 under 0x64
+            const uint32_t x23 = __byte_perm(w[2 * t + h], 0x64u, 0x4342u);
+            v[4 * t + 2 * h] = pf_q4_pair(x01 & 0xFF0FFF0Fu, d2, c);
+            v[4 * t + 2 * h + 1] = pf_q4_pair(x23 & 0xFF0FFF0Fu, d2, c);
+            v[16 + 4 * t + 2 * h] = pf_q4_pair(x01 & 0xFFF0FFF0u, d2, c + 4);
+            v[16 + 4 * t + 2 * h + 1] = pf_q4_pair(x23 & 0xFFF0FFF0u, d2, c + 4);
+        }
 }
 
-// the constants of Q6_K atom t (sub-blocks 4t .. 4t + 3): {fs_hi, fs_lo} x 4
+// the constants of Q6_K atom g (sub-blocks 4g .. 4g + 3): {fs_hi, fs_lo} x 4
 // with fs = d * sc (exact in fp32)
 __device__ __forceinline__ void pf_q6_consts(float d6, uint32_t sc4, uint32_t (&c)[8]) {
 #pragma unroll
     for (int u = 0; u < 4; u++) pf_split(d6 * (float)(int8_t)(sc4 >> (8 * u)), c[2 * u], c[2 * u + 1]);
 }
 
-// Q6_K atom A (sub-blocks 4A .. 4A + 3): q = this lane's 12 words of the row
-// (per half h: ql words at 6h + w, qh words at 6h + 4 + w', the high bit of
-// every qh pair stored inverted); it holds k = 16 s + 4 t + i of sub-block s.
-// With the inverted bit the 6-bit field nib | qh2 << 4 is q ^ 32; one more
-// xor restores q.  o[s4] = byte offset of k = 16 s4 + 4 t in the atom.
+// Q6_K atom A of one row (sub-blocks 4A + s4, half h = A / 2): q[6t + ..] =
+// lane chunk t's ql words s4 = 0..3 and qh words 0, 1 of half h (the high
+// bit of every qh pair stored inverted, so the 6-bit field nib | qh2 << 4 is
+// q ^ 32; one more xor restores q).  k = 16 s4 + 4 t + i -> register
+// 8 s4 + 2 t + i / 2.
 template <int A>
-__device__ __forceinline__ void pf_deq_q6(const uint32_t (&q)[12], const uint32_t (&c)[8], uint8_t *atom,
-                                          const uint32_t (&o)[4]) {
-    constexpr int h = A >> 1;
+__device__ __forceinline__ void pf_deq_q6(const uint32_t (&q)[24], const uint32_t (&c)[8], uint32_t (&v)[32]) {
     const __half2 off = pf_u2h(0x64206420u);  // 1056 = 1024 + 32
 #pragma unroll
-    for (int s4 = 0; s4 < 4; s4++) {
-        const int sp = 4 * (A & 1) + s4, f = sp >> 1;
-        const uint32_t W = q[6 * h + s4];
-        const uint32_t Hq = q[6 * h + 4 + (s4 & 1)];
-        const uint32_t nib = (sp < 4 ? W : W >> 4) & 0x0F0F0F0Fu;
-        const uint32_t hb = (2 * f <= 4 ? Hq << (4 - 2 * f) : Hq >> (2 * f - 4)) & 0x30303030u;
-        const uint32_t q6 = nib | (hb ^ 0x20202020u);  // four values q in bytes
-        const __half2 fh = pf_u2h(c[2 * s4]), fl = pf_u2h(c[2 * s4 + 1]);
-        const __half2 v01 = __hsub2(pf_u2h(__byte_perm(q6, 0x64u, 0x4140u)), off);  // q - 32, exact
-        const __half2 v23 = __hsub2(pf_u2h(__byte_perm(q6, 0x64u, 0x4342u)), off);
-        *reinterpret_cast<uint2 *>(atom + o[s4]) = make_uint2(pf_h2u(__hfma2(v01, fh, __hmul2(v01, fl))),
-                                                              pf_h2u(__hfma2(v23, fh, __hmul2(v23, fl))));
-    }
+    for (int t = 0; t < 4; t++)
+#pragma unroll
+        for (int s4 = 0; s4 < 4; s4++) {
+            const int sp = 4 * (A & 1) + s4, f = sp >> 1;
+            const uint32_t W = q[6 * t + s4];
+            const uint32_t Hq = q[6 * t + 4 + (s4 & 1)];
+            const uint32_t nib = (sp < 4 ? W : W >> 4) & 0x0F0F0F0Fu;
+            const uint32_t hb = (2 * f <= 4 ? Hq << (4 - 2 * f) : Hq >> (2 * f - 4)) & 0x30303030u;
+            const uint32_t q6 = nib | (hb ^ 0x20202020u);  // four values q in bytes
+            const __half2 fh = pf_u2h(c[2 * s4]), fl = pf_u2h(c[2 * s4 + 1]);
+            const __half2 v01 = __hsub2(pf_u2h(__byte_perm(q6, 0x64u, 0x4140u)), off);  // q - 32, exact
+            const __half2 v23 = __hsub2(pf_u2h(__byte_perm(q6, 0x64u, 0x4342u)), off);
+            v[8 * s4 + 2 * t] = pf_h2u(__hfma2(v01, fh, __hmul2(v01, fl)));
+            v[8 * s4 + 2 * t + 1] = pf_h2u(__hfma2(v23, fh, __hmul2(v23, fl)));
+        }
 }
 
 // ===========================================================================
@@ -317,13 +307,13 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     k_prefill_gemm(MoeDims d, const __grid_constant__ MoeLayerDev L, MoePlan plan,
                    const __grid_constant__ CUtensorMap tmB, __half *__restrict__ act, float *__restrict__ eo) {
     constexpr int RAW = MODE == 2 ? PF_RAW_Q6 : PF_RAW_Q4;
-    constexpr int PF_RAW_NS = MODE == 2 ? PF_RAW_NS_Q6 : PF_RAW_NS_Q4;
+    constexpr int BRING = MODE == 2 ? PF_BRING_Q6 : PF_BRING_Q4;
     extern __shared__ uint8_t pf_raw[];
     uint8_t *sm = pf_raw + ((1024u - (umma_smem_u32(pf_raw) & 1023u)) & 1023u);
-    uint8_t *sa = sm, *sb = sm + PF_NS * PF_ATOM, *sr = sb + PF_NS * PF_BATOM;
+    uint8_t *sb = sm, *sr = sm + BRING;
     uint8_t *sd = sr + PF_RAW_NS * RAW;  // Q6_K d plane of the tile (rows x 2 nb_pad bytes)
-    __shared__ __align__(8) uint64_t raw_full[PF_RAW_NS_MAX], raw_empty[PF_RAW_NS_MAX], a_full[PF_NS], b_full[PF_NS],
-        ab_empty[PF_NS], acc_full;
+    __shared__ __align__(8) uint64_t raw_full[PF_RAW_NS], raw_empty[PF_RAW_NS], a_full[PF_NSA], a_empty[PF_NSA],
+        b_full[PF_NSB_MAX], b_empty[PF_NSB_MAX], acc_full;
     __shared__ uint32_t tmem_base;
     __shared__ int s_skip;
 
@@ -343,163 +333,169 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     const int slot = e == d.E ? L.n_local : e - L.e0;
     const int K = MODE == 0 ? d.H : d.I, NB = K / MOE_QK, n_atoms = 4 * NB;
     const int nbp = q6r_nb_pad(NB);
-    uint8_t *sk = sd + (MODE == 2 ? 128 * 2 * nbp : 0);  // per-quad atom constants (one quad per row)
+    // activation stage: one 128-row box (16 KB) for a tile of <= 128 pairs, else two
+    const int BST = ntile > 128 ? 2 * PF_ATOM : PF_ATOM, NSB = BRING / BST;
     if (tid == 0) {
         for (int i = 0; i < PF_RAW_NS; i++) { pf_mbar_init(&raw_full[i], 1); pf_mbar_init(&raw_empty[i], PF_DQ_WARPS); }
-        for (int i = 0; i < PF_NS; i++) {
-            pf_mbar_init(&a_full[i], PF_DQ_WARPS);
-            pf_mbar_init(&b_full[i], 1);
-            pf_mbar_init(&ab_empty[i], 1);
-        }
+        for (int i = 0; i < PF_NSA; i++) { pf_mbar_init(&a_full[i], 4); pf_mbar_init(&a_empty[i], 1); }
+        for (int i = 0; i < PF_NSB_MAX; i++) { pf_mbar_init(&b_full[i], 1); pf_mbar_init(&b_empty[i], 1); }
         pf_mbar_init(&acc_full, 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
     }
-    if (warp == 1) tmem_alloc(&tmem_base, PF_TILE_N);
+    // tensor memory: accumulator in columns [0, 256), A stages in [256, 512)
+    if (warp == 1) tmem_alloc(&tmem_base, 512);
     tmem_fence_before();
     __syncthreads();
     tmem_fence_after();
-    const uint32_t tmem = tmem_base;
+    const uint32_t tmem = tmem_base, tmem_a = tmem_base + PF_TILE_N;
     bool ok = true;
 
     if (warp == 0) {
         // weight producer: the raw tiles of each super-block, PF_RAW_NS ahead
-        if (lane == 0) {
-            int issued = 0;
-            for (int sbk = 0; sbk < NB && ok; sbk++) {
-                const int rs = sbk % PF_RAW_NS;
-                if (!pf_wait(&raw_empty[rs], ((sbk / PF_RAW_NS) & 1) ^ 1)) { ok = false; break; }
-                uint8_t *r = sr + rs * RAW;
+        // (the warp loops together, one elected lane issues the copies)
+        const uint32_t leader = elect_one();
+        int issued = 0;
+        for (int sbk = 0; sbk < NB && ok; sbk++) {
+            const int rs = sbk % PF_RAW_NS;
+            if (!pf_wait_warp(&raw_empty[rs], ((sbk / PF_RAW_NS) & 1) ^ 1)) { ok = false; break; }
+            uint8_t *r = sr + rs * RAW;
+            if (leader) {
                 if (MODE == 0) {
                     pf_expect(&raw_full[rs], RAW);
                     pf_tma3(r, &L.tm_gu, sbk * MOE_Q4K_BYTES, rb * 64, slot, &raw_full[rs]);
-                    pf_tma3(r + 64 * MOE_Q4K_BYTES, &L.tm_gu, sbk * MOE_Q4K_BYTES, d.I + rb * 64, slot, &raw_full[rs]);
+                    pf_tma3(r + 64 * MOE_Q4K_BYTES, &L.tm_gu, sbk * MOE_Q4K_BYTES, d.I + rb * 64, slot,
+                            &raw_full[rs]);
                 } else if (MODE == 1) {
                     pf_expect(&raw_full[rs], RAW);
                     pf_tma3(r, &L.tm_d4, sbk * MOE_Q4K_BYTES, rb * 128, slot, &raw_full[rs]);
                 } else {
                     pf_expect(&raw_full[rs], RAW + (sbk == 0 ? 128 * 2 * nbp : 0));
-                    pf_tma3(r, &L.tm_d6q, sbk * 192, rb * 128, slot, &raw_full[rs]);
-                    pf_tma3(r + 128 * 192, &L.tm_d6s, sbk * 16, rb * 128, slot, &raw_full[rs]);
+                    pf_tma3(r, &L.tm_pf6q, sbk * 192, rb * 128, slot, &raw_full[rs]);
+                    pf_tma3(r + 128 * PF_Q6_ROW, &L.tm_d6s, sbk * 16, rb * 128, slot, &raw_full[rs]);
                     if (sbk == 0) pf_tma3(sd, &L.tm_d6d, 0, rb * 128, slot, &raw_full[rs]);
                 }
-                issued = sbk + 1;
             }
-            if (!ok) {
-                atomicExch(plan.error, PF_ERR_TIMEOUT);
-                pf_drain(raw_full, issued, PF_RAW_NS);
-            }
+            issued = sbk + 1;
+        }
+        if (!ok && leader) {
+            atomicExch(plan.error, PF_ERR_TIMEOUT);
+            pf_drain(raw_full, issued, PF_RAW_NS);
         }
     } else if (warp == 2) {
-        // activation producer: the pairs' 64-column slices, PF_NS atoms ahead
-        if (lane == 0) {
-            int issued = 0;
-            for (int i = 0; i < n_atoms && ok; i++) {
-                const int st = i % PF_NS;
-                if (!pf_wait(&ab_empty[st], ((i / PF_NS) & 1) ^ 1)) { ok = false; break; }
-                // one 128-row box, or two for a tile of more than 128 pairs
-                pf_expect(&b_full[st], ntile > 128 ? 2 * PF_ATOM : PF_ATOM);
-                pf_tma2(sb + st * PF_BATOM, &tmB, 64 * i, p0, &b_full[st]);
-                if (ntile > 128) pf_tma2(sb + st * PF_BATOM + PF_ATOM, &tmB, 64 * i, p0 + 128, &b_full[st]);
-                issued = i + 1;
+        // activation producer: the pairs' 64-column slices, NSB atoms ahead
+        const uint32_t leader = elect_one();
+        int issued = 0;
+        for (int i = 0; i < n_atoms && ok; i++) {
+            const int st = i % NSB;
+            if (!pf_wait_warp(&b_empty[st], ((i / NSB) & 1) ^ 1)) { ok = false; break; }
+            if (leader) {
+                pf_expect(&b_full[st], BST);
+                pf_tma2(sb + st * BST, &tmB, 64 * i, p0, &b_full[st]);
+                if (ntile > 128) pf_tma2(sb + st * BST + PF_ATOM, &tmB, 64 * i, p0 + 128, &b_full[st]);
             }
-            if (!ok) {
-                atomicExch(plan.error, PF_ERR_TIMEOUT);
-                pf_drain(b_full, issued, PF_NS);
-            }
+            issued = i + 1;
+        }
+        if (!ok && leader) {
+            atomicExch(plan.error, PF_ERR_TIMEOUT);
+            pf_drain(b_full, issued, NSB);
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            // N = the tile's pairs rounded up to 16 (M = 128 takes N = 16 .. 256 in steps of 16)
-            const uint32_t idesc = umma_idesc_f16(PF_TILE, (ntile + 15) & ~15);
-            for (int i = 0; i < n_atoms && ok; i++) {
-                const int st = i % PF_NS;
-                const uint32_t ph = (i / PF_NS) & 1;
-                if (!pf_wait(&a_full[st], ph) || !pf_wait(&b_full[st], ph)) { ok = false; break; }
-                tmem_fence_after();
-                const uint32_t a0 = umma_smem_u32(sa + st * PF_ATOM), b0 = umma_smem_u32(sb + st * PF_BATOM);
+        // MMA issuer: the whole warp runs the loop (uniform operands), one
+        // elected lane issues each MMA and commit.
+        // N = the tile's pairs rounded up to 16 (M = 128 takes N = 16 .. 256 in steps of 16)
+        const uint32_t idesc = umma_idesc_f16(PF_TILE, (ntile + 15) & ~15);
+        for (int i = 0; i < n_atoms && ok; i++) {
+            const int sa = i % PF_NSA, sbq = i % NSB;
+            if (!pf_wait_warp(&a_full[sa], (i / PF_NSA) & 1) || !pf_wait_warp(&b_full[sbq], (i / NSB) & 1)) {
+                ok = false;
+                break;
+            }
+            tmem_fence_after();
+            const uint32_t b0 = umma_smem_u32(sb + sbq * BST);
 #pragma unroll
-                for (int kk = 0; kk < 4; kk++)
-                    umma_f16(tmem, umma_desc_sw128(a0 + 32 * kk), umma_desc_sw128(b0 + 32 * kk), idesc,
-                             (i | kk) != 0);
-                umma_commit(&ab_empty[st]);
-            }
-            umma_commit(&acc_full);
-            if (!ok) {
-                // the MMAs already issued finish before tensor memory is freed
-                atomicExch(plan.error, PF_ERR_TIMEOUT);
-                pf_wait(&acc_full, 0);
-            }
+            for (int kk = 0; kk < 4; kk++)
+                umma_f16_ta_warp(tmem, tmem_a + 32 * sa + 8 * kk, umma_desc_sw128(b0 + 32 * kk), idesc, (i | kk) != 0);
+            umma_commit_warp(&a_empty[sa]);
+            umma_commit_warp(&b_empty[sbq]);
+        }
+        umma_commit_warp(&acc_full);
+        if (!ok) {
+            // the MMAs already issued finish before tensor memory is freed
+            if (lane == 0) atomicExch(plan.error, PF_ERR_TIMEOUT);
+            pf_wait_warp(&acc_full, 0);
         }
     } else {
-        // dequantization: lane quad (j / 4) of the 16 warps owns one A row
-        static_assert(4 * PF_TILE == 32 * PF_DQ_WARPS, "one weight row per lane quad");
-        const int j = tid - 32 * PF_DQ_WARP0, t = j & 3, ri = (j >> 2) & 7;
-        const int row = (j & ~31) / 4 + (((ri & 1) << 2) | (ri & 2) | (ri >> 2));  // 8 w + brev3(ri)
+        // dequantization: warp (q = warp % 4, g) owns tensor-memory lanes
+        // 32 q .. 32 q + 31 (A rows; lane = row) and atom g of every super-block
+        const int q = warp & 3, g = (warp - PF_DQ_WARP0) >> 2, row = 32 * q + lane;
         int rraw = row;  // raw tile row holding A row `row`
         if (MODE == 0) {
-            const int q = row >> 5, h = (row >> 4) & 1, i = row & 15;  // row = 32 q + 16 h + i
-            rraw = h * 64 + 16 * q + i;                                // gate rows first, then up rows
+            const int h = (row >> 4) & 1, i = row & 15;  // row = 32 q + 16 h + i
+            rraw = h * 64 + 16 * q + i;                   // gate rows first, then up rows
         }
-        // byte offsets of this lane's stores inside an atom
-        const uint32_t rbase = (uint32_t)((row >> 3) * 1024 + (row & 7) * 128), rx = (uint32_t)(row & 7);
-        const uint32_t oL = rbase + (((uint32_t)t ^ rx) << 4), oH = rbase + (((uint32_t)(4 + t) ^ rx) << 4);
-        uint32_t o6[4];
-#pragma unroll
-        for (int s4 = 0; s4 < 4; s4++) o6[s4] = rbase + (((uint32_t)(2 * s4 + (t >> 1)) ^ rx) << 4) + 8 * (t & 1);
-        uint8_t *kq = sk + (size_t)(j >> 2) * PF_CONST_ROW;  // this quad's constants
+        const uint32_t tlane = (uint32_t)(32 * q) << 16;
         for (int sbk = 0; sbk < NB && ok; sbk++) {
             const int rs = sbk % PF_RAW_NS;
             if (!pf_wait_warp(&raw_full[rs], (sbk / PF_RAW_NS) & 1)) { ok = false; break; }
             const uint8_t *r = sr + rs * RAW;
-            // the lane's bytes of its row for the whole super-block; the
-            // constants of atom t go to the quad's table
-            uint32_t qw[12], c[8];
-            __half2 d2 = __float2half2_rn(0.0f);
+            uint32_t c[8], v[32];
             if (MODE == 2) {
-                const uint4 *src = reinterpret_cast<const uint4 *>(r + rraw * 192 + 48 * t);
+                // chunk t: ql words s4 = 0..3 and qh words 0, 1 of half g / 2
+                // (bytes 0-23 or 24-47 of the chunk: one 16-byte and one
+                // 8-byte load)
+                uint32_t qw[24];
 #pragma unroll
-                for (int v = 0; v < 3; v++) {
-                    const uint4 x = src[v];
-                    qw[4 * v] = x.x; qw[4 * v + 1] = x.y; qw[4 * v + 2] = x.z; qw[4 * v + 3] = x.w;
+                for (int t = 0; t < 4; t++) {
+                    const uint8_t *cp = r + rraw * PF_Q6_ROW + 48 * t;
+                    if (g < 2) {
+                        const uint4 a = *reinterpret_cast<const uint4 *>(cp);
+                        const uint2 b = *reinterpret_cast<const uint2 *>(cp + 16);
+                        qw[6 * t] = a.x; qw[6 * t + 1] = a.y; qw[6 * t + 2] = a.z; qw[6 * t + 3] = a.w;
+                        qw[6 * t + 4] = b.x; qw[6 * t + 5] = b.y;
+                    } else {
+                        const uint2 a = *reinterpret_cast<const uint2 *>(cp + 24);
+                        const uint4 b = *reinterpret_cast<const uint4 *>(cp + 32);
+                        qw[6 * t] = a.x; qw[6 * t + 1] = a.y; qw[6 * t + 2] = b.x; qw[6 * t + 3] = b.y;
+                        qw[6 * t + 4] = b.z; qw[6 * t + 5] = b.w;
+                    }
                 }
-                const uint32_t sc4 = reinterpret_cast<const uint32_t *>(r + 128 * 192 + rraw * 16)[t];
+                const uint32_t sc4 = reinterpret_cast<const uint32_t *>(r + 128 * PF_Q6_ROW + rraw * 16)[g];
                 pf_q6_consts(__half2float(reinterpret_cast<const __half *>(sd)[rraw * nbp + sbk]), sc4, c);
+                // the stage is released before the loaded words are used: the
+                // proxy fence orders these shared-memory reads before the
+                // next TMA write into the stage
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) pf_arrive(&raw_empty[rs]);
+                if (g == 0) pf_deq_q6<0>(qw, c, v);
+                else if (g == 1) pf_deq_q6<1>(qw, c, v);
+                else if (g == 2) pf_deq_q6<2>(qw, c, v);
+                else pf_deq_q6<3>(qw, c, v);
             } else {
                 const uint8_t *blk = r + rraw * MOE_Q4K_BYTES;
                 const uint4 hd = *reinterpret_cast<const uint4 *>(blk);
-                const uint4 x = *reinterpret_cast<const uint4 *>(blk + 16 + 32 * t);
-                const uint4 y = *reinterpret_cast<const uint4 *>(blk + 32 + 32 * t);
-                qw[0] = x.x; qw[1] = x.y; qw[2] = x.z; qw[3] = x.w;
-                qw[4] = y.x; qw[5] = y.y; qw[6] = y.z; qw[7] = y.w;
-                d2 = pf_u2h(__byte_perm(hd.x, 0, 0x1010));  // (d, d)
-                pf_q4_consts(hd, t, c);
-            }
-            __syncwarp();  // the previous super-block's constants are no longer read
-            *reinterpret_cast<uint4 *>(kq + 32 * t) = make_uint4(c[0], c[1], c[2], c[3]);
-            *reinterpret_cast<uint4 *>(kq + 32 * t + 16) = make_uint4(c[4], c[5], c[6], c[7]);
-            __syncwarp();
-            if (lane == 0) pf_arrive(&raw_empty[rs]);  // everything needed is in registers
+                uint32_t w[8];
 #pragma unroll
-            for (int a = 0; a < 4; a++) {
-                const int i = 4 * sbk + a, st = i % PF_NS;
-                if (!pf_wait_warp(&ab_empty[st], ((i / PF_NS) & 1) ^ 1)) { ok = false; break; }
-                uint8_t *atom = sa + st * PF_ATOM;
-                const uint4 k0 = *reinterpret_cast<const uint4 *>(kq + 32 * a);
-                const uint4 k1 = *reinterpret_cast<const uint4 *>(kq + 32 * a + 16);
-                const uint32_t ka[8] = {k0.x, k0.y, k0.z, k0.w, k1.x, k1.y, k1.z, k1.w};
-                if (MODE == 2) {
-                    if (a == 0) pf_deq_q6<0>(qw, ka, atom, o6);
-                    else if (a == 1) pf_deq_q6<1>(qw, ka, atom, o6);
-                    else if (a == 2) pf_deq_q6<2>(qw, ka, atom, o6);
-                    else pf_deq_q6<3>(qw, ka, atom, o6);
-                } else {
-                    pf_deq_q4(qw[2 * a], qw[2 * a + 1], d2, ka, atom, oL, oH);
+                for (int t = 0; t < 4; t++) {
+                    const uint2 x = *reinterpret_cast<const uint2 *>(blk + 16 + 32 * t + 8 * g);
+                    w[2 * t] = x.x;
+                    w[2 * t + 1] = x.y;
                 }
-                fence_async_smem();
+                fence_async_smem();  // as above
                 __syncwarp();
-                if (lane == 0) pf_arrive(&a_full[st]);
+                if (lane == 0) pf_arrive(&raw_empty[rs]);
+                pf_q4_consts(hd, g, c);
+                pf_deq_q4(w, pf_u2h(__byte_perm(hd.x, 0, 0x1010)), c, v);  // d in both halves
             }
+            const int i = 4 * sbk + g, sa = i % PF_NSA;
+            if (!pf_wait_warp(&a_empty[sa], ((i / PF_NSA) & 1) ^ 1)) { ok = false; break; }
+            tmem_fence_after();
+            tmem_st32(tmem_a + tlane + 32 * sa, v);
+            tmem_wait_st();
+            tmem_fence_before();
+            __syncwarp();
+            if (lane == 0) pf_arrive(&a_full[sa]);
         }
         // epilogue: this warp reads tensor-memory lanes 32 (warp % 4) .. + 31
         if (ok && pf_wait_warp(&acc_full, 0)) {
@@ -532,7 +528,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     }
     tmem_fence_before();
     __syncthreads();
-    if (warp == 1) tmem_free(tmem, PF_TILE_N);
+    if (warp == 1) tmem_free(tmem, 512);
 }
 
 // ===========================================================================
@@ -540,9 +536,8 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 // ===========================================================================
 static size_t pf_smem(int mode, int nbp) {
     const size_t raw = mode == 2 ? PF_RAW_Q6 : PF_RAW_Q4;
-    const size_t ns = mode == 2 ? PF_RAW_NS_Q6 : PF_RAW_NS_Q4;
-    return 1024 + (size_t)PF_NS * (PF_ATOM + PF_BATOM) + ns * raw + (mode == 2 ? 128 * 2 * (size_t)nbp : 0) +
-           (size_t)PF_TILE * PF_CONST_ROW;
+    return 1024 + (size_t)(mode == 2 ? PF_BRING_Q6 : PF_BRING_Q4) + PF_RAW_NS * raw +
+           (mode == 2 ? 128 * 2 * (size_t)nbp : 0);
 }
 
 template <int MODE>

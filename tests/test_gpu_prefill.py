@@ -1,7 +1,8 @@
 """tcgen05 (fifth-generation tensor core) building blocks used by the
 prefill GEMMs: a one-CTA fp16 GEMM through tensor memory, with the A tile
-written by threads in the 128-byte swizzle and B loaded by TMA, against an
-fp32 product of the same fp16 values."""
+written by threads either into 128-byte-swizzled shared memory or straight
+into tensor memory, and B loaded by TMA, against an fp32 product of the same
+fp16 values; then the prefill path against the oracle."""
 import ctypes as C
 import os
 import subprocess
@@ -21,19 +22,20 @@ def selftest_lib():
                     "-cudart", "static"], check=True, capture_output=True)
     lib = C.CDLL(so)
     lib.umma_selftest.restype = C.c_int
-    lib.umma_selftest.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p]
+    lib.umma_selftest.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
     return lib
 
 
 @pytest.mark.gpu
-def test_umma_f16_gemm_selftest(selftest_lib):
+@pytest.mark.parametrize("a_in_tmem", [0, 1])
+def test_umma_f16_gemm_selftest(selftest_lib, a_in_tmem):
     import torch
     g = torch.Generator().manual_seed(3)
     A = torch.randn(128, 256, generator=g).half()
     B = torch.randn(128, 256, generator=g).half()
     dA, dB = A.cuda(), B.cuda()
     dC = torch.zeros(128, 128, device="cuda")
-    rc = selftest_lib.umma_selftest(dA.data_ptr(), dB.data_ptr(), dC.data_ptr())
+    rc = selftest_lib.umma_selftest(dA.data_ptr(), dB.data_ptr(), dC.data_ptr(), a_in_tmem)
     assert rc == 0, rc
     ref = A.double() @ B.double().T
     err = float((dC.cpu().double() - ref).abs().max() / ref.abs().max())
