@@ -852,6 +852,9 @@ int moe_prefill_device(moe_ctx *c, int layer, const float *d_h, int T, float *d_
     int rc = check_layer(c, layer);
     if (rc) return rc;
     if (c->world > 1) return fail(c, MOE_ERR_STATE, "moe_prefill runs on one GPU (world_size 1)");
+    if (c->d.H % 256 || c->d.I % 128 || c->d.K > 63 || c->d.E > 1024)
+        return fail(c, MOE_ERR_ARG,
+                    "moe_prefill needs hidden %% 256 == 0, intermediate %% 128 == 0, top_k <= 63, n_experts <= 1024");
     CK(cudaSetDevice(c->device));
     if (moe_prefill_alloc(c->pf, c->d, T))
         return fail(c, MOE_ERR_CUDA, "prefill workspace for %d tokens could not be allocated", T);

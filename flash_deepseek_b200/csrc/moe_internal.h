@@ -103,6 +103,7 @@ struct MoePrefillWs {
     int cap = 0;                 // tokens
     float *part = nullptr, *logits = nullptr, *w = nullptr, *eo = nullptr;
     int *idx = nullptr, *counters = nullptr;
+    int *pcnt = nullptr, *pcur = nullptr;  // plan: per-expert counts and scatter cursors (E + 2 each)
     __half *xg = nullptr, *act = nullptr;
     MoePlan plan{};
     CUtensorMap tm_xg, tm_act;

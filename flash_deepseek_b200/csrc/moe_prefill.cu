@@ -35,17 +35,18 @@
 #include "moe_internal.h"
 #include "moe_umma.cuh"
 
-#define PF_TILE 128                // weight rows per tile (MMA M)
-#define PF_TILE_N 256              // pairs per tile (MMA N <= 256)
+#define PF_TILE 128                // weight rows per accumulator (MMA M)
+#define PF_RB 2                    // row blocks per CTA: M = 256 rows share each activation stage
+#define PF_TILE_N 128              // pairs per tile (MMA N <= 128)
 #define PF_ATOM 16384              // one 128-row x 128-byte activation box (64 columns of K)
-#define PF_NSA 8                   // A stages in tensor memory (32 columns each, after the accumulator)
-#define PF_BRING_Q4 (160 * 1024)   // activation ring: 10 stages of <= 128 pairs or 5 of <= 256
-#define PF_BRING_Q6 (128 * 1024)   // 8 or 4
-#define PF_NSB_MAX 10
-#define PF_RAW_Q4 (128 * 144)      // 128 Q4_K rows of one super-block
+#define PF_NSA 4                   // A stages in tensor memory (PF_RB x 32 columns each, after the accumulators)
+#define PF_NSB 6                   // activation stages
 #define PF_Q6_ROW 208              // Q6_K Q-plane row stride in shared memory (192 B used)
-#define PF_RAW_Q6 (128 * PF_Q6_ROW + 128 * 16)
-#define PF_RAW_NS 3                // raw super-block stages
+#define PF_RAW_Q4 (PF_RB * 128 * 144)                  // PF_RB x 128 Q4_K rows of one super-block
+#define PF_RAW_Q6 (PF_RB * 128 * (PF_Q6_ROW + 16))     // Q planes of both blocks, then their scale planes
+#define PF_RAW_NS_Q4 3             // raw super-block stages
+#define PF_RAW_NS_Q6 2
+#define PF_RAW_NS_MAX 3
 #define PF_DQ_WARPS 16                              // dequantize + epilogue (warps 3 ..)
 #define PF_DQ_WARP0 3                               // warps 0-2: weight TMA, MMA, activation TMA
 #define PF_THREADS (32 * (PF_DQ_WARP0 + PF_DQ_WARPS))
@@ -113,54 +114,95 @@ __device__ __forceinline__ uint32_t pf_h2(float a, float b) {
 }
 
 // ===========================================================================
-// plan: counting sort of the pairs by expert (one block).  Pair order inside
-// an expert follows arrival; every pair's result depends on its own token
-// and expert only, so the output does not.
+// plan: counting sort of the (token, slot) pairs by expert, in three
+// launches (count, offsets + tile list, scatter).  Pair order inside an
+// expert follows arrival; every pair's result depends on its own token and
+// expert only (each MMA column is an independent dot product), so the output
+// does not.  cnt[E + 1] / cur[E + 1] are zero between calls.
 // ===========================================================================
-__global__ void __launch_bounds__(1024) k_prefill_plan(MoeDims d, const int *__restrict__ idx,
-                                                       const float *__restrict__ w, int T, MoePlan plan) {
-    __shared__ int cnt[1025], off[1026], fill[1025], toff[1026];
-    const int E = d.E, K = d.K, NE = E + 1;
-    for (int e = threadIdx.x; e < NE; e += blockDim.x) cnt[e] = fill[e] = 0;
+#define PF_PLAN_PAIRS 2048  // pairs per block of the count and scatter kernels
+
+__global__ void __launch_bounds__(256) k_pf_count(MoeDims d, const int *__restrict__ idx, int n, int *__restrict__ cnt,
+                                                  int *__restrict__ error) {
+    __shared__ int h[1025];
+    for (int e = threadIdx.x; e < d.E; e += blockDim.x) h[e] = 0;
     __syncthreads();
-    for (int p = threadIdx.x; p < T * K; p += blockDim.x) {
+    const int p0 = blockIdx.x * PF_PLAN_PAIRS, p1 = min(n, p0 + PF_PLAN_PAIRS);
+    for (int p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
         const int e = idx[p];
-        if (e < 0 || e >= E) { atomicExch(plan.error, 1); continue; }
-        atomicAdd(&cnt[e], 1);
+        if (e < 0 || e >= d.E) { atomicExch(error, 1); continue; }
+        atomicAdd(&h[e], 1);
     }
-    if (threadIdx.x == 0) cnt[E] = T;
+    __syncthreads();
+    for (int e = threadIdx.x; e < d.E; e += blockDim.x)
+        if (h[e]) atomicAdd(&cnt[e], h[e]);
+}
+
+// one block: expert offsets (routed experts, then the shared expert's T
+// pairs), the tile list, the scatter cursors; clears cnt for the next call
+__global__ void __launch_bounds__(1024) k_pf_offsets(MoeDims d, int T, int *__restrict__ cnt, int *__restrict__ cur,
+                                                     MoePlan plan) {
+    __shared__ int c[1025], off[1026], toff[1026];
+    const int E = d.E, NE = E + 1;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) { c[e] = cnt[e]; cnt[e] = 0; }
+    if (threadIdx.x == 0) c[E] = T;
     __syncthreads();
     if (threadIdx.x == 0) {
         int a = 0, b = 0;
         for (int e = 0; e < NE; e++) {
             off[e] = a;
             toff[e] = b;
-            a += cnt[e];
-            b += (cnt[e] + PF_TILE_N - 1) / PF_TILE_N;
+            a += c[e];
+            b += (c[e] + PF_TILE_N - 1) / PF_TILE_N;
         }
-        off[NE] = a;
-        toff[NE] = b;
         plan.counts[0] = a;
         plan.counts[1] = b;
+        plan.counts[2] = off[E];
     }
     __syncthreads();
-    for (int e = threadIdx.x; e < NE; e += blockDim.x)
-        for (int c = 0; c * PF_TILE_N < cnt[e]; c++) {
-            plan.chunk_expert[toff[e] + c] = e;
-            plan.chunk_pair0[toff[e] + c] = off[e] + c * PF_TILE_N;
-            plan.chunk_ntok[toff[e] + c] = min(PF_TILE_N, cnt[e] - c * PF_TILE_N);
+    for (int e = threadIdx.x; e < NE; e += blockDim.x) {
+        cur[e] = off[e];
+        for (int k = 0; k * PF_TILE_N < c[e]; k++) {
+            plan.chunk_expert[toff[e] + k] = e;
+            plan.chunk_pair0[toff[e] + k] = off[e] + k * PF_TILE_N;
+            plan.chunk_ntok[toff[e] + k] = min(PF_TILE_N, c[e] - k * PF_TILE_N);
         }
-    for (int p = threadIdx.x; p < T * K; p += blockDim.x) {
+    }
+}
+
+// pairs of PF_PLAN_PAIRS per block: a block reserves each expert's range
+// with one global atomic, then places its pairs inside it
+__global__ void __launch_bounds__(256) k_pf_scatter(MoeDims d, const int *__restrict__ idx,
+                                                    const float *__restrict__ w, int T, int *__restrict__ cur,
+                                                    MoePlan plan) {
+    __shared__ int h[1025], base[1025];
+    const int E = d.E, K = d.K, n = T * K;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) h[e] = 0;
+    __syncthreads();
+    const int p0 = blockIdx.x * PF_PLAN_PAIRS, p1 = min(n, p0 + PF_PLAN_PAIRS);
+    for (int p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
+        const int e = idx[p];
+        if (e >= 0 && e < E) atomicAdd(&h[e], 1);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        base[e] = h[e] ? atomicAdd(&cur[e], h[e]) : 0;
+        h[e] = 0;
+    }
+    __syncthreads();
+    for (int p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
         const int t = p / K, k = p % K, e = idx[p];
         if (e < 0 || e >= E) { plan.slot_pair[t * (K + 1) + k] = -1; continue; }
-        const int pos = off[e] + atomicAdd(&fill[e], 1);
+        const int pos = base[e] + atomicAdd(&h[e], 1);
         plan.pair_expert[pos] = e;
         plan.pair_token[pos] = t;
         plan.pair_w[pos] = w[p];
         plan.slot_pair[t * (K + 1) + k] = pos;
     }
-    for (int t = threadIdx.x; t < T; t += blockDim.x) {
-        const int pos = off[E] + t;
+    // the shared expert's pairs: token order after the routed pairs
+    const int sh0 = plan.counts[2];
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < T; t += gridDim.x * blockDim.x) {
+        const int pos = sh0 + t;
         plan.pair_expert[pos] = E;
         plan.pair_token[pos] = t;
         plan.pair_w[pos] = 1.0f;
@@ -168,17 +210,48 @@ __global__ void __launch_bounds__(1024) k_prefill_plan(MoeDims d, const int *__r
     }
 }
 
-// fp16 rows of the pairs' tokens: xg[p] = half(x[token(p)])
-__global__ void __launch_bounds__(256) k_prefill_gather(const float *__restrict__ x, int H, MoePlan plan,
+// fp16 rows of the pairs, token-major: block t converts token t's row once
+// and writes it to each of its K + 1 pair rows, xg[p] = half(x[token(p)])
+__global__ void __launch_bounds__(256) k_prefill_gather(const float *__restrict__ x, int H, int K, MoePlan plan,
                                                         __half *__restrict__ xg) {
-    const int n = plan.counts[0];
-    for (int p = blockIdx.x; p < n; p += gridDim.x) {
-        const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)plan.pair_token[p] * H);
-        uint2 *dst = reinterpret_cast<uint2 *>(xg + (size_t)p * H);
-        for (int i = threadIdx.x; i < H / 4; i += blockDim.x) {
-            const float4 v = __ldg(src + i);
-            dst[i] = make_uint2(pf_h2(v.x, v.y), pf_h2(v.z, v.w));
+    __shared__ int pos[64];
+    const int t = blockIdx.x;
+    if (threadIdx.x <= K) pos[threadIdx.x] = plan.slot_pair[t * (K + 1) + threadIdx.x];
+    __syncthreads();
+    const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)t * H);
+    for (int i = threadIdx.x; i < H / 4; i += blockDim.x) {
+        const float4 v = __ldg(src + i);
+        const uint2 hv = make_uint2(pf_h2(v.x, v.y), pf_h2(v.z, v.w));
+        for (int k = 0; k <= K; k++)
+            if (pos[k] >= 0) reinterpret_cast<uint2 *>(xg + (size_t)pos[k] * H)[i] = hv;
+    }
+}
+
+// combine (infer.m:1915-1922), token-major: out[t] = sum_k w_k eo[pair(t, k)]
+// in slot order, then + the shared expert's row -- the same fp32 operations
+// in the same order as the decode combine, four columns per thread
+__global__ void __launch_bounds__(256) k_prefill_combine(MoeDims d, MoePlan plan, const float *__restrict__ eo,
+                                                         float *__restrict__ out) {
+    __shared__ int pos[64];
+    __shared__ float wk[64];
+    const int t = blockIdx.x, K = d.K, H = d.H;
+    if (threadIdx.x <= K) {
+        const int p = plan.slot_pair[t * (K + 1) + threadIdx.x];
+        pos[threadIdx.x] = p;
+        wk[threadIdx.x] = p >= 0 ? plan.pair_w[p] : 0.0f;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < H / 4; i += blockDim.x) {
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int k = 0; k < K; k++) {
+            if (pos[k] < 0) continue;
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(eo + (size_t)pos[k] * H) + i);
+            const float wv = wk[k];
+            acc = make_float4(fmaf(wv, v.x, acc.x), fmaf(wv, v.y, acc.y), fmaf(wv, v.z, acc.z), fmaf(wv, v.w, acc.w));
         }
+        const float4 sv = __ldg(reinterpret_cast<const float4 *>(eo + (size_t)pos[K] * H) + i);
+        reinterpret_cast<float4 *>(out + (size_t)t * H)[i] =
+            make_float4(acc.x + sv.x, acc.y + sv.y, acc.z + sv.z, acc.w + sv.w);
     }
 }
 
@@ -298,27 +371,30 @@ __device__ __forceinline__ void pf_deq_q6(const uint32_t (&q)[24], const uint32_
 
 // ===========================================================================
 // GEMM.  MODE 0: gate/up (Q4_K) -> act (fp16, SwiGLU); 1: down Q4_K -> eo;
-// 2: down Q6_K -> eo.  blockIdx.x = row block, blockIdx.y = tile (expert,
-// <= 256 pairs): the CTAs resident at one time work on a few tiles, so each
-// tile's activation slices are read from DRAM once and then hit in L2.
+// 2: down Q6_K -> eo.  blockIdx.x = row group (PF_RB row blocks of 128
+// accumulator rows; MODE 0: a block is 64 gate rows + the matching 64 up
+// rows), blockIdx.y = tile (expert, <= 128 pairs).  The CTAs resident at
+// one time work on a few tiles, so each tile's activation slices are read
+// from DRAM once and then hit in L2; each activation stage feeds PF_RB MMAs.
 // ===========================================================================
 template <int MODE>
 __global__ void __launch_bounds__(PF_THREADS, 1)
     k_prefill_gemm(MoeDims d, const __grid_constant__ MoeLayerDev L, MoePlan plan,
                    const __grid_constant__ CUtensorMap tmB, __half *__restrict__ act, float *__restrict__ eo) {
     constexpr int RAW = MODE == 2 ? PF_RAW_Q6 : PF_RAW_Q4;
-    constexpr int BRING = MODE == 2 ? PF_BRING_Q6 : PF_BRING_Q4;
+    constexpr int RAW_NS = MODE == 2 ? PF_RAW_NS_Q6 : PF_RAW_NS_Q4;
+    constexpr int QB = MODE == 2 ? 128 * PF_Q6_ROW : 128 * 144;  // one block's Q bytes in a raw stage
     extern __shared__ uint8_t pf_raw[];
     uint8_t *sm = pf_raw + ((1024u - (umma_smem_u32(pf_raw) & 1023u)) & 1023u);
-    uint8_t *sb = sm, *sr = sm + BRING;
-    uint8_t *sd = sr + PF_RAW_NS * RAW;  // Q6_K d plane of the tile (rows x 2 nb_pad bytes)
-    __shared__ __align__(8) uint64_t raw_full[PF_RAW_NS], raw_empty[PF_RAW_NS], a_full[PF_NSA], a_empty[PF_NSA],
-        b_full[PF_NSB_MAX], b_empty[PF_NSB_MAX], acc_full;
+    uint8_t *sb = sm, *sr = sm + PF_NSB * PF_ATOM;
+    uint8_t *sd = sr + RAW_NS * RAW;  // Q6_K d planes of the blocks (PF_RB x 128 rows x 2 nb_pad bytes)
+    __shared__ __align__(8) uint64_t raw_full[PF_RAW_NS_MAX], raw_empty[PF_RAW_NS_MAX], a_full[PF_NSA], a_empty[PF_NSA],
+        b_full[PF_NSB], b_empty[PF_NSB], acc_full;
     __shared__ uint32_t tmem_base;
     __shared__ int s_skip;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int tile = blockIdx.y, rb = blockIdx.x;
+    const int tile = blockIdx.y, rg = blockIdx.x;
     if (tid == 0) {
         int skip = tile >= plan.counts[1];
         if (!skip && MODE > 0) {
@@ -333,72 +409,72 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     const int slot = e == d.E ? L.n_local : e - L.e0;
     const int K = MODE == 0 ? d.H : d.I, NB = K / MOE_QK, n_atoms = 4 * NB;
     const int nbp = q6r_nb_pad(NB);
-    // activation stage: one 128-row box (16 KB) for a tile of <= 128 pairs, else two
-    const int BST = ntile > 128 ? 2 * PF_ATOM : PF_ATOM, NSB = BRING / BST;
     if (tid == 0) {
-        for (int i = 0; i < PF_RAW_NS; i++) { pf_mbar_init(&raw_full[i], 1); pf_mbar_init(&raw_empty[i], PF_DQ_WARPS); }
+        for (int i = 0; i < RAW_NS; i++) { pf_mbar_init(&raw_full[i], 1); pf_mbar_init(&raw_empty[i], PF_DQ_WARPS); }
         for (int i = 0; i < PF_NSA; i++) { pf_mbar_init(&a_full[i], 4); pf_mbar_init(&a_empty[i], 1); }
-        for (int i = 0; i < PF_NSB_MAX; i++) { pf_mbar_init(&b_full[i], 1); pf_mbar_init(&b_empty[i], 1); }
+        for (int i = 0; i < PF_NSB; i++) { pf_mbar_init(&b_full[i], 1); pf_mbar_init(&b_empty[i], 1); }
         pf_mbar_init(&acc_full, 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
     }
-    // tensor memory: accumulator in columns [0, 256), A stages in [256, 512)
+    // tensor memory: accumulator b in columns [128 b, 128 b + 128), A stage s
+    // of block b in [256 + 64 s + 32 b, + 32)
     if (warp == 1) tmem_alloc(&tmem_base, 512);
     tmem_fence_before();
     __syncthreads();
     tmem_fence_after();
-    const uint32_t tmem = tmem_base, tmem_a = tmem_base + PF_TILE_N;
+    const uint32_t tmem = tmem_base, tmem_a = tmem_base + PF_RB * PF_TILE_N;
     bool ok = true;
 
     if (warp == 0) {
-        // weight producer: the raw tiles of each super-block, PF_RAW_NS ahead
+        // weight producer: the raw tiles of each super-block, RAW_NS ahead
         // (the warp loops together, one elected lane issues the copies)
         const uint32_t leader = elect_one();
         int issued = 0;
         for (int sbk = 0; sbk < NB && ok; sbk++) {
-            const int rs = sbk % PF_RAW_NS;
-            if (!pf_wait_warp(&raw_empty[rs], ((sbk / PF_RAW_NS) & 1) ^ 1)) { ok = false; break; }
+            const int rs = sbk % RAW_NS;
+            if (!pf_wait_warp(&raw_empty[rs], ((sbk / RAW_NS) & 1) ^ 1)) { ok = false; break; }
             uint8_t *r = sr + rs * RAW;
             if (leader) {
-                if (MODE == 0) {
-                    pf_expect(&raw_full[rs], RAW);
-                    pf_tma3(r, &L.tm_gu, sbk * MOE_Q4K_BYTES, rb * 64, slot, &raw_full[rs]);
-                    pf_tma3(r + 64 * MOE_Q4K_BYTES, &L.tm_gu, sbk * MOE_Q4K_BYTES, d.I + rb * 64, slot,
-                            &raw_full[rs]);
-                } else if (MODE == 1) {
-                    pf_expect(&raw_full[rs], RAW);
-                    pf_tma3(r, &L.tm_d4, sbk * MOE_Q4K_BYTES, rb * 128, slot, &raw_full[rs]);
-                } else {
-                    pf_expect(&raw_full[rs], RAW + (sbk == 0 ? 128 * 2 * nbp : 0));
-                    pf_tma3(r, &L.tm_pf6q, sbk * 192, rb * 128, slot, &raw_full[rs]);
-                    pf_tma3(r + 128 * PF_Q6_ROW, &L.tm_d6s, sbk * 16, rb * 128, slot, &raw_full[rs]);
-                    if (sbk == 0) pf_tma3(sd, &L.tm_d6d, 0, rb * 128, slot, &raw_full[rs]);
+                pf_expect(&raw_full[rs], RAW + (MODE == 2 && sbk == 0 ? PF_RB * 128 * 2 * nbp : 0));
+#pragma unroll
+                for (int b = 0; b < PF_RB; b++) {
+                    const int blk = PF_RB * rg + b;
+                    if (MODE == 0) {
+                        pf_tma3(r + b * QB, &L.tm_gu, sbk * MOE_Q4K_BYTES, blk * 64, slot, &raw_full[rs]);
+                        pf_tma3(r + b * QB + 64 * MOE_Q4K_BYTES, &L.tm_gu, sbk * MOE_Q4K_BYTES, d.I + blk * 64, slot,
+                                &raw_full[rs]);
+                    } else if (MODE == 1) {
+                        pf_tma3(r + b * QB, &L.tm_d4, sbk * MOE_Q4K_BYTES, blk * 128, slot, &raw_full[rs]);
+                    } else {
+                        pf_tma3(r + b * QB, &L.tm_pf6q, sbk * 192, blk * 128, slot, &raw_full[rs]);
+                        pf_tma3(r + PF_RB * QB + b * 2048, &L.tm_d6s, sbk * 16, blk * 128, slot, &raw_full[rs]);
+                        if (sbk == 0) pf_tma3(sd + b * 256 * nbp, &L.tm_d6d, 0, blk * 128, slot, &raw_full[rs]);
+                    }
                 }
             }
             issued = sbk + 1;
         }
         if (!ok && leader) {
             atomicExch(plan.error, PF_ERR_TIMEOUT);
-            pf_drain(raw_full, issued, PF_RAW_NS);
+            pf_drain(raw_full, issued, RAW_NS);
         }
     } else if (warp == 2) {
-        // activation producer: the pairs' 64-column slices, NSB atoms ahead
+        // activation producer: the pairs' 64-column slices, PF_NSB atoms ahead
         const uint32_t leader = elect_one();
         int issued = 0;
         for (int i = 0; i < n_atoms && ok; i++) {
-            const int st = i % NSB;
-            if (!pf_wait_warp(&b_empty[st], ((i / NSB) & 1) ^ 1)) { ok = false; break; }
+            const int st = i % PF_NSB;
+            if (!pf_wait_warp(&b_empty[st], ((i / PF_NSB) & 1) ^ 1)) { ok = false; break; }
             if (leader) {
-                pf_expect(&b_full[st], BST);
-                pf_tma2(sb + st * BST, &tmB, 64 * i, p0, &b_full[st]);
-                if (ntile > 128) pf_tma2(sb + st * BST + PF_ATOM, &tmB, 64 * i, p0 + 128, &b_full[st]);
+                pf_expect(&b_full[st], PF_ATOM);
+                pf_tma2(sb + st * PF_ATOM, &tmB, 64 * i, p0, &b_full[st]);
             }
             issued = i + 1;
         }
         if (!ok && leader) {
             atomicExch(plan.error, PF_ERR_TIMEOUT);
-            pf_drain(b_full, issued, NSB);
+            pf_drain(b_full, issued, PF_NSB);
         }
     } else if (warp == 1) {
         // MMA issuer: the whole warp runs the loop (uniform operands), one
@@ -406,16 +482,19 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         // N = the tile's pairs rounded up to 16 (M = 128 takes N = 16 .. 256 in steps of 16)
         const uint32_t idesc = umma_idesc_f16(PF_TILE, (ntile + 15) & ~15);
         for (int i = 0; i < n_atoms && ok; i++) {
-            const int sa = i % PF_NSA, sbq = i % NSB;
-            if (!pf_wait_warp(&a_full[sa], (i / PF_NSA) & 1) || !pf_wait_warp(&b_full[sbq], (i / NSB) & 1)) {
+            const int sa = i % PF_NSA, sbq = i % PF_NSB;
+            if (!pf_wait_warp(&a_full[sa], (i / PF_NSA) & 1) || !pf_wait_warp(&b_full[sbq], (i / PF_NSB) & 1)) {
                 ok = false;
                 break;
             }
             tmem_fence_after();
-            const uint32_t b0 = umma_smem_u32(sb + sbq * BST);
+            const uint32_t b0 = umma_smem_u32(sb + sbq * PF_ATOM);
 #pragma unroll
-            for (int kk = 0; kk < 4; kk++)
-                umma_f16_ta_warp(tmem, tmem_a + 32 * sa + 8 * kk, umma_desc_sw128(b0 + 32 * kk), idesc, (i | kk) != 0);
+            for (int b = 0; b < PF_RB; b++)
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++)
+                    umma_f16_ta_warp(tmem + PF_TILE_N * b, tmem_a + 64 * sa + 32 * b + 8 * kk,
+                                     umma_desc_sw128(b0 + 32 * kk), idesc, (i | kk) != 0);
             umma_commit_warp(&a_empty[sa]);
             umma_commit_warp(&b_empty[sbq]);
         }
@@ -427,99 +506,109 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         }
     } else {
         // dequantization: warp (q = warp % 4, g) owns tensor-memory lanes
-        // 32 q .. 32 q + 31 (A rows; lane = row) and atom g of every super-block
+        // 32 q .. 32 q + 31 (A rows; lane = row) of both blocks, and atom g
+        // of every super-block
         const int q = warp & 3, g = (warp - PF_DQ_WARP0) >> 2, row = 32 * q + lane;
-        int rraw = row;  // raw tile row holding A row `row`
+        int rraw = row;  // raw tile row (inside a block) holding A row `row`
         if (MODE == 0) {
             const int h = (row >> 4) & 1, i = row & 15;  // row = 32 q + 16 h + i
             rraw = h * 64 + 16 * q + i;                   // gate rows first, then up rows
         }
         const uint32_t tlane = (uint32_t)(32 * q) << 16;
         for (int sbk = 0; sbk < NB && ok; sbk++) {
-            const int rs = sbk % PF_RAW_NS;
-            if (!pf_wait_warp(&raw_full[rs], (sbk / PF_RAW_NS) & 1)) { ok = false; break; }
+            const int rs = sbk % RAW_NS;
+            if (!pf_wait_warp(&raw_full[rs], (sbk / RAW_NS) & 1)) { ok = false; break; }
             const uint8_t *r = sr + rs * RAW;
-            uint32_t c[8], v[32];
-            if (MODE == 2) {
-                // chunk t: ql words s4 = 0..3 and qh words 0, 1 of half g / 2
-                // (bytes 0-23 or 24-47 of the chunk: one 16-byte and one
-                // 8-byte load)
-                uint32_t qw[24];
+            // atom g of this lane's rows in both blocks, dequantized into
+            // registers before the tensor-memory stage is waited for
+            uint32_t v[PF_RB][32];
 #pragma unroll
-                for (int t = 0; t < 4; t++) {
-                    const uint8_t *cp = r + rraw * PF_Q6_ROW + 48 * t;
-                    if (g < 2) {
-                        const uint4 a = *reinterpret_cast<const uint4 *>(cp);
-                        const uint2 b = *reinterpret_cast<const uint2 *>(cp + 16);
-                        qw[6 * t] = a.x; qw[6 * t + 1] = a.y; qw[6 * t + 2] = a.z; qw[6 * t + 3] = a.w;
-                        qw[6 * t + 4] = b.x; qw[6 * t + 5] = b.y;
-                    } else {
-                        const uint2 a = *reinterpret_cast<const uint2 *>(cp + 24);
-                        const uint4 b = *reinterpret_cast<const uint4 *>(cp + 32);
-                        qw[6 * t] = a.x; qw[6 * t + 1] = a.y; qw[6 * t + 2] = b.x; qw[6 * t + 3] = b.y;
-                        qw[6 * t + 4] = b.z; qw[6 * t + 5] = b.w;
+            for (int b = 0; b < PF_RB; b++) {
+                uint32_t c[8];
+                if constexpr (MODE == 2) {
+                    // chunk t: ql words s4 = 0..3 and qh words 0, 1 of half g / 2
+                    // (bytes 0-23 or 24-47 of the chunk: a 16-byte and an 8-byte load)
+                    uint32_t w[24];
+#pragma unroll
+                    for (int t = 0; t < 4; t++) {
+                        const uint8_t *cp = r + b * QB + rraw * PF_Q6_ROW + 48 * t;
+                        if (g < 2) {
+                            const uint4 x = *reinterpret_cast<const uint4 *>(cp);
+                            const uint2 y = *reinterpret_cast<const uint2 *>(cp + 16);
+                            w[6 * t] = x.x; w[6 * t + 1] = x.y; w[6 * t + 2] = x.z; w[6 * t + 3] = x.w;
+                            w[6 * t + 4] = y.x; w[6 * t + 5] = y.y;
+                        } else {
+                            const uint2 x = *reinterpret_cast<const uint2 *>(cp + 24);
+                            const uint4 y = *reinterpret_cast<const uint4 *>(cp + 32);
+                            w[6 * t] = x.x; w[6 * t + 1] = x.y; w[6 * t + 2] = y.x; w[6 * t + 3] = y.y;
+                            w[6 * t + 4] = y.z; w[6 * t + 5] = y.w;
+                        }
                     }
-                }
-                const uint32_t sc4 = reinterpret_cast<const uint32_t *>(r + 128 * PF_Q6_ROW + rraw * 16)[g];
-                pf_q6_consts(__half2float(reinterpret_cast<const __half *>(sd)[rraw * nbp + sbk]), sc4, c);
-                // the stage is released before the loaded words are used: the
-                // proxy fence orders these shared-memory reads before the
-                // next TMA write into the stage
-                fence_async_smem();
-                __syncwarp();
-                if (lane == 0) pf_arrive(&raw_empty[rs]);
-                if (g == 0) pf_deq_q6<0>(qw, c, v);
-                else if (g == 1) pf_deq_q6<1>(qw, c, v);
-                else if (g == 2) pf_deq_q6<2>(qw, c, v);
-                else pf_deq_q6<3>(qw, c, v);
-            } else {
-                const uint8_t *blk = r + rraw * MOE_Q4K_BYTES;
-                const uint4 hd = *reinterpret_cast<const uint4 *>(blk);
-                uint32_t w[8];
+                    const uint32_t sc4 = reinterpret_cast<const uint32_t *>(r + PF_RB * QB + b * 2048 + rraw * 16)[g];
+                    const float d6 = __half2float(reinterpret_cast<const __half *>(sd + b * 256 * nbp)[rraw * nbp + sbk]);
+                    pf_q6_consts(d6, sc4, c);
+                    if (g == 0) pf_deq_q6<0>(w, c, v[b]);
+                    else if (g == 1) pf_deq_q6<1>(w, c, v[b]);
+                    else if (g == 2) pf_deq_q6<2>(w, c, v[b]);
+                    else pf_deq_q6<3>(w, c, v[b]);
+                } else {
+                    const uint8_t *blk = r + b * QB + rraw * MOE_Q4K_BYTES;
+                    const uint4 hd = *reinterpret_cast<const uint4 *>(blk);
+                    uint32_t w[8];
 #pragma unroll
-                for (int t = 0; t < 4; t++) {
-                    const uint2 x = *reinterpret_cast<const uint2 *>(blk + 16 + 32 * t + 8 * g);
-                    w[2 * t] = x.x;
-                    w[2 * t + 1] = x.y;
+                    for (int t = 0; t < 4; t++) {
+                        const uint2 x = *reinterpret_cast<const uint2 *>(blk + 16 + 32 * t + 8 * g);
+                        w[2 * t] = x.x;
+                        w[2 * t + 1] = x.y;
+                    }
+                    pf_q4_consts(hd, g, c);
+                    pf_deq_q4(w, pf_u2h(__byte_perm(hd.x, 0, 0x1010)), c, v[b]);  // d in both halves
                 }
-                fence_async_smem();  // as above
-                __syncwarp();
-                if (lane == 0) pf_arrive(&raw_empty[rs]);
-                pf_q4_consts(hd, g, c);
-                pf_deq_q4(w, pf_u2h(__byte_perm(hd.x, 0, 0x1010)), c, v);  // d in both halves
             }
+            // all reads of the stage are done (their values are consumed): the
+            // proxy fence orders them before the next TMA write into it
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) pf_arrive(&raw_empty[rs]);
             const int i = 4 * sbk + g, sa = i % PF_NSA;
             if (!pf_wait_warp(&a_empty[sa], ((i / PF_NSA) & 1) ^ 1)) { ok = false; break; }
             tmem_fence_after();
-            tmem_st32(tmem_a + tlane + 32 * sa, v);
+#pragma unroll
+            for (int b = 0; b < PF_RB; b++) tmem_st32(tmem_a + tlane + 64 * sa + 32 * b, v[b]);
             tmem_wait_st();
             tmem_fence_before();
             __syncwarp();
             if (lane == 0) pf_arrive(&a_full[sa]);
         }
         // epilogue: this warp reads tensor-memory lanes 32 (warp % 4) .. + 31
+        // of both accumulators
         if (ok && pf_wait_warp(&acc_full, 0)) {
             tmem_fence_after();
             // PF_DQ_WARPS / 4 warps per lane quarter: column chunks alternate between them
-            const int q = warp & 3, sub = (warp - PF_DQ_WARP0) >> 2;
-            for (int c = 16 * sub; c < PF_TILE_N; c += 16 * (PF_DQ_WARPS / 4)) {
-                if (c >= ntile) break;
-                float v[16];
-                tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + c, v);
-                if (MODE == 0) {
-                    // lanes 0-15: gate rows, 16-31: the matching up rows
-                    const int i = lane & 15, rI = rb * 64 + 16 * q + i;
+            const int sub = (warp - PF_DQ_WARP0) >> 2;
+#pragma unroll 1
+            for (int b = 0; b < PF_RB; b++) {
+                const int blk = PF_RB * rg + b;
+                for (int c = 16 * sub; c < PF_TILE_N; c += 16 * (PF_DQ_WARPS / 4)) {
+                    if (c >= ntile) break;
+                    float v[16];
+                    tmem_ld16(tmem + PF_TILE_N * b + ((uint32_t)(32 * q) << 16) + c, v);
+                    if (MODE == 0) {
+                        // lanes 0-15: gate rows, 16-31: the matching up rows
+                        const int i = lane & 15, rI = blk * 64 + 16 * q + i;
 #pragma unroll
-                    for (int j = 0; j < 16; j++) {
-                        const float u = __shfl_xor_sync(0xffffffffu, v[j], 16);
-                        if (lane < 16 && c + j < ntile)
-                            act[(size_t)(p0 + c + j) * d.I + rI] = __float2half_rn((v[j] / (1.0f + expf(-v[j]))) * u);
+                        for (int j = 0; j < 16; j++) {
+                            const float u = __shfl_xor_sync(0xffffffffu, v[j], 16);
+                            if (lane < 16 && c + j < ntile)
+                                act[(size_t)(p0 + c + j) * d.I + rI] =
+                                    __float2half_rn((v[j] / (1.0f + expf(-v[j]))) * u);
+                        }
+                    } else {
+                        const int rH = blk * 128 + 32 * q + lane;
+#pragma unroll
+                        for (int j = 0; j < 16; j++)
+                            if (c + j < ntile) eo[(size_t)(p0 + c + j) * d.H + rH] = v[j];
                     }
-                } else {
-                    const int rH = rb * 128 + 32 * q + lane;
-#pragma unroll
-                    for (int j = 0; j < 16; j++)
-                        if (c + j < ntile) eo[(size_t)(p0 + c + j) * d.H + rH] = v[j];
                 }
             }
         } else if (lane == 0) {
@@ -536,27 +625,27 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 // ===========================================================================
 static size_t pf_smem(int mode, int nbp) {
     const size_t raw = mode == 2 ? PF_RAW_Q6 : PF_RAW_Q4;
-    return 1024 + (size_t)(mode == 2 ? PF_BRING_Q6 : PF_BRING_Q4) + PF_RAW_NS * raw +
-           (mode == 2 ? 128 * 2 * (size_t)nbp : 0);
+    return 1024 + (size_t)PF_NSB * PF_ATOM + (mode == 2 ? PF_RAW_NS_Q6 : PF_RAW_NS_Q4) * raw +
+           (mode == 2 ? PF_RB * 128 * 2 * (size_t)nbp : 0);
 }
 
 template <int MODE>
 static void pf_launch(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const CUtensorMap &tmB,
-                      __half *act, float *eo, int max_tiles, int row_blocks, cudaStream_t s, uint64_t *launches) {
+                      __half *act, float *eo, int max_tiles, int row_groups, cudaStream_t s, uint64_t *launches) {
     const size_t smem = pf_smem(MODE, q6r_nb_pad(d.I / MOE_QK));
     static size_t attr = 0;
     if (smem > attr) {
         cudaFuncSetAttribute(k_prefill_gemm<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         attr = smem;
     }
-    k_prefill_gemm<MODE><<<dim3(row_blocks, max_tiles), PF_THREADS, smem, s>>>(d, L, plan, tmB, act, eo);
+    k_prefill_gemm<MODE><<<dim3(row_groups, max_tiles), PF_THREADS, smem, s>>>(d, L, plan, tmB, act, eo);
     LAUNCH_COUNT(launches);
 }
 
 void moe_prefill_free(MoePrefillWs &ws) {
     void *b[] = {ws.part, ws.logits, ws.w, ws.eo, ws.idx, ws.counters, ws.xg, ws.act, ws.plan.counts,
                  ws.plan.pair_expert, ws.plan.pair_token, ws.plan.pair_w, ws.plan.chunk_expert, ws.plan.chunk_pair0,
-                 ws.plan.chunk_ntok, ws.plan.slot_pair, ws.plan.error};
+                 ws.plan.chunk_ntok, ws.plan.slot_pair, ws.plan.error, ws.pcnt, ws.pcur};
     for (void *p : b) cudaFree(p);
     ws = MoePrefillWs{};
 }
@@ -588,9 +677,12 @@ int moe_prefill_alloc(MoePrefillWs &ws, const MoeDims &d, int T) {
     PFA(ws.plan.chunk_ntok, sizeof(int) * tiles);
     PFA(ws.plan.slot_pair, sizeof(int) * (size_t)cap * (d.K + 1));
     PFA(ws.plan.error, sizeof(int));
+    PFA(ws.pcnt, sizeof(int) * (size_t)(d.E + 2));
+    PFA(ws.pcur, sizeof(int) * (size_t)(d.E + 2));
 #undef PFA
     if (e == cudaSuccess) e = cudaMemset(ws.counters, 0, sizeof(int) * ((size_t)(d.E + 31) / 32) * (cap / 64 + 1));
     if (e == cudaSuccess) e = cudaMemset(ws.plan.error, 0, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(ws.pcnt, 0, sizeof(int) * (size_t)(d.E + 2));
     if (e == cudaSuccess) e = cudaMemset(ws.xg, 0, sizeof(__half) * P * d.H);
     if (e == cudaSuccess) e = cudaMemset(ws.act, 0, sizeof(__half) * P * d.I);
     if (e != cudaSuccess) {
@@ -608,16 +700,19 @@ int moe_prefill_alloc(MoePrefillWs &ws, const MoeDims &d, int T) {
 
 void moe_launch_prefill_experts(const MoeDims &d, const MoeLayerDev &L, MoePrefillWs &ws, const float *x, int T,
                                 float *out, cudaStream_t s, uint64_t *launches) {
-    k_prefill_plan<<<1, 1024, 0, s>>>(d, ws.idx, ws.w, T, ws.plan);
-    LAUNCH_COUNT(launches);
+    const int n = T * d.K, nblk = (n + PF_PLAN_PAIRS - 1) / PF_PLAN_PAIRS;
+    k_pf_count<<<nblk, 256, 0, s>>>(d, ws.idx, n, ws.pcnt, ws.plan.error);
+    k_pf_offsets<<<1, 1024, 0, s>>>(d, T, ws.pcnt, ws.pcur, ws.plan);
+    k_pf_scatter<<<nblk, 256, 0, s>>>(d, ws.idx, ws.w, T, ws.pcur, ws.plan);
+    k_prefill_gather<<<T, 256, 0, s>>>(x, d.H, d.K, ws.plan, ws.xg);
+    if (launches) *launches += 4;
     const int P = T * (d.K + 1);
-    k_prefill_gather<<<P < 148 * 8 ? P : 148 * 8, 256, 0, s>>>(x, d.H, ws.plan, ws.xg);
-    LAUNCH_COUNT(launches);
     const int max_tiles = d.E + 1 + P / PF_TILE_N + 1;
-    pf_launch<0>(d, L, ws.plan, ws.tm_xg, ws.act, nullptr, max_tiles, d.I / 64, s, launches);
+    pf_launch<0>(d, L, ws.plan, ws.tm_xg, ws.act, nullptr, max_tiles, d.I / (64 * PF_RB), s, launches);
     if (L.down_type == MOE_TYPE_Q6_K || L.sh_down_type == MOE_TYPE_Q6_K)
-        pf_launch<2>(d, L, ws.plan, ws.tm_act, nullptr, ws.eo, max_tiles, d.H / 128, s, launches);
+        pf_launch<2>(d, L, ws.plan, ws.tm_act, nullptr, ws.eo, max_tiles, d.H / (128 * PF_RB), s, launches);
     if (L.down_type == MOE_TYPE_Q4_K || L.sh_down_type == MOE_TYPE_Q4_K)
-        pf_launch<1>(d, L, ws.plan, ws.tm_act, nullptr, ws.eo, max_tiles, d.H / 128, s, launches);
-    moe_launch_combine(d, ws.plan, ws.eo, T, 1, 1, nullptr, out, s, launches);
+        pf_launch<1>(d, L, ws.plan, ws.tm_act, nullptr, ws.eo, max_tiles, d.H / (128 * PF_RB), s, launches);
+    k_prefill_combine<<<T, 256, 0, s>>>(d, ws.plan, ws.eo, out);
+    LAUNCH_COUNT(launches);
 }
