@@ -861,8 +861,7 @@ int moe_prefill_device(moe_ctx *c, int layer, const float *d_h, int T, float *d_
     cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
     MoeLayerDev &L = c->layers[layer];
     const MoeDims &d = c->d;
-    moe_launch_router_logits(L.router, d_h, T, d.H, d.E, c->pf.part, d.H / MOE_QK, c->pf.logits, c->pf.counters, s,
-                             &c->launches);
+    moe_launch_prefill_router(d, L.router, c->pf, d_h, T, s, &c->launches);
     moe_launch_route_and_plan(d, nullptr, 0, c->pf.logits, L.bias, L.logit_bias, 0, nullptr, nullptr, T, c->pf.idx,
                               c->pf.w, d_h, nullptr, 1, 0, c->pf.plan, c->counter, s, &c->launches);
     moe_launch_prefill_experts(d, L, c->pf, d_h, T, d_out, s, &c->launches);

@@ -105,11 +105,15 @@ struct MoePrefillWs {
     int *idx = nullptr, *counters = nullptr;
     int *pcnt = nullptr, *pcur = nullptr;  // plan: per-expert counts and scatter cursors (E + 2 each)
     __half *xg = nullptr, *act = nullptr;
+    __half *wh = nullptr, *wl = nullptr, *xh = nullptr, *xl = nullptr;  // fp16 hi/lo splits for the router
     MoePlan plan{};
-    CUtensorMap tm_xg, tm_act;
+    CUtensorMap tm_xg, tm_act, tm_wh, tm_wl, tm_xh, tm_xl;
 };
 int moe_prefill_alloc(MoePrefillWs &ws, const MoeDims &d, int T);
 void moe_prefill_free(MoePrefillWs &ws);
+// router logits of T tokens into ws.logits (tensor cores, fp16 hi/lo splits)
+void moe_launch_prefill_router(const MoeDims &d, const float *Wr, MoePrefillWs &ws, const float *x, int T,
+                               cudaStream_t s, uint64_t *launches);
 // plan + gather + the two tcgen05 GEMMs + combine, after ws.idx / ws.w hold
 // the routing of T tokens
 void moe_launch_prefill_experts(const MoeDims &d, const MoeLayerDev &L, MoePrefillWs &ws, const float *x, int T,

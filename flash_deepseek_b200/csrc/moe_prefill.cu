@@ -210,20 +210,20 @@ __global__ void __launch_bounds__(256) k_pf_scatter(MoeDims d, const int *__rest
     }
 }
 
-// fp16 rows of the pairs, token-major: block t converts token t's row once
-// and writes it to each of its K + 1 pair rows, xg[p] = half(x[token(p)])
-__global__ void __launch_bounds__(256) k_prefill_gather(const float *__restrict__ x, int H, int K, MoePlan plan,
+// fp16 rows of the pairs, token-major: block t copies token t's fp16 row
+// (xh = half(x), written by the router's split) to each of its K + 1 pair
+// rows, xg[p] = half(x[token(p)])
+__global__ void __launch_bounds__(256) k_prefill_gather(const __half *__restrict__ xh, int H, int K, MoePlan plan,
                                                         __half *__restrict__ xg) {
     __shared__ int pos[64];
     const int t = blockIdx.x;
     if (threadIdx.x <= K) pos[threadIdx.x] = plan.slot_pair[t * (K + 1) + threadIdx.x];
     __syncthreads();
-    const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)t * H);
-    for (int i = threadIdx.x; i < H / 4; i += blockDim.x) {
-        const float4 v = __ldg(src + i);
-        const uint2 hv = make_uint2(pf_h2(v.x, v.y), pf_h2(v.z, v.w));
+    const uint4 *src = reinterpret_cast<const uint4 *>(xh + (size_t)t * H);
+    for (int i = threadIdx.x; i < H / 8; i += blockDim.x) {
+        const uint4 v = __ldg(src + i);
         for (int k = 0; k <= K; k++)
-            if (pos[k] >= 0) reinterpret_cast<uint2 *>(xg + (size_t)pos[k] * H)[i] = hv;
+            if (pos[k] >= 0) reinterpret_cast<uint4 *>(xg + (size_t)pos[k] * H)[i] = v;
     }
 }
 
@@ -621,6 +621,162 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 }
 
 // ===========================================================================
+// router logits for many tokens on the tensor cores, to fp32 accuracy:
+// logits = W x with W (E x H) and x (T x H) fp32 (the reference's fp32 sgemv,
+// infer.m:1881).  Both are split into fp16 pairs, W * 256 = Wh + Wl and
+// x = xh + xl (each hi/lo pair holds 22 significant bits; the scale 2^8 is
+// exact and keeps Wl out of the fp16 subnormal range), and
+//   256 W x = Wh xh + Wh xl + Wl xh   (+ Wl xl, below 2^-22 relative, dropped)
+// with fp16 x fp16 products exact in the fp32 accumulator.  The CTA computes
+// 128 experts x 128 tokens over one of nsplit slices of K (nsplit sized so
+// that the grid covers the SMs); the slices are summed in a fixed order and
+// scaled by 1/256 (exact).
+// ===========================================================================
+#define RT_NS 3
+#define RT_THREADS 192  // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+#define RT_SCALE 256.0f
+
+// dst_hi = half(src * scale), dst_lo = half(src * scale - dst_hi), n % 4 == 0
+__global__ void __launch_bounds__(256) k_pf_split(const float *__restrict__ src, size_t n, float scale,
+                                                  __half *__restrict__ hi, __half *__restrict__ lo) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n / 4; i += (size_t)gridDim.x * blockDim.x) {
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(src) + i);
+        const float a[4] = {v.x * scale, v.y * scale, v.z * scale, v.w * scale};
+        __half h[4], l[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            h[j] = __float2half_rn(a[j]);
+            l[j] = __float2half_rn(a[j] - __half2float(h[j]));
+        }
+        reinterpret_cast<uint2 *>(hi)[i] = make_uint2(pf_h2u(__halves2half2(h[0], h[1])), pf_h2u(__halves2half2(h[2], h[3])));
+        reinterpret_cast<uint2 *>(lo)[i] = make_uint2(pf_h2u(__halves2half2(l[0], l[1])), pf_h2u(__halves2half2(l[2], l[3])));
+    }
+}
+
+// part[split][t][e] for 128 experts (blockIdx.x) x 128 tokens (blockIdx.y),
+// K slice blockIdx.z of nsplit
+__global__ void __launch_bounds__(RT_THREADS, 1)
+    k_pf_router(int T, int H, int E, int nsplit, const __grid_constant__ CUtensorMap tm_wh, const __grid_constant__ CUtensorMap tm_wl,
+                const __grid_constant__ CUtensorMap tm_xh, const __grid_constant__ CUtensorMap tm_xl,
+                float *__restrict__ part, int *__restrict__ error) {
+    extern __shared__ uint8_t rt_raw[];
+    uint8_t *sm = rt_raw + ((1024u - (umma_smem_u32(rt_raw) & 1023u)) & 1023u);  // RT_NS stages of 4 boxes
+    __shared__ __align__(8) uint64_t full[RT_NS], empty[RT_NS], acc_full;
+    __shared__ uint32_t tmem_base;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int m0 = 128 * blockIdx.x, n0 = 128 * blockIdx.y, split = blockIdx.z;
+    const int na = H / 64 / nsplit, a0 = na * split;
+    if (tid == 0) {
+        for (int i = 0; i < RT_NS; i++) { pf_mbar_init(&full[i], 1); pf_mbar_init(&empty[i], 1); }
+        pf_mbar_init(&acc_full, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+    }
+    if (warp == 1) tmem_alloc(&tmem_base, 128);
+    tmem_fence_before();
+    __syncthreads();
+    tmem_fence_after();
+    const uint32_t tmem = tmem_base;
+    bool ok = true;
+    if (warp == 0) {
+        const uint32_t leader = elect_one();
+        int issued = 0;
+        for (int i = 0; i < na && ok; i++) {
+            const int st = i % RT_NS;
+            if (!pf_wait_warp(&empty[st], ((i / RT_NS) & 1) ^ 1)) { ok = false; break; }
+            if (leader) {
+                uint8_t *b = sm + st * 4 * PF_ATOM;
+                const int kx = 64 * (a0 + i);
+                pf_expect(&full[st], 4 * PF_ATOM);
+                pf_tma2(b, &tm_wh, kx, m0, &full[st]);
+                pf_tma2(b + PF_ATOM, &tm_wl, kx, m0, &full[st]);
+                pf_tma2(b + 2 * PF_ATOM, &tm_xh, kx, n0, &full[st]);
+                pf_tma2(b + 3 * PF_ATOM, &tm_xl, kx, n0, &full[st]);
+            }
+            issued = i + 1;
+        }
+        if (!ok && leader) {
+            atomicExch(error, PF_ERR_TIMEOUT);
+            pf_drain(full, issued, RT_NS);
+        }
+    } else if (warp == 1) {
+        const uint32_t idesc = umma_idesc_f16(128, 128);
+        for (int i = 0; i < na && ok; i++) {
+            const int st = i % RT_NS;
+            if (!pf_wait_warp(&full[st], (i / RT_NS) & 1)) { ok = false; break; }
+            tmem_fence_after();
+            const uint32_t b = umma_smem_u32(sm + st * 4 * PF_ATOM);
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) {
+                const uint64_t wh = umma_desc_sw128(b + 32 * kk), wl = umma_desc_sw128(b + PF_ATOM + 32 * kk);
+                const uint64_t xh = umma_desc_sw128(b + 2 * PF_ATOM + 32 * kk), xl = umma_desc_sw128(b + 3 * PF_ATOM + 32 * kk);
+                umma_f16_warp(tmem, wh, xh, idesc, (i | kk) != 0);
+                umma_f16_warp(tmem, wh, xl, idesc, 1);
+                umma_f16_warp(tmem, wl, xh, idesc, 1);
+            }
+            umma_commit_warp(&empty[st]);
+        }
+        umma_commit_warp(&acc_full);
+        if (!ok) {
+            if (lane == 0) atomicExch(error, PF_ERR_TIMEOUT);
+            pf_wait_warp(&acc_full, 0);
+        }
+    } else {
+        // tensor-memory lanes 32 (warp % 4) .. + 31 = experts, columns = tokens
+        if (pf_wait_warp(&acc_full, 0)) {
+            tmem_fence_after();
+            const int q = warp & 3, e = m0 + 32 * q + lane;
+            for (int c = 0; c < 128; c += 16) {
+                if (n0 + c >= T) break;
+                float v[16];
+                tmem_ld16(tmem + ((uint32_t)(32 * q) << 16) + c, v);
+#pragma unroll
+                for (int j = 0; j < 16; j++)
+                    if (n0 + c + j < T && e < E) part[((size_t)split * T + n0 + c + j) * E + e] = v[j];
+            }
+        } else if (lane == 0) {
+            atomicExch(error, PF_ERR_TIMEOUT);
+        }
+    }
+    tmem_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_free(tmem, 128);
+}
+
+// logits = (part[0] + part[1] + ...) / 256, in slice order
+__global__ void __launch_bounds__(256) k_pf_router_sum(const float *__restrict__ part, size_t n, int nsplit,
+                                                       float *__restrict__ logits) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        float a = part[i];
+        for (int k = 1; k < nsplit; k++) a += part[(size_t)k * n + i];
+        logits[i] = a * (1.0f / RT_SCALE);
+    }
+}
+
+void moe_launch_prefill_router(const MoeDims &d, const float *Wr, MoePrefillWs &ws, const float *x, int T,
+                               cudaStream_t s, uint64_t *launches) {
+    const size_t nw = (size_t)d.E * d.H, nx = (size_t)T * d.H;
+    k_pf_split<<<(unsigned)((nw / 4 + 255) / 256), 256, 0, s>>>(Wr, nw, RT_SCALE, ws.wh, ws.wl);
+    k_pf_split<<<(unsigned)((nx / 4 + 255) / 256 < 148 * 16 ? (nx / 4 + 255) / 256 : 148 * 16), 256, 0, s>>>(
+        x, nx, 1.0f, ws.xh, ws.xl);
+    const size_t smem = 1024 + (size_t)RT_NS * 4 * PF_ATOM;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(k_pf_router, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        attr = true;
+    }
+    // K slices: a power of two dividing H / 64, up to 16, until the grid covers the SMs
+    const int tiles = ((d.E + 127) / 128) * ((T + 127) / 128);
+    int nsplit = 1;
+    while (nsplit < 16 && tiles * nsplit < 148 && (d.H / 64) % (2 * nsplit) == 0) nsplit *= 2;
+    k_pf_router<<<dim3((d.E + 127) / 128, (T + 127) / 128, nsplit), RT_THREADS, smem, s>>>(
+        T, d.H, d.E, nsplit, ws.tm_wh, ws.tm_wl, ws.tm_xh, ws.tm_xl, ws.part, ws.plan.error);
+    const size_t nl = (size_t)T * d.E;
+    k_pf_router_sum<<<(unsigned)((nl + 255) / 256), 256, 0, s>>>(ws.part, nl, nsplit, ws.logits);
+    if (launches) *launches += 4;
+}
+
+// ===========================================================================
 // host side
 // ===========================================================================
 static size_t pf_smem(int mode, int nbp) {
@@ -645,7 +801,8 @@ static void pf_launch(const MoeDims &d, const MoeLayerDev &L, const MoePlan &pla
 void moe_prefill_free(MoePrefillWs &ws) {
     void *b[] = {ws.part, ws.logits, ws.w, ws.eo, ws.idx, ws.counters, ws.xg, ws.act, ws.plan.counts,
                  ws.plan.pair_expert, ws.plan.pair_token, ws.plan.pair_w, ws.plan.chunk_expert, ws.plan.chunk_pair0,
-                 ws.plan.chunk_ntok, ws.plan.slot_pair, ws.plan.error, ws.pcnt, ws.pcur};
+                 ws.plan.chunk_ntok, ws.plan.slot_pair, ws.plan.error, ws.pcnt, ws.pcur, ws.wh, ws.wl,
+                 ws.xh, ws.xl};
     for (void *p : b) cudaFree(p);
     ws = MoePrefillWs{};
 }
@@ -656,7 +813,7 @@ int moe_prefill_alloc(MoePrefillWs &ws, const MoeDims &d, int T) {
     const int cap = (T + 255) & ~255;
     const size_t P = (size_t)cap * (d.K + 1) + PF_TILE_N;  // pairs (+ slack rows for the last TMA box)
     const size_t tiles = (size_t)d.E + 1 + P / PF_TILE_N + 1;
-    const int nsplit = d.H / MOE_QK;
+    const int nsplit = d.H / MOE_QK > 16 ? d.H / MOE_QK : 16;  // router partial slices (at most 16)
     cudaError_t e = cudaSuccess;
 #define PFA(ptr, bytes) \
     if (e == cudaSuccess) e = cudaMalloc((void **)&(ptr), (bytes))
@@ -678,11 +835,18 @@ int moe_prefill_alloc(MoePrefillWs &ws, const MoeDims &d, int T) {
     PFA(ws.plan.slot_pair, sizeof(int) * (size_t)cap * (d.K + 1));
     PFA(ws.plan.error, sizeof(int));
     PFA(ws.pcnt, sizeof(int) * (size_t)(d.E + 2));
+    const size_t Ep = (size_t)(d.E + 127) & ~(size_t)127;  // router rows padded to the 128-row box (zero rows)
+    PFA(ws.wh, sizeof(__half) * Ep * d.H);
+    PFA(ws.wl, sizeof(__half) * Ep * d.H);
+    PFA(ws.xh, sizeof(__half) * (size_t)cap * d.H);
+    PFA(ws.xl, sizeof(__half) * (size_t)cap * d.H);
     PFA(ws.pcur, sizeof(int) * (size_t)(d.E + 2));
 #undef PFA
     if (e == cudaSuccess) e = cudaMemset(ws.counters, 0, sizeof(int) * ((size_t)(d.E + 31) / 32) * (cap / 64 + 1));
     if (e == cudaSuccess) e = cudaMemset(ws.plan.error, 0, sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(ws.pcnt, 0, sizeof(int) * (size_t)(d.E + 2));
+    if (e == cudaSuccess) e = cudaMemset(ws.wh, 0, sizeof(__half) * Ep * d.H);
+    if (e == cudaSuccess) e = cudaMemset(ws.wl, 0, sizeof(__half) * Ep * d.H);
     if (e == cudaSuccess) e = cudaMemset(ws.xg, 0, sizeof(__half) * P * d.H);
     if (e == cudaSuccess) e = cudaMemset(ws.act, 0, sizeof(__half) * P * d.I);
     if (e != cudaSuccess) {
@@ -690,7 +854,11 @@ int moe_prefill_alloc(MoePrefillWs &ws, const MoeDims &d, int T) {
         return -1;
     }
     if (moe_make_map_f16_sw128(&ws.tm_xg, ws.xg, d.H, P, 64, PF_TILE) ||
-        moe_make_map_f16_sw128(&ws.tm_act, ws.act, d.I, P, 64, PF_TILE)) {
+        moe_make_map_f16_sw128(&ws.tm_act, ws.act, d.I, P, 64, PF_TILE) ||
+        moe_make_map_f16_sw128(&ws.tm_wh, ws.wh, d.H, Ep, 64, 128) ||
+        moe_make_map_f16_sw128(&ws.tm_wl, ws.wl, d.H, Ep, 64, 128) ||
+        moe_make_map_f16_sw128(&ws.tm_xh, ws.xh, d.H, cap, 64, 128) ||
+        moe_make_map_f16_sw128(&ws.tm_xl, ws.xl, d.H, cap, 64, 128)) {
         moe_prefill_free(ws);
         return -2;
     }
@@ -704,7 +872,7 @@ void moe_launch_prefill_experts(const MoeDims &d, const MoeLayerDev &L, MoePrefi
     k_pf_count<<<nblk, 256, 0, s>>>(d, ws.idx, n, ws.pcnt, ws.plan.error);
     k_pf_offsets<<<1, 1024, 0, s>>>(d, T, ws.pcnt, ws.pcur, ws.plan);
     k_pf_scatter<<<nblk, 256, 0, s>>>(d, ws.idx, ws.w, T, ws.pcur, ws.plan);
-    k_prefill_gather<<<T, 256, 0, s>>>(x, d.H, d.K, ws.plan, ws.xg);
+    k_prefill_gather<<<T, 256, 0, s>>>(ws.xh, d.H, d.K, ws.plan, ws.xg);
     if (launches) *launches += 4;
     const int P = T * (d.K + 1);
     const int max_tiles = d.E + 1 + P / PF_TILE_N + 1;
