@@ -38,7 +38,8 @@
 #define PF_TILE 128                // weight rows per accumulator (MMA M)
 #define PF_RB 2                    // row blocks per CTA: M = 256 rows share each activation stage
 #define PF_TILE_N 128              // pairs per tile (MMA N <= 128)
-#define PF_ATOM 16384              // one 128-row x 128-byte activation box (64 columns of K)
+#define PF_ATOM 16384              // one 128-row x 128-byte activation stage (64 columns of K)
+#define PF_BOX32 4096              // one 32-row activation box (4 swizzle atoms of 8 rows)
 #define PF_NSA 4                   // A stages in tensor memory (PF_RB x 32 columns each, after the accumulators)
 #define PF_NSB 6                   // activation stages
 #define PF_Q6_ROW 208              // Q6_K Q-plane row stride in shared memory (192 B used)
@@ -408,7 +409,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     const int e = plan.chunk_expert[tile], p0 = plan.chunk_pair0[tile], ntile = plan.chunk_ntok[tile];
     const int slot = e == d.E ? L.n_local : e - L.e0;
     const int K = MODE == 0 ? d.H : d.I, NB = K / MOE_QK, n_atoms = 4 * NB;
-    const int nbp = q6r_nb_pad(NB);
+    const int nbp = q6r_nb_pad(NB), nbox = (ntile + 31) / 32;
     if (tid == 0) {
         for (int i = 0; i < RAW_NS; i++) { pf_mbar_init(&raw_full[i], 1); pf_mbar_init(&raw_empty[i], PF_DQ_WARPS); }
         for (int i = 0; i < PF_NSA; i++) { pf_mbar_init(&a_full[i], 4); pf_mbar_init(&a_empty[i], 1); }
@@ -467,8 +468,10 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
             const int st = i % PF_NSB;
             if (!pf_wait_warp(&b_empty[st], ((i / PF_NSB) & 1) ^ 1)) { ok = false; break; }
             if (leader) {
-                pf_expect(&b_full[st], PF_ATOM);
-                pf_tma2(sb + st * PF_ATOM, &tmB, 64 * i, p0, &b_full[st]);
+                // only the 32-row boxes the tile's pairs reach (L2 traffic)
+                pf_expect(&b_full[st], nbox * PF_BOX32);
+                for (int bx = 0; bx < nbox; bx++)
+                    pf_tma2(sb + st * PF_ATOM + bx * PF_BOX32, &tmB, 64 * i, p0 + 32 * bx, &b_full[st]);
             }
             issued = i + 1;
         }
@@ -598,10 +601,12 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
                         const int i = lane & 15, rI = blk * 64 + 16 * q + i;
 #pragma unroll
                         for (int j = 0; j < 16; j++) {
+                            // silu(g) * u with the fast exponential and division: the
+                            // result is rounded to fp16 (2^-11), far above their error
                             const float u = __shfl_xor_sync(0xffffffffu, v[j], 16);
                             if (lane < 16 && c + j < ntile)
                                 act[(size_t)(p0 + c + j) * d.I + rI] =
-                                    __float2half_rn((v[j] / (1.0f + expf(-v[j]))) * u);
+                                    __float2half_rn(__fdividef(v[j], 1.0f + __expf(-v[j])) * u);
                         }
                     } else {
                         const int rH = blk * 128 + 32 * q + lane;
@@ -853,8 +858,8 @@ int moe_prefill_alloc(MoePrefillWs &ws, const MoeDims &d, int T) {
         moe_prefill_free(ws);
         return -1;
     }
-    if (moe_make_map_f16_sw128(&ws.tm_xg, ws.xg, d.H, P, 64, PF_TILE) ||
-        moe_make_map_f16_sw128(&ws.tm_act, ws.act, d.I, P, 64, PF_TILE) ||
+    if (moe_make_map_f16_sw128(&ws.tm_xg, ws.xg, d.H, P, 64, 32) ||
+        moe_make_map_f16_sw128(&ws.tm_act, ws.act, d.I, P, 64, 32) ||
         moe_make_map_f16_sw128(&ws.tm_wh, ws.wh, d.H, Ep, 64, 128) ||
         moe_make_map_f16_sw128(&ws.tm_wl, ws.wl, d.H, Ep, 64, 128) ||
         moe_make_map_f16_sw128(&ws.tm_xh, ws.xh, d.H, cap, 64, 128) ||
