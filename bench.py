@@ -339,7 +339,8 @@ def run_ours(args):
             "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "fp32 (Q4_K/Q6_K weights decoded exactly to fp16 integers, fp32 accumulation)",
+            "dtype": "int8 tensor-core products of Q4_K/Q6_K integers and 21-bit activation planes (exact), fp32 "
+                     "accumulation",
             "data": "synthetic: random-init N(0,0.02) weights quantized on device, N(0,1) tokens",
             "config": {"workload": W["name"], "global_batch": B, "tokens_per_gpu": b_loc, "hidden": H,
                        "intermediate": I, "experts": NE, "top_k": K, "gate_up": "Q4_K", "down": "Q6_K",
@@ -528,7 +529,11 @@ def run_extra(args):
     clk.__exit__(None, None, None)
     line = {"metric": METRIC, "value": round(value, 2), "unit": unit, "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "fp32 accumulation over exact int8 products",
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": ("fp16 operands (dequantized weights, activations) on tcgen05, fp32 accumulation"
+                      if args.workload == "prefill4096" else
+                      "int8 tensor-core products of Q4_K/Q6_K integers and 21-bit activation planes (exact), fp32 "
+                      "accumulation"),
             "data": "synthetic: random-init N(0,0.02) weights quantized on device, N(0,1) tokens",
             "config": dict({"workload": W["name"], "global_batch": W["B"], "hidden": H, "intermediate": I,
                             "experts": E, "parallelism": "ep1"}, **extra),
