@@ -388,12 +388,15 @@ def run_extra(args):
     import torch
     import flash_deepseek_b200 as F
     W = EXTRA[args.workload]
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(0)
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1 and args.workload != "prefill4096":
+        raise SystemExit(f"--workload {args.workload} runs on one GPU")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(local)
     g = torch.Generator(device="cpu").manual_seed(1234)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
     peak, peak_kind = peaks()
-    clk = Clocks(0).__enter__()
+    clk = Clocks(local).__enter__()
     extra = {}
     if args.workload == "expert1":
         cfg = F.MoeConfig(n_layers=1, max_tokens=1, top_k=1)
@@ -485,18 +488,36 @@ def run_extra(args):
         e2e = {"value": round(B * n_e2e / e2e_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 3 * B * H * 4,
                "d2h_bytes_per_step": 3 * B * H * 4, "timer": "host wall clock (synchronous calls)"}
         extra = {"layers_resident": n_res, "layer_calls_per_step": 58}
-    else:  # prefill4096: one moe_prefill_device call (tcgen05 GEMMs) per step
+    else:  # prefill4096: one moe_prefill_device call (tcgen05 GEMMs) per step and rank
+        from flash_deepseek_b200 import ep
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        pg = None
+        if world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+            pg = dist
         B = int(os.environ.get("MOE_PREFILL_TOKENS", "4096"))
         NE = args.experts
+        t0, bl = ep.local_tokens(B, world, rank)  # this rank's share of the global batch
+        uid = ep.share_unique_id(pg, rank, F.get_unique_id) if world > 1 else None
         cfg = F.MoeConfig(n_layers=1, max_tokens=64, n_experts=NE)
-        moe = F.MoE(cfg)
+        moe = F.MoE(cfg, device=dev.index, rank=rank, world_size=world, unique_id=uid)
         moe.init_layer_synthetic(0, seed=0, down_type=F.TYPE_Q6_K)
-        xs = [torch.randn(B, H, generator=g).to(dev) for _ in range(2)]
-        out = torch.empty(B, H, device=dev)
+        xs = [torch.randn(B, H, generator=g)[t0:t0 + bl].contiguous().to(dev) for _ in range(2)]
+        out = torch.empty(max(1, bl), H, device=dev)
         stream = torch.cuda.ExternalStream(moe.stream, device=dev)
+
+        def sync_all():
+            torch.cuda.synchronize()
+            if pg:
+                pg.barrier()
+            torch.cuda.synchronize()
+
         for i in range(max(1, args.warmup)):
-            moe.prefill_device(0, xs[i % 2], B, out)
-        torch.cuda.synchronize()
+            moe.prefill_device(0, xs[i % 2], bl, out)
+        sync_all()
         n = max(1, args.steps)
         l0 = moe.kernel_launches
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
@@ -504,16 +525,20 @@ def run_extra(args):
             for i in range(n):
                 flush.zero_()
                 ev[i][0].record(stream)
-                moe.prefill_device(0, xs[i % 2], B, out)
+                moe.prefill_device(0, xs[i % 2], bl, out)
                 ev[i][1].record(stream)
-        torch.cuda.synchronize()
+        sync_all()
         ms = sum(a.elapsed_time(b) for a, b in ev)
+        if pg:
+            t = torch.tensor([ms], dtype=torch.float64)
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+            ms = float(t[0])
         launches = moe.kernel_launches - l0
         ms_step = ms / n
         value = B * n / (ms / 1e3)
         unit = "tokens/s"
         flops = 2.0 * B * (K + 1) * (3 * H * I) + 2.0 * B * NE * H
-        tf = flops / (ms_step / 1e3) / 1e12
+        tf = flops / world / (ms_step / 1e3) / 1e12  # per GPU
         pk = 1642.1
         try:
             with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -521,13 +546,20 @@ def run_extra(args):
         except Exception:
             pass
         roof = {"bound": "tensor", "kernel": "whole step (router, route, plan, gather, tcgen05 gate/up and down "
-                "GEMMs, combine)", "achieved": round(tf, 2), "peak": pk, "unit": "TFLOP/s", "frac": round(tf / pk, 4),
+                "GEMMs, combine" + (", NCCL dispatch and combine" if world > 1 else "") + "), per GPU",
+                "achieved": round(tf, 2), "peak": pk, "unit": "TFLOP/s", "frac": round(tf / pk, 4),
                 "peak_source": "measured dense bf16 burst (fp16 MMA, same rate)", "flops_per_step": flops,
                 "traffic": None}
         e2e = None
-        extra = {"tokens_per_call": B, "path": "moe_prefill_device (tcgen05)"}
+        extra = {"tokens_per_call": B, "tokens_per_rank": bl, "path": "moe_prefill_device (tcgen05)",
+                 "parallelism": f"ep{world}"}
+        if rank != 0:
+            clk.__exit__(None, None, None)
+            moe.close()
+            return
     clk.__exit__(None, None, None)
-    line = {"metric": METRIC, "value": round(value, 2), "unit": unit, "n_gpus": 1, "steps": args.steps,
+    line = {"metric": METRIC, "value": round(value, 2), "unit": unit,
+            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None,
             "dtype": ("fp16 operands (dequantized weights, activations) on tcgen05, fp32 accumulation"

@@ -282,6 +282,7 @@ void moe_destroy(moe_ctx *c) {
     for (cudaEvent_t e : c->ev) cudaEventDestroy(e);
     for (auto &g : c->graphs) cudaGraphExecDestroy(g.exec);
     moe_prefill_free(c->pf);
+    cudaFree(c->pf.tcount);
     for (auto &L : c->layers) {
         cudaFree(L.experts);
         cudaFree(L.router);
@@ -845,20 +846,81 @@ int moe_route(moe_ctx *c, const float *logits, const float *bias, int T, int *id
     return MOE_OK;
 }
 
+// Expert-parallel prefill: every rank routes its own tokens, sends each
+// token's fp16 row and routing to the ranks that own its experts (fixed
+// capacity: the largest token count of any rank, agreed first), runs the
+// tcgen05 expert GEMMs over the rows it received, pre-combines them per row
+// in slot order, sends the partial sums back, and adds them up in rank order
+// plus its own shared expert.  Every rank calls, even with 0 tokens.
+static int run_prefill_ep(moe_ctx *c, int layer, const float *d_h, int T, float *d_out, int *d_idx, float *d_w,
+                          cudaStream_t s) {
+    const MoeDims &d = c->d;
+    MoeLayerDev &L = c->layers[layer];
+    const int N = c->world, mw = 2 + 2 * d.K;
+    if (N > 64) return fail(c, MOE_ERR_ARG, "moe_prefill: world size above 64");
+    MoePrefillWs &ws = c->pf;
+    if (!ws.tcount && cudaMalloc((void **)&ws.tcount, sizeof(int) * 66) != cudaSuccess)
+        return fail(c, MOE_ERR_CUDA, "prefill token-count buffer");
+    // the rows per peer: the largest n_tokens of any rank (one host sync)
+    CK(cudaMemcpyAsync(ws.tcount, &T, sizeof(int), cudaMemcpyHostToDevice, s));
+    NK(moe_nccl()->GroupStart());
+    for (int p = 0; p < N; p++) {
+        NK(moe_nccl()->Send(ws.tcount, 1, ncclInt32, p, c->comm, s));
+        NK(moe_nccl()->Recv(ws.tcount + 2 + p, 1, ncclInt32, p, c->comm, s));
+    }
+    NK(moe_nccl()->GroupEnd());
+    int counts[64];
+    CK(cudaMemcpyAsync(counts, ws.tcount + 2, sizeof(int) * N, cudaMemcpyDeviceToHost, s));
+    CK(cudaStreamSynchronize(s));
+    int ecap = 1;
+    for (int p = 0; p < N; p++) ecap = counts[p] > ecap ? counts[p] : ecap;
+    if (moe_prefill_alloc(ws, d, T > 0 ? T : 1, N, ecap))
+        return fail(c, MOE_ERR_CUDA, "prefill workspace for %d tokens x %d ranks could not be allocated", ecap, N);
+    const size_t rows = (size_t)ws.ecap;
+    if (T > 0) {
+        moe_launch_prefill_router(d, L.router, ws, d_h, T, s, &c->launches);
+        moe_launch_route_and_plan(d, nullptr, 0, ws.logits, L.bias, L.logit_bias, 0, nullptr, nullptr, T, ws.idx,
+                                  ws.w, d_h, nullptr, 1, 0, ws.plan, c->counter, s, &c->launches);
+    }
+    moe_launch_pfe_dispatch(d, ws, T, c->n_local, s, &c->launches);
+    NK(moe_nccl()->GroupStart());
+    for (int p = 0; p < N; p++) {
+        NK(moe_nccl()->Send(ws.send_xh + p * rows * d.H, rows * d.H, ncclFloat16, p, c->comm, s));
+        NK(moe_nccl()->Recv(ws.recv_xh + p * rows * d.H, rows * d.H, ncclFloat16, p, c->comm, s));
+        NK(moe_nccl()->Send(ws.send_meta + p * rows * mw, rows * mw, ncclInt32, p, c->comm, s));
+        NK(moe_nccl()->Recv(ws.recv_meta + p * rows * mw, rows * mw, ncclInt32, p, c->comm, s));
+    }
+    NK(moe_nccl()->GroupEnd());
+    moe_launch_pfe_experts(d, L, ws, T, s, &c->launches);
+    NK(moe_nccl()->GroupStart());
+    for (int p = 0; p < N; p++) {
+        NK(moe_nccl()->Send(ws.send_y + p * rows * d.H, rows * d.H, ncclFloat32, p, c->comm, s));
+        NK(moe_nccl()->Recv(ws.recv_y + p * rows * d.H, rows * d.H, ncclFloat32, p, c->comm, s));
+    }
+    NK(moe_nccl()->GroupEnd());
+    if (T > 0) moe_launch_pfe_final(d, ws, T, d_out, s, &c->launches);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(c, MOE_ERR_CUDA, "prefill launch: %s", cudaGetErrorString(e));
+    if (T > 0 && d_idx) CK(cudaMemcpyAsync(d_idx, ws.idx, sizeof(int) * T * d.K, cudaMemcpyDeviceToDevice, s));
+    if (T > 0 && d_w) CK(cudaMemcpyAsync(d_w, ws.w, sizeof(float) * T * d.K, cudaMemcpyDeviceToDevice, s));
+    return MOE_OK;
+}
+
 int moe_prefill_device(moe_ctx *c, int layer, const float *d_h, int T, float *d_out, int *d_idx, float *d_w,
                        void *stream) {
     if (!c) return MOE_ERR_ARG;
-    if (T <= 0 || !d_h || !d_out) return fail(c, MOE_ERR_ARG, "moe_prefill_device: need n_tokens >= 1 and buffers");
+    if (T < 0 || (T > 0 && (!d_h || !d_out)) || (T == 0 && c->world == 1))
+        return fail(c, MOE_ERR_ARG, "moe_prefill_device: need n_tokens >= 1 and buffers (0 only in expert parallelism)");
     int rc = check_layer(c, layer);
     if (rc) return rc;
-    if (c->world > 1) return fail(c, MOE_ERR_STATE, "moe_prefill runs on one GPU (world_size 1)");
     if (c->d.H % 256 || c->d.I % 128 || c->d.K > 63 || c->d.E > 1024)
         return fail(c, MOE_ERR_ARG,
                     "moe_prefill needs hidden %% 256 == 0, intermediate %% 128 == 0, top_k <= 63, n_experts <= 1024");
     CK(cudaSetDevice(c->device));
+    cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    if (c->world > 1) return run_prefill_ep(c, layer, d_h, T, d_out, d_idx, d_w, s);
     if (moe_prefill_alloc(c->pf, c->d, T))
         return fail(c, MOE_ERR_CUDA, "prefill workspace for %d tokens could not be allocated", T);
-    cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
     MoeLayerDev &L = c->layers[layer];
     const MoeDims &d = c->d;
     moe_launch_prefill_router(d, L.router, c->pf, d_h, T, s, &c->launches);
@@ -874,8 +936,14 @@ int moe_prefill_device(moe_ctx *c, int layer, const float *d_h, int T, float *d_
 
 int moe_prefill(moe_ctx *c, int layer, const float *h, int T, float *out, int *idx_out, float *w_out) {
     if (!c) return MOE_ERR_ARG;
-    if (T <= 0 || !h || !out) return fail(c, MOE_ERR_ARG, "moe_prefill: need n_tokens >= 1 and buffers");
+    if (T < 0 || (T > 0 && (!h || !out)) || (T == 0 && c->world == 1))
+        return fail(c, MOE_ERR_ARG, "moe_prefill: need n_tokens >= 1 and buffers (0 only in expert parallelism)");
     CK(cudaSetDevice(c->device));
+    if (T == 0) {  // a rank without tokens still takes part in the exchanges
+        const int rc = moe_prefill_device(c, layer, nullptr, 0, nullptr, nullptr, nullptr, nullptr);
+        CK(cudaStreamSynchronize(c->stream));
+        return rc;
+    }
     const size_t n = (size_t)T * c->d.H;
     float *dh = nullptr, *dout = nullptr;
     CK(cudaMalloc((void **)&dh, n * sizeof(float)));

@@ -106,10 +106,24 @@ struct MoePrefillWs {
     int *pcnt = nullptr, *pcur = nullptr;  // plan: per-expert counts and scatter cursors (E + 2 each)
     __half *xg = nullptr, *act = nullptr;
     __half *wh = nullptr, *wl = nullptr, *xh = nullptr, *xl = nullptr;  // fp16 hi/lo splits for the router
+    // expert parallelism (world > 1): ecap rows per peer, fp16 rows out, fp32 partial sums back
+    int world = 1, ecap = 0;
+    size_t P = 0;                            // pairs capacity
+    __half *send_xh = nullptr, *recv_xh = nullptr;
+    int *send_meta = nullptr, *recv_meta = nullptr, *tok_slot = nullptr;
+    float *send_y = nullptr, *recv_y = nullptr;
+    int *tcount = nullptr;                   // [2 + world] token counts exchanged by the ranks
     MoePlan plan{};
     CUtensorMap tm_xg, tm_act, tm_wh, tm_wl, tm_xh, tm_xl;
 };
-int moe_prefill_alloc(MoePrefillWs &ws, const MoeDims &d, int T);
+// grows the workspace for T own tokens (world > 1: ecap rows per peer)
+int moe_prefill_alloc(MoePrefillWs &ws, const MoeDims &d, int T, int world = 1, int ecap = 0);
+// expert-parallel prefill steps (moe_api.cu runs the NCCL exchanges between them)
+void moe_launch_pfe_dispatch(const MoeDims &d, MoePrefillWs &ws, int T, int n_local, cudaStream_t s,
+                             uint64_t *launches);
+void moe_launch_pfe_experts(const MoeDims &d, const MoeLayerDev &L, MoePrefillWs &ws, int T, cudaStream_t s,
+                            uint64_t *launches);
+void moe_launch_pfe_final(const MoeDims &d, MoePrefillWs &ws, int T, float *out, cudaStream_t s, uint64_t *launches);
 void moe_prefill_free(MoePrefillWs &ws);
 // router logits of T tokens into ws.logits (tensor cores, fp16 hi/lo splits)
 void moe_launch_prefill_router(const MoeDims &d, const float *Wr, MoePrefillWs &ws, const float *x, int T,

@@ -782,6 +782,216 @@ void moe_launch_prefill_router(const MoeDims &d, const float *Wr, MoePrefillWs &
 }
 
 // ===========================================================================
+// expert parallelism for prefill (one process per GPU, experts sharded
+// n_experts / world per rank, router and shared expert replicated).  Row
+// space on rank r (world N, ecap rows per peer):
+//   rows [p*ecap, p*ecap + ecap)  fp16 token rows received from rank p
+//   rows [N*ecap, N*ecap + T)     this rank's own tokens (shared expert)
+// Metadata of a sent row: [valid, src_token, idx[K], w_bits[K]].  The
+// exchanges are NCCL send/recv of fixed-size buffers (moe_api.cu).
+// ===========================================================================
+
+// block p: tok_slot[t][p] = position of token t among the rows sent to rank
+// p (tokens with at least one expert there, in token order) or -1; clears
+// the valid flag of the unused rows
+__global__ void __launch_bounds__(1024) k_pfe_slots(const int *__restrict__ idx, int T, int K, int n_local, int N,
+                                                    int ecap, int *__restrict__ tok_slot, int *__restrict__ send_meta) {
+    __shared__ int wsum[32], carry;
+    const int p = blockIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    if (threadIdx.x == 0) carry = 0;
+    __syncthreads();
+    for (int base = 0; base < T; base += blockDim.x) {
+        const int t = base + threadIdx.x;
+        int hit = 0;
+        if (t < T)
+            for (int k = 0; k < K; k++) {
+                const int e = idx[t * K + k];
+                if (e >= 0 && e / n_local == p) hit = 1;
+            }
+        int x = hit;
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        if (lane == 31) wsum[wid] = x;
+        __syncthreads();
+        if (wid == 0) {
+            int v = lane < (int)(blockDim.x >> 5) ? wsum[lane] : 0;
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, v, o);
+                if (lane >= o) v += y;
+            }
+            wsum[lane] = v;
+        }
+        __syncthreads();
+        const int excl = carry + (wid ? wsum[wid - 1] : 0) + x - hit;
+        if (t < T) tok_slot[t * N + p] = hit ? excl : -1;
+        __syncthreads();
+        if (threadIdx.x == 0) carry += wsum[(blockDim.x >> 5) - 1];
+        __syncthreads();
+    }
+    const int mw = 2 + 2 * K;
+    for (int r = carry + threadIdx.x; r < ecap; r += blockDim.x) send_meta[((size_t)p * ecap + r) * mw] = 0;
+}
+
+// token t: its fp16 row and metadata to every rank it routes to
+__global__ void __launch_bounds__(256) k_pfe_pack(const __half *__restrict__ xh, const int *__restrict__ idx,
+                                                  const float *__restrict__ w, int K, int H, int N, int ecap,
+                                                  const int *__restrict__ tok_slot, __half *__restrict__ send_xh,
+                                                  int *__restrict__ send_meta) {
+    const int t = blockIdx.x, mw = 2 + 2 * K;
+    const uint4 *src = reinterpret_cast<const uint4 *>(xh + (size_t)t * H);
+    for (int p = 0; p < N; p++) {
+        const int sl = tok_slot[t * N + p];
+        if (sl < 0) continue;
+        const size_t row = (size_t)p * ecap + sl;
+        uint4 *dst = reinterpret_cast<uint4 *>(send_xh + row * H);
+        for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = __ldg(src + i);
+        int *m = send_meta + row * mw;
+        if (threadIdx.x == 0) { m[0] = 1; m[1] = t; }
+        for (int k = threadIdx.x; k < K; k += blockDim.x) {
+            m[2 + k] = idx[t * K + k];
+            m[2 + K + k] = __float_as_int(w[t * K + k]);
+        }
+    }
+}
+
+// pairs (received row, expert of this rank) per expert, PF_PLAN_PAIRS per block
+__global__ void __launch_bounds__(256) k_pfe_count(MoeDims d, const int *__restrict__ recv_meta, int R, int e0,
+                                                   int n_local, int *__restrict__ cnt, int *__restrict__ error) {
+    __shared__ int h[1025];
+    const int K = d.K, mw = 2 + 2 * K;
+    for (int e = threadIdx.x; e < d.E; e += blockDim.x) h[e] = 0;
+    __syncthreads();
+    const int p0 = blockIdx.x * PF_PLAN_PAIRS, p1 = min(R * K, p0 + PF_PLAN_PAIRS);
+    for (int p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
+        const int *m = recv_meta + (size_t)(p / K) * mw;
+        if (!m[0]) continue;
+        const int e = m[2 + p % K];
+        if (e < 0 || e >= d.E) { atomicExch(error, 1); continue; }
+        if (e >= e0 && e < e0 + n_local) atomicAdd(&h[e], 1);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < d.E; e += blockDim.x)
+        if (h[e]) atomicAdd(&cnt[e], h[e]);
+}
+
+__global__ void __launch_bounds__(256) k_pfe_scatter(MoeDims d, const int *__restrict__ recv_meta, int R, int T,
+                                                     int e0, int n_local, int *__restrict__ cur, MoePlan plan) {
+    __shared__ int h[1025], base[1025];
+    const int E = d.E, K = d.K, mw = 2 + 2 * K;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) h[e] = 0;
+    __syncthreads();
+    const int p0 = blockIdx.x * PF_PLAN_PAIRS, p1 = min(R * K, p0 + PF_PLAN_PAIRS);
+    for (int p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
+        const int *m = recv_meta + (size_t)(p / K) * mw;
+        const int e = m[0] ? m[2 + p % K] : -1;
+        if (e >= e0 && e < e0 + n_local && e < E) atomicAdd(&h[e], 1);
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        base[e] = h[e] ? atomicAdd(&cur[e], h[e]) : 0;
+        h[e] = 0;
+    }
+    __syncthreads();
+    for (int p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
+        const int r = p / K, k = p % K;
+        const int *m = recv_meta + (size_t)r * mw;
+        const int e = m[0] ? m[2 + k] : -1;
+        int pos = -1;
+        if (e >= e0 && e < e0 + n_local && e < E) {
+            pos = base[e] + atomicAdd(&h[e], 1);
+            plan.pair_expert[pos] = e;
+            plan.pair_token[pos] = r;
+            plan.pair_w[pos] = __int_as_float(m[2 + K + k]);
+        }
+        plan.slot_pair[(size_t)r * (K + 1) + k] = pos;
+        if (k == 0) plan.slot_pair[(size_t)r * (K + 1) + K] = -1;
+    }
+    // own tokens: the shared expert only (their routed pairs come back through the exchange)
+    const int sh0 = plan.counts[2];
+    for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < T; t += gridDim.x * blockDim.x) {
+        const int pos = sh0 + t, r = R + t;
+        plan.pair_expert[pos] = E;
+        plan.pair_token[pos] = r;
+        plan.pair_w[pos] = 1.0f;
+        for (int k = 0; k < K; k++) plan.slot_pair[(size_t)r * (K + 1) + k] = -1;
+        plan.slot_pair[(size_t)r * (K + 1) + K] = pos;
+    }
+}
+
+// row r of the row space to each of its pair rows
+__global__ void __launch_bounds__(256) k_pfe_gather(const __half *__restrict__ recv_xh, const __half *__restrict__ xh,
+                                                    int R, int H, int K, MoePlan plan, __half *__restrict__ xg) {
+    __shared__ int pos[64];
+    __shared__ int any;
+    const int r = blockIdx.x;
+    if (threadIdx.x == 0) any = 0;
+    __syncthreads();
+    if (threadIdx.x <= K) {
+        pos[threadIdx.x] = plan.slot_pair[(size_t)r * (K + 1) + threadIdx.x];
+        if (pos[threadIdx.x] >= 0) any = 1;
+    }
+    __syncthreads();
+    if (!any) return;
+    const uint4 *src = reinterpret_cast<const uint4 *>(r < R ? recv_xh + (size_t)r * H : xh + (size_t)(r - R) * H);
+    for (int i = threadIdx.x; i < H / 8; i += blockDim.x) {
+        const uint4 v = __ldg(src + i);
+        for (int k = 0; k <= K; k++)
+            if (pos[k] >= 0) reinterpret_cast<uint4 *>(xg + (size_t)pos[k] * H)[i] = v;
+    }
+}
+
+// pre-combine on the expert side: send_y[r] = sum over the slots of received
+// row r whose expert lives here, in slot order, of w_k * eo
+__global__ void __launch_bounds__(256) k_pfe_partial(MoeDims d, MoePlan plan, const int *__restrict__ recv_meta,
+                                                     const float *__restrict__ eo, float *__restrict__ send_y) {
+    __shared__ int pos[64];
+    __shared__ float wk[64];
+    const int r = blockIdx.x, K = d.K, H = d.H;
+    if (!recv_meta[(size_t)r * (2 + 2 * K)]) return;
+    if (threadIdx.x < K) {
+        const int p = plan.slot_pair[(size_t)r * (K + 1) + threadIdx.x];
+        pos[threadIdx.x] = p;
+        wk[threadIdx.x] = p >= 0 ? plan.pair_w[p] : 0.0f;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < H / 4; i += blockDim.x) {
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int k = 0; k < K; k++) {
+            if (pos[k] < 0) continue;
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(eo + (size_t)pos[k] * H) + i);
+            const float wv = wk[k];
+            acc = make_float4(fmaf(wv, v.x, acc.x), fmaf(wv, v.y, acc.y), fmaf(wv, v.z, acc.z), fmaf(wv, v.w, acc.w));
+        }
+        reinterpret_cast<float4 *>(send_y + (size_t)r * H)[i] = acc;
+    }
+}
+
+// owner side: out[t] = sum over ranks (rank order) of the returned partials
+// + the shared expert
+__global__ void __launch_bounds__(256) k_pfe_final(MoeDims d, MoePlan plan, const float *__restrict__ recv_y,
+                                                   const int *__restrict__ tok_slot, int N, int ecap, int R,
+                                                   const float *__restrict__ eo, float *__restrict__ out) {
+    __shared__ int sl[64];
+    __shared__ int sp;
+    const int t = blockIdx.x, H = d.H;
+    if (threadIdx.x < N) sl[threadIdx.x] = tok_slot[t * N + threadIdx.x];
+    if (threadIdx.x == 0) sp = plan.slot_pair[(size_t)(R + t) * (d.K + 1) + d.K];
+    __syncthreads();
+    for (int i = threadIdx.x; i < H / 4; i += blockDim.x) {
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int p = 0; p < N; p++) {
+            if (sl[p] < 0) continue;
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(recv_y + ((size_t)p * ecap + sl[p]) * H) + i);
+            acc = make_float4(acc.x + v.x, acc.y + v.y, acc.z + v.z, acc.w + v.w);
+        }
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(eo + (size_t)sp * H) + i);
+        reinterpret_cast<float4 *>(out + (size_t)t * H)[i] = make_float4(acc.x + v.x, acc.y + v.y, acc.z + v.z, acc.w + v.w);
+    }
+}
+
+// ===========================================================================
 // host side
 // ===========================================================================
 static size_t pf_smem(int mode, int nbp) {
@@ -807,18 +1017,25 @@ void moe_prefill_free(MoePrefillWs &ws) {
     void *b[] = {ws.part, ws.logits, ws.w, ws.eo, ws.idx, ws.counters, ws.xg, ws.act, ws.plan.counts,
                  ws.plan.pair_expert, ws.plan.pair_token, ws.plan.pair_w, ws.plan.chunk_expert, ws.plan.chunk_pair0,
                  ws.plan.chunk_ntok, ws.plan.slot_pair, ws.plan.error, ws.pcnt, ws.pcur, ws.wh, ws.wl,
-                 ws.xh, ws.xl};
+                 ws.xh, ws.xl, ws.send_xh, ws.recv_xh, ws.send_meta, ws.recv_meta, ws.send_y, ws.recv_y,
+                 ws.tok_slot};
     for (void *p : b) cudaFree(p);
+    int *tc = ws.tcount;  // the token-count exchange buffer outlives the workspace
     ws = MoePrefillWs{};
+    ws.tcount = tc;
 }
 
-int moe_prefill_alloc(MoePrefillWs &ws, const MoeDims &d, int T) {
-    if (ws.cap >= T) return 0;
+int moe_prefill_alloc(MoePrefillWs &ws, const MoeDims &d, int T, int world, int ecap_req) {
+    const int ecap = world > 1 ? (ecap_req + 7) & ~7 : 0;  // rows per peer in the exchange
+    if (ws.cap >= T && ws.world == world && ws.ecap >= ecap) return 0;
     moe_prefill_free(ws);
-    const int cap = (T + 255) & ~255;
-    const size_t P = (size_t)cap * (d.K + 1) + PF_TILE_N;  // pairs (+ slack rows for the last TMA box)
+    const int cap = (T + 255) & ~255;                       // own tokens
+    const size_t R = (size_t)world * ecap;                  // received rows (0 on one GPU)
+    const size_t rows = world > 1 ? R + cap : (size_t)cap;  // row space of the plan
+    const size_t P = (world > 1 ? R * d.K + cap : (size_t)cap * (d.K + 1)) + PF_TILE_N;  // pairs (+ box slack)
     const size_t tiles = (size_t)d.E + 1 + P / PF_TILE_N + 1;
     const int nsplit = d.H / MOE_QK > 16 ? d.H / MOE_QK : 16;  // router partial slices (at most 16)
+    const int mw = 2 + 2 * d.K;
     cudaError_t e = cudaSuccess;
 #define PFA(ptr, bytes) \
     if (e == cudaSuccess) e = cudaMalloc((void **)&(ptr), (bytes))
@@ -837,7 +1054,7 @@ int moe_prefill_alloc(MoePrefillWs &ws, const MoeDims &d, int T) {
     PFA(ws.plan.chunk_expert, sizeof(int) * tiles);
     PFA(ws.plan.chunk_pair0, sizeof(int) * tiles);
     PFA(ws.plan.chunk_ntok, sizeof(int) * tiles);
-    PFA(ws.plan.slot_pair, sizeof(int) * (size_t)cap * (d.K + 1));
+    PFA(ws.plan.slot_pair, sizeof(int) * rows * (d.K + 1));
     PFA(ws.plan.error, sizeof(int));
     PFA(ws.pcnt, sizeof(int) * (size_t)(d.E + 2));
     const size_t Ep = (size_t)(d.E + 127) & ~(size_t)127;  // router rows padded to the 128-row box (zero rows)
@@ -846,6 +1063,15 @@ int moe_prefill_alloc(MoePrefillWs &ws, const MoeDims &d, int T) {
     PFA(ws.xh, sizeof(__half) * (size_t)cap * d.H);
     PFA(ws.xl, sizeof(__half) * (size_t)cap * d.H);
     PFA(ws.pcur, sizeof(int) * (size_t)(d.E + 2));
+    if (world > 1) {
+        PFA(ws.send_xh, sizeof(__half) * R * d.H);
+        PFA(ws.recv_xh, sizeof(__half) * R * d.H);
+        PFA(ws.send_meta, sizeof(int) * R * mw);
+        PFA(ws.recv_meta, sizeof(int) * R * mw);
+        PFA(ws.send_y, sizeof(float) * R * d.H);
+        PFA(ws.recv_y, sizeof(float) * R * d.H);
+        PFA(ws.tok_slot, sizeof(int) * (size_t)cap * world);
+    }
 #undef PFA
     if (e == cudaSuccess) e = cudaMemset(ws.counters, 0, sizeof(int) * ((size_t)(d.E + 31) / 32) * (cap / 64 + 1));
     if (e == cudaSuccess) e = cudaMemset(ws.plan.error, 0, sizeof(int));
@@ -868,7 +1094,51 @@ int moe_prefill_alloc(MoePrefillWs &ws, const MoeDims &d, int T) {
         return -2;
     }
     ws.cap = cap;
+    ws.world = world;
+    ws.ecap = ecap;
+    ws.P = P;
     return 0;
+}
+
+// tcgen05 expert GEMMs over the plan; P = pairs capacity of the workspace
+static void pf_gemms(const MoeDims &d, const MoeLayerDev &L, MoePrefillWs &ws, size_t npairs, cudaStream_t s,
+                     uint64_t *launches) {
+    const int max_tiles = (int)(d.E + 1 + npairs / PF_TILE_N + 1);
+    pf_launch<0>(d, L, ws.plan, ws.tm_xg, ws.act, nullptr, max_tiles, d.I / (64 * PF_RB), s, launches);
+    if (L.down_type == MOE_TYPE_Q6_K || L.sh_down_type == MOE_TYPE_Q6_K)
+        pf_launch<2>(d, L, ws.plan, ws.tm_act, nullptr, ws.eo, max_tiles, d.H / (128 * PF_RB), s, launches);
+    if (L.down_type == MOE_TYPE_Q4_K || L.sh_down_type == MOE_TYPE_Q4_K)
+        pf_launch<1>(d, L, ws.plan, ws.tm_act, nullptr, ws.eo, max_tiles, d.H / (128 * PF_RB), s, launches);
+}
+
+void moe_launch_pfe_dispatch(const MoeDims &d, MoePrefillWs &ws, int T, int n_local, cudaStream_t s,
+                             uint64_t *launches) {
+    k_pfe_slots<<<ws.world, 1024, 0, s>>>(ws.idx, T, d.K, n_local, ws.world, ws.ecap, ws.tok_slot, ws.send_meta);
+    LAUNCH_COUNT(launches);
+    if (T > 0) {
+        k_pfe_pack<<<T, 256, 0, s>>>(ws.xh, ws.idx, ws.w, d.K, d.H, ws.world, ws.ecap, ws.tok_slot, ws.send_xh,
+                                     ws.send_meta);
+        LAUNCH_COUNT(launches);
+    }
+}
+
+void moe_launch_pfe_experts(const MoeDims &d, const MoeLayerDev &L, MoePrefillWs &ws, int T, cudaStream_t s,
+                            uint64_t *launches) {
+    const int R = ws.world * ws.ecap, n = R * d.K, nblk = (n + PF_PLAN_PAIRS - 1) / PF_PLAN_PAIRS;
+    k_pfe_count<<<nblk, 256, 0, s>>>(d, ws.recv_meta, R, L.e0, L.n_local, ws.pcnt, ws.plan.error);
+    k_pf_offsets<<<1, 1024, 0, s>>>(d, T, ws.pcnt, ws.pcur, ws.plan);
+    k_pfe_scatter<<<nblk, 256, 0, s>>>(d, ws.recv_meta, R, T, L.e0, L.n_local, ws.pcur, ws.plan);
+    k_pfe_gather<<<R + T, 256, 0, s>>>(ws.recv_xh, ws.xh, R, d.H, d.K, ws.plan, ws.xg);
+    if (launches) *launches += 4;
+    pf_gemms(d, L, ws, (size_t)n + T, s, launches);
+    k_pfe_partial<<<R, 256, 0, s>>>(d, ws.plan, ws.recv_meta, ws.eo, ws.send_y);
+    LAUNCH_COUNT(launches);
+}
+
+void moe_launch_pfe_final(const MoeDims &d, MoePrefillWs &ws, int T, float *out, cudaStream_t s, uint64_t *launches) {
+    k_pfe_final<<<T, 256, 0, s>>>(d, ws.plan, ws.recv_y, ws.tok_slot, ws.world, ws.ecap, ws.world * ws.ecap, ws.eo,
+                                  out);
+    LAUNCH_COUNT(launches);
 }
 
 void moe_launch_prefill_experts(const MoeDims &d, const MoeLayerDev &L, MoePrefillWs &ws, const float *x, int T,
@@ -879,13 +1149,7 @@ void moe_launch_prefill_experts(const MoeDims &d, const MoeLayerDev &L, MoePrefi
     k_pf_scatter<<<nblk, 256, 0, s>>>(d, ws.idx, ws.w, T, ws.pcur, ws.plan);
     k_prefill_gather<<<T, 256, 0, s>>>(ws.xh, d.H, d.K, ws.plan, ws.xg);
     if (launches) *launches += 4;
-    const int P = T * (d.K + 1);
-    const int max_tiles = d.E + 1 + P / PF_TILE_N + 1;
-    pf_launch<0>(d, L, ws.plan, ws.tm_xg, ws.act, nullptr, max_tiles, d.I / (64 * PF_RB), s, launches);
-    if (L.down_type == MOE_TYPE_Q6_K || L.sh_down_type == MOE_TYPE_Q6_K)
-        pf_launch<2>(d, L, ws.plan, ws.tm_act, nullptr, ws.eo, max_tiles, d.H / (128 * PF_RB), s, launches);
-    if (L.down_type == MOE_TYPE_Q4_K || L.sh_down_type == MOE_TYPE_Q4_K)
-        pf_launch<1>(d, L, ws.plan, ws.tm_act, nullptr, ws.eo, max_tiles, d.H / (128 * PF_RB), s, launches);
+    pf_gemms(d, L, ws, (size_t)T * (d.K + 1), s, launches);
     k_prefill_combine<<<T, 256, 0, s>>>(d, ws.plan, ws.eo, out);
     LAUNCH_COUNT(launches);
 }

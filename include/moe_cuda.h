@@ -172,16 +172,21 @@ int moe_forward_stack_device(moe_ctx *ctx, int first_layer, int n_layers, float 
                              int n_tokens, void *stream);
 int moe_forward_stack(moe_ctx *ctx, int first_layer, int n_layers, float *hidden, int n_tokens);
 
-/* The MoE block for a long batch of tokens (prompt prefill), one GPU:
+/* The MoE block for a long batch of tokens (prompt prefill):
  * out[t] = sum_k w_k E_{idx_k}(h[t]) + shared(h[t]) like moe_forward, for any
- * n_tokens >= 1 (not bounded by max_tokens).  The expert products run as
- * tensor-core GEMMs (tcgen05) over fp16 copies of the dequantized weights and
- * of the activations with fp32 accumulation, so results agree with
- * moe_forward to about 1e-3 relative, not bit for bit.  The first call (and
- * any call with more tokens than before) allocates the prefill workspace
- * (about 0.5 MB per token).  idx_out / w_out are optional.  The reference
- * prefills one token at a time through layer_forward (infer.m:2215-2229); this entry
- * point has no counterpart there. */
+ * n_tokens >= 1 (not bounded by max_tokens).  The router and the expert
+ * products run as tensor-core GEMMs (tcgen05): the router on fp16 hi/lo
+ * splits to fp32 accuracy, the experts over fp16 copies of the dequantized
+ * weights and of the activations with fp32 accumulation, so results agree
+ * with moe_forward to about 1e-3 relative, not bit for bit.  With expert
+ * parallelism (world_size > 1) every rank calls with its own tokens (0
+ * allowed); the token rows go to the ranks that own their experts and the
+ * partial sums come back (NCCL), as in moe_forward.  The first call (and any
+ * call with more tokens than before) allocates the prefill workspace (about
+ * 0.5 MB per token, more with expert parallelism).  idx_out / w_out are
+ * optional.  The reference prefills one token at a time through
+ * layer_forward (infer.m:2215-2229); this entry point has no counterpart
+ * there. */
 int moe_prefill_device(moe_ctx *ctx, int layer, const float *d_h_post, int n_tokens, float *d_out,
                        int *d_idx, float *d_w, void *stream);
 int moe_prefill(moe_ctx *ctx, int layer, const float *h_post, int n_tokens, float *out, int *idx_out,

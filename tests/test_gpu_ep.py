@@ -97,3 +97,70 @@ def test_ep2_matches_oracle(cuda_lib, oracle, down_type):
             ref, _, _, _ = O.moe_layer(oracle_cfg(cfg, down_type), blobs, router, bias, h, force_idx=idx, force_w=w)
             err = rel_err(out, ref)
             assert err < TOL and err < GUARD, (rank, step, err)
+
+
+def _ep_prefill_rank(rank, world, uid, cfg_kw, down_type, batches, q):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    try:
+        import flash_deepseek_b200 as F
+        m = F.MoE(F.MoeConfig(**cfg_kw), device=rank, rank=rank, world_size=world, unique_id=uid)
+        m.init_layer_synthetic(0, seed=SEED, down_type=down_type)
+        res = [m.prefill(0, h) for h in batches[rank]]
+        m.close()
+        q.put((rank, res, None))
+    except Exception as e:  # reported to the parent, which fails the test
+        q.put((rank, None, repr(e)))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("down_type", [12, 14])
+def test_ep2_prefill_matches_oracle(cuda_lib, oracle, down_type):
+    """Expert-parallel prefill (tensor-core GEMMs) at 2 GPUs: ragged token
+    counts, then a step where rank 1 has none; every rank's output against the
+    oracle within the prefill bound."""
+    if _gpu_count() < 2:
+        pytest.skip("expert parallelism needs 2 GPUs")
+    from test_gpu_prefill import PREFILL_TOL
+    cfg = small_cfg(intermediate=2048 if down_type == 14 else 512)
+    H, E, O = cfg.hidden, cfg.n_experts, oracle
+
+    def toks(strm, T):
+        return O.normal(strm, O.stream(0, 0, O.KIND_ACT), max(T, 1) * H, 1.0)[:T * H].reshape(T, H)
+
+    batches = {0: [toks(300, 300), toks(301, 40)], 1: [toks(400, 170), toks(401, 0)]}
+    uid = cuda_lib.get_unique_id()
+    ctx = mp.get_context("spawn")
+    qq = ctx.Queue()
+    kw = dict(hidden=cfg.hidden, intermediate=cfg.intermediate, n_experts=cfg.n_experts, n_group=cfg.n_group,
+              topk_group=cfg.topk_group, top_k=cfg.top_k, n_layers=cfg.n_layers, max_tokens=cfg.max_tokens)
+    procs = [ctx.Process(target=_ep_prefill_rank, args=(r, 2, uid, kw, down_type, batches, qq)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = {}
+    try:
+        for _ in range(2):
+            rank, res, err = qq.get(timeout=240)
+            assert err is None, f"rank {rank}: {err}"
+            got[rank] = res
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.terminate()
+                p.join(timeout=30)
+    router, bias = router_of(O, SEED, 0, cfg)
+    blobs = {}
+    for rank in (0, 1):
+        for step, h in enumerate(batches[rank]):
+            out, idx, w = got[rank][step]
+            if h.shape[0] == 0:
+                assert out.shape == (0, H)
+                continue
+            logits = (h.astype(np.float64) @ router.astype(np.float64).T).astype(np.float32)
+            check_routing(O, cfg, logits, bias, idx, w)
+            for e in set(idx.reshape(-1).tolist()) | {E}:
+                if e not in blobs:
+                    blobs[e] = O.gen_expert(SEED, 0, e, H, cfg.intermediate, down_type)
+            ref, _, _, _ = O.moe_layer(oracle_cfg(cfg, down_type), blobs, router, bias, h, force_idx=idx, force_w=w)
+            err = rel_err(out, ref)
+            assert err < PREFILL_TOL, (rank, step, err)
