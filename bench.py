@@ -49,8 +49,9 @@ WORKLOADS = {
 # further BASELINE configs, measured on one GPU by run_extra()
 EXTRA = {
     "expert1": dict(B=1, name="config1_single_q4k_expert"),
-    "stack_b1": dict(B=1, name="config4_stack58_b1_1gpu"),
-    "stack_b8": dict(B=8, name="config4_stack58_b8_1gpu"),
+    "stack_b1": dict(B=1, name="config4_stack58_b1"),
+    "stack_b8": dict(B=8, name="config4_stack58_b8"),
+    "stack_b32": dict(B=32, name="config4_stack58_b32"),
     "prefill4096": dict(B=4096, name="config5_prefill4096_1layer"),
 }
 Q4_DOWN_BYTES = H * (I // 256) * 144         # 8,257,536
@@ -389,7 +390,8 @@ def run_extra(args):
     import flash_deepseek_b200 as F
     W = EXTRA[args.workload]
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    if int(os.environ.get("WORLD_SIZE", "1")) > 1 and args.workload != "prefill4096":
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1 and not (args.workload == "prefill4096" or
+                                                             args.workload.startswith("stack")):
         raise SystemExit(f"--workload {args.workload} runs on one GPU")
     dev = torch.device("cuda", local)
     torch.cuda.set_device(local)
@@ -430,24 +432,50 @@ def run_extra(args):
         unit, ms_step = "expert calls/s", per_call
         e2e = None
     elif args.workload.startswith("stack"):
+        # one GPU holds 20 of the 58 layers (137 GB) and runs them in the order
+        # 0-19, 0-19, 0-17; with expert parallelism every rank holds its
+        # n_experts / world experts of every layer (all 58 at 8 GPUs, ~51 GB)
+        from flash_deepseek_b200 import ep
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        pg = None
+        if world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+            pg = dist
         B = W["B"]
-        n_res, seq = 20, [(0, 20), (0, 20), (0, 18)]
-        cfg = F.MoeConfig(n_layers=n_res, max_tokens=B)
-        moe = F.MoE(cfg)
+        layer_gb = (E / world * 26.6 + 28.6 + 7.4) / 1e3  # experts of this rank + shared + router, GB
+        n_res = min(58, max(1, int(140 / layer_gb)))
+        seq, left = [], 58
+        while left > 0:
+            seq.append((0, min(n_res, left)))
+            left -= seq[-1][1]
+        t0, bl = ep.local_tokens(B, world, rank)
+        uid = ep.share_unique_id(pg, rank, F.get_unique_id) if world > 1 else None
+        cfg = F.MoeConfig(n_layers=n_res, max_tokens=max(1, -(-B // world)))  # the same capacity on every rank
+        moe = F.MoE(cfg, device=local, rank=rank, world_size=world, unique_id=uid)
         for l in range(n_res):
             moe.init_layer_synthetic(l, seed=0, down_type=F.TYPE_Q6_K if l % 2 == 0 else F.TYPE_Q4_K)
-        hs = [torch.randn(B, H, generator=g).to(dev) for _ in range(4)]
-        hid = torch.empty(B, H, device=dev)
+        hs = [torch.randn(B, H, generator=g)[t0:t0 + bl].contiguous().to(dev) for _ in range(4)]
+        hid = torch.empty(max(1, bl), H, device=dev)
         stream = torch.cuda.ExternalStream(moe.stream, device=dev)
 
+        def sync_all():
+            torch.cuda.synchronize()
+            if pg:
+                pg.barrier()
+            torch.cuda.synchronize()
+
         def step(i):
-            hid.copy_(hs[i % 4])
+            if bl:
+                hid[:bl].copy_(hs[i % 4])
             for f0, nl in seq:
-                moe.forward_stack_device(f0, nl, hid, B, stream=moe.stream)
+                moe.forward_stack_device(f0, nl, hid, bl, stream=moe.stream)
         with torch.cuda.stream(stream):
             for i in range(args.warmup):
                 step(i)
-        torch.cuda.synchronize()
+        sync_all()
         l0 = moe.kernel_launches
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
         with torch.cuda.stream(stream):
@@ -455,39 +483,51 @@ def run_extra(args):
                 ev[i][0].record(stream)
                 step(i)
                 ev[i][1].record(stream)
-        torch.cuda.synchronize()
+        sync_all()
         ms = sum(x.elapsed_time(y) for x, y in ev)
+        if pg:
+            t = torch.tensor([ms], dtype=torch.float64)
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+            ms = float(t[0])
         launches = moe.kernel_launches - l0
         ms_step = ms / args.steps
         value = B * args.steps / (ms / 1e3)
         unit = "tokens/s"
         # B = 1: every layer reads the router and exactly K + 1 = 9 distinct experts
         layer_b = [ROUTER_BYTES + (K + 1) * (2 * GATE_BYTES + (DOWN_Q6_BYTES if l % 2 == 0 else Q4_DOWN_BYTES))
-                   for l in range(n_res)]
-        step_b = sum(sum(layer_b[f0:f0 + nl]) for f0, nl in seq)
+                   for l in range(58)]
+        step_b = sum(layer_b)
         roof = None
         if B == 1:
-            roof = {"bound": "hbm", "kernel": "whole 58-layer step", "achieved": round(step_b / (ms_step / 1e3) / 1e9, 1),
-                    "peak": peak, "unit": "GB/s", "frac": round(step_b / (ms_step / 1e3) / 1e9 / peak, 4),
+            roof = {"bound": "hbm", "kernel": "whole 58-layer step" + (f", {world} GPUs (peak = {world} x HBM)"
+                                                                      if world > 1 else ""),
+                    "achieved": round(step_b / (ms_step / 1e3) / 1e9, 1), "peak": peak * world, "unit": "GB/s",
+                    "frac": round(step_b / (ms_step / 1e3) / 1e9 / (peak * world), 4),
                     "peak_source": peak_kind, "algorithmic_bytes_per_step": step_b, "traffic": None}
-        h_pin = hs[0].cpu().pin_memory().numpy()
-        lib = moe.lib
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        buf = h_pin.copy()
-        lib.moe_forward_stack(moe.ctx, 0, 20, buf.ctypes.data, B)
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        n_e2e = max(2, args.steps // 4)
-        for i in range(n_e2e):
-            buf[:] = h_pin
-            for f0, nl in seq:
-                rc = lib.moe_forward_stack(moe.ctx, f0, nl, buf.ctypes.data, B)
-                if rc != 0:
-                    raise RuntimeError(lib.moe_last_error(moe.ctx))
-        e2e_s = time.perf_counter() - t0
-        e2e = {"value": round(B * n_e2e / e2e_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 3 * B * H * 4,
-               "d2h_bytes_per_step": 3 * B * H * 4, "timer": "host wall clock (synchronous calls)"}
-        extra = {"layers_resident": n_res, "layer_calls_per_step": 58}
+        e2e = None
+        if world == 1:
+            h_pin = hs[0].cpu().pin_memory().numpy()
+            lib = moe.lib
+            buf = h_pin.copy()
+            lib.moe_forward_stack(moe.ctx, 0, n_res, buf.ctypes.data, B)
+            torch.cuda.synchronize()
+            t_0 = time.perf_counter()
+            n_e2e = max(2, args.steps // 4)
+            for i in range(n_e2e):
+                buf[:] = h_pin
+                for f0, nl in seq:
+                    rc = lib.moe_forward_stack(moe.ctx, f0, nl, buf.ctypes.data, B)
+                    if rc != 0:
+                        raise RuntimeError(lib.moe_last_error(moe.ctx))
+            e2e_s = time.perf_counter() - t_0
+            e2e = {"value": round(B * n_e2e / e2e_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": 3 * B * H * 4,
+                   "d2h_bytes_per_step": 3 * B * H * 4, "timer": "host wall clock (synchronous calls)"}
+        extra = {"layers_resident": n_res, "layer_calls_per_step": 58, "tokens_per_rank": bl,
+                 "parallelism": f"ep{world}"}
+        if rank != 0:
+            clk.__exit__(None, None, None)
+            moe.close()
+            return
     else:  # prefill4096: one moe_prefill_device call (tcgen05 GEMMs) per step and rank
         from flash_deepseek_b200 import ep
         world = int(os.environ.get("WORLD_SIZE", "1"))
