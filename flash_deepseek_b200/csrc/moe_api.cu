@@ -83,6 +83,15 @@ struct moe_ctx {
     int *send_meta = nullptr, *recv_meta = nullptr;
     float *rows_partial = nullptr;
     int *tok_slot = nullptr;
+    // NVLink peer-memory exchange (moe_ep.cu): own mailbox, the peers' mapped
+    // mailboxes (device array of world pointers), region offsets, step number
+    bool p2p = false;
+    uint8_t *mbox = nullptr;
+    uint8_t **d_peers = nullptr;
+    std::vector<uint8_t *> peer_map;
+    size_t mb_x = 0, mb_meta = 0, mb_y = 0;
+    int *ep_done = nullptr;  // [2] block counters of the two signalling kernels
+    unsigned long long ep_seq = 0;
     std::string err;
     bool timing = false;
     int ring = 0, ring_pos = 0, ring_used = 0;  // per-step phase events
@@ -209,6 +218,81 @@ static int ctx_alloc(moe_ctx *c) {
     return MOE_OK;
 }
 
+// Maps every peer's mailbox into this process (CUDA IPC handles exchanged
+// once over NCCL).  Falls back to the NCCL send/recv exchange when a mapping
+// is refused (no peer access) or MOE_EP_NCCL=1.
+static int ep_p2p_init(moe_ctx *c) {
+    const char *env = getenv("MOE_EP_NCCL");
+    if (env && env[0] == '1') return MOE_OK;
+    const int N = c->world, K = c->d.K, H = c->d.H;
+    if (N > 64) return MOE_OK;
+    const size_t R = (size_t)N * c->max_tok, mw = 2 + 2 * (size_t)K;
+    auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
+    c->mb_x = 1024;
+    c->mb_meta = c->mb_x + al(2 * R * H * sizeof(float));
+    c->mb_y = c->mb_meta + al(2 * R * mw * sizeof(int));
+    const size_t total = c->mb_y + 2 * R * H * sizeof(float);
+    CK(cudaMalloc((void **)&c->mbox, total));
+    CK(cudaMemset(c->mbox, 0, total));
+    CK(cudaMalloc((void **)&c->ep_done, 2 * sizeof(int)));
+    CK(cudaMemset(c->ep_done, 0, 2 * sizeof(int)));
+    CK(cudaMalloc((void **)&c->d_peers, N * sizeof(uint8_t *)));
+    cudaIpcMemHandle_t mine;
+    CK(cudaIpcGetMemHandle(&mine, c->mbox));
+    uint8_t *dh = nullptr;
+    CK(cudaMalloc((void **)&dh, (N + 1) * sizeof(cudaIpcMemHandle_t)));
+    CK(cudaMemcpy(dh, &mine, sizeof(mine), cudaMemcpyHostToDevice));
+    NK(moe_nccl()->GroupStart());
+    for (int p = 0; p < N; p++) {
+        NK(moe_nccl()->Send(dh, sizeof(mine), ncclUint8, p, c->comm, c->stream));
+        NK(moe_nccl()->Recv(dh + (p + 1) * sizeof(mine), sizeof(mine), ncclUint8, p, c->comm, c->stream));
+    }
+    NK(moe_nccl()->GroupEnd());
+    std::vector<cudaIpcMemHandle_t> hs(N);
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaMemcpy(hs.data(), dh + sizeof(mine), N * sizeof(mine), cudaMemcpyDeviceToHost));
+    cudaFree(dh);
+    c->peer_map.assign(N, nullptr);
+    bool ok = true;
+    for (int p = 0; p < N && ok; p++) {
+        if (p == c->rank) { c->peer_map[p] = c->mbox; continue; }
+        void *ptr = nullptr;
+        if (cudaIpcOpenMemHandle(&ptr, hs[p], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            ok = false;
+        } else {
+            c->peer_map[p] = (uint8_t *)ptr;
+        }
+    }
+    // every rank must take the same path: agree on the outcome
+    int *dflag = nullptr;
+    CK(cudaMalloc((void **)&dflag, (N + 1) * sizeof(int)));
+    const int mine_ok = ok ? 1 : 0;
+    CK(cudaMemcpy(dflag, &mine_ok, sizeof(int), cudaMemcpyHostToDevice));
+    NK(moe_nccl()->GroupStart());
+    for (int p = 0; p < N; p++) {
+        NK(moe_nccl()->Send(dflag, 1, ncclInt32, p, c->comm, c->stream));
+        NK(moe_nccl()->Recv(dflag + 1 + p, 1, ncclInt32, p, c->comm, c->stream));
+    }
+    NK(moe_nccl()->GroupEnd());
+    std::vector<int> oks(N);
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaMemcpy(oks.data(), dflag + 1, N * sizeof(int), cudaMemcpyDeviceToHost));
+    cudaFree(dflag);
+    for (int p = 0; p < N; p++) ok = ok && oks[p];
+    if (!ok) {
+        for (int p = 0; p < N; p++)
+            if (c->peer_map[p] && p != c->rank) cudaIpcCloseMemHandle(c->peer_map[p]);
+        c->peer_map.clear();
+        cudaFree(c->mbox);
+        c->mbox = nullptr;
+        return MOE_OK;  // the NCCL send/recv exchange
+    }
+    CK(cudaMemcpy(c->d_peers, c->peer_map.data(), N * sizeof(uint8_t *), cudaMemcpyHostToDevice));
+    c->p2p = true;
+    return MOE_OK;
+}
+
 moe_ctx *moe_create(const moe_config *cfg, int device, int rank, int world_size, const void *uid) {
     if (!cfg) return nullptr;
     moe_ctx *c = new moe_ctx();
@@ -270,6 +354,11 @@ moe_ctx *moe_create(const moe_config *cfg, int device, int rank, int world_size,
             moe_destroy(c);
             return nullptr;
         }
+        if (ep_p2p_init(c) != MOE_OK) {
+            fprintf(stderr, "[moe_cuda] ERROR: moe_create: %s\n", c->err.c_str());
+            moe_destroy(c);
+            return nullptr;
+        }
     }
     return c;
 }
@@ -278,6 +367,11 @@ void moe_destroy(moe_ctx *c) {
     if (!c) return;
     cudaSetDevice(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
+    for (size_t p = 0; p < c->peer_map.size(); p++)
+        if (c->peer_map[p] && (int)p != c->rank) cudaIpcCloseMemHandle(c->peer_map[p]);
+    cudaFree(c->mbox);
+    cudaFree(c->d_peers);
+    cudaFree(c->ep_done);
     if (c->comm) moe_nccl()->CommDestroy(c->comm);
     for (cudaEvent_t e : c->ev) cudaEventDestroy(e);
     for (auto &g : c->graphs) cudaGraphExecDestroy(g.exec);
@@ -627,18 +721,34 @@ static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_i
         moe_launch_route_and_plan(d, nullptr, 0, c->logits, L.bias, L.logit_bias, mode, idx_in, w_in, T, c->idx,
                                   c->wts, x, nullptr, 0, 0, c->plan, c->counter, s, &c->launches);
     mark(c, MOE_PHASE_DISPATCH, s);
-    moe_launch_ep_pack(x, c->idx, c->wts, T, d.K, d.H, N, c->n_local, cap, c->send_x, c->send_meta, c->tok_slot, s,
-                       &c->launches);
-    NK(moe_nccl()->GroupStart());
-    for (int p = 0; p < N; p++) {
-        NK(moe_nccl()->Send(c->send_x + (size_t)p * cap * d.H, (size_t)cap * d.H, ncclFloat32, p, c->comm, s));
-        NK(moe_nccl()->Recv(c->recv_x + (size_t)p * cap * d.H, (size_t)cap * d.H, ncclFloat32, p, c->comm, s));
-        NK(moe_nccl()->Send(c->send_meta + (size_t)p * cap * mw, (size_t)cap * mw, ncclInt32, p, c->comm, s));
-        NK(moe_nccl()->Recv(c->recv_meta + (size_t)p * cap * mw, (size_t)cap * mw, ncclInt32, p, c->comm, s));
+    // the step's mailbox regions (peer-memory exchange) or the NCCL buffers
+    EpP2P q{c->d_peers, c->mb_x, c->mb_meta, c->mb_y, N, c->rank, 0, 0};
+    float *recv_x = c->recv_x, *recv_y = c->recv_y;
+    int *recv_meta = c->recv_meta;
+    if (c->p2p) {
+        q.seq = ++c->ep_seq;
+        q.parity = (int)(q.seq & 1);
+        recv_x = reinterpret_cast<float *>(c->mbox + c->mb_x) + (size_t)q.parity * R * d.H;
+        recv_meta = reinterpret_cast<int *>(c->mbox + c->mb_meta) + (size_t)q.parity * R * mw;
+        recv_y = reinterpret_cast<float *>(c->mbox + c->mb_y) + (size_t)q.parity * R * d.H;
+        moe_launch_ep_pack_p2p(x, c->idx, c->wts, T, d.K, d.H, c->n_local, cap, q, c->tok_slot, c->ep_done, s,
+                               &c->launches);
+        moe_launch_ep_wait(reinterpret_cast<const unsigned long long *>(c->mbox), N, q.seq, c->plan.error, s,
+                           &c->launches);
+    } else {
+        moe_launch_ep_pack(x, c->idx, c->wts, T, d.K, d.H, N, c->n_local, cap, c->send_x, c->send_meta, c->tok_slot,
+                           s, &c->launches);
+        NK(moe_nccl()->GroupStart());
+        for (int p = 0; p < N; p++) {
+            NK(moe_nccl()->Send(c->send_x + (size_t)p * cap * d.H, (size_t)cap * d.H, ncclFloat32, p, c->comm, s));
+            NK(moe_nccl()->Recv(c->recv_x + (size_t)p * cap * d.H, (size_t)cap * d.H, ncclFloat32, p, c->comm, s));
+            NK(moe_nccl()->Send(c->send_meta + (size_t)p * cap * mw, (size_t)cap * mw, ncclInt32, p, c->comm, s));
+            NK(moe_nccl()->Recv(c->recv_meta + (size_t)p * cap * mw, (size_t)cap * mw, ncclInt32, p, c->comm, s));
+        }
+        NK(moe_nccl()->GroupEnd());
     }
-    NK(moe_nccl()->GroupEnd());
-    moe_launch_ep_plan(d, c->recv_meta, N, cap, T, c->e0, c->n_local, c->plan, s, &c->launches);
-    moe_launch_prep_rows(c->recv_x, c->recv_meta, mw, R, x, T, d.H, c->xop, s, &c->launches);
+    moe_launch_ep_plan(d, recv_meta, N, cap, T, c->e0, c->n_local, c->plan, s, &c->launches);
+    moe_launch_prep_rows(recv_x, recv_meta, mw, R, x, T, d.H, c->xop, s, &c->launches);
     const int P = R * d.K + T;
     const int max_chunks = (P + MOE_TC - 1) / MOE_TC + d.E + 1;
     mark(c, MOE_PHASE_GATEUP, s);
@@ -649,16 +759,22 @@ static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_i
     mark(c, MOE_PHASE_DOWN, s);
     moe_launch_down(d, L, c->plan, c->dop, c->eo, max_chunks, s, &c->launches);
     mark(c, MOE_PHASE_COMBINE, s);
-    moe_launch_ep_partial(d, c->plan, c->recv_meta, c->eo, R, c->send_y, s, &c->launches);
-    NK(moe_nccl()->GroupStart());
-    for (int p = 0; p < N; p++) {
-        NK(moe_nccl()->Send(c->send_y + (size_t)p * cap * d.H, (size_t)cap * d.H, ncclFloat32, p, c->comm, s));
-        NK(moe_nccl()->Recv(c->recv_y + (size_t)p * cap * d.H, (size_t)cap * d.H, ncclFloat32, p, c->comm, s));
+    if (c->p2p) {
+        moe_launch_ep_partial_p2p(d, c->plan, recv_meta, c->eo, cap, q, c->ep_done + 1, s, &c->launches);
+        moe_launch_ep_wait(reinterpret_cast<const unsigned long long *>(c->mbox) + 64, N, q.seq, c->plan.error, s,
+                           &c->launches);
+    } else {
+        moe_launch_ep_partial(d, c->plan, c->recv_meta, c->eo, R, c->send_y, s, &c->launches);
+        NK(moe_nccl()->GroupStart());
+        for (int p = 0; p < N; p++) {
+            NK(moe_nccl()->Send(c->send_y + (size_t)p * cap * d.H, (size_t)cap * d.H, ncclFloat32, p, c->comm, s));
+            NK(moe_nccl()->Recv(c->recv_y + (size_t)p * cap * d.H, (size_t)cap * d.H, ncclFloat32, p, c->comm, s));
+        }
+        NK(moe_nccl()->GroupEnd());
     }
-    NK(moe_nccl()->GroupEnd());
     mark(c, MOE_PHASE_OUTPUT, s);
     if (T > 0)
-        moe_launch_ep_final(d, c->plan, c->recv_y, c->tok_slot, N, cap, T, c->eo, residual, out, s, &c->launches);
+        moe_launch_ep_final(d, c->plan, recv_y, c->tok_slot, N, cap, T, c->eo, residual, out, s, &c->launches);
     mark(c, MOE_N_PHASES, s);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(c, MOE_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));

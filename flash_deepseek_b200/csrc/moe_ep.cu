@@ -251,3 +251,151 @@ void moe_launch_ep_final(const MoeDims &d, const MoePlan &plan, const float *rec
     k_ep_final<<<grid, 256, 0, s>>>(d, plan, recv_y, tok_slot, world, cap, T, eo, residual, out);
     LAUNCH_COUNT(launches);
 }
+
+// ===========================================================================
+// NVLink peer-memory exchange.  Every rank owns a mailbox (one allocation,
+// mapped into every peer with CUDA IPC):
+//   [flags: dispatch[64], combine[64] (u64 step numbers)]
+//   [recv_x  (2 parities) [world*cap][H] fp32]
+//   [recv_meta (2)        [world*cap][2+2K] int]
+//   [recv_y  (2)          [world*cap][H] fp32]
+// The pack kernel stores each token row straight into the mailboxes of the
+// ranks that own its experts, and the pre-combine kernel stores each partial
+// row straight into the mailbox of the token's rank: the copy is part of the
+// kernel that produces the data, there is no separate collective.  When a
+// kernel's blocks are done (every thread fences its stores at system scope),
+// its last block writes the step number into the matching flag of every
+// peer (release, system scope).  The consumers wait (acquire, bounded) for
+// the flags of all peers.  Buffers alternate by step parity: a rank cannot
+// reach step n + 2 before every peer has finished consuming step n (it needs
+// their step n + 1 partials first).
+// ===========================================================================
+#define EP_WAIT_NS 2000000000ull
+#define EP_ERR_TIMEOUT 0x7300
+
+__device__ __forceinline__ unsigned long long ep_ld_acquire(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void ep_st_release(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ep_now() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// every thread: wait until flags[p] >= seq for all p < world (bounded)
+__device__ bool ep_wait_flags(const unsigned long long *flags, int world, unsigned long long seq, int *error) {
+    const unsigned long long t0 = ep_now();
+    for (int p = 0; p < world; p++)
+        while (ep_ld_acquire(flags + p) < seq) {
+            if (ep_now() - t0 > EP_WAIT_NS) {
+                atomicExch(error, EP_ERR_TIMEOUT);
+                return false;
+            }
+        }
+    return true;
+}
+
+// after the block's stores: the last block of the grid raises flags[me] = seq
+// in every peer's mailbox (flag_off = byte offset of the flag array)
+__device__ void ep_signal(const EpP2P &q, size_t flag_off, int *done) {
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned int nblk = gridDim.x * gridDim.y;
+        if (atomicAdd(done, 1) == (int)nblk - 1) {
+            *done = 0;  // stream order keeps the next launch behind this reset
+            __threadfence_system();
+            for (int p = 0; p < q.world; p++)
+                ep_st_release(reinterpret_cast<unsigned long long *>(q.peers[p] + flag_off) + q.me, q.seq);
+        }
+    }
+}
+
+// grid = T blocks (+1 that clears the unused rows' valid flags on every peer)
+__global__ void k_ep_pack_p2p(const float *__restrict__ x, const int *__restrict__ idx, const float *__restrict__ w,
+                              int T, int K, int H, int n_local, int cap, EpP2P q, int *__restrict__ tok_slot,
+                              int *done) {
+    __shared__ unsigned long long pm[64];
+    const int world = q.world, meta_w = 2 + 2 * K;
+    const size_t R = (size_t)world * cap;
+    for (int p = threadIdx.x; p < world; p += blockDim.x) pm[p] = peer_mask(idx, T, K, n_local, p);
+    __syncthreads();
+    if (blockIdx.x == T) {
+        for (int s = threadIdx.x; s < world * cap; s += blockDim.x) {
+            const int p = s / cap, i = s % cap;
+            if (i >= __popcll(pm[p])) {
+                int *meta = reinterpret_cast<int *>(q.peers[p] + q.off_meta) + (size_t)q.parity * R * meta_w;
+                meta[((size_t)q.me * cap + i) * meta_w] = 0;
+            }
+        }
+    } else {
+        const int t = blockIdx.x;
+        for (int p = 0; p < world; p++) {
+            const bool hit = (pm[p] >> t) & 1ull;
+            const int slot = hit ? __popcll(pm[p] & ((1ull << t) - 1ull)) : -1;
+            if (threadIdx.x == 0) tok_slot[t * world + p] = slot;
+            if (!hit) continue;
+            const size_t row = (size_t)q.parity * R + (size_t)q.me * cap + slot;
+            const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)t * H);
+            float4 *dst = reinterpret_cast<float4 *>(reinterpret_cast<float *>(q.peers[p] + q.off_x) + row * H);
+            for (int i = threadIdx.x; i < H / 4; i += blockDim.x) dst[i] = src[i];
+            int *m = reinterpret_cast<int *>(q.peers[p] + q.off_meta) + row * meta_w;
+            if (threadIdx.x == 0) { m[0] = 1; m[1] = t; }
+            for (int k = threadIdx.x; k < K; k += blockDim.x) {
+                m[2 + k] = idx[t * K + k];
+                m[2 + K + k] = __float_as_int(w[t * K + k]);
+            }
+        }
+    }
+    ep_signal(q, 0, done);
+}
+
+// pre-combine (k_ep_partial's sum) stored straight into the token rank's
+// mailbox: received row r = (source p, slot s) -> p's recv_y row me*cap + s
+__global__ void k_ep_partial_p2p(MoeDims d, MoePlan plan, const int *__restrict__ recv_meta,
+                                 const float *__restrict__ eo, int cap, EpP2P q, int *done) {
+    const int r = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int K = d.K;
+    if (i < d.H && recv_meta[(size_t)r * (2 + 2 * K)]) {
+        float acc = 0.0f;
+        for (int k = 0; k < K; k++) {
+            const int p = plan.slot_pair[(size_t)r * (K + 1) + k];
+            if (p < 0) continue;
+            acc = fmaf(plan.pair_w[p], eo[(size_t)p * d.H + i], acc);
+        }
+        const int src = r / cap, s = r % cap;
+        const size_t R = (size_t)q.world * cap;
+        float *y = reinterpret_cast<float *>(q.peers[src] + q.off_y) + (size_t)q.parity * R * d.H;
+        y[((size_t)q.me * cap + s) * d.H + i] = acc;
+    }
+    ep_signal(q, 64 * sizeof(unsigned long long), done);
+}
+
+// the dispatch flags of every peer, before the plan reads the mailbox
+__global__ void k_ep_wait(const unsigned long long *flags, int world, unsigned long long seq, int *error) {
+    ep_wait_flags(flags, world, seq, error);
+}
+
+void moe_launch_ep_pack_p2p(const float *x, const int *idx, const float *w, int T, int K, int H, int n_local,
+                            int cap, const EpP2P &q, int *tok_slot, int *done, cudaStream_t s, uint64_t *launches) {
+    k_ep_pack_p2p<<<T + 1, 256, 0, s>>>(x, idx, w, T, K, H, n_local, cap, q, tok_slot, done);
+    LAUNCH_COUNT(launches);
+}
+
+void moe_launch_ep_partial_p2p(const MoeDims &d, const MoePlan &plan, const int *recv_meta, const float *eo, int cap,
+                               const EpP2P &q, int *done, cudaStream_t s, uint64_t *launches) {
+    dim3 grid((d.H + 255) / 256, q.world * cap);
+    k_ep_partial_p2p<<<grid, 256, 0, s>>>(d, plan, recv_meta, eo, cap, q, done);
+    LAUNCH_COUNT(launches);
+}
+
+void moe_launch_ep_wait(const unsigned long long *flags, int world, unsigned long long seq, int *error, cudaStream_t s,
+                        uint64_t *launches) {
+    k_ep_wait<<<1, 32, 0, s>>>(flags, world, seq, error);
+    LAUNCH_COUNT(launches);
+}

@@ -150,6 +150,20 @@ void moe_launch_prep_rows(const float *recv, const int *meta, int meta_w, int R,
 // expert parallel (moe_ep.cu)
 void moe_launch_ep_pack(const float *x, const int *idx, const float *w, int T, int K, int H, int world, int n_local,
                         int cap, float *send_x, int *send_meta, int *tok_slot, cudaStream_t s, uint64_t *launches);
+// NVLink peer-memory exchange (moe_ep.cu): mailbox base of every rank
+// (peers[me] = own), byte offsets of its regions, the step's parity and number
+struct EpP2P {
+    uint8_t *const *peers;
+    size_t off_x, off_meta, off_y;
+    int world, me, parity;
+    unsigned long long seq;
+};
+void moe_launch_ep_pack_p2p(const float *x, const int *idx, const float *w, int T, int K, int H, int n_local,
+                            int cap, const EpP2P &q, int *tok_slot, int *done, cudaStream_t s, uint64_t *launches);
+void moe_launch_ep_partial_p2p(const MoeDims &d, const MoePlan &plan, const int *recv_meta, const float *eo, int cap,
+                               const EpP2P &q, int *done, cudaStream_t s, uint64_t *launches);
+void moe_launch_ep_wait(const unsigned long long *flags, int world, unsigned long long seq, int *error, cudaStream_t s,
+                        uint64_t *launches);
 void moe_launch_ep_plan(const MoeDims &d, const int *recv_meta, int world, int cap, int T, int e0, int n_local,
                         const MoePlan &plan, cudaStream_t s, uint64_t *launches);
 void moe_launch_ep_partial(const MoeDims &d, const MoePlan &plan, const int *recv_meta, const float *eo, int rows,
