@@ -458,8 +458,50 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
     if (tid == 0) counters[blockIdx.z * gridDim.x + blockIdx.x] = 0;
 }
 
+// Few tokens (T <= RS_MAX_T): one CTA per expert reads the expert's whole
+// router row (H fp32, all loads in flight at once) and reduces in a fixed
+// order, so there is no second pass over partials.  Same fp32 dot product as
+// the reference's sgemv (infer.m:1881) up to summation order.
+#define RS_MAX_T 4
+__global__ void __launch_bounds__(256) k_router_small(const float *__restrict__ Wr, const float *__restrict__ x, int T,
+                                                      int H, int E, float *__restrict__ logits) {
+    __shared__ float red[RS_MAX_T][8];
+    moe_pdl_wait();
+    moe_pdl_trigger();
+    const int e = blockIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const float4 *w4 = reinterpret_cast<const float4 *>(Wr + (size_t)e * H);
+    float acc[RS_MAX_T] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int i = threadIdx.x; i < H / 4; i += blockDim.x) {
+        const float4 w = __ldg(w4 + i);
+#pragma unroll
+        for (int t = 0; t < RS_MAX_T; t++) {
+            if (t >= T) break;
+            const float4 v = __ldg(reinterpret_cast<const float4 *>(x + (size_t)t * H) + i);
+            acc[t] = fmaf(w.x, v.x, fmaf(w.y, v.y, fmaf(w.z, v.z, fmaf(w.w, v.w, acc[t]))));
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < RS_MAX_T; t++) {
+        float v = acc[t];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) red[t][wid] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x < T) {
+        float v = 0.0f;
+        for (int w = 0; w < 8; w++) v += red[threadIdx.x][w];
+        logits[(size_t)threadIdx.x * E + e] = v;
+    }
+}
+
 void moe_launch_router_logits(const float *Wr, const float *x, int T, int H, int E, float *part, int n_split,
                               float *logits, int *counters, cudaStream_t s, uint64_t *launches) {
+    if (T <= RS_MAX_T && H % 4 == 0) {
+        moe_launch_pdl(k_router_small, dim3(E), dim3(256), 0, s, Wr, x, T, H, E, logits);
+        LAUNCH_COUNT(launches);
+        return;
+    }
     dim3 grid((E + 31) / 32, n_split, (T + 63) / 64);
     const size_t smem = sizeof(float) * (32 * RL_WPAD + RL_KS * 64);
     static bool attr = false;
