@@ -515,14 +515,32 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
         fence_barrier_init();
     }
     __syncthreads();
-    moe_pdl_wait();
+    // The plan (two launches older) and the weights do not depend on the
+    // previous kernel, only the down operand does: the producer issues the
+    // weight copies of its first NS stages before the dependency wait and
+    // their operand copies after it.  The consumers only read shared memory
+    // behind the full barriers.
     moe_pdl_trigger();
     const int n_chunks = plan.counts[1];
     const int n_items = n_chunks * (d.H / DN_ROWS);
     uint32_t seq = 0, nitem = 0;
     if (warp == EX_CONSUMERS) {  // producer
         const size_t opst = op_bytes(d.I);
-        bool ok = true;
+        bool ok = true, waited = false;
+        int ndef = 0, def_st[NS], def_p0[NS], def_nt[NS], def_sb[NS];
+        auto issue_ops = [&](int st, int p0, int ntok, int sb) {
+            if (lane < ntok) {
+                uint8_t *od = sm + (size_t)st * STAGE + (TY == MOE_TYPE_Q6_K ? DN6_QBOX + DN6_SBOX : DN4_WBOX) +
+                              lane * OPB_SB;
+                bulk_load(od, dop + (size_t)(p0 + lane) * opst + (size_t)sb * OPB_SB, OPB_SB, &full[st]);
+            }
+        };
+        auto flush_deferred = [&]() {
+            moe_pdl_wait();
+            waited = true;
+            for (int k = 0; k < ndef; k++) issue_ops(def_st[k], def_p0[k], def_nt[k], def_sb[k]);
+            ndef = 0;
+        };
         for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
             ExItem it;
             ex_item(plan, L, d.E, n_chunks, item, it);
@@ -546,17 +564,21 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
                     }
                 }
                 __syncwarp();
-                if (lane < it.ntok) {
-                    uint8_t *od = stage + (TY == MOE_TYPE_Q6_K ? DN6_QBOX + DN6_SBOX : DN4_WBOX) + lane * OPB_SB;
-                    bulk_load(od, dop + (size_t)(it.p0 + lane) * opst + (size_t)sb * OPB_SB, OPB_SB, &full[st]);
+                if (waited) {
+                    issue_ops(st, it.p0, it.ntok, sb);
+                } else {
+                    def_st[ndef] = st; def_p0[ndef] = it.p0; def_nt[ndef] = it.ntok; def_sb[ndef] = sb;
+                    if (++ndef == NS) flush_deferred();
                 }
             }
         }
+        if (!waited) flush_deferred();
         if (!ok && lane == 0) atomicExch(plan.error, EX_ERR_TIMEOUT);
         for (uint32_t k = seq > (uint32_t)NS ? seq - NS : 0; k < seq; k++)
             if (!mbar_wait(&full[k % NS], (k / NS) & 1)) break;
         return;
     }
+    moe_pdl_wait();
     for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
         ExItem it;
         ex_item(plan, L, d.E, n_chunks, item, it);
