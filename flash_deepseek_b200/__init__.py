@@ -132,6 +132,12 @@ class MoE:
     def last_weight_bytes(self) -> int:
         return int(self.lib.moe_last_weight_bytes(self.ctx))
 
+    def record_expert_hits(self, d_hits):
+        """While d_hits (device int32 [n_layers]) is set, every device forward
+        writes d_hits[layer] = routed experts of this rank hit by that layer;
+        None stops recording."""
+        self._check(self.lib.moe_record_expert_hits(self.ctx, _ptr(d_hits)), "moe_record_expert_hits")
+
     def set_timing(self, ring_steps: int = 1):
         """Record per-phase CUDA events for the last `ring_steps` forward calls
         (0 turns timing off)."""

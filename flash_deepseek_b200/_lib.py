@@ -56,6 +56,7 @@ SIGNATURES = {
     "moe_kernel_launches": (C.c_uint64, [_vp]),
     "moe_reset_kernel_launches": (None, [_vp]),
     "moe_last_weight_bytes": (C.c_uint64, [_vp]),
+    "moe_record_expert_hits": (C.c_int, [_vp, _vp]),
     "moe_set_timing": (C.c_int, [_vp, C.c_int]),
     "moe_get_timing": (C.c_int, [_vp, _vp, C.c_int]),
     "moe_get_timing_at": (C.c_int, [_vp, C.c_int, _vp, C.c_int]),

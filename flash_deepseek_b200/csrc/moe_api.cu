@@ -91,6 +91,7 @@ struct moe_ctx {
     std::vector<uint8_t *> peer_map;
     size_t mb_x = 0, mb_meta = 0, mb_y = 0;
     int *ep_done = nullptr;  // [2] block counters of the two signalling kernels
+    int *hits = nullptr;     // moe_record_expert_hits target, or nullptr
     unsigned long long ep_seq = 0;
     std::string err;
     bool timing = false;
@@ -839,6 +840,22 @@ static int forward_local_kernels(moe_ctx *c, int layer, const float *d_h, int T,
     return MOE_OK;
 }
 
+// d_hits[layer] = routed experts of this rank hit by the layer that just ran
+// (plan count 2), or 0 when the layer did not run here.
+static int record_hits(moe_ctx *c, int layer, bool ran, cudaStream_t s) {
+    if (!c->hits) return MOE_OK;
+    if (ran) CK(cudaMemcpyAsync(c->hits + layer, c->plan.counts + 2, sizeof(int), cudaMemcpyDeviceToDevice, s));
+    else CK(cudaMemsetAsync(c->hits + layer, 0, sizeof(int), s));
+    return MOE_OK;
+}
+
+int moe_record_expert_hits(moe_ctx *c, int *d_hits) {
+    if (!c) return MOE_ERR_ARG;
+    drop_graphs(c);
+    c->hits = d_hits;
+    return MOE_OK;
+}
+
 int moe_forward_device(moe_ctx *c, int layer, const float *d_h, int T, float *d_out, int *d_idx, float *d_w,
                        void *stream) {
     if (!c) return MOE_ERR_ARG;
@@ -851,13 +868,13 @@ int moe_forward_device(moe_ctx *c, int layer, const float *d_h, int T, float *d_
         rc = run_ep(c, layer, d_h, T, nullptr, nullptr, nullptr, d_out, s);  // every rank joins, even with T == 0
         if (rc) return rc;
     } else {
-        if (T == 0) return MOE_OK;
+        if (T == 0) return record_hits(c, layer, false, s);
         rc = forward_local_kernels(c, layer, d_h, T, d_out, s);
         if (rc) return rc;
     }
     if (d_idx) CK(cudaMemcpyAsync(d_idx, c->idx, sizeof(int) * T * c->d.K, cudaMemcpyDeviceToDevice, s));
     if (d_w) CK(cudaMemcpyAsync(d_w, c->wts, sizeof(float) * T * c->d.K, cudaMemcpyDeviceToDevice, s));
-    return MOE_OK;
+    return record_hits(c, layer, true, s);
 }
 
 static int finish_sync(moe_ctx *c) {
@@ -1101,6 +1118,8 @@ int moe_forward_stack_device(moe_ctx *c, int first, int n_layers, float *d_hidde
                                       &c->launches);
         if (c->world > 1) rc = run_ep(c, l, c->h_post, T, nullptr, nullptr, d_hidden, d_hidden, s);
         else if (T > 0) rc = run_local(c, l, c->h_post, T, nullptr, nullptr, 1, 1, d_hidden, d_hidden, s);
+        if (rc) return rc;
+        rc = record_hits(c, l, c->world > 1 || T > 0, s);
         if (rc) return rc;
     }
     return MOE_OK;

@@ -243,6 +243,13 @@ void moe_reset_kernel_launches(moe_ctx *ctx);
 /* Weight bytes the last forward call had to read on this rank (routed experts
  * actually hit + shared + router), for roofline accounting. */
 uint64_t moe_last_weight_bytes(const moe_ctx *ctx);
+/* Per-layer record of the routed experts this rank read, for critical-path
+ * roofline accounting over a layer stack: while d_hits (device int
+ * [n_layers]) is set, every moe_forward_device / moe_forward_stack_device
+ * layer writes d_hits[layer] = the number of this rank's routed experts
+ * that got at least one token (a device-to-device copy on the call's stream).
+ * NULL stops recording.  Changing it drops the captured CUDA graphs. */
+int moe_record_expert_hits(moe_ctx *ctx, int *d_hits);
 
 #ifdef __cplusplus
 }

@@ -303,3 +303,38 @@ def test_graph_replay_matches_direct_launch(cuda_lib, oracle, monkeypatch):
         m.close()
         monkeypatch.delenv("MOE_NO_GRAPHS", raising=False)
     assert np.array_equal(outs["graphs"].view(np.uint32), outs["direct"].view(np.uint32))
+
+
+@pytest.mark.gpu
+def test_record_expert_hits(cuda_lib, oracle):
+    """moe_record_expert_hits: every device forward of a layer records the
+    number of distinct routed experts its tokens hit, also through the stack
+    entry point, and nothing once recording stops."""
+    import torch
+    cfg = small_cfg(n_layers=2)
+    m = cuda_lib.MoE(cfg)
+    for l in range(2):
+        m.init_layer_synthetic(l, seed=11 + l, down_type=14)
+    T = 5
+    h = oracle.normal(8, oracle.stream(0, 0, oracle.KIND_ACT), T * cfg.hidden, 1.0).reshape(T, cfg.hidden)
+    d_h = torch.from_numpy(h).cuda()
+    d_out = torch.empty_like(d_h)
+    d_idx = torch.empty(T, cfg.top_k, dtype=torch.int32, device="cuda")
+    hits = torch.full((2,), -1, dtype=torch.int32, device="cuda")
+    m.record_expert_hits(hits)
+    for l in range(2):
+        m.forward_device(l, d_h, T, d_out, d_idx=d_idx)
+        torch.cuda.synchronize()
+        assert int(hits[l]) == len(np.unique(d_idx.cpu().numpy())), (l, hits)
+    hits.fill_(-1)
+    d_hid = d_h.clone()
+    m.forward_stack_device(0, 2, d_hid, T)
+    torch.cuda.synchronize()
+    hv = hits.cpu().numpy()
+    assert ((hv >= cfg.top_k) & (hv <= min(T * cfg.top_k, cfg.n_experts))).all(), hv
+    m.record_expert_hits(None)
+    hits.fill_(-1)
+    m.forward_device(0, d_h, T, d_out)
+    torch.cuda.synchronize()
+    assert (hits.cpu().numpy() == -1).all()
+    m.close()
