@@ -301,11 +301,14 @@ __device__ bool ep_wait_flags(const unsigned long long *flags, int world, unsign
 }
 
 // after the block's stores: the last block of the grid raises flags[me] = seq
-// in every peer's mailbox (flag_off = byte offset of the flag array)
+// in every peer's mailbox (flag_off = byte offset of the flag array).  The
+// block barrier orders every thread's stores before thread 0's system-scope
+// fence, which is cumulative, so one fence per block publishes them all (the
+// pattern of a cooperative grid barrier).
 __device__ void ep_signal(const EpP2P &q, size_t flag_off, int *done) {
-    __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) {
+        __threadfence_system();
         const unsigned int nblk = gridDim.x * gridDim.y;
         if (atomicAdd(done, 1) == (int)nblk - 1) {
             *done = 0;  // stream order keeps the next launch behind this reset
@@ -359,19 +362,24 @@ __global__ void k_ep_pack_p2p(const float *__restrict__ x, const int *__restrict
 // mailbox: received row r = (source p, slot s) -> p's recv_y row me*cap + s
 __global__ void k_ep_partial_p2p(MoeDims d, MoePlan plan, const int *__restrict__ recv_meta,
                                  const float *__restrict__ eo, int cap, EpP2P q, int *done) {
-    const int r = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int r = blockIdx.y, i4 = blockIdx.x * blockDim.x + threadIdx.x;  // float4 column
     const int K = d.K;
-    if (i < d.H && recv_meta[(size_t)r * (2 + 2 * K)]) {
-        float acc = 0.0f;
+    if (i4 < d.H / 4 && recv_meta[(size_t)r * (2 + 2 * K)]) {
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         for (int k = 0; k < K; k++) {
             const int p = plan.slot_pair[(size_t)r * (K + 1) + k];
             if (p < 0) continue;
-            acc = fmaf(plan.pair_w[p], eo[(size_t)p * d.H + i], acc);
+            const float wp = plan.pair_w[p];
+            const float4 e = reinterpret_cast<const float4 *>(eo + (size_t)p * d.H)[i4];
+            acc.x = fmaf(wp, e.x, acc.x);
+            acc.y = fmaf(wp, e.y, acc.y);
+            acc.z = fmaf(wp, e.z, acc.z);
+            acc.w = fmaf(wp, e.w, acc.w);
         }
         const int src = r / cap, s = r % cap;
         const size_t R = (size_t)q.world * cap;
         float *y = reinterpret_cast<float *>(q.peers[src] + q.off_y) + (size_t)q.parity * R * d.H;
-        y[((size_t)q.me * cap + s) * d.H + i] = acc;
+        reinterpret_cast<float4 *>(y + ((size_t)q.me * cap + s) * d.H)[i4] = acc;
     }
     ep_signal(q, 64 * sizeof(unsigned long long), done);
 }
@@ -389,7 +397,7 @@ void moe_launch_ep_pack_p2p(const float *x, const int *idx, const float *w, int 
 
 void moe_launch_ep_partial_p2p(const MoeDims &d, const MoePlan &plan, const int *recv_meta, const float *eo, int cap,
                                const EpP2P &q, int *done, cudaStream_t s, uint64_t *launches) {
-    dim3 grid((d.H + 255) / 256, q.world * cap);
+    dim3 grid((d.H / 4 + 255) / 256, q.world * cap);  // H % 256 == 0 (checked at create)
     k_ep_partial_p2p<<<grid, 256, 0, s>>>(d, plan, recv_meta, eo, cap, q, done);
     LAUNCH_COUNT(launches);
 }
