@@ -307,3 +307,128 @@ def test_q6_stage_emulation(tables, oracle):
     ref = np.stack([wdq @ v[0].astype(np.float64), wdq @ v[1].astype(np.float64)], axis=1)
     err = np.max(np.abs(out - ref)) / np.max(np.abs(ref))
     assert err < 1e-12, err
+
+
+# ---------------------------------------------------------------------------
+# The prefill GEMMs' dequantization of one 64-column atom into fp16 pairs
+# (moe_prefill.cu: pf_q4_consts / pf_deq_q4 and pf_q6_consts / pf_deq_q6),
+# emulated step by step with single fp16 roundings, from the repacked bytes
+# the kernels read, against the quant.c dequantization.
+
+def f16(x):
+    """round to the nearest fp16 (ties to even), as a Python float"""
+    return float(np.float16(x))
+
+
+def hfma(a, b, c):
+    return f16(a * b + c)   # a * b is exact in binary64 for fp16 inputs
+
+
+def byte_perm(x, y, s):
+    """__byte_perm(x, y, s): result byte n is byte (s >> 4n) & 7 of y:x"""
+    src = x | (y << 32)
+    return sum(((src >> (8 * ((s >> (4 * n)) & 7))) & 0xFF) << (8 * n) for n in range(4))
+
+
+def h2(u):
+    """the two fp16 halves of a 32-bit word, low first"""
+    return np.array([u & 0xFFFF, u >> 16], np.uint16).view(np.float16).astype(np.float64)
+
+
+def q4_scale_min(sb, j):
+    """get_scale_min_k4 (quant.c:26-34) on the 12 scale bytes"""
+    if j < 4:
+        return sb[j] & 63, sb[j + 4] & 63
+    return (sb[j + 4] & 0xF) | ((sb[j - 4] >> 6) << 4), (sb[j + 4] >> 4) | ((sb[j] >> 6) << 4)
+
+
+def split16(x):
+    hi = f16(np.float32(x))
+    return hi, f16(np.float32(np.float32(x) - np.float32(hi)))
+
+
+def weight_blocks(oracle, qtype, rows, seed):
+    rng = np.random.default_rng(seed)
+    sig = np.array([0.02, 0.5, 1e-3, 3.0, 0.02, 0.1, 2e-4, 0.02][:rows])[:, None]
+    W = (rng.standard_normal((rows, 256)) * sig).astype(np.float32)
+    W[-1, ::7] = 0.0
+    bb = 144 if qtype == oracle.TYPE_Q4_K else 210
+    blocks = oracle.quantize(W.reshape(-1), qtype).reshape(rows, bb)
+    ref = oracle.dequant(blocks.reshape(-1), qtype, rows * 256).reshape(rows, 256).astype(np.float64)
+    return blocks, ref
+
+
+def check_fp16_dequant(out, ref, max_ulps):
+    """error against the fp32 dequantization in units of the fp16 spacing at
+    the correctly rounded value (0.5 = correctly rounded)"""
+    cr = np.vectorize(f16)(ref)
+    ulp = np.maximum(np.spacing(np.abs(cr).astype(np.float16)).astype(np.float64), 2.0 ** -24)
+    e = float(np.max(np.abs(out - ref) / ulp))
+    assert e <= max_ulps, e
+
+
+def test_prefill_q4_dequant_emulation(tables, oracle):
+    rows = 8
+    blocks, ref = weight_blocks(oracle, oracle.TYPE_Q4_K, rows, 21)
+    rep = blocks.copy()
+    for p, s in tables["q4r"].items():   # the load-time transpose of the qs bytes
+        rep[:, 16 + p] = blocks[:, 16 + s]
+    out = np.zeros((rows, 256))
+    for r in range(rows):
+        blk = rep[r]
+        d = float(blk[0:2].view(np.float16)[0])
+        dmin = np.float32(blk[2:4].view(np.float16)[0])
+        sb = [int(b) for b in blk[4:16]]
+        for g in range(4):
+            sc0, m0 = q4_scale_min(sb, 2 * g)
+            sc1, m1 = q4_scale_min(sb, 2 * g + 1)
+            c = [f16(sc0), f16(-1024.0 * sc0), *split16(-dmin * np.float32(m0)),
+                 f16(0.0625 * sc1), f16(-64.0 * sc1), *split16(-dmin * np.float32(m1))]
+            v = np.zeros(64)
+            for t in range(4):
+                for h in range(2):
+                    w = w32(blk, 16 + 32 * t + 8 * g + 4 * h)
+                    x01, x23 = byte_perm(w, 0x64, 0x4140), byte_perm(w, 0x64, 0x4342)
+                    for reg, x, hi in ((4 * t + 2 * h, x01 & 0xFF0FFF0F, 0), (4 * t + 2 * h + 1, x23 & 0xFF0FFF0F, 0),
+                                       (16 + 4 * t + 2 * h, x01 & 0xFFF0FFF0, 1),
+                                       (16 + 4 * t + 2 * h + 1, x23 & 0xFFF0FFF0, 1)):
+                        cc = c[4 * hi:4 * hi + 4]
+                        for i, xv in enumerate(h2(x)):
+                            p = hfma(xv, cc[0], cc[1])
+                            assert p == (xv - 1024.0) / (16.0 if hi else 1.0) * (sc1 if hi else sc0)  # v * sc, exact
+                            v[2 * reg + i] = f16(hfma(p, d, cc[2]) + cc[3])
+            out[r, 64 * g:64 * g + 64] = v
+    check_fp16_dequant(out, ref, 1.0)   # fma, then the low half of dmin*m: two roundings
+
+
+def test_prefill_q6_dequant_emulation(tables, oracle):
+    rows = 8
+    blocks, ref = weight_blocks(oracle, oracle.TYPE_Q6_K, rows, 22)
+    Q = np.zeros((rows, 192), np.uint8)
+    for p, sidx in tables["q6r"].items():   # the load-time Q plane (qh pairs' high bit inverted)
+        Q[:, p] = blocks[:, sidx] ^ (0xAA if sidx >= 128 else 0)
+    S = blocks[:, 192:208].view(np.int8)
+    D = blocks[:, 208:210].copy().view(np.float16)[:, 0]
+    out = np.zeros((rows, 256))
+    for r in range(rows):
+        for A in range(4):
+            h = A >> 1
+            q = [w32(Q[r], 48 * t + 24 * h + 4 * u) for t in range(4) for u in range(6)]
+            c = [x for u in range(4) for x in split16(np.float32(D[r]) * np.float32(S[r, 4 * A + u]))]
+            v = np.zeros(64)
+            for t in range(4):
+                for s4 in range(4):
+                    sp = 4 * (A & 1) + s4
+                    f = sp >> 1
+                    W, Hq = q[6 * t + s4], q[6 * t + 4 + (s4 & 1)]
+                    nib = (W if sp < 4 else W >> 4) & 0x0F0F0F0F
+                    hb = ((Hq << (4 - 2 * f)) if 2 * f <= 4 else (Hq >> (2 * f - 4))) & 0x30303030
+                    q6 = nib | (hb ^ 0x20202020)
+                    fh, fl = c[2 * s4], c[2 * s4 + 1]
+                    for reg, sel in ((8 * s4 + 2 * t, 0x4140), (8 * s4 + 2 * t + 1, 0x4342)):
+                        for i, xv in enumerate(h2(byte_perm(q6, 0x64, sel))):
+                            vq = f16(xv - 1056.0)
+                            assert vq == xv - 1056.0   # q - 32 is exact
+                            v[2 * reg + i] = hfma(vq, fh, f16(vq * fl))
+            out[r, 64 * A:64 * A + 64] = v
+    check_fp16_dequant(out, ref, 0.5)   # correctly rounded: one rounding of (q - 32) * d * sc
