@@ -883,8 +883,11 @@ static int finish_sync(moe_ctx *c) {
     CK(cudaMemcpy(&errflag, c->plan.error, sizeof(int), cudaMemcpyDeviceToHost));
     if (errflag) {
         cudaMemset(c->plan.error, 0, sizeof(int));
-        if (errflag == 0x7100) return fail(c, MOE_ERR_CUDA, "expert pipeline wait timed out");
-        return fail(c, MOE_ERR_ARG, "expert index out of range in routing");
+        if (errflag == EX_ERR_TIMEOUT) return fail(c, MOE_ERR_CUDA, "expert pipeline wait timed out");
+        if (errflag == EP_ERR_TIMEOUT)
+            return fail(c, MOE_ERR_CUDA, "peer exchange wait timed out (a peer rank stopped calling)");
+        if (errflag == MOE_DEV_ERR_INDEX) return fail(c, MOE_ERR_ARG, "expert index out of range in routing");
+        return fail(c, MOE_ERR_CUDA, "device error code 0x%x", errflag);
     }
     return MOE_OK;
 }
@@ -1101,7 +1104,9 @@ int moe_prefill(moe_ctx *c, int layer, const float *h, int T, float *out, int *i
     CK(cudaMemcpy(&errflag, c->pf.plan.error, sizeof(int), cudaMemcpyDeviceToHost));
     if (errflag) {
         cudaMemset(c->pf.plan.error, 0, sizeof(int));
-        return fail(c, errflag == 1 ? MOE_ERR_ARG : MOE_ERR_CUDA, "prefill error code 0x%x", errflag);
+        if (errflag == MOE_DEV_ERR_INDEX) return fail(c, MOE_ERR_ARG, "expert index out of range in routing");
+        if (errflag == PF_ERR_TIMEOUT) return fail(c, MOE_ERR_CUDA, "prefill pipeline wait timed out");
+        return fail(c, MOE_ERR_CUDA, "prefill error code 0x%x", errflag);
     }
     return MOE_OK;
 }

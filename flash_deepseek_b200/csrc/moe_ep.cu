@@ -82,7 +82,7 @@ __global__ void __launch_bounds__(512) k_ep_plan(MoeDims d, const int *__restric
         const int *m = recv_meta + (size_t)r * meta_w;
         if (!m[0]) continue;
         const int e = m[2 + k];
-        if (e < 0 || e >= E) { atomicExch(plan.error, 1); continue; }
+        if (e < 0 || e >= E) { atomicExch(plan.error, MOE_DEV_ERR_INDEX); continue; }
         if (e < e0 || e >= e0 + n_local) continue;
         atomicAdd(&cnt[e], 1);
         atomicOr(&mask[(size_t)e * MW + (r >> 6)], 1ull << (r & 63));
@@ -271,7 +271,6 @@ void moe_launch_ep_final(const MoeDims &d, const MoePlan &plan, const float *rec
 // their step n + 1 partials first).
 // ===========================================================================
 #define EP_WAIT_NS 2000000000ull
-#define EP_ERR_TIMEOUT 0x7300
 
 __device__ __forceinline__ unsigned long long ep_ld_acquire(const unsigned long long *p) {
     unsigned long long v;

@@ -31,7 +31,6 @@
 #define EX_THREADS (32 * (EX_CONSUMERS + 1))
 #define EX_OPND (MOE_TC * OPB_SB)  // operand bytes of one stage (<= 8 vectors)
 #define EX_WAIT_CYCLES (1ll << 31)
-#define EX_ERR_TIMEOUT 0x7100
 
 // gate/up: item = 64 rows of I (gate and up rows), K = H
 #define GU_ROWS 64

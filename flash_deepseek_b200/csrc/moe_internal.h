@@ -69,6 +69,14 @@ static inline cudaError_t moe_launch_pdl(void (*kernel)(KArgs...), dim3 grid, di
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
+// Codes that kernels store in MoePlan::error with atomicExch (when several
+// fire, the last store is the one reported); the host turns them into
+// messages when it next synchronizes.
+#define MOE_DEV_ERR_INDEX 1          // routed expert index out of range
+#define EX_ERR_TIMEOUT 0x7100        // expert GEMV pipeline: an mbarrier wait gave up
+#define PF_ERR_TIMEOUT 0x7200        // prefill GEMM pipeline: an mbarrier wait gave up
+#define EP_ERR_TIMEOUT 0x7300        // peer exchange: a peer's step flag did not arrive
+
 #define MOE_TC 8  // tokens per chunk (four 8-column MMA tiles of 2 tokens x 3 planes)
 
 // ---- launchers (moe_kernels.cu); every one counts its kernel launches ------

@@ -615,7 +615,7 @@ __device__ void build_plan_block(const RouteArgs &a) {
     for (int p = threadIdx.x; p < n_routed; p += blockDim.x) {
         const int t = p / K;
         const int e = __ldcg(a.idx_out + p);
-        if (e < 0 || e >= E) { atomicExch(a.plan.error, 1); continue; }
+        if (e < 0 || e >= E) { atomicExch(a.plan.error, MOE_DEV_ERR_INDEX); continue; }
         atomicAdd(&cnt[e], 1);
         atomicOr(&mask[e], 1ull << t);
     }

@@ -53,7 +53,6 @@
 #define PF_THREADS (32 * (PF_DQ_WARP0 + PF_DQ_WARPS))
 #define PF_WAIT_CYCLES (1ll << 31)
 #define PF_SUSPEND_NS 1000000u    // a waiting thread sleeps up to 1 ms per try (woken when the phase completes)
-#define PF_ERR_TIMEOUT 0x7200
 
 #define LAUNCH_COUNT(p) \
     do {                \
@@ -131,7 +130,7 @@ __global__ void __launch_bounds__(256) k_pf_count(MoeDims d, const int *__restri
     const int p0 = blockIdx.x * PF_PLAN_PAIRS, p1 = min(n, p0 + PF_PLAN_PAIRS);
     for (int p = p0 + threadIdx.x; p < p1; p += blockDim.x) {
         const int e = idx[p];
-        if (e < 0 || e >= d.E) { atomicExch(error, 1); continue; }
+        if (e < 0 || e >= d.E) { atomicExch(error, MOE_DEV_ERR_INDEX); continue; }
         atomicAdd(&h[e], 1);
     }
     __syncthreads();
@@ -868,7 +867,7 @@ __global__ void __launch_bounds__(256) k_pfe_count(MoeDims d, const int *__restr
         const int *m = recv_meta + (size_t)(p / K) * mw;
         if (!m[0]) continue;
         const int e = m[2 + p % K];
-        if (e < 0 || e >= d.E) { atomicExch(error, 1); continue; }
+        if (e < 0 || e >= d.E) { atomicExch(error, MOE_DEV_ERR_INDEX); continue; }
         if (e >= e0 && e < e0 + n_local) atomicAdd(&h[e], 1);
     }
     __syncthreads();
