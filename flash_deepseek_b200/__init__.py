@@ -132,6 +132,11 @@ class MoE:
     def last_weight_bytes(self) -> int:
         return int(self.lib.moe_last_weight_bytes(self.ctx))
 
+    @property
+    def ep_peer_memory(self) -> bool:
+        """True when the expert-parallel exchanges run over NVLink peer memory."""
+        return bool(self.lib.moe_ep_peer_memory(self.ctx))
+
     def record_expert_hits(self, d_hits):
         """While d_hits (device int32 [n_layers]) is set, every device forward
         writes d_hits[layer] = routed experts of this rank hit by that layer;

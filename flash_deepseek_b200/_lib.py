@@ -31,6 +31,7 @@ SIGNATURES = {
     "moe_stream": (_vp, [_vp]),
     "moe_rank": (C.c_int, [_vp]),
     "moe_world_size": (C.c_int, [_vp]),
+    "moe_ep_peer_memory": (C.c_int, [_vp]),
     "moe_load_layer": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, C.c_int, _vp, _vp, _vp, _vp, _vp, C.c_int]),
     "moe_load_layer_packed": (C.c_int, [_vp, C.c_int, _vp, C.c_size_t, _vp, _vp, _vp, _vp, _vp, C.c_int]),
     "moe_init_layer_synthetic": (C.c_int, [_vp, C.c_int, C.c_uint64, C.c_int, C.c_double, C.c_double,

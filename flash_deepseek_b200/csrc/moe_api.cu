@@ -849,6 +849,8 @@ static int record_hits(moe_ctx *c, int layer, bool ran, cudaStream_t s) {
     return MOE_OK;
 }
 
+int moe_ep_peer_memory(const moe_ctx *c) { return c && c->p2p ? 1 : 0; }
+
 int moe_record_expert_hits(moe_ctx *c, int *d_hits) {
     if (!c) return MOE_ERR_ARG;
     drop_graphs(c);

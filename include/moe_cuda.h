@@ -85,6 +85,10 @@ const char *moe_last_error(const moe_ctx *ctx);
 void *moe_stream(moe_ctx *ctx);
 int moe_rank(const moe_ctx *ctx);
 int moe_world_size(const moe_ctx *ctx);
+/* 1 when the expert-parallel exchanges of this context run over NVLink peer
+ * memory (bounded waits), 0 when they run over NCCL send/recv (world_size 1:
+ * 0). */
+int moe_ep_peer_memory(const moe_ctx *ctx);
 
 /* ---------------------------------------------------------------- weights */
 /* Loads one MoE layer from the GGUF tensors of layer L (host pointers):

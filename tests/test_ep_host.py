@@ -129,3 +129,83 @@ def test_ep_decomposition_matches_oracle_layer(oracle):
         out[t] += sh[t]
     err = float(np.max(np.abs(out - full)) / np.max(np.abs(full)))
     assert err < 1e-5, err
+
+
+def _watch_rank(rank, world, port, mode, q):
+    """Three good steps, then rank 1 fails in `mode`: "exit" (dies without a
+    word), "raise" (an exception, handled by leaving) or "late" (arrives
+    after the timeout)."""
+    try:
+        import time
+        from datetime import timedelta
+        from torch.distributed import TCPStore
+        store = TCPStore("127.0.0.1", port, world, rank == 0, timedelta(seconds=30))
+        w = ep.PeerWatch(store, rank, world, timeout=1.0)
+        for step in range(3):
+            w.beat(step)
+            w.wait(step)
+        if rank == 1:
+            if mode == "exit":
+                q.put((rank, "exited", 0.0))
+                q.close()
+                q.join_thread()   # the message is out before the process dies
+                os._exit(0)
+            if mode == "raise":
+                try:
+                    raise RuntimeError("planted failure")
+                except RuntimeError:
+                    w.leave()
+                q.put((rank, "left", 0.0))
+                time.sleep(3)   # keep the store's peer alive while rank 0 checks
+                return
+            time.sleep(2.0)      # late
+            w.beat(3)
+            q.put((rank, "late", 0.0))
+            time.sleep(1)
+            return
+        w.beat(3)
+        t0 = time.monotonic()
+        try:
+            w.wait(3)
+            got = "no error"
+        except ep.PeerLost as e:
+            got = f"lost {e.ranks} left {e.left}"
+        q.put((rank, got, time.monotonic() - t0))
+        time.sleep(0.5)
+    except Exception as e:
+        q.put((rank, "EXC " + repr(e), 0.0))
+
+
+@pytest.mark.parametrize("mode", ["exit", "raise", "late"])
+def test_peer_watch_detects_a_lost_rank(mode):
+    """Host-side failure detection between steps (no GPU): a rank that dies,
+    leaves after an exception, or misses the timeout is reported to the
+    others by PeerWatch.wait before their next launch."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_watch_rank, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in range(2):
+            rank, got, dt = q.get(timeout=120)
+            res[rank] = (got, dt)
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.terminate()
+    got, dt = res[0]
+    if mode == "raise":
+        assert got == "lost [1] left [1]", got
+        assert dt < 0.9, dt      # at once, not after the timeout
+    else:
+        assert got == "lost [1] left []", got
+        assert 0.9 < dt < 10, dt
+
+
+def test_peer_watch_validates_arguments():
+    with pytest.raises(ValueError):
+        ep.PeerWatch(None, 2, 2)
