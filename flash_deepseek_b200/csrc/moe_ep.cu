@@ -228,11 +228,8 @@ void moe_launch_ep_plan(const MoeDims &d, const int *recv_meta, int world, int c
                         const MoePlan &plan, cudaStream_t s, uint64_t *launches) {
     const int MW = (world * cap + T + 63) / 64;
     const size_t smem = sizeof(unsigned long long) * (size_t)(d.E + 1) * MW;
-    static size_t attr = 0;
-    if (smem > 48 * 1024 && smem > attr) {
-        cudaFuncSetAttribute(k_ep_plan, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr = smem;
-    }
+    static size_t attr[MOE_MAX_DEVICES];
+    if (smem > 48 * 1024) moe_smem_limit(k_ep_plan, smem, attr);
     k_ep_plan<<<1, 512, smem, s>>>(d, recv_meta, world, cap, T, e0, n_local, plan);
     LAUNCH_COUNT(launches);
 }

@@ -608,11 +608,8 @@ void moe_launch_gateup(const MoeDims &d, const MoeLayerDev &L, const MoePlan &pl
     if (grid > max_items) grid = max_items;
     if (grid < 1) grid = 1;
     const size_t smem = (size_t)GU_NS * GU_STAGE + 128;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(k_gateup, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr = true;
-    }
+    static size_t attr[MOE_MAX_DEVICES];
+    moe_smem_limit(k_gateup, smem, attr);
     moe_launch_pdl(k_gateup, dim3(grid), dim3(EX_THREADS), smem, s, d, L, plan, xop, act);
     LAUNCH_COUNT(launches);
 }
@@ -626,16 +623,9 @@ void moe_launch_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan
     const int nbp = q6r_nb_pad(d.I / MOE_QK);
     const size_t sm6 = (size_t)DN6_NS * DN6_STAGE + 2 * (size_t)DN_ROWS * 2 * nbp + 128;
     const size_t sm4 = (size_t)DN4_NS * DN4_STAGE + 128;
-    static size_t attr6 = 0;
-    static bool attr4 = false;
-    if (sm6 > attr6) {
-        cudaFuncSetAttribute(k_down<MOE_TYPE_Q6_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm6);
-        attr6 = sm6;
-    }
-    if (!attr4) {
-        cudaFuncSetAttribute(k_down<MOE_TYPE_Q4_K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm4);
-        attr4 = true;
-    }
+    static size_t attr6[MOE_MAX_DEVICES], attr4[MOE_MAX_DEVICES];
+    moe_smem_limit(k_down<MOE_TYPE_Q6_K>, sm6, attr6);
+    moe_smem_limit(k_down<MOE_TYPE_Q4_K>, sm4, attr4);
     if (L.down_type == MOE_TYPE_Q6_K || L.sh_down_type == MOE_TYPE_Q6_K) {
         moe_launch_pdl(k_down<MOE_TYPE_Q6_K>, dim3(grid), dim3(EX_THREADS), sm6, s, d, L, plan, dop, eo);
         LAUNCH_COUNT(launches);

@@ -77,6 +77,23 @@ static inline cudaError_t moe_launch_pdl(void (*kernel)(KArgs...), dim3 grid, di
 #define PF_ERR_TIMEOUT 0x7200        // prefill GEMM pipeline: an mbarrier wait gave up
 #define EP_ERR_TIMEOUT 0x7300        // peer exchange: a peer's step flag did not arrive
 
+// Raises a kernel's dynamic shared-memory limit on the current device when
+// `bytes` exceeds what was set there before.  The attribute belongs to the
+// device, so a process that drives contexts on several GPUs sets it on each;
+// `done` is the kernel's record per device ordinal.
+#define MOE_MAX_DEVICES 64
+template <typename F>
+inline void moe_smem_limit(F *kernel, size_t bytes, size_t (&done)[MOE_MAX_DEVICES]) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MOE_MAX_DEVICES) {
+        cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+        return;
+    }
+    if (bytes <= done[dev]) return;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) == cudaSuccess)
+        done[dev] = bytes;
+}
+
 #define MOE_TC 8  // tokens per chunk (four 8-column MMA tiles of 2 tokens x 3 planes)
 
 // ---- launchers (moe_kernels.cu); every one counts its kernel launches ------

@@ -504,11 +504,8 @@ void moe_launch_router_logits(const float *Wr, const float *x, int T, int H, int
     }
     dim3 grid((E + 31) / 32, n_split, (T + 63) / 64);
     const size_t smem = sizeof(float) * (32 * RL_WPAD + RL_KS * 64);
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(k_router_logits, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr = true;
-    }
+    static size_t attr[MOE_MAX_DEVICES];
+    moe_smem_limit(k_router_logits, smem, attr);
     moe_launch_pdl(k_router_logits, grid, dim3(256), smem, s, Wr, x, T, H, E, part, logits, counters);
     LAUNCH_COUNT(launches);
 }

@@ -764,11 +764,8 @@ void moe_launch_prefill_router(const MoeDims &d, const float *Wr, MoePrefillWs &
     k_pf_split<<<(unsigned)((nx / 4 + 255) / 256 < 148 * 16 ? (nx / 4 + 255) / 256 : 148 * 16), 256, 0, s>>>(
         x, nx, 1.0f, ws.xh, ws.xl);
     const size_t smem = 1024 + (size_t)RT_NS * 4 * PF_ATOM;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(k_pf_router, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr = true;
-    }
+    static size_t attr[MOE_MAX_DEVICES];
+    moe_smem_limit(k_pf_router, smem, attr);
     // K slices: a power of two dividing H / 64, up to 16, until the grid covers the SMs
     const int tiles = ((d.E + 127) / 128) * ((T + 127) / 128);
     int nsplit = 1;
@@ -1003,11 +1000,8 @@ template <int MODE>
 static void pf_launch(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const CUtensorMap &tmB,
                       __half *act, float *eo, int max_tiles, int row_groups, cudaStream_t s, uint64_t *launches) {
     const size_t smem = pf_smem(MODE, q6r_nb_pad(d.I / MOE_QK));
-    static size_t attr = 0;
-    if (smem > attr) {
-        cudaFuncSetAttribute(k_prefill_gemm<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        attr = smem;
-    }
+    static size_t attr[MOE_MAX_DEVICES];
+    moe_smem_limit(k_prefill_gemm<MODE>, smem, attr);
     k_prefill_gemm<MODE><<<dim3(row_groups, max_tiles), PF_THREADS, smem, s>>>(d, L, plan, tmB, act, eo);
     LAUNCH_COUNT(launches);
 }
