@@ -1,7 +1,9 @@
 // moe_api.cu -- context, weight residency and the C ABI of libmoe_cuda.so
-// (include/moe_cuda.h).  One context per GPU; expert-parallel contexts talk
-// over NCCL (dispatch / combine) with fixed-capacity buffers so that a forward
-// step needs no host synchronisation.
+// (include/moe_cuda.h).  One context per GPU; expert-parallel contexts
+// exchange token rows and partial sums (dispatch / combine) through
+// fixed-capacity mailboxes in NVLink peer memory, or over NCCL send/recv when
+// the peers cannot be mapped, so that a decode step needs no host
+// synchronisation.
 #include <dlfcn.h>
 #include <stdarg.h>
 #include <stdlib.h>
@@ -140,6 +142,20 @@ static int fail(moe_ctx *c, int code, const char *fmt, ...) {
         ncclResult_t r_ = (call);                                                                    \
         if (r_ != ncclSuccess) return fail(c, MOE_ERR_NCCL, "%s: %s", #call, moe_nccl()->GetErrorString(r_)); \
     } while (0)
+
+// Makes the context's device current for one entry-point call and gives the
+// caller back its own current device on return (nothing happens when they
+// are the same device).
+struct DeviceScope {
+    int prev = -1;
+    explicit DeviceScope(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess || prev == dev) prev = -1;
+        else cudaSetDevice(dev);
+    }
+    ~DeviceScope() {
+        if (prev >= 0) cudaSetDevice(prev);
+    }
+};
 
 template <typename T>
 static cudaError_t dmalloc(T **p, size_t n) {
@@ -463,6 +479,7 @@ int moe_load_layer(moe_ctx *c, int layer, const void *gate_exps, const void *up_
                    int down_type, const float *router_w, const float *bias, const void *sh_gate, const void *sh_up,
                    const void *sh_down, int sh_down_type) {
     if (!c) return MOE_ERR_ARG;
+    DeviceScope ds(c->device);
     if (!gate_exps || !up_exps || !down_exps || !router_w || !sh_gate || !sh_up || !sh_down)
         return fail(c, MOE_ERR_ARG, "moe_load_layer: null weight pointer");
     int rc = layer_alloc(c, layer, down_type, sh_down_type);
@@ -499,6 +516,7 @@ int moe_load_layer_packed(moe_ctx *c, int layer, const void *blob, size_t expert
                           const float *bias, const void *sh_gate, const void *sh_up, const void *sh_down,
                           int sh_down_type) {
     if (!c || !blob) return MOE_ERR_ARG;
+    DeviceScope ds(c->device);
     const int H = c->d.H, I = c->d.I;
     const size_t gb = row_bytes(MOE_TYPE_Q4_K, H) * I;
     int down_type;
@@ -534,6 +552,7 @@ int moe_load_layer_packed(moe_ctx *c, int layer, const void *blob, size_t expert
 int moe_init_layer_synthetic(moe_ctx *c, int layer, uint64_t seed, int down_type, double w_sigma,
                              double router_sigma, double bias_sigma) {
     if (!c) return MOE_ERR_ARG;
+    DeviceScope ds(c->device);
     int rc = layer_alloc(c, layer, down_type, down_type);
     if (rc) return rc;
     MoeLayerDev &L = c->layers[layer];
@@ -570,6 +589,7 @@ int moe_init_layer_synthetic(moe_ctx *c, int layer, uint64_t seed, int down_type
 
 int moe_add_router_bias(moe_ctx *c, int layer, const float *extra) {
     if (!c || !extra) return MOE_ERR_ARG;
+    DeviceScope ds(c->device);
     if (layer < 0 || layer >= (int)c->layers.size() || !c->layers[layer].bias)
         return fail(c, MOE_ERR_STATE, "layer %d not loaded", layer);
     std::vector<float> b(c->d.E);
@@ -584,7 +604,7 @@ int moe_set_logit_bias(moe_ctx *c, int layer, const float *lb) {
     drop_graphs(c);  // the kernels take this layer's pointers by value
     if (layer < 0 || layer >= (int)c->layers.size() || !c->layers[layer].router)
         return fail(c, MOE_ERR_STATE, "layer %d not loaded", layer);
-    CK(cudaSetDevice(c->device));
+    DeviceScope ds(c->device);
     MoeLayerDev &L = c->layers[layer];
     if (!lb) {
         cudaFree(L.logit_bias);
@@ -600,7 +620,7 @@ int moe_set_norm_weight(moe_ctx *c, int layer, const float *w) {
     if (!c || !w) return MOE_ERR_ARG;
     drop_graphs(c);  // the kernels take this layer's pointers by value
     if (layer < 0 || layer >= (int)c->layers.size()) return fail(c, MOE_ERR_ARG, "layer %d out of range", layer);
-    CK(cudaSetDevice(c->device));
+    DeviceScope ds(c->device);
     MoeLayerDev &L = c->layers[layer];
     if (!L.norm) CK(cudaMalloc((void **)&L.norm, sizeof(float) * c->d.H));
     CK(cudaMemcpy(L.norm, w, sizeof(float) * c->d.H, cudaMemcpyHostToDevice));
@@ -624,7 +644,7 @@ int moe_read_expert(moe_ctx *c, int layer, int expert, void *dst, size_t dst_siz
     const int ty = expert == c->d.E ? L.sh_down_type : L.down_type;
     const size_t db = row_bytes(ty, c->d.I) * c->d.H;
     if (dst_size < 2 * L.gate_bytes + db) return fail(c, MOE_ERR_ARG, "moe_read_expert: buffer too small");
-    CK(cudaSetDevice(c->device));
+    DeviceScope ds(c->device);
     const uint8_t *src = L.experts + (size_t)j * L.expert_stride;
     // undo the load-time repacks in a device copy: Q4_K qs transpose (its
     // own inverse) of gate, up and a Q4_K down; Q6_K planes -> GGUF blocks
@@ -861,6 +881,7 @@ int moe_record_expert_hits(moe_ctx *c, int *d_hits) {
 int moe_forward_device(moe_ctx *c, int layer, const float *d_h, int T, float *d_out, int *d_idx, float *d_w,
                        void *stream) {
     if (!c) return MOE_ERR_ARG;
+    DeviceScope ds(c->device);
     if (T > 0 && (!d_h || !d_out)) return fail(c, MOE_ERR_ARG, "moe_forward_device: null input or output");
     int rc = check_layer(c, layer);
     if (rc) return rc;
@@ -898,7 +919,7 @@ int moe_forward(moe_ctx *c, int layer, const float *h, int T, float *out, int *i
     if (!c) return MOE_ERR_ARG;
     if (T > 0 && (!h || !out)) return fail(c, MOE_ERR_ARG, "moe_forward: null input or output");
     if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
-    CK(cudaSetDevice(c->device));
+    DeviceScope ds(c->device);
     const size_t n = (size_t)T * c->d.H;
     if (n) CK(cudaMemcpyAsync(c->d_in, h, n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
     int rc = moe_forward_device(c, layer, c->d_in, T, c->d_out, nullptr, nullptr, nullptr);
@@ -913,6 +934,7 @@ int moe_forward(moe_ctx *c, int layer, const float *h, int T, float *out, int *i
 int moe_experts_forward_device(moe_ctx *c, int layer, const float *d_h, int T, const int *d_idx, const float *d_w,
                                int K, float *d_out, void *stream) {
     if (!c) return MOE_ERR_ARG;
+    DeviceScope ds(c->device);
     if (T > 0 && (!d_h || !d_idx || !d_w || !d_out))
         return fail(c, MOE_ERR_ARG, "moe_experts_forward_device: null pointer");
     int rc = check_layer(c, layer);
@@ -934,7 +956,7 @@ int moe_experts_forward(moe_ctx *c, int layer, const float *h, int T, const int 
     if (K != c->d.K) return fail(c, MOE_ERR_ARG, "K %d differs from the context's top_k %d", K, c->d.K);
     for (int i = 0; i < T * K; i++)
         if (idx[i] < 0 || idx[i] >= c->d.E) return fail(c, MOE_ERR_ARG, "expert index %d out of range", idx[i]);
-    CK(cudaSetDevice(c->device));
+    DeviceScope ds(c->device);
     const size_t n = (size_t)T * c->d.H;
     CK(cudaMemcpyAsync(c->d_in, h, n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
     CK(cudaMemcpyAsync(c->idx_given, idx, sizeof(int) * T * K, cudaMemcpyHostToDevice, c->stream));
@@ -952,7 +974,7 @@ int moe_shared_forward(moe_ctx *c, int layer, const float *h, int T, float *sd) 
     if (rc) return rc;
     if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
     if (T == 0) return MOE_OK;
-    CK(cudaSetDevice(c->device));
+    DeviceScope ds(c->device);
     const size_t n = (size_t)T * c->d.H;
     CK(cudaMemcpyAsync(c->d_in, h, n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
     // shared only: routed slots are empty (routing given as "none")
@@ -967,7 +989,7 @@ int moe_route(moe_ctx *c, const float *logits, const float *bias, int T, int *id
     if (T > 0 && (!logits || !idx || !w)) return fail(c, MOE_ERR_ARG, "moe_route: null pointer");
     if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
     if (T == 0) return MOE_OK;
-    CK(cudaSetDevice(c->device));
+    DeviceScope ds(c->device);
     const int E = c->d.E, K = c->d.K;
     float *d_lg = c->part, *d_b = nullptr;
     CK(cudaMemcpyAsync(d_lg, logits, sizeof(float) * T * E, cudaMemcpyHostToDevice, c->stream));
@@ -1054,7 +1076,7 @@ int moe_prefill_device(moe_ctx *c, int layer, const float *d_h, int T, float *d_
     if (c->d.H % 256 || c->d.I % 128 || c->d.K > 63 || c->d.E > 1024)
         return fail(c, MOE_ERR_ARG,
                     "moe_prefill needs hidden %% 256 == 0, intermediate %% 128 == 0, top_k <= 63, n_experts <= 1024");
-    CK(cudaSetDevice(c->device));
+    DeviceScope ds(c->device);
     cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
     if (c->world > 1) return run_prefill_ep(c, layer, d_h, T, d_out, d_idx, d_w, s);
     if (moe_prefill_alloc(c->pf, c->d, T))
@@ -1076,7 +1098,7 @@ int moe_prefill(moe_ctx *c, int layer, const float *h, int T, float *out, int *i
     if (!c) return MOE_ERR_ARG;
     if (T < 0 || (T > 0 && (!h || !out)) || (T == 0 && c->world == 1))
         return fail(c, MOE_ERR_ARG, "moe_prefill: need n_tokens >= 1 and buffers (0 only in expert parallelism)");
-    CK(cudaSetDevice(c->device));
+    DeviceScope ds(c->device);
     if (T == 0) {  // a rank without tokens still takes part in the exchanges
         const int rc = moe_prefill_device(c, layer, nullptr, 0, nullptr, nullptr, nullptr, nullptr);
         CK(cudaStreamSynchronize(c->stream));
@@ -1115,6 +1137,7 @@ int moe_prefill(moe_ctx *c, int layer, const float *h, int T, float *out, int *i
 
 int moe_forward_stack_device(moe_ctx *c, int first, int n_layers, float *d_hidden, int T, void *stream) {
     if (!c) return MOE_ERR_ARG;
+    DeviceScope ds(c->device);
     if (T > 0 && !d_hidden) return fail(c, MOE_ERR_ARG, "moe_forward_stack_device: null hidden");
     if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
     cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
@@ -1136,7 +1159,7 @@ int moe_forward_stack(moe_ctx *c, int first, int n_layers, float *hidden, int T)
     if (!c) return MOE_ERR_ARG;
     if (T > 0 && !hidden) return fail(c, MOE_ERR_ARG, "moe_forward_stack: null hidden");
     if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
-    CK(cudaSetDevice(c->device));
+    DeviceScope ds(c->device);
     const size_t n = (size_t)T * c->d.H;
     if (n) CK(cudaMemcpyAsync(c->d_in, hidden, n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
     int rc = moe_forward_stack_device(c, first, n_layers, c->d_in, T, nullptr);
@@ -1148,7 +1171,7 @@ int moe_forward_stack(moe_ctx *c, int first, int n_layers, float *hidden, int T)
 int moe_set_timing(moe_ctx *c, int enable) {
     if (!c || enable < 0) return MOE_ERR_ARG;
     drop_graphs(c);
-    CK(cudaSetDevice(c->device));
+    DeviceScope ds(c->device);
     if (enable > 0 && enable != c->ring) {
         for (cudaEvent_t e : c->ev) cudaEventDestroy(e);
         c->ev.assign((size_t)enable * (MOE_N_PHASES + 1), nullptr);
