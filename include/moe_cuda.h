@@ -73,10 +73,13 @@ typedef struct moe_ctx moe_ctx;
  * to the other ranks by the caller). */
 int moe_get_unique_id(void *out_id128);
 
-/* Creates a context on CUDA device `device`.  world_size == 1 needs no id.
- * For world_size > 1 (expert parallel, one process per GPU) routed expert e
- * lives on rank e / (n_experts / world_size); router and shared expert are
- * replicated.  Returns NULL on error (message on stderr). */
+/* Creates a context on CUDA device `device` (left current on return).
+ * world_size == 1 needs no id.  For world_size > 1 (expert parallel, one
+ * process per GPU) routed expert e lives on rank e / (n_experts /
+ * world_size); router and shared expert are replicated.  Returns NULL on
+ * error (message on stderr).  Every later call on the context runs on its
+ * device and gives the caller's current device back on return, so several
+ * contexts on different GPUs can share a host thread. */
 moe_ctx *moe_create(const moe_config *cfg, int device, int rank, int world_size,
                     const void *unique_id128);
 void moe_destroy(moe_ctx *ctx);
