@@ -873,6 +873,7 @@ int moe_ep_peer_memory(const moe_ctx *c) { return c && c->p2p ? 1 : 0; }
 
 int moe_record_expert_hits(moe_ctx *c, int *d_hits) {
     if (!c) return MOE_ERR_ARG;
+    DeviceScope ds(c->device);
     drop_graphs(c);
     c->hits = d_hits;
     return MOE_OK;
@@ -1187,6 +1188,7 @@ int moe_set_timing(moe_ctx *c, int enable) {
 
 int moe_get_timing_at(moe_ctx *c, int back, float *ms, int n) {
     if (!c || !ms) return MOE_ERR_ARG;
+    DeviceScope ds(c->device);
     if (!c->timing || c->ring == 0) return fail(c, MOE_ERR_STATE, "timing is not enabled");
     if (back < 0 || back >= c->ring_used) return fail(c, MOE_ERR_ARG, "step %d is not in the timing ring", back);
     const int slot = ((c->ring_pos - back) % c->ring + c->ring) % c->ring;
@@ -1210,6 +1212,7 @@ int moe_get_timing(moe_ctx *c, float *ms, int n) { return moe_get_timing_at(c, 0
 uint64_t moe_last_weight_bytes(const moe_ctx *cc) {
     moe_ctx *c = const_cast<moe_ctx *>(cc);
     if (!c || c->last_layer < 0) return 0;
+    DeviceScope ds(c->device);
     if (cudaStreamSynchronize(c->stream) != cudaSuccess) return 0;
     int counts[4] = {0, 0, 0, 0};
     if (cudaMemcpy(counts, c->plan.counts, sizeof(counts), cudaMemcpyDeviceToHost) != cudaSuccess) return 0;
