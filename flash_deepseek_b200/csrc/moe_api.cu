@@ -10,8 +10,10 @@
 #include <stdio.h>
 #include <string.h>
 
-#include <string>
 #include <array>
+#include <chrono>
+#include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/moe_cuda.h"
@@ -94,6 +96,7 @@ struct moe_ctx {
     size_t mb_x = 0, mb_meta = 0, mb_y = 0;
     int *ep_done = nullptr;  // [2] block counters of the two signalling kernels
     int *hits = nullptr;     // moe_record_expert_hits target, or nullptr
+    bool comm_aborted = false;  // a host wait gave up on an NCCL exchange
     unsigned long long ep_seq = 0;
     std::string err;
     bool timing = false;
@@ -732,6 +735,7 @@ static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_i
     const MoeDims &d = c->d;
     const int N = c->world, cap = c->max_tok, R = N * cap, mw = 2 + 2 * d.K;
     const int mode = idx_in ? 1 : 0;
+    if (c->comm_aborted) return fail(c, MOE_ERR_STATE, "an exchange failed and the communicator was aborted");
     mark_begin(c);
     mark(c, MOE_PHASE_ROUTER, s);
     if (mode == 0 && T > 0)
@@ -901,8 +905,49 @@ int moe_forward_device(moe_ctx *c, int layer, const float *d_h, int T, float *d_
     return record_hits(c, layer, true, s);
 }
 
+// Host wait for stream s.  A step that ran NCCL (the expert-parallel
+// prefill, or the decode exchange when the peers could not be mapped) has no
+// bounded wait of its own, so the host polls the communicator's
+// asynchronous error while it waits and gives up after MOE_EP_TIMEOUT_S
+// seconds (default 120): the communicator is then aborted, which ends its
+// kernels, and the context answers every later call with an error.
+static int stream_wait(moe_ctx *c, cudaStream_t s, bool nccl_in_step) {
+    if (!nccl_in_step || !c->comm) {
+        CK(cudaStreamSynchronize(s));
+        return MOE_OK;
+    }
+    const char *env = getenv("MOE_EP_TIMEOUT_S");
+    const double limit = env && atof(env) > 0 ? atof(env) : 120.0;
+    const auto t0 = std::chrono::steady_clock::now();
+    for (unsigned it = 0;; it++) {
+        const cudaError_t q = cudaStreamQuery(s);
+        if (q == cudaSuccess) return MOE_OK;
+        if (q != cudaErrorNotReady) return fail(c, MOE_ERR_CUDA, "stream wait: %s", cudaGetErrorString(q));
+        ncclResult_t ae = ncclSuccess;
+        const bool nccl_err = moe_nccl()->CommGetAsyncError(c->comm, &ae) == ncclSuccess && ae != ncclSuccess &&
+                              ae != ncclInProgress;
+        const double waited = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        if (nccl_err || waited > limit) {
+            moe_nccl()->CommAbort(c->comm);
+            c->comm = nullptr;
+            c->comm_aborted = true;
+            if (nccl_err)
+                return fail(c, MOE_ERR_NCCL, "NCCL error during the exchange: %s; communicator aborted",
+                            moe_nccl()->GetErrorString(ae));
+            return fail(c, MOE_ERR_NCCL,
+                        "exchange did not finish within %.0f s (a peer rank stopped calling); communicator aborted",
+                        limit);
+        }
+        if (it < 1000) std::this_thread::yield();
+        else std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
 static int finish_sync(moe_ctx *c) {
-    CK(cudaStreamSynchronize(c->stream));
+    {
+        const int rc = stream_wait(c, c->stream, c->world > 1 && !c->p2p);
+        if (rc) return rc;
+    }
     int errflag = 0;
     CK(cudaMemcpy(&errflag, c->plan.error, sizeof(int), cudaMemcpyDeviceToHost));
     if (errflag) {
@@ -1019,6 +1064,7 @@ static int run_prefill_ep(moe_ctx *c, int layer, const float *d_h, int T, float 
     MoeLayerDev &L = c->layers[layer];
     const int N = c->world, mw = 2 + 2 * d.K;
     if (N > 64) return fail(c, MOE_ERR_ARG, "moe_prefill: world size above 64");
+    if (c->comm_aborted) return fail(c, MOE_ERR_STATE, "an exchange failed and the communicator was aborted");
     MoePrefillWs &ws = c->pf;
     if (!ws.tcount && cudaMalloc((void **)&ws.tcount, sizeof(int) * 66) != cudaSuccess)
         return fail(c, MOE_ERR_CUDA, "prefill token-count buffer");
@@ -1032,7 +1078,10 @@ static int run_prefill_ep(moe_ctx *c, int layer, const float *d_h, int T, float 
     NK(moe_nccl()->GroupEnd());
     int counts[64];
     CK(cudaMemcpyAsync(counts, ws.tcount + 2, sizeof(int) * N, cudaMemcpyDeviceToHost, s));
-    CK(cudaStreamSynchronize(s));
+    {
+        const int rc = stream_wait(c, s, true);
+        if (rc) return rc;
+    }
     int ecap = 1;
     for (int p = 0; p < N; p++) ecap = counts[p] > ecap ? counts[p] : ecap;
     if (moe_prefill_alloc(ws, d, T > 0 ? T : 1, N, ecap))
@@ -1102,8 +1151,8 @@ int moe_prefill(moe_ctx *c, int layer, const float *h, int T, float *out, int *i
     DeviceScope ds(c->device);
     if (T == 0) {  // a rank without tokens still takes part in the exchanges
         const int rc = moe_prefill_device(c, layer, nullptr, 0, nullptr, nullptr, nullptr, nullptr);
-        CK(cudaStreamSynchronize(c->stream));
-        return rc;
+        const int wrc = stream_wait(c, c->stream, c->world > 1);
+        return rc ? rc : wrc;
     }
     const size_t n = (size_t)T * c->d.H;
     float *dh = nullptr, *dout = nullptr;
@@ -1121,10 +1170,13 @@ int moe_prefill(moe_ctx *c, int layer, const float *h, int T, float *out, int *i
     if (!rc && idx_out)
         cudaMemcpyAsync(idx_out, c->pf.idx, sizeof(int) * T * c->d.K, cudaMemcpyDeviceToHost, c->stream);
     if (!rc && w_out) cudaMemcpyAsync(w_out, c->pf.w, sizeof(float) * T * c->d.K, cudaMemcpyDeviceToHost, c->stream);
-    cudaStreamSynchronize(c->stream);
-    cudaFree(dh);
-    cudaFree(dout);
+    const int wrc = stream_wait(c, c->stream, c->world > 1);
+    if (wrc == MOE_OK) {  // after an abort the buffers may still be in use
+        cudaFree(dh);
+        cudaFree(dout);
+    }
     if (rc) return rc;
+    if (wrc) return wrc;
     int errflag = 0;
     CK(cudaMemcpy(&errflag, c->pf.plan.error, sizeof(int), cudaMemcpyDeviceToHost));
     if (errflag) {
