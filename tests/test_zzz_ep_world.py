@@ -8,7 +8,6 @@ from test_gpu_ep import _gpu_count, check_ranks, run_ranks
 from test_gpu_moe import small_cfg
 
 
-
 @pytest.mark.gpu
 @pytest.mark.parametrize("world", [4, 8])
 def test_ep_world_matches_oracle(cuda_lib, oracle, world):
