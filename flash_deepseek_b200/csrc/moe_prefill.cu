@@ -6,19 +6,21 @@
 // the weights are dequantized once per tile into fp16 tiles that feed
 // tcgen05.mma, with the fp32 accumulator in tensor memory:
 //   plan     counting sort of the (token, slot) pairs by expert, tiles of
-//            <= 256 pairs per expert
+//            <= 128 pairs per expert
 //   gather   fp16 copy of each pair's token row, pairs grouped by expert
-//   gemm1    gate/up rows (64 + 64 per tile) x <= 256 pairs, SwiGLU in the
-//            epilogue (infer.m:378-383), act in fp16
-//   gemm2    down rows (128 per tile) x <= 256 pairs, fp32 expert outputs
+//   gemm1    gate/up rows (2 blocks of 64 + 64 per CTA) x <= 128 pairs,
+//            SwiGLU in the epilogue (infer.m:378-383), act in fp16
+//   gemm2    down rows (2 blocks of 128 per CTA) x <= 128 pairs, fp32
+//            expert outputs
 //   combine  slot order, then the shared expert (infer.m:1915-1922)
 // Differences from the reference's fp32 dot: weights and activations are
 // rounded to fp16 (11-bit significands) before the fp32-accumulated product.
 //
 // GEMM CTA (one per SM): warp 0 streams the raw Q4_K / Q6_K tiles, one
 // super-block per stage; warp 2 streams the pairs' 64-column activation
-// slices (TMA, 128-byte swizzle) into a ring of 16 KB or 32 KB stages; warp
-// 1 owns tensor memory and issues the MMAs from one thread.  16 warps
+// slices (TMA, 128-byte swizzle) into a ring of 16 KB stages; warp 1 owns
+// tensor memory and runs the MMA loop, one elected lane issuing each MMA
+// (both row blocks share every activation stage).  16 warps
 // dequantize: warp (q, g) writes atom g of every super-block for tensor-
 // memory lanes 32q .. 32q + 31 straight into tensor memory (tcgen05.st), so
 // the A operand never touches shared memory, and the MMA reads A from tensor
