@@ -1,7 +1,10 @@
 // moe_ep.cu -- expert-parallel dispatch / combine kernels (one process per GPU,
 // experts sharded n_experts / world per rank, router and shared expert
-// replicated).  The all-to-all itself is NCCL send/recv with fixed-capacity
-// buffers (moe_api.cu), so a step needs no host synchronisation.
+// replicated).  The exchange runs inside the kernels that produce the data,
+// as stores into the peers' mailboxes in NVLink peer memory (second half of
+// this file), or, when the peers cannot be mapped, as NCCL send/recv between
+// fixed-capacity buffers (moe_api.cu); either way a step needs no host
+// synchronisation.
 //
 // Row space of the expert kernels on rank r (world N, capacity cap = max
 // tokens per rank):

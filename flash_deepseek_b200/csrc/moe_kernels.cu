@@ -1,13 +1,15 @@
 // moe_kernels.cu -- device kernels of the DeepSeek-V3/R1 MoE block for B200.
 //
 //   router logits   fp32 [T x H] x [H x E], split over H into partial sums
+//                   (one CTA per expert over the whole row for <= 4 tokens)
 //   route + plan    sigmoid, grouped top-k (infer.m:920-991), dispatch plan,
 //                   activation operand of the gate/up GEMV
-//   gate/up         grouped Q4_K GEMV with SwiGLU epilogue (infer.m:1564-1568)
 //   prep_down       activation operand of the down GEMV
-//   down            grouped Q6_K / Q4_K GEMV (infer.m:1570, 1611)
 //   combine         sum_k w_k eo_k in slot order + shared (infer.m:1915-1922)
+//   rmsnorm         the stack's per-layer norm (infer.m:369-374)
 //   codec / synth   dequant twins of quant.c, generator + quantizer, repack
+// The expert GEMVs themselves (gate/up with the SwiGLU epilogue, down) are in
+// moe_experts.cu.
 #include <math.h>
 #include <stdio.h>
 
