@@ -15,6 +15,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "liboracle.so")
 REF_PATH = os.path.join(HERE, "_ref", "libref_moe.so")
+REF_GGUF_PATH = os.path.join(HERE, "_ref", "libref_gguf.so")
 
 TYPE_Q4_K = 12
 TYPE_Q6_K = 14
@@ -108,6 +109,33 @@ def ref():
                                         _f32p, C.c_void_p, C.c_void_p, C.c_int]
         _ref = R
     return _ref
+
+
+def ref_gguf_available() -> bool:
+    return os.path.exists(REF_GGUF_PATH)
+
+
+def ref_gguf_tensor(path: str, name: str):
+    """(dims, ggml type, bytes) of tensor `name` in the GGUF file at `path`,
+    read by the reference's own gguf.c (gguf_load_manifest / gguf_find /
+    gguf_tensor_pread, gguf.h:168-192); None if the tensor is absent."""
+    R = C.CDLL(REF_GGUF_PATH)
+    R.ref_gguf_tensor.restype = C.c_int
+    R.ref_gguf_tensor.argtypes = [C.c_char_p, C.c_char_p, C.POINTER(C.c_uint64), C.POINTER(C.c_uint32),
+                                  C.POINTER(C.c_int), C.POINTER(C.c_uint64), C.c_void_p, C.c_uint64]
+    dims = (C.c_uint64 * 4)()
+    nd, ty, nb = C.c_uint32(), C.c_int(), C.c_uint64()
+    rc = R.ref_gguf_tensor(path.encode(), name.encode(), dims, C.byref(nd), C.byref(ty), C.byref(nb), None, 0)
+    if rc == -2:
+        return None
+    if rc != 0:
+        raise RuntimeError(f"gguf.c could not read {path} ({rc})")
+    buf = np.empty(nb.value, np.uint8)
+    rc = R.ref_gguf_tensor(path.encode(), name.encode(), dims, C.byref(nd), C.byref(ty), C.byref(nb),
+                           buf.ctypes.data, buf.size)
+    if rc != 0:
+        raise RuntimeError(f"gguf.c could not read {name} ({rc})")
+    return [int(dims[i]) for i in range(nd.value)], ty.value, buf
 
 
 def _ptr(a):
