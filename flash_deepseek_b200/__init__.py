@@ -222,6 +222,12 @@ class MoE:
         self._check(self.lib.moe_forward_device(self.ctx, layer, _ptr(d_h), n_tokens, _ptr(d_out), _ptr(d_idx),
                                                 _ptr(d_w), _ptr(stream)), "moe_forward_device")
 
+    def check_error(self):
+        """Waits for the context stream; raises MoeError if a kernel recorded
+        an error (timed-out bounded wait, bad routing index) since the last
+        check."""
+        self._check(self.lib.moe_check_error(self.ctx), "moe_check_error")
+
     def experts_forward(self, layer: int, h_post, exp_idx, exp_w):
         """Routed experts with the routing given (metal_moe_forward)."""
         h = _f32(h_post).reshape(-1, self.cfg.hidden)

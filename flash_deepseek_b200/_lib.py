@@ -43,6 +43,7 @@ SIGNATURES = {
     "moe_expert_bytes": (C.c_size_t, [_vp, C.c_int]),
     "moe_forward": (C.c_int, [_vp, C.c_int, _vp, C.c_int, _vp, _vp, _vp]),
     "moe_forward_device": (C.c_int, [_vp, C.c_int, _vp, C.c_int, _vp, _vp, _vp, _vp]),
+    "moe_check_error": (C.c_int, [_vp]),
     "moe_experts_forward": (C.c_int, [_vp, C.c_int, _vp, C.c_int, _vp, _vp, C.c_int, _vp]),
     "moe_experts_forward_device": (C.c_int, [_vp, C.c_int, _vp, C.c_int, _vp, _vp, C.c_int, _vp, _vp]),
     "moe_shared_forward": (C.c_int, [_vp, C.c_int, _vp, C.c_int, _vp]),

@@ -11,6 +11,7 @@
 #include <string.h>
 
 #include <array>
+#include <initializer_list>
 #include <chrono>
 #include <string>
 #include <thread>
@@ -20,6 +21,7 @@
 #include "moe_common.cuh"
 #include "moe_internal.h"
 #include "moe_nccl.h"
+#include "moe_wait.h"
 
 const MoeNccl *moe_nccl() {
     static MoeNccl api;
@@ -97,6 +99,7 @@ struct moe_ctx {
     int *ep_done = nullptr;  // [2] block counters of the two signalling kernels
     int *hits = nullptr;     // moe_record_expert_hits target, or nullptr
     bool comm_aborted = false;  // a host wait gave up on an NCCL exchange
+    bool ep_failed = false;     // a peer-exchange wait gave up: the ranks are out of step
     unsigned long long ep_seq = 0;
     std::string err;
     bool timing = false;
@@ -736,6 +739,8 @@ static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_i
     const int N = c->world, cap = c->max_tok, R = N * cap, mw = 2 + 2 * d.K;
     const int mode = idx_in ? 1 : 0;
     if (c->comm_aborted) return fail(c, MOE_ERR_STATE, "an exchange failed and the communicator was aborted");
+    if (c->ep_failed)
+        return fail(c, MOE_ERR_STATE, "a peer exchange timed out earlier; the ranks are out of step (recreate the context)");
     mark_begin(c);
     mark(c, MOE_PHASE_ROUTER, s);
     if (mode == 0 && T > 0)
@@ -918,47 +923,98 @@ static int stream_wait(moe_ctx *c, cudaStream_t s, bool nccl_in_step) {
     }
     const char *env = getenv("MOE_EP_TIMEOUT_S");
     const double limit = env && atof(env) > 0 ? atof(env) : 120.0;
-    const auto t0 = std::chrono::steady_clock::now();
-    for (unsigned it = 0;; it++) {
-        const cudaError_t q = cudaStreamQuery(s);
-        if (q == cudaSuccess) return MOE_OK;
-        if (q != cudaErrorNotReady) return fail(c, MOE_ERR_CUDA, "stream wait: %s", cudaGetErrorString(q));
-        ncclResult_t ae = ncclSuccess;
-        const bool nccl_err = moe_nccl()->CommGetAsyncError(c->comm, &ae) == ncclSuccess && ae != ncclSuccess &&
-                              ae != ncclInProgress;
-        const double waited = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
-        if (nccl_err || waited > limit) {
+    cudaError_t qerr = cudaSuccess;
+    ncclResult_t ae = ncclSuccess;
+    const MoeWaitOutcome o = moe_wait_poll(
+        [&]() {
+            qerr = cudaStreamQuery(s);
+            return qerr == cudaSuccess ? 0 : qerr == cudaErrorNotReady ? 1 : 2;
+        },
+        [&]() {
+            return moe_nccl()->CommGetAsyncError(c->comm, &ae) == ncclSuccess && ae != ncclSuccess &&
+                   ae != ncclInProgress;
+        },
+        [&]() {
             moe_nccl()->CommAbort(c->comm);
             c->comm = nullptr;
             c->comm_aborted = true;
-            if (nccl_err)
-                return fail(c, MOE_ERR_NCCL, "NCCL error during the exchange: %s; communicator aborted",
-                            moe_nccl()->GetErrorString(ae));
+        },
+        limit);
+    switch (o) {
+        case MOE_WAIT_DONE: return MOE_OK;
+        case MOE_WAIT_STREAM_ERROR: return fail(c, MOE_ERR_CUDA, "stream wait: %s", cudaGetErrorString(qerr));
+        case MOE_WAIT_NCCL_ERROR:
+            return fail(c, MOE_ERR_NCCL, "NCCL error during the exchange: %s; communicator aborted",
+                        moe_nccl()->GetErrorString(ae));
+        default:
             return fail(c, MOE_ERR_NCCL,
                         "exchange did not finish within %.0f s (a peer rank stopped calling); communicator aborted",
                         limit);
-        }
-        if (it < 1000) std::this_thread::yield();
-        else std::this_thread::sleep_for(std::chrono::microseconds(50));
     }
+}
+
+// Reads and clears the device error words that the kernels set (decode plan
+// and prefill plan) once the context stream has finished.  A peer-exchange
+// timeout leaves the ranks out of step (the step numbers have advanced on
+// this rank), so it also marks the context: every later expert-parallel
+// call is refused.
+static int take_device_error(moe_ctx *c) {
+    int err[2] = {0, 0};
+    CK(cudaMemcpy(&err[0], c->plan.error, sizeof(int), cudaMemcpyDeviceToHost));
+    if (c->pf.plan.error) CK(cudaMemcpy(&err[1], c->pf.plan.error, sizeof(int), cudaMemcpyDeviceToHost));
+    for (int i = 0; i < 2; i++) {
+        const int e = err[i];
+        if (!e) continue;
+        cudaMemset(i == 0 ? c->plan.error : c->pf.plan.error, 0, sizeof(int));
+        if (e == EP_ERR_TIMEOUT) {
+            c->ep_failed = true;
+            return fail(c, MOE_ERR_TIMEOUT, "peer exchange wait timed out (a peer rank stopped calling)");
+        }
+        if (e == EX_ERR_TIMEOUT) return fail(c, MOE_ERR_TIMEOUT, "expert pipeline wait timed out");
+        if (e == PF_ERR_TIMEOUT) return fail(c, MOE_ERR_TIMEOUT, "prefill pipeline wait timed out");
+        if (e == MOE_DEV_ERR_INDEX) return fail(c, MOE_ERR_ARG, "expert index out of range in routing");
+        return fail(c, MOE_ERR_CUDA, "device error code 0x%x", e);
+    }
+    return MOE_OK;
+}
+
+// True when the decode step's exchange runs over NCCL (no bounded wait).
+static bool step_uses_nccl(const moe_ctx *c) { return c->world > 1 && !c->p2p; }
+
+// Copies device results into caller memory.  When the step ran NCCL
+// kernels, the host first waits with the polling wait: a copy into pageable
+// memory returns only when the stream has drained, so a peer that stopped
+// calling would otherwise block the host inside the copy with no limit.
+struct HostCopy {
+    void *dst;
+    const void *src;
+    size_t bytes;
+};
+static int copy_out(moe_ctx *c, cudaStream_t s, bool nccl_in_step, std::initializer_list<HostCopy> cps) {
+    if (nccl_in_step) {
+        const int rc = stream_wait(c, s, true);
+        if (rc) return rc;
+        for (const HostCopy &h : cps)
+            if (h.dst && h.bytes) CK(cudaMemcpy(h.dst, h.src, h.bytes, cudaMemcpyDeviceToHost));
+        return MOE_OK;
+    }
+    for (const HostCopy &h : cps)
+        if (h.dst && h.bytes) CK(cudaMemcpyAsync(h.dst, h.src, h.bytes, cudaMemcpyDeviceToHost, s));
+    return MOE_OK;
 }
 
 static int finish_sync(moe_ctx *c) {
     {
-        const int rc = stream_wait(c, c->stream, c->world > 1 && !c->p2p);
+        const int rc = stream_wait(c, c->stream, step_uses_nccl(c));
         if (rc) return rc;
     }
-    int errflag = 0;
-    CK(cudaMemcpy(&errflag, c->plan.error, sizeof(int), cudaMemcpyDeviceToHost));
-    if (errflag) {
-        cudaMemset(c->plan.error, 0, sizeof(int));
-        if (errflag == EX_ERR_TIMEOUT) return fail(c, MOE_ERR_CUDA, "expert pipeline wait timed out");
-        if (errflag == EP_ERR_TIMEOUT)
-            return fail(c, MOE_ERR_CUDA, "peer exchange wait timed out (a peer rank stopped calling)");
-        if (errflag == MOE_DEV_ERR_INDEX) return fail(c, MOE_ERR_ARG, "expert index out of range in routing");
-        return fail(c, MOE_ERR_CUDA, "device error code 0x%x", errflag);
-    }
-    return MOE_OK;
+    return take_device_error(c);
+}
+
+int moe_check_error(moe_ctx *c) {
+    if (!c) return MOE_ERR_ARG;
+    DeviceScope ds(c->device);
+    return finish_sync(c);
 }
 
 int moe_forward(moe_ctx *c, int layer, const float *h, int T, float *out, int *idx_out, float *w_out) {
@@ -971,9 +1027,11 @@ int moe_forward(moe_ctx *c, int layer, const float *h, int T, float *out, int *i
     int rc = moe_forward_device(c, layer, c->d_in, T, c->d_out, nullptr, nullptr, nullptr);
     if (rc) return rc;
     if (n == 0) return finish_sync(c);
-    CK(cudaMemcpyAsync(out, c->d_out, n * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
-    if (idx_out) CK(cudaMemcpyAsync(idx_out, c->idx, sizeof(int) * T * c->d.K, cudaMemcpyDeviceToHost, c->stream));
-    if (w_out) CK(cudaMemcpyAsync(w_out, c->wts, sizeof(float) * T * c->d.K, cudaMemcpyDeviceToHost, c->stream));
+    rc = copy_out(c, c->stream, step_uses_nccl(c),
+                  {{out, c->d_out, n * sizeof(float)},
+                   {idx_out, c->idx, sizeof(int) * T * c->d.K},
+                   {w_out, c->wts, sizeof(float) * T * c->d.K}});
+    if (rc) return rc;
     return finish_sync(c);
 }
 
@@ -1077,9 +1135,8 @@ static int run_prefill_ep(moe_ctx *c, int layer, const float *d_h, int T, float 
     }
     NK(moe_nccl()->GroupEnd());
     int counts[64];
-    CK(cudaMemcpyAsync(counts, ws.tcount + 2, sizeof(int) * N, cudaMemcpyDeviceToHost, s));
     {
-        const int rc = stream_wait(c, s, true);
+        const int rc = copy_out(c, s, true, {{counts, ws.tcount + 2, sizeof(int) * N}});
         if (rc) return rc;
     }
     int ecap = 1;
@@ -1165,27 +1222,21 @@ int moe_prefill(moe_ctx *c, int layer, const float *h, int T, float *out, int *i
     if (cudaMemcpyAsync(dh, h, n * sizeof(float), cudaMemcpyHostToDevice, c->stream) != cudaSuccess)
         rc = fail(c, MOE_ERR_CUDA, "moe_prefill: copy in");
     if (!rc) rc = moe_prefill_device(c, layer, dh, T, dout, nullptr, nullptr, nullptr);
-    if (!rc && cudaMemcpyAsync(out, dout, n * sizeof(float), cudaMemcpyDeviceToHost, c->stream) != cudaSuccess)
-        rc = fail(c, MOE_ERR_CUDA, "moe_prefill: copy out");
-    if (!rc && idx_out)
-        cudaMemcpyAsync(idx_out, c->pf.idx, sizeof(int) * T * c->d.K, cudaMemcpyDeviceToHost, c->stream);
-    if (!rc && w_out) cudaMemcpyAsync(w_out, c->pf.w, sizeof(float) * T * c->d.K, cudaMemcpyDeviceToHost, c->stream);
-    const int wrc = stream_wait(c, c->stream, c->world > 1);
+    // with expert parallelism the host waits (polling, bounded) before it
+    // copies into the caller's memory
+    if (!rc)
+        rc = copy_out(c, c->stream, c->world > 1,
+                      {{out, dout, n * sizeof(float)},
+                       {idx_out, c->pf.idx, sizeof(int) * T * c->d.K},
+                       {w_out, c->pf.w, sizeof(float) * T * c->d.K}});
+    const int wrc = c->comm_aborted ? MOE_ERR_NCCL : stream_wait(c, c->stream, c->world > 1);
     if (wrc == MOE_OK) {  // after an abort the buffers may still be in use
         cudaFree(dh);
         cudaFree(dout);
     }
     if (rc) return rc;
     if (wrc) return wrc;
-    int errflag = 0;
-    CK(cudaMemcpy(&errflag, c->pf.plan.error, sizeof(int), cudaMemcpyDeviceToHost));
-    if (errflag) {
-        cudaMemset(c->pf.plan.error, 0, sizeof(int));
-        if (errflag == MOE_DEV_ERR_INDEX) return fail(c, MOE_ERR_ARG, "expert index out of range in routing");
-        if (errflag == PF_ERR_TIMEOUT) return fail(c, MOE_ERR_CUDA, "prefill pipeline wait timed out");
-        return fail(c, MOE_ERR_CUDA, "prefill error code 0x%x", errflag);
-    }
-    return MOE_OK;
+    return take_device_error(c);
 }
 
 int moe_forward_stack_device(moe_ctx *c, int first, int n_layers, float *d_hidden, int T, void *stream) {
@@ -1217,7 +1268,8 @@ int moe_forward_stack(moe_ctx *c, int first, int n_layers, float *hidden, int T)
     if (n) CK(cudaMemcpyAsync(c->d_in, hidden, n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
     int rc = moe_forward_stack_device(c, first, n_layers, c->d_in, T, nullptr);
     if (rc) return rc;
-    if (n) CK(cudaMemcpyAsync(hidden, c->d_in, n * sizeof(float), cudaMemcpyDeviceToHost, c->stream));
+    rc = copy_out(c, c->stream, step_uses_nccl(c), {{hidden, c->d_in, n * sizeof(float)}});
+    if (rc) return rc;
     return finish_sync(c);
 }
 

@@ -16,9 +16,10 @@
 
 // Scratch limits (floats): the router kernel keeps n_split * T * E partial
 // sums (n_split = hidden / 256) and T * E final logits, plus one counter per
-// 32 experts.  1 MiB + 256 KiB + 256 bytes, held by every GPU that loads the
-// library until the process exits.
-#define NOALLOC_MAX_PART (256 * 1024)
+// 32 experts.  The partial sums cover DeepSeek-V3 at its largest decode batch
+// (28 splits x 64 tokens x 256 experts): 1.75 MiB + 256 KiB + 256 bytes, held
+// by every GPU that loads the library until the process exits.
+#define NOALLOC_MAX_PART (28 * 64 * 256)
 #define NOALLOC_MAX_LOGITS (64 * 1024)
 #define NOALLOC_MAX_GROUPS 64
 #define NOALLOC_MAX_DEVICES 64
@@ -48,7 +49,7 @@ extern "C" int moe_route_hidden_noalloc(const moe_config *cfg, const float *d_ro
     if (T <= 0 || T > 64) return noalloc_fail("n_tokens must be in 1..64");
     const int n_split = H / 256;
     if ((size_t)n_split * T * E > NOALLOC_MAX_PART)
-        return noalloc_fail("hidden/256 * n_tokens * n_experts exceeds the 262144-float scratch");
+        return noalloc_fail("hidden/256 * n_tokens * n_experts exceeds the 458752-float scratch");
     if ((size_t)T * E > NOALLOC_MAX_LOGITS) return noalloc_fail("n_tokens * n_experts exceeds 65536");
     if ((E + 31) / 32 > NOALLOC_MAX_GROUPS) return noalloc_fail("too many expert groups");
 

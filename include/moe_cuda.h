@@ -151,9 +151,23 @@ size_t moe_expert_bytes(const moe_ctx *ctx, int layer);
  * reference's slot order. */
 int moe_forward(moe_ctx *ctx, int layer, const float *h_post, int n_tokens, float *out,
                 int *idx_out, float *w_out);
-/* Same on device buffers, asynchronous on `stream` (NULL = context stream). */
+/* Same on device buffers, asynchronous on `stream` (NULL = context stream).
+ * Errors that the kernels detect (a bounded wait that gave up, a routing
+ * index out of range) are not known when this returns: moe_check_error()
+ * reports them. */
 int moe_forward_device(moe_ctx *ctx, int layer, const float *d_h_post, int n_tokens,
                        float *d_out, int *d_idx_out, float *d_w_out, void *stream);
+
+/* Waits for the context stream and reports the first error the kernels
+ * recorded since the last host-pointer call or check: MOE_ERR_TIMEOUT when a
+ * bounded device wait gave up (expert pipeline, prefill pipeline, or a peer
+ * exchange -- after which the context refuses further expert-parallel
+ * calls), MOE_ERR_ARG for a routing index out of range.  The error word is
+ * cleared.  Host-pointer calls (moe_forward, ...) do this themselves; callers
+ * of the *_device entry points call it after a batch of steps.  With the
+ * NCCL exchange the wait polls and aborts the communicator after
+ * MOE_EP_TIMEOUT_S seconds (default 120). */
+int moe_check_error(moe_ctx *ctx);
 
 /* Routed experts only, with the routing given (metal_moe_forward,
  * infer.m:1604): moe_out[t] = sum_k exp_w[t,k] E_{exp_idx[t,k]}(h[t]). */
@@ -205,9 +219,9 @@ int moe_prefill(moe_ctx *ctx, int layer, const float *h_post, int n_tokens, floa
  * routing inside moe_forward().  For callers that cannot call cudaMalloc (a
  * fixed memory pool, or a latency-critical decode loop where an allocation
  * may synchronize the device): all scratch lives in a fixed array inside the
- * library (1.25 MiB per GPU, held until exit).  Limits: n_tokens <= 64,
- * (hidden/256) * n_tokens * n_experts <= 262144, n_tokens * n_experts <=
- * 65536.  All pointers are device pointers; the call is asynchronous on
+ * library (2 MiB per GPU, held until exit).  Limits: n_tokens <= 64,
+ * (hidden/256) * n_tokens * n_experts <= 458752 (DeepSeek-V3 at 64 tokens),
+ * n_tokens * n_experts <= 65536.  All pointers are device pointers; the call is asynchronous on
  * `stream` (NULL = default stream).  The first call on a device looks up the
  * array's device address; make it before any stream capture.  Every call
  * shares the one array, so calls that overlap on the GPU (other streams,

@@ -1,8 +1,11 @@
 """GPU: moe_route_hidden_noalloc -- routing for callers that cannot allocate
 device memory (a fixed memory pool, or a decode loop where cudaMalloc may
 synchronize the device) -- gives the same routing as moe_forward, through the
-C ABI, on two calls in a row (its scratch array is shared and keeps the last
-call's contents).  Collected last on purpose."""
+C ABI, at DeepSeek-V3 shapes.  Calls follow each other on one shared scratch
+array that keeps the last call's contents: 3 tokens (one-pass router kernel,
+no scratch), then 5 and 64 tokens (split-K router: partial sums and
+completion counters in the array), then 64 tokens again with other inputs.
+Collected last on purpose."""
 import ctypes as C
 
 import numpy as np
@@ -14,7 +17,7 @@ def test_route_hidden_noalloc_matches_forward(cuda_lib, oracle):
     import torch
     from flash_deepseek_b200 import MoeConfig, _lib
 
-    cfg = MoeConfig(n_layers=1, max_tokens=4)
+    cfg = MoeConfig(n_layers=1, max_tokens=64)
     m = cuda_lib.MoE(cfg)
     m.init_layer_synthetic(0, seed=3, down_type=cuda_lib.TYPE_Q6_K)
     O = oracle
@@ -26,8 +29,7 @@ def test_route_hidden_noalloc_matches_forward(cuda_lib, oracle):
     d_bias = torch.from_numpy(bias).to(dev)
     lib = _lib.load()
     ccfg = cfg.c()
-    for call in range(2):
-        T = 3 if call == 0 else 4
+    for call, T in enumerate((3, 5, 64, 64)):
         h = O.normal(40 + call, O.stream(0, 0, O.KIND_ACT), T * cfg.hidden, 1.0).reshape(T, cfg.hidden)
         _, idx_ref, w_ref = m.forward(0, h)          # existing entry point
         d_h = torch.from_numpy(h).to(dev)
@@ -38,8 +40,8 @@ def test_route_hidden_noalloc_matches_forward(cuda_lib, oracle):
         assert rc == 0
         torch.cuda.synchronize()
         idx, w = d_idx.cpu().numpy(), d_w.cpu().numpy()
-        assert np.array_equal(idx, idx_ref), call
-        assert np.allclose(w, w_ref, rtol=1e-6, atol=0), call
+        assert np.array_equal(idx, idx_ref), (call, T)
+        assert np.allclose(w, w_ref, rtol=1e-6, atol=0), (call, T)
     # sizes beyond the fixed scratch are rejected, not truncated
     big = MoeConfig(n_experts=1024, n_group=8, max_tokens=64).c()
     d_h = torch.zeros((64, cfg.hidden), dtype=torch.float32, device=dev)
