@@ -488,3 +488,87 @@ void or_moe_layer(const or_layer_cfg *cfg, const void *const *experts, const flo
     }
     free(logits); free(eo); free(acc);
 }
+
+/* ------------------------------------------------------------------------ */
+/* The same layer for a batch with the routing given, grouped by expert: each */
+/* weight row is dequantized once and dotted with every token the routing     */
+/* sends to that expert.  The per-row dot (k order, fp64 or fp32), the SwiGLU */
+/* and the combine (slot order, then + shared) are those of or_moe_layer, so  */
+/* the outputs are identical bit for bit; only the loop nest differs.         */
+/* ------------------------------------------------------------------------ */
+typedef struct {
+    const uint8_t *W; int type, cols; size_t rb;
+    const float *const *xs; float *const *ys; int n; int dbl;
+} mvn_ctx;
+static void mvn_rows(void *c, long lo, long hi) {
+    mvn_ctx *m = (mvn_ctx *)c;
+    float *row = (float *)malloc(sizeof(float) * (size_t)m->cols);
+    for (long r = lo; r < hi; r++) {
+        if (m->type == OR_TYPE_Q6_K) or_dequant_q6k(m->W + (size_t)r * m->rb, row, (size_t)m->cols);
+        else or_dequant_q4k(m->W + (size_t)r * m->rb, row, (size_t)m->cols);
+        for (int j = 0; j < m->n; j++) {
+            const float *x = m->xs[j];
+            if (m->dbl) {
+                double a = 0.0;
+                for (int k = 0; k < m->cols; k++) a += (double)row[k] * (double)x[k];
+                m->ys[j][r] = (float)a;
+            } else {
+                float a = 0.0f;
+                for (int k = 0; k < m->cols; k++) a += row[k] * x[k];
+                m->ys[j][r] = a;
+            }
+        }
+    }
+    free(row);
+}
+
+void or_moe_layer_given(const or_layer_cfg *cfg, const void *const *experts, const float *x, int B,
+                        const int *idx, const float *w, float *out, int acc_double, int n_threads) {
+    const int H = cfg->H, I = cfg->I, K = cfg->K, E = cfg->n_experts;
+    const size_t gb = or_row_bytes(OR_TYPE_Q4_K, (size_t)H) * (size_t)I;
+    const long P = (long)B * (K + 1);  /* pair p = b * (K + 1) + k, k = K: shared */
+    float *eo = (float *)malloc(sizeof(float) * (size_t)P * H);
+    float *g = (float *)malloc(sizeof(float) * (size_t)B * I * 3);
+    float *u = g + (size_t)B * I, *a = u + (size_t)B * I;
+    const float **xs = (const float **)malloc(sizeof(float *) * (size_t)B);
+    float **gs = (float **)malloc(sizeof(float *) * (size_t)B * 4);
+    float **us = gs + B, **as_ = us + B, **es = as_ + B;
+    long *pairs = (long *)malloc(sizeof(long) * (size_t)P);
+    for (int e = 0; e <= E; e++) {
+        int n = 0;
+        for (int b = 0; b < B; b++) {
+            for (int k = 0; k < K; k++)
+                if (e < E && idx[(size_t)b * K + k] == e) pairs[n++] = (long)b * (K + 1) + k;
+            if (e == E) pairs[n++] = (long)b * (K + 1) + K;
+        }
+        if (!n) continue;
+        const uint8_t *blob = (const uint8_t *)experts[e];
+        for (int j = 0; j < n; j++) {
+            xs[j] = x + (size_t)(pairs[j] / (K + 1)) * H;
+            gs[j] = g + (size_t)j * I;
+            us[j] = u + (size_t)j * I;
+            as_[j] = a + (size_t)j * I;
+            es[j] = eo + (size_t)pairs[j] * H;
+        }
+        mvn_ctx cg = {blob, OR_TYPE_Q4_K, H, or_row_bytes(OR_TYPE_Q4_K, (size_t)H), xs, gs, n, acc_double};
+        parallel_for(I, n_threads, mvn_rows, &cg);
+        mvn_ctx cu = {blob + gb, OR_TYPE_Q4_K, H, or_row_bytes(OR_TYPE_Q4_K, (size_t)H), xs, us, n, acc_double};
+        parallel_for(I, n_threads, mvn_rows, &cu);
+        for (int j = 0; j < n; j++) or_silu_mul(gs[j], us[j], as_[j], I);
+        mvn_ctx cd = {blob + 2 * gb, cfg->down_type, I, or_row_bytes(cfg->down_type, (size_t)I),
+                      (const float *const *)as_, es, n, acc_double};
+        parallel_for(H, n_threads, mvn_rows, &cd);
+    }
+    for (int b = 0; b < B; b++) {
+        float *o = out + (size_t)b * H;
+        for (int i = 0; i < H; i++) o[i] = 0.0f;
+        for (int k = 0; k < K; k++) {
+            const float *ek = eo + ((size_t)b * (K + 1) + k) * H;
+            const float wk = w[(size_t)b * K + k];
+            for (int i = 0; i < H; i++) o[i] += wk * ek[i];
+        }
+        const float *es_ = eo + ((size_t)b * (K + 1) + K) * H;
+        for (int i = 0; i < H; i++) o[i] = o[i] + es_[i];
+    }
+    free(pairs); free(gs); free(xs); free(g); free(eo);
+}

@@ -94,6 +94,13 @@ void or_moe_layer(const or_layer_cfg *cfg, const void *const *experts,
                   float *out, int *idx_out, float *w_out, float *logits_out,
                   int acc_double, int n_threads);
 
+/* The same layer with the routing given (idx / w [B x K]), grouped by
+ * expert: every weight row is dequantized once per expert and dotted with all
+ * of its tokens.  Same arithmetic as or_moe_layer, bit for bit. */
+void or_moe_layer_given(const or_layer_cfg *cfg, const void *const *experts,
+                        const float *x, int B, const int *idx, const float *w,
+                        float *out, int acc_double, int n_threads);
+
 size_t or_expert_bytes(int H, int I, int down_type);
 
 #ifdef __cplusplus

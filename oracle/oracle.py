@@ -82,6 +82,8 @@ def lib():
         L.or_moe_layer.argtypes = [C.POINTER(LayerCfg), C.POINTER(C.c_void_p), _f32p, C.c_void_p, _f32p, C.c_int,
                                    C.c_void_p, C.c_void_p, _f32p, C.c_void_p, C.c_void_p, C.c_void_p,
                                    C.c_int, C.c_int]
+        L.or_moe_layer_given.argtypes = [C.POINTER(LayerCfg), C.POINTER(C.c_void_p), _f32p, C.c_int, _i32p, _f32p,
+                                         _f32p, C.c_int, C.c_int]
         _lib = L
     return _lib
 
@@ -257,3 +259,28 @@ def moe_layer(cfg: dict, experts: dict, router_w, bias, x, force_idx=None, force
                        _ptr(None if bias is None else np.ascontiguousarray(bias, np.float32)), x, B,
                        _ptr(fi), _ptr(fw), out, _ptr(idx), _ptr(w), _ptr(logits), int(acc_double), threads)
     return out, idx, w, logits
+
+
+def moe_layer_given(cfg: dict, experts: dict, x, idx, w, acc_double=True, threads=None):
+    """The layer's output for a batch whose routing is given, grouped by
+    expert (each weight row dequantized once per expert): identical, bit for
+    bit, to moe_layer(..., force_idx=idx, force_w=w), and much faster for
+    many tokens.  experts: {expert_id: blob} for every routed id and the
+    shared expert (id n_experts)."""
+    if threads is None:
+        threads = max(1, len(os.sched_getaffinity(0)))
+    E = cfg["n_experts"]
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, cfg["H"])
+    B = x.shape[0]
+    c = LayerCfg(cfg["H"], cfg["I"], E, cfg["n_group"], cfg["topk_group"], cfg["K"],
+                 cfg["routed_scale"], cfg["down_type"])
+    table = (C.c_void_p * (E + 1))()
+    keep = []
+    for e, blob in experts.items():
+        blob = np.ascontiguousarray(blob, np.uint8)
+        keep.append(blob)
+        table[e] = blob.ctypes.data
+    out = np.empty((B, cfg["H"]), np.float32)
+    lib().or_moe_layer_given(C.byref(c), table, x, B, np.ascontiguousarray(idx, np.int32),
+                             np.ascontiguousarray(w, np.float32), out, int(acc_double), threads)
+    return out

@@ -135,28 +135,48 @@ def test_experts_and_shared_entry_points(cuda_lib, oracle):
     m.close()
 
 
+def _near_tie(logits, bias):
+    """True when two different choice scores (sigmoid + bias) lie within 1e-6
+    of each other: only there may the device's sigmoid (one ulp away from
+    libm's) change the selection or its slot order."""
+    c = np.sort(1.0 / (1.0 + np.exp(-logits.astype(np.float64))) + bias.astype(np.float64))
+    d = np.diff(c)
+    return bool(np.any((d > 0) & (d < 1e-6)))
+
+
 @pytest.mark.gpu
 def test_route_entry_point_golden(cuda_lib):
     """moe_route reproduces the reference route() (golden vectors produced by
-    the reference itself), slot order included; near-tie cases may differ
-    only by swaps within 1e-6."""
+    the reference itself): the exact slot order (it fixes the combine order,
+    infer.m:970-980) and the weights by index in every case without a near
+    tie -- random logits, exact ties decided by the tie rules, all-equal.
+    Near-tie cases (scores within 1e-6) may differ only by swaps within 1e-6
+    of the selection boundary; the test counts them."""
     import os
     from flash_deepseek_b200 import MoeConfig
     g = np.load(os.path.join(os.path.dirname(__file__), "golden", "route_golden.npz"))
     m = cuda_lib.MoE(MoeConfig(max_tokens=1, n_layers=1, intermediate=256, hidden=256))
     L, B, I, W = g["logits"], g["bias"], g["idx"], g["w"]
-    exact = 0
+    near = [i for i in range(len(L)) if _near_tie(L[i], B[i])]
+    differ = []
     for i in range(len(L)):
         idx, w = m.route(L[i][None], B[i])
-        if np.array_equal(idx[0], I[i]):
-            exact += 1
-            assert np.allclose(w[0], W[i], rtol=1e-6, atol=0)
-        else:
+        same_set = set(idx[0].tolist()) == set(I[i].tolist())
+        if i not in near:
+            assert np.array_equal(idx[0], I[i]), (i, idx[0], I[i])
+        if same_set:
+            wo = dict(zip(I[i].tolist(), W[i].tolist()))
+            for e, wv in zip(idx[0].tolist(), w[0].tolist()):
+                assert abs(wv - wo[e]) <= 1e-6 * max(1.0, abs(wo[e])), (i, e)
+        if not np.array_equal(idx[0], I[i]):
+            differ.append(i)
             choice = 1.0 / (1.0 + np.exp(-L[i].astype(np.float64))) + B[i]
             kth = np.sort(choice[I[i]])[0]
             for e in set(idx[0].tolist()) ^ set(I[i].tolist()):
                 assert abs(choice[e] - kth) < 1e-6, i
-    assert exact >= len(L) - 20
+    assert set(differ) <= set(near), (near, differ)
+    assert len(near) < len(L) // 4  # the golden set is mostly decided cases
+    print(f"route golden: {len(L)} cases, {len(near)} near ties, {len(differ)} of them differ in set or slot order")
     m.close()
 
 
@@ -201,8 +221,8 @@ def test_config2_layer_b1(cuda_lib, oracle):
 
 @pytest.mark.gpu
 def test_config3_shape_b64_zipf(cuda_lib, oracle):
-    """Config 3 on one GPU: decode batch 64, Zipf-skewed router; routing of all
-    64 tokens and outputs of a sample of tokens against the oracle."""
+    """Config 3 on one GPU: decode batch 64, Zipf-skewed router; routing and
+    outputs of all 64 tokens against the oracle."""
     from flash_deepseek_b200 import MoeConfig
     cfg = MoeConfig(n_layers=1, max_tokens=64)
     m = cuda_lib.MoE(cfg)
@@ -218,10 +238,14 @@ def test_config3_shape_b64_zipf(cuda_lib, oracle):
     counts = np.bincount(idx.reshape(-1), minlength=256)
     assert counts.max() >= 9  # skew reaches multi-chunk experts
     assert (counts > 0).sum() >= 64  # but load still spreads over many experts
-    sample = [0, 17, 42, 63]
-    ref = oracle_layer(oracle, m, cfg, 0, 14, h[sample], idx[sample], w[sample], router, bias)
-    err = rel_err(out[sample], ref)
+    # every one of the 64 output rows against the oracle (expert rows
+    # dequantized once per expert; the hot experts' multi-chunk items included)
+    experts = {e: m.read_expert(0, e) for e in sorted(set(idx.reshape(-1).tolist())) + [cfg.n_experts]}
+    ref = oracle.moe_layer_given(oracle_cfg(cfg, 14), experts, h, idx, w)
+    err = rel_err(out, ref)
     assert err < TOL and err < GUARD, err
+    rows = [rel_err(out[t], ref[t]) for t in range(64)]
+    assert max(rows) < GUARD, max(rows)
     # token independence: a token's output does not depend on its batch mates
     o1, i1, _ = m.forward(0, h[17:18])
     assert np.array_equal(i1[0], idx[17]) and rel_err(o1[0], out[17]) < 1e-6
@@ -337,4 +361,48 @@ def test_record_expert_hits(cuda_lib, oracle):
     m.forward_device(0, d_h, T, d_out)
     torch.cuda.synchronize()
     assert (hits.cpu().numpy() == -1).all()
+    m.close()
+
+
+@pytest.mark.gpu
+def test_stack_deepseek_shape_alternating_down(cuda_lib, oracle):
+    """Config 4 at its own shape: four DeepSeek-V3 layers (hidden 7168, 256 + 1
+    experts), Q6_K down on even and Q4_K down on odd layers, chained through
+    moe_forward_stack_device (RMSNorm eps 1e-6, hidden += MoE(h_post)),
+    against the oracle chain (infer.m:1850, 1922) that routes on its own
+    fp64 logits at every layer."""
+    import torch
+    from flash_deepseek_b200 import MoeConfig
+    n_layers, T = 4, 3
+    cfg = MoeConfig(n_layers=n_layers, max_tokens=T)
+    m = cuda_lib.MoE(cfg)
+    H, O = cfg.hidden, oracle
+    norms, dts = [], []
+    for L in range(n_layers):
+        dts.append(14 if L % 2 == 0 else 12)
+        m.init_layer_synthetic(L, seed=7, down_type=dts[L])
+        nw = (1.0 + 0.1 * O.normal(7, O.stream(L, 0, O.KIND_NORM), H, 1.0)).astype(np.float32)
+        m.set_norm_weight(L, nw)
+        norms.append(nw)
+    h0 = O.normal(8, O.stream(0, 0, O.KIND_ACT), T * H, 1.0).reshape(T, H)
+    d_hid = torch.from_numpy(h0).cuda()
+    m.forward_stack_device(0, n_layers, d_hid, T)
+    m.check_error()
+    got = d_hid.cpu().numpy()
+    hid = h0.copy()
+    for L in range(n_layers):
+        post = np.empty_like(hid)
+        for t in range(T):
+            O.lib().or_rms_norm(np.ascontiguousarray(hid[t]), norms[L].ctypes.data, post[t], H, 1e-6)
+        router, bias = router_of(O, 7, L, cfg)
+        logits = (post.astype(np.float64) @ router.astype(np.float64).T).astype(np.float32)
+        idx = np.empty((T, cfg.top_k), np.int32)
+        w = np.empty((T, cfg.top_k), np.float32)
+        for t in range(T):
+            idx[t], w[t] = O.route(logits[t], bias, cfg.n_group, cfg.topk_group, cfg.top_k, cfg.routed_scale)
+        experts = {e: m.read_expert(L, e) for e in sorted(set(idx.reshape(-1).tolist())) + [cfg.n_experts]}
+        moe = O.moe_layer_given(oracle_cfg(cfg, dts[L]), experts, post, idx, w)
+        hid = hid + moe
+    err = rel_err(got, hid)
+    assert err < TOL and err < GUARD, err
     m.close()

@@ -104,3 +104,47 @@ def test_prefill_router_logits_accuracy(cuda_lib, oracle):
     logits = (h.astype(np.float64) @ router.astype(np.float64).T).astype(np.float32)
     check_routing(oracle, cfg, logits, bias, idx, w)
     m.close()
+
+
+def _prefill_sample(idx, n_experts, rng, per_group=16):
+    """Rows that cover the hottest expert's tiles, the coldest experts and the
+    batch edges (tile boundaries of the shared expert), plus random rows."""
+    counts = np.bincount(idx.reshape(-1), minlength=n_experts)
+    hot = int(np.argmax(counts))
+    rows = set(np.nonzero((idx == hot).any(axis=1))[0][:per_group].tolist())
+    live = np.nonzero(counts)[0]
+    for e in live[np.argsort(counts[live])][:per_group]:
+        rows.add(int(np.nonzero((idx == e).any(axis=1))[0][0]))
+    T = idx.shape[0]
+    rows |= {0, 127, 128, T - 1}
+    rows |= set(rng.choice(T, per_group, replace=False).tolist())
+    return sorted(rows), hot, int(counts[hot])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("down_type,T", [(14, 4096), (12, 2048)])
+def test_prefill_full_size_matches_oracle(cuda_lib, oracle, down_type, T):
+    """Config 5 at its own shape: DeepSeek-V3 layer (hidden 7168, 256 + 1
+    experts, Q4_K gate/up, Q6_K or Q4_K down), 4096 (2048) tokens, so that
+    experts average 128 (64) pairs and the busy ones fill whole 128-pair
+    tcgen05 tiles, the shared expert 32 (16) of them.  The routing of every
+    token against fp64 logits; the outputs of a sample of rows (the hottest
+    expert's tokens, the coldest experts' tokens, tile edges, random rows)
+    against the oracle on the same routing."""
+    from test_gpu_moe import check_routing, oracle_cfg, rel_err, router_of
+    cfg = cuda_lib.MoeConfig(n_layers=1, max_tokens=64)
+    m = cuda_lib.MoE(cfg)
+    m.init_layer_synthetic(0, seed=0, down_type=down_type)
+    h = oracle.normal(21, oracle.stream(0, 0, oracle.KIND_ACT), T * cfg.hidden, 1.0).reshape(T, cfg.hidden)
+    out, idx, w = m.prefill(0, h)
+    router, bias = router_of(oracle, 0, 0, cfg)
+    logits = (h.astype(np.float64) @ router.astype(np.float64).T).astype(np.float32)
+    check_routing(oracle, cfg, logits, bias, idx, w)
+    rows, hot, n_hot = _prefill_sample(idx, cfg.n_experts, np.random.default_rng(5))
+    assert n_hot >= (128 if T >= 4096 else 64)  # the busiest expert fills (or half fills) a 128-pair tile
+    experts = {e: m.read_expert(0, e) for e in sorted(set(idx[rows].reshape(-1).tolist())) + [cfg.n_experts]}
+    ref = oracle.moe_layer_given(oracle_cfg(cfg, down_type), experts, h[rows], idx[rows], w[rows])
+    e = rel_err(out[rows], ref)
+    assert e < PREFILL_TOL, e
+    print(f"prefill T={T} down={down_type}: {len(rows)} rows, hottest expert {hot} with {n_hot} pairs, err {e:.2e}")
+    m.close()

@@ -131,3 +131,20 @@ def test_expert_forward_precision_variants(oracle):
     a = O.expert_forward(blob, H, I, O.TYPE_Q4_K, x, acc_double=True)
     b = O.expert_forward(blob, H, I, O.TYPE_Q4_K, x, acc_double=False)
     assert np.max(np.abs(a - b)) / np.max(np.abs(a)) < 1e-5
+
+
+@pytest.mark.parametrize("down_type", [12, 14])
+def test_grouped_layer_equals_per_token_layer(oracle, down_type):
+    """moe_layer_given (rows dequantized once per expert, all of its tokens
+    at once) is the per-token or_moe_layer restatement, bit for bit."""
+    O = oracle
+    H, I, E, K = 512, 256, 8, 3
+    cfg = dict(H=H, I=I, n_experts=E, n_group=4, topk_group=2, K=K, routed_scale=2.5, down_type=down_type)
+    experts = {e: O.gen_expert(5, 0, e, H, I, down_type) for e in range(E + 1)}
+    router = O.normal(5, O.stream(0, 0, O.KIND_ROUTER), E * H, 0.05).reshape(E, H)
+    x = O.normal(6, O.stream(0, 0, O.KIND_ACT), 7 * H, 1.0).reshape(7, H)
+    out, idx, w, _ = O.moe_layer(cfg, experts, router, None, x)
+    for dbl in (True, False):
+        ref, _, _, _ = O.moe_layer(cfg, experts, router, None, x, force_idx=idx, force_w=w, acc_double=dbl)
+        got = O.moe_layer_given(cfg, experts, x, idx, w, acc_double=dbl)
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
