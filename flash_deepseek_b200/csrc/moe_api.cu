@@ -78,11 +78,11 @@ struct moe_ctx {
     int *rl_counters = nullptr;
     int *idx = nullptr, *idx_given = nullptr;
     float *wts = nullptr, *w_given = nullptr, *bias_tmp = nullptr;
-    uint8_t *xop = nullptr;   // int8-plane operand rows, op_bytes(H) each
+    uint8_t *xop = nullptr;   // activation operand rows (int8 planes, then fp16 planes), opx_row(H) each
     MoePlan plan{};
     int *counter = nullptr;
     float *act = nullptr, *eo = nullptr;
-    uint8_t *dop = nullptr;   // down operand, op_bytes(I) per pair
+    uint8_t *dop = nullptr;   // down operand, opw_bytes(I) per pair (int8 or fp16 planes by chunk)
     int *h_counts = nullptr;  // pinned [4]
     // expert-parallel buffers
     float *send_x = nullptr, *recv_x = nullptr, *send_y = nullptr, *recv_y = nullptr;
@@ -206,8 +206,8 @@ static int ctx_alloc(moe_ctx *c) {
     CK(dmalloc(&c->w_given, (size_t)R * K));
     CK(dmalloc(&c->bias_tmp, (size_t)E));
     const int RT = (c->world > 1 ? R + T : R);  // EP: received rows + local rows
-    CK(dmalloc(&c->xop, (size_t)RT * op_bytes(H)));
-    CK(cudaMemset(c->xop, 0, (size_t)RT * op_bytes(H)));
+    CK(dmalloc(&c->xop, (size_t)RT * opx_row(H)));
+    CK(cudaMemset(c->xop, 0, (size_t)RT * opx_row(H)));
     const int P = c->max_pairs;
     CK(dmalloc(&c->plan.counts, 4));
     CK(dmalloc(&c->plan.pair_expert, P));
@@ -223,8 +223,8 @@ static int ctx_alloc(moe_ctx *c) {
     CK(dmalloc(&c->counter, 1));
     CK(cudaMemset(c->counter, 0, sizeof(int)));
     CK(dmalloc(&c->act, (size_t)P * I));
-    CK(dmalloc(&c->dop, (size_t)P * op_bytes(I)));
-    CK(cudaMemset(c->dop, 0, (size_t)P * op_bytes(I)));
+    CK(dmalloc(&c->dop, (size_t)P * opw_bytes(I)));
+    CK(cudaMemset(c->dop, 0, (size_t)P * opw_bytes(I)));
     CK(dmalloc(&c->eo, (size_t)P * H));
     CK(cudaMallocHost((void **)&c->h_counts, 4 * sizeof(int)));
     if (c->world > 1) {

@@ -57,6 +57,40 @@ __host__ __device__ __forceinline__ int opq4_xsum_off(int jj) {
 }
 
 // ---------------------------------------------------------------------------
+// Wide activation operand (fp16 planes), for the expert GEMVs' fp16 path: x
+// times a power of two s per super-block (max |x s| in [2^14, 2^15)) is split
+// into x_hi = fp16(x s) and x_lo = fp16(x s - x_hi) (22 significant bits
+// together).  Per vector and super-block, OPW_SB = 1088 bytes:
+//   [0, 512)     x_hi, 256 fp16 in lane order (style Q4 or Q6, below)
+//   [512, 528)   style Q4: fp16 hi parts of the 8 sub-block sums / 32
+//   [528, 544)   style Q4: fp16 lo parts of the same
+//   [544, 548)   1/s (fp32)
+//   [576, 1088)  x_lo in the same order (576: the two planes' 16-byte
+//                fragment loads of one quarter-warp fall on distinct banks)
+// Style Q4 (m16n8k16 fp16, Q4_K weights): element 8 t + i of sub-block j
+// (32 weights) sits at fp16 index 32 j + 8 t + perm(i), perm = 0 2 1 3 4 6 5 7,
+// so that one 16-byte load gives lane t the B fragments of both k16 steps.
+// Style Q6 (Q6_K weights, one sub-block of 16 per k16 step): element 4 t + i
+// of sub-block s sits at fp16 index 32 (s / 2) + 8 t + 4 (s % 2) + i.
+// ---------------------------------------------------------------------------
+#define OPW_SB 1088
+#define OPW_XSUM 512
+#define OPW_SCALE 544
+#define OPW_LO 576
+#define OPW_TOP 15  // max |x s| in [2^14, 2^15)
+__host__ __device__ __forceinline__ size_t opw_bytes(int K) { return (size_t)(K / 256) * OPW_SB; }
+// one decode activation row: the int8 planes, then the fp16 planes
+__host__ __device__ __forceinline__ size_t opx_row(int K) { return op_bytes(K) + opw_bytes(K); }
+__host__ __device__ __forceinline__ int opw4_idx(int k) {
+    const int j = k >> 5, t = (k >> 3) & 3, i = k & 7;
+    return 32 * j + 8 * t + ((i & 4) | ((i & 1) << 1) | ((i >> 1) & 1));
+}
+__host__ __device__ __forceinline__ int opw6_idx(int k) {
+    const int s = k >> 4, t = (k >> 2) & 3, i = k & 3;
+    return 32 * (s >> 1) + 8 * t + 4 * (s & 1) + i;
+}
+
+// ---------------------------------------------------------------------------
 // Repacked Q4_K block (lossless, done once at load): the 16-byte header
 // (d, dmin, 12 scale bytes) stays, the 128 qs bytes are transposed as a 4x4
 // grid of 8-byte chunks, new chunk 4 t + j = old chunk 4 j + t, so that lane
@@ -140,19 +174,6 @@ __device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c0), "f"(c1), "f"(c2), "f"(c3));
 }
 
-// Integer tensor-core step: D = A(16x16 u8 / s8, row) * B(16x8 s8, col) + C (s32).
-__device__ __forceinline__ void mma_u8s8_16816(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0, int c0, int c1,
-                                               int c2, int c3) {
-    asm("mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%8,%9,%10};\n"
-        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-        : "r"(a0), "r"(a1), "r"(b0), "r"(c0), "r"(c1), "r"(c2), "r"(c3));
-}
-__device__ __forceinline__ void mma_s8s8_16816(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0, int c0, int c1,
-                                               int c2, int c3) {
-    asm("mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%8,%9,%10};\n"
-        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-        : "r"(a0), "r"(a1), "r"(b0), "r"(c0), "r"(c1), "r"(c2), "r"(c3));
-}
 // sign-extended byte `i` (compile-time) of w
 template <int I>
 __device__ __forceinline__ int sext_byte(uint32_t w) {
@@ -163,38 +184,6 @@ __device__ __forceinline__ int sext_byte(uint32_t w) {
 
 __device__ __forceinline__ uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 __device__ __forceinline__ __half2 u32_as_h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
-
-// Streaming 16-byte load of weight bytes: read-only path, no L1 allocation
-// (each weight byte is used once per launch).
-__device__ __forceinline__ uint4 ldg_stream16(const void *p) {
-    uint4 r;
-    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                 : "l"(p));
-    return r;
-}
-// Activation-operand load (16 bytes, cached in L1: shared by many warps).
-__device__ __forceinline__ uint4 ldg_op16(const void *p) {
-    uint4 r;
-    asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];\n" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
-    return r;
-}
-
-// Asynchronous 16-byte global -> shared copy (L2 only), completed with
-// cp.async.wait_group.  Each lane later reads back only what it copied, so
-// no barrier is needed between the copy and its use.
-__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
-    const unsigned sa = (unsigned)__cvta_generic_to_shared(smem);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(gmem) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
-}
-#define MOE_STAGES 3        // per-warp weight pipeline depth
-#define MOE_Q4_WORDS 6      // 16-byte words per lane per Q4_K super-block (2 rows)
-#define MOE_Q6_WORDS 8      // 16-byte words per lane per Q6_K super-block (2 rows)
 
 // ---------------------------------------------------------------------------
 // Counter-based N(0, sigma) generator, bit-identical to the test oracle:

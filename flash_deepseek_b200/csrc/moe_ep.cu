@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(512) k_ep_plan(MoeDims d, const int *__restric
         int v[3] = {0, 0, 0};
         if (e < NE) {
             v[0] = cnt[e];
-            v[1] = (cnt[e] + MOE_TC - 1) / MOE_TC;
+            v[1] = moe_n_chunks(cnt[e]);
             v[2] = (e < E && cnt[e] > 0) ? 1 : 0;
         }
         int inc[3];
@@ -175,11 +175,14 @@ __global__ void __launch_bounds__(512) k_ep_plan(MoeDims d, const int *__restric
     }
     for (int e = threadIdx.x; e < NE; e += blockDim.x) {
         const int n = cnt[e];
-        for (int c = 0; c * MOE_TC < n; c++) {
+        const int nc = moe_n_chunks(n);
+        for (int c = 0; c < nc; c++) {
+            int start, ntf;
+            moe_chunk(n, c, start, ntf);
             const int ci = coff[e] + c;
             plan.chunk_expert[ci] = e;
-            plan.chunk_pair0[ci] = off[e] + c * MOE_TC;
-            plan.chunk_ntok[ci] = min(MOE_TC, n - c * MOE_TC);
+            plan.chunk_pair0[ci] = off[e] + start;
+            plan.chunk_ntok[ci] = ntf;
         }
     }
 }

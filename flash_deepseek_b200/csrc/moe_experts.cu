@@ -5,18 +5,28 @@
 //   down      eo[p][h]  = Wd[e] act[p]                Q6_K or Q4_K
 //             (infer.m:1570, 1087-1090)
 //
-// Work item = (chunk of <= 8 tokens of one expert, group of rows).  A
-// persistent CTA runs one producer warp and eight consumer warps over a ring
-// of shared-memory stages, one stage per 256-weight super-block of K:
+// Work item = (chunk of one expert's tokens, group of rows).  A persistent
+// CTA runs one producer warp and eight consumer warps over a ring of
+// shared-memory stages, one stage per 256-weight super-block of K:
 //   producer   waits for a free stage (mbarrier), then TMA-loads the item's
 //              weight tile of that super-block (3-D tensor map over
 //              [expert slot][row][byte]) and bulk-copies the chunk's
 //              activation operand slice; completion is counted in bytes on
 //              the stage's mbarrier
 //   consumers  wait for the stage, decode the weights in registers and
-//              reduce on the tensor cores with exact integer products
-//              (int8 activation planes, see moe_common.cuh), flush to fp32
-//              once per super-block, release the stage
+//              reduce on the tensor cores, flush to fp32 once per
+//              super-block, release the stage
+// Two reductions, chosen per chunk (moe_internal.h):
+//   int8 path  (chunks of few tokens) exact integer products of the weight
+//              integers and 21-bit activation planes (moe_common.cuh); the
+//              6-bit sub-block scales are applied to the int32 results
+//   fp16 path  (busy experts) the sub-block scale is folded into A exactly
+//              (Q4_K: q sc <= 945; Q6_K: (q - 32) sc as a rounded fp16 product
+//              plus its exact residual in a second MMA on the same B), the
+//              activations are fp16 hi/lo planes (22 bits), products exact,
+//              fp32 accumulation; 4 tokens per 8-column tile and no per-
+//              sub-block integer work, so each weight block is decoded once
+//              for up to 16 tokens
 // Every wait is bounded (about one second); on expiry the CTA records an
 // error in plan.error and leaves, after the producer has waited (again
 // bounded) for the copies it issued.
@@ -29,23 +39,24 @@
 
 #define EX_CONSUMERS 8
 #define EX_THREADS (32 * (EX_CONSUMERS + 1))
-#define EX_OPND (MOE_TC * OPB_SB)  // operand bytes of one stage (<= 8 vectors)
+// operand bytes of one stage: <= MOE_TC int8-plane vectors or <= MOE_WIDE_TC fp16-plane vectors
+#define EX_OPND (MOE_TC * OPB_SB > MOE_WIDE_TC * OPW_SB ? MOE_TC * OPB_SB : MOE_WIDE_TC * OPW_SB)
 #define EX_WAIT_CYCLES (1ll << 31)
 
 // gate/up: item = 64 rows of I (gate and up rows), K = H
 #define GU_ROWS 64
 #define GU_WBOX (GU_ROWS * MOE_Q4K_BYTES)
 #define GU_STAGE (2 * GU_WBOX + EX_OPND)
-#define GU_NS 4
+#define GU_NS 3
 // down: item = 128 rows of H, K = I
 #define DN_ROWS 128
 #define DN4_WBOX (DN_ROWS * MOE_Q4K_BYTES)
 #define DN4_STAGE (DN4_WBOX + EX_OPND)
-#define DN4_NS 4
+#define DN4_NS 3
 #define DN6_QBOX (DN_ROWS * 192)
 #define DN6_SBOX (DN_ROWS * 16)
 #define DN6_STAGE (DN6_QBOX + DN6_SBOX + EX_OPND)
-#define DN6_NS 3
+#define DN6_NS 2
 
 #define LAUNCH_COUNT(p) \
     do {                \
@@ -134,8 +145,45 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     return r;
 }
 
+// D += A(16x16 fp16, row) x B(16x8 fp16, col), fp32 accumulators
+__device__ __forceinline__ void mma_f16_acc(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                            uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// D = A(16x8 fp16, row) x B(8x8 fp16, col), fp32
+__device__ __forceinline__ void mma_f16_1688(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm("mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};\n"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a0), "r"(a1), "r"(b0), "f"(0.0f));
+}
+__device__ __forceinline__ uint32_t hfma2u(uint32_t a, uint32_t b, uint32_t c) {
+    return h2_as_u32(__hfma2(u32_as_h2(a), u32_as_h2(b), u32_as_h2(c)));
+}
+__device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
+    return h2_as_u32(__hmul2(u32_as_h2(a), u32_as_h2(b)));
+}
+__device__ __forceinline__ uint32_t hsub2u(uint32_t a, uint32_t b) {
+    return h2_as_u32(__hsub2(u32_as_h2(a), u32_as_h2(b)));
+}
+// fp16 pair constants
+#define H2_1024 0x64006400u
+#define H2_M1024 0xE400E400u
+#define H2_1056 0x64206420u
+#define H2_1152 0x64806480u
+#define H2_16TH 0x2C002C00u
+#define H2_M64 0xD400D400u
+// (v, v) for byte B of w (an integer v < 1024): bytes (v, 0x64) are 1024 + v
+template <int B>
+__device__ __forceinline__ uint32_t byte_h2(uint32_t w, uint32_t minus) {
+    return hsub2u(prmt(w, 0x64u, (uint32_t)(B | (4 << 4) | (B << 8) | (4 << 12))), minus);
+}
+
 struct ExItem {
     int rg, e, slot, p0, ntok;
+    bool wide;  // MOE_CHUNK_WIDE: the expert's tokens span several chunks
 };
 __device__ __forceinline__ void ex_item(const MoePlan &plan, const MoeLayerDev &L, int E, int n_chunks, int item,
                                         ExItem &it) {
@@ -143,7 +191,9 @@ __device__ __forceinline__ void ex_item(const MoePlan &plan, const MoeLayerDev &
     it.rg = item / n_chunks;
     it.e = plan.chunk_expert[c];
     it.p0 = plan.chunk_pair0[c];
-    it.ntok = plan.chunk_ntok[c];
+    const int v = plan.chunk_ntok[c];
+    it.ntok = MOE_CHUNK_NTOK(v);
+    it.wide = (v & MOE_CHUNK_WIDE) != 0;
     it.slot = it.e == E ? L.n_local : it.e - L.e0;
 }
 
@@ -347,6 +397,161 @@ __device__ __forceinline__ float planes_to_vector(float c0, float c1, int t) {
 }
 
 // ===========================================================================
+// fp16 path, Q4_K super-block of two rows (A rows g, g + 8) against NT tiles
+// of 4 tokens x 2 planes (column c: token c / 2 of the tile, plane c % 2).
+// A = q sc exactly in fp16: the nibble under the exponent of 1024 (1024 + q,
+// or 1024 + 16 q for a high nibble masked in place), then
+// fma(1024 + q, sc, -1024 sc) = q sc (or with sc / 16 and -64 sc), one
+// rounding of an exact integer <= 945.  Lane t's qs bytes 8 t .. 8 t + 7 of
+// sub-block pair jj give elements (0, 2), (1, 3) (k16 step 0) and (4, 6),
+// (5, 7) (step 1) of the low and of the high sub-block; the operand stores
+// B in the same order (style Q4, moe_common.cuh).  The min term
+// sum_j m_j xsum_j is one m16n8k8 MMA over the sub-block sums.  Per
+// super-block and lane column (token 4 n + t, both planes summed):
+//   acc_f += (d / s) (hi + lo) - (32 dmin / s) (min_hi + min_lo)
+// ===========================================================================
+template <int NT>
+__device__ __forceinline__ void q4w_stage(const uint8_t *rowg, const uint8_t *row8, const uint8_t *opnd, int g,
+                                          int t, float (&accf)[NT][2]) {
+    const uint4 hg = lds128(rowg), h8 = lds128(row8);
+    // 6-bit scales of sub-blocks 0-3 / 4-7, one per byte (get_scale_min_k4, quant.c:26-34)
+    const uint32_t scg[2] = {hg.y & 0x3F3F3F3Fu, (hg.w & 0x0F0F0F0Fu) | ((hg.y >> 2) & 0x30303030u)};
+    const uint32_t sc8[2] = {h8.y & 0x3F3F3F3Fu, (h8.w & 0x0F0F0F0Fu) | ((h8.y >> 2) & 0x30303030u)};
+    // this lane's B column: token g / 2 of the tile, plane g % 2
+    const uint8_t *bp = opnd + (g >> 1) * OPW_SB + (g & 1) * OPW_LO + 16 * t;
+    float acc[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+#pragma unroll
+    for (int jj = 0; jj < 4; jj++) {
+        const uint2 wg = lds64(rowg + 16 + 32 * t + 8 * jj), w8 = lds64(row8 + 16 + 32 * t + 8 * jj);
+        // scale constants of sub-blocks 2 jj (low nibbles) and 2 jj + 1 (high)
+        uint32_t sl_g, sl_8, sh_g, sh_8;
+        if ((jj & 1) == 0) {
+            sl_g = byte_h2<0>(scg[jj >> 1], H2_1024); sh_g = byte_h2<1>(scg[jj >> 1], H2_1024);
+            sl_8 = byte_h2<0>(sc8[jj >> 1], H2_1024); sh_8 = byte_h2<1>(sc8[jj >> 1], H2_1024);
+        } else {
+            sl_g = byte_h2<2>(scg[jj >> 1], H2_1024); sh_g = byte_h2<3>(scg[jj >> 1], H2_1024);
+            sl_8 = byte_h2<2>(sc8[jj >> 1], H2_1024); sh_8 = byte_h2<3>(sc8[jj >> 1], H2_1024);
+        }
+        const uint32_t nl_g = hmul2u(sl_g, H2_M1024), nl_8 = hmul2u(sl_8, H2_M1024);
+        const uint32_t nh_g = hmul2u(sh_g, H2_M64), nh_8 = hmul2u(sh_8, H2_M64);
+        sh_g = hmul2u(sh_g, H2_16TH);
+        sh_8 = hmul2u(sh_8, H2_16TH);
+        uint32_t lo[2][4], hi[2][4];  // [row g / g + 8][(0,2) (1,3) (4,6) (5,7)]
+        const uint32_t wv[2][2] = {{wg.x, wg.y}, {w8.x, w8.y}};
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            const uint32_t sl = r ? sl_8 : sl_g, nl = r ? nl_8 : nl_g, sh = r ? sh_8 : sh_g, nh = r ? nh_8 : nh_g;
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const uint32_t w = wv[r][h], ws = w >> 8;
+                lo[r][2 * h] = hfma2u((w & 0x000F000Fu) | H2_1024, sl, nl);
+                lo[r][2 * h + 1] = hfma2u((ws & 0x000F000Fu) | H2_1024, sl, nl);
+                hi[r][2 * h] = hfma2u((w & 0x00F000F0u) | H2_1024, sh, nh);
+                hi[r][2 * h + 1] = hfma2u((ws & 0x00F000F0u) | H2_1024, sh, nh);
+            }
+        }
+#pragma unroll
+        for (int n = 0; n < NT; n++) {
+            const uint4 bl = lds128(bp + 4 * n * OPW_SB + 128 * jj);
+            const uint4 bh = lds128(bp + 4 * n * OPW_SB + 128 * jj + 64);
+            mma_f16_acc(acc[n], lo[0][0], lo[1][0], lo[0][1], lo[1][1], bl.x, bl.y);
+            mma_f16_acc(acc[n], lo[0][2], lo[1][2], lo[0][3], lo[1][3], bl.z, bl.w);
+            mma_f16_acc(acc[n], hi[0][0], hi[1][0], hi[0][1], hi[1][1], bh.x, bh.y);
+            mma_f16_acc(acc[n], hi[0][2], hi[1][2], hi[0][3], hi[1][3], bh.z, bh.w);
+        }
+    }
+    // mins m_2t, m_2t+1 of rows g and g + 8 (A of the m16n8k8 min-term MMA)
+    const uint32_t mng[2] = {hg.z & 0x3F3F3F3Fu, ((hg.w >> 4) & 0x0F0F0F0Fu) | ((hg.z >> 2) & 0x30303030u)};
+    const uint32_t mn8[2] = {h8.z & 0x3F3F3F3Fu, ((h8.w >> 4) & 0x0F0F0F0Fu) | ((h8.z >> 2) & 0x30303030u)};
+    const uint32_t bsel = 2u * (uint32_t)(t & 1);
+    const uint32_t msel = bsel | (4u << 4) | ((bsel + 1u) << 8) | (4u << 12);
+    const uint32_t ma = hsub2u(prmt(mng[t >> 1], 0x64u, msel), H2_1024);
+    const uint32_t mb = hsub2u(prmt(mn8[t >> 1], 0x64u, msel), H2_1024);
+    const float dg = h2f_bits((uint16_t)(hg.x & 0xFFFFu)), dmg = 32.0f * h2f_bits((uint16_t)(hg.x >> 16));
+    const float d8 = h2f_bits((uint16_t)(h8.x & 0xFFFFu)), dm8 = 32.0f * h2f_bits((uint16_t)(h8.x >> 16));
+    const uint8_t *xs = opnd + (g >> 1) * OPW_SB + OPW_XSUM + 16 * (g & 1) + 4 * t;
+#pragma unroll
+    for (int n = 0; n < NT; n++) {
+        float mt[4];
+        mma_f16_1688(mt, ma, mb, *reinterpret_cast<const uint32_t *>(xs + 4 * n * OPW_SB));
+        const float inv = *reinterpret_cast<const float *>(opnd + (4 * n + t) * OPW_SB + OPW_SCALE);
+        accf[n][0] = fmaf(dg * inv, acc[n][0] + acc[n][1], fmaf(-dmg * inv, mt[0] + mt[1], accf[n][0]));
+        accf[n][1] = fmaf(d8 * inv, acc[n][2] + acc[n][3], fmaf(-dm8 * inv, mt[2] + mt[3], accf[n][1]));
+    }
+}
+
+// ===========================================================================
+// fp16 path, Q6_K super-block of two rows against NT tiles of 4 tokens x 2
+// planes.  q (6 bits, from the repacked planes, high qh bit restored) under
+// the exponent of 1024 minus 1056 gives Q = q - 32 exactly; v = Q sc
+// (|v| <= 4096) is P = fp16(Q sc) plus R = fma(Q, sc, -P) in {-1, 0, 1}, both
+// exact, and P and R run as two MMAs on the same B.  Lane t holds elements
+// 4 t .. 4 t + 3 of every sub-block (style Q6).  Per super-block:
+// acc_f += (d / s) (hi + lo).
+// ===========================================================================
+template <int NT>
+__device__ __forceinline__ void q6w_stage(const uint8_t *qg, const uint8_t *q8, const uint8_t *sg_p,
+                                          const uint8_t *s8_p, float dg, float d8, const uint8_t *opnd, int g, int t,
+                                          float (&accf)[NT][2]) {
+    const uint4 u0 = lds128(qg + 48 * t), u1 = lds128(qg + 48 * t + 16), u2 = lds128(qg + 48 * t + 32);
+    const uint4 v0 = lds128(q8 + 48 * t), v1 = lds128(q8 + 48 * t + 16), v2 = lds128(q8 + 48 * t + 32);
+    const uint32_t wq[2][2][6] = {{{u0.x, u0.y, u0.z, u0.w, u1.x, u1.y}, {u1.z, u1.w, u2.x, u2.y, u2.z, u2.w}},
+                                  {{v0.x, v0.y, v0.z, v0.w, v1.x, v1.y}, {v1.z, v1.w, v2.x, v2.y, v2.z, v2.w}}};
+    // int8 scales + 128 (bytes under 0x64 give 1152 + sc)
+    const uint4 sgv = lds128(sg_p), s8v = lds128(s8_p);
+    const uint32_t sw[2][4] = {{sgv.x ^ 0x80808080u, sgv.y ^ 0x80808080u, sgv.z ^ 0x80808080u, sgv.w ^ 0x80808080u},
+                               {s8v.x ^ 0x80808080u, s8v.y ^ 0x80808080u, s8v.z ^ 0x80808080u, s8v.w ^ 0x80808080u}};
+    const uint8_t *bp = opnd + (g >> 1) * OPW_SB + (g & 1) * OPW_LO + 16 * t;
+    float acc[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+#pragma unroll
+    for (int s2 = 0; s2 < 8; s2++) {
+        uint32_t P[2][2][2], R[2][2][2];  // [sub-block even / odd][row][elements (0,1) / (2,3)]
+#pragma unroll
+        for (int o = 0; o < 2; o++) {
+            const int s = 2 * s2 + o, h = s >> 3, sp = s & 7, f = sp >> 1;
+#pragma unroll
+            for (int r = 0; r < 2; r++) {
+                const uint32_t W = wq[r][h][sp & 3], Hq = wq[r][h][4 + (sp & 1)];
+                const uint32_t nib = (sp < 4 ? W : W >> 4) & 0x0F0F0F0Fu;
+                const uint32_t hb = (2 * f <= 4 ? Hq << (4 - 2 * f) : Hq >> (2 * f - 4)) & 0x30303030u;
+                const uint32_t q6 = nib | (hb ^ 0x20202020u);  // four values q (0..63) in bytes
+                uint32_t sc;
+                switch (s & 3) {
+                    case 0: sc = byte_h2<0>(sw[r][s >> 2], H2_1152); break;
+                    case 1: sc = byte_h2<1>(sw[r][s >> 2], H2_1152); break;
+                    case 2: sc = byte_h2<2>(sw[r][s >> 2], H2_1152); break;
+                    default: sc = byte_h2<3>(sw[r][s >> 2], H2_1152); break;
+                }
+                const uint32_t q01 = hsub2u(prmt(q6, 0x64u, 0x4140u), H2_1056);  // q - 32, exact
+                const uint32_t q23 = hsub2u(prmt(q6, 0x64u, 0x4342u), H2_1056);
+                P[o][r][0] = hmul2u(q01, sc);
+                P[o][r][1] = hmul2u(q23, sc);
+                R[o][r][0] = hfma2u(q01, sc, P[o][r][0] ^ 0x80008000u);  // Q sc - P, exact
+                R[o][r][1] = hfma2u(q23, sc, P[o][r][1] ^ 0x80008000u);
+            }
+        }
+#pragma unroll
+        for (int n = 0; n < NT; n++) {
+            const uint4 b = lds128(bp + 4 * n * OPW_SB + 64 * s2);
+            mma_f16_acc(acc[n], P[0][0][0], P[0][1][0], P[0][0][1], P[0][1][1], b.x, b.y);
+            mma_f16_acc(acc[n], R[0][0][0], R[0][1][0], R[0][0][1], R[0][1][1], b.x, b.y);
+            mma_f16_acc(acc[n], P[1][0][0], P[1][1][0], P[1][0][1], P[1][1][1], b.z, b.w);
+            mma_f16_acc(acc[n], R[1][0][0], R[1][1][0], R[1][0][1], R[1][1][1], b.z, b.w);
+        }
+    }
+#pragma unroll
+    for (int n = 0; n < NT; n++) {
+        const float inv = *reinterpret_cast<const float *>(opnd + (4 * n + t) * OPW_SB + OPW_SCALE);
+        accf[n][0] = fmaf(dg * inv, acc[n][0] + acc[n][1], accf[n][0]);
+        accf[n][1] = fmaf(d8 * inv, acc[n][2] + acc[n][3], accf[n][1]);
+    }
+}
+
+// ===========================================================================
 // gate/up
 // ===========================================================================
 template <int NT>
@@ -372,6 +577,35 @@ __device__ __forceinline__ bool gu_item(const MoeDims &d, const MoePlan &plan, f
         const float uv = planes_to_vector(accf[n][2], accf[n][3], t);
         const int tk = 2 * n + t;
         if (t < 2 && tk < it.ntok) act[(size_t)(it.p0 + tk) * d.I + row] = (gv / (1.0f + expf(-gv))) * uv;
+    }
+    return true;
+}
+
+// fp16-path gate/up item: lane (g, t) ends with the gate (row g) and up
+// (row g + 8) values of token 4 n + t, so SwiGLU needs no shuffle.
+template <int NT>
+__device__ __forceinline__ bool gu_item_w(const MoeDims &d, float *__restrict__ act, const ExItem &it, int NB,
+                                          uint8_t *sm, uint64_t *full, uint64_t *empty, uint32_t &seq, int w,
+                                          int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    float accf[NT][2];
+#pragma unroll
+    for (int n = 0; n < NT; n++) accf[n][0] = accf[n][1] = 0.0f;
+    for (int sb = 0; sb < NB; sb++, seq++) {
+        const int st = seq % GU_NS;
+        if (!mbar_wait(&full[st], (seq / GU_NS) & 1)) return false;
+        const uint8_t *stage = sm + (size_t)st * GU_STAGE;
+        q4w_stage<NT>(stage + (8 * w + g) * MOE_Q4K_BYTES, stage + GU_WBOX + (8 * w + g) * MOE_Q4K_BYTES,
+                      stage + 2 * GU_WBOX, g, t, accf);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    const int row = it.rg * GU_ROWS + 8 * w + g;
+#pragma unroll
+    for (int n = 0; n < NT; n++) {
+        const int tk = 4 * n + t;
+        const float gv = accf[n][0], uv = accf[n][1];
+        if (tk < it.ntok) act[(size_t)(it.p0 + tk) * d.I + row] = (gv / (1.0f + expf(-gv))) * uv;
     }
     return true;
 }
@@ -402,26 +636,29 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
     const int n_items = n_chunks * (d.I / GU_ROWS);
     uint32_t seq = 0;
     if (warp == EX_CONSUMERS) {  // producer
-        const size_t opst = op_bytes(d.H);
+        const size_t rowst = opx_row(d.H), wide_off = op_bytes(d.H);
         bool ok = true;
         for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
             ExItem it;
             ex_item(plan, L, d.E, n_chunks, item, it);
+            // the chunk's operand form: fp16 planes for >= MOE_GU_WIDE_MIN tokens
+            const bool fp = it.ntok >= MOE_GU_WIDE_MIN;
+            const uint32_t osb = fp ? OPW_SB : OPB_SB;
+            const uint8_t *src = lane < it.ntok ? xop + (size_t)plan.pair_token[it.p0 + lane] * rowst +
+                                                      (fp ? wide_off : 0)
+                                                : nullptr;
             for (int sb = 0; sb < NB; sb++, seq++) {
                 const int st = seq % GU_NS;
                 if (!mbar_wait(&empty[st], ((seq / GU_NS) & 1) ^ 1)) { ok = false; break; }
                 uint8_t *stage = sm + (size_t)st * GU_STAGE;
                 if (lane == 0) {
-                    mbar_expect_tx(&full[st], 2 * GU_WBOX + it.ntok * OPB_SB);
+                    mbar_expect_tx(&full[st], 2 * GU_WBOX + it.ntok * osb);
                     tma_load_3d(stage, &L.tm_gu, sb * MOE_Q4K_BYTES, it.rg * GU_ROWS, it.slot, &full[st]);
                     tma_load_3d(stage + GU_WBOX, &L.tm_gu, sb * MOE_Q4K_BYTES, d.I + it.rg * GU_ROWS, it.slot,
                                 &full[st]);
                 }
                 __syncwarp();
-                if (lane < it.ntok)
-                    bulk_load(stage + 2 * GU_WBOX + lane * OPB_SB,
-                              xop + (size_t)plan.pair_token[it.p0 + lane] * opst + (size_t)sb * OPB_SB, OPB_SB,
-                              &full[st]);
+                if (lane < it.ntok) bulk_load(stage + 2 * GU_WBOX + lane * osb, src + (size_t)sb * osb, osb, &full[st]);
             }
         }
         if (!ok && lane == 0) atomicExch(plan.error, EX_ERR_TIMEOUT);
@@ -434,11 +671,17 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
         ExItem it;
         ex_item(plan, L, d.E, n_chunks, item, it);
         bool ok;
-        switch ((it.ntok + 1) >> 1) {
-            case 1: ok = gu_item<1>(d, plan, act, it, NB, sm, full, empty, seq, warp, lane); break;
-            case 2: ok = gu_item<2>(d, plan, act, it, NB, sm, full, empty, seq, warp, lane); break;
-            case 3: ok = gu_item<3>(d, plan, act, it, NB, sm, full, empty, seq, warp, lane); break;
-            default: ok = gu_item<4>(d, plan, act, it, NB, sm, full, empty, seq, warp, lane); break;
+        if (it.ntok >= MOE_GU_WIDE_MIN) {
+            switch ((it.ntok + 3) >> 2) {
+                case 2: ok = gu_item_w<2>(d, act, it, NB, sm, full, empty, seq, warp, lane); break;
+                case 3: ok = gu_item_w<3>(d, act, it, NB, sm, full, empty, seq, warp, lane); break;
+                default: ok = gu_item_w<4>(d, act, it, NB, sm, full, empty, seq, warp, lane); break;
+            }
+        } else {
+            switch ((it.ntok + 1) >> 1) {
+                case 1: ok = gu_item<1>(d, plan, act, it, NB, sm, full, empty, seq, warp, lane); break;
+                default: ok = gu_item<2>(d, plan, act, it, NB, sm, full, empty, seq, warp, lane); break;
+            }
         }
         if (!ok) {
             if (lane == 0) atomicExch(plan.error, EX_ERR_TIMEOUT);
@@ -492,6 +735,45 @@ __device__ __forceinline__ bool dn_item(const MoeDims &d, float *__restrict__ eo
     return true;
 }
 
+// fp16-path down item (chunks marked MOE_CHUNK_WIDE)
+template <int NT, int TY>
+__device__ __forceinline__ bool dn_item_w(const MoeDims &d, float *__restrict__ eo, const ExItem &it, int NB,
+                                          int nbp, uint8_t *sm, const uint8_t *dbuf, uint64_t *full, uint64_t *empty,
+                                          uint32_t &seq, int w, int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    constexpr int NS = TY == MOE_TYPE_Q6_K ? DN6_NS : DN4_NS;
+    constexpr int STAGE = TY == MOE_TYPE_Q6_K ? DN6_STAGE : DN4_STAGE;
+    const int rl = 16 * w + g;  // local rows rl, rl + 8 of the item
+    float accf[NT][2];
+#pragma unroll
+    for (int n = 0; n < NT; n++) accf[n][0] = accf[n][1] = 0.0f;
+    for (int sb = 0; sb < NB; sb++, seq++) {
+        const int st = seq % NS;
+        if (!mbar_wait(&full[st], (seq / NS) & 1)) return false;
+        const uint8_t *stage = sm + (size_t)st * STAGE;
+        if (TY == MOE_TYPE_Q6_K) {
+            const __half *dp = reinterpret_cast<const __half *>(dbuf);
+            const float dg = __half2float(dp[rl * nbp + sb]), d8 = __half2float(dp[(rl + 8) * nbp + sb]);
+            q6w_stage<NT>(stage + rl * 192, stage + (rl + 8) * 192, stage + DN6_QBOX + rl * 16,
+                          stage + DN6_QBOX + (rl + 8) * 16, dg, d8, stage + DN6_QBOX + DN6_SBOX, g, t, accf);
+        } else {
+            q4w_stage<NT>(stage + rl * MOE_Q4K_BYTES, stage + (rl + 8) * MOE_Q4K_BYTES, stage + DN4_WBOX, g, t, accf);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    const int row = it.rg * DN_ROWS + rl;
+#pragma unroll
+    for (int n = 0; n < NT; n++) {
+        const int tk = 4 * n + t;
+        if (tk < it.ntok) {
+            eo[(size_t)(it.p0 + tk) * d.H + row] = accf[n][0];
+            eo[(size_t)(it.p0 + tk) * d.H + row + 8] = accf[n][1];
+        }
+    }
+    return true;
+}
+
 // One instance per down type; chunks of the other type are skipped.
 template <int TY>
 __global__ void __launch_bounds__(EX_THREADS, 2)
@@ -524,20 +806,22 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
     const int n_items = n_chunks * (d.H / DN_ROWS);
     uint32_t seq = 0, nitem = 0;
     if (warp == EX_CONSUMERS) {  // producer
-        const size_t opst = op_bytes(d.I);
+        const size_t opst = opw_bytes(d.I);  // pair rows of the down operand
         bool ok = true, waited = false;
         int ndef = 0, def_st[NS], def_p0[NS], def_nt[NS], def_sb[NS];
-        auto issue_ops = [&](int st, int p0, int ntok, int sb) {
+        bool def_fp[NS];
+        auto issue_ops = [&](int st, int p0, int ntok, int sb, bool fp) {
             if (lane < ntok) {
+                const uint32_t osb = fp ? OPW_SB : OPB_SB;
                 uint8_t *od = sm + (size_t)st * STAGE + (TY == MOE_TYPE_Q6_K ? DN6_QBOX + DN6_SBOX : DN4_WBOX) +
-                              lane * OPB_SB;
-                bulk_load(od, dop + (size_t)(p0 + lane) * opst + (size_t)sb * OPB_SB, OPB_SB, &full[st]);
+                              lane * osb;
+                bulk_load(od, dop + (size_t)(p0 + lane) * opst + (size_t)sb * osb, osb, &full[st]);
             }
         };
         auto flush_deferred = [&]() {
             moe_pdl_wait();
             waited = true;
-            for (int k = 0; k < ndef; k++) issue_ops(def_st[k], def_p0[k], def_nt[k], def_sb[k]);
+            for (int k = 0; k < ndef; k++) issue_ops(def_st[k], def_p0[k], def_nt[k], def_sb[k], def_fp[k]);
             ndef = 0;
         };
         for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
@@ -550,23 +834,25 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
                 const int st = seq % NS;
                 if (!mbar_wait(&empty[st], ((seq / NS) & 1) ^ 1)) { ok = false; break; }
                 uint8_t *stage = sm + (size_t)st * STAGE;
+                const uint32_t osb = it.wide ? OPW_SB : OPB_SB;
                 if (lane == 0) {
                     const int y = it.rg * DN_ROWS;
                     if (TY == MOE_TYPE_Q6_K) {
-                        mbar_expect_tx(&full[st], DN6_QBOX + DN6_SBOX + it.ntok * OPB_SB + (sb == 0 ? dbytes : 0));
+                        mbar_expect_tx(&full[st], DN6_QBOX + DN6_SBOX + it.ntok * osb + (sb == 0 ? dbytes : 0));
                         tma_load_3d(stage, &L.tm_d6q, sb * 192, y, it.slot, &full[st]);
                         tma_load_3d(stage + DN6_QBOX, &L.tm_d6s, sb * 16, y, it.slot, &full[st]);
                         if (sb == 0) tma_load_3d(dbuf, &L.tm_d6d, 0, y, it.slot, &full[st]);
                     } else {
-                        mbar_expect_tx(&full[st], DN4_WBOX + it.ntok * OPB_SB);
+                        mbar_expect_tx(&full[st], DN4_WBOX + it.ntok * osb);
                         tma_load_3d(stage, &L.tm_d4, sb * MOE_Q4K_BYTES, y, it.slot, &full[st]);
                     }
                 }
                 __syncwarp();
                 if (waited) {
-                    issue_ops(st, it.p0, it.ntok, sb);
+                    issue_ops(st, it.p0, it.ntok, sb, it.wide);
                 } else {
                     def_st[ndef] = st; def_p0[ndef] = it.p0; def_nt[ndef] = it.ntok; def_sb[ndef] = sb;
+                    def_fp[ndef] = it.wide;
                     if (++ndef == NS) flush_deferred();
                 }
             }
@@ -585,11 +871,20 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
         const uint8_t *dbuf = dbuf0 + (size_t)(nitem & 1) * dbytes;
         nitem++;
         bool ok;
-        switch ((it.ntok + 1) >> 1) {
-            case 1: ok = dn_item<1, TY>(d, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
-            case 2: ok = dn_item<2, TY>(d, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
-            case 3: ok = dn_item<3, TY>(d, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
-            default: ok = dn_item<4, TY>(d, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
+        if (it.wide) {
+            switch ((it.ntok + 3) >> 2) {
+                case 1: ok = dn_item_w<1, TY>(d, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
+                case 2: ok = dn_item_w<2, TY>(d, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
+                case 3: ok = dn_item_w<3, TY>(d, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
+                default: ok = dn_item_w<4, TY>(d, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
+            }
+        } else {
+            switch ((it.ntok + 1) >> 1) {
+                case 1: ok = dn_item<1, TY>(d, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
+                case 2: ok = dn_item<2, TY>(d, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
+                case 3: ok = dn_item<3, TY>(d, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
+                default: ok = dn_item<4, TY>(d, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
+            }
         }
         if (!ok) {
             if (lane == 0) atomicExch(plan.error, EX_ERR_TIMEOUT);

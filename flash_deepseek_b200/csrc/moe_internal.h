@@ -94,7 +94,32 @@ inline void moe_smem_limit(F *kernel, size_t bytes, size_t (&done)[MOE_MAX_DEVIC
         done[dev] = bytes;
 }
 
-#define MOE_TC 8  // tokens per chunk (four 8-column MMA tiles of 2 tokens x 3 planes)
+// Chunks of an expert's tokens (the unit of work of the expert GEMVs).  An
+// expert with at most MOE_TC tokens is one chunk; a busier one is split into
+// ceil(n / MOE_WIDE_TC) chunks of nearly equal size, each marked with
+// MOE_CHUNK_WIDE in chunk_ntok (the low 16 bits hold the token count).  The
+// gate/up GEMV runs a chunk on the fp16 path when it has at least
+// MOE_GU_WIDE_MIN tokens, the down GEMV when it is marked wide; otherwise on
+// the int8-plane path.
+#define MOE_TC 8           // tokens of an int8-path chunk (four 8-column tiles of 2 tokens x 3 planes)
+#define MOE_WIDE_TC 16     // tokens of an fp16-path chunk (four 8-column tiles of 4 tokens x 2 planes)
+#define MOE_GU_WIDE_MIN 5
+#define MOE_CHUNK_WIDE (1 << 16)
+#define MOE_CHUNK_NTOK(v) ((v) & 0xFFFF)
+__host__ __device__ __forceinline__ int moe_n_chunks(int n) {
+    return n <= 0 ? 0 : n <= MOE_TC ? 1 : (n + MOE_WIDE_TC - 1) / MOE_WIDE_TC;
+}
+// chunk c of an expert with n tokens: first token (relative) and chunk_ntok value
+__host__ __device__ __forceinline__ void moe_chunk(int n, int c, int &start, int &ntok_flags) {
+    if (n <= MOE_TC) {
+        start = 0;
+        ntok_flags = n;
+        return;
+    }
+    const int nc = (n + MOE_WIDE_TC - 1) / MOE_WIDE_TC, q = n / nc, r = n % nc;
+    start = c * q + (c < r ? c : r);
+    ntok_flags = (q + (c < r ? 1 : 0)) | MOE_CHUNK_WIDE;
+}
 
 // ---- launchers (moe_kernels.cu); every one counts its kernel launches ------
 extern "C++" {

@@ -575,12 +575,74 @@ __device__ __forceinline__ void build_op_sb(const float *__restrict__ x, uint8_t
     if (lane == 0) *reinterpret_cast<float *>(op + OPB_SCALE) = inv;
 }
 
-// Operand of a K-vector by the warps of the block, one super-block per warp.
-__device__ __forceinline__ void build_op_rows(const float *__restrict__ x, int K, uint8_t *__restrict__ op,
-                                              int style) {
+// One 256-weight super-block of one vector in the wide (fp16 hi/lo) form,
+// built by one warp (layout in moe_common.cuh): s = power of two from the
+// super-block's max |x| (max |x s| in [2^14, 2^15)), x_hi = fp16(x s),
+// x_lo = fp16(x s - x_hi), both planes in the lane order of `style`; style 4
+// adds the sub-block sums of x_hi + x_lo (divided by 32, as fp16 hi/lo) for
+// the Q4_K min term.  x must be 16-byte aligned.
+__device__ __forceinline__ void build_opw_sb(const float *__restrict__ x, uint8_t *__restrict__ op, int style,
+                                             int lane) {
+    const float4 a = __ldg(reinterpret_cast<const float4 *>(x) + 2 * lane);
+    const float4 b = __ldg(reinterpret_cast<const float4 *>(x) + 2 * lane + 1);
+    const float v8[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    float m = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) m = fmaxf(m, fabsf(v8[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float inv;
+    const float sc = op_scale(m, &inv, OPW_TOP);
+    __half hi[8], lo[8];
+    float sum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const float xs = __fmul_rn(v8[i], sc);  // exact: sc is a power of two
+        hi[i] = __float2half_rn(xs);
+        const float hv = __half2float(hi[i]);
+        lo[i] = __float2half_rn(__fsub_rn(xs, hv));  // xs - hv is exact in fp32
+        sum = __fadd_rn(sum, __fadd_rn(hv, __half2float(lo[i])));  // hv + lo exact (22 bits)
+    }
+    __half *H = reinterpret_cast<__half *>(op), *L = reinterpret_cast<__half *>(op + OPW_LO);
+    if (style == 4) {
+        // elements 8 lane + i: sub-block lane / 4, t = lane % 4 -> 16 contiguous bytes
+        const int base = 8 * lane;  // opw4_idx(8 lane + i) = 8 lane + perm(i)
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int ix = base + ((i & 4) | ((i & 1) << 1) | ((i >> 1) & 1));
+            H[ix] = hi[i];
+            L[ix] = lo[i];
+        }
+        // sub-block j = lane / 4: sum over its four lanes in a fixed order
+        sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 1));
+        sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 2));
+        if ((lane & 3) == 0) {
+            const float s32 = __fmul_rn(sum, 0.03125f);  // exact
+            const __half sh = __float2half_rn(s32);
+            const __half sl = __float2half_rn(__fsub_rn(s32, __half2float(sh)));
+            reinterpret_cast<__half *>(op + OPW_XSUM)[lane >> 2] = sh;
+            reinterpret_cast<__half *>(op + OPW_XSUM + 16)[lane >> 2] = sl;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int ix = opw6_idx(8 * lane + i);
+            H[ix] = hi[i];
+            L[ix] = lo[i];
+        }
+    }
+    if (lane == 0) *reinterpret_cast<float *>(op + OPW_SCALE) = inv;
+}
+
+// Operand of a K-vector by the warps of the block, one super-block per warp:
+// the int8 planes into op8 and, when opw is set, the fp16 planes into opw.
+__device__ __forceinline__ void build_op_rows(const float *__restrict__ x, int K, uint8_t *__restrict__ op8,
+                                              uint8_t *__restrict__ opw, int style) {
     const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    for (int sb = threadIdx.x >> 5; sb < K / MOE_QK; sb += nw)
-        build_op_sb(x + (size_t)sb * MOE_QK, op + (size_t)sb * OPB_SB, style, lane);
+    for (int sb = threadIdx.x >> 5; sb < K / MOE_QK; sb += nw) {
+        if (op8) build_op_sb(x + (size_t)sb * MOE_QK, op8 + (size_t)sb * OPB_SB, style, lane);
+        if (opw) build_opw_sb(x + (size_t)sb * MOE_QK, opw + (size_t)sb * OPW_SB, style, lane);
+    }
 }
 
 // ===========================================================================
@@ -633,7 +695,7 @@ __device__ void build_plan_block(const RouteArgs &a) {
         int v[3] = {0, 0, 0};
         if (e < NE) {
             v[0] = cnt[e];
-            v[1] = (cnt[e] + MOE_TC - 1) / MOE_TC;
+            v[1] = moe_n_chunks(cnt[e]);
             v[2] = (e < E && cnt[e] > 0) ? 1 : 0;
         }
         int inc[3];
@@ -703,11 +765,14 @@ __device__ void build_plan_block(const RouteArgs &a) {
     }
     for (int e = threadIdx.x; e < NE; e += blockDim.x) {
         const int n = cnt[e];
-        for (int c = 0; c * MOE_TC < n; c++) {
+        const int nc = moe_n_chunks(n);
+        for (int c = 0; c < nc; c++) {
+            int start, ntf;
+            moe_chunk(n, c, start, ntf);
             const int ci = coff[e] + c;
             a.plan.chunk_expert[ci] = e;
-            a.plan.chunk_pair0[ci] = off[e] + c * MOE_TC;
-            a.plan.chunk_ntok[ci] = min(MOE_TC, n - c * MOE_TC);
+            a.plan.chunk_pair0[ci] = off[e] + start;
+            a.plan.chunk_ntok[ci] = ntf;
         }
     }
 }
@@ -814,9 +879,12 @@ __global__ void __launch_bounds__(256) k_route_plan(RouteArgs a) {
         const int nbh = a.d.H / MOE_QK;
         const int item = ((int)blockIdx.x - a.T) * (blockDim.x >> 5) + (threadIdx.x >> 5);
         if (item < a.T * nbh) {
+            // both forms of the token's super-block (the expert GEMVs pick one per chunk)
             const int tk = item / nbh, sb = item % nbh;
-            build_op_sb(a.x + (size_t)tk * a.d.H + (size_t)sb * MOE_QK,
-                        a.xop + (size_t)tk * op_bytes(a.d.H) + (size_t)sb * OPB_SB, 4, threadIdx.x & 31);
+            const float *xs = a.x + (size_t)tk * a.d.H + (size_t)sb * MOE_QK;
+            uint8_t *row = a.xop + (size_t)tk * opx_row(a.d.H);
+            build_op_sb(xs, row + (size_t)sb * OPB_SB, 4, threadIdx.x & 31);
+            build_opw_sb(xs, row + op_bytes(a.d.H) + (size_t)sb * OPW_SB, 4, threadIdx.x & 31);
         }
         route_plan_finish(a, is_last);
         return;
@@ -916,27 +984,40 @@ void moe_launch_route_and_plan(const MoeDims &d, const float *part, int n_split,
 // ===========================================================================
 // down operand: per pair, scale + operand of the expert's down type
 // ===========================================================================
+// Per chunk: the int8 planes, or the fp16 planes for a chunk the down GEMV
+// runs on its fp16 path; one super-block of one pair per warp.  Pair rows
+// are opw_bytes(I) apart (the larger of the two forms).
 __global__ void __launch_bounds__(256) k_prep_down(MoeDims d, MoeLayerDev L, MoePlan plan,
                                                    const float *__restrict__ act, uint8_t *__restrict__ dop) {
     moe_pdl_wait();
     moe_pdl_trigger();
-    const int n_pairs = plan.counts[0];
-    const size_t opst = op_bytes(d.I);
-    for (int p = blockIdx.x; p < n_pairs; p += gridDim.x) {
-        const int e = plan.pair_expert[p];
-        const int ty = (e == d.E) ? L.sh_down_type : L.down_type;
-        build_op_rows(act + (size_t)p * d.I, d.I, dop + (size_t)p * opst, ty == 14 ? 6 : 4);
+    const int n_chunks = plan.counts[1];
+    const size_t opst = opw_bytes(d.I);
+    const int nb = d.I / MOE_QK, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    for (int c = blockIdx.x; c < n_chunks; c += gridDim.x) {
+        const int e = plan.chunk_expert[c], p0 = plan.chunk_pair0[c], v = plan.chunk_ntok[c];
+        const int style = ((e == d.E) ? L.sh_down_type : L.down_type) == 14 ? 6 : 4;
+        const bool wide = (v & MOE_CHUNK_WIDE) != 0;
+        for (int task = threadIdx.x >> 5; task < MOE_CHUNK_NTOK(v) * nb; task += nw) {
+            const int p = p0 + task / nb, sb = task % nb;
+            const float *x = act + (size_t)p * d.I + (size_t)sb * MOE_QK;
+            uint8_t *o = dop + (size_t)p * opst;
+            if (wide) build_opw_sb(x, o + (size_t)sb * OPW_SB, style, lane);
+            else build_op_sb(x, o + (size_t)sb * OPB_SB, style, lane);
+        }
     }
 }
 
-// Q4_K operand of activation rows: rows [0, R) come from `recv` (skipped when
-// their metadata says the slot is empty), rows [R, R + T) from `local`.
+// Q4_K operand rows (both forms, opx_row(H) apart) of activation rows: rows
+// [0, R) come from `recv` (skipped when their metadata says the slot is
+// empty), rows [R, R + T) from `local`.
 __global__ void __launch_bounds__(256) k_prep_rows(const float *__restrict__ recv, const int *__restrict__ meta,
                                                    int meta_w, int R, const float *__restrict__ local, int H,
                                                    uint8_t *__restrict__ xop) {
     const int r = blockIdx.x;
     if (r < R && !meta[(size_t)r * meta_w]) return;
-    build_op_rows(r < R ? recv + (size_t)r * H : local + (size_t)(r - R) * H, H, xop + (size_t)r * op_bytes(H), 4);
+    uint8_t *row = xop + (size_t)r * opx_row(H);
+    build_op_rows(r < R ? recv + (size_t)r * H : local + (size_t)(r - R) * H, H, row, row + op_bytes(H), 4);
 }
 
 void moe_launch_prep_rows(const float *recv, const int *meta, int meta_w, int R, const float *local, int T, int H,
@@ -947,7 +1028,7 @@ void moe_launch_prep_rows(const float *recv, const int *meta, int meta_w, int R,
 
 void moe_launch_prep_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const float *act,
                           uint8_t *dop, int max_pairs, cudaStream_t s, uint64_t *launches) {
-    int grid = max_pairs;
+    int grid = max_pairs;  // bounds the chunk count too
     if (grid > num_sms() * 4) grid = num_sms() * 4;
     if (grid < 1) grid = 1;
     moe_launch_pdl(k_prep_down, dim3(grid), dim3(256), 0, s, d, L, plan, act, dop);

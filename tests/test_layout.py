@@ -1,7 +1,7 @@
 """CPU: the operand and repack maps of moe_common.cuh, and a lane-by-lane
 emulation of the tensor-core arithmetic of the expert kernels
-(moe_experts.cu: q4_stage, q6_stage, planes_to_vector) against the
-quant.c dequantization, so that a fragment-layout or decode error shows up
+(moe_experts.cu: q4_stage, q6_stage, planes_to_vector on the int8 path;
+q4w_stage, q6w_stage on the fp16 path) against the quant.c dequantization, so that a fragment-layout or decode error shows up
 without a GPU.  The maps come from a host build of the same header; the MMA
 fragment layouts are those of the PTX ISA for mma.m16n8k32 / m16n8k16."""
 import os
@@ -26,8 +26,10 @@ def tables():
         if not line:
             continue
         f = line.split()
-        if f[0] in ("opq4", "opq6", "xsum", "q4r", "q6r"):
+        if f[0] in ("opq4", "opq6", "xsum", "q4r", "q6r", "opw4", "opw6"):
             t[f[0]][int(f[1])] = int(f[2])
+        elif f[0] == "opw":
+            t["opw"] = tuple(map(int, f[1:]))
         elif f[0] == "sizes":
             t["sizes"] = tuple(map(int, f[1:]))
         elif f[0] == "f2h":
@@ -432,3 +434,201 @@ def test_prefill_q6_dequant_emulation(tables, oracle):
                             v[2 * reg + i] = hfma(vq, fh, f16(vq * fl))
             out[r, 64 * A:64 * A + 64] = v
     check_fp16_dequant(out, ref, 0.5)   # correctly rounded: one rounding of (q - 32) * d * sc
+
+
+
+# ---------------------------------------------------------------------------
+# fp16 path of the expert GEMVs (moe_experts.cu: q4w_stage, q6w_stage; the
+# operand of moe_kernels.cu: build_opw_sb), lane by lane with single fp16
+# roundings, on two 4-token tiles.
+
+def test_wide_operand_maps(tables):
+    sb, xsum, scale, lo, top = tables["opw"]
+    assert (sb, xsum, scale, lo, top) == (1088, 512, 544, 576, 15)
+    assert lo % 128 == 64 and sb % 16 == 0  # planes' quarter-warp loads on distinct banks; bulk-copy size
+    for name in ("opw4", "opw6"):
+        assert sorted(tables[name].values()) == list(range(256))
+    for k in range(256):  # style Q4: lane t = (k / 8) % 4 of sub-block k / 32 owns 8 contiguous fp16
+        j, t, i = k >> 5, (k >> 3) & 3, k & 7
+        assert tables["opw4"][k] == 32 * j + 8 * t + [0, 2, 1, 3, 4, 6, 5, 7][i]
+        s, t6, i6 = k >> 4, (k >> 2) & 3, k & 3
+        assert tables["opw6"][k] == 32 * (s >> 1) + 8 * t6 + 4 * (s & 1) + i6
+
+
+def build_wide_operand(tables, xs, style):
+    """build_opw_sb for each vector of xs [n, 256]: bytes, and the exact
+    values (hi + lo) / s the MMAs see."""
+    ops, vals = [], []
+    for x in xs.astype(np.float32):
+        amax = float(np.max(np.abs(x)))
+        s = 2.0 ** (15 - np.frexp(amax)[1])
+        xsc = (x.astype(np.float64) * s).astype(np.float32)
+        hi = xsc.astype(np.float16)
+        lo = (xsc - hi.astype(np.float32)).astype(np.float16)
+        op = np.zeros(1088, np.uint8)
+        H = np.zeros(256, np.float16)
+        L = np.zeros(256, np.float16)
+        m = tables["opw4" if style == 4 else "opw6"]
+        for k in range(256):
+            H[m[k]], L[m[k]] = hi[k], lo[k]
+        op[0:512] = np.frombuffer(H.tobytes(), np.uint8)
+        op[576:1088] = np.frombuffer(L.tobytes(), np.uint8)
+        v = hi.astype(np.float32) + lo.astype(np.float32)   # exact
+        if style == 4:
+            for j in range(8):
+                lane_sums = [np.float32(0)] * 4
+                for t in range(4):   # each lane sums its 8 values in order, then xor 1, xor 2
+                    acc = np.float32(0)
+                    for i in range(8):
+                        acc = np.float32(acc + v[32 * j + 8 * t + i])
+                    lane_sums[t] = acc
+                a = [np.float32(lane_sums[t] + lane_sums[t ^ 1]) for t in range(4)]
+                tot = np.float32(a[0] + a[2])
+                s32 = np.float32(tot * np.float32(0.03125))
+                sh = np.float16(s32)
+                sl = np.float16(np.float32(s32 - np.float32(sh)))
+                op[512 + 2 * j:514 + 2 * j] = np.frombuffer(sh.tobytes(), np.uint8)
+                op[528 + 2 * j:530 + 2 * j] = np.frombuffer(sl.tobytes(), np.uint8)
+        op[544:548] = np.frombuffer(np.float32(1.0 / s).tobytes(), np.uint8)
+        ops.append(op)
+        vals.append(v.astype(np.float64) / s)
+    return np.concatenate(ops), np.stack(vals)
+
+
+def h2pair(a, b):
+    return int(np.array([a, b], np.float16).view(np.uint32)[0])
+
+
+def test_q4w_stage_emulation(tables, oracle):
+    rng = np.random.default_rng(17)
+    W = (rng.standard_normal((16, 256)) * 0.02).astype(np.float32)
+    blocks = oracle.quantize(W.reshape(-1), oracle.TYPE_Q4_K).reshape(16, 144)
+    wdq = oracle.dequant(blocks.reshape(-1), oracle.TYPE_Q4_K, 16 * 256).reshape(16, 256).astype(np.float64)
+    rep = blocks.copy()
+    for p, sidx in tables["q4r"].items():
+        rep[:, 16 + p] = blocks[:, 16 + sidx]
+    NTOK = 8
+    x = (rng.standard_normal((NTOK, 256)) * np.array([1, 1e-3, 50, 1, 1, 1, 1e-5, 3])[:, None]).astype(np.float32)
+    opnd, xv = build_wide_operand(tables, x, 4)
+
+    def sc_of(row, s):
+        sc_lo, sc_hi = header_words(rep[row])[:2]
+        return ((sc_lo if s < 4 else sc_hi) >> (8 * (s & 3))) & 0x3F
+
+    def dec(word, row, s, high):
+        # (w & mask) | 0x6400 pairs -> fma(1024 + v, c, n): q sc exactly
+        sc = sc_of(row, s)
+        m = 0x00F000F0 if high else 0x000F000F
+        u = (word & m) | 0x64006400
+        a, b = halves_of(u)
+        c, n = (sc / 16.0, -64.0 * sc) if high else (float(sc), -1024.0 * sc)
+        return h2pair(hfma(a, c, n), hfma(b, c, n))
+
+    out = np.zeros((16, NTOK))
+    for n_tile in range(NTOK // 4):
+        acc = [[0.0] * 4 for _ in range(32)]
+        for jj in range(4):
+            for step_hi in (0, 1):      # sub-block 2 jj (low nibbles), 2 jj + 1 (high)
+                for step in range(2):   # k16 steps: elements (0,2),(1,3) then (4,6),(5,7)
+                    a, b = {}, {}
+                    for lane in range(32):
+                        g, t = lane >> 2, lane & 3
+                        regs = []
+                        for row in (g, g + 8):
+                            w = w32(rep[row], 16 + 32 * t + 8 * jj + 4 * step)
+                            regs.append((dec(w, row, 2 * jj + step_hi, step_hi),
+                                         dec(w >> 8, row, 2 * jj + step_hi, step_hi)))
+                        a[lane] = [regs[0][0], regs[1][0], regs[0][1], regs[1][1]]
+                        tok = 4 * n_tile + (g >> 1)
+                        base = tok * 1088 + (g & 1) * 576 + 16 * t + 64 * (2 * jj + step_hi) + 8 * step
+                        b[lane] = [w32(opnd, base), w32(opnd, base + 4)]
+                    d = mma(a, b, 16, "f16")
+                    for lane in range(32):
+                        for q in range(4):
+                            acc[lane][q] += d[lane][q]
+        am, bm = {}, {}
+        for lane in range(32):
+            g, t = lane >> 2, lane & 3
+            mg, m8 = mins_words(rep[g]), mins_words(rep[g + 8])
+            am[lane] = [h2pair(mg[2 * t], mg[2 * t + 1]), h2pair(m8[2 * t], m8[2 * t + 1]), 0, 0]
+            tok = 4 * n_tile + (g >> 1)
+            bm[lane] = [w32(opnd, tok * 1088 + 512 + 16 * (g & 1) + 4 * t), 0]
+        mt = mma(am, bm, 16, "f16")
+        for lane in range(32):
+            g, t = lane >> 2, lane & 3
+            tok = 4 * n_tile + t
+            inv = float(np.frombuffer(bytes(opnd[tok * 1088 + 544:tok * 1088 + 548]), np.float32)[0])
+            for r, row in enumerate((g, g + 8)):
+                d_, dm = rep[row][:4].view(np.float16).astype(np.float64)
+                out[row, tok] = d_ * inv * (acc[lane][2 * r] + acc[lane][2 * r + 1]) \
+                    - 32 * dm * inv * (mt[lane][2 * r] + mt[lane][2 * r + 1])
+    ref = wdq @ x.astype(np.float64).T
+    for tk in range(NTOK):   # per token: the product of the exact weights with x, to the 22-bit split
+        err = np.max(np.abs(out[:, tk] - ref[:, tk])) / np.max(np.abs(ref[:, tk]))
+        assert err < 2e-6, (tk, err)
+
+
+def test_q6w_stage_emulation(tables, oracle):
+    rng = np.random.default_rng(18)
+    W = (rng.standard_normal((16, 256)) * 0.02).astype(np.float32)
+    W[3, :16] *= 40.0   # a sub-block with a large scale: |(q - 32) sc| beyond 2048 (residual MMA)
+    blocks = oracle.quantize(W.reshape(-1), oracle.TYPE_Q6_K).reshape(16, 210)
+    wdq = oracle.dequant(blocks.reshape(-1), oracle.TYPE_Q6_K, 16 * 256).reshape(16, 256).astype(np.float64)
+    Q = np.zeros((16, 192), np.uint8)
+    for p, sidx in tables["q6r"].items():
+        Q[:, p] = blocks[:, sidx] ^ (0xAA if sidx >= 128 else 0)
+    S = blocks[:, 192:208].view(np.int8).astype(int)
+    D = blocks[:, 208:210].copy().view(np.float16).astype(np.float64)[:, 0]
+    NTOK = 8
+    x = (rng.standard_normal((NTOK, 256)) * np.array([1, 1e-3, 50, 1, 1, 1, 1e-5, 3])[:, None]).astype(np.float32)
+    opnd, xv = build_wide_operand(tables, x, 6)
+    big = 0
+
+    def dec(Wq, Hq, sp, sc):
+        nonlocal big
+        nib = (Wq if sp < 4 else Wq >> 4) & 0x0F0F0F0F
+        f = sp >> 1
+        hb = ((Hq << (4 - 2 * f)) if 2 * f <= 4 else (Hq >> (2 * f - 4))) & 0x30303030
+        q6 = nib | (hb ^ 0x20202020)
+        P, R = [], []
+        for sel in (0x4140, 0x4342):
+            qa, qb = [h - 1056.0 for h in halves_of(byte_perm(q6, 0x64, sel))]
+            p_ = [f16(qa * sc), f16(qb * sc)]
+            r_ = [hfma(qa, sc, -p_[0]), hfma(qb, sc, -p_[1])]
+            big += sum(1 for v in r_ if v != 0)
+            P.append(h2pair(*p_))
+            R.append(h2pair(*r_))
+        return P, R
+
+    out = np.zeros((16, NTOK))
+    for n_tile in range(NTOK // 4):
+        acc = [[0.0] * 4 for _ in range(32)]
+        for s in range(16):
+            h, sp = s >> 3, s & 7
+            aP, aR, b = {}, {}, {}
+            for lane in range(32):
+                g, t = lane >> 2, lane & 3
+                rg = []
+                for row in (g, g + 8):
+                    wq = [w32(Q[row], 48 * t + 24 * h + 4 * i) for i in range(6)]
+                    rg.append(dec(wq[sp & 3], wq[4 + (sp & 1)], sp, float(S[row, s])))
+                aP[lane] = [rg[0][0][0], rg[1][0][0], rg[0][0][1], rg[1][0][1]]
+                aR[lane] = [rg[0][1][0], rg[1][1][0], rg[0][1][1], rg[1][1][1]]
+                tok = 4 * n_tile + (g >> 1)
+                base = tok * 1088 + (g & 1) * 576 + 16 * t + 64 * (s >> 1) + 8 * (s & 1)
+                b[lane] = [w32(opnd, base), w32(opnd, base + 4)]
+            for d in (mma(aP, b, 16, "f16"), mma(aR, b, 16, "f16")):
+                for lane in range(32):
+                    for q in range(4):
+                        acc[lane][q] += d[lane][q]
+        for lane in range(32):
+            g, t = lane >> 2, lane & 3
+            tok = 4 * n_tile + t
+            inv = float(np.frombuffer(bytes(opnd[tok * 1088 + 544:tok * 1088 + 548]), np.float32)[0])
+            for r, row in enumerate((g, g + 8)):
+                out[row, tok] = D[row] * inv * (acc[lane][2 * r] + acc[lane][2 * r + 1])
+    assert big > 0   # the residual MMA carried something
+    ref = wdq @ x.astype(np.float64).T
+    for tk in range(NTOK):
+        err = np.max(np.abs(out[:, tk] - ref[:, tk])) / np.max(np.abs(ref[:, tk]))
+        assert err < 2e-6, (tk, err)
