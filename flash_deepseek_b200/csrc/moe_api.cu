@@ -209,17 +209,18 @@ static int ctx_alloc(moe_ctx *c) {
     CK(dmalloc(&c->xop, (size_t)RT * opx_row(H)));
     CK(cudaMemset(c->xop, 0, (size_t)RT * opx_row(H)));
     const int P = c->max_pairs;
-    CK(dmalloc(&c->plan.counts, 4));
+    CK(dmalloc(&c->plan.counts, MOE_PLAN_COUNTS));
     CK(dmalloc(&c->plan.pair_expert, P));
     CK(dmalloc(&c->plan.pair_token, P));
     CK(dmalloc(&c->plan.pair_w, P));
     CK(dmalloc(&c->plan.chunk_expert, P));
     CK(dmalloc(&c->plan.chunk_pair0, P));
     CK(dmalloc(&c->plan.chunk_ntok, P));
+    CK(dmalloc(&c->plan.chunk_order, P));
     CK(dmalloc(&c->plan.slot_pair, (size_t)RT * (K + 1)));
     CK(dmalloc(&c->plan.error, 1));
     CK(cudaMemset(c->plan.error, 0, sizeof(int)));
-    CK(cudaMemset(c->plan.counts, 0, 4 * sizeof(int)));
+    CK(cudaMemset(c->plan.counts, 0, MOE_PLAN_COUNTS * sizeof(int)));
     CK(dmalloc(&c->counter, 1));
     CK(cudaMemset(c->counter, 0, sizeof(int)));
     CK(dmalloc(&c->act, (size_t)P * I));
@@ -409,7 +410,7 @@ void moe_destroy(moe_ctx *c) {
     }
     void *bufs[] = {c->part, c->logits, c->rl_counters, c->d_in, c->d_out, c->h_post, c->idx, c->wts, c->idx_given, c->w_given, c->bias_tmp, c->xop, c->plan.counts,
                     c->plan.pair_expert, c->plan.pair_token, c->plan.pair_w, c->plan.chunk_expert,
-                    c->plan.chunk_pair0, c->plan.chunk_ntok, c->plan.slot_pair, c->plan.error, c->counter, c->act,
+                    c->plan.chunk_pair0, c->plan.chunk_ntok, c->plan.chunk_order, c->plan.slot_pair, c->plan.error, c->counter, c->act,
                     c->dop, c->eo, c->send_x, c->recv_x, c->send_y, c->recv_y, c->send_meta,
                     c->recv_meta, c->rows_partial, c->tok_slot};
     for (void *b : bufs) cudaFree(b);

@@ -177,14 +177,16 @@ __global__ void __launch_bounds__(512) k_ep_plan(MoeDims d, const int *__restric
         const int n = cnt[e];
         const int nc = moe_n_chunks(n);
         for (int c = 0; c < nc; c++) {
-            int start, ntf;
-            moe_chunk(n, c, start, ntf);
+            int start, nt;
+            moe_chunk(n, c, start, nt);
             const int ci = coff[e] + c;
             plan.chunk_expert[ci] = e;
             plan.chunk_pair0[ci] = off[e] + start;
-            plan.chunk_ntok[ci] = ntf;
+            plan.chunk_ntok[ci] = nt;
         }
     }
+    __syncthreads();
+    moe_plan_order_chunks(plan, carry[1]);
 }
 
 // Pre-combine on the expert side: partial[r] = sum over the slots of received

@@ -183,17 +183,17 @@ __device__ __forceinline__ uint32_t byte_h2(uint32_t w, uint32_t minus) {
 
 struct ExItem {
     int rg, e, slot, p0, ntok;
-    bool wide;  // MOE_CHUNK_WIDE: the expert's tokens span several chunks
 };
-__device__ __forceinline__ void ex_item(const MoePlan &plan, const MoeLayerDev &L, int E, int n_chunks, int item,
+// Work item `item` = (chunk chunk_order[item / n_rg], row group item % n_rg):
+// the row groups of one chunk are consecutive items, and the chunks with
+// the most tokens come first.
+__device__ __forceinline__ void ex_item(const MoePlan &plan, const MoeLayerDev &L, int E, int n_rg, int item,
                                         ExItem &it) {
-    const int c = item % n_chunks;
-    it.rg = item / n_chunks;
+    const int c = plan.chunk_order[item / n_rg];
+    it.rg = item % n_rg;
     it.e = plan.chunk_expert[c];
     it.p0 = plan.chunk_pair0[c];
-    const int v = plan.chunk_ntok[c];
-    it.ntok = MOE_CHUNK_NTOK(v);
-    it.wide = (v & MOE_CHUNK_WIDE) != 0;
+    it.ntok = plan.chunk_ntok[c];
     it.slot = it.e == E ? L.n_local : it.e - L.e0;
 }
 
@@ -619,6 +619,7 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
              float *__restrict__ act) {
     extern __shared__ uint8_t ex_raw[];
     __shared__ __align__(8) uint64_t full[GU_NS], empty[GU_NS];
+    __shared__ int stage_item[GU_NS];  // item whose first super-block the stage holds; -1: no more items
     uint8_t *sm = align128(ex_raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int NB = d.H / MOE_QK;
@@ -632,17 +633,30 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
     __syncthreads();
     moe_pdl_wait();  // the plan and the operand come from the previous kernels
     moe_pdl_trigger();
-    const int n_chunks = plan.counts[1];
-    const int n_items = n_chunks * (d.I / GU_ROWS);
+    const int n_rg = d.I / GU_ROWS;
+    const int n_items = plan.counts[1] * n_rg;
     uint32_t seq = 0;
-    if (warp == EX_CONSUMERS) {  // producer
+    if (warp == EX_CONSUMERS) {  // producer: takes items from the plan's counter
         const size_t rowst = opx_row(d.H), wide_off = op_bytes(d.H);
         bool ok = true;
-        for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+        for (;;) {
+            int item = 0;
+            if (lane == 0) item = atomicAdd(&plan.counts[4], 1);
+            item = __shfl_sync(0xffffffffu, item, 0);
+            if (item >= n_items) {  // end marker for the consumers
+                const int st = seq % GU_NS;
+                if (!mbar_wait(&empty[st], ((seq / GU_NS) & 1) ^ 1)) { ok = false; break; }
+                if (lane == 0) {
+                    stage_item[st] = -1;
+                    mbar_arrive(&full[st]);
+                }
+                seq++;
+                break;
+            }
             ExItem it;
-            ex_item(plan, L, d.E, n_chunks, item, it);
-            // the chunk's operand form: fp16 planes for >= MOE_GU_WIDE_MIN tokens
-            const bool fp = it.ntok >= MOE_GU_WIDE_MIN;
+            ex_item(plan, L, d.E, n_rg, item, it);
+            // the chunk's operand form: fp16 planes on the fp16 path
+            const bool fp = moe_gu_wide(it.ntok);
             const uint32_t osb = fp ? OPW_SB : OPB_SB;
             const uint8_t *src = lane < it.ntok ? xop + (size_t)plan.pair_token[it.p0 + lane] * rowst +
                                                       (fp ? wide_off : 0)
@@ -652,6 +666,7 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
                 if (!mbar_wait(&empty[st], ((seq / GU_NS) & 1) ^ 1)) { ok = false; break; }
                 uint8_t *stage = sm + (size_t)st * GU_STAGE;
                 if (lane == 0) {
+                    if (sb == 0) stage_item[st] = item;
                     mbar_expect_tx(&full[st], 2 * GU_WBOX + it.ntok * osb);
                     tma_load_3d(stage, &L.tm_gu, sb * MOE_Q4K_BYTES, it.rg * GU_ROWS, it.slot, &full[st]);
                     tma_load_3d(stage + GU_WBOX, &L.tm_gu, sb * MOE_Q4K_BYTES, d.I + it.rg * GU_ROWS, it.slot,
@@ -660,6 +675,7 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
                 __syncwarp();
                 if (lane < it.ntok) bulk_load(stage + 2 * GU_WBOX + lane * osb, src + (size_t)sb * osb, osb, &full[st]);
             }
+            if (!ok) break;
         }
         if (!ok && lane == 0) atomicExch(plan.error, EX_ERR_TIMEOUT);
         // the copies of the last stages must land before the CTA leaves
@@ -667,11 +683,18 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
             if (!mbar_wait(&full[k % GU_NS], (k / GU_NS) & 1)) break;
         return;
     }
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+    for (;;) {  // consumers: the items in the producer's order
+        const int st = seq % GU_NS;
+        if (!mbar_wait(&full[st], (seq / GU_NS) & 1)) {
+            if (lane == 0) atomicExch(plan.error, EX_ERR_TIMEOUT);
+            return;
+        }
+        const int item = stage_item[st];
+        if (item < 0) return;
         ExItem it;
-        ex_item(plan, L, d.E, n_chunks, item, it);
+        ex_item(plan, L, d.E, n_rg, item, it);
         bool ok;
-        if (it.ntok >= MOE_GU_WIDE_MIN) {
+        if (moe_gu_wide(it.ntok)) {
             switch ((it.ntok + 3) >> 2) {
                 case 2: ok = gu_item_w<2>(d, act, it, NB, sm, full, empty, seq, warp, lane); break;
                 case 3: ok = gu_item_w<3>(d, act, it, NB, sm, full, empty, seq, warp, lane); break;
@@ -680,7 +703,8 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
         } else {
             switch ((it.ntok + 1) >> 1) {
                 case 1: ok = gu_item<1>(d, plan, act, it, NB, sm, full, empty, seq, warp, lane); break;
-                default: ok = gu_item<2>(d, plan, act, it, NB, sm, full, empty, seq, warp, lane); break;
+                case 2: ok = gu_item<2>(d, plan, act, it, NB, sm, full, empty, seq, warp, lane); break;
+                default: ok = gu_item<3>(d, plan, act, it, NB, sm, full, empty, seq, warp, lane); break;
             }
         }
         if (!ok) {
@@ -735,7 +759,7 @@ __device__ __forceinline__ bool dn_item(const MoeDims &d, float *__restrict__ eo
     return true;
 }
 
-// fp16-path down item (chunks marked MOE_CHUNK_WIDE)
+// fp16-path down item (chunks of more than MOE_TC tokens)
 template <int NT, int TY>
 __device__ __forceinline__ bool dn_item_w(const MoeDims &d, float *__restrict__ eo, const ExItem &it, int NB,
                                           int nbp, uint8_t *sm, const uint8_t *dbuf, uint64_t *full, uint64_t *empty,
@@ -783,6 +807,7 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
     constexpr int STAGE = TY == MOE_TYPE_Q6_K ? DN6_STAGE : DN4_STAGE;
     extern __shared__ uint8_t ex_raw[];
     __shared__ __align__(8) uint64_t full[NS], empty[NS];
+    __shared__ int stage_item[NS];  // item whose first super-block the stage holds; -1: no more items
     uint8_t *sm = align128(ex_raw);
     const int NB = d.I / MOE_QK, nbp = q6r_nb_pad(NB);
     const int dbytes = DN_ROWS * 2 * nbp;  // per item (Q6_K d plane)
@@ -802,17 +827,17 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
     // their operand copies after it.  The consumers only read shared memory
     // behind the full barriers.
     moe_pdl_trigger();
-    const int n_chunks = plan.counts[1];
-    const int n_items = n_chunks * (d.H / DN_ROWS);
+    const int n_rg = d.H / DN_ROWS;
+    const int n_items = plan.counts[1] * n_rg;
+    int *counter = &plan.counts[TY == MOE_TYPE_Q6_K ? 5 : 6];
     uint32_t seq = 0, nitem = 0;
-    if (warp == EX_CONSUMERS) {  // producer
+    if (warp == EX_CONSUMERS) {  // producer: takes items from the plan's counter
         const size_t opst = opw_bytes(d.I);  // pair rows of the down operand
         bool ok = true, waited = false;
         int ndef = 0, def_st[NS], def_p0[NS], def_nt[NS], def_sb[NS];
-        bool def_fp[NS];
-        auto issue_ops = [&](int st, int p0, int ntok, int sb, bool fp) {
+        auto issue_ops = [&](int st, int p0, int ntok, int sb) {
             if (lane < ntok) {
-                const uint32_t osb = fp ? OPW_SB : OPB_SB;
+                const uint32_t osb = moe_dn_wide(ntok) ? OPW_SB : OPB_SB;
                 uint8_t *od = sm + (size_t)st * STAGE + (TY == MOE_TYPE_Q6_K ? DN6_QBOX + DN6_SBOX : DN4_WBOX) +
                               lane * osb;
                 bulk_load(od, dop + (size_t)(p0 + lane) * opst + (size_t)sb * osb, osb, &full[st]);
@@ -821,21 +846,35 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
         auto flush_deferred = [&]() {
             moe_pdl_wait();
             waited = true;
-            for (int k = 0; k < ndef; k++) issue_ops(def_st[k], def_p0[k], def_nt[k], def_sb[k], def_fp[k]);
+            for (int k = 0; k < ndef; k++) issue_ops(def_st[k], def_p0[k], def_nt[k], def_sb[k]);
             ndef = 0;
         };
-        for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+        for (;;) {
+            int item = 0;
+            if (lane == 0) item = atomicAdd(counter, 1);
+            item = __shfl_sync(0xffffffffu, item, 0);
+            if (item >= n_items) {  // end marker for the consumers
+                const int st = seq % NS;
+                if (!mbar_wait(&empty[st], ((seq / NS) & 1) ^ 1)) { ok = false; break; }
+                if (lane == 0) {
+                    stage_item[st] = -1;
+                    mbar_arrive(&full[st]);
+                }
+                seq++;
+                break;
+            }
             ExItem it;
-            ex_item(plan, L, d.E, n_chunks, item, it);
+            ex_item(plan, L, d.E, n_rg, item, it);
             if (((it.e == d.E) ? L.sh_down_type : L.down_type) != TY) continue;
             uint8_t *dbuf = dbuf0 + (size_t)(nitem & 1) * dbytes;
             nitem++;
+            const uint32_t osb = moe_dn_wide(it.ntok) ? OPW_SB : OPB_SB;
             for (int sb = 0; sb < NB; sb++, seq++) {
                 const int st = seq % NS;
                 if (!mbar_wait(&empty[st], ((seq / NS) & 1) ^ 1)) { ok = false; break; }
                 uint8_t *stage = sm + (size_t)st * STAGE;
-                const uint32_t osb = it.wide ? OPW_SB : OPB_SB;
                 if (lane == 0) {
+                    if (sb == 0) stage_item[st] = item;
                     const int y = it.rg * DN_ROWS;
                     if (TY == MOE_TYPE_Q6_K) {
                         mbar_expect_tx(&full[st], DN6_QBOX + DN6_SBOX + it.ntok * osb + (sb == 0 ? dbytes : 0));
@@ -849,13 +888,13 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
                 }
                 __syncwarp();
                 if (waited) {
-                    issue_ops(st, it.p0, it.ntok, sb, it.wide);
+                    issue_ops(st, it.p0, it.ntok, sb);
                 } else {
                     def_st[ndef] = st; def_p0[ndef] = it.p0; def_nt[ndef] = it.ntok; def_sb[ndef] = sb;
-                    def_fp[ndef] = it.wide;
                     if (++ndef == NS) flush_deferred();
                 }
             }
+            if (!ok) break;
         }
         if (!waited) flush_deferred();
         if (!ok && lane == 0) atomicExch(plan.error, EX_ERR_TIMEOUT);
@@ -864,17 +903,21 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
         return;
     }
     moe_pdl_wait();
-    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+    for (;;) {  // consumers: the items in the producer's order
+        const int st = seq % NS;
+        if (!mbar_wait(&full[st], (seq / NS) & 1)) {
+            if (lane == 0) atomicExch(plan.error, EX_ERR_TIMEOUT);
+            return;
+        }
+        const int item = stage_item[st];
+        if (item < 0) return;
         ExItem it;
-        ex_item(plan, L, d.E, n_chunks, item, it);
-        if (((it.e == d.E) ? L.sh_down_type : L.down_type) != TY) continue;
+        ex_item(plan, L, d.E, n_rg, item, it);
         const uint8_t *dbuf = dbuf0 + (size_t)(nitem & 1) * dbytes;
         nitem++;
         bool ok;
-        if (it.wide) {
+        if (moe_dn_wide(it.ntok)) {
             switch ((it.ntok + 3) >> 2) {
-                case 1: ok = dn_item_w<1, TY>(d, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
-                case 2: ok = dn_item_w<2, TY>(d, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
                 case 3: ok = dn_item_w<3, TY>(d, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
                 default: ok = dn_item_w<4, TY>(d, eo, it, NB, nbp, sm, dbuf, full, empty, seq, warp, lane); break;
             }

@@ -7,16 +7,17 @@
 #include <stdint.h>
 
 // Dispatch plan of one forward step on one GPU: (token, expert) pairs grouped
-// by expert, and chunks of at most `tc` tokens of one expert (the unit of
-// work of the expert kernels).
+// by expert, and chunks of one expert's tokens (the unit of work of the
+// expert kernels).
 struct MoePlan {
-    int *counts;        // [4]: n_pairs, n_chunks, routed experts hit, spare
+    int *counts;        // [MOE_PLAN_COUNTS]: n_pairs, n_chunks, routed experts hit, -, work counters
     int *pair_expert;   // [max_pairs]  global expert id (n_experts = shared)
     int *pair_token;    // [max_pairs]  row of the activation operand
     float *pair_w;      // [max_pairs]  routing weight (1 for the shared expert)
     int *chunk_expert;  // [max_pairs]
     int *chunk_pair0;   // [max_pairs]
     int *chunk_ntok;    // [max_pairs]
+    int *chunk_order;   // [max_pairs] chunk ids, most tokens first (decode plans only)
     int *slot_pair;     // [max_tokens][K+1] pair of (token, slot); slot K = shared
     int *error;         // [1] set to a non-zero code by device-side checks
 };
@@ -96,30 +97,63 @@ inline void moe_smem_limit(F *kernel, size_t bytes, size_t (&done)[MOE_MAX_DEVIC
 
 // Chunks of an expert's tokens (the unit of work of the expert GEMVs).  An
 // expert with at most MOE_TC tokens is one chunk; a busier one is split into
-// ceil(n / MOE_WIDE_TC) chunks of nearly equal size, each marked with
-// MOE_CHUNK_WIDE in chunk_ntok (the low 16 bits hold the token count).  The
-// gate/up GEMV runs a chunk on the fp16 path when it has at least
-// MOE_GU_WIDE_MIN tokens, the down GEMV when it is marked wide; otherwise on
-// the int8-plane path.
+// chunks of MOE_WIDE_TC tokens and one chunk of the remainder.  The gate/up
+// GEMV runs a chunk on the fp16 path when it has at least MOE_GU_WIDE_MIN
+// tokens, the down GEMV when it has more than MOE_TC (the int8-plane path
+// otherwise).  The GEMVs take their work items from a counter in the plan,
+// chunks in the order chunk_order (most tokens first).
 #define MOE_TC 8           // tokens of an int8-path chunk (four 8-column tiles of 2 tokens x 3 planes)
 #define MOE_WIDE_TC 16     // tokens of an fp16-path chunk (four 8-column tiles of 4 tokens x 2 planes)
-#define MOE_GU_WIDE_MIN 5
-#define MOE_CHUNK_WIDE (1 << 16)
-#define MOE_CHUNK_NTOK(v) ((v) & 0xFFFF)
+#define MOE_GU_WIDE_MIN 7
+__host__ __device__ __forceinline__ bool moe_gu_wide(int ntok) { return ntok >= MOE_GU_WIDE_MIN; }
+__host__ __device__ __forceinline__ bool moe_dn_wide(int ntok) { return ntok > MOE_TC; }
 __host__ __device__ __forceinline__ int moe_n_chunks(int n) {
     return n <= 0 ? 0 : n <= MOE_TC ? 1 : (n + MOE_WIDE_TC - 1) / MOE_WIDE_TC;
 }
-// chunk c of an expert with n tokens: first token (relative) and chunk_ntok value
-__host__ __device__ __forceinline__ void moe_chunk(int n, int c, int &start, int &ntok_flags) {
+// chunk c of an expert with n tokens: first token (relative) and token count
+__host__ __device__ __forceinline__ void moe_chunk(int n, int c, int &start, int &ntok) {
     if (n <= MOE_TC) {
         start = 0;
-        ntok_flags = n;
+        ntok = n;
         return;
     }
-    const int nc = (n + MOE_WIDE_TC - 1) / MOE_WIDE_TC, q = n / nc, r = n % nc;
-    start = c * q + (c < r ? c : r);
-    ntok_flags = (q + (c < r ? 1 : 0)) | MOE_CHUNK_WIDE;
+    start = c * MOE_WIDE_TC;
+    ntok = n - start < MOE_WIDE_TC ? n - start : MOE_WIDE_TC;
 }
+// plan.counts: [0] pairs, [1] chunks, [2] routed experts hit, [4] gate/up,
+// [5] Q6_K down, [6] Q4_K down work counters (zeroed by the plan builder)
+#define MOE_PLAN_COUNTS 8
+
+#ifdef __CUDACC__
+// Block-wide, after the block has written the plan's n_chunks chunks:
+// chunk_order = chunk ids grouped by token count, most tokens first (so the
+// GEMVs start the long items first and finish on short ones), and the work
+// counters zeroed.  Every thread of the block calls it.
+__device__ __forceinline__ void moe_plan_order_chunks(const MoePlan &plan, int n_chunks) {
+    __shared__ int bucket[MOE_WIDE_TC + 1];
+    for (int i = threadIdx.x; i <= MOE_WIDE_TC; i += blockDim.x) bucket[i] = 0;
+    __syncthreads();
+    for (int c = threadIdx.x; c < n_chunks; c += blockDim.x) {
+        const int k = plan.chunk_ntok[c];
+        atomicAdd(&bucket[k < MOE_WIDE_TC ? k : MOE_WIDE_TC], 1);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int acc = 0;
+        for (int k = MOE_WIDE_TC; k >= 0; k--) {
+            const int v = bucket[k];
+            bucket[k] = acc;
+            acc += v;
+        }
+        for (int i = 4; i < MOE_PLAN_COUNTS; i++) plan.counts[i] = 0;
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < n_chunks; c += blockDim.x) {
+        const int k = plan.chunk_ntok[c];
+        plan.chunk_order[atomicAdd(&bucket[k < MOE_WIDE_TC ? k : MOE_WIDE_TC], 1)] = c;
+    }
+}
+#endif
 
 // ---- launchers (moe_kernels.cu); every one counts its kernel launches ------
 extern "C++" {

@@ -767,14 +767,16 @@ __device__ void build_plan_block(const RouteArgs &a) {
         const int n = cnt[e];
         const int nc = moe_n_chunks(n);
         for (int c = 0; c < nc; c++) {
-            int start, ntf;
-            moe_chunk(n, c, start, ntf);
+            int start, nt;
+            moe_chunk(n, c, start, nt);
             const int ci = coff[e] + c;
             a.plan.chunk_expert[ci] = e;
             a.plan.chunk_pair0[ci] = off[e] + start;
-            a.plan.chunk_ntok[ci] = ntf;
+            a.plan.chunk_ntok[ci] = nt;
         }
     }
+    __syncthreads();
+    moe_plan_order_chunks(a.plan, coff[NE]);
 }
 
 // Top groups by repeated argmax, the lowest index winning ties and only
@@ -984,9 +986,10 @@ void moe_launch_route_and_plan(const MoeDims &d, const float *part, int n_split,
 // ===========================================================================
 // down operand: per pair, scale + operand of the expert's down type
 // ===========================================================================
-// Per chunk: the int8 planes, or the fp16 planes for a chunk the down GEMV
-// runs on its fp16 path; one super-block of one pair per warp.  Pair rows
-// are opw_bytes(I) apart (the larger of the two forms).
+// The down operand of every pair: the int8 planes, or the fp16 planes when
+// the pair's chunk runs on the down GEMV's fp16 path.  One super-block of
+// one pair per warp; tasks (chunk, pair slot, super-block) are spread over
+// the whole grid.  Pair rows are opw_bytes(I) apart (the larger form).
 __global__ void __launch_bounds__(256) k_prep_down(MoeDims d, MoeLayerDev L, MoePlan plan,
                                                    const float *__restrict__ act, uint8_t *__restrict__ dop) {
     moe_pdl_wait();
@@ -994,17 +997,17 @@ __global__ void __launch_bounds__(256) k_prep_down(MoeDims d, MoeLayerDev L, Moe
     const int n_chunks = plan.counts[1];
     const size_t opst = opw_bytes(d.I);
     const int nb = d.I / MOE_QK, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    for (int c = blockIdx.x; c < n_chunks; c += gridDim.x) {
-        const int e = plan.chunk_expert[c], p0 = plan.chunk_pair0[c], v = plan.chunk_ntok[c];
+    const int per_chunk = MOE_WIDE_TC * nb, total = n_chunks * per_chunk;
+    for (int task = blockIdx.x * nw + (threadIdx.x >> 5); task < total; task += gridDim.x * nw) {
+        const int c = task / per_chunk, j = (task / nb) % MOE_WIDE_TC, sb = task % nb;
+        const int ntok = plan.chunk_ntok[c];
+        if (j >= ntok) continue;
+        const int e = plan.chunk_expert[c], p = plan.chunk_pair0[c] + j;
         const int style = ((e == d.E) ? L.sh_down_type : L.down_type) == 14 ? 6 : 4;
-        const bool wide = (v & MOE_CHUNK_WIDE) != 0;
-        for (int task = threadIdx.x >> 5; task < MOE_CHUNK_NTOK(v) * nb; task += nw) {
-            const int p = p0 + task / nb, sb = task % nb;
-            const float *x = act + (size_t)p * d.I + (size_t)sb * MOE_QK;
-            uint8_t *o = dop + (size_t)p * opst;
-            if (wide) build_opw_sb(x, o + (size_t)sb * OPW_SB, style, lane);
-            else build_op_sb(x, o + (size_t)sb * OPB_SB, style, lane);
-        }
+        const float *x = act + (size_t)p * d.I + (size_t)sb * MOE_QK;
+        uint8_t *o = dop + (size_t)p * opst;
+        if (moe_dn_wide(ntok)) build_opw_sb(x, o + (size_t)sb * OPW_SB, style, lane);
+        else build_op_sb(x, o + (size_t)sb * OPB_SB, style, lane);
     }
 }
 

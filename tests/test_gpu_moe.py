@@ -246,9 +246,13 @@ def test_config3_shape_b64_zipf(cuda_lib, oracle):
     assert err < TOL and err < GUARD, err
     rows = [rel_err(out[t], ref[t]) for t in range(64)]
     assert max(rows) < GUARD, max(rows)
-    # token independence: a token's output does not depend on its batch mates
+    print(f"config 3: normwise {err:.2e}, worst row {max(rows):.2e}")
+    # token independence: alone, a token takes the int8-plane path of the
+    # expert GEMVs; in the batch, its busy experts take the fp16 path.  Both
+    # are exact products with fp32 sums and differ only in how the
+    # activations are rounded (21-bit planes vs a 22-bit hi/lo split)
     o1, i1, _ = m.forward(0, h[17:18])
-    assert np.array_equal(i1[0], idx[17]) and rel_err(o1[0], out[17]) < 1e-6
+    assert np.array_equal(i1[0], idx[17]) and rel_err(o1[0], out[17]) < 1e-5
     m.close()
 
 
