@@ -60,20 +60,23 @@ __host__ __device__ __forceinline__ int opq4_xsum_off(int jj) {
 // Wide activation operand (fp16 planes), for the expert GEMVs' fp16 path: x
 // times a power of two s per super-block (max |x s| in [2^14, 2^15)) is split
 // into x_hi = fp16(x s) and x_lo = fp16(x s - x_hi) (22 significant bits
-// together).  Per vector and super-block, OPW_SB = 1088 bytes:
+// together).  Per vector and super-block, OPW_SB = 1104 bytes:
 //   [0, 512)     x_hi, 256 fp16 in lane order (style Q4 or Q6, below)
 //   [512, 528)   style Q4: fp16 hi parts of the 8 sub-block sums / 32
 //   [528, 544)   style Q4: fp16 lo parts of the same
 //   [544, 548)   1/s (fp32)
 //   [576, 1088)  x_lo in the same order (576: the two planes' 16-byte
 //                fragment loads of one quarter-warp fall on distinct banks)
+//   [1088, 1104) padding: vectors 4 apart differ by 64 mod 128 bytes, so the
+//                x_hi loads of tokens k and k + 4 by one quarter-warp (the
+//                Q6_K residual tiles) fall on distinct banks too
 // Style Q4 (m16n8k16 fp16, Q4_K weights): element 8 t + i of sub-block j
 // (32 weights) sits at fp16 index 32 j + 8 t + perm(i), perm = 0 2 1 3 4 6 5 7,
 // so that one 16-byte load gives lane t the B fragments of both k16 steps.
 // Style Q6 (Q6_K weights, one sub-block of 16 per k16 step): element 4 t + i
 // of sub-block s sits at fp16 index 32 (s / 2) + 8 t + 4 (s % 2) + i.
 // ---------------------------------------------------------------------------
-#define OPW_SB 1088
+#define OPW_SB 1104
 #define OPW_XSUM 512
 #define OPW_SCALE 544
 #define OPW_LO 576

@@ -487,9 +487,11 @@ __device__ __forceinline__ void q4w_stage(const uint8_t *rowg, const uint8_t *ro
 // planes.  q (6 bits, from the repacked planes, high qh bit restored) under
 // the exponent of 1024 minus 1056 gives Q = q - 32 exactly; v = Q sc
 // (|v| <= 4096) is P = fp16(Q sc) plus R = fma(Q, sc, -P) in {-1, 0, 1}, both
-// exact, and P and R run as two MMAs on the same B.  Lane t holds elements
-// 4 t .. 4 t + 3 of every sub-block (style Q6).  Per super-block:
-// acc_f += (d / s) (hi + lo).
+// exact.  P multiplies both planes of x; R only x_hi (R x_lo is below 2^-23
+// of P x), on tiles of 8 tokens whose column order (token (c / 2) + 4 (c % 2)
+// of the pair of P tiles) puts in lane t the same tokens as its P columns.
+// Lane t holds elements 4 t .. 4 t + 3 of every sub-block (style Q6).  Per
+// super-block: acc_f += (d / s) (hi + lo + r).
 // ===========================================================================
 template <int NT>
 __device__ __forceinline__ void q6w_stage(const uint8_t *qg, const uint8_t *q8, const uint8_t *sg_p,
@@ -504,9 +506,14 @@ __device__ __forceinline__ void q6w_stage(const uint8_t *qg, const uint8_t *q8, 
     const uint32_t sw[2][4] = {{sgv.x ^ 0x80808080u, sgv.y ^ 0x80808080u, sgv.z ^ 0x80808080u, sgv.w ^ 0x80808080u},
                                {s8v.x ^ 0x80808080u, s8v.y ^ 0x80808080u, s8v.z ^ 0x80808080u, s8v.w ^ 0x80808080u}};
     const uint8_t *bp = opnd + (g >> 1) * OPW_SB + (g & 1) * OPW_LO + 16 * t;
-    float acc[NT][4];
+    // R tiles: x_hi of token 8 r + (g / 2) + 4 (g % 2)
+    const uint8_t *br = opnd + ((g >> 1) + 4 * (g & 1)) * OPW_SB + 16 * t;
+    constexpr int NR = (NT + 1) / 2;
+    float acc[NT][4], accr[NR][4];
 #pragma unroll
     for (int n = 0; n < NT; n++) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.0f;
+#pragma unroll
+    for (int n = 0; n < NR; n++) accr[n][0] = accr[n][1] = accr[n][2] = accr[n][3] = 0.0f;
 #pragma unroll
     for (int s2 = 0; s2 < 8; s2++) {
         uint32_t P[2][2][2], R[2][2][2];  // [sub-block even / odd][row][elements (0,1) / (2,3)]
@@ -538,16 +545,21 @@ __device__ __forceinline__ void q6w_stage(const uint8_t *qg, const uint8_t *q8, 
         for (int n = 0; n < NT; n++) {
             const uint4 b = lds128(bp + 4 * n * OPW_SB + 64 * s2);
             mma_f16_acc(acc[n], P[0][0][0], P[0][1][0], P[0][0][1], P[0][1][1], b.x, b.y);
-            mma_f16_acc(acc[n], R[0][0][0], R[0][1][0], R[0][0][1], R[0][1][1], b.x, b.y);
             mma_f16_acc(acc[n], P[1][0][0], P[1][1][0], P[1][0][1], P[1][1][1], b.z, b.w);
-            mma_f16_acc(acc[n], R[1][0][0], R[1][1][0], R[1][0][1], R[1][1][1], b.z, b.w);
+        }
+#pragma unroll
+        for (int n = 0; n < NR; n++) {
+            const uint4 b = lds128(br + 8 * n * OPW_SB + 64 * s2);
+            mma_f16_acc(accr[n], R[0][0][0], R[0][1][0], R[0][0][1], R[0][1][1], b.x, b.y);
+            mma_f16_acc(accr[n], R[1][0][0], R[1][1][0], R[1][0][1], R[1][1][1], b.z, b.w);
         }
     }
 #pragma unroll
     for (int n = 0; n < NT; n++) {
         const float inv = *reinterpret_cast<const float *>(opnd + (4 * n + t) * OPW_SB + OPW_SCALE);
-        accf[n][0] = fmaf(dg * inv, acc[n][0] + acc[n][1], accf[n][0]);
-        accf[n][1] = fmaf(d8 * inv, acc[n][2] + acc[n][3], accf[n][1]);
+        const float rg = accr[n >> 1][n & 1], r8 = accr[n >> 1][2 + (n & 1)];
+        accf[n][0] = fmaf(dg * inv, (acc[n][0] + acc[n][1]) + rg, accf[n][0]);
+        accf[n][1] = fmaf(d8 * inv, (acc[n][2] + acc[n][3]) + r8, accf[n][1]);
     }
 }
 
@@ -614,7 +626,7 @@ __device__ __forceinline__ uint8_t *align128(uint8_t *p) {
     return p + ((128u - (smem_u32(p) & 127u)) & 127u);
 }
 
-__global__ void __launch_bounds__(EX_THREADS, 2)
+__global__ void __maxnreg__(112)
     k_gateup(MoeDims d, const __grid_constant__ MoeLayerDev L, MoePlan plan, const uint8_t *__restrict__ xop,
              float *__restrict__ act) {
     extern __shared__ uint8_t ex_raw[];
@@ -800,7 +812,7 @@ __device__ __forceinline__ bool dn_item_w(const MoeDims &d, float *__restrict__ 
 
 // One instance per down type; chunks of the other type are skipped.
 template <int TY>
-__global__ void __launch_bounds__(EX_THREADS, 2)
+__global__ void __maxnreg__(112)
     k_down(MoeDims d, const __grid_constant__ MoeLayerDev L, MoePlan plan, const uint8_t *__restrict__ dop,
            float *__restrict__ eo) {
     constexpr int NS = TY == MOE_TYPE_Q6_K ? DN6_NS : DN4_NS;

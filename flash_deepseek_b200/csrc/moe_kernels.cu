@@ -1031,8 +1031,11 @@ void moe_launch_prep_rows(const float *recv, const int *meta, int meta_w, int R,
 
 void moe_launch_prep_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const float *act,
                           uint8_t *dop, int max_pairs, cudaStream_t s, uint64_t *launches) {
-    int grid = max_pairs;  // bounds the chunk count too
-    if (grid > num_sms() * 4) grid = num_sms() * 4;
+    // one warp per (chunk, pair slot, super-block) task where the plan can
+    // have that many, at most 2 blocks per SM
+    long tasks = (long)max_pairs * MOE_WIDE_TC * (d.I / MOE_QK);
+    int grid = (int)((tasks + 7) / 8);
+    if (grid > num_sms() * 2) grid = num_sms() * 2;
     if (grid < 1) grid = 1;
     moe_launch_pdl(k_prep_down, dim3(grid), dim3(256), 0, s, d, L, plan, act, dop);
     LAUNCH_COUNT(launches);

@@ -444,8 +444,9 @@ def test_prefill_q6_dequant_emulation(tables, oracle):
 
 def test_wide_operand_maps(tables):
     sb, xsum, scale, lo, top = tables["opw"]
-    assert (sb, xsum, scale, lo, top) == (1088, 512, 544, 576, 15)
+    assert (sb, xsum, scale, lo, top) == (1104, 512, 544, 576, 15)
     assert lo % 128 == 64 and sb % 16 == 0  # planes' quarter-warp loads on distinct banks; bulk-copy size
+    assert (4 * sb) % 128 == 64             # x_hi of tokens k, k + 4 (Q6_K residual tiles) on distinct banks
     for name in ("opw4", "opw6"):
         assert sorted(tables[name].values()) == list(range(256))
     for k in range(256):  # style Q4: lane t = (k / 8) % 4 of sub-block k / 32 owns 8 contiguous fp16
@@ -453,6 +454,9 @@ def test_wide_operand_maps(tables):
         assert tables["opw4"][k] == 32 * j + 8 * t + [0, 2, 1, 3, 4, 6, 5, 7][i]
         s, t6, i6 = k >> 4, (k >> 2) & 3, k & 3
         assert tables["opw6"][k] == 32 * (s >> 1) + 8 * t6 + 4 * (s & 1) + i6
+
+
+OPW = 1104  # OPW_SB, checked against the header by test_wide_operand_maps
 
 
 def build_wide_operand(tables, xs, style):
@@ -465,7 +469,7 @@ def build_wide_operand(tables, xs, style):
         xsc = (x.astype(np.float64) * s).astype(np.float32)
         hi = xsc.astype(np.float16)
         lo = (xsc - hi.astype(np.float32)).astype(np.float16)
-        op = np.zeros(1088, np.uint8)
+        op = np.zeros(OPW, np.uint8)
         H = np.zeros(256, np.float16)
         L = np.zeros(256, np.float16)
         m = tables["opw4" if style == 4 else "opw6"]
@@ -540,7 +544,7 @@ def test_q4w_stage_emulation(tables, oracle):
                                          dec(w >> 8, row, 2 * jj + step_hi, step_hi)))
                         a[lane] = [regs[0][0], regs[1][0], regs[0][1], regs[1][1]]
                         tok = 4 * n_tile + (g >> 1)
-                        base = tok * 1088 + (g & 1) * 576 + 16 * t + 64 * (2 * jj + step_hi) + 8 * step
+                        base = tok * OPW + (g & 1) * 576 + 16 * t + 64 * (2 * jj + step_hi) + 8 * step
                         b[lane] = [w32(opnd, base), w32(opnd, base + 4)]
                     d = mma(a, b, 16, "f16")
                     for lane in range(32):
@@ -552,12 +556,12 @@ def test_q4w_stage_emulation(tables, oracle):
             mg, m8 = mins_words(rep[g]), mins_words(rep[g + 8])
             am[lane] = [h2pair(mg[2 * t], mg[2 * t + 1]), h2pair(m8[2 * t], m8[2 * t + 1]), 0, 0]
             tok = 4 * n_tile + (g >> 1)
-            bm[lane] = [w32(opnd, tok * 1088 + 512 + 16 * (g & 1) + 4 * t), 0]
+            bm[lane] = [w32(opnd, tok * OPW + 512 + 16 * (g & 1) + 4 * t), 0]
         mt = mma(am, bm, 16, "f16")
         for lane in range(32):
             g, t = lane >> 2, lane & 3
             tok = 4 * n_tile + t
-            inv = float(np.frombuffer(bytes(opnd[tok * 1088 + 544:tok * 1088 + 548]), np.float32)[0])
+            inv = float(np.frombuffer(bytes(opnd[tok * OPW + 544:tok * OPW + 548]), np.float32)[0])
             for r, row in enumerate((g, g + 8)):
                 d_, dm = rep[row][:4].view(np.float16).astype(np.float64)
                 out[row, tok] = d_ * inv * (acc[lane][2 * r] + acc[lane][2 * r + 1]) \
@@ -605,7 +609,7 @@ def test_q6w_stage_emulation(tables, oracle):
         acc = [[0.0] * 4 for _ in range(32)]
         for s in range(16):
             h, sp = s >> 3, s & 7
-            aP, aR, b = {}, {}, {}
+            aP, aR, b, br = {}, {}, {}, {}
             for lane in range(32):
                 g, t = lane >> 2, lane & 3
                 rg = []
@@ -615,16 +619,25 @@ def test_q6w_stage_emulation(tables, oracle):
                 aP[lane] = [rg[0][0][0], rg[1][0][0], rg[0][0][1], rg[1][0][1]]
                 aR[lane] = [rg[0][1][0], rg[1][1][0], rg[0][1][1], rg[1][1][1]]
                 tok = 4 * n_tile + (g >> 1)
-                base = tok * 1088 + (g & 1) * 576 + 16 * t + 64 * (s >> 1) + 8 * (s & 1)
+                base = tok * OPW + (g & 1) * 576 + 16 * t + 64 * (s >> 1) + 8 * (s & 1)
                 b[lane] = [w32(opnd, base), w32(opnd, base + 4)]
-            for d in (mma(aP, b, 16, "f16"), mma(aR, b, 16, "f16")):
-                for lane in range(32):
-                    for q in range(4):
-                        acc[lane][q] += d[lane][q]
+                # the R tile: x_hi of token (g / 2) + 4 (g % 2) of the 8-token group
+                tokr = 8 * (n_tile >> 1) + (g >> 1) + 4 * (g & 1)
+                baser = tokr * OPW + 16 * t + 64 * (s >> 1) + 8 * (s & 1)
+                br[lane] = [w32(opnd, baser), w32(opnd, baser + 4)]
+            d = mma(aP, b, 16, "f16")
+            dr = mma(aR, br, 16, "f16")
+            for lane in range(32):
+                for q in range(4):
+                    acc[lane][q] += d[lane][q]
+                # lane t's R columns 2t, 2t+1 are tokens t and t + 4 of the group:
+                # this tile's token 4 n + t is column 2t + (n % 2)
+                acc[lane][0] += dr[lane][n_tile & 1]
+                acc[lane][2] += dr[lane][2 + (n_tile & 1)]
         for lane in range(32):
             g, t = lane >> 2, lane & 3
             tok = 4 * n_tile + t
-            inv = float(np.frombuffer(bytes(opnd[tok * 1088 + 544:tok * 1088 + 548]), np.float32)[0])
+            inv = float(np.frombuffer(bytes(opnd[tok * OPW + 544:tok * OPW + 548]), np.float32)[0])
             for r, row in enumerate((g, g + 8)):
                 out[row, tok] = D[row] * inv * (acc[lane][2 * r] + acc[lane][2 * r + 1])
     assert big > 0   # the residual MMA carried something
