@@ -626,7 +626,7 @@ __device__ __forceinline__ uint8_t *align128(uint8_t *p) {
     return p + ((128u - (smem_u32(p) & 127u)) & 127u);
 }
 
-__global__ void __maxnreg__(112)
+__global__ void __launch_bounds__(EX_THREADS, 2)
     k_gateup(MoeDims d, const __grid_constant__ MoeLayerDev L, MoePlan plan, const uint8_t *__restrict__ xop,
              float *__restrict__ act) {
     extern __shared__ uint8_t ex_raw[];
@@ -812,7 +812,7 @@ __device__ __forceinline__ bool dn_item_w(const MoeDims &d, float *__restrict__ 
 
 // One instance per down type; chunks of the other type are skipped.
 template <int TY>
-__global__ void __maxnreg__(112)
+__global__ void __launch_bounds__(EX_THREADS, 2)
     k_down(MoeDims d, const __grid_constant__ MoeLayerDev L, MoePlan plan, const uint8_t *__restrict__ dop,
            float *__restrict__ eo) {
     constexpr int NS = TY == MOE_TYPE_Q6_K ? DN6_NS : DN4_NS;
