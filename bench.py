@@ -4,7 +4,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME] [--impl ours|reference]
 
 One JSON line on rank 0.  A "step" is one decode step of one MoE layer over
-one batch of synthetic tokens.  Workloads:
+one batch of synthetic tokens.  Workloads (the reference's headline configs):
   decode_b64_zipf  (default) config 3: 64 tokens, router skewed by a Zipf(1.1)
                    per-expert bias, 256 experts sharded over N GPUs
   decode_b1        config 2: one token on one GPU
@@ -33,7 +33,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-from flash_deepseek_b200.workloads import zipf_logit_bias  # noqa: E402
+from flash_deepseek_b200.workloads import token_pool, zipf_logit_bias  # noqa: E402
 
 METRIC = "MoE decode tokens/s at 1/2/4/8 B200; expert matvec HBM GB/s vs 8 TB/s peak"
 H, I, E, K = 7168, 2048, 256, 8
@@ -46,7 +46,7 @@ WORKLOADS = {
     "decode_b64_zipf": dict(B=64, zipf=True, name="config3_decode_b64_zipf"),
     "decode_b1": dict(B=1, zipf=False, name="config2_decode_b1"),
 }
-# further BASELINE configs, measured on one GPU by run_extra()
+# the other headline configs (one expert, the 58-layer stack, prefill), measured by run_extra()
 EXTRA = {
     "expert1": dict(B=1, name="config1_single_q4k_expert"),
     "stack_b1": dict(B=1, name="config4_stack58_b1"),
@@ -55,6 +55,20 @@ EXTRA = {
     "prefill4096": dict(B=4096, name="config5_prefill4096_1layer"),
 }
 Q4_DOWN_BYTES = H * (I // 256) * 144         # 8,257,536
+
+
+NVLINK_GBS = 900.0          # NVLink 5, per direction per GPU (nominal)
+NVLINK_MEASURED_GBS = 770.0  # peer copy per direction measured on this pool's B200 boxes
+N_POOL = 4
+
+
+def workload_config(W, NE, world, b_loc):
+    """The `config` object of both arms' JSON lines."""
+    return {"workload": W["name"], "global_batch": W["B"], "tokens_per_gpu": b_loc, "hidden": H,
+            "intermediate": I, "experts": NE, "top_k": K, "gate_up": "Q4_K", "down": "Q6_K",
+            "router_skew": "zipf(1.1) logit bias" if W["zipf"] else "none",
+            "parallelism": f"ep{world}", "l2": "flushed: 256 MiB write between timed steps",
+            "tokens": f"numpy default_rng(1234) N(0,1), {N_POOL} batches in turn"}
 
 
 def peaks():
@@ -145,9 +159,10 @@ def cpu_reference(workload: str, steps: int, warmup: int, seconds: float = 20.0)
     router = O.normal(0, O.stream(0, 0, O.KIND_ROUTER), E * H, 0.006, threads=threads).reshape(E, H)
     bias = O.normal(0, O.stream(0, 0, O.KIND_BIAS), E, 0.01, threads=threads)
     lbias = zipf_logit_bias() if W["zipf"] else np.zeros(E, np.float32)
-    rng = np.random.default_rng(1234)
+    # the GPU arm's token batches, one token at a time in the same order
     n_tok = max(1, steps + warmup)
-    xs = rng.standard_normal((n_tok, H)).astype(np.float32)
+    pool = token_pool(W["B"], N_POOL)
+    xs = np.stack([pool[(i // W["B"]) % N_POOL][i % W["B"]] for i in range(n_tok)])
     need = set()
     for t in range(n_tok):
         lg = (router.astype(np.float64) @ xs[t].astype(np.float64) + lbias).astype(np.float32)
@@ -209,9 +224,8 @@ def run_ours(args):
 
     dev = torch.device("cuda", local)
     stream = torch.cuda.ExternalStream(moe.stream, device=dev)
-    n_pool = 4
-    g = torch.Generator(device="cpu").manual_seed(1234)
-    pool_h = [torch.randn(B, H, generator=g, dtype=torch.float32) for _ in range(n_pool)]
+    n_pool = N_POOL
+    pool_h = [torch.from_numpy(x) for x in token_pool(B, n_pool)]
     pool = [p[t0_loc:t0_loc + b_loc].contiguous().to(dev) for p in pool_h]
     out = torch.empty(max(1, b_loc), H, device=dev)
     steps_total = args.warmup + args.steps
@@ -256,6 +270,7 @@ def run_ours(args):
         moe.forward_device(0, pool[(args.warmup + s) % n_pool], b_loc, out, d_idx=idx_all[args.warmup + s])
         ev[s][1].record(stream)
     barrier()
+    moe.check_error()  # a bounded device wait that gave up would surface here
     clk_lines_timed = clk.lines[n_clk0:]
     launches = moe.kernel_launches - launches0
     step_ms = [a.elapsed_time(b) for a, b in ev]
@@ -293,6 +308,47 @@ def run_ours(args):
         active.append(n_act)
         gu_bytes.append(n_act * 2 * GATE_BYTES + rows * H * 4 + pairs * I * 4)
         dn_bytes.append(n_act * DOWN_Q6_BYTES + pairs * (I * 4 + H * 4))
+    # expert-parallel exchange and the per-GPU critical path, from the
+    # global routing of every timed step (all ranks compute the same figures)
+    nv = None
+    crit = None
+    if world > 1:
+        row_b = H * 4 + (2 + 2 * K) * 4        # a dispatched token row: fp32 activations + routing metadata
+        part_b = H * 4                          # a returned partial sum (fp32)
+        starts = [ep.local_tokens(B, world, r)[0] for r in range(world)]
+        counts_r = [ep.local_tokens(B, world, r)[1] for r in range(world)]
+        send = np.zeros((args.steps, world))
+        recv = np.zeros((args.steps, world))
+        hbm = np.zeros((args.steps, world))
+        for s_ in range(args.steps):
+            own = ep.expert_owner(idx_g[s_], NE, world)  # [B, K] owning rank of every routed expert
+            for r in range(world):
+                n_exp = len(ep.experts_hit(idx_g[s_], NE, world, r))
+                hbm[s_, r] = n_exp * EXPERT_BYTES + ((NE * H * 4 + NE * 4 + EXPERT_BYTES) if counts_r[r] else 0)
+            for tkn in range(B):
+                src = next(r for r in range(world) if starts[r] <= tkn < starts[r] + counts_r[r])
+                for dst in set(own[tkn].tolist()) - {src}:
+                    send[s_, src] += row_b      # dispatch: token row to the expert owner
+                    recv[s_, dst] += row_b
+                    send[s_, dst] += part_b     # combine: partial sum back to the token's rank
+                    recv[s_, src] += part_b
+        ex_ms = float(np.mean([p["dispatch"] + p["combine_a2a"] for p in phases]))
+        ex_ms = max_over_ranks(ex_ms)
+        crit_link = float(np.maximum(send, recv).max(1).mean())   # busiest direction of the busiest rank
+        nv = {"bytes_per_step_busiest_rank": round(crit_link), "dispatch_plus_combine_ms": round(ex_ms, 5),
+              "achieved_gbs": round(crit_link / (ex_ms / 1e3) / 1e9, 2) if ex_ms > 0 else None,
+              "frac_of_900": round(crit_link / (ex_ms / 1e3) / 1e9 / NVLINK_GBS, 5) if ex_ms > 0 else None,
+              "frac_of_measured_770": round(crit_link / (ex_ms / 1e3) / 1e9 / NVLINK_MEASURED_GBS, 5)
+              if ex_ms > 0 else None,
+              "send_bytes_per_rank": [round(x) for x in send.mean(0)],
+              "recv_bytes_per_rank": [round(x) for x in recv.mean(0)],
+              "note": "exchange phases include waiting for the busiest rank's experts"}
+        crit_b = float(hbm.max(1).mean())
+        crit = {"bytes_per_step_busiest_rank": round(crit_b),
+                "achieved_gbs": round(crit_b / (total_ms / args.steps / 1e3) / 1e9, 1),
+                "frac": round(crit_b / (total_ms / args.steps / 1e3) / 1e9 / peaks()[0], 4),
+                "aggregate_frac": round(float(hbm.sum(1).mean()) / (total_ms / args.steps / 1e3) / 1e9 /
+                                        (peaks()[0] * world), 4)}
     gu_ms = float(np.mean([p["gateup"] for p in phases]))
     dn_ms = float(np.mean([p["down"] for p in phases]))
     peak, peak_kind = peaks()
@@ -324,6 +380,7 @@ def run_ours(args):
         if rc != 0:
             raise RuntimeError(moe.lib.moe_last_error(moe.ctx))
     barrier()
+    moe.check_error()
     e2e_ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in ev2))
     clk.__exit__(None, None, None)
     if len(clk_lines_timed) < 3:   # timed region shorter than the sampling period
@@ -333,20 +390,17 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cpu = cpu_reference(args.workload, steps=4, warmup=1, seconds=15.0)
+        cpu = cpu_reference(args.workload, steps=20, warmup=1, seconds=15.0)
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "int8 tensor-core products of Q4_K/Q6_K integers and 21-bit activation planes (exact), fp32 "
-                     "accumulation",
+            "dtype": "exact tensor-core products of the Q4_K/Q6_K integers (sub-block scales folded in) with "
+                     "fp16 hi/lo (22-bit) or int8-plane (21-bit) activations, fp32 accumulation",
             "data": "synthetic: random-init N(0,0.02) weights quantized on device, N(0,1) tokens",
-            "config": {"workload": W["name"], "global_batch": B, "tokens_per_gpu": b_loc, "hidden": H,
-                       "intermediate": I, "experts": NE, "top_k": K, "gate_up": "Q4_K", "down": "Q6_K",
-                       "router_skew": "zipf(1.1) logit bias" if W["zipf"] else "none",
-                       "parallelism": f"ep{world}", "l2": "flushed: 256 MiB write between timed steps"},
+            "config": workload_config(W, NE, world, b_loc),
             "roofline": {"bound": "hbm", "kernel": "k_gateup (grouped Q4_K gate/up GEMV + SwiGLU)",
                          "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(ach / peak, 4), "peak_source": peak_kind,
@@ -360,6 +414,8 @@ def run_ours(args):
                          "achieved_gbs": round(step_bytes / (total_ms / args.steps / 1e3) / 1e9, 1),
                          "active_experts_per_step": round(float(np.mean(active)), 2)},
             "phase_ms": {k: round(float(np.mean([p[k] for p in phases])), 5) for k in phases[0]},
+            "nvlink": nv,
+            "step_hbm_critical_path": crit,
             "e2e": {"value": round(e2e, 2), "unit": "tokens/s", "h2d_bytes_per_step": B * H * 4,
                     "d2h_bytes_per_step": B * H * 4 + B * K * 8},
             "gpu_launches": int(launches),
@@ -646,13 +702,16 @@ def run_reference(args):
         return
     W = WORKLOADS[args.workload]
     cpu = cpu_reference(args.workload, steps=args.steps, warmup=args.warmup, seconds=60.0)
+    # the GPU arm's config at this world size (its per-GPU token share)
+    from flash_deepseek_b200 import ep
+    b_loc = ep.local_tokens(W["B"], world, 0)[1]
     line = {
         "impl": "reference", "metric": METRIC, "value": round(cpu["value"], 4), "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(1e3 / cpu["value"], 3), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "fp32", "data": "synthetic (same generator and seed as the GPU arm)",
-        "config": {"workload": W["name"], "global_batch": W["B"], "hidden": H, "intermediate": I, "experts": E,
-                   "top_k": K, "gate_up": "Q4_K", "down": "Q6_K"},
+        "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic: the GPU arm's weights (same generator and seed) and its token batches, token by token",
+        "config": workload_config(W, E, world, b_loc),
         "cpu_baseline": cpu,
         "e2e": {"value": round(cpu["value"], 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},

@@ -1,6 +1,7 @@
-"""Synthetic workloads of the reference's headline configurations
-for tests and bench.py: shapes, seeds and the
-Zipf expert-load skew.  Weights are random-init N(0, 0.02) quantized to Q4_K
+"""Synthetic workloads of the reference's headline configurations (configs
+1-5: one expert, one layer at batch 1 and 64, the 58-layer stack, a
+4096-token prefill) for tests and bench.py: shapes, seeds and the Zipf
+expert-load skew.  Weights are random-init N(0, 0.02) quantized to Q4_K
 (gate/up) and Q6_K or Q4_K (down); router N(0, 0.006), selection bias
 N(0, 0.01); tokens N(0, 1)."""
 from __future__ import annotations
@@ -31,3 +32,11 @@ def zipf_logit_bias(n: int = E, s: float = 1.1, seed: int = 0, beta: float | Non
 
 def tokens(batch: int, seed: int = 1234) -> np.ndarray:
     return np.random.default_rng(seed).standard_normal((batch, H)).astype(np.float32)
+
+
+def token_pool(batch: int, n_pool: int = 4, seed: int = 1234) -> list:
+    """n_pool batches of N(0, 1) tokens [batch, H] from one generator, in
+    order: the inputs of bench.py's GPU steps (step s uses batch s % n_pool)
+    and, token by token in the same order, of its CPU reference arm."""
+    rng = np.random.default_rng(seed)
+    return [rng.standard_normal((batch, H)).astype(np.float32) for _ in range(n_pool)]
