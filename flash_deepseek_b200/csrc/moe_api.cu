@@ -96,28 +96,35 @@ struct moe_ctx {
     uint8_t **d_peers = nullptr;
     std::vector<uint8_t *> peer_map;
     size_t mb_x = 0, mb_meta = 0, mb_y = 0;
-    int *ep_done = nullptr;  // [2] block counters of the two signalling kernels
+    int *ep_done = nullptr;  // [3] block counters of the pack, pre-combine and final kernels
+    unsigned long long *d_seq = nullptr;  // peer-exchange steps completed by this rank (device)
     int *hits = nullptr;     // moe_record_expert_hits target, or nullptr
     bool comm_aborted = false;  // a host wait gave up on an NCCL exchange
     bool ep_failed = false;     // a peer-exchange wait gave up: the ranks are out of step
-    unsigned long long ep_seq = 0;
     std::string err;
     bool timing = false;
     int ring = 0, ring_pos = 0, ring_used = 0;  // per-step phase events
     std::vector<cudaEvent_t> ev;                // [ring][MOE_N_PHASES + 1]
     std::vector<uint8_t> ev_valid;
     uint64_t launches = 0;
-    // replayable CUDA graphs of the 1-GPU forward, one per call signature
-    struct Graph {
-        int layer, T;
-        const void *h, *out, *idx, *w;
+    // replayable CUDA graphs, one per call signature: kind 0 = one layer's
+    // forward (a = layer), kind 1 = a layer stack (a = first, b = count)
+    struct GraphSig {
+        int kind, a, b, T;
+        const void *p1, *p2;
         cudaStream_t s;
+        bool operator==(const GraphSig &o) const {
+            return kind == o.kind && a == o.a && b == o.b && T == o.T && p1 == o.p1 && p2 == o.p2 && s == o.s;
+        }
+    };
+    struct Graph {
+        GraphSig sig;
         cudaGraphExec_t exec;
         uint64_t kernels, last_use;
     };
     std::vector<Graph> graphs;
     MoePrefillWs pf;  // prefill workspace, allocated on first use
-    std::vector<std::array<const void *, 5>> seen;  // signatures run once eagerly (attributes set)
+    std::vector<GraphSig> seen;  // signatures run once directly (kernel attributes set)
     bool use_graphs = true;
     uint64_t clock = 0;
     uint64_t last_bytes = 0;
@@ -258,8 +265,10 @@ static int ep_p2p_init(moe_ctx *c) {
     const size_t total = c->mb_y + 2 * R * H * sizeof(float);
     CK(cudaMalloc((void **)&c->mbox, total));
     CK(cudaMemset(c->mbox, 0, total));
-    CK(cudaMalloc((void **)&c->ep_done, 2 * sizeof(int)));
-    CK(cudaMemset(c->ep_done, 0, 2 * sizeof(int)));
+    CK(cudaMalloc((void **)&c->ep_done, 3 * sizeof(int)));
+    CK(cudaMemset(c->ep_done, 0, 3 * sizeof(int)));
+    CK(cudaMalloc((void **)&c->d_seq, sizeof(unsigned long long)));
+    CK(cudaMemset(c->d_seq, 0, sizeof(unsigned long long)));
     CK(cudaMalloc((void **)&c->d_peers, N * sizeof(uint8_t *)));
     cudaIpcMemHandle_t mine;
     CK(cudaIpcGetMemHandle(&mine, c->mbox));
@@ -396,6 +405,7 @@ void moe_destroy(moe_ctx *c) {
     cudaFree(c->mbox);
     cudaFree(c->d_peers);
     cudaFree(c->ep_done);
+    cudaFree(c->d_seq);
     if (c->comm) moe_nccl()->CommDestroy(c->comm);
     for (cudaEvent_t e : c->ev) cudaEventDestroy(e);
     for (auto &g : c->graphs) cudaGraphExecDestroy(g.exec);
@@ -752,21 +762,31 @@ static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_i
         moe_launch_route_and_plan(d, nullptr, 0, c->logits, L.bias, L.logit_bias, mode, idx_in, w_in, T, c->idx,
                                   c->wts, x, nullptr, 0, 0, c->plan, c->counter, s, &c->launches);
     mark(c, MOE_PHASE_DISPATCH, s);
-    // the step's mailbox regions (peer-memory exchange) or the NCCL buffers
-    EpP2P q{c->d_peers, c->mb_x, c->mb_meta, c->mb_y, N, c->rank, 0, 0};
-    float *recv_x = c->recv_x, *recv_y = c->recv_y;
-    int *recv_meta = c->recv_meta;
+    const int P = R * d.K + T;
+    const int max_chunks = (P + MOE_TC - 1) / MOE_TC + d.E + 1;
     if (c->p2p) {
-        q.seq = ++c->ep_seq;
-        q.parity = (int)(q.seq & 1);
-        recv_x = reinterpret_cast<float *>(c->mbox + c->mb_x) + (size_t)q.parity * R * d.H;
-        recv_meta = reinterpret_cast<int *>(c->mbox + c->mb_meta) + (size_t)q.parity * R * mw;
-        recv_y = reinterpret_cast<float *>(c->mbox + c->mb_y) + (size_t)q.parity * R * d.H;
-        moe_launch_ep_pack_p2p(x, c->idx, c->wts, T, d.K, d.H, c->n_local, cap, q, c->tok_slot, c->ep_done, s,
-                               &c->launches);
-        moe_launch_ep_wait(reinterpret_cast<const unsigned long long *>(c->mbox), N, q.seq, c->plan.error, s,
-                           &c->launches);
-    } else {
+        // peer-memory exchange: no host step in between, the step number
+        // lives on the device (the launches replay as a graph)
+        const EpP2P q{c->d_peers, c->mb_x, c->mb_meta, c->mb_y, N, c->rank, c->d_seq, c->ep_done, c->plan.error};
+        moe_launch_ep_pack_p2p(x, c->idx, c->wts, T, d.K, d.H, c->n_local, cap, q, c->tok_slot, s, &c->launches);
+        moe_launch_ep_plan_rows_p2p(d, q, cap, T, c->e0, c->n_local, c->plan, x, c->xop, s, &c->launches);
+        mark(c, MOE_PHASE_GATEUP, s);
+        moe_launch_gateup(d, L, c->plan, c->xop, c->act, max_chunks, s, &c->launches);
+        mark(c, MOE_PHASE_PREP, s);
+        moe_launch_prep_down(d, L, c->plan, c->act, c->dop, P, s, &c->launches);
+        mark(c, MOE_PHASE_DOWN, s);
+        moe_launch_down(d, L, c->plan, c->dop, c->eo, max_chunks, s, &c->launches);
+        mark(c, MOE_PHASE_COMBINE, s);
+        moe_launch_ep_partial_p2p(d, c->plan, c->eo, cap, q, s, &c->launches);
+        moe_launch_ep_final_p2p(d, c->plan, q, c->tok_slot, cap, T, c->eo, residual, out, s, &c->launches);
+        mark(c, MOE_PHASE_OUTPUT, s);
+        mark(c, MOE_N_PHASES, s);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return fail(c, MOE_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+        c->last_layer = layer;
+        return MOE_OK;
+    }
+    {
         moe_launch_ep_pack(x, c->idx, c->wts, T, d.K, d.H, N, c->n_local, cap, c->send_x, c->send_meta, c->tok_slot,
                            s, &c->launches);
         NK(moe_nccl()->GroupStart());
@@ -778,10 +798,8 @@ static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_i
         }
         NK(moe_nccl()->GroupEnd());
     }
-    moe_launch_ep_plan(d, recv_meta, N, cap, T, c->e0, c->n_local, c->plan, s, &c->launches);
-    moe_launch_prep_rows(recv_x, recv_meta, mw, R, x, T, d.H, c->xop, s, &c->launches);
-    const int P = R * d.K + T;
-    const int max_chunks = (P + MOE_TC - 1) / MOE_TC + d.E + 1;
+    moe_launch_ep_plan(d, c->recv_meta, N, cap, T, c->e0, c->n_local, c->plan, s, &c->launches);
+    moe_launch_prep_rows(c->recv_x, c->recv_meta, mw, R, x, T, d.H, c->xop, s, &c->launches);
     mark(c, MOE_PHASE_GATEUP, s);
     moe_launch_gateup(d, L, c->plan, c->xop, c->act,
                       max_chunks, s, &c->launches);
@@ -790,11 +808,7 @@ static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_i
     mark(c, MOE_PHASE_DOWN, s);
     moe_launch_down(d, L, c->plan, c->dop, c->eo, max_chunks, s, &c->launches);
     mark(c, MOE_PHASE_COMBINE, s);
-    if (c->p2p) {
-        moe_launch_ep_partial_p2p(d, c->plan, recv_meta, c->eo, cap, q, c->ep_done + 1, s, &c->launches);
-        moe_launch_ep_wait(reinterpret_cast<const unsigned long long *>(c->mbox) + 64, N, q.seq, c->plan.error, s,
-                           &c->launches);
-    } else {
+    {
         moe_launch_ep_partial(d, c->plan, c->recv_meta, c->eo, R, c->send_y, s, &c->launches);
         NK(moe_nccl()->GroupStart());
         for (int p = 0; p < N; p++) {
@@ -805,7 +819,7 @@ static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_i
     }
     mark(c, MOE_PHASE_OUTPUT, s);
     if (T > 0)
-        moe_launch_ep_final(d, c->plan, recv_y, c->tok_slot, N, cap, T, c->eo, residual, out, s, &c->launches);
+        moe_launch_ep_final(d, c->plan, c->recv_y, c->tok_slot, N, cap, T, c->eo, residual, out, s, &c->launches);
     mark(c, MOE_N_PHASES, s);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(c, MOE_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
@@ -813,40 +827,38 @@ static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_i
     return MOE_OK;
 }
 
-// One forward on one GPU: the kernel sequence of run_local plus the routing
-// copies.  A signature (layer, T, buffers, stream) seen before is replayed
-// as a CUDA graph (captured on its second call, when every kernel attribute
-// is already set); the per-phase timing ring and a stream that is already
-// being captured by the caller run the kernels directly.
-static int forward_local_once(moe_ctx *c, int layer, const float *d_h, int T, float *d_out, cudaStream_t s) {
-    return run_local(c, layer, d_h, T, nullptr, nullptr, 1, 1, nullptr, d_out, s);
-}
-
-static int forward_local_kernels(moe_ctx *c, int layer, const float *d_h, int T, float *d_out, cudaStream_t s) {
+// Runs `body` (a sequence of launches on stream s) as a CUDA graph: a
+// signature seen before is replayed (captured on its second call, when every
+// kernel attribute is already set).  Direct launches while the per-phase
+// timing ring is on, when the caller is capturing the stream itself, or on
+// the NCCL exchange path.  On the expert-parallel peer-memory path every
+// rank makes the same calls, so every rank captures and replays the same
+// sequences; the step number the kernels need is in device memory.
+}  // extern "C"
+template <typename F>
+static int run_graphed(moe_ctx *c, const moe_ctx::GraphSig &sig, cudaStream_t s, F &&body) {
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-    if (!c->use_graphs || c->timing || cudaStreamIsCapturing(s, &cs) != cudaSuccess ||
+    if (!c->use_graphs || c->timing || (c->world > 1 && !c->p2p) || cudaStreamIsCapturing(s, &cs) != cudaSuccess ||
         cs != cudaStreamCaptureStatusNone)
-        return forward_local_once(c, layer, d_h, T, d_out, s);
+        return body();
     c->clock++;
     for (auto &g : c->graphs)
-        if (g.layer == layer && g.T == T && g.h == d_h && g.out == d_out && g.s == s) {
+        if (g.sig == sig) {
             g.last_use = c->clock;
             CK(cudaGraphLaunch(g.exec, s));
             c->launches += g.kernels;
             return MOE_OK;
         }
-    const std::array<const void *, 5> sig = {(const void *)(intptr_t)(layer * 4096 + T), d_h, d_out, nullptr,
-                                             (const void *)s};
     bool seen = false;
     for (auto &x : c->seen) seen = seen || x == sig;
     if (!seen) {  // first call: run directly (sets kernel attributes)
         if (c->seen.size() > 64) c->seen.erase(c->seen.begin());
         c->seen.push_back(sig);
-        return forward_local_once(c, layer, d_h, T, d_out, s);
+        return body();
     }
     const uint64_t k0 = c->launches;
     CK(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
-    const int rc = forward_local_once(c, layer, d_h, T, d_out, s);
+    const int rc = body();
     cudaGraph_t graph = nullptr;
     const cudaError_t ec = cudaStreamEndCapture(s, &graph);
     if (rc) {
@@ -865,8 +877,20 @@ static int forward_local_kernels(moe_ctx *c, int layer, const float *d_h, int T,
         cudaGraphExecDestroy(c->graphs[lru].exec);
         c->graphs.erase(c->graphs.begin() + lru);
     }
-    c->graphs.push_back({layer, T, d_h, d_out, nullptr, nullptr, s, exec, c->launches - k0, c->clock});
+    c->graphs.push_back({sig, exec, c->launches - k0, c->clock});
     CK(cudaGraphLaunch(exec, s));
+    return MOE_OK;
+}
+
+extern "C" {
+
+// an expert-parallel context refuses work after a failed exchange (checked
+// on the host before any launch, graph replays included)
+static int ep_usable(moe_ctx *c) {
+    if (c->world == 1) return MOE_OK;
+    if (c->comm_aborted) return fail(c, MOE_ERR_STATE, "an exchange failed and the communicator was aborted");
+    if (c->ep_failed)
+        return fail(c, MOE_ERR_STATE, "a peer exchange timed out earlier; the ranks are out of step (recreate the context)");
     return MOE_OK;
 }
 
@@ -898,14 +922,16 @@ int moe_forward_device(moe_ctx *c, int layer, const float *d_h, int T, float *d_
     if (rc) return rc;
     if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
     cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
-    if (c->world > 1) {
-        rc = run_ep(c, layer, d_h, T, nullptr, nullptr, nullptr, d_out, s);  // every rank joins, even with T == 0
-        if (rc) return rc;
-    } else {
-        if (T == 0) return record_hits(c, layer, false, s);
-        rc = forward_local_kernels(c, layer, d_h, T, d_out, s);
-        if (rc) return rc;
-    }
+    rc = ep_usable(c);
+    if (rc) return rc;
+    if (c->world == 1 && T == 0) return record_hits(c, layer, false, s);
+    // every rank of an expert-parallel context joins, even with T == 0
+    const moe_ctx::GraphSig sig{0, layer, 0, T, d_h, d_out, s};
+    rc = run_graphed(c, sig, s, [&]() {
+        return c->world > 1 ? run_ep(c, layer, d_h, T, nullptr, nullptr, nullptr, d_out, s)
+                            : run_local(c, layer, d_h, T, nullptr, nullptr, 1, 1, nullptr, d_out, s);
+    });
+    if (rc) return rc;
     if (d_idx) CK(cudaMemcpyAsync(d_idx, c->idx, sizeof(int) * T * c->d.K, cudaMemcpyDeviceToDevice, s));
     if (d_w) CK(cudaMemcpyAsync(d_w, c->wts, sizeof(float) * T * c->d.K, cudaMemcpyDeviceToDevice, s));
     return record_hits(c, layer, true, s);
@@ -1247,17 +1273,27 @@ int moe_forward_stack_device(moe_ctx *c, int first, int n_layers, float *d_hidde
     if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
     cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
     for (int l = first; l < first + n_layers; l++) {
-        int rc = check_layer(c, l);
-        if (rc) return rc;
-        if (T > 0) moe_launch_rmsnorm(d_hidden, c->layers[l].norm, c->h_post, T, c->d.H, c->cfg.rms_eps, s,
-                                      &c->launches);
-        if (c->world > 1) rc = run_ep(c, l, c->h_post, T, nullptr, nullptr, d_hidden, d_hidden, s);
-        else if (T > 0) rc = run_local(c, l, c->h_post, T, nullptr, nullptr, 1, 1, d_hidden, d_hidden, s);
-        if (rc) return rc;
-        rc = record_hits(c, l, c->world > 1 || T > 0, s);
+        const int rc = check_layer(c, l);
         if (rc) return rc;
     }
-    return MOE_OK;
+    int rc = ep_usable(c);
+    if (rc) return rc;
+    // the whole stack is one launch sequence (one graph once replayed)
+    const moe_ctx::GraphSig sig{1, first, n_layers, T, d_hidden, nullptr, s};
+    return run_graphed(c, sig, s, [&]() {
+        for (int l = first; l < first + n_layers; l++) {
+            int r = MOE_OK;
+            if (T > 0)
+                moe_launch_rmsnorm(d_hidden, c->layers[l].norm, c->h_post, T, c->d.H, c->cfg.rms_eps, s,
+                                   &c->launches);
+            if (c->world > 1) r = run_ep(c, l, c->h_post, T, nullptr, nullptr, d_hidden, d_hidden, s);
+            else if (T > 0) r = run_local(c, l, c->h_post, T, nullptr, nullptr, 1, 1, d_hidden, d_hidden, s);
+            if (r) return r;
+            r = record_hits(c, l, c->world > 1 || T > 0, s);
+            if (r) return r;
+        }
+        return MOE_OK;
+    });
 }
 
 int moe_forward_stack(moe_ctx *c, int first, int n_layers, float *hidden, int T) {

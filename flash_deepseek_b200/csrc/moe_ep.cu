@@ -67,10 +67,10 @@ __global__ void k_ep_pack(const float *__restrict__ x, const int *__restrict__ i
 }
 
 // Plan over the received rows (experts this rank owns) + the shared expert on
-// the local rows.  One block; dynamic smem = (E+1) * MW * 8 bytes of masks.
-__global__ void __launch_bounds__(512) k_ep_plan(MoeDims d, const int *__restrict__ recv_meta, int world, int cap,
-                                                 int T, int e0, int n_local, MoePlan plan) {
-    extern __shared__ unsigned long long mask[];  // [E+1][MW]
+// the local rows, by one block; mask = dynamic shared memory of
+// (E+1) * MW * 8 bytes.
+__device__ void ep_plan_block(const MoeDims &d, const int *__restrict__ recv_meta, int world, int cap, int T, int e0,
+                              int n_local, const MoePlan &plan, unsigned long long *mask) {
     __shared__ int cnt[1025], off[1026], coff[1026];
     __shared__ int wsum[3][32], carry[3];
     const int E = d.E, K = d.K, NE = E + 1;
@@ -189,6 +189,12 @@ __global__ void __launch_bounds__(512) k_ep_plan(MoeDims d, const int *__restric
     moe_plan_order_chunks(plan, carry[1]);
 }
 
+__global__ void __launch_bounds__(512) k_ep_plan(MoeDims d, const int *__restrict__ recv_meta, int world, int cap,
+                                                 int T, int e0, int n_local, MoePlan plan) {
+    extern __shared__ unsigned long long ep_mask[];  // [E+1][MW]
+    ep_plan_block(d, recv_meta, world, cap, T, e0, n_local, plan, ep_mask);
+}
+
 // Pre-combine on the expert side: partial[r] = sum over the slots of received
 // row r whose expert lives here, in slot order, of w_k * eo.
 __global__ void k_ep_partial(MoeDims d, MoePlan plan, const int *__restrict__ recv_meta, const float *__restrict__ eo,
@@ -271,9 +277,13 @@ void moe_launch_ep_final(const MoeDims &d, const MoePlan &plan, const float *rec
 // kernel's blocks are done (every thread fences its stores at system scope),
 // its last block writes the step number into the matching flag of every
 // peer (release, system scope).  The consumers wait (acquire, bounded) for
-// the flags of all peers.  Buffers alternate by step parity: a rank cannot
-// reach step n + 2 before every peer has finished consuming step n (it needs
-// their step n + 1 partials first).
+// the flags of all peers: the plan / operand kernel for the dispatch flags,
+// the final sum for the combine flags.  Buffers alternate by step parity: a
+// rank cannot reach step n + 2 before every peer has finished consuming step
+// n (it needs their step n + 1 partials first).  The step number lives in
+// device memory (EpP2P::d_seq): every kernel of a step reads seq = *d_seq +
+// 1, and the final sum's last block stores seq, so a step's launches carry
+// no per-step host arguments and replay as a CUDA graph.
 // ===========================================================================
 #define EP_WAIT_NS 2000000000ull
 
@@ -290,12 +300,26 @@ __device__ __forceinline__ unsigned long long ep_now() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+// the step this launch belongs to
+__device__ __forceinline__ unsigned long long ep_step(const EpP2P &q) { return *q.d_seq + 1ull; }
 
-// every thread: wait until flags[p] >= seq for all p < world (bounded)
+__device__ bool ep_wait_flags(const unsigned long long *flags, int world, unsigned long long seq, int *error);
+// the whole block waits: thread 0 acquires the flags (system scope), the
+// block barrier then orders every thread's later reads after the peers'
+// released stores
+__device__ __forceinline__ void ep_block_wait(const unsigned long long *flags, int world, unsigned long long seq,
+                                              int *error) {
+    if (threadIdx.x == 0) ep_wait_flags(flags, world, seq, error);
+    __syncthreads();
+}
+
+// every thread: wait until flags[p] >= seq for all p < world (bounded; a
+// wait that another thread of the step already gave up on is not repeated)
 __device__ bool ep_wait_flags(const unsigned long long *flags, int world, unsigned long long seq, int *error) {
     const unsigned long long t0 = ep_now();
     for (int p = 0; p < world; p++)
         while (ep_ld_acquire(flags + p) < seq) {
+            if (*reinterpret_cast<volatile int *>(error) == EP_ERR_TIMEOUT) return false;
             if (ep_now() - t0 > EP_WAIT_NS) {
                 atomicExch(error, EP_ERR_TIMEOUT);
                 return false;
@@ -309,7 +333,7 @@ __device__ bool ep_wait_flags(const unsigned long long *flags, int world, unsign
 // block barrier orders every thread's stores before thread 0's system-scope
 // fence, which is cumulative, so one fence per block publishes them all (the
 // pattern of a cooperative grid barrier).
-__device__ void ep_signal(const EpP2P &q, size_t flag_off, int *done) {
+__device__ void ep_signal(const EpP2P &q, size_t flag_off, int *done, unsigned long long seq) {
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence_system();
@@ -318,16 +342,17 @@ __device__ void ep_signal(const EpP2P &q, size_t flag_off, int *done) {
             *done = 0;  // stream order keeps the next launch behind this reset
             __threadfence_system();
             for (int p = 0; p < q.world; p++)
-                ep_st_release(reinterpret_cast<unsigned long long *>(q.peers[p] + flag_off) + q.me, q.seq);
+                ep_st_release(reinterpret_cast<unsigned long long *>(q.peers[p] + flag_off) + q.me, seq);
         }
     }
 }
 
 // grid = T blocks (+1 that clears the unused rows' valid flags on every peer)
 __global__ void k_ep_pack_p2p(const float *__restrict__ x, const int *__restrict__ idx, const float *__restrict__ w,
-                              int T, int K, int H, int n_local, int cap, EpP2P q, int *__restrict__ tok_slot,
-                              int *done) {
+                              int T, int K, int H, int n_local, int cap, EpP2P q, int *__restrict__ tok_slot) {
     __shared__ unsigned long long pm[64];
+    const unsigned long long seq = ep_step(q);
+    const int parity = (int)(seq & 1ull);
     const int world = q.world, meta_w = 2 + 2 * K;
     const size_t R = (size_t)world * cap;
     for (int p = threadIdx.x; p < world; p += blockDim.x) pm[p] = peer_mask(idx, T, K, n_local, p);
@@ -336,7 +361,7 @@ __global__ void k_ep_pack_p2p(const float *__restrict__ x, const int *__restrict
         for (int s = threadIdx.x; s < world * cap; s += blockDim.x) {
             const int p = s / cap, i = s % cap;
             if (i >= __popcll(pm[p])) {
-                int *meta = reinterpret_cast<int *>(q.peers[p] + q.off_meta) + (size_t)q.parity * R * meta_w;
+                int *meta = reinterpret_cast<int *>(q.peers[p] + q.off_meta) + (size_t)parity * R * meta_w;
                 meta[((size_t)q.me * cap + i) * meta_w] = 0;
             }
         }
@@ -347,7 +372,7 @@ __global__ void k_ep_pack_p2p(const float *__restrict__ x, const int *__restrict
             const int slot = hit ? __popcll(pm[p] & ((1ull << t) - 1ull)) : -1;
             if (threadIdx.x == 0) tok_slot[t * world + p] = slot;
             if (!hit) continue;
-            const size_t row = (size_t)q.parity * R + (size_t)q.me * cap + slot;
+            const size_t row = (size_t)parity * R + (size_t)q.me * cap + slot;
             const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)t * H);
             float4 *dst = reinterpret_cast<float4 *>(reinterpret_cast<float *>(q.peers[p] + q.off_x) + row * H);
             for (int i = threadIdx.x; i < H / 4; i += blockDim.x) dst[i] = src[i];
@@ -359,15 +384,43 @@ __global__ void k_ep_pack_p2p(const float *__restrict__ x, const int *__restrict
             }
         }
     }
-    ep_signal(q, 0, done);
+    ep_signal(q, 0, q.done, seq);
+}
+
+// After the peers' dispatch flags: block 0 builds the plan over the received
+// rows (experts of this rank) and the local rows (shared expert); block
+// 1 + r builds the operand of row r (received rows [0, R) whose slot is in
+// use, then the T local rows).  Dynamic shared memory: the plan's masks.
+__global__ void __launch_bounds__(512) k_ep_plan_rows_p2p(MoeDims d, EpP2P q, int cap, int T, int e0, int n_local,
+                                                          MoePlan plan, const float *__restrict__ local,
+                                                          uint8_t *__restrict__ xop) {
+    extern __shared__ unsigned long long ep_mask2[];
+    const unsigned long long seq = ep_step(q);
+    const int parity = (int)(seq & 1ull);
+    const int R = q.world * cap, meta_w = 2 + 2 * d.K;
+    const uint8_t *own = q.peers[q.me];
+    ep_block_wait(reinterpret_cast<const unsigned long long *>(own), q.world, seq, q.error);
+    const int *meta = reinterpret_cast<const int *>(own + q.off_meta) + (size_t)parity * R * meta_w;
+    if (blockIdx.x == 0) {
+        ep_plan_block(d, meta, q.world, cap, T, e0, n_local, plan, ep_mask2);
+        return;
+    }
+    const int r = blockIdx.x - 1;
+    if (r < R && !__ldcg(meta + (size_t)r * meta_w)) return;
+    const float *recv = reinterpret_cast<const float *>(own + q.off_x) + (size_t)parity * R * d.H;
+    uint8_t *row = xop + (size_t)r * opx_row(d.H);
+    build_op_rows(r < R ? recv + (size_t)r * d.H : local + (size_t)(r - R) * d.H, d.H, row, row + op_bytes(d.H), 4);
 }
 
 // pre-combine (k_ep_partial's sum) stored straight into the token rank's
 // mailbox: received row r = (source p, slot s) -> p's recv_y row me*cap + s
-__global__ void k_ep_partial_p2p(MoeDims d, MoePlan plan, const int *__restrict__ recv_meta,
-                                 const float *__restrict__ eo, int cap, EpP2P q, int *done) {
+__global__ void k_ep_partial_p2p(MoeDims d, MoePlan plan, const float *__restrict__ eo, int cap, EpP2P q) {
+    const unsigned long long seq = ep_step(q);
+    const int parity = (int)(seq & 1ull);
     const int r = blockIdx.y, i4 = blockIdx.x * blockDim.x + threadIdx.x;  // float4 column
     const int K = d.K;
+    const size_t R = (size_t)q.world * cap;
+    const int *recv_meta = reinterpret_cast<const int *>(q.peers[q.me] + q.off_meta) + (size_t)parity * R * (2 + 2 * K);
     if (i4 < d.H / 4 && recv_meta[(size_t)r * (2 + 2 * K)]) {
         float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         for (int k = 0; k < K; k++) {
@@ -381,33 +434,75 @@ __global__ void k_ep_partial_p2p(MoeDims d, MoePlan plan, const int *__restrict_
             acc.w = fmaf(wp, e.w, acc.w);
         }
         const int src = r / cap, s = r % cap;
-        const size_t R = (size_t)q.world * cap;
-        float *y = reinterpret_cast<float *>(q.peers[src] + q.off_y) + (size_t)q.parity * R * d.H;
+        float *y = reinterpret_cast<float *>(q.peers[src] + q.off_y) + (size_t)parity * R * d.H;
         reinterpret_cast<float4 *>(y + ((size_t)q.me * cap + s) * d.H)[i4] = acc;
     }
-    ep_signal(q, 64 * sizeof(unsigned long long), done);
+    ep_signal(q, 64 * sizeof(unsigned long long), q.done + 1, seq);
 }
 
-// the dispatch flags of every peer, before the plan reads the mailbox
-__global__ void k_ep_wait(const unsigned long long *flags, int world, unsigned long long seq, int *error) {
-    ep_wait_flags(flags, world, seq, error);
+// After the peers' combine flags: out[t] = sum over ranks (rank order) of the
+// returned partials + shared expert (+ residual); then the last block stores
+// the step number (the step is complete on this rank).  grid.y = max(T, 1).
+__global__ void k_ep_final_p2p(MoeDims d, MoePlan plan, EpP2P q, const int *__restrict__ tok_slot, int cap, int T,
+                               const float *__restrict__ eo, const float *__restrict__ residual,
+                               float *__restrict__ out) {
+    const unsigned long long seq = ep_step(q);
+    const int parity = (int)(seq & 1ull);
+    const int t = blockIdx.y, i = blockIdx.x * blockDim.x + threadIdx.x;
+    const uint8_t *own = q.peers[q.me];
+    ep_block_wait(reinterpret_cast<const unsigned long long *>(own) + 64, q.world, seq, q.error);
+    if (t < T && i < d.H) {
+        const size_t R = (size_t)q.world * cap;
+        const float *recv_y = reinterpret_cast<const float *>(own + q.off_y) + (size_t)parity * R * d.H;
+        float acc = 0.0f;
+        for (int p = 0; p < q.world; p++) {
+            const int s = tok_slot[t * q.world + p];
+            if (s >= 0) acc = acc + __ldcg(recv_y + ((size_t)p * cap + s) * d.H + i);
+        }
+        const int sp = plan.slot_pair[(size_t)(q.world * cap + t) * (d.K + 1) + d.K];
+        acc = acc + eo[(size_t)sp * d.H + i];
+        if (residual) acc = residual[(size_t)t * d.H + i] + acc;
+        out[(size_t)t * d.H + i] = acc;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned int nblk = gridDim.x * gridDim.y;
+        if (atomicAdd(q.done + 2, 1) == (int)nblk - 1) {  // every block has read the step number
+            q.done[2] = 0;
+            *q.d_seq = seq;
+        }
+    }
 }
 
 void moe_launch_ep_pack_p2p(const float *x, const int *idx, const float *w, int T, int K, int H, int n_local,
-                            int cap, const EpP2P &q, int *tok_slot, int *done, cudaStream_t s, uint64_t *launches) {
-    k_ep_pack_p2p<<<T + 1, 256, 0, s>>>(x, idx, w, T, K, H, n_local, cap, q, tok_slot, done);
+                            int cap, const EpP2P &q, int *tok_slot, cudaStream_t s, uint64_t *launches) {
+    k_ep_pack_p2p<<<T + 1, 256, 0, s>>>(x, idx, w, T, K, H, n_local, cap, q, tok_slot);
     LAUNCH_COUNT(launches);
 }
 
-void moe_launch_ep_partial_p2p(const MoeDims &d, const MoePlan &plan, const int *recv_meta, const float *eo, int cap,
-                               const EpP2P &q, int *done, cudaStream_t s, uint64_t *launches) {
+void moe_launch_ep_plan_rows_p2p(const MoeDims &d, const EpP2P &q, int cap, int T, int e0, int n_local,
+                                 const MoePlan &plan, const float *local, uint8_t *xop, cudaStream_t s,
+                                 uint64_t *launches) {
+    const int R = q.world * cap;
+    const int MW = (R + T + 63) / 64;
+    const size_t smem = sizeof(unsigned long long) * (size_t)(d.E + 1) * MW;
+    static size_t attr[MOE_MAX_DEVICES];
+    if (smem > 48 * 1024) moe_smem_limit(k_ep_plan_rows_p2p, smem, attr);
+    k_ep_plan_rows_p2p<<<1 + R + T, 512, smem, s>>>(d, q, cap, T, e0, n_local, plan, local, xop);
+    LAUNCH_COUNT(launches);
+}
+
+void moe_launch_ep_partial_p2p(const MoeDims &d, const MoePlan &plan, const float *eo, int cap, const EpP2P &q,
+                               cudaStream_t s, uint64_t *launches) {
     dim3 grid((d.H / 4 + 255) / 256, q.world * cap);  // H % 256 == 0 (checked at create)
-    k_ep_partial_p2p<<<grid, 256, 0, s>>>(d, plan, recv_meta, eo, cap, q, done);
+    k_ep_partial_p2p<<<grid, 256, 0, s>>>(d, plan, eo, cap, q);
     LAUNCH_COUNT(launches);
 }
 
-void moe_launch_ep_wait(const unsigned long long *flags, int world, unsigned long long seq, int *error, cudaStream_t s,
-                        uint64_t *launches) {
-    k_ep_wait<<<1, 32, 0, s>>>(flags, world, seq, error);
+void moe_launch_ep_final_p2p(const MoeDims &d, const MoePlan &plan, const EpP2P &q, const int *tok_slot, int cap,
+                             int T, const float *eo, const float *residual, float *out, cudaStream_t s,
+                             uint64_t *launches) {
+    dim3 grid((d.H + 255) / 256, T > 0 ? T : 1);
+    k_ep_final_p2p<<<grid, 256, 0, s>>>(d, plan, q, tok_slot, cap, T, eo, residual, out);
     LAUNCH_COUNT(launches);
 }

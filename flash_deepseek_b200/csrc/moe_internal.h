@@ -235,19 +235,31 @@ void moe_launch_prep_rows(const float *recv, const int *meta, int meta_w, int R,
 void moe_launch_ep_pack(const float *x, const int *idx, const float *w, int T, int K, int H, int world, int n_local,
                         int cap, float *send_x, int *send_meta, int *tok_slot, cudaStream_t s, uint64_t *launches);
 // NVLink peer-memory exchange (moe_ep.cu): mailbox base of every rank
-// (peers[me] = own), byte offsets of its regions, the step's parity and number
+// (peers[me] = own), byte offsets of its regions, and the step counter in
+// device memory (steps completed by this rank; every kernel of a step uses
+// seq = *d_seq + 1 and the buffers of parity seq & 1, and the step's last
+// kernel advances it), so that a step's launches replay as a CUDA graph.
 struct EpP2P {
     uint8_t *const *peers;
     size_t off_x, off_meta, off_y;
-    int world, me, parity;
-    unsigned long long seq;
+    int world, me;
+    unsigned long long *d_seq;
+    int *done;   // [3] block counters of the three signalling kernels
+    int *error;  // plan.error: a peer's flag that did not arrive
 };
 void moe_launch_ep_pack_p2p(const float *x, const int *idx, const float *w, int T, int K, int H, int n_local,
-                            int cap, const EpP2P &q, int *tok_slot, int *done, cudaStream_t s, uint64_t *launches);
-void moe_launch_ep_partial_p2p(const MoeDims &d, const MoePlan &plan, const int *recv_meta, const float *eo, int cap,
-                               const EpP2P &q, int *done, cudaStream_t s, uint64_t *launches);
-void moe_launch_ep_wait(const unsigned long long *flags, int world, unsigned long long seq, int *error, cudaStream_t s,
-                        uint64_t *launches);
+                            int cap, const EpP2P &q, int *tok_slot, cudaStream_t s, uint64_t *launches);
+// waits for the peers' dispatch flags, then one block builds the plan and the
+// others the operand rows of the received and local rows
+void moe_launch_ep_plan_rows_p2p(const MoeDims &d, const EpP2P &q, int cap, int T, int e0, int n_local,
+                                 const MoePlan &plan, const float *local, uint8_t *xop, cudaStream_t s,
+                                 uint64_t *launches);
+void moe_launch_ep_partial_p2p(const MoeDims &d, const MoePlan &plan, const float *eo, int cap, const EpP2P &q,
+                               cudaStream_t s, uint64_t *launches);
+// waits for the peers' combine flags, sums, and advances the step counter
+void moe_launch_ep_final_p2p(const MoeDims &d, const MoePlan &plan, const EpP2P &q, const int *tok_slot, int cap,
+                             int T, const float *eo, const float *residual, float *out, cudaStream_t s,
+                             uint64_t *launches);
 void moe_launch_ep_plan(const MoeDims &d, const int *recv_meta, int world, int cap, int T, int e0, int n_local,
                         const MoePlan &plan, cudaStream_t s, uint64_t *launches);
 void moe_launch_ep_partial(const MoeDims &d, const MoePlan &plan, const int *recv_meta, const float *eo, int rows,

@@ -512,139 +512,6 @@ void moe_launch_router_logits(const float *Wr, const float *x, int T, int H, int
     LAUNCH_COUNT(launches);
 }
 
-// power-of-two scale s with max|x| * s in [2^(top-1), 2^top); returns s, sets
-// *inv = 1/s.  The int8-plane operand uses top = 20 (|rint(x * s)| <= 2^20).
-__device__ __forceinline__ float op_scale(float amax, float *inv, int top) {
-    if (!(amax > 0.0f) || !isfinite(amax)) { *inv = 1.0f; return 1.0f; }
-    int ex;
-    frexpf(amax, &ex);  // amax = m 2^ex, m in [0.5, 1)
-    int e = top - ex;
-    if (e > 120) e = 120;
-    if (e < -120) e = -120;
-    *inv = ldexpf(1.0f, -e);
-    return ldexpf(1.0f, e);
-}
-
-// One 256-weight super-block of one vector, built by one warp: s = power of
-// two from the super-block's max |x| (|rint(x s)| <= 2^20), int8 planes in
-// the lane order of `style` (4: Q4_K weights, with the fp16 sums of 16
-// consecutive plane values; 6: Q6_K weights) and 1/s.  Layout in
-// moe_common.cuh.  x must be 16-byte aligned.
-__device__ __forceinline__ void build_op_sb(const float *__restrict__ x, uint8_t *__restrict__ op, int style,
-                                            int lane) {
-    const float4 a = __ldg(reinterpret_cast<const float4 *>(x) + 2 * lane);
-    const float4 b = __ldg(reinterpret_cast<const float4 *>(x) + 2 * lane + 1);
-    const float v8[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    float m = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; i++) m = fmaxf(m, fabsf(v8[i]));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float inv;
-    const float s = op_scale(m, &inv, 20);
-    uint32_t w[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};
-    int ps[3] = {0, 0, 0};
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const int v = __float2int_rn(__fmul_rn(v8[i], s));
-        const int p0 = v & 127, p1 = (v >> 7) & 127, p2 = v >> 14;
-        w[0][i >> 2] |= (uint32_t)p0 << (8 * (i & 3));
-        w[1][i >> 2] |= (uint32_t)p1 << (8 * (i & 3));
-        w[2][i >> 2] |= (uint32_t)(p2 & 255) << (8 * (i & 3));
-        ps[0] += p0;
-        ps[1] += p1;
-        ps[2] += p2;
-    }
-    const int k = 8 * lane;
-    const int off0 = style == 4 ? opq4_off(k) : opq6_off(k), off1 = style == 4 ? opq4_off(k + 4) : opq6_off(k + 4);
-#pragma unroll
-    for (int p = 0; p < 3; p++) {
-        *reinterpret_cast<uint32_t *>(op + p * OPB_PLANE + off0) = w[p][0];
-        *reinterpret_cast<uint32_t *>(op + p * OPB_PLANE + off1) = w[p][1];
-    }
-    if (style == 4) {  // lanes 2j, 2j + 1 hold the 16 values [16 j, 16 j + 16)
-        int tot[3];
-#pragma unroll
-        for (int p = 0; p < 3; p++) tot[p] = ps[p] + __shfl_xor_sync(0xffffffffu, ps[p], 1);
-        if ((lane & 1) == 0) {
-#pragma unroll
-            for (int p = 0; p < 3; p++)
-                *reinterpret_cast<__half *>(op + p * OPB_PLANE + opq4_xsum_off(lane >> 1)) = __int2half_rn(tot[p]);
-        }
-    }
-    if (lane == 0) *reinterpret_cast<float *>(op + OPB_SCALE) = inv;
-}
-
-// One 256-weight super-block of one vector in the wide (fp16 hi/lo) form,
-// built by one warp (layout in moe_common.cuh): s = power of two from the
-// super-block's max |x| (max |x s| in [2^14, 2^15)), x_hi = fp16(x s),
-// x_lo = fp16(x s - x_hi), both planes in the lane order of `style`; style 4
-// adds the sub-block sums of x_hi + x_lo (divided by 32, as fp16 hi/lo) for
-// the Q4_K min term.  x must be 16-byte aligned.
-__device__ __forceinline__ void build_opw_sb(const float *__restrict__ x, uint8_t *__restrict__ op, int style,
-                                             int lane) {
-    const float4 a = __ldg(reinterpret_cast<const float4 *>(x) + 2 * lane);
-    const float4 b = __ldg(reinterpret_cast<const float4 *>(x) + 2 * lane + 1);
-    const float v8[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    float m = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; i++) m = fmaxf(m, fabsf(v8[i]));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float inv;
-    const float sc = op_scale(m, &inv, OPW_TOP);
-    __half hi[8], lo[8];
-    float sum = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const float xs = __fmul_rn(v8[i], sc);  // exact: sc is a power of two
-        hi[i] = __float2half_rn(xs);
-        const float hv = __half2float(hi[i]);
-        lo[i] = __float2half_rn(__fsub_rn(xs, hv));  // xs - hv is exact in fp32
-        sum = __fadd_rn(sum, __fadd_rn(hv, __half2float(lo[i])));  // hv + lo exact (22 bits)
-    }
-    __half *H = reinterpret_cast<__half *>(op), *L = reinterpret_cast<__half *>(op + OPW_LO);
-    if (style == 4) {
-        // elements 8 lane + i: sub-block lane / 4, t = lane % 4 -> 16 contiguous bytes
-        const int base = 8 * lane;  // opw4_idx(8 lane + i) = 8 lane + perm(i)
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const int ix = base + ((i & 4) | ((i & 1) << 1) | ((i >> 1) & 1));
-            H[ix] = hi[i];
-            L[ix] = lo[i];
-        }
-        // sub-block j = lane / 4: sum over its four lanes in a fixed order
-        sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 1));
-        sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, 2));
-        if ((lane & 3) == 0) {
-            const float s32 = __fmul_rn(sum, 0.03125f);  // exact
-            const __half sh = __float2half_rn(s32);
-            const __half sl = __float2half_rn(__fsub_rn(s32, __half2float(sh)));
-            reinterpret_cast<__half *>(op + OPW_XSUM)[lane >> 2] = sh;
-            reinterpret_cast<__half *>(op + OPW_XSUM + 16)[lane >> 2] = sl;
-        }
-    } else {
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const int ix = opw6_idx(8 * lane + i);
-            H[ix] = hi[i];
-            L[ix] = lo[i];
-        }
-    }
-    if (lane == 0) *reinterpret_cast<float *>(op + OPW_SCALE) = inv;
-}
-
-// Operand of a K-vector by the warps of the block, one super-block per warp:
-// the int8 planes into op8 and, when opw is set, the fp16 planes into opw.
-__device__ __forceinline__ void build_op_rows(const float *__restrict__ x, int K, uint8_t *__restrict__ op8,
-                                              uint8_t *__restrict__ opw, int style) {
-    const int lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    for (int sb = threadIdx.x >> 5; sb < K / MOE_QK; sb += nw) {
-        if (op8) build_op_sb(x + (size_t)sb * MOE_QK, op8 + (size_t)sb * OPB_SB, style, lane);
-        if (opw) build_opw_sb(x + (size_t)sb * MOE_QK, opw + (size_t)sb * OPW_SB, style, lane);
-    }
-}
-
 // ===========================================================================
 // Route + plan.  Grid = T blocks of 256 threads (one thread per expert).
 // ===========================================================================
