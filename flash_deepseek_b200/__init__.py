@@ -17,6 +17,7 @@ library; if it is missing, importing ``load_library`` raises.
 from __future__ import annotations
 
 import ctypes as C
+import os
 from dataclasses import dataclass
 
 import numpy as np
@@ -165,6 +166,27 @@ class MoE:
         self._check(self.lib.moe_load_layer(self.ctx, layer, _ptr(arrs[0]), _ptr(arrs[1]), _ptr(arrs[2]), down_type,
                                             _ptr(rw), _ptr(b), _ptr(arrs[3]), _ptr(arrs[4]), _ptr(arrs[5]),
                                             sh_down_type), "moe_load_layer")
+
+    def shard_range(self, per_expert_bytes: int) -> tuple[int, int]:
+        """(offset, bytes) of this rank's experts inside a stacked expert tensor."""
+        off, n = C.c_size_t(), C.c_size_t()
+        self._check(self.lib.moe_shard_range(self.ctx, per_expert_bytes, C.byref(off), C.byref(n)),
+                    "moe_shard_range")
+        return off.value, n.value
+
+    def load_layer_shard(self, layer, gate_slice, up_slice, down_slice, down_type, router_w, bias, sh_gate, sh_up,
+                         sh_down, sh_down_type):
+        """moe_load_layer with the expert tensors cut to this rank's slice."""
+        arrs = [np.ascontiguousarray(a, np.uint8) for a in (gate_slice, up_slice, down_slice, sh_gate, sh_up, sh_down)]
+        rw = _f32(router_w)
+        b = None if bias is None else _f32(bias)
+        self._check(self.lib.moe_load_layer_shard(self.ctx, layer, _ptr(arrs[0]), _ptr(arrs[1]), _ptr(arrs[2]),
+                                                  down_type, _ptr(rw), _ptr(b), _ptr(arrs[3]), _ptr(arrs[4]),
+                                                  _ptr(arrs[5]), sh_down_type), "moe_load_layer_shard")
+
+    def write_layer_packed(self, layer: int, path: str):
+        """This rank's experts of `layer` into the reference's packed layer file."""
+        self._check(self.lib.moe_write_layer_packed(self.ctx, layer, os.fsencode(path)), "moe_write_layer_packed")
 
     def load_layer_packed(self, layer, layer_blob, expert_size, router_w, bias, sh_gate, sh_up, sh_down,
                           sh_down_type):

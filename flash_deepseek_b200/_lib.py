@@ -33,6 +33,8 @@ SIGNATURES = {
     "moe_world_size": (C.c_int, [_vp]),
     "moe_ep_peer_memory": (C.c_int, [_vp]),
     "moe_load_layer": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, C.c_int, _vp, _vp, _vp, _vp, _vp, C.c_int]),
+    "moe_load_layer_shard": (C.c_int, [_vp, C.c_int, _vp, _vp, _vp, C.c_int, _vp, _vp, _vp, _vp, _vp, C.c_int]),
+    "moe_shard_range": (C.c_int, [_vp, C.c_size_t, C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
     "moe_load_layer_packed": (C.c_int, [_vp, C.c_int, _vp, C.c_size_t, _vp, _vp, _vp, _vp, _vp, C.c_int]),
     "moe_init_layer_synthetic": (C.c_int, [_vp, C.c_int, C.c_uint64, C.c_int, C.c_double, C.c_double,
                                            C.c_double]),
@@ -41,6 +43,7 @@ SIGNATURES = {
     "moe_set_norm_weight": (C.c_int, [_vp, C.c_int, _vp]),
     "moe_read_expert": (C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_size_t]),
     "moe_expert_bytes": (C.c_size_t, [_vp, C.c_int]),
+    "moe_write_layer_packed": (C.c_int, [_vp, C.c_int, C.c_char_p]),
     "moe_forward": (C.c_int, [_vp, C.c_int, _vp, C.c_int, _vp, _vp, _vp]),
     "moe_forward_device": (C.c_int, [_vp, C.c_int, _vp, C.c_int, _vp, _vp, _vp, _vp]),
     "moe_check_error": (C.c_int, [_vp]),

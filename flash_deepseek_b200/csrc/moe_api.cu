@@ -492,9 +492,10 @@ static int put_down(moe_ctx *c, uint8_t *dst, const void *src, int type, bool sr
     return MOE_OK;
 }
 
-int moe_load_layer(moe_ctx *c, int layer, const void *gate_exps, const void *up_exps, const void *down_exps,
-                   int down_type, const float *router_w, const float *bias, const void *sh_gate, const void *sh_up,
-                   const void *sh_down, int sh_down_type) {
+// slice: the expert tensors hold only this rank's experts (e0 .. e0 + n_local - 1)
+static int load_layer_impl(moe_ctx *c, int layer, const void *gate_exps, const void *up_exps, const void *down_exps,
+                           int down_type, const float *router_w, const float *bias, const void *sh_gate,
+                           const void *sh_up, const void *sh_down, int sh_down_type, bool slice) {
     if (!c) return MOE_ERR_ARG;
     DeviceScope ds(c->device);
     if (!gate_exps || !up_exps || !down_exps || !router_w || !sh_gate || !sh_up || !sh_down)
@@ -509,7 +510,7 @@ int moe_load_layer(moe_ctx *c, int layer, const void *gate_exps, const void *up_
     for (int j = 0; j <= c->n_local; j++) {
         uint8_t *dst = L.experts + (size_t)j * L.expert_stride;
         const bool sh = j == c->n_local;
-        const int e = c->e0 + j;
+        const int e = slice ? j : c->e0 + j;  // index inside the tensors given
         const uint8_t *g = sh ? (const uint8_t *)sh_gate : (const uint8_t *)gate_exps + (size_t)e * gb;
         const uint8_t *u = sh ? (const uint8_t *)sh_up : (const uint8_t *)up_exps + (size_t)e * gb;
         const uint8_t *dn = sh ? (const uint8_t *)sh_down : (const uint8_t *)down_exps + (size_t)e * db;
@@ -526,6 +527,27 @@ int moe_load_layer(moe_ctx *c, int layer, const void *gate_exps, const void *up_
     if (bias) CK(cudaMemcpyAsync(L.bias, bias, sizeof(float) * E, cudaMemcpyHostToDevice, c->stream));
     else CK(cudaMemsetAsync(L.bias, 0, sizeof(float) * E, c->stream));
     CK(cudaStreamSynchronize(c->stream));
+    return MOE_OK;
+}
+
+int moe_load_layer(moe_ctx *c, int layer, const void *gate_exps, const void *up_exps, const void *down_exps,
+                   int down_type, const float *router_w, const float *bias, const void *sh_gate, const void *sh_up,
+                   const void *sh_down, int sh_down_type) {
+    return load_layer_impl(c, layer, gate_exps, up_exps, down_exps, down_type, router_w, bias, sh_gate, sh_up,
+                           sh_down, sh_down_type, false);
+}
+
+int moe_load_layer_shard(moe_ctx *c, int layer, const void *gate_slice, const void *up_slice, const void *down_slice,
+                         int down_type, const float *router_w, const float *bias, const void *sh_gate,
+                         const void *sh_up, const void *sh_down, int sh_down_type) {
+    return load_layer_impl(c, layer, gate_slice, up_slice, down_slice, down_type, router_w, bias, sh_gate, sh_up,
+                           sh_down, sh_down_type, true);
+}
+
+int moe_shard_range(const moe_ctx *c, size_t per_expert_bytes, size_t *offset, size_t *bytes) {
+    if (!c || !offset || !bytes) return MOE_ERR_ARG;
+    *offset = (size_t)c->e0 * per_expert_bytes;
+    *bytes = (size_t)c->n_local * per_expert_bytes;
     return MOE_OK;
 }
 
@@ -685,6 +707,31 @@ int moe_read_expert(moe_ctx *c, int layer, int expert, void *dst, size_t dst_siz
     if (e1 != cudaSuccess || e2 != cudaSuccess || e3 != cudaSuccess)
         return fail(c, MOE_ERR_CUDA, "moe_read_expert: unpack failed");
     return MOE_OK;
+}
+
+int moe_write_layer_packed(moe_ctx *c, int layer, const char *path) {
+    if (!c || !path) return MOE_ERR_ARG;
+    if (layer < 0 || layer >= (int)c->layers.size() || !c->layers[layer].experts)
+        return fail(c, MOE_ERR_STATE, "layer %d not loaded", layer);
+    const size_t es = moe_expert_bytes(c, layer);
+    FILE *f = fopen(path, "r+b");
+    if (!f) f = fopen(path, "w+b");
+    if (!f) return fail(c, MOE_ERR_ARG, "moe_write_layer_packed: cannot open %s", path);
+    std::vector<uint8_t> buf(es);
+    int rc = MOE_OK;
+    // the file holds all n_experts experts (a rank writes only its own range)
+    if (fseeko(f, (off_t)((size_t)c->d.E * es) - 1, SEEK_SET) != 0 || fgetc(f) == EOF) {
+        if (fseeko(f, (off_t)((size_t)c->d.E * es) - 1, SEEK_SET) != 0 || fputc(0, f) == EOF)
+            rc = fail(c, MOE_ERR_ARG, "moe_write_layer_packed: cannot size %s", path);
+    }
+    for (int j = 0; j < c->n_local && rc == MOE_OK; j++) {
+        const int e = c->e0 + j;
+        rc = moe_read_expert(c, layer, e, buf.data(), es);
+        if (rc == MOE_OK && (fseeko(f, (off_t)((size_t)e * es), SEEK_SET) != 0 || fwrite(buf.data(), 1, es, f) != es))
+            rc = fail(c, MOE_ERR_ARG, "moe_write_layer_packed: write to %s failed", path);
+    }
+    if (fclose(f) != 0 && rc == MOE_OK) rc = fail(c, MOE_ERR_ARG, "moe_write_layer_packed: closing %s failed", path);
+    return rc;
 }
 
 // ------------------------------------------------------------------ forward

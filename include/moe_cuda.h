@@ -110,6 +110,21 @@ int moe_load_layer(moe_ctx *ctx, int layer, const void *gate_exps, const void *u
                    const float *bias, const void *sh_gate, const void *sh_up,
                    const void *sh_down, int sh_down_type);
 
+/* Same, with the stacked expert tensors holding only this rank's routed
+ * experts (global ids moe_shard_range's offset / per-expert size on, n_experts
+ * / world_size of them), so that each rank of an expert-parallel context
+ * reads just its slice of blk.L.ffn_{gate,up,down}_exps.weight with
+ * gguf_tensor_pread(t, buf, bytes, offset) (gguf.h:192) instead of the whole
+ * tensor.  Router, bias and shared expert as for moe_load_layer. */
+int moe_load_layer_shard(moe_ctx *ctx, int layer, const void *gate_slice, const void *up_slice,
+                         const void *down_slice, int down_type, const float *router_w,
+                         const float *bias, const void *sh_gate, const void *sh_up,
+                         const void *sh_down, int sh_down_type);
+/* Byte range of this rank's experts inside a stacked expert tensor of
+ * per_expert_bytes per expert: *offset = first expert * per_expert_bytes,
+ * *bytes = experts per rank * per_expert_bytes. */
+int moe_shard_range(const moe_ctx *ctx, size_t per_expert_bytes, size_t *offset, size_t *bytes);
+
 /* Same, from the reference's packed expert file layout (packed_experts/
  * layer_XX.bin: expert e at e*expert_size = [gate][up][down],
  * repack_experts.c:157-238, infer.m:1802-1823); the down type is inferred
@@ -143,6 +158,15 @@ int moe_set_norm_weight(moe_ctx *ctx, int layer, const float *w);
  * be at least moe_expert_bytes(). */
 int moe_read_expert(moe_ctx *ctx, int layer, int expert, void *dst, size_t dst_size);
 size_t moe_expert_bytes(const moe_ctx *ctx, int layer);
+
+/* Writes the routed experts of layer L that this rank holds into the
+ * reference's packed per-layer expert file (packed_experts/layer_XX.bin,
+ * written by repack_experts.c:157-238 and read by infer.m:1802-1823): expert
+ * e's GGUF bytes [gate][up][down] at e * moe_expert_bytes(), no header.  The
+ * file is sized for all n_experts experts and opened without truncation, so
+ * the ranks of an expert-parallel context can each write their part of one
+ * file. */
+int moe_write_layer_packed(moe_ctx *ctx, int layer, const char *path);
 
 /* ---------------------------------------------------------------- forward */
 /* The full MoE block for n_tokens tokens held by this rank (host buffers):

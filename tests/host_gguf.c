@@ -3,8 +3,10 @@
  * gguf_load_manifest / gguf_find / gguf_tensor_pread, gguf.h:168-192), reads
  * one MoE layer's tensors under the names infer.m uses (infer.m:297-305:
  * blk.L.ffn_{gate,up,down}_exps.weight, blk.L.ffn_gate_inp.weight,
- * blk.L.exp_probs_b.bias, blk.L.ffn_{gate,up,down}_shexp.weight), hands them
- * to moe_load_layer and runs moe_forward on the tokens of a raw fp32 file.
+ * blk.L.exp_probs_b.bias, blk.L.ffn_{gate,up,down}_shexp.weight) -- of the
+ * stacked expert tensors only the rank's slice (moe_shard_range) -- hands
+ * them to moe_load_layer_shard and runs moe_forward on the tokens of a raw
+ * fp32 file.
  *
  *   host_gguf <file.gguf> <layer> <hidden> <intermediate> <n_experts> <n_group>
  *             <topk_group> <top_k> <tokens.f32> <n_tokens> <out prefix>
@@ -30,6 +32,30 @@ static void *read_tensor(const gguf_manifest *m, const char *fmt, int L, const g
     void *buf = malloc(t->nbytes);
     if (!buf || gguf_tensor_pread(t, buf, t->nbytes, 0) != (int64_t)t->nbytes) {
         fprintf(stderr, "[host] ERROR: cannot read %s\n", name);
+        free(buf);
+        return NULL;
+    }
+    if (out) *out = t;
+    return buf;
+}
+
+/* The rank's slice of a stacked expert tensor (ne2 = n_experts experts):
+ * moe_shard_range gives its byte range, gguf_tensor_pread reads just that
+ * (gguf.h:192, `rel` = the offset inside the tensor). */
+static void *read_expert_slice(const gguf_manifest *m, const char *fmt, int L, const moe_ctx *moe, int n_experts,
+                               const gguf_tensor **out) {
+    char name[256];
+    snprintf(name, sizeof(name), fmt, L);
+    const gguf_tensor *t = gguf_find(m, name);
+    if (!t || t->nbytes % (uint64_t)n_experts) {
+        fprintf(stderr, "[host] ERROR: tensor %s missing or not %d experts\n", name, n_experts);
+        return NULL;
+    }
+    size_t off = 0, bytes = 0;
+    if (moe_shard_range(moe, (size_t)(t->nbytes / (uint64_t)n_experts), &off, &bytes) != 0) return NULL;
+    void *buf = malloc(bytes);
+    if (!buf || gguf_tensor_pread(t, buf, bytes, off) != (int64_t)bytes) {
+        fprintf(stderr, "[host] ERROR: cannot read the expert slice of %s\n", name);
         free(buf);
         return NULL;
     }
@@ -79,28 +105,29 @@ int main(int argc, char **argv) {
     }
     const gguf_tensor *tg = NULL, *tu = NULL, *td = NULL, *tr = NULL, *tb = NULL, *tsg = NULL, *tsu = NULL,
                       *tsd = NULL;
-    void *g = read_tensor(&m, "blk.%d.ffn_gate_exps.weight", L, &tg);
-    void *u = read_tensor(&m, "blk.%d.ffn_up_exps.weight", L, &tu);
-    void *d = read_tensor(&m, "blk.%d.ffn_down_exps.weight", L, &td);
+    int rc = 1;
+    float *h = NULL, *out = NULL, *w = NULL;
+    int *idx = NULL;
+    void *g = NULL, *u = NULL, *d = NULL;
+    /* a rank's context first: it says which experts (bytes) this rank reads */
+    moe_ctx *moe = moe_create(&cfg, 0, 0, 1, NULL);
     void *router = read_tensor(&m, "blk.%d.ffn_gate_inp.weight", L, &tr);
     void *bias = read_tensor(&m, "blk.%d.exp_probs_b.bias", L, &tb);
     void *sg = read_tensor(&m, "blk.%d.ffn_gate_shexp.weight", L, &tsg);
     void *su = read_tensor(&m, "blk.%d.ffn_up_shexp.weight", L, &tsu);
     void *sd = read_tensor(&m, "blk.%d.ffn_down_shexp.weight", L, &tsd);
-    int rc = 1;
-    moe_ctx *moe = NULL;
-    float *h = NULL, *out = NULL, *w = NULL;
-    int *idx = NULL;
+    if (!moe) goto done;
+    g = read_expert_slice(&m, "blk.%d.ffn_gate_exps.weight", L, moe, cfg.n_experts, &tg);
+    u = read_expert_slice(&m, "blk.%d.ffn_up_exps.weight", L, moe, cfg.n_experts, &tu);
+    d = read_expert_slice(&m, "blk.%d.ffn_down_exps.weight", L, moe, cfg.n_experts, &td);
     if (!g || !u || !d || !router || !bias || !sg || !su || !sd) goto done;
     if (tr->type != 0 || tb->type != 0) {  /* GGML_TYPE_F32 */
         fprintf(stderr, "[host] ERROR: router and bias must be F32\n");
         goto done;
     }
-    moe = moe_create(&cfg, 0, 0, 1, NULL);
-    if (!moe) goto done;
     /* the layer goes into slot 0 of this one-layer context */
-    if (moe_load_layer(moe, 0, g, u, d, (int)td->type, (const float *)router, (const float *)bias, sg, su, sd,
-                       (int)tsd->type) != 0) {
+    if (moe_load_layer_shard(moe, 0, g, u, d, (int)td->type, (const float *)router, (const float *)bias, sg, su,
+                             sd, (int)tsd->type) != 0) {
         fprintf(stderr, "[host] ERROR: %s\n", moe_last_error(moe));
         goto done;
     }

@@ -410,3 +410,41 @@ def test_stack_deepseek_shape_alternating_down(cuda_lib, oracle):
     err = rel_err(got, hid)
     assert err < TOL and err < GUARD, err
     m.close()
+
+
+@pytest.mark.gpu
+def test_packed_layer_file_round_trip(cuda_lib, oracle, tmp_path):
+    """moe_write_layer_packed writes the reference's packed layer file
+    (repack_experts.c:157-238: expert e's GGUF bytes [gate][up][down] at
+    e * expert_size, no header); moe_load_layer_packed reads it back into a
+    context that computes bit-identical outputs.  Also moe_load_layer_shard
+    on one GPU (the slice is every expert)."""
+    cfg = small_cfg()
+    H, I, E = cfg.hidden, cfg.intermediate, cfg.n_experts
+    a = cuda_lib.MoE(cfg)
+    a.init_layer_synthetic(0, seed=9, down_type=14)
+    path = str(tmp_path / "layer_00.bin")
+    a.write_layer_packed(0, path)
+    es = a.expert_bytes(0)
+    blob = np.fromfile(path, np.uint8)
+    assert blob.size == E * es
+    for e in range(E):
+        assert np.array_equal(blob[e * es:(e + 1) * es], oracle.gen_expert(9, 0, e, H, I, 14)), e
+    sh = a.read_expert(0, E)
+    gb = oracle.row_bytes(12, H) * I
+    router, bias = router_of(oracle, 9, 0, cfg)
+    b = cuda_lib.MoE(cfg)
+    b.load_layer_packed(0, blob, es, router, bias, sh[:gb], sh[gb:2 * gb], sh[2 * gb:], 14)
+    c = cuda_lib.MoE(cfg)
+    assert c.shard_range(gb) == (0, E * gb)
+    c.load_layer_shard(0, np.concatenate([blob[e * es:e * es + gb] for e in range(E)]),
+                       np.concatenate([blob[e * es + gb:e * es + 2 * gb] for e in range(E)]),
+                       np.concatenate([blob[e * es + 2 * gb:(e + 1) * es] for e in range(E)]), 14, router, bias,
+                       sh[:gb], sh[gb:2 * gb], sh[2 * gb:], 14)
+    h = oracle.normal(10, oracle.stream(0, 0, oracle.KIND_ACT), 5 * H, 1.0).reshape(5, H)
+    oa, ia, _ = a.forward(0, h)
+    for m in (b, c):
+        o, i, _ = m.forward(0, h)
+        assert np.array_equal(i, ia) and np.array_equal(o.view(np.uint32), oa.view(np.uint32))
+    for m in (a, b, c):
+        m.close()
