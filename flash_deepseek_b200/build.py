@@ -19,6 +19,8 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
          "-diag-suppress", "177,550", f"-I{os.path.join(ROOT, 'include')}"]
+# extra nvcc flags (e.g. -D overrides of tuning constants for a side-by-side build)
+FLAGS += os.environ.get("MOE_NVCC_EXTRA", "").split()
 
 
 def _stale() -> bool:

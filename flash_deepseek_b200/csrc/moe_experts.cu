@@ -47,16 +47,22 @@
 #define GU_ROWS 64
 #define GU_WBOX (GU_ROWS * MOE_Q4K_BYTES)
 #define GU_STAGE (2 * GU_WBOX + EX_OPND)
+#ifndef GU_NS
 #define GU_NS 3
+#endif
 // down: item = 128 rows of H, K = I
 #define DN_ROWS 128
 #define DN4_WBOX (DN_ROWS * MOE_Q4K_BYTES)
 #define DN4_STAGE (DN4_WBOX + EX_OPND)
+#ifndef DN4_NS
 #define DN4_NS 3
+#endif
 #define DN6_QBOX (DN_ROWS * 192)
 #define DN6_SBOX (DN_ROWS * 16)
 #define DN6_STAGE (DN6_QBOX + DN6_SBOX + EX_OPND)
+#ifndef DN6_NS
 #define DN6_NS 2
+#endif
 
 #define LAUNCH_COUNT(p) \
     do {                \
@@ -713,10 +719,11 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
                 default: ok = gu_item_w<4>(d, act, it, NB, sm, full, empty, seq, warp, lane); break;
             }
         } else {
-            switch ((it.ntok + 1) >> 1) {
+            switch ((it.ntok + 1) >> 1) {  // int8-path chunks have at most MOE_TC tokens
                 case 1: ok = gu_item<1>(d, plan, act, it, NB, sm, full, empty, seq, warp, lane); break;
                 case 2: ok = gu_item<2>(d, plan, act, it, NB, sm, full, empty, seq, warp, lane); break;
-                default: ok = gu_item<3>(d, plan, act, it, NB, sm, full, empty, seq, warp, lane); break;
+                case 3: ok = gu_item<3>(d, plan, act, it, NB, sm, full, empty, seq, warp, lane); break;
+                default: ok = gu_item<4>(d, plan, act, it, NB, sm, full, empty, seq, warp, lane); break;
             }
         }
         if (!ok) {

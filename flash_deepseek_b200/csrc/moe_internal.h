@@ -104,7 +104,11 @@ inline void moe_smem_limit(F *kernel, size_t bytes, size_t (&done)[MOE_MAX_DEVIC
 // chunks in the order chunk_order (most tokens first).
 #define MOE_TC 8           // tokens of an int8-path chunk (four 8-column tiles of 2 tokens x 3 planes)
 #define MOE_WIDE_TC 16     // tokens of an fp16-path chunk (four 8-column tiles of 4 tokens x 2 planes)
+#ifndef MOE_GU_WIDE_MIN
 #define MOE_GU_WIDE_MIN 7
+#endif
+static_assert(MOE_GU_WIDE_MIN >= 2 && MOE_GU_WIDE_MIN <= MOE_TC + 1,
+              "chunks below MOE_GU_WIDE_MIN tokens run on the int8 path, which takes at most MOE_TC tokens");
 __host__ __device__ __forceinline__ bool moe_gu_wide(int ntok) { return ntok >= MOE_GU_WIDE_MIN; }
 __host__ __device__ __forceinline__ bool moe_dn_wide(int ntok) { return ntok > MOE_TC; }
 __host__ __device__ __forceinline__ int moe_n_chunks(int n) {
