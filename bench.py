@@ -10,7 +10,10 @@ one batch of synthetic tokens.  Workloads (the reference's headline configs):
   decode_b1        config 2: one token on one GPU
 Weights are random-init N(0, 0.02) quantized to Q4_K gate/up and Q6_K down on
 the device; inputs N(0, 1) from a fixed seed.  Between timed steps a 256 MiB
-buffer is written to flush the 126 MB L2.
+buffer is written to flush the 126 MB L2.  On one GPU the default run then
+measures the other configs too (one expert per call, one token, the 4096-token
+prefill, the 58-layer stack at batch 1) and reports them under "configs";
+--no-extra skips them.
 
 --impl reference times the reference's own CPU path (quant.c dequant + fp32
 dots + route(), built in place under oracle/_ref) on this host's cores, on a
@@ -210,7 +213,9 @@ def run_ours(args):
         import torch.distributed as dist
         dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=120))
         pg = dist
-    W = WORKLOADS[args.workload]
+    W = dict(WORKLOADS[args.workload])
+    if args.batch:
+        W["B"] = args.batch
     B = W["B"]
     # tokens of this rank: an even share, or (batch < GPUs) one token on the
     # first B ranks and none elsewhere
@@ -422,11 +427,11 @@ def run_ours(args):
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
         }
-        print(json.dumps(line), flush=True)
     moe.close()
     if pg:
         pg.barrier()
         pg.destroy_process_group()
+    return line if rank == 0 else None
 
 
 def run_extra(args):
@@ -608,7 +613,7 @@ def run_extra(args):
         if rank != 0:
             clk.__exit__(None, None, None)
             moe.close()
-            return
+            return None
     else:  # prefill4096: one moe_prefill_device call (tcgen05 GEMMs) per step and rank
         from flash_deepseek_b200 import ep
         world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -677,7 +682,7 @@ def run_extra(args):
         if rank != 0:
             clk.__exit__(None, None, None)
             moe.close()
-            return
+            return None
     clk.__exit__(None, None, None)
     line = {"metric": METRIC, "value": round(value, 2), "unit": unit,
             "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps,
@@ -691,8 +696,8 @@ def run_extra(args):
             "config": dict({"workload": W["name"], "global_batch": W["B"], "hidden": H, "intermediate": I,
                             "experts": E, "parallelism": "ep1"}, **extra),
             "roofline": roof, "e2e": e2e, "gpu_launches": int(launches), "clocks": clk.summary()}
-    print(json.dumps(line), flush=True)
     moe.close()
+    return line
 
 
 def run_reference(args):
@@ -727,20 +732,49 @@ def main():
     ap.add_argument("--workload", default="decode_b64_zipf", choices=sorted(WORKLOADS) + sorted(EXTRA))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="default workload only: skip the other configurations measured after it")
     ap.add_argument("--experts", type=int, default=E,
                     help="routed experts (default 256); smaller values only to keep ncu captures small")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="tokens per step of decode_b64_zipf / decode_b1 (default: the workload's); other "
+                         "values only to size ncu captures (with --experts, the same pairs per expert)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
-    if args.workload in EXTRA:
-        if args.impl == "reference":
+    if args.impl == "reference":
+        if args.workload in EXTRA:
             print(json.dumps({"impl": "reference", "unavailable": "the reference arm times configs 2 and 3"}))
             return
-        run_extra(args)
-    elif args.impl == "reference":
         run_reference(args)
-    else:
-        run_ours(args)
+        return
+    line = run_extra(args) if args.workload in EXTRA else run_ours(args)
+    if line is None:
+        return
+    if (args.workload == "decode_b64_zipf" and int(os.environ.get("WORLD_SIZE", "1")) == 1 and not args.no_extra
+            and args.experts == E and not args.batch):
+        line["configs"] = other_configs(args)
+    print(json.dumps(line), flush=True)
+
+
+def other_configs(args):
+    """The other headline configurations, measured in the same run on the same
+    GPU after the default one (each in its own context, with its own warm-up,
+    timed loop, L2 handling and clock sampling, as its --workload line would
+    be): config 2 (one token), config 1 (one expert per call), config 5 (4096-
+    token prefill) and config 4 (the 58-layer stack at batch 1)."""
+    keep = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "dtype", "roofline", "roofline_down",
+            "phase_ms", "e2e", "gpu_launches", "clocks", "config")
+    out = {}
+    for wl, steps in (("decode_b1", 100), ("expert1", 256), ("prefill4096", 3), ("stack_b1", 3)):
+        a = argparse.Namespace(**vars(args))
+        a.workload, a.steps, a.warmup, a.no_cpu = wl, steps, 3, True
+        try:
+            ln = run_extra(a) if wl in EXTRA else run_ours(a)
+            out[wl] = {k: ln[k] for k in keep if k in ln}
+        except Exception as e:  # reported in the line; the default measurement stands
+            out[wl] = {"error": repr(e)[:300]}
+    return out
 
 
 if __name__ == "__main__":
