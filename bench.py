@@ -361,6 +361,7 @@ def run_ours(args):
     ach_dn = float(np.mean(dn_bytes)) / (dn_ms / 1e3) / 1e9
     step_bytes = float(np.mean([a * EXPERT_BYTES for a in active])) + NE * H * 4 + NE * 4
     traffic = traffic_from_profiles("k_gateup", args.workload, float(np.mean(gu_bytes)))
+    traffic_dn = traffic_from_profiles("k_down", args.workload, float(np.mean(dn_bytes)))
 
     # ---- end-to-end leg through the C ABI with host buffers
     h_pin = [p[t0_loc:t0_loc + max(1, b_loc)].contiguous().pin_memory() for p in pool_h]
@@ -414,7 +415,9 @@ def run_ours(args):
                          "algorithmic_bytes_per_launch": round(float(np.mean(gu_bytes))),
                          "launch_ms": round(gu_ms, 5)},
             "roofline_down": {"kernel": "k_down (grouped Q6_K down GEMV)", "achieved": round(ach_dn, 1),
-                              "frac": round(ach_dn / peak, 4), "launch_ms": round(dn_ms, 5)},
+                              "frac": round(ach_dn / peak, 4), "traffic": traffic_dn,
+                              "algorithmic_bytes_per_launch": round(float(np.mean(dn_bytes))),
+                              "launch_ms": round(dn_ms, 5)},
             "step_hbm": {"weight_bytes_per_step": round(step_bytes),
                          "achieved_gbs": round(step_bytes / (total_ms / args.steps / 1e3) / 1e9, 1),
                          "active_experts_per_step": round(float(np.mean(active)), 2)},
