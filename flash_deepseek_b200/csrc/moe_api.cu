@@ -83,6 +83,8 @@ struct moe_ctx {
     int *counter = nullptr;
     float *act = nullptr, *eo = nullptr;
     uint8_t *dop = nullptr;   // down operand, opw_bytes(I) per pair (int8 or fp16 planes by chunk)
+    uint8_t *xtc = nullptr;   // gate/up fp16 operand rows of the tcgen05 chunks' pairs, opw_bytes(H) per pair
+    CUtensorMap tm_xtc, tm_dop;  // TMA maps of the tcgen05 kernels over xtc and dop
     int *h_counts = nullptr;  // pinned [4]
     // expert-parallel buffers
     float *send_x = nullptr, *recv_x = nullptr, *send_y = nullptr, *recv_y = nullptr;
@@ -233,6 +235,12 @@ static int ctx_alloc(moe_ctx *c) {
     CK(dmalloc(&c->act, (size_t)P * I));
     CK(dmalloc(&c->dop, (size_t)P * opw_bytes(I)));
     CK(cudaMemset(c->dop, 0, (size_t)P * opw_bytes(I)));
+    if (c->d.tc) {
+        CK(dmalloc(&c->xtc, (size_t)P * opw_bytes(H)));
+        CK(cudaMemset(c->xtc, 0, (size_t)P * opw_bytes(H)));
+        if (moe_make_map_opw(&c->tm_xtc, c->xtc, H, (uint64_t)P) || moe_make_map_opw(&c->tm_dop, c->dop, I, (uint64_t)P))
+            return fail(c, MOE_ERR_CUDA, "tensor maps of the tcgen05 operand rows");
+    }
     CK(dmalloc(&c->eo, (size_t)P * H));
     CK(cudaMallocHost((void **)&c->h_counts, 4 * sizeof(int)));
     if (c->world > 1) {
@@ -332,7 +340,12 @@ moe_ctx *moe_create(const moe_config *cfg, int device, int rank, int world_size,
     c->cfg = *cfg;
     c->use_graphs = getenv("MOE_NO_GRAPHS") == nullptr;
     c->d = MoeDims{cfg->hidden, cfg->intermediate, cfg->n_experts, cfg->n_group, cfg->topk_group, cfg->top_k,
-                   cfg->routed_scale};
+                   cfg->routed_scale, 1};
+    {
+        // MOE_TC=0 keeps busy experts on the GEMVs' fp16 path (16-token chunks)
+        const char *e = getenv("MOE_TC");
+        if (e && e[0] == '0') c->d.tc = 0;
+    }
     c->device = device;
     c->rank = rank;
     c->world = world_size;
@@ -421,7 +434,7 @@ void moe_destroy(moe_ctx *c) {
     void *bufs[] = {c->part, c->logits, c->rl_counters, c->d_in, c->d_out, c->h_post, c->idx, c->wts, c->idx_given, c->w_given, c->bias_tmp, c->xop, c->plan.counts,
                     c->plan.pair_expert, c->plan.pair_token, c->plan.pair_w, c->plan.chunk_expert,
                     c->plan.chunk_pair0, c->plan.chunk_ntok, c->plan.chunk_order, c->plan.slot_pair, c->plan.error, c->counter, c->act,
-                    c->dop, c->eo, c->send_x, c->recv_x, c->send_y, c->recv_y, c->send_meta,
+                    c->dop, c->xtc, c->eo, c->send_x, c->recv_x, c->send_y, c->recv_y, c->send_meta,
                     c->recv_meta, c->rows_partial, c->tok_slot};
     for (void *b : bufs) cudaFree(b);
     if (c->h_counts) cudaFreeHost(c->h_counts);
@@ -770,12 +783,21 @@ static int run_local(moe_ctx *c, int layer, const float *x, int T, const int *id
     moe_launch_route_and_plan(d, nullptr, 0, c->logits, L.bias, L.logit_bias, mode, idx_in, w_in, T, c->idx, c->wts,
                               x, c->xop, with_shared, 1, c->plan, c->counter, s, &c->launches);
     const int max_chunks = (T * d.K + T + MOE_TC - 1) / MOE_TC + d.E + 1;
+    // an expert gets at most T tokens: with more than MOE_TC there can be
+    // tcgen05 chunks
+    const bool tc = d.tc && T > MOE_TC;
+    const int P = T * d.K + T;
     mark(c, MOE_PHASE_GATEUP, s);
+    if (tc) {
+        moe_launch_tc_gather(d, c->plan, c->xop, c->xtc, P, s, &c->launches);
+        moe_launch_gateup_tc(d, L, c->plan, c->tm_xtc, c->act, P, s, &c->launches);
+    }
     moe_launch_gateup(d, L, c->plan, c->xop, c->act,
                       max_chunks, s, &c->launches);
     mark(c, MOE_PHASE_PREP, s);
-    moe_launch_prep_down(d, L, c->plan, c->act, c->dop, T * d.K + T, s, &c->launches);
+    moe_launch_prep_down(d, L, c->plan, c->act, c->dop, P, s, &c->launches);
     mark(c, MOE_PHASE_DOWN, s);
+    if (tc) moe_launch_down_tc(d, L, c->plan, c->tm_dop, c->eo, P, s, &c->launches);
     moe_launch_down(d, L, c->plan, c->dop, c->eo, max_chunks, s, &c->launches);
     mark(c, MOE_PHASE_OUTPUT, s);
     moe_launch_combine(d, c->plan, c->eo, T, routed, with_shared, residual, out, s, &c->launches);
@@ -811,6 +833,8 @@ static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_i
     mark(c, MOE_PHASE_DISPATCH, s);
     const int P = R * d.K + T;
     const int max_chunks = (P + MOE_TC - 1) / MOE_TC + d.E + 1;
+    // a routed expert gets at most R received rows, the shared one T local rows
+    const bool tc = d.tc && (R > MOE_TC || T > MOE_TC);
     if (c->p2p) {
         // peer-memory exchange: no host step in between, the step number
         // lives on the device (the launches replay as a graph)
@@ -818,10 +842,15 @@ static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_i
         moe_launch_ep_pack_p2p(x, c->idx, c->wts, T, d.K, d.H, c->n_local, cap, q, c->tok_slot, s, &c->launches);
         moe_launch_ep_plan_rows_p2p(d, q, cap, T, c->e0, c->n_local, c->plan, x, c->xop, s, &c->launches);
         mark(c, MOE_PHASE_GATEUP, s);
+        if (tc) {
+            moe_launch_tc_gather(d, c->plan, c->xop, c->xtc, P, s, &c->launches);
+            moe_launch_gateup_tc(d, L, c->plan, c->tm_xtc, c->act, P, s, &c->launches);
+        }
         moe_launch_gateup(d, L, c->plan, c->xop, c->act, max_chunks, s, &c->launches);
         mark(c, MOE_PHASE_PREP, s);
         moe_launch_prep_down(d, L, c->plan, c->act, c->dop, P, s, &c->launches);
         mark(c, MOE_PHASE_DOWN, s);
+        if (tc) moe_launch_down_tc(d, L, c->plan, c->tm_dop, c->eo, P, s, &c->launches);
         moe_launch_down(d, L, c->plan, c->dop, c->eo, max_chunks, s, &c->launches);
         mark(c, MOE_PHASE_COMBINE, s);
         moe_launch_ep_partial_p2p(d, c->plan, c->eo, cap, q, s, &c->launches);
@@ -848,11 +877,16 @@ static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_i
     moe_launch_ep_plan(d, c->recv_meta, N, cap, T, c->e0, c->n_local, c->plan, s, &c->launches);
     moe_launch_prep_rows(c->recv_x, c->recv_meta, mw, R, x, T, d.H, c->xop, s, &c->launches);
     mark(c, MOE_PHASE_GATEUP, s);
+    if (tc) {
+        moe_launch_tc_gather(d, c->plan, c->xop, c->xtc, P, s, &c->launches);
+        moe_launch_gateup_tc(d, L, c->plan, c->tm_xtc, c->act, P, s, &c->launches);
+    }
     moe_launch_gateup(d, L, c->plan, c->xop, c->act,
                       max_chunks, s, &c->launches);
     mark(c, MOE_PHASE_PREP, s);
     moe_launch_prep_down(d, L, c->plan, c->act, c->dop, P, s, &c->launches);
     mark(c, MOE_PHASE_DOWN, s);
+    if (tc) moe_launch_down_tc(d, L, c->plan, c->tm_dop, c->eo, P, s, &c->launches);
     moe_launch_down(d, L, c->plan, c->dop, c->eo, max_chunks, s, &c->launches);
     mark(c, MOE_PHASE_COMBINE, s);
     {

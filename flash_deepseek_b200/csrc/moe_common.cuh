@@ -188,6 +188,37 @@ __device__ __forceinline__ int sext_byte(uint32_t w) {
 __device__ __forceinline__ uint32_t h2_as_u32(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 __device__ __forceinline__ __half2 u32_as_h2(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
 
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;\n" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+// fp16 pair arithmetic on raw 32-bit words (sm_53 and later; the layout
+// tools that include this header on the host compile without them)
+#if !defined(__CUDA_ARCH__) || __CUDA_ARCH__ >= 530
+__device__ __forceinline__ uint32_t hfma2u(uint32_t a, uint32_t b, uint32_t c) {
+    return h2_as_u32(__hfma2(u32_as_h2(a), u32_as_h2(b), u32_as_h2(c)));
+}
+__device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
+    return h2_as_u32(__hmul2(u32_as_h2(a), u32_as_h2(b)));
+}
+__device__ __forceinline__ uint32_t hsub2u(uint32_t a, uint32_t b) {
+    return h2_as_u32(__hsub2(u32_as_h2(a), u32_as_h2(b)));
+}
+// fp16 pair constants
+#define H2_1024 0x64006400u
+#define H2_M1024 0xE400E400u
+#define H2_1056 0x64206420u
+#define H2_1152 0x64806480u
+#define H2_16TH 0x2C002C00u
+#define H2_M64 0xD400D400u
+// (v, v) for byte B of w (an integer v < 1024): bytes (v, 0x64) are 1024 + v
+template <int B>
+__device__ __forceinline__ uint32_t byte_h2(uint32_t w, uint32_t minus) {
+    return hsub2u(prmt(w, 0x64u, (uint32_t)(B | (4 << 4) | (B << 8) | (4 << 12))), minus);
+}
+#endif
+
 // ---------------------------------------------------------------------------
 // Counter-based N(0, sigma) generator, bit-identical to the test oracle:
 // splitmix64 keyed by (seed, stream, element) -> Marsaglia polar method with
@@ -376,3 +407,18 @@ __device__ __forceinline__ void build_op_rows(const float *__restrict__ x, int K
     }
 }
 
+// scale and min of sub-block J of a Q4_K block (get_scale_min_k4,
+// quant.c:26-34); h.y, h.z, h.w = the 12 scale bytes
+template <int J>
+__device__ __forceinline__ void q4_scale_min(uint4 h, int &sc, int &m) {
+    const uint32_t s[3] = {h.y, h.z, h.w};
+#define PF_B(k) ((int)((s[(k) >> 2] >> (8 * ((k) & 3))) & 0xFFu))
+    if (J < 4) {
+        sc = PF_B(J) & 63;
+        m = PF_B(J + 4) & 63;
+    } else {
+        sc = (PF_B(J + 4) & 0xF) | ((PF_B(J - 4) >> 6) << 4);
+        m = (PF_B(J + 4) >> 4) | ((PF_B(J) >> 6) << 4);
+    }
+#undef PF_B
+}

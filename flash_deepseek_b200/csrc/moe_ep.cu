@@ -104,7 +104,7 @@ __device__ void ep_plan_block(const MoeDims &d, const int *__restrict__ recv_met
         int v[3] = {0, 0, 0};
         if (e < NE) {
             v[0] = cnt[e];
-            v[1] = moe_n_chunks(cnt[e]);
+            v[1] = moe_n_chunks(cnt[e], d.tc);
             v[2] = (e < E && cnt[e] > 0) ? 1 : 0;
         }
         int inc[3];
@@ -175,10 +175,10 @@ __device__ void ep_plan_block(const MoeDims &d, const int *__restrict__ recv_met
     }
     for (int e = threadIdx.x; e < NE; e += blockDim.x) {
         const int n = cnt[e];
-        const int nc = moe_n_chunks(n);
+        const int nc = moe_n_chunks(n, d.tc);
         for (int c = 0; c < nc; c++) {
             int start, nt;
-            moe_chunk(n, c, start, nt);
+            moe_chunk(n, c, d.tc, start, nt);
             const int ci = coff[e] + c;
             plan.chunk_expert[ci] = e;
             plan.chunk_pair0[ci] = off[e] + start;
@@ -186,7 +186,7 @@ __device__ void ep_plan_block(const MoeDims &d, const int *__restrict__ recv_met
         }
     }
     __syncthreads();
-    moe_plan_order_chunks(plan, carry[1]);
+    moe_plan_order_chunks(plan, carry[1], d.tc);
 }
 
 __global__ void __launch_bounds__(512) k_ep_plan(MoeDims d, const int *__restrict__ recv_meta, int world, int cap,

@@ -145,11 +145,6 @@ __device__ __forceinline__ void mma_s8s8_16816z(int (&d)[4], uint32_t a0, uint32
         : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
         : "r"(a0), "r"(a1), "r"(b0), "r"(0));
 }
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-    uint32_t r;
-    asm("prmt.b32 %0, %1, %2, %3;\n" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
-    return r;
-}
 
 // D += A(16x16 fp16, row) x B(16x8 fp16, col), fp32 accumulators
 __device__ __forceinline__ void mma_f16_acc(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
@@ -165,37 +160,16 @@ __device__ __forceinline__ void mma_f16_1688(float (&d)[4], uint32_t a0, uint32_
         : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
         : "r"(a0), "r"(a1), "r"(b0), "f"(0.0f));
 }
-__device__ __forceinline__ uint32_t hfma2u(uint32_t a, uint32_t b, uint32_t c) {
-    return h2_as_u32(__hfma2(u32_as_h2(a), u32_as_h2(b), u32_as_h2(c)));
-}
-__device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
-    return h2_as_u32(__hmul2(u32_as_h2(a), u32_as_h2(b)));
-}
-__device__ __forceinline__ uint32_t hsub2u(uint32_t a, uint32_t b) {
-    return h2_as_u32(__hsub2(u32_as_h2(a), u32_as_h2(b)));
-}
-// fp16 pair constants
-#define H2_1024 0x64006400u
-#define H2_M1024 0xE400E400u
-#define H2_1056 0x64206420u
-#define H2_1152 0x64806480u
-#define H2_16TH 0x2C002C00u
-#define H2_M64 0xD400D400u
-// (v, v) for byte B of w (an integer v < 1024): bytes (v, 0x64) are 1024 + v
-template <int B>
-__device__ __forceinline__ uint32_t byte_h2(uint32_t w, uint32_t minus) {
-    return hsub2u(prmt(w, 0x64u, (uint32_t)(B | (4 << 4) | (B << 8) | (4 << 12))), minus);
-}
-
 struct ExItem {
     int rg, e, slot, p0, ntok;
 };
-// Work item `item` = (chunk chunk_order[item / n_rg], row group item % n_rg):
-// the row groups of one chunk are consecutive items, and the chunks with
-// the most tokens come first.
+// Work item `item` = (chunk chunk_order[counts[3] + item / n_rg], row group
+// item % n_rg): the row groups of one chunk are consecutive items, and the
+// chunks with the most tokens come first.  The first plan.counts[3] chunks
+// of the order run on the tcgen05 kernels instead.
 __device__ __forceinline__ void ex_item(const MoePlan &plan, const MoeLayerDev &L, int E, int n_rg, int item,
                                         ExItem &it) {
-    const int c = plan.chunk_order[item / n_rg];
+    const int c = plan.chunk_order[plan.counts[3] + item / n_rg];
     it.rg = item % n_rg;
     it.e = plan.chunk_expert[c];
     it.p0 = plan.chunk_pair0[c];
@@ -652,7 +626,7 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
     moe_pdl_wait();  // the plan and the operand come from the previous kernels
     moe_pdl_trigger();
     const int n_rg = d.I / GU_ROWS;
-    const int n_items = plan.counts[1] * n_rg;
+    const int n_items = (plan.counts[1] - plan.counts[3]) * n_rg;
     uint32_t seq = 0;
     if (warp == EX_CONSUMERS) {  // producer: takes items from the plan's counter
         const size_t rowst = opx_row(d.H), wide_off = op_bytes(d.H);
@@ -847,7 +821,7 @@ __global__ void __launch_bounds__(EX_THREADS, 2)
     // behind the full barriers.
     moe_pdl_trigger();
     const int n_rg = d.H / DN_ROWS;
-    const int n_items = plan.counts[1] * n_rg;
+    const int n_items = (plan.counts[1] - plan.counts[3]) * n_rg;
     int *counter = &plan.counts[TY == MOE_TYPE_Q6_K ? 5 : 6];
     uint32_t seq = 0, nitem = 0;
     if (warp == EX_CONSUMERS) {  // producer: takes items from the plan's counter

@@ -45,6 +45,7 @@ struct MoeLayerDev {
 struct MoeDims {
     int H, I, E, n_group, topk_group, K;
     float scale;
+    int tc;  // 1: experts with more than MOE_TC tokens run on the tcgen05 kernels (moe_experts_tc.cu)
 };
 
 // Programmatic dependent launch: a forward-path kernel may start while its
@@ -96,14 +97,18 @@ inline void moe_smem_limit(F *kernel, size_t bytes, size_t (&done)[MOE_MAX_DEVIC
 }
 
 // Chunks of an expert's tokens (the unit of work of the expert GEMVs).  An
-// expert with at most MOE_TC tokens is one chunk; a busier one is split into
-// chunks of MOE_WIDE_TC tokens and one chunk of the remainder.  The gate/up
-// GEMV runs a chunk on the fp16 path when it has at least MOE_GU_WIDE_MIN
-// tokens, the down GEMV when it has more than MOE_TC (the int8-plane path
-// otherwise).  The GEMVs take their work items from a counter in the plan,
-// chunks in the order chunk_order (most tokens first).
+// expert with at most MOE_TC tokens is one chunk.  A busier one is, with
+// MoeDims::tc set, split evenly into chunks of at most MOE_CHUNK_MAX tokens
+// that run on the tcgen05 kernels (moe_experts_tc.cu); without it, into
+// chunks of MOE_WIDE_TC tokens and one chunk of the remainder on the GEMVs.
+// The gate/up GEMV runs a chunk on the fp16 path when it has at least
+// MOE_GU_WIDE_MIN tokens, the down GEMV when it has more than MOE_TC (the
+// int8-plane path otherwise).  The GEMVs take their work items from a
+// counter in the plan, chunks in the order chunk_order (most tokens first;
+// the first plan.counts[3] chunks are the tcgen05 kernels').
 #define MOE_TC 8           // tokens of an int8-path chunk (four 8-column tiles of 2 tokens x 3 planes)
 #define MOE_WIDE_TC 16     // tokens of an fp16-path chunk (four 8-column tiles of 4 tokens x 2 planes)
+#define MOE_CHUNK_MAX 32   // tokens of a tcgen05 chunk
 #ifndef MOE_GU_WIDE_MIN
 #define MOE_GU_WIDE_MIN 7
 #endif
@@ -111,21 +116,30 @@ static_assert(MOE_GU_WIDE_MIN >= 2 && MOE_GU_WIDE_MIN <= MOE_TC + 1,
               "chunks below MOE_GU_WIDE_MIN tokens run on the int8 path, which takes at most MOE_TC tokens");
 __host__ __device__ __forceinline__ bool moe_gu_wide(int ntok) { return ntok >= MOE_GU_WIDE_MIN; }
 __host__ __device__ __forceinline__ bool moe_dn_wide(int ntok) { return ntok > MOE_TC; }
-__host__ __device__ __forceinline__ int moe_n_chunks(int n) {
-    return n <= 0 ? 0 : n <= MOE_TC ? 1 : (n + MOE_WIDE_TC - 1) / MOE_WIDE_TC;
+__host__ __device__ __forceinline__ int moe_n_chunks(int n, int tc) {
+    if (n <= 0) return 0;
+    if (n <= MOE_TC) return 1;
+    return tc ? (n + MOE_CHUNK_MAX - 1) / MOE_CHUNK_MAX : (n + MOE_WIDE_TC - 1) / MOE_WIDE_TC;
 }
 // chunk c of an expert with n tokens: first token (relative) and token count
-__host__ __device__ __forceinline__ void moe_chunk(int n, int c, int &start, int &ntok) {
+__host__ __device__ __forceinline__ void moe_chunk(int n, int c, int tc, int &start, int &ntok) {
     if (n <= MOE_TC) {
         start = 0;
         ntok = n;
         return;
     }
+    if (tc) {
+        const int nc = (n + MOE_CHUNK_MAX - 1) / MOE_CHUNK_MAX;
+        start = c * n / nc;
+        ntok = (c + 1) * n / nc - start;
+        return;
+    }
     start = c * MOE_WIDE_TC;
     ntok = n - start < MOE_WIDE_TC ? n - start : MOE_WIDE_TC;
 }
-// plan.counts: [0] pairs, [1] chunks, [2] routed experts hit, [4] gate/up,
-// [5] Q6_K down, [6] Q4_K down work counters (zeroed by the plan builder)
+// plan.counts: [0] pairs, [1] chunks, [2] routed experts hit, [3] tcgen05
+// chunks, [4] gate/up, [5] Q6_K down, [6] Q4_K down work counters (zeroed by
+// the plan builder)
 #define MOE_PLAN_COUNTS 8
 
 #ifdef __CUDACC__
@@ -133,28 +147,30 @@ __host__ __device__ __forceinline__ void moe_chunk(int n, int c, int &start, int
 // chunk_order = chunk ids grouped by token count, most tokens first (so the
 // GEMVs start the long items first and finish on short ones), and the work
 // counters zeroed.  Every thread of the block calls it.
-__device__ __forceinline__ void moe_plan_order_chunks(const MoePlan &plan, int n_chunks) {
-    __shared__ int bucket[MOE_WIDE_TC + 1];
-    for (int i = threadIdx.x; i <= MOE_WIDE_TC; i += blockDim.x) bucket[i] = 0;
+__device__ __forceinline__ void moe_plan_order_chunks(const MoePlan &plan, int n_chunks, int tc) {
+    __shared__ int bucket[MOE_CHUNK_MAX + 1];
+    for (int i = threadIdx.x; i <= MOE_CHUNK_MAX; i += blockDim.x) bucket[i] = 0;
     __syncthreads();
     for (int c = threadIdx.x; c < n_chunks; c += blockDim.x) {
         const int k = plan.chunk_ntok[c];
-        atomicAdd(&bucket[k < MOE_WIDE_TC ? k : MOE_WIDE_TC], 1);
+        atomicAdd(&bucket[k < MOE_CHUNK_MAX ? k : MOE_CHUNK_MAX], 1);
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-        int acc = 0;
-        for (int k = MOE_WIDE_TC; k >= 0; k--) {
+        int acc = 0, n_tc = 0;
+        for (int k = MOE_CHUNK_MAX; k >= 0; k--) {
             const int v = bucket[k];
             bucket[k] = acc;
             acc += v;
+            if (tc && k > MOE_TC) n_tc += v;
         }
+        plan.counts[3] = n_tc;
         for (int i = 4; i < MOE_PLAN_COUNTS; i++) plan.counts[i] = 0;
     }
     __syncthreads();
     for (int c = threadIdx.x; c < n_chunks; c += blockDim.x) {
         const int k = plan.chunk_ntok[c];
-        plan.chunk_order[atomicAdd(&bucket[k < MOE_WIDE_TC ? k : MOE_WIDE_TC], 1)] = c;
+        plan.chunk_order[atomicAdd(&bucket[k < MOE_CHUNK_MAX ? k : MOE_CHUNK_MAX], 1)] = c;
     }
 }
 #endif
@@ -180,6 +196,19 @@ void moe_launch_prep_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan 
                           uint8_t *dop, int max_pairs, cudaStream_t s, uint64_t *launches);
 void moe_launch_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const uint8_t *dop, float *eo,
                      int max_chunks, cudaStream_t s, uint64_t *launches);
+// busy experts on tcgen05 (moe_experts_tc.cu): the plan's first counts[3]
+// chunks (in chunk_order).  xtc: fp16 operand rows of their pairs (opw_bytes(H)
+// each, row = pair), gathered from the token rows of xop; tm_xtc / tm_dop:
+// 2-D maps over xtc / dop (moe_make_map_opw); max_pairs bounds the grid.
+void moe_launch_tc_gather(const MoeDims &d, const MoePlan &plan, const uint8_t *xop, uint8_t *xtc, int max_pairs,
+                          cudaStream_t s, uint64_t *launches);
+void moe_launch_gateup_tc(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const CUtensorMap &tm_xtc,
+                          float *act, int max_pairs, cudaStream_t s, uint64_t *launches);
+void moe_launch_down_tc(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, const CUtensorMap &tm_dop,
+                        float *eo, int max_pairs, cudaStream_t s, uint64_t *launches);
+// 2-D map over operand rows (opw_bytes(K) each, `rows` of them) for the
+// tcgen05 kernels (boxes of 64 fp16 x box_rows rows, 128-byte swizzle)
+int moe_make_map_opw(CUtensorMap *m, const void *base, int K, uint64_t rows);
 // TMA maps of a layer (after its weights are allocated); 0 = ok
 int moe_make_layer_maps(MoeLayerDev &L, const MoeDims &d);
 // 2-D map over a row-major fp16 matrix [rows][cols] with 128-byte swizzle

@@ -562,7 +562,7 @@ __device__ void build_plan_block(const RouteArgs &a) {
         int v[3] = {0, 0, 0};
         if (e < NE) {
             v[0] = cnt[e];
-            v[1] = moe_n_chunks(cnt[e]);
+            v[1] = moe_n_chunks(cnt[e], a.d.tc);
             v[2] = (e < E && cnt[e] > 0) ? 1 : 0;
         }
         int inc[3];
@@ -632,10 +632,10 @@ __device__ void build_plan_block(const RouteArgs &a) {
     }
     for (int e = threadIdx.x; e < NE; e += blockDim.x) {
         const int n = cnt[e];
-        const int nc = moe_n_chunks(n);
+        const int nc = moe_n_chunks(n, a.d.tc);
         for (int c = 0; c < nc; c++) {
             int start, nt;
-            moe_chunk(n, c, start, nt);
+            moe_chunk(n, c, a.d.tc, start, nt);
             const int ci = coff[e] + c;
             a.plan.chunk_expert[ci] = e;
             a.plan.chunk_pair0[ci] = off[e] + start;
@@ -643,7 +643,7 @@ __device__ void build_plan_block(const RouteArgs &a) {
         }
     }
     __syncthreads();
-    moe_plan_order_chunks(a.plan, coff[NE]);
+    moe_plan_order_chunks(a.plan, coff[NE], a.d.tc);
 }
 
 // Top groups by repeated argmax, the lowest index winning ties and only
@@ -854,7 +854,8 @@ void moe_launch_route_and_plan(const MoeDims &d, const float *part, int n_split,
 // down operand: per pair, scale + operand of the expert's down type
 // ===========================================================================
 // The down operand of every pair: the int8 planes, or the fp16 planes when
-// the pair's chunk runs on the down GEMV's fp16 path.  One super-block of
+// the pair's chunk runs on the down GEMV's fp16 path or on the tcgen05
+// kernel (chunks of more than MOE_TC tokens).  One super-block of
 // one pair per warp; tasks (chunk, pair slot, super-block) are spread over
 // the whole grid.  Pair rows are opw_bytes(I) apart (the larger form).
 __global__ void __launch_bounds__(256) k_prep_down(MoeDims d, MoeLayerDev L, MoePlan plan,
@@ -864,9 +865,9 @@ __global__ void __launch_bounds__(256) k_prep_down(MoeDims d, MoeLayerDev L, Moe
     const int n_chunks = plan.counts[1];
     const size_t opst = opw_bytes(d.I);
     const int nb = d.I / MOE_QK, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    const int per_chunk = MOE_WIDE_TC * nb, total = n_chunks * per_chunk;
+    const int per_chunk = MOE_CHUNK_MAX * nb, total = n_chunks * per_chunk;
     for (int task = blockIdx.x * nw + (threadIdx.x >> 5); task < total; task += gridDim.x * nw) {
-        const int c = task / per_chunk, j = (task / nb) % MOE_WIDE_TC, sb = task % nb;
+        const int c = task / per_chunk, j = (task / nb) % MOE_CHUNK_MAX, sb = task % nb;
         const int ntok = plan.chunk_ntok[c];
         if (j >= ntok) continue;
         const int e = plan.chunk_expert[c], p = plan.chunk_pair0[c] + j;
@@ -900,7 +901,7 @@ void moe_launch_prep_down(const MoeDims &d, const MoeLayerDev &L, const MoePlan 
                           uint8_t *dop, int max_pairs, cudaStream_t s, uint64_t *launches) {
     // one warp per (chunk, pair slot, super-block) task where the plan can
     // have that many, at most 2 blocks per SM
-    long tasks = (long)max_pairs * MOE_WIDE_TC * (d.I / MOE_QK);
+    long tasks = (long)max_pairs * MOE_CHUNK_MAX * (d.I / MOE_QK);
     int grid = (int)((tasks + 7) / 8);
     if (grid > num_sms() * 2) grid = num_sms() * 2;
     if (grid < 1) grid = 1;

@@ -53,61 +53,12 @@
 #define PF_DQ_WARPS 16                              // dequantize + epilogue (warps 3 ..)
 #define PF_DQ_WARP0 3                               // warps 0-2: weight TMA, MMA, activation TMA
 #define PF_THREADS (32 * (PF_DQ_WARP0 + PF_DQ_WARPS))
-#define PF_WAIT_CYCLES (1ll << 31)
-#define PF_SUSPEND_NS 1000000u    // a waiting thread sleeps up to 1 ms per try (woken when the phase completes)
 
 #define LAUNCH_COUNT(p) \
     do {                \
         if (p) (*(p))++; \
     } while (0)
 
-__device__ __forceinline__ void pf_mbar_init(uint64_t *b, int n) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(umma_smem_u32(b)), "r"(n) : "memory");
-}
-__device__ __forceinline__ void pf_expect(uint64_t *b, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(umma_smem_u32(b)), "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ void pf_arrive(uint64_t *b) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(umma_smem_u32(b)) : "memory");
-}
-__device__ __forceinline__ bool pf_wait(uint64_t *b, uint32_t parity) {
-    const long long t0 = clock64();
-    for (;;) {
-        uint32_t ok;
-        asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
-            " selp.u32 %0, 1, 0, p;\n}\n"
-            : "=r"(ok)
-            : "r"(umma_smem_u32(b)), "r"(parity), "r"(PF_SUSPEND_NS)
-            : "memory");
-        if (ok) return true;
-        if (clock64() - t0 > PF_WAIT_CYCLES) return false;
-    }
-}
-// after a producer gave up: wait (bounded) for the copies it issued into
-// the last `ns` stages of a ring, so that none lands after the CTA exits
-__device__ __forceinline__ void pf_drain(uint64_t *full, int issued, int ns) {
-    for (int k = issued > ns ? issued - ns : 0; k < issued; k++) pf_wait(&full[k % ns], (k / ns) & 1);
-}
-// the same, agreed by the whole warp (a lane that gave up fails them all)
-__device__ __forceinline__ bool pf_wait_warp(uint64_t *b, uint32_t parity) {
-    return __all_sync(0xffffffffu, pf_wait(b, parity));
-}
-__device__ __forceinline__ void pf_tma3(void *dst, const CUtensorMap *m, int x, int y, int z, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-        "[%5];\n" ::"r"(umma_smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(z), "r"(umma_smem_u32(bar))
-        : "memory");
-}
-__device__ __forceinline__ void pf_tma2(void *dst, const CUtensorMap *m, int x, int y, uint64_t *bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::
-            "r"(umma_smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(umma_smem_u32(bar))
-        : "memory");
-}
 // exact float of a small non-negative integer (< 2^23)
 __device__ __forceinline__ float pf_i2f(uint32_t q) { return __uint_as_float(0x4B000000u | q) - 8388608.0f; }
 __device__ __forceinline__ uint32_t pf_h2(float a, float b) {
@@ -281,22 +232,6 @@ __device__ __forceinline__ void pf_split(float x, uint32_t &hi, uint32_t &lo) {
     lo = pf_dup(x - h);
 }
 
-// scale and min of sub-block J of a Q4_K block (get_scale_min_k4,
-// quant.c:26-34); h.y, h.z, h.w = the 12 scale bytes
-template <int J>
-__device__ __forceinline__ void q4_scale_min(uint4 h, int &sc, int &m) {
-    const uint32_t s[3] = {h.y, h.z, h.w};
-#define PF_B(k) ((int)((s[(k) >> 2] >> (8 * ((k) & 3))) & 0xFFu))
-    if (J < 4) {
-        sc = PF_B(J) & 63;
-        m = PF_B(J + 4) & 63;
-    } else {
-        sc = (PF_B(J + 4) & 0xF) | ((PF_B(J - 4) >> 6) << 4);
-        m = (PF_B(J + 4) >> 4) | ((PF_B(J) >> 6) << 4);
-    }
-#undef PF_B
-}
-
 // the constants of Q4_K atom g (sub-blocks 2g, 2g + 1):
 // {sc0, -1024 sc0, -dm0_hi, -dm0_lo, sc1/16, -64 sc1, -dm1_hi, -dm1_lo}
 __device__ __forceinline__ void pf_q4_consts(uint4 h, int g, uint32_t (&c)[8]) {
@@ -412,10 +347,10 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     const int K = MODE == 0 ? d.H : d.I, NB = K / MOE_QK, n_atoms = 4 * NB;
     const int nbp = q6r_nb_pad(NB), nbox = (ntile + 31) / 32;
     if (tid == 0) {
-        for (int i = 0; i < RAW_NS; i++) { pf_mbar_init(&raw_full[i], 1); pf_mbar_init(&raw_empty[i], PF_DQ_WARPS); }
-        for (int i = 0; i < PF_NSA; i++) { pf_mbar_init(&a_full[i], 4); pf_mbar_init(&a_empty[i], 1); }
-        for (int i = 0; i < PF_NSB; i++) { pf_mbar_init(&b_full[i], 1); pf_mbar_init(&b_empty[i], 1); }
-        pf_mbar_init(&acc_full, 1);
+        for (int i = 0; i < RAW_NS; i++) { tc_mbar_init(&raw_full[i], 1); tc_mbar_init(&raw_empty[i], PF_DQ_WARPS); }
+        for (int i = 0; i < PF_NSA; i++) { tc_mbar_init(&a_full[i], 4); tc_mbar_init(&a_empty[i], 1); }
+        for (int i = 0; i < PF_NSB; i++) { tc_mbar_init(&b_full[i], 1); tc_mbar_init(&b_empty[i], 1); }
+        tc_mbar_init(&acc_full, 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
     }
@@ -435,23 +370,23 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         int issued = 0;
         for (int sbk = 0; sbk < NB && ok; sbk++) {
             const int rs = sbk % RAW_NS;
-            if (!pf_wait_warp(&raw_empty[rs], ((sbk / RAW_NS) & 1) ^ 1)) { ok = false; break; }
+            if (!tc_wait_warp(&raw_empty[rs], ((sbk / RAW_NS) & 1) ^ 1)) { ok = false; break; }
             uint8_t *r = sr + rs * RAW;
             if (leader) {
-                pf_expect(&raw_full[rs], RAW + (MODE == 2 && sbk == 0 ? PF_RB * 128 * 2 * nbp : 0));
+                tc_expect(&raw_full[rs], RAW + (MODE == 2 && sbk == 0 ? PF_RB * 128 * 2 * nbp : 0));
 #pragma unroll
                 for (int b = 0; b < PF_RB; b++) {
                     const int blk = PF_RB * rg + b;
                     if (MODE == 0) {
-                        pf_tma3(r + b * QB, &L.tm_gu, sbk * MOE_Q4K_BYTES, blk * 64, slot, &raw_full[rs]);
-                        pf_tma3(r + b * QB + 64 * MOE_Q4K_BYTES, &L.tm_gu, sbk * MOE_Q4K_BYTES, d.I + blk * 64, slot,
+                        tc_tma3(r + b * QB, &L.tm_gu, sbk * MOE_Q4K_BYTES, blk * 64, slot, &raw_full[rs]);
+                        tc_tma3(r + b * QB + 64 * MOE_Q4K_BYTES, &L.tm_gu, sbk * MOE_Q4K_BYTES, d.I + blk * 64, slot,
                                 &raw_full[rs]);
                     } else if (MODE == 1) {
-                        pf_tma3(r + b * QB, &L.tm_d4, sbk * MOE_Q4K_BYTES, blk * 128, slot, &raw_full[rs]);
+                        tc_tma3(r + b * QB, &L.tm_d4, sbk * MOE_Q4K_BYTES, blk * 128, slot, &raw_full[rs]);
                     } else {
-                        pf_tma3(r + b * QB, &L.tm_pf6q, sbk * 192, blk * 128, slot, &raw_full[rs]);
-                        pf_tma3(r + PF_RB * QB + b * 2048, &L.tm_d6s, sbk * 16, blk * 128, slot, &raw_full[rs]);
-                        if (sbk == 0) pf_tma3(sd + b * 256 * nbp, &L.tm_d6d, 0, blk * 128, slot, &raw_full[rs]);
+                        tc_tma3(r + b * QB, &L.tm_pf6q, sbk * 192, blk * 128, slot, &raw_full[rs]);
+                        tc_tma3(r + PF_RB * QB + b * 2048, &L.tm_d6s, sbk * 16, blk * 128, slot, &raw_full[rs]);
+                        if (sbk == 0) tc_tma3(sd + b * 256 * nbp, &L.tm_d6d, 0, blk * 128, slot, &raw_full[rs]);
                     }
                 }
             }
@@ -459,7 +394,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         }
         if (!ok && leader) {
             atomicExch(plan.error, PF_ERR_TIMEOUT);
-            pf_drain(raw_full, issued, RAW_NS);
+            tc_drain(raw_full, issued, RAW_NS);
         }
     } else if (warp == 2) {
         // activation producer: the pairs' 64-column slices, PF_NSB atoms ahead
@@ -467,18 +402,18 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         int issued = 0;
         for (int i = 0; i < n_atoms && ok; i++) {
             const int st = i % PF_NSB;
-            if (!pf_wait_warp(&b_empty[st], ((i / PF_NSB) & 1) ^ 1)) { ok = false; break; }
+            if (!tc_wait_warp(&b_empty[st], ((i / PF_NSB) & 1) ^ 1)) { ok = false; break; }
             if (leader) {
                 // only the 32-row boxes the tile's pairs reach (L2 traffic)
-                pf_expect(&b_full[st], nbox * PF_BOX32);
+                tc_expect(&b_full[st], nbox * PF_BOX32);
                 for (int bx = 0; bx < nbox; bx++)
-                    pf_tma2(sb + st * PF_ATOM + bx * PF_BOX32, &tmB, 64 * i, p0 + 32 * bx, &b_full[st]);
+                    tc_tma2(sb + st * PF_ATOM + bx * PF_BOX32, &tmB, 64 * i, p0 + 32 * bx, &b_full[st]);
             }
             issued = i + 1;
         }
         if (!ok && leader) {
             atomicExch(plan.error, PF_ERR_TIMEOUT);
-            pf_drain(b_full, issued, PF_NSB);
+            tc_drain(b_full, issued, PF_NSB);
         }
     } else if (warp == 1) {
         // MMA issuer: the whole warp runs the loop (uniform operands), one
@@ -487,7 +422,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         const uint32_t idesc = umma_idesc_f16(PF_TILE, (ntile + 15) & ~15);
         for (int i = 0; i < n_atoms && ok; i++) {
             const int sa = i % PF_NSA, sbq = i % PF_NSB;
-            if (!pf_wait_warp(&a_full[sa], (i / PF_NSA) & 1) || !pf_wait_warp(&b_full[sbq], (i / PF_NSB) & 1)) {
+            if (!tc_wait_warp(&a_full[sa], (i / PF_NSA) & 1) || !tc_wait_warp(&b_full[sbq], (i / PF_NSB) & 1)) {
                 ok = false;
                 break;
             }
@@ -506,7 +441,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         if (!ok) {
             // the MMAs already issued finish before tensor memory is freed
             if (lane == 0) atomicExch(plan.error, PF_ERR_TIMEOUT);
-            pf_wait_warp(&acc_full, 0);
+            tc_wait_warp(&acc_full, 0);
         }
     } else {
         // dequantization: warp (q = warp % 4, g) owns tensor-memory lanes
@@ -521,7 +456,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         const uint32_t tlane = (uint32_t)(32 * q) << 16;
         for (int sbk = 0; sbk < NB && ok; sbk++) {
             const int rs = sbk % RAW_NS;
-            if (!pf_wait_warp(&raw_full[rs], (sbk / RAW_NS) & 1)) { ok = false; break; }
+            if (!tc_wait_warp(&raw_full[rs], (sbk / RAW_NS) & 1)) { ok = false; break; }
             const uint8_t *r = sr + rs * RAW;
             // atom g of this lane's rows in both blocks, dequantized into
             // registers before the tensor-memory stage is waited for
@@ -573,20 +508,20 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
             // proxy fence orders them before the next TMA write into it
             fence_async_smem();
             __syncwarp();
-            if (lane == 0) pf_arrive(&raw_empty[rs]);
+            if (lane == 0) tc_arrive(&raw_empty[rs]);
             const int i = 4 * sbk + g, sa = i % PF_NSA;
-            if (!pf_wait_warp(&a_empty[sa], ((i / PF_NSA) & 1) ^ 1)) { ok = false; break; }
+            if (!tc_wait_warp(&a_empty[sa], ((i / PF_NSA) & 1) ^ 1)) { ok = false; break; }
             tmem_fence_after();
 #pragma unroll
             for (int b = 0; b < PF_RB; b++) tmem_st32(tmem_a + tlane + 64 * sa + 32 * b, v[b]);
             tmem_wait_st();
             tmem_fence_before();
             __syncwarp();
-            if (lane == 0) pf_arrive(&a_full[sa]);
+            if (lane == 0) tc_arrive(&a_full[sa]);
         }
         // epilogue: this warp reads tensor-memory lanes 32 (warp % 4) .. + 31
         // of both accumulators
-        if (ok && pf_wait_warp(&acc_full, 0)) {
+        if (ok && tc_wait_warp(&acc_full, 0)) {
             tmem_fence_after();
             // PF_DQ_WARPS / 4 warps per lane quarter: column chunks alternate between them
             const int sub = (warp - PF_DQ_WARP0) >> 2;
@@ -673,8 +608,8 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
     const int m0 = 128 * blockIdx.x, n0 = 128 * blockIdx.y, split = blockIdx.z;
     const int na = H / 64 / nsplit, a0 = na * split;
     if (tid == 0) {
-        for (int i = 0; i < RT_NS; i++) { pf_mbar_init(&full[i], 1); pf_mbar_init(&empty[i], 1); }
-        pf_mbar_init(&acc_full, 1);
+        for (int i = 0; i < RT_NS; i++) { tc_mbar_init(&full[i], 1); tc_mbar_init(&empty[i], 1); }
+        tc_mbar_init(&acc_full, 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
     }
@@ -689,27 +624,27 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
         int issued = 0;
         for (int i = 0; i < na && ok; i++) {
             const int st = i % RT_NS;
-            if (!pf_wait_warp(&empty[st], ((i / RT_NS) & 1) ^ 1)) { ok = false; break; }
+            if (!tc_wait_warp(&empty[st], ((i / RT_NS) & 1) ^ 1)) { ok = false; break; }
             if (leader) {
                 uint8_t *b = sm + st * 4 * PF_ATOM;
                 const int kx = 64 * (a0 + i);
-                pf_expect(&full[st], 4 * PF_ATOM);
-                pf_tma2(b, &tm_wh, kx, m0, &full[st]);
-                pf_tma2(b + PF_ATOM, &tm_wl, kx, m0, &full[st]);
-                pf_tma2(b + 2 * PF_ATOM, &tm_xh, kx, n0, &full[st]);
-                pf_tma2(b + 3 * PF_ATOM, &tm_xl, kx, n0, &full[st]);
+                tc_expect(&full[st], 4 * PF_ATOM);
+                tc_tma2(b, &tm_wh, kx, m0, &full[st]);
+                tc_tma2(b + PF_ATOM, &tm_wl, kx, m0, &full[st]);
+                tc_tma2(b + 2 * PF_ATOM, &tm_xh, kx, n0, &full[st]);
+                tc_tma2(b + 3 * PF_ATOM, &tm_xl, kx, n0, &full[st]);
             }
             issued = i + 1;
         }
         if (!ok && leader) {
             atomicExch(error, PF_ERR_TIMEOUT);
-            pf_drain(full, issued, RT_NS);
+            tc_drain(full, issued, RT_NS);
         }
     } else if (warp == 1) {
         const uint32_t idesc = umma_idesc_f16(128, 128);
         for (int i = 0; i < na && ok; i++) {
             const int st = i % RT_NS;
-            if (!pf_wait_warp(&full[st], (i / RT_NS) & 1)) { ok = false; break; }
+            if (!tc_wait_warp(&full[st], (i / RT_NS) & 1)) { ok = false; break; }
             tmem_fence_after();
             const uint32_t b = umma_smem_u32(sm + st * 4 * PF_ATOM);
 #pragma unroll
@@ -725,11 +660,11 @@ __global__ void __launch_bounds__(RT_THREADS, 1)
         umma_commit_warp(&acc_full);
         if (!ok) {
             if (lane == 0) atomicExch(error, PF_ERR_TIMEOUT);
-            pf_wait_warp(&acc_full, 0);
+            tc_wait_warp(&acc_full, 0);
         }
     } else {
         // tensor-memory lanes 32 (warp % 4) .. + 31 = experts, columns = tokens
-        if (pf_wait_warp(&acc_full, 0)) {
+        if (tc_wait_warp(&acc_full, 0)) {
             tmem_fence_after();
             const int q = warp & 3, e = m0 + 32 * q + lane;
             for (int c = 0; c < 128; c += 16) {

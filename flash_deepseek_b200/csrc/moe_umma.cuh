@@ -1,10 +1,12 @@
 // moe_umma.cuh -- the fifth-generation tensor-core (tcgen05) pieces used by
-// the prefill GEMMs: tensor-memory allocation, shared-memory matrix
-// descriptors for K-major 128-byte-swizzled tiles, the instruction
-// descriptor of kind::f16, the MMA, its commit to an mbarrier, and the
-// tensor-memory loads of the epilogue.  Field layouts follow the PTX ISA for
-// sm_100a (the same encodings CUTLASS writes in cute/arch/mma_sm100_desc.hpp).
+// the prefill GEMMs and the busy-expert kernels: tensor-memory allocation,
+// shared-memory matrix descriptors for K-major 128-byte-swizzled tiles, the
+// instruction descriptor of kind::f16, the MMA, its commit to an mbarrier,
+// the tensor-memory loads and stores, and the mbarrier / TMA hand-offs of
+// their pipelines.  Field layouts follow the PTX ISA for sm_100a (the same
+// encodings CUTLASS writes in cute/arch/mma_sm100_desc.hpp).
 #pragma once
+#include <cuda.h>
 #include <stdint.h>
 
 // ---------------------------------------------------------------------------
@@ -93,6 +95,32 @@ __device__ __forceinline__ void tmem_ld16(uint32_t addr, float (&v)[16]) {
     for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
+// 32 consecutive fp32 columns of this thread's lane (see tmem_ld16)
+__device__ __forceinline__ void tmem_ld32(uint32_t addr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(addr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+// 8 consecutive fp32 columns of this thread's lane (see tmem_ld16)
+__device__ __forceinline__ void tmem_ld8(uint32_t addr, float (&v)[8]) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(addr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 8; i++) v[i] = __uint_as_float(r[i]);
+}
+
 // Orders this thread's generic-proxy shared-memory writes before later
 // async-proxy reads (the tensor core reading an operand tile).
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
@@ -122,6 +150,12 @@ __device__ __forceinline__ void tmem_st32(uint32_t addr, const uint32_t (&v)[32]
         "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]),
         "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
         : "memory");
+}
+// 8 consecutive 32-bit columns of this thread's lane (see tmem_st32)
+__device__ __forceinline__ void tmem_st8(uint32_t addr, const uint32_t (&v)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n" ::"r"(addr), "r"(v[0]),
+                 "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+                 : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory"); }
 
@@ -166,5 +200,73 @@ __device__ __forceinline__ void umma_f16_warp(uint32_t tmem_d, uint64_t desc_a, 
         "setp.ne.b32 p, %4, 0;\n\t"
         "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}\n" ::"r"(tmem_d),
         "l"(desc_a), "l"(desc_b), "r"(idesc), "r"(accumulate), "r"(0u)
+        : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Pipeline hand-offs of the tcgen05 kernels: mbarriers whose waits give up
+// after about a second (the caller records an error instead of hanging), and
+// TMA tile loads that complete on an mbarrier.
+// ---------------------------------------------------------------------------
+#define TC_WAIT_CYCLES (1ll << 31)
+#define TC_SUSPEND_NS 1000000u  // a waiting thread sleeps up to 1 ms per try (woken when the phase completes)
+
+__device__ __forceinline__ void tc_mbar_init(uint64_t *b, int n) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(umma_smem_u32(b)), "r"(n) : "memory");
+}
+__device__ __forceinline__ void tc_expect(uint64_t *b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(umma_smem_u32(b)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_arrive(uint64_t *b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(umma_smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool tc_wait(uint64_t *b, uint32_t parity) {
+    {
+        // completed phases (the common case in a pipeline that keeps up) cost
+        // one non-blocking test, without the suspend hint and the clock read
+        uint32_t ok;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+            " selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(ok)
+            : "r"(umma_smem_u32(b)), "r"(parity)
+            : "memory");
+        if (ok) return true;
+    }
+    const long long t0 = clock64();
+    for (;;) {
+        uint32_t ok;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+            " selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(ok)
+            : "r"(umma_smem_u32(b)), "r"(parity), "r"(TC_SUSPEND_NS)
+            : "memory");
+        if (ok) return true;
+        if (clock64() - t0 > TC_WAIT_CYCLES) return false;
+    }
+}
+// after a producer gave up: wait (bounded) for the copies it issued into
+// the last `ns` stages of a ring, so that none lands after the CTA exits
+__device__ __forceinline__ void tc_drain(uint64_t *full, int issued, int ns) {
+    for (int k = issued > ns ? issued - ns : 0; k < issued; k++) tc_wait(&full[k % ns], (k / ns) & 1);
+}
+// the same, agreed by the whole warp (a lane that gave up fails them all)
+__device__ __forceinline__ bool tc_wait_warp(uint64_t *b, uint32_t parity) {
+    return __all_sync(0xffffffffu, tc_wait(b, parity));
+}
+__device__ __forceinline__ void tc_tma3(void *dst, const CUtensorMap *m, int x, int y, int z, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];\n" ::"r"(umma_smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(z), "r"(umma_smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void tc_tma2(void *dst, const CUtensorMap *m, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::
+            "r"(umma_smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(umma_smem_u32(bar))
         : "memory");
 }
