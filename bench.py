@@ -60,6 +60,7 @@ EXTRA = {
 Q4_DOWN_BYTES = H * (I // 256) * 144         # 8,257,536
 
 
+TC_MIN_TOKENS = 9           # an expert with this many tokens or more runs on the tcgen05 kernels (MOE_TC + 1)
 NVLINK_GBS = 900.0          # NVLink 5, per direction per GPU (nominal)
 NVLINK_MEASURED_GBS = 770.0  # peer copy per direction measured on this pool's B200 boxes
 N_POOL = 4
@@ -304,15 +305,26 @@ def run_ours(args):
     else:
         idx_g = idx_loc.numpy()
     NE = args.experts
-    gu_bytes, dn_bytes, active = [], [], []
+    # algorithmic bytes per launch, split between the GEMVs and the tcgen05
+    # kernels: an expert with more than TC_MIN_TOKENS - 1 tokens on this rank
+    # runs on tcgen05 (the shared expert with this rank's b_loc tokens too)
+    gu_bytes, dn_bytes, gu_tc, dn_tc, active = [], [], [], [], []
     for s in range(args.steps):
         mine = ep.expert_owner(idx_g[s], NE, world) == rank
         n_act = len(ep.experts_hit(idx_g[s], NE, world, rank)) + 1
-        rows = int(mine.any(axis=1).sum()) + b_loc
-        pairs = int(mine.sum()) + b_loc
+        cnt = np.bincount(idx_g[s][mine].reshape(-1), minlength=NE)
+        ntok = [int(c) for c in cnt if c > 0] + [b_loc]
         active.append(n_act)
-        gu_bytes.append(n_act * 2 * GATE_BYTES + rows * H * 4 + pairs * I * 4)
-        dn_bytes.append(n_act * DOWN_Q6_BYTES + pairs * (I * 4 + H * 4))
+        g = [0, 0]   # gate/up bytes: GEMV, tcgen05
+        dd = [0, 0]
+        for n in ntok:
+            tc = 1 if n >= TC_MIN_TOKENS else 0
+            g[tc] += 2 * GATE_BYTES + n * H * 4 + n * I * 4
+            dd[tc] += DOWN_Q6_BYTES + n * (I * 4 + H * 4)
+        gu_bytes.append(g[0])
+        gu_tc.append(g[1])
+        dn_bytes.append(dd[0])
+        dn_tc.append(dd[1])
     # expert-parallel exchange and the per-GPU critical path, from the
     # global routing of every timed step (all ranks compute the same figures)
     nv = None
@@ -356,9 +368,18 @@ def run_ours(args):
                                         (peaks()[0] * world), 4)}
     gu_ms = float(np.mean([p["gateup"] for p in phases]))
     dn_ms = float(np.mean([p["down"] for p in phases]))
+    gut_ms = float(np.mean([p["gateup_tc"] for p in phases]))
+    dnt_ms = float(np.mean([p["down_tc"] for p in phases]))
     peak, peak_kind = peaks()
     ach = float(np.mean(gu_bytes)) / (gu_ms / 1e3) / 1e9
     ach_dn = float(np.mean(dn_bytes)) / (dn_ms / 1e3) / 1e9
+
+    def tc_roof(nbytes, ms, kernel):
+        if ms <= 0 or nbytes <= 0:
+            return None
+        a = nbytes / (ms / 1e3) / 1e9
+        return {"kernel": kernel, "achieved": round(a, 1), "frac": round(a / peak, 4),
+                "algorithmic_bytes_per_launch": round(nbytes), "launch_ms": round(ms, 5)}
     step_bytes = float(np.mean([a * EXPERT_BYTES for a in active])) + NE * H * 4 + NE * 4
     traffic = traffic_from_profiles("k_gateup", args.workload, float(np.mean(gu_bytes)))
     traffic_dn = traffic_from_profiles("k_down", args.workload, float(np.mean(dn_bytes)))
@@ -404,10 +425,12 @@ def run_ours(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "exact tensor-core products of the Q4_K/Q6_K integers (sub-block scales folded in) with "
-                     "fp16 hi/lo (22-bit) or int8-plane (21-bit) activations, fp32 accumulation",
+                     "fp16 hi/lo (22-bit) or int8-plane (21-bit) activations, fp32 accumulation (tcgen05 for "
+                     "experts with 9+ tokens, mma.sync GEMVs for the rest)",
             "data": "synthetic: random-init N(0,0.02) weights quantized on device, N(0,1) tokens",
             "config": workload_config(W, NE, world, b_loc),
-            "roofline": {"bound": "hbm", "kernel": "k_gateup (grouped Q4_K gate/up GEMV + SwiGLU)",
+            "roofline": {"bound": "hbm", "kernel": "k_gateup (grouped Q4_K gate/up GEMV + SwiGLU; experts with at "
+                                                   "most 8 tokens, the largest kernel of the step)",
                          "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(ach / peak, 4), "peak_source": peak_kind,
                          "frac_of_8TBs": round(ach / 8000.0, 4),
@@ -418,6 +441,14 @@ def run_ours(args):
                               "frac": round(ach_dn / peak, 4), "traffic": traffic_dn,
                               "algorithmic_bytes_per_launch": round(float(np.mean(dn_bytes))),
                               "launch_ms": round(dn_ms, 5)},
+            "roofline_tc": {"gateup": tc_roof(float(np.mean(gu_tc)), gut_ms,
+                                              "k_tc_gather + k_experts_tc<0> (busy experts' gate/up on tcgen05)"),
+                            "down": tc_roof(float(np.mean(dn_tc)), dnt_ms,
+                                            "k_experts_tc<2> (busy experts' Q6_K down on tcgen05)")},
+            "roofline_phases": {
+                "gateup": round(float(np.mean(gu_bytes) + np.mean(gu_tc)) / ((gu_ms + gut_ms) / 1e3) / 1e9 / peak, 4),
+                "down": round(float(np.mean(dn_bytes) + np.mean(dn_tc)) / ((dn_ms + dnt_ms) / 1e3) / 1e9 / peak, 4),
+                "note": "all weight and activation bytes of the phase over the phase's time, fraction of measured HBM"},
             "step_hbm": {"weight_bytes_per_step": round(step_bytes),
                          "achieved_gbs": round(step_bytes / (total_ms / args.steps / 1e3) / 1e9, 1),
                          "active_experts_per_step": round(float(np.mean(active)), 2)},
@@ -767,6 +798,7 @@ def other_configs(args):
     be): config 2 (one token), config 1 (one expert per call), config 5 (4096-
     token prefill) and config 4 (the 58-layer stack at batch 1)."""
     keep = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "dtype", "roofline", "roofline_down",
+            "roofline_tc", "roofline_phases",
             "phase_ms", "e2e", "gpu_launches", "clocks", "config")
     out = {}
     for wl, steps in (("decode_b1", 100), ("expert1", 256), ("prefill4096", 3), ("stack_b1", 3)):

@@ -67,7 +67,7 @@ SIGNATURES = {
     "moe_get_timing_at": (C.c_int, [_vp, C.c_int, _vp, C.c_int]),
 }
 
-PHASES = ["router", "route", "dispatch", "gateup", "prep", "down", "combine_a2a", "output"]
+PHASES = ["router", "route", "dispatch", "gateup_tc", "gateup", "prep", "down_tc", "down", "combine_a2a", "output"]
 
 _lib = None
 

@@ -787,17 +787,19 @@ static int run_local(moe_ctx *c, int layer, const float *x, int T, const int *id
     // tcgen05 chunks
     const bool tc = d.tc && T > MOE_TC;
     const int P = T * d.K + T;
-    mark(c, MOE_PHASE_GATEUP, s);
+    mark(c, MOE_PHASE_GATEUP_TC, s);
     if (tc) {
         moe_launch_tc_gather(d, c->plan, c->xop, c->xtc, P, s, &c->launches);
         moe_launch_gateup_tc(d, L, c->plan, c->tm_xtc, c->act, P, s, &c->launches);
     }
+    mark(c, MOE_PHASE_GATEUP, s);
     moe_launch_gateup(d, L, c->plan, c->xop, c->act,
                       max_chunks, s, &c->launches);
     mark(c, MOE_PHASE_PREP, s);
     moe_launch_prep_down(d, L, c->plan, c->act, c->dop, P, s, &c->launches);
-    mark(c, MOE_PHASE_DOWN, s);
+    mark(c, MOE_PHASE_DOWN_TC, s);
     if (tc) moe_launch_down_tc(d, L, c->plan, c->tm_dop, c->eo, P, s, &c->launches);
+    mark(c, MOE_PHASE_DOWN, s);
     moe_launch_down(d, L, c->plan, c->dop, c->eo, max_chunks, s, &c->launches);
     mark(c, MOE_PHASE_OUTPUT, s);
     moe_launch_combine(d, c->plan, c->eo, T, routed, with_shared, residual, out, s, &c->launches);
@@ -841,16 +843,18 @@ static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_i
         const EpP2P q{c->d_peers, c->mb_x, c->mb_meta, c->mb_y, N, c->rank, c->d_seq, c->ep_done, c->plan.error};
         moe_launch_ep_pack_p2p(x, c->idx, c->wts, T, d.K, d.H, c->n_local, cap, q, c->tok_slot, s, &c->launches);
         moe_launch_ep_plan_rows_p2p(d, q, cap, T, c->e0, c->n_local, c->plan, x, c->xop, s, &c->launches);
-        mark(c, MOE_PHASE_GATEUP, s);
+        mark(c, MOE_PHASE_GATEUP_TC, s);
         if (tc) {
             moe_launch_tc_gather(d, c->plan, c->xop, c->xtc, P, s, &c->launches);
             moe_launch_gateup_tc(d, L, c->plan, c->tm_xtc, c->act, P, s, &c->launches);
         }
+        mark(c, MOE_PHASE_GATEUP, s);
         moe_launch_gateup(d, L, c->plan, c->xop, c->act, max_chunks, s, &c->launches);
         mark(c, MOE_PHASE_PREP, s);
         moe_launch_prep_down(d, L, c->plan, c->act, c->dop, P, s, &c->launches);
-        mark(c, MOE_PHASE_DOWN, s);
+        mark(c, MOE_PHASE_DOWN_TC, s);
         if (tc) moe_launch_down_tc(d, L, c->plan, c->tm_dop, c->eo, P, s, &c->launches);
+        mark(c, MOE_PHASE_DOWN, s);
         moe_launch_down(d, L, c->plan, c->dop, c->eo, max_chunks, s, &c->launches);
         mark(c, MOE_PHASE_COMBINE, s);
         moe_launch_ep_partial_p2p(d, c->plan, c->eo, cap, q, s, &c->launches);
@@ -876,17 +880,19 @@ static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_i
     }
     moe_launch_ep_plan(d, c->recv_meta, N, cap, T, c->e0, c->n_local, c->plan, s, &c->launches);
     moe_launch_prep_rows(c->recv_x, c->recv_meta, mw, R, x, T, d.H, c->xop, s, &c->launches);
-    mark(c, MOE_PHASE_GATEUP, s);
+    mark(c, MOE_PHASE_GATEUP_TC, s);
     if (tc) {
         moe_launch_tc_gather(d, c->plan, c->xop, c->xtc, P, s, &c->launches);
         moe_launch_gateup_tc(d, L, c->plan, c->tm_xtc, c->act, P, s, &c->launches);
     }
+    mark(c, MOE_PHASE_GATEUP, s);
     moe_launch_gateup(d, L, c->plan, c->xop, c->act,
                       max_chunks, s, &c->launches);
     mark(c, MOE_PHASE_PREP, s);
     moe_launch_prep_down(d, L, c->plan, c->act, c->dop, P, s, &c->launches);
-    mark(c, MOE_PHASE_DOWN, s);
+    mark(c, MOE_PHASE_DOWN_TC, s);
     if (tc) moe_launch_down_tc(d, L, c->plan, c->tm_dop, c->eo, P, s, &c->launches);
+    mark(c, MOE_PHASE_DOWN, s);
     moe_launch_down(d, L, c->plan, c->dop, c->eo, max_chunks, s, &c->launches);
     mark(c, MOE_PHASE_COMBINE, s);
     {

@@ -263,15 +263,17 @@ int moe_dequantize_row_q6_K(const void *src, float *dst, size_t n);
  * the reference's moe_prof_t phase records, infer.m:177-261): when enabled,
  * CUDA events are recorded on the context stream between the phases below and
  * moe_get_timing() returns their durations in milliseconds. */
-#define MOE_PHASE_ROUTER 0   /* router logits GEMV */
-#define MOE_PHASE_ROUTE 1    /* sigmoid + grouped top-k + plan + operand */
-#define MOE_PHASE_DISPATCH 2 /* expert-parallel dispatch (0 on one GPU) */
-#define MOE_PHASE_GATEUP 3   /* gate/up GEMV + SwiGLU */
-#define MOE_PHASE_PREP 4     /* down-operand preparation */
-#define MOE_PHASE_DOWN 5     /* down GEMV */
-#define MOE_PHASE_COMBINE 6  /* combine all-to-all (0 on one GPU) */
-#define MOE_PHASE_OUTPUT 7   /* weighted combine + shared (+ residual) */
-#define MOE_N_PHASES 8
+#define MOE_PHASE_ROUTER 0     /* router logits GEMV */
+#define MOE_PHASE_ROUTE 1      /* sigmoid + grouped top-k + plan + operand */
+#define MOE_PHASE_DISPATCH 2   /* expert-parallel dispatch (0 on one GPU) */
+#define MOE_PHASE_GATEUP_TC 3  /* busy experts' gate/up on tcgen05 (+ their operand gather) */
+#define MOE_PHASE_GATEUP 4     /* gate/up GEMV + SwiGLU (the other experts) */
+#define MOE_PHASE_PREP 5       /* down-operand preparation */
+#define MOE_PHASE_DOWN_TC 6    /* busy experts' down on tcgen05 */
+#define MOE_PHASE_DOWN 7       /* down GEMV (the other experts) */
+#define MOE_PHASE_COMBINE 8    /* combine all-to-all (0 on one GPU) */
+#define MOE_PHASE_OUTPUT 9     /* weighted combine + shared (+ residual) */
+#define MOE_N_PHASES 10
 /* enable > 0 turns timing on with a ring of `enable` steps (each forward call
  * records into the next slot), 0 turns it off. */
 int moe_set_timing(moe_ctx *ctx, int enable);
