@@ -15,6 +15,7 @@
 #include <chrono>
 #include <string>
 #include <thread>
+#include <algorithm>
 #include <vector>
 
 #include "../../include/moe_cuda.h"
@@ -782,7 +783,8 @@ static int run_local(moe_ctx *c, int layer, const float *x, int T, const int *id
     mark(c, MOE_PHASE_ROUTE, s);
     moe_launch_route_and_plan(d, nullptr, 0, c->logits, L.bias, L.logit_bias, mode, idx_in, w_in, T, c->idx, c->wts,
                               x, c->xop, with_shared, 1, c->plan, c->counter, s, &c->launches);
-    const int max_chunks = (T * d.K + T + MOE_TC - 1) / MOE_TC + d.E + 1;
+    // a chunk holds at least one pair (the GEMV grids are sized by this bound)
+    const int max_chunks = std::min(T * d.K + T, (T * d.K + T + MOE_TC - 1) / MOE_TC + d.E + 1);
     // an expert gets at most T tokens: with more than MOE_TC there can be
     // tcgen05 chunks
     const bool tc = d.tc && T > MOE_TC;
@@ -834,7 +836,7 @@ static int run_ep(moe_ctx *c, int layer, const float *x, int T, const int *idx_i
                                   c->wts, x, nullptr, 0, 0, c->plan, c->counter, s, &c->launches);
     mark(c, MOE_PHASE_DISPATCH, s);
     const int P = R * d.K + T;
-    const int max_chunks = (P + MOE_TC - 1) / MOE_TC + d.E + 1;
+    const int max_chunks = std::min(P, (P + MOE_TC - 1) / MOE_TC + d.E + 1);
     // a routed expert gets at most R received rows, the shared one T local rows
     const bool tc = d.tc && (R > MOE_TC || T > MOE_TC);
     if (c->p2p) {
