@@ -1088,6 +1088,7 @@ static int take_device_error(moe_ctx *c) {
         }
         if (e == EX_ERR_TIMEOUT) return fail(c, MOE_ERR_TIMEOUT, "expert pipeline wait timed out");
         if (e == PF_ERR_TIMEOUT) return fail(c, MOE_ERR_TIMEOUT, "prefill pipeline wait timed out");
+        if (e == PF_ERR_PAIR) return fail(c, MOE_ERR_CUDA, "prefill CTA pair: tensor-memory allocations differ");
         if (e == MOE_DEV_ERR_INDEX) return fail(c, MOE_ERR_ARG, "expert index out of range in routing");
         return fail(c, MOE_ERR_CUDA, "device error code 0x%x", e);
     }
@@ -1296,9 +1297,10 @@ int moe_prefill_device(moe_ctx *c, int layer, const float *d_h, int T, float *d_
         return fail(c, MOE_ERR_ARG, "moe_prefill_device: need n_tokens >= 1 and buffers (0 only in expert parallelism)");
     int rc = check_layer(c, layer);
     if (rc) return rc;
-    if (c->d.H % 256 || c->d.I % 128 || c->d.K > 63 || c->d.E > 1024)
+    // row groups of the CTA pairs: gate/up 2 x 128 rows of I, down 2 x 256 rows of H
+    if (c->d.H % 512 || c->d.I % 256 || c->d.K > 63 || c->d.E > 1024)
         return fail(c, MOE_ERR_ARG,
-                    "moe_prefill needs hidden %% 256 == 0, intermediate %% 128 == 0, top_k <= 63, n_experts <= 1024");
+                    "moe_prefill needs hidden %% 512 == 0, intermediate %% 256 == 0, top_k <= 63, n_experts <= 1024");
     DeviceScope ds(c->device);
     cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
     if (c->world > 1) return run_prefill_ep(c, layer, d_h, T, d_out, d_idx, d_w, s);

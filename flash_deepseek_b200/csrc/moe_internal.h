@@ -77,6 +77,7 @@ static inline cudaError_t moe_launch_pdl(void (*kernel)(KArgs...), dim3 grid, di
 #define MOE_DEV_ERR_INDEX 1          // routed expert index out of range
 #define EX_ERR_TIMEOUT 0x7100        // expert GEMV pipeline: an mbarrier wait gave up
 #define PF_ERR_TIMEOUT 0x7200        // prefill GEMM pipeline: an mbarrier wait gave up
+#define PF_ERR_PAIR 0x7201           // prefill GEMM: the CTA pair's tensor-memory columns differ
 #define EP_ERR_TIMEOUT 0x7300        // peer exchange: a peer's step flag did not arrive
 
 // Raises a kernel's dynamic shared-memory limit on the current device when

@@ -5,24 +5,27 @@
 // (C = W X^T, M = weight rows, N = tokens, K = hidden or intermediate), so
 // the weights are dequantized once per tile into fp16 tiles that feed
 // tcgen05.mma, with the fp32 accumulator in tensor memory:
-//   plan     counting sort of the (token, slot) pairs by expert, tiles of
-//            <= 128 pairs per expert
+//   plan     counting sort of the (token, slot) pairs by expert; an
+//            expert's pairs split evenly into tiles of <= 160
 //   gather   fp16 copy of each pair's token row, pairs grouped by expert
-//   gemm1    gate/up rows (2 blocks of 64 + 64 per CTA) x <= 128 pairs,
-//            SwiGLU in the epilogue (infer.m:378-383), act in fp16
-//   gemm2    down rows (2 blocks of 128 per CTA) x <= 128 pairs, fp32
+//   gemm1    gate/up rows (2 blocks of 64 + 64 per CTA, a CTA pair per
+//            tile) x <= 160 pairs, SwiGLU in the epilogue
+//            (infer.m:378-383), act in fp16
+//   gemm2    down rows (2 blocks of 128 per CTA) x <= 160 pairs, fp32
 //            expert outputs
 //   combine  slot order, then the shared expert (infer.m:1915-1922)
 // Differences from the reference's fp32 dot: weights and activations are
 // rounded to fp16 (11-bit significands) before the fp32-accumulated product.
 //
-// GEMM CTA (one per SM): warp 0 streams the raw Q4_K / Q6_K tiles, one
-// super-block per stage; warp 2 streams the pairs' 64-column activation
-// slices (TMA, 128-byte swizzle) into a ring of 16 KB stages; warp 1 owns
-// tensor memory and runs the MMA loop, one elected lane issuing each MMA
-// (both row blocks share every activation stage).  16 warps
-// dequantize: warp (q, g) writes atom g of every super-block for tensor-
-// memory lanes 32q .. 32q + 31 straight into tensor memory (tcgen05.st), so
+// GEMM CTA (one per SM, two SMs of a TPC per tile as a cta_group::2 pair):
+// warp 0 streams the raw Q4_K / Q6_K tiles of its own rows, one super-block
+// per stage; warp 2 streams its half of the pairs' 64-column activation
+// slices (TMA, 128-byte swizzle) into a ring of 10 KB stages; warp 1 of the
+// leader runs the MMA loop, one elected lane issuing each M = 256 pair MMA
+// (both row blocks share every activation stage).  12 warps
+// dequantize: warp (q, g) writes the K atoms g, g + 3, ... through A stage g
+// for tensor-memory lanes 32q .. 32q + 31 straight into tensor memory
+// (tcgen05.st), so
 // the A operand never touches shared memory, and the MMA reads A from tensor
 // memory and B from shared memory; the same warps run the epilogue.  All
 // hand-offs are mbarriers; every wait gives up after about a second and
@@ -37,20 +40,21 @@
 #include "moe_internal.h"
 #include "moe_umma.cuh"
 
-#define PF_TILE 128                // weight rows per accumulator (MMA M)
-#define PF_RB 2                    // row blocks per CTA: M = 256 rows share each activation stage
-#define PF_TILE_N 128              // pairs per tile (MMA N <= 128)
-#define PF_ATOM 16384              // one 128-row x 128-byte activation stage (64 columns of K)
-#define PF_BOX32 4096              // one 32-row activation box (4 swizzle atoms of 8 rows)
-#define PF_NSA 4                   // A stages in tensor memory (PF_RB x 32 columns each, after the accumulators)
-#define PF_NSB 6                   // activation stages
+#define PF_TILE 128                // weight rows per accumulator block of one CTA (the pair MMA has M = 256)
+#define PF_RB 2                    // row blocks per CTA: 2 x 128 rows share each activation stage
+#define PF_TILE_N 160              // pairs per tile (pair MMA N <= 160, a multiple of 32)
+#define PF_ATOM 16384              // one 128-row x 128-byte tile (64 columns of K; router stages)
+#define PF_BST (PF_TILE_N / 2 * 128)  // one activation stage of a CTA: its half of the pairs x 128 B
+#define PF_BOX16 2048              // one 16-row activation box (2 swizzle atoms of 8 rows)
+#define PF_NSA 3                   // A stages in tensor memory (PF_RB x 32 columns each, after the accumulators)
+#define PF_NSB 8                   // activation stages
 #define PF_Q6_ROW 208              // Q6_K Q-plane row stride in shared memory (192 B used)
 #define PF_RAW_Q4 (PF_RB * 128 * 144)                  // PF_RB x 128 Q4_K rows of one super-block
 #define PF_RAW_Q6 (PF_RB * 128 * (PF_Q6_ROW + 16))     // Q planes of both blocks, then their scale planes
 #define PF_RAW_NS_Q4 3             // raw super-block stages
 #define PF_RAW_NS_Q6 2
 #define PF_RAW_NS_MAX 3
-#define PF_DQ_WARPS 16                              // dequantize + epilogue (warps 3 ..)
+#define PF_DQ_WARPS (4 * PF_NSA)                    // dequantize + epilogue (warps 3 ..): 4 per A stage
 #define PF_DQ_WARP0 3                               // warps 0-2: weight TMA, MMA, activation TMA
 #define PF_THREADS (32 * (PF_DQ_WARP0 + PF_DQ_WARPS))
 
@@ -106,7 +110,7 @@ __global__ void __launch_bounds__(1024) k_pf_offsets(MoeDims d, int T, int *__re
             off[e] = a;
             toff[e] = b;
             a += c[e];
-            b += (c[e] + PF_TILE_N - 1) / PF_TILE_N;
+            b += (c[e] + PF_TILE_N - 1) / PF_TILE_N;  // tiles of the expert
         }
         plan.counts[0] = a;
         plan.counts[1] = b;
@@ -115,10 +119,14 @@ __global__ void __launch_bounds__(1024) k_pf_offsets(MoeDims d, int T, int *__re
     __syncthreads();
     for (int e = threadIdx.x; e < NE; e += blockDim.x) {
         cur[e] = off[e];
-        for (int k = 0; k * PF_TILE_N < c[e]; k++) {
+        // the expert's pairs split evenly (sizes differ by at most one), so no
+        // tile is a small remainder that pays for a whole dequantization
+        const int nt = (c[e] + PF_TILE_N - 1) / PF_TILE_N;
+        for (int k = 0; k < nt; k++) {
+            const int a = (int)((long long)k * c[e] / nt), z = (int)((long long)(k + 1) * c[e] / nt);
             plan.chunk_expert[toff[e] + k] = e;
-            plan.chunk_pair0[toff[e] + k] = off[e] + k * PF_TILE_N;
-            plan.chunk_ntok[toff[e] + k] = min(PF_TILE_N, c[e] - k * PF_TILE_N);
+            plan.chunk_pair0[toff[e] + k] = off[e] + a;
+            plan.chunk_ntok[toff[e] + k] = z - a;
         }
     }
 }
@@ -308,14 +316,19 @@ __device__ __forceinline__ void pf_deq_q6(const uint32_t (&q)[24], const uint32_
 
 // ===========================================================================
 // GEMM.  MODE 0: gate/up (Q4_K) -> act (fp16, SwiGLU); 1: down Q4_K -> eo;
-// 2: down Q6_K -> eo.  blockIdx.x = row group (PF_RB row blocks of 128
-// accumulator rows; MODE 0: a block is 64 gate rows + the matching 64 up
-// rows), blockIdx.y = tile (expert, <= 128 pairs).  The CTAs resident at
-// one time work on a few tiles, so each tile's activation slices are read
-// from DRAM once and then hit in L2; each activation stage feeds PF_RB MMAs.
+// 2: down Q6_K -> eo.  A 2-CTA cluster (a CTA pair on one TPC) works on one
+// tile (expert, <= PF_TILE_N pairs): blockIdx.x = row group (PF_RB row
+// blocks of 128 accumulator rows per CTA; MODE 0: a block is 64 gate rows +
+// the matching 64 up rows; the pair holds two consecutive row groups),
+// blockIdx.y = tile.  Each pair MMA (M = 256: block b of both CTAs) takes the
+// first half of the tile's pairs from the leader's activation stage and the
+// second half from the peer's, so each SM streams half of the tile's
+// activations per K step, and each stage feeds PF_RB pair MMAs.  The CTAs
+// resident at one time work on a few tiles, so each tile's activation slices
+// are read from DRAM once and then hit in L2.
 // ===========================================================================
 template <int MODE>
-__global__ void __launch_bounds__(PF_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
     k_prefill_gemm(MoeDims d, const __grid_constant__ MoeLayerDev L, MoePlan plan,
                    const __grid_constant__ CUtensorMap tmB, __half *__restrict__ act, float *__restrict__ eo) {
     constexpr int RAW = MODE == 2 ? PF_RAW_Q6 : PF_RAW_Q4;
@@ -323,7 +336,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
     constexpr int QB = MODE == 2 ? 128 * PF_Q6_ROW : 128 * 144;  // one block's Q bytes in a raw stage
     extern __shared__ uint8_t pf_raw[];
     uint8_t *sm = pf_raw + ((1024u - (umma_smem_u32(pf_raw) & 1023u)) & 1023u);
-    uint8_t *sb = sm, *sr = sm + PF_NSB * PF_ATOM;
+    uint8_t *sb = sm, *sr = sm + PF_NSB * PF_BST;
     uint8_t *sd = sr + RAW_NS * RAW;  // Q6_K d planes of the blocks (PF_RB x 128 rows x 2 nb_pad bytes)
     __shared__ __align__(8) uint64_t raw_full[PF_RAW_NS_MAX], raw_empty[PF_RAW_NS_MAX], a_full[PF_NSA], a_empty[PF_NSA],
         b_full[PF_NSB], b_empty[PF_NSB], acc_full;
@@ -332,6 +345,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int tile = blockIdx.y, rg = blockIdx.x;
+    const uint32_t rank = cluster_ctarank();  // 0: the leader, which issues the pair MMAs
     if (tid == 0) {
         int skip = tile >= plan.counts[1];
         if (!skip && MODE > 0) {
@@ -341,31 +355,41 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
         s_skip = skip;
     }
     __syncthreads();
-    if (s_skip) return;
+    if (s_skip) return;  // both CTAs of the pair read the same tile: both leave here, or neither
     const int e = plan.chunk_expert[tile], p0 = plan.chunk_pair0[tile], ntile = plan.chunk_ntok[tile];
     const int slot = e == d.E ? L.n_local : e - L.e0;
     const int K = MODE == 0 ? d.H : d.I, NB = K / MOE_QK, n_atoms = 4 * NB;
-    const int nbp = q6r_nb_pad(NB), nbox = (ntile + 31) / 32;
+    const int nbp = q6r_nb_pad(NB);
+    const int npair = (ntile + 31) & ~31, nhalf = npair / 2;  // pair MMA N (a multiple of 32); pairs per CTA
     if (tid == 0) {
-        for (int i = 0; i < RAW_NS; i++) { tc_mbar_init(&raw_full[i], 1); tc_mbar_init(&raw_empty[i], PF_DQ_WARPS); }
-        for (int i = 0; i < PF_NSA; i++) { tc_mbar_init(&a_full[i], 4); tc_mbar_init(&a_empty[i], 1); }
+        // raw_empty: 4 atoms x 4 lane-quarter warps per super-block
+        for (int i = 0; i < RAW_NS; i++) { tc_mbar_init(&raw_full[i], 1); tc_mbar_init(&raw_empty[i], 16); }
+        // a_full / b_full are used in the leader: 4 dequantizing warps of each CTA; the
+        // leader's expect_tx (both CTAs' copies complete on it).  The empty barriers and
+        // acc_full of both CTAs receive the leader's commits (tcgen05.commit to both).
+        for (int i = 0; i < PF_NSA; i++) { tc_mbar_init(&a_full[i], 8); tc_mbar_init(&a_empty[i], 1); }
         for (int i = 0; i < PF_NSB; i++) { tc_mbar_init(&b_full[i], 1); tc_mbar_init(&b_empty[i], 1); }
         tc_mbar_init(&acc_full, 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
     }
-    // tensor memory: accumulator b in columns [128 b, 128 b + 128), A stage s
-    // of block b in [256 + 64 s + 32 b, + 32)
-    if (warp == 1) tmem_alloc(&tmem_base, 512);
+    // tensor memory (the same columns in both CTAs): accumulator b in columns
+    // [PF_TILE_N b, + PF_TILE_N), A stage s of block b in [2 PF_TILE_N + 64 s + 32 b, + 32)
+    if (warp == 1) tmem_alloc_pair(&tmem_base, 512);
     tmem_fence_before();
-    __syncthreads();
+    cluster_sync_all();
     tmem_fence_after();
     const uint32_t tmem = tmem_base, tmem_a = tmem_base + PF_RB * PF_TILE_N;
-    bool ok = true;
+    // the pair MMAs address both CTAs' tensor memory with the leader's columns
+    bool ok = cluster_ld_u32(cluster_map(&tmem_base, rank ^ 1u)) == tmem;
+    if (!ok && tid == 0) atomicExch(plan.error, PF_ERR_PAIR);
 
-    if (warp == 0) {
-        // weight producer: the raw tiles of each super-block, RAW_NS ahead
-        // (the warp loops together, one elected lane issues the copies)
+    if (!ok) {
+        // nothing issued: both CTAs go straight to the teardown
+    } else if (warp == 0) {
+        // weight producer: the raw tiles of this CTA's blocks, one super-block
+        // per stage, RAW_NS ahead (the warp loops together, one elected lane
+        // issues the copies)
         const uint32_t leader = elect_one();
         int issued = 0;
         for (int sbk = 0; sbk < NB && ok; sbk++) {
@@ -397,56 +421,72 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
             tc_drain(raw_full, issued, RAW_NS);
         }
     } else if (warp == 2) {
-        // activation producer: the pairs' 64-column slices, PF_NSB atoms ahead
+        // activation producer: this CTA's half of the tile's pairs (16-row
+        // boxes), PF_NSB atoms ahead.  The copies of both CTAs complete on the
+        // leader's b_full, where the leader expects the bytes of both halves.
         const uint32_t leader = elect_one();
+        const int nbox = nhalf / 16, y0 = p0 + (int)rank * nhalf;
         int issued = 0;
         for (int i = 0; i < n_atoms && ok; i++) {
             const int st = i % PF_NSB;
             if (!tc_wait_warp(&b_empty[st], ((i / PF_NSB) & 1) ^ 1)) { ok = false; break; }
             if (leader) {
-                // only the 32-row boxes the tile's pairs reach (L2 traffic)
-                tc_expect(&b_full[st], nbox * PF_BOX32);
+                if (rank == 0) tc_expect(&b_full[st], 2 * nbox * PF_BOX16);
+                const uint32_t bar = cluster_map(&b_full[st], 0);
                 for (int bx = 0; bx < nbox; bx++)
-                    tc_tma2(sb + st * PF_ATOM + bx * PF_BOX32, &tmB, 64 * i, p0 + 32 * bx, &b_full[st]);
+                    tc_tma2_pair(sb + st * PF_BST + bx * PF_BOX16, &tmB, 64 * i, y0 + 16 * bx, bar);
             }
             issued = i + 1;
         }
         if (!ok && leader) {
             atomicExch(plan.error, PF_ERR_TIMEOUT);
-            tc_drain(b_full, issued, PF_NSB);
+            // the leader waits (bounded) for the last stages; the peer's copies
+            // complete on the leader's barriers, and a peer that gave up here
+            // issued its last copy at least one wait limit earlier
+            if (rank == 0) tc_drain(b_full, issued, PF_NSB);
         }
     } else if (warp == 1) {
-        // MMA issuer: the whole warp runs the loop (uniform operands), one
-        // elected lane issues each MMA and commit.
-        // N = the tile's pairs rounded up to 16 (M = 128 takes N = 16 .. 256 in steps of 16)
-        const uint32_t idesc = umma_idesc_f16(PF_TILE, (ntile + 15) & ~15);
-        for (int i = 0; i < n_atoms && ok; i++) {
-            const int sa = i % PF_NSA, sbq = i % PF_NSB;
-            if (!tc_wait_warp(&a_full[sa], (i / PF_NSA) & 1) || !tc_wait_warp(&b_full[sbq], (i / PF_NSB) & 1)) {
-                ok = false;
-                break;
+        if (rank == 0) {
+            // MMA issuer (leader): the whole warp runs the loop, one elected lane
+            // issues each MMA and commit; the operands are broadcast from lane 0 so
+            // that they sit in uniform registers and the MMAs issue back to back.
+            // The commits arrive on the barrier of the same address in both CTAs.
+            const uint32_t idesc = __shfl_sync(0xffffffffu, umma_idesc_f16(2 * PF_TILE, npair), 0);
+            const uint32_t td = __shfl_sync(0xffffffffu, tmem, 0), ta0 = __shfl_sync(0xffffffffu, tmem_a, 0);
+            for (int i = 0; i < n_atoms && ok; i++) {
+                const int sa = i % PF_NSA, sbq = i % PF_NSB;
+                if (!tc_wait_warp(&a_full[sa], (i / PF_NSA) & 1) || !tc_wait_warp(&b_full[sbq], (i / PF_NSB) & 1)) {
+                    ok = false;
+                    break;
+                }
+                tmem_fence_after();
+                const uint64_t bdesc = umma_desc_sw128(__shfl_sync(0xffffffffu, umma_smem_u32(sb + sbq * PF_BST), 0));
+                const uint32_t ta = __shfl_sync(0xffffffffu, ta0 + 64 * sa, 0);
+                const uint32_t acc = __shfl_sync(0xffffffffu, i, 0) != 0 ? 1u : 0u;
+#pragma unroll
+                for (int b = 0; b < PF_RB; b++)
+#pragma unroll
+                    for (int kk = 0; kk < 4; kk++)  // +32 B of K per step: +2 in the descriptor's address field
+                        umma_f16_ta_pair_warp(td + PF_TILE_N * b, ta + 32 * b + 8 * kk, bdesc + (uint64_t)(2 * kk),
+                                              idesc, (acc | kk) ? 1u : 0u);
+                umma_commit_pair_warp(&a_empty[sa]);
+                umma_commit_pair_warp(&b_empty[sbq]);
             }
-            tmem_fence_after();
-            const uint32_t b0 = umma_smem_u32(sb + sbq * PF_ATOM);
-#pragma unroll
-            for (int b = 0; b < PF_RB; b++)
-#pragma unroll
-                for (int kk = 0; kk < 4; kk++)
-                    umma_f16_ta_warp(tmem + PF_TILE_N * b, tmem_a + 64 * sa + 32 * b + 8 * kk,
-                                     umma_desc_sw128(b0 + 32 * kk), idesc, (i | kk) != 0);
-            umma_commit_warp(&a_empty[sa]);
-            umma_commit_warp(&b_empty[sbq]);
-        }
-        umma_commit_warp(&acc_full);
-        if (!ok) {
-            // the MMAs already issued finish before tensor memory is freed
-            if (lane == 0) atomicExch(plan.error, PF_ERR_TIMEOUT);
-            tc_wait_warp(&acc_full, 0);
+            umma_commit_pair_warp(&acc_full);
+            if (!ok) {
+                // the MMAs already issued finish before tensor memory is freed
+                if (lane == 0) atomicExch(plan.error, PF_ERR_TIMEOUT);
+                tc_wait_warp(&acc_full, 0);
+            }
         }
     } else {
         // dequantization: warp (q = warp % 4, g) owns tensor-memory lanes
-        // 32 q .. 32 q + 31 (A rows; lane = row) of both blocks, and atom g
-        // of every super-block
+        // 32 q .. 32 q + 31 (A rows; lane = row) of both blocks, and atoms
+        // i = g, g + PF_NSA, g + 2 PF_NSA, ... (K order), all of them through
+        // A stage g.  A stage has one producer group that takes its uses in
+        // order, so a parity wait on it is never a whole phase early; every
+        // group meets every super-block (4 consecutive atoms cover all
+        // residues mod PF_NSA), in order, so the raw-stage waits are exact too.
         const int q = warp & 3, g = (warp - PF_DQ_WARP0) >> 2, row = 32 * q + lane;
         int rraw = row;  // raw tile row (inside a block) holding A row `row`
         if (MODE == 0) {
@@ -454,24 +494,25 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
             rraw = h * 64 + 16 * q + i;                   // gate rows first, then up rows
         }
         const uint32_t tlane = (uint32_t)(32 * q) << 16;
-        for (int sbk = 0; sbk < NB && ok; sbk++) {
+        for (int i = g, use = 0; i < n_atoms && ok; i += PF_NSA, use++) {
+            const int sbk = i >> 2, ga = i & 3;  // super-block, atom inside it
             const int rs = sbk % RAW_NS;
             if (!tc_wait_warp(&raw_full[rs], (sbk / RAW_NS) & 1)) { ok = false; break; }
             const uint8_t *r = sr + rs * RAW;
-            // atom g of this lane's rows in both blocks, dequantized into
+            // atom ga of this lane's rows in both blocks, dequantized into
             // registers before the tensor-memory stage is waited for
             uint32_t v[PF_RB][32];
 #pragma unroll
             for (int b = 0; b < PF_RB; b++) {
                 uint32_t c[8];
                 if constexpr (MODE == 2) {
-                    // chunk t: ql words s4 = 0..3 and qh words 0, 1 of half g / 2
+                    // chunk t: ql words s4 = 0..3 and qh words 0, 1 of half ga / 2
                     // (bytes 0-23 or 24-47 of the chunk: a 16-byte and an 8-byte load)
                     uint32_t w[24];
 #pragma unroll
                     for (int t = 0; t < 4; t++) {
                         const uint8_t *cp = r + b * QB + rraw * PF_Q6_ROW + 48 * t;
-                        if (g < 2) {
+                        if (ga < 2) {
                             const uint4 x = *reinterpret_cast<const uint4 *>(cp);
                             const uint2 y = *reinterpret_cast<const uint2 *>(cp + 16);
                             w[6 * t] = x.x; w[6 * t + 1] = x.y; w[6 * t + 2] = x.z; w[6 * t + 3] = x.w;
@@ -483,12 +524,12 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
                             w[6 * t + 4] = y.z; w[6 * t + 5] = y.w;
                         }
                     }
-                    const uint32_t sc4 = reinterpret_cast<const uint32_t *>(r + PF_RB * QB + b * 2048 + rraw * 16)[g];
+                    const uint32_t sc4 = reinterpret_cast<const uint32_t *>(r + PF_RB * QB + b * 2048 + rraw * 16)[ga];
                     const float d6 = __half2float(reinterpret_cast<const __half *>(sd + b * 256 * nbp)[rraw * nbp + sbk]);
                     pf_q6_consts(d6, sc4, c);
-                    if (g == 0) pf_deq_q6<0>(w, c, v[b]);
-                    else if (g == 1) pf_deq_q6<1>(w, c, v[b]);
-                    else if (g == 2) pf_deq_q6<2>(w, c, v[b]);
+                    if (ga == 0) pf_deq_q6<0>(w, c, v[b]);
+                    else if (ga == 1) pf_deq_q6<1>(w, c, v[b]);
+                    else if (ga == 2) pf_deq_q6<2>(w, c, v[b]);
                     else pf_deq_q6<3>(w, c, v[b]);
                 } else {
                     const uint8_t *blk = r + b * QB + rraw * MOE_Q4K_BYTES;
@@ -496,11 +537,11 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
                     uint32_t w[8];
 #pragma unroll
                     for (int t = 0; t < 4; t++) {
-                        const uint2 x = *reinterpret_cast<const uint2 *>(blk + 16 + 32 * t + 8 * g);
+                        const uint2 x = *reinterpret_cast<const uint2 *>(blk + 16 + 32 * t + 8 * ga);
                         w[2 * t] = x.x;
                         w[2 * t + 1] = x.y;
                     }
-                    pf_q4_consts(hd, g, c);
+                    pf_q4_consts(hd, ga, c);
                     pf_deq_q4(w, pf_u2h(__byte_perm(hd.x, 0, 0x1010)), c, v[b]);  // d in both halves
                 }
             }
@@ -509,15 +550,14 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
             fence_async_smem();
             __syncwarp();
             if (lane == 0) tc_arrive(&raw_empty[rs]);
-            const int i = 4 * sbk + g, sa = i % PF_NSA;
-            if (!tc_wait_warp(&a_empty[sa], ((i / PF_NSA) & 1) ^ 1)) { ok = false; break; }
+            if (!tc_wait_warp(&a_empty[g], (use & 1) ^ 1)) { ok = false; break; }
             tmem_fence_after();
 #pragma unroll
-            for (int b = 0; b < PF_RB; b++) tmem_st32(tmem_a + tlane + 64 * sa + 32 * b, v[b]);
+            for (int b = 0; b < PF_RB; b++) tmem_st32(tmem_a + tlane + 64 * g + 32 * b, v[b]);
             tmem_wait_st();
             tmem_fence_before();
             __syncwarp();
-            if (lane == 0) tc_arrive(&a_full[sa]);
+            if (lane == 0) tc_arrive_cluster(cluster_map(&a_full[g], 0));  // the leader's barrier
         }
         // epilogue: this warp reads tensor-memory lanes 32 (warp % 4) .. + 31
         // of both accumulators
@@ -528,8 +568,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
 #pragma unroll 1
             for (int b = 0; b < PF_RB; b++) {
                 const int blk = PF_RB * rg + b;
-                for (int c = 16 * sub; c < PF_TILE_N; c += 16 * (PF_DQ_WARPS / 4)) {
-                    if (c >= ntile) break;
+                for (int c = 16 * sub; c < ntile; c += 16 * (PF_DQ_WARPS / 4)) {
                     float v[16];
                     tmem_ld16(tmem + PF_TILE_N * b + ((uint32_t)(32 * q) << 16) + c, v);
                     if (MODE == 0) {
@@ -556,9 +595,12 @@ __global__ void __launch_bounds__(PF_THREADS, 1)
             atomicExch(plan.error, PF_ERR_TIMEOUT);
         }
     }
+    // teardown: every thread of both CTAs arrives (no access from the other CTA
+    // after this), then each CTA frees its tensor memory
     tmem_fence_before();
-    __syncthreads();
-    if (warp == 1) tmem_free(tmem, 512);
+    __syncwarp();
+    cluster_sync_all();
+    if (warp == 1) tmem_free_pair(tmem, 512);
 }
 
 // ===========================================================================
@@ -929,7 +971,7 @@ __global__ void __launch_bounds__(256) k_pfe_final(MoeDims d, MoePlan plan, cons
 // ===========================================================================
 static size_t pf_smem(int mode, int nbp) {
     const size_t raw = mode == 2 ? PF_RAW_Q6 : PF_RAW_Q4;
-    return 1024 + (size_t)PF_NSB * PF_ATOM + (mode == 2 ? PF_RAW_NS_Q6 : PF_RAW_NS_Q4) * raw +
+    return 1024 + (size_t)PF_NSB * PF_BST + (mode == 2 ? PF_RAW_NS_Q6 : PF_RAW_NS_Q4) * raw +
            (mode == 2 ? PF_RB * 128 * 2 * (size_t)nbp : 0);
 }
 
@@ -1014,8 +1056,8 @@ int moe_prefill_alloc(MoePrefillWs &ws, const MoeDims &d, int T, int world, int 
         moe_prefill_free(ws);
         return -1;
     }
-    if (moe_make_map_f16_sw128(&ws.tm_xg, ws.xg, d.H, P, 64, 32) ||
-        moe_make_map_f16_sw128(&ws.tm_act, ws.act, d.I, P, 64, 32) ||
+    if (moe_make_map_f16_sw128(&ws.tm_xg, ws.xg, d.H, P, 64, 16) ||
+        moe_make_map_f16_sw128(&ws.tm_act, ws.act, d.I, P, 64, 16) ||
         moe_make_map_f16_sw128(&ws.tm_wh, ws.wh, d.H, Ep, 64, 128) ||
         moe_make_map_f16_sw128(&ws.tm_wl, ws.wl, d.H, Ep, 64, 128) ||
         moe_make_map_f16_sw128(&ws.tm_xh, ws.xh, d.H, cap, 64, 128) ||

@@ -270,3 +270,85 @@ __device__ __forceinline__ void tc_tma2(void *dst, const CUtensorMap *m, int x, 
         "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(umma_smem_u32(bar))
         : "memory");
 }
+
+// ---------------------------------------------------------------------------
+// CTA pairs (cta_group::2).  Two CTAs of a 2-CTA cluster run on the two SMs
+// of one TPC; one tcgen05.mma.cta_group::2 issued by the even CTA (the
+// leader) computes M = 256 rows: A rows 0-127 from the leader's tensor
+// memory and 128-255 from the peer's (the same column address in both), B
+// columns 0 .. N/2 - 1 from the leader's shared memory and N/2 .. N - 1 from
+// the peer's (the same shared address in both), and D rows 0-127 / 128-255
+// into the leader's / the peer's tensor memory, all N columns in each.  Every
+// tcgen05 instruction of such a kernel uses cta_group::2.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+    return r;
+}
+// every thread of both CTAs; orders the mbarrier inits and the tensor-memory
+// allocation of each CTA before any access from the other one
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+// the shared::cluster address of the same variable in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t cluster_map(const void *p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(umma_smem_u32(p)), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_ld_u32(uint32_t cluster_addr) {
+    uint32_t v;
+    asm volatile("ld.shared::cluster.u32 %0, [%1];\n" : "=r"(v) : "r"(cluster_addr) : "memory");
+    return v;
+}
+// one arrival on an mbarrier of either CTA of the pair (cluster address).  The
+// default (CTA-scope) semantics: a cluster-scope release here costs a memory
+// barrier per arrival.  Tensor-memory stores are ordered for the MMA that the
+// other CTA issues by tcgen05.wait::st + tcgen05.fence::before_thread_sync
+// before the arrival and tcgen05.fence::after_thread_sync after the wait.
+__device__ __forceinline__ void tc_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];\n" ::"r"(cluster_addr) : "memory");
+}
+// 2D tile load into this CTA's shared memory whose completion (complete_tx)
+// is signalled on an mbarrier of either CTA of the pair (cluster address)
+__device__ __forceinline__ void tc_tma2_pair(void *dst, const CUtensorMap *m, int x, int y, uint32_t bar_cluster) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];\n" ::"r"(umma_smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(x), "r"(y), "r"(bar_cluster)
+        : "memory");
+}
+// tensor memory of the pair: the same warp index in both CTAs allocates / frees
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(umma_smem_u32(dst)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ void tmem_free_pair(uint32_t base, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;\n" ::"r"(base), "r"(ncols) : "memory");
+}
+// leader only, warp-wide form (see umma_f16_ta_warp): D (+)= A[tmem] * B[smem]^T over the pair
+__device__ __forceinline__ void umma_f16_ta_pair_warp(uint32_t tmem_d, uint32_t tmem_a, uint64_t desc_b,
+                                                      uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "@e tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}\n" ::"r"(
+            tmem_d),
+        "r"(tmem_a), "l"(desc_b), "r"(idesc), "r"(accumulate), "r"(0u)
+        : "memory");
+}
+// leader only, elected lane: one arrival on `bar` (the same shared address)
+// in both CTAs once every pair MMA issued so far has completed
+__device__ __forceinline__ void umma_commit_pair_warp(uint64_t *bar) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t"
+        "elect.sync _|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n\t}\n" ::
+            "r"(umma_smem_u32(bar)),
+        "h"((uint16_t)3)
+        : "memory");
+}

@@ -223,7 +223,9 @@ int moe_forward_stack(moe_ctx *ctx, int first_layer, int n_layers, float *hidden
  * products run as tensor-core GEMMs (tcgen05): the router on fp16 hi/lo
  * splits to fp32 accuracy, the experts over fp16 copies of the dequantized
  * weights and of the activations with fp32 accumulation, so results agree
- * with moe_forward to about 1e-3 relative, not bit for bit.  With expert
+ * with moe_forward to about 1e-3 relative, not bit for bit.  Shapes: hidden
+ * a multiple of 512, intermediate a multiple of 256 (MOE_ERR_ARG otherwise).
+ * With expert
  * parallelism (world_size > 1) every rank calls with its own tokens (0
  * allowed); the token rows go to the ranks that own their experts and the
  * partial sums come back (NCCL), as in moe_forward.  The first call (and any

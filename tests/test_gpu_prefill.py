@@ -23,6 +23,8 @@ def selftest_lib():
     lib = C.CDLL(so)
     lib.umma_selftest.restype = C.c_int
     lib.umma_selftest.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
+    lib.umma_selftest_pair.restype = C.c_int
+    lib.umma_selftest_pair.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int]
     return lib
 
 
@@ -42,6 +44,26 @@ def test_umma_f16_gemm_selftest(selftest_lib, a_in_tmem):
     assert err < 1e-5, err
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("N,dcol,acol", [(128, 0, 256), (96, 0, 384), (160, 0, 384), (160, 160, 384),
+                                         (96, 160, 320)])
+def test_umma_pair_selftest(selftest_lib, N, dcol, acol):
+    """The CTA-pair MMA (cta_group::2, M = 256, A in tensor memory): each CTA
+    holds 128 rows of A and N/2 rows of B and gets its 128 rows of C over all
+    N columns; accumulator and A at the column offsets the prefill GEMM uses."""
+    import torch
+    g = torch.Generator().manual_seed(5)
+    A = torch.randn(256, 256, generator=g).half()
+    B = torch.randn(N, 256, generator=g).half()
+    dA, dB = A.cuda(), B.cuda()
+    dC = torch.zeros(256, N, device="cuda")
+    rc = selftest_lib.umma_selftest_pair(dA.data_ptr(), dB.data_ptr(), dC.data_ptr(), N, dcol, acol)
+    assert rc == 0, rc
+    ref = A.double() @ B.double().T
+    err = float((dC.cpu().double() - ref).abs().max() / ref.abs().max())
+    assert err < 1e-5, err
+
+
 PREFILL_TOL = 2e-3   # north-star bound; fp16 weights and activations, fp32 accumulation
 
 
@@ -53,7 +75,7 @@ def test_prefill_matches_oracle(cuda_lib, oracle, down_type):
     m = cuda_lib.MoE(cfg)
     m.init_layer_synthetic(0, seed=11, down_type=down_type)
     router, bias = router_of(oracle, 11, 0, cfg)
-    T = 300   # the shared expert spans three 128-pair tiles
+    T = 300   # the shared expert spans two tiles of 150 pairs
     h = oracle.normal(4, oracle.stream(0, 0, oracle.KIND_ACT), T * cfg.hidden, 1.0).reshape(T, cfg.hidden)
     out, idx, w = m.prefill(0, h)
     logits = (h.astype(np.float64) @ router.astype(np.float64).T).astype(np.float32)
@@ -126,8 +148,8 @@ def _prefill_sample(idx, n_experts, rng, per_group=16):
 def test_prefill_full_size_matches_oracle(cuda_lib, oracle, down_type, T):
     """Config 5 at its own shape: DeepSeek-V3 layer (hidden 7168, 256 + 1
     experts, Q4_K gate/up, Q6_K or Q4_K down), 4096 (2048) tokens, so that
-    experts average 128 (64) pairs and the busy ones fill whole 128-pair
-    tcgen05 tiles, the shared expert 32 (16) of them.  The routing of every
+    experts average 128 (64) pairs and most fill one tile of up to 160 pairs
+    (pair MMA N = 160), the shared expert 26 (13) tiles.  The routing of every
     token against fp64 logits; the outputs of a sample of rows (the hottest
     expert's tokens, the coldest experts' tokens, tile edges, random rows)
     against the oracle on the same routing."""
@@ -141,7 +163,7 @@ def test_prefill_full_size_matches_oracle(cuda_lib, oracle, down_type, T):
     logits = (h.astype(np.float64) @ router.astype(np.float64).T).astype(np.float32)
     check_routing(oracle, cfg, logits, bias, idx, w)
     rows, hot, n_hot = _prefill_sample(idx, cfg.n_experts, np.random.default_rng(5))
-    assert n_hot >= (128 if T >= 4096 else 64)  # the busiest expert fills (or half fills) a 128-pair tile
+    assert n_hot >= (128 if T >= 4096 else 64)  # the busiest expert fills (or half fills) a tile
     experts = {e: m.read_expert(0, e) for e in sorted(set(idx[rows].reshape(-1).tolist())) + [cfg.n_experts]}
     ref = oracle.moe_layer_given(oracle_cfg(cfg, down_type), experts, h[rows], idx[rows], w[rows])
     e = rel_err(out[rows], ref)
