@@ -199,6 +199,16 @@ static void drop_graphs(moe_ctx *c) {
     c->seen.clear();
 }
 
+// The context's kernels run on a non-blocking stream (and on callers'
+// streams), which the legacy default stream does not order against: clears
+// and uploads go on the context stream, and the setup paths below wait for
+// them before anything else can be launched.
+static cudaError_t zero_async(moe_ctx *c, void *p, size_t bytes) { return cudaMemsetAsync(p, 0, bytes, c->stream); }
+static cudaError_t upload_sync(moe_ctx *c, void *dst, const void *src, size_t bytes) {
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, c->stream);
+    return e == cudaSuccess ? cudaStreamSynchronize(c->stream) : e;
+}
+
 static int ctx_alloc(moe_ctx *c) {
     const int T = c->max_tok, R = c->max_rows, H = c->d.H, I = c->d.I, E = c->d.E, K = c->d.K;
     c->max_pairs = R * K + T;
@@ -206,7 +216,7 @@ static int ctx_alloc(moe_ctx *c) {
     CK(dmalloc(&c->part, (size_t)c->n_split * T * E));
     CK(dmalloc(&c->logits, (size_t)T * E));
     CK(dmalloc(&c->rl_counters, (size_t)(E + 31) / 32));
-    CK(cudaMemset(c->rl_counters, 0, sizeof(int) * ((E + 31) / 32 + 64)));
+    CK(zero_async(c, c->rl_counters, sizeof(int) * ((E + 31) / 32 + 64)));
     CK(dmalloc(&c->d_in, (size_t)T * H));
     CK(dmalloc(&c->d_out, (size_t)T * H));
     CK(dmalloc(&c->h_post, (size_t)T * H));
@@ -217,7 +227,7 @@ static int ctx_alloc(moe_ctx *c) {
     CK(dmalloc(&c->bias_tmp, (size_t)E));
     const int RT = (c->world > 1 ? R + T : R);  // EP: received rows + local rows
     CK(dmalloc(&c->xop, (size_t)RT * opx_row(H)));
-    CK(cudaMemset(c->xop, 0, (size_t)RT * opx_row(H)));
+    CK(zero_async(c, c->xop, (size_t)RT * opx_row(H)));
     const int P = c->max_pairs;
     CK(dmalloc(&c->plan.counts, MOE_PLAN_COUNTS));
     CK(dmalloc(&c->plan.pair_expert, P));
@@ -229,16 +239,16 @@ static int ctx_alloc(moe_ctx *c) {
     CK(dmalloc(&c->plan.chunk_order, P));
     CK(dmalloc(&c->plan.slot_pair, (size_t)RT * (K + 1)));
     CK(dmalloc(&c->plan.error, 1));
-    CK(cudaMemset(c->plan.error, 0, sizeof(int)));
-    CK(cudaMemset(c->plan.counts, 0, MOE_PLAN_COUNTS * sizeof(int)));
+    CK(zero_async(c, c->plan.error, sizeof(int)));
+    CK(zero_async(c, c->plan.counts, MOE_PLAN_COUNTS * sizeof(int)));
     CK(dmalloc(&c->counter, 1));
-    CK(cudaMemset(c->counter, 0, sizeof(int)));
+    CK(zero_async(c, c->counter, sizeof(int)));
     CK(dmalloc(&c->act, (size_t)P * I));
     CK(dmalloc(&c->dop, (size_t)P * opw_bytes(I)));
-    CK(cudaMemset(c->dop, 0, (size_t)P * opw_bytes(I)));
+    CK(zero_async(c, c->dop, (size_t)P * opw_bytes(I)));
     if (c->d.tc) {
         CK(dmalloc(&c->xtc, (size_t)P * opw_bytes(H)));
-        CK(cudaMemset(c->xtc, 0, (size_t)P * opw_bytes(H)));
+        CK(zero_async(c, c->xtc, (size_t)P * opw_bytes(H)));
         if (moe_make_map_opw(&c->tm_xtc, c->xtc, H, (uint64_t)P) || moe_make_map_opw(&c->tm_dop, c->dop, I, (uint64_t)P))
             return fail(c, MOE_ERR_CUDA, "tensor maps of the tcgen05 operand rows");
     }
@@ -255,6 +265,7 @@ static int ctx_alloc(moe_ctx *c) {
         CK(dmalloc(&c->rows_partial, rows * H));
         CK(dmalloc(&c->tok_slot, (size_t)T * c->world));
     }
+    CK(cudaStreamSynchronize(c->stream));  // the clears above, before any launch on any stream
     return MOE_OK;
 }
 
@@ -273,17 +284,18 @@ static int ep_p2p_init(moe_ctx *c) {
     c->mb_y = c->mb_meta + al(2 * R * mw * sizeof(int));
     const size_t total = c->mb_y + 2 * R * H * sizeof(float);
     CK(cudaMalloc((void **)&c->mbox, total));
-    CK(cudaMemset(c->mbox, 0, total));
+    CK(zero_async(c, c->mbox, total));
     CK(cudaMalloc((void **)&c->ep_done, 3 * sizeof(int)));
-    CK(cudaMemset(c->ep_done, 0, 3 * sizeof(int)));
+    CK(zero_async(c, c->ep_done, 3 * sizeof(int)));
     CK(cudaMalloc((void **)&c->d_seq, sizeof(unsigned long long)));
-    CK(cudaMemset(c->d_seq, 0, sizeof(unsigned long long)));
+    CK(zero_async(c, c->d_seq, sizeof(unsigned long long)));
+    CK(cudaStreamSynchronize(c->stream));  // cleared before a peer can map the mailbox
     CK(cudaMalloc((void **)&c->d_peers, N * sizeof(uint8_t *)));
     cudaIpcMemHandle_t mine;
     CK(cudaIpcGetMemHandle(&mine, c->mbox));
     uint8_t *dh = nullptr;
     CK(cudaMalloc((void **)&dh, (N + 1) * sizeof(cudaIpcMemHandle_t)));
-    CK(cudaMemcpy(dh, &mine, sizeof(mine), cudaMemcpyHostToDevice));
+    CK(upload_sync(c, dh, &mine, sizeof(mine)));
     NK(moe_nccl()->GroupStart());
     for (int p = 0; p < N; p++) {
         NK(moe_nccl()->Send(dh, sizeof(mine), ncclUint8, p, c->comm, c->stream));
@@ -310,7 +322,7 @@ static int ep_p2p_init(moe_ctx *c) {
     int *dflag = nullptr;
     CK(cudaMalloc((void **)&dflag, (N + 1) * sizeof(int)));
     const int mine_ok = ok ? 1 : 0;
-    CK(cudaMemcpy(dflag, &mine_ok, sizeof(int), cudaMemcpyHostToDevice));
+    CK(upload_sync(c, dflag, &mine_ok, sizeof(int)));
     NK(moe_nccl()->GroupStart());
     for (int p = 0; p < N; p++) {
         NK(moe_nccl()->Send(dflag, 1, ncclInt32, p, c->comm, c->stream));
@@ -330,7 +342,7 @@ static int ep_p2p_init(moe_ctx *c) {
         c->mbox = nullptr;
         return MOE_OK;  // the NCCL send/recv exchange
     }
-    CK(cudaMemcpy(c->d_peers, c->peer_map.data(), N * sizeof(uint8_t *), cudaMemcpyHostToDevice));
+    CK(upload_sync(c, c->d_peers, c->peer_map.data(), N * sizeof(uint8_t *)));
     c->p2p = true;
     return MOE_OK;
 }
@@ -648,7 +660,7 @@ int moe_add_router_bias(moe_ctx *c, int layer, const float *extra) {
     std::vector<float> b(c->d.E);
     CK(cudaMemcpy(b.data(), c->layers[layer].bias, sizeof(float) * c->d.E, cudaMemcpyDeviceToHost));
     for (int e = 0; e < c->d.E; e++) b[e] += extra[e];
-    CK(cudaMemcpy(c->layers[layer].bias, b.data(), sizeof(float) * c->d.E, cudaMemcpyHostToDevice));
+    CK(upload_sync(c, c->layers[layer].bias, b.data(), sizeof(float) * c->d.E));
     return MOE_OK;
 }
 
@@ -665,7 +677,7 @@ int moe_set_logit_bias(moe_ctx *c, int layer, const float *lb) {
         return MOE_OK;
     }
     if (!L.logit_bias) CK(cudaMalloc((void **)&L.logit_bias, sizeof(float) * c->d.E));
-    CK(cudaMemcpy(L.logit_bias, lb, sizeof(float) * c->d.E, cudaMemcpyHostToDevice));
+    CK(upload_sync(c, L.logit_bias, lb, sizeof(float) * c->d.E));
     return MOE_OK;
 }
 
@@ -676,7 +688,7 @@ int moe_set_norm_weight(moe_ctx *c, int layer, const float *w) {
     DeviceScope ds(c->device);
     MoeLayerDev &L = c->layers[layer];
     if (!L.norm) CK(cudaMalloc((void **)&L.norm, sizeof(float) * c->d.H));
-    CK(cudaMemcpy(L.norm, w, sizeof(float) * c->d.H, cudaMemcpyHostToDevice));
+    CK(upload_sync(c, L.norm, w, sizeof(float) * c->d.H));
     return MOE_OK;
 }
 
@@ -1081,7 +1093,9 @@ static int take_device_error(moe_ctx *c) {
     for (int i = 0; i < 2; i++) {
         const int e = err[i];
         if (!e) continue;
-        cudaMemset(i == 0 ? c->plan.error : c->pf.plan.error, 0, sizeof(int));
+        // cleared before the next call's kernels (on any stream) can set it again
+        if (zero_async(c, i == 0 ? c->plan.error : c->pf.plan.error, sizeof(int)) == cudaSuccess)
+            cudaStreamSynchronize(c->stream);
         if (e == EP_ERR_TIMEOUT) {
             c->ep_failed = true;
             return fail(c, MOE_ERR_TIMEOUT, "peer exchange wait timed out (a peer rank stopped calling)");

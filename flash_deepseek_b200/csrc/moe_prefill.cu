@@ -316,60 +316,83 @@ __device__ __forceinline__ void pf_deq_q6(const uint32_t (&q)[24], const uint32_
 
 // ===========================================================================
 // GEMM.  MODE 0: gate/up (Q4_K) -> act (fp16, SwiGLU); 1: down Q4_K -> eo;
-// 2: down Q6_K -> eo.  A 2-CTA cluster (a CTA pair on one TPC) works on one
-// tile (expert, <= PF_TILE_N pairs): blockIdx.x = row group (PF_RB row
-// blocks of 128 accumulator rows per CTA; MODE 0: a block is 64 gate rows +
-// the matching 64 up rows; the pair holds two consecutive row groups),
-// blockIdx.y = tile.  Each pair MMA (M = 256: block b of both CTAs) takes the
-// first half of the tile's pairs from the leader's activation stage and the
-// second half from the peer's, so each SM streams half of the tile's
-// activations per K step, and each stage feeds PF_RB pair MMAs.  The CTAs
-// resident at one time work on a few tiles, so each tile's activation slices
-// are read from DRAM once and then hit in L2.
+// 2: down Q6_K -> eo.  Persistent 2-CTA clusters (a CTA pair on one TPC):
+// cluster c takes the work items c, c + clusters, ... in order; item =
+// tile x pair row group (PR per tile), tile = (expert, <= PF_TILE_N pairs).
+// In a pair, CTA r holds row group 2 x pair row group + r (PF_RB row blocks
+// of 128 accumulator rows; MODE 0: a block is 64 gate rows + the matching 64
+// up rows).  Each pair MMA (M = 256: block b of both CTAs) takes the first
+// half of the tile's pairs from the leader's activation stage and the second
+// half from the peer's, so each SM streams half of the tile's activations per
+// K step, and each stage feeds PF_RB pair MMAs.  The clusters resident at one
+// time work on neighbouring items (a few tiles), so each tile's activation
+// slices are read from DRAM once and then hit in L2.  Every role keeps its
+// ring positions across items: the weight and activation producers run ahead
+// into the next item while the last MMAs and the epilogue of the current one
+// run, and each dequantizing group writes its first A stage of the next item
+// before it reads back the previous item's accumulator, so the MMAs restart
+// as soon as the accumulator has been read (acc_empty).
 // ===========================================================================
+struct PfItem {
+    int e, p0, ntile, slot, rg, npair;
+};
+
+// the item's tile and rows; false for a tile of the other down type (the
+// shared and the routed experts may differ), which every role skips alike
+template <int MODE>
+__device__ __forceinline__ bool pf_item(const MoeDims &d, const MoeLayerDev &L, const MoePlan &plan, int item, int PR,
+                                        uint32_t rank, PfItem &it) {
+    const int tile = item / PR;
+    it.e = plan.chunk_expert[tile];
+    if (MODE > 0 && ((it.e == d.E) ? L.sh_down_type : L.down_type) != (MODE == 2 ? MOE_TYPE_Q6_K : MOE_TYPE_Q4_K))
+        return false;
+    it.p0 = plan.chunk_pair0[tile];
+    it.ntile = plan.chunk_ntok[tile];
+    it.slot = it.e == d.E ? L.n_local : it.e - L.e0;
+    it.rg = 2 * (item % PR) + (int)rank;
+    it.npair = (it.ntile + 31) & ~31;  // pair MMA N (a multiple of 32); N / 2 pairs per CTA
+    return true;
+}
+
+// uses of A stage s per item: the atoms i < n_atoms with i % PF_NSA == s
+__device__ __forceinline__ int pf_stage_uses(int n_atoms, int s) { return (n_atoms - s + PF_NSA - 1) / PF_NSA; }
+
 template <int MODE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
     k_prefill_gemm(MoeDims d, const __grid_constant__ MoeLayerDev L, MoePlan plan,
-                   const __grid_constant__ CUtensorMap tmB, __half *__restrict__ act, float *__restrict__ eo) {
+                   const __grid_constant__ CUtensorMap tmB, int PR, __half *__restrict__ act, float *__restrict__ eo) {
     constexpr int RAW = MODE == 2 ? PF_RAW_Q6 : PF_RAW_Q4;
     constexpr int RAW_NS = MODE == 2 ? PF_RAW_NS_Q6 : PF_RAW_NS_Q4;
     constexpr int QB = MODE == 2 ? 128 * PF_Q6_ROW : 128 * 144;  // one block's Q bytes in a raw stage
     extern __shared__ uint8_t pf_raw[];
     uint8_t *sm = pf_raw + ((1024u - (umma_smem_u32(pf_raw) & 1023u)) & 1023u);
     uint8_t *sb = sm, *sr = sm + PF_NSB * PF_BST;
-    uint8_t *sd = sr + RAW_NS * RAW;  // Q6_K d planes of the blocks (PF_RB x 128 rows x 2 nb_pad bytes)
+    // Q6_K d planes of the blocks (PF_RB x 128 rows x 2 nb_pad bytes), two
+    // buffers by item parity: the producer refills one only after the raw
+    // ring shows every warp past the item that read it (NB >= RAW_NS)
+    uint8_t *sd = sr + RAW_NS * RAW;
     __shared__ __align__(8) uint64_t raw_full[PF_RAW_NS_MAX], raw_empty[PF_RAW_NS_MAX], a_full[PF_NSA], a_empty[PF_NSA],
-        b_full[PF_NSB], b_empty[PF_NSB], acc_full;
+        b_full[PF_NSB], b_empty[PF_NSB], acc_full, acc_empty;
     __shared__ uint32_t tmem_base;
-    __shared__ int s_skip;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int tile = blockIdx.y, rg = blockIdx.x;
     const uint32_t rank = cluster_ctarank();  // 0: the leader, which issues the pair MMAs
-    if (tid == 0) {
-        int skip = tile >= plan.counts[1];
-        if (!skip && MODE > 0) {
-            const int e = plan.chunk_expert[tile];
-            skip = ((e == d.E) ? L.sh_down_type : L.down_type) != (MODE == 2 ? MOE_TYPE_Q6_K : MOE_TYPE_Q4_K);
-        }
-        s_skip = skip;
-    }
-    __syncthreads();
-    if (s_skip) return;  // both CTAs of the pair read the same tile: both leave here, or neither
-    const int e = plan.chunk_expert[tile], p0 = plan.chunk_pair0[tile], ntile = plan.chunk_ntok[tile];
-    const int slot = e == d.E ? L.n_local : e - L.e0;
+    const int cl = blockIdx.x >> 1, ncl = gridDim.x >> 1;
     const int K = MODE == 0 ? d.H : d.I, NB = K / MOE_QK, n_atoms = 4 * NB;
-    const int nbp = q6r_nb_pad(NB);
-    const int npair = (ntile + 31) & ~31, nhalf = npair / 2;  // pair MMA N (a multiple of 32); pairs per CTA
+    const int nbp = q6r_nb_pad(NB), dpl = PF_RB * 256 * nbp;  // bytes of one d-plane buffer
+    const int n_items = plan.counts[1] * PR;                   // the same in both CTAs
     if (tid == 0) {
-        // raw_empty: 4 atoms x 4 lane-quarter warps per super-block
+        // raw_empty: 4 atoms x 4 lane-quarter warps per super-block.  a_full /
+        // b_full / acc_empty are used in the leader: 4 dequantizing warps of
+        // each CTA; the leader's expect_tx (both CTAs' copies complete on it);
+        // every dequantizing warp of both CTAs.  The empty barriers and
+        // acc_full of both CTAs receive the leader's commits (tcgen05.commit
+        // to both).
         for (int i = 0; i < RAW_NS; i++) { tc_mbar_init(&raw_full[i], 1); tc_mbar_init(&raw_empty[i], 16); }
-        // a_full / b_full are used in the leader: 4 dequantizing warps of each CTA; the
-        // leader's expect_tx (both CTAs' copies complete on it).  The empty barriers and
-        // acc_full of both CTAs receive the leader's commits (tcgen05.commit to both).
         for (int i = 0; i < PF_NSA; i++) { tc_mbar_init(&a_full[i], 8); tc_mbar_init(&a_empty[i], 1); }
         for (int i = 0; i < PF_NSB; i++) { tc_mbar_init(&b_full[i], 1); tc_mbar_init(&b_empty[i], 1); }
         tc_mbar_init(&acc_full, 1);
+        tc_mbar_init(&acc_empty, 2 * PF_DQ_WARPS);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
     }
@@ -391,59 +414,68 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
         // per stage, RAW_NS ahead (the warp loops together, one elected lane
         // issues the copies)
         const uint32_t leader = elect_one();
-        int issued = 0;
-        for (int sbk = 0; sbk < NB && ok; sbk++) {
-            const int rs = sbk % RAW_NS;
-            if (!tc_wait_warp(&raw_empty[rs], ((sbk / RAW_NS) & 1) ^ 1)) { ok = false; break; }
-            uint8_t *r = sr + rs * RAW;
-            if (leader) {
-                tc_expect(&raw_full[rs], RAW + (MODE == 2 && sbk == 0 ? PF_RB * 128 * 2 * nbp : 0));
+        int gs = 0, jn = 0;  // super-blocks issued, items taken
+        for (int item = cl; item < n_items && ok; item += ncl) {
+            PfItem it;
+            if (!pf_item<MODE>(d, L, plan, item, PR, rank, it)) continue;
+            for (int sbk = 0; sbk < NB; sbk++, gs++) {
+                const int rs = gs % RAW_NS;
+                if (!tc_wait_warp(&raw_empty[rs], ((gs / RAW_NS) & 1) ^ 1)) { ok = false; break; }
+                uint8_t *r = sr + rs * RAW;
+                if (leader) {
+                    tc_expect(&raw_full[rs], RAW + (MODE == 2 && sbk == 0 ? dpl : 0));
 #pragma unroll
-                for (int b = 0; b < PF_RB; b++) {
-                    const int blk = PF_RB * rg + b;
-                    if (MODE == 0) {
-                        tc_tma3(r + b * QB, &L.tm_gu, sbk * MOE_Q4K_BYTES, blk * 64, slot, &raw_full[rs]);
-                        tc_tma3(r + b * QB + 64 * MOE_Q4K_BYTES, &L.tm_gu, sbk * MOE_Q4K_BYTES, d.I + blk * 64, slot,
-                                &raw_full[rs]);
-                    } else if (MODE == 1) {
-                        tc_tma3(r + b * QB, &L.tm_d4, sbk * MOE_Q4K_BYTES, blk * 128, slot, &raw_full[rs]);
-                    } else {
-                        tc_tma3(r + b * QB, &L.tm_pf6q, sbk * 192, blk * 128, slot, &raw_full[rs]);
-                        tc_tma3(r + PF_RB * QB + b * 2048, &L.tm_d6s, sbk * 16, blk * 128, slot, &raw_full[rs]);
-                        if (sbk == 0) tc_tma3(sd + b * 256 * nbp, &L.tm_d6d, 0, blk * 128, slot, &raw_full[rs]);
+                    for (int b = 0; b < PF_RB; b++) {
+                        const int blk = PF_RB * it.rg + b;
+                        if (MODE == 0) {
+                            tc_tma3(r + b * QB, &L.tm_gu, sbk * MOE_Q4K_BYTES, blk * 64, it.slot, &raw_full[rs]);
+                            tc_tma3(r + b * QB + 64 * MOE_Q4K_BYTES, &L.tm_gu, sbk * MOE_Q4K_BYTES, d.I + blk * 64,
+                                    it.slot, &raw_full[rs]);
+                        } else if (MODE == 1) {
+                            tc_tma3(r + b * QB, &L.tm_d4, sbk * MOE_Q4K_BYTES, blk * 128, it.slot, &raw_full[rs]);
+                        } else {
+                            tc_tma3(r + b * QB, &L.tm_pf6q, sbk * 192, blk * 128, it.slot, &raw_full[rs]);
+                            tc_tma3(r + PF_RB * QB + b * 2048, &L.tm_d6s, sbk * 16, blk * 128, it.slot, &raw_full[rs]);
+                            if (sbk == 0)
+                                tc_tma3(sd + (jn & 1) * dpl + b * 256 * nbp, &L.tm_d6d, 0, blk * 128, it.slot,
+                                        &raw_full[rs]);
+                        }
                     }
                 }
             }
-            issued = sbk + 1;
+            jn++;
         }
         if (!ok && leader) {
             atomicExch(plan.error, PF_ERR_TIMEOUT);
-            tc_drain(raw_full, issued, RAW_NS);
+            tc_drain(raw_full, gs, RAW_NS);
         }
     } else if (warp == 2) {
         // activation producer: this CTA's half of the tile's pairs (16-row
         // boxes), PF_NSB atoms ahead.  The copies of both CTAs complete on the
         // leader's b_full, where the leader expects the bytes of both halves.
         const uint32_t leader = elect_one();
-        const int nbox = nhalf / 16, y0 = p0 + (int)rank * nhalf;
-        int issued = 0;
-        for (int i = 0; i < n_atoms && ok; i++) {
-            const int st = i % PF_NSB;
-            if (!tc_wait_warp(&b_empty[st], ((i / PF_NSB) & 1) ^ 1)) { ok = false; break; }
-            if (leader) {
-                if (rank == 0) tc_expect(&b_full[st], 2 * nbox * PF_BOX16);
-                const uint32_t bar = cluster_map(&b_full[st], 0);
-                for (int bx = 0; bx < nbox; bx++)
-                    tc_tma2_pair(sb + st * PF_BST + bx * PF_BOX16, &tmB, 64 * i, y0 + 16 * bx, bar);
+        int gb = 0;  // atoms issued
+        for (int item = cl; item < n_items && ok; item += ncl) {
+            PfItem it;
+            if (!pf_item<MODE>(d, L, plan, item, PR, rank, it)) continue;
+            const int nbox = it.npair / 32, y0 = it.p0 + (int)rank * (it.npair / 2);
+            for (int i = 0; i < n_atoms; i++, gb++) {
+                const int st = gb % PF_NSB;
+                if (!tc_wait_warp(&b_empty[st], ((gb / PF_NSB) & 1) ^ 1)) { ok = false; break; }
+                if (leader) {
+                    if (rank == 0) tc_expect(&b_full[st], 2 * nbox * PF_BOX16);
+                    const uint32_t bar = cluster_map(&b_full[st], 0);
+                    for (int bx = 0; bx < nbox; bx++)
+                        tc_tma2_pair(sb + st * PF_BST + bx * PF_BOX16, &tmB, 64 * i, y0 + 16 * bx, bar);
+                }
             }
-            issued = i + 1;
         }
         if (!ok && leader) {
             atomicExch(plan.error, PF_ERR_TIMEOUT);
             // the leader waits (bounded) for the last stages; the peer's copies
             // complete on the leader's barriers, and a peer that gave up here
             // issued its last copy at least one wait limit earlier
-            if (rank == 0) tc_drain(b_full, issued, PF_NSB);
+            if (rank == 0) tc_drain(b_full, gb, PF_NSB);
         }
     } else if (warp == 1) {
         if (rank == 0) {
@@ -451,42 +483,58 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
             // issues each MMA and commit; the operands are broadcast from lane 0 so
             // that they sit in uniform registers and the MMAs issue back to back.
             // The commits arrive on the barrier of the same address in both CTAs.
-            const uint32_t idesc = __shfl_sync(0xffffffffu, umma_idesc_f16(2 * PF_TILE, npair), 0);
             const uint32_t td = __shfl_sync(0xffffffffu, tmem, 0), ta0 = __shfl_sync(0xffffffffu, tmem_a, 0);
-            for (int i = 0; i < n_atoms && ok; i++) {
-                const int sa = i % PF_NSA, sbq = i % PF_NSB;
-                if (!tc_wait_warp(&a_full[sa], (i / PF_NSA) & 1) || !tc_wait_warp(&b_full[sbq], (i / PF_NSB) & 1)) {
-                    ok = false;
-                    break;
-                }
+            int gb = 0, jn = 0;  // atoms consumed, items taken
+            for (int item = cl; item < n_items && ok; item += ncl) {
+                PfItem it;
+                if (!pf_item<MODE>(d, L, plan, item, PR, rank, it)) continue;
+                const uint32_t idesc = __shfl_sync(0xffffffffu, umma_idesc_f16(2 * PF_TILE, it.npair), 0);
+                // the previous item's accumulator has been read by every epilogue warp
+                if (!tc_wait_warp(&acc_empty, (jn & 1) ^ 1)) { ok = false; break; }
                 tmem_fence_after();
-                const uint64_t bdesc = umma_desc_sw128(__shfl_sync(0xffffffffu, umma_smem_u32(sb + sbq * PF_BST), 0));
-                const uint32_t ta = __shfl_sync(0xffffffffu, ta0 + 64 * sa, 0);
-                const uint32_t acc = __shfl_sync(0xffffffffu, i, 0) != 0 ? 1u : 0u;
+                for (int i = 0; i < n_atoms; i++, gb++) {
+                    const int sa = i % PF_NSA, sbq = gb % PF_NSB;
+                    const int use = jn * pf_stage_uses(n_atoms, sa) + i / PF_NSA;
+                    if (!tc_wait_warp(&a_full[sa], use & 1) || !tc_wait_warp(&b_full[sbq], (gb / PF_NSB) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    tmem_fence_after();
+                    const uint64_t bdesc =
+                        umma_desc_sw128(__shfl_sync(0xffffffffu, umma_smem_u32(sb + sbq * PF_BST), 0));
+                    const uint32_t ta = __shfl_sync(0xffffffffu, ta0 + 64 * sa, 0);
+                    const uint32_t acc = __shfl_sync(0xffffffffu, i, 0) != 0 ? 1u : 0u;
 #pragma unroll
-                for (int b = 0; b < PF_RB; b++)
+                    for (int b = 0; b < PF_RB; b++)
 #pragma unroll
-                    for (int kk = 0; kk < 4; kk++)  // +32 B of K per step: +2 in the descriptor's address field
-                        umma_f16_ta_pair_warp(td + PF_TILE_N * b, ta + 32 * b + 8 * kk, bdesc + (uint64_t)(2 * kk),
-                                              idesc, (acc | kk) ? 1u : 0u);
-                umma_commit_pair_warp(&a_empty[sa]);
-                umma_commit_pair_warp(&b_empty[sbq]);
+                        for (int kk = 0; kk < 4; kk++)  // +32 B of K per step: +2 in the descriptor's address field
+                            umma_f16_ta_pair_warp(td + PF_TILE_N * b, ta + 32 * b + 8 * kk,
+                                                  bdesc + (uint64_t)(2 * kk), idesc, (acc | kk) ? 1u : 0u);
+                    umma_commit_pair_warp(&a_empty[sa]);
+                    umma_commit_pair_warp(&b_empty[sbq]);
+                }
+                if (!ok) break;
+                umma_commit_pair_warp(&acc_full);
+                jn++;
             }
-            umma_commit_pair_warp(&acc_full);
             if (!ok) {
-                // the MMAs already issued finish before tensor memory is freed
+                // the MMAs already issued finish before tensor memory is freed:
+                // one more commit completes phase jn of acc_full after all of them
                 if (lane == 0) atomicExch(plan.error, PF_ERR_TIMEOUT);
-                tc_wait_warp(&acc_full, 0);
+                umma_commit_pair_warp(&acc_full);
+                tc_wait_warp(&acc_full, jn & 1);
             }
         }
     } else {
         // dequantization: warp (q = warp % 4, g) owns tensor-memory lanes
         // 32 q .. 32 q + 31 (A rows; lane = row) of both blocks, and atoms
-        // i = g, g + PF_NSA, g + 2 PF_NSA, ... (K order), all of them through
-        // A stage g.  A stage has one producer group that takes its uses in
-        // order, so a parity wait on it is never a whole phase early; every
-        // group meets every super-block (4 consecutive atoms cover all
-        // residues mod PF_NSA), in order, so the raw-stage waits are exact too.
+        // i = g, g + PF_NSA, g + 2 PF_NSA, ... (K order) of every item, all of
+        // them through A stage g.  A stage has one producer group that takes
+        // its uses in order, so a parity wait on it is never a whole phase
+        // early; every group meets every super-block (4 consecutive atoms
+        // cover all residues mod PF_NSA), in order, so the raw-stage waits are
+        // exact too.  The same warps run the epilogue of each item, after
+        // their first A stage of the next item.
         const int q = warp & 3, g = (warp - PF_DQ_WARP0) >> 2, row = 32 * q + lane;
         int rraw = row;  // raw tile row (inside a block) holding A row `row`
         if (MODE == 0) {
@@ -494,81 +542,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
             rraw = h * 64 + 16 * q + i;                   // gate rows first, then up rows
         }
         const uint32_t tlane = (uint32_t)(32 * q) << 16;
-        for (int i = g, use = 0; i < n_atoms && ok; i += PF_NSA, use++) {
-            const int sbk = i >> 2, ga = i & 3;  // super-block, atom inside it
-            const int rs = sbk % RAW_NS;
-            if (!tc_wait_warp(&raw_full[rs], (sbk / RAW_NS) & 1)) { ok = false; break; }
-            const uint8_t *r = sr + rs * RAW;
-            // atom ga of this lane's rows in both blocks, dequantized into
-            // registers before the tensor-memory stage is waited for
-            uint32_t v[PF_RB][32];
-#pragma unroll
-            for (int b = 0; b < PF_RB; b++) {
-                uint32_t c[8];
-                if constexpr (MODE == 2) {
-                    // chunk t: ql words s4 = 0..3 and qh words 0, 1 of half ga / 2
-                    // (bytes 0-23 or 24-47 of the chunk: a 16-byte and an 8-byte load)
-                    uint32_t w[24];
-#pragma unroll
-                    for (int t = 0; t < 4; t++) {
-                        const uint8_t *cp = r + b * QB + rraw * PF_Q6_ROW + 48 * t;
-                        if (ga < 2) {
-                            const uint4 x = *reinterpret_cast<const uint4 *>(cp);
-                            const uint2 y = *reinterpret_cast<const uint2 *>(cp + 16);
-                            w[6 * t] = x.x; w[6 * t + 1] = x.y; w[6 * t + 2] = x.z; w[6 * t + 3] = x.w;
-                            w[6 * t + 4] = y.x; w[6 * t + 5] = y.y;
-                        } else {
-                            const uint2 x = *reinterpret_cast<const uint2 *>(cp + 24);
-                            const uint4 y = *reinterpret_cast<const uint4 *>(cp + 32);
-                            w[6 * t] = x.x; w[6 * t + 1] = x.y; w[6 * t + 2] = y.x; w[6 * t + 3] = y.y;
-                            w[6 * t + 4] = y.z; w[6 * t + 5] = y.w;
-                        }
-                    }
-                    const uint32_t sc4 = reinterpret_cast<const uint32_t *>(r + PF_RB * QB + b * 2048 + rraw * 16)[ga];
-                    const float d6 = __half2float(reinterpret_cast<const __half *>(sd + b * 256 * nbp)[rraw * nbp + sbk]);
-                    pf_q6_consts(d6, sc4, c);
-                    if (ga == 0) pf_deq_q6<0>(w, c, v[b]);
-                    else if (ga == 1) pf_deq_q6<1>(w, c, v[b]);
-                    else if (ga == 2) pf_deq_q6<2>(w, c, v[b]);
-                    else pf_deq_q6<3>(w, c, v[b]);
-                } else {
-                    const uint8_t *blk = r + b * QB + rraw * MOE_Q4K_BYTES;
-                    const uint4 hd = *reinterpret_cast<const uint4 *>(blk);
-                    uint32_t w[8];
-#pragma unroll
-                    for (int t = 0; t < 4; t++) {
-                        const uint2 x = *reinterpret_cast<const uint2 *>(blk + 16 + 32 * t + 8 * ga);
-                        w[2 * t] = x.x;
-                        w[2 * t + 1] = x.y;
-                    }
-                    pf_q4_consts(hd, ga, c);
-                    pf_deq_q4(w, pf_u2h(__byte_perm(hd.x, 0, 0x1010)), c, v[b]);  // d in both halves
-                }
-            }
-            // all reads of the stage are done (their values are consumed): the
-            // proxy fence orders them before the next TMA write into it
-            fence_async_smem();
-            __syncwarp();
-            if (lane == 0) tc_arrive(&raw_empty[rs]);
-            if (!tc_wait_warp(&a_empty[g], (use & 1) ^ 1)) { ok = false; break; }
+        const int uses = pf_stage_uses(n_atoms, g);
+        const int sub = (warp - PF_DQ_WARP0) >> 2;  // epilogue: column chunks alternate between the groups
+        const uint32_t acc_empty_leader = cluster_map(&acc_empty, 0);
+        // epilogue of item P (the jp-th taken): this warp reads tensor-memory
+        // lanes 32 (warp % 4) .. + 31 of both accumulators, then releases them
+        auto epilogue = [&](const PfItem &P, int jp) -> bool {
+            if (!tc_wait_warp(&acc_full, jp & 1)) return false;
             tmem_fence_after();
-#pragma unroll
-            for (int b = 0; b < PF_RB; b++) tmem_st32(tmem_a + tlane + 64 * g + 32 * b, v[b]);
-            tmem_wait_st();
-            tmem_fence_before();
-            __syncwarp();
-            if (lane == 0) tc_arrive_cluster(cluster_map(&a_full[g], 0));  // the leader's barrier
-        }
-        // epilogue: this warp reads tensor-memory lanes 32 (warp % 4) .. + 31
-        // of both accumulators
-        if (ok && tc_wait_warp(&acc_full, 0)) {
-            tmem_fence_after();
-            // PF_DQ_WARPS / 4 warps per lane quarter: column chunks alternate between them
-            const int sub = (warp - PF_DQ_WARP0) >> 2;
 #pragma unroll 1
             for (int b = 0; b < PF_RB; b++) {
-                const int blk = PF_RB * rg + b;
-                for (int c = 16 * sub; c < ntile; c += 16 * (PF_DQ_WARPS / 4)) {
+                const int blk = PF_RB * P.rg + b;
+                for (int c = 16 * sub; c < P.ntile; c += 16 * (PF_DQ_WARPS / 4)) {
                     float v[16];
                     tmem_ld16(tmem + PF_TILE_N * b + ((uint32_t)(32 * q) << 16) + c, v);
                     if (MODE == 0) {
@@ -579,21 +564,110 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
                             // silu(g) * u with the fast exponential and division: the
                             // result is rounded to fp16 (2^-11), far above their error
                             const float u = __shfl_xor_sync(0xffffffffu, v[j], 16);
-                            if (lane < 16 && c + j < ntile)
-                                act[(size_t)(p0 + c + j) * d.I + rI] =
+                            if (lane < 16 && c + j < P.ntile)
+                                act[(size_t)(P.p0 + c + j) * d.I + rI] =
                                     __float2half_rn(__fdividef(v[j], 1.0f + __expf(-v[j])) * u);
                         }
                     } else {
                         const int rH = blk * 128 + 32 * q + lane;
 #pragma unroll
                         for (int j = 0; j < 16; j++)
-                            if (c + j < ntile) eo[(size_t)(p0 + c + j) * d.H + rH] = v[j];
+                            if (c + j < P.ntile) eo[(size_t)(P.p0 + c + j) * d.H + rH] = v[j];
                     }
                 }
             }
-        } else if (lane == 0) {
-            atomicExch(plan.error, PF_ERR_TIMEOUT);
+            tmem_fence_before();
+            __syncwarp();
+            if (lane == 0) tc_arrive_cluster(acc_empty_leader);
+            return true;
+        };
+        int gs0 = 0, jn = 0;  // first super-block of the item in the raw ring, items taken
+        PfItem prev{};
+        bool pending = false;  // prev's epilogue not yet run
+        for (int item = cl; item < n_items && ok; item += ncl) {
+            PfItem it;
+            if (!pf_item<MODE>(d, L, plan, item, PR, rank, it)) continue;
+            const uint8_t *dplane = sd + (jn & 1) * dpl;
+            for (int i = g, j = 0; i < n_atoms; i += PF_NSA, j++) {
+                const int sbk = i >> 2, ga = i & 3, gs = gs0 + sbk;  // super-block, atom inside it
+                const int rs = gs % RAW_NS;
+                if (!tc_wait_warp(&raw_full[rs], (gs / RAW_NS) & 1)) { ok = false; break; }
+                const uint8_t *r = sr + rs * RAW;
+                // atom ga of this lane's rows in both blocks, dequantized into
+                // registers before the tensor-memory stage is waited for
+                uint32_t v[PF_RB][32];
+#pragma unroll
+                for (int b = 0; b < PF_RB; b++) {
+                    uint32_t c[8];
+                    if constexpr (MODE == 2) {
+                        // chunk t: ql words s4 = 0..3 and qh words 0, 1 of half ga / 2
+                        // (bytes 0-23 or 24-47 of the chunk: a 16-byte and an 8-byte load)
+                        uint32_t w[24];
+#pragma unroll
+                        for (int t = 0; t < 4; t++) {
+                            const uint8_t *cp = r + b * QB + rraw * PF_Q6_ROW + 48 * t;
+                            if (ga < 2) {
+                                const uint4 x = *reinterpret_cast<const uint4 *>(cp);
+                                const uint2 y = *reinterpret_cast<const uint2 *>(cp + 16);
+                                w[6 * t] = x.x; w[6 * t + 1] = x.y; w[6 * t + 2] = x.z; w[6 * t + 3] = x.w;
+                                w[6 * t + 4] = y.x; w[6 * t + 5] = y.y;
+                            } else {
+                                const uint2 x = *reinterpret_cast<const uint2 *>(cp + 24);
+                                const uint4 y = *reinterpret_cast<const uint4 *>(cp + 32);
+                                w[6 * t] = x.x; w[6 * t + 1] = x.y; w[6 * t + 2] = y.x; w[6 * t + 3] = y.y;
+                                w[6 * t + 4] = y.z; w[6 * t + 5] = y.w;
+                            }
+                        }
+                        const uint32_t sc4 =
+                            reinterpret_cast<const uint32_t *>(r + PF_RB * QB + b * 2048 + rraw * 16)[ga];
+                        const float d6 =
+                            __half2float(reinterpret_cast<const __half *>(dplane + b * 256 * nbp)[rraw * nbp + sbk]);
+                        pf_q6_consts(d6, sc4, c);
+                        if (ga == 0) pf_deq_q6<0>(w, c, v[b]);
+                        else if (ga == 1) pf_deq_q6<1>(w, c, v[b]);
+                        else if (ga == 2) pf_deq_q6<2>(w, c, v[b]);
+                        else pf_deq_q6<3>(w, c, v[b]);
+                    } else {
+                        const uint8_t *blk = r + b * QB + rraw * MOE_Q4K_BYTES;
+                        const uint4 hd = *reinterpret_cast<const uint4 *>(blk);
+                        uint32_t w[8];
+#pragma unroll
+                        for (int t = 0; t < 4; t++) {
+                            const uint2 x = *reinterpret_cast<const uint2 *>(blk + 16 + 32 * t + 8 * ga);
+                            w[2 * t] = x.x;
+                            w[2 * t + 1] = x.y;
+                        }
+                        pf_q4_consts(hd, ga, c);
+                        pf_deq_q4(w, pf_u2h(__byte_perm(hd.x, 0, 0x1010)), c, v[b]);  // d in both halves
+                    }
+                }
+                // all reads of the stage are done (their values are consumed): the
+                // proxy fence orders them before the next TMA write into it
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) tc_arrive(&raw_empty[rs]);
+                if (!tc_wait_warp(&a_empty[g], ((jn * uses + j) & 1) ^ 1)) { ok = false; break; }
+                tmem_fence_after();
+#pragma unroll
+                for (int b = 0; b < PF_RB; b++) tmem_st32(tmem_a + tlane + 64 * g + 32 * b, v[b]);
+                tmem_wait_st();
+                tmem_fence_before();
+                __syncwarp();
+                if (lane == 0) tc_arrive_cluster(cluster_map(&a_full[g], 0));  // the leader's barrier
+                if (j == 0 && pending) {
+                    // the previous item's epilogue, now that this group's first
+                    // stage of this item is written
+                    if (!epilogue(prev, jn - 1)) { ok = false; break; }
+                    pending = false;
+                }
+            }
+            prev = it;
+            pending = true;
+            gs0 += NB;
+            jn++;
         }
+        if (ok && pending && !epilogue(prev, jn - 1)) ok = false;
+        if (!ok && lane == 0) atomicExch(plan.error, PF_ERR_TIMEOUT);
     }
     // teardown: every thread of both CTAs arrives (no access from the other CTA
     // after this), then each CTA frees its tensor memory
@@ -972,7 +1046,7 @@ __global__ void __launch_bounds__(256) k_pfe_final(MoeDims d, MoePlan plan, cons
 static size_t pf_smem(int mode, int nbp) {
     const size_t raw = mode == 2 ? PF_RAW_Q6 : PF_RAW_Q4;
     return 1024 + (size_t)PF_NSB * PF_BST + (mode == 2 ? PF_RAW_NS_Q6 : PF_RAW_NS_Q4) * raw +
-           (mode == 2 ? PF_RB * 128 * 2 * (size_t)nbp : 0);
+           (mode == 2 ? 2 * PF_RB * 128 * 2 * (size_t)nbp : 0);  // two d-plane buffers
 }
 
 template <int MODE>
@@ -981,7 +1055,17 @@ static void pf_launch(const MoeDims &d, const MoeLayerDev &L, const MoePlan &pla
     const size_t smem = pf_smem(MODE, q6r_nb_pad(d.I / MOE_QK));
     static size_t attr[MOE_MAX_DEVICES];
     moe_smem_limit(k_prefill_gemm<MODE>, smem, attr);
-    k_prefill_gemm<MODE><<<dim3(row_groups, max_tiles), PF_THREADS, smem, s>>>(d, L, plan, tmB, act, eo);
+    // persistent: one cluster per TPC (one CTA per SM), at most one per item
+    static int n_sm[MOE_MAX_DEVICES];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= MOE_MAX_DEVICES) dev = 0;
+    if (!n_sm[dev] && cudaDeviceGetAttribute(&n_sm[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        n_sm[dev] = 148;
+    const int PR = row_groups / 2;
+    const long long items = (long long)max_tiles * PR;
+    const int clusters = (int)std::min<long long>(std::max(n_sm[dev] / 2, 1), items);
+    k_prefill_gemm<MODE><<<2 * clusters, PF_THREADS, smem, s>>>(d, L, plan, tmB, PR, act, eo);
     LAUNCH_COUNT(launches);
 }
 
@@ -1052,6 +1136,11 @@ int moe_prefill_alloc(MoePrefillWs &ws, const MoeDims &d, int T, int world, int 
     if (e == cudaSuccess) e = cudaMemset(ws.wl, 0, sizeof(__half) * Ep * d.H);
     if (e == cudaSuccess) e = cudaMemset(ws.xg, 0, sizeof(__half) * P * d.H);
     if (e == cudaSuccess) e = cudaMemset(ws.act, 0, sizeof(__half) * P * d.I);
+    // the clears run on the legacy default stream, which does not order
+    // against the context's non-blocking stream (nor a caller's): wait for
+    // them here, or a late clear can land after the first call's kernels have
+    // written wl / xg / act
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         moe_prefill_free(ws);
         return -1;
