@@ -465,6 +465,7 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
 // order, so there is no second pass over partials.  Same fp32 dot product as
 // the reference's sgemv (infer.m:1881) up to summation order.
 #define RS_MAX_T 4
+#define RS_U 8  // float4 loads in flight per thread
 __global__ void __launch_bounds__(256) k_router_small(const float *__restrict__ Wr, const float *__restrict__ x, int T,
                                                       int H, int E, float *__restrict__ logits) {
     __shared__ float red[RS_MAX_T][8];
@@ -473,13 +474,27 @@ __global__ void __launch_bounds__(256) k_router_small(const float *__restrict__ 
     const int e = blockIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const float4 *w4 = reinterpret_cast<const float4 *>(Wr + (size_t)e * H);
     float acc[RS_MAX_T] = {0.0f, 0.0f, 0.0f, 0.0f};
-    for (int i = threadIdx.x; i < H / 4; i += blockDim.x) {
-        const float4 w = __ldg(w4 + i);
+    // the row's loads of a thread are issued together (RS_U in flight, one
+    // DRAM latency instead of one per load); the products are added in the
+    // same order as one load at a time
+    const int n4 = H / 4;
+    for (int i0 = threadIdx.x; i0 < n4; i0 += RS_U * blockDim.x) {
+        float4 w[RS_U];
 #pragma unroll
-        for (int t = 0; t < RS_MAX_T; t++) {
-            if (t >= T) break;
-            const float4 v = __ldg(reinterpret_cast<const float4 *>(x + (size_t)t * H) + i);
-            acc[t] = fmaf(w.x, v.x, fmaf(w.y, v.y, fmaf(w.z, v.z, fmaf(w.w, v.w, acc[t]))));
+        for (int u = 0; u < RS_U; u++) {
+            const int i = i0 + u * blockDim.x;
+            w[u] = i < n4 ? __ldg(w4 + i) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+#pragma unroll
+        for (int u = 0; u < RS_U; u++) {
+            const int i = i0 + u * blockDim.x;
+            if (i >= n4) break;
+#pragma unroll
+            for (int t = 0; t < RS_MAX_T; t++) {
+                if (t >= T) break;
+                const float4 v = __ldg(reinterpret_cast<const float4 *>(x + (size_t)t * H) + i);
+                acc[t] = fmaf(w[u].x, v.x, fmaf(w[u].y, v.y, fmaf(w[u].z, v.z, fmaf(w[u].w, v.w, acc[t]))));
+            }
         }
     }
 #pragma unroll
@@ -646,47 +661,56 @@ __device__ void build_plan_block(const RouteArgs &a) {
     moe_plan_order_chunks(a.plan, coff[NE], a.d.tc);
 }
 
-// Top groups by repeated argmax, the lowest index winning ties and only
-// scores above -1e30 counting (infer.m:944-954), with one warp: lane l holds
-// groups l and l + 32.
+// Top groups of infer.m:944-954 (repeated argmax, the lowest index winning
+// ties, only scores above -1e30 counting), with one warp: lane l ranks groups
+// l and l + 32 directly -- a group is taken when its score is above -1e30 and
+// fewer than TG groups come before it in (score descending, index ascending)
+// order, which is the set the repeated argmax takes, in one step instead of
+// TG rounds of shuffles.  NaN scores are never taken and rank no group.
 __device__ __forceinline__ unsigned long long top_groups_warp(const float *gs, int G, int TG, int lane) {
     unsigned long long taken = 0ull;
-    const float v0 = lane < G ? gs[lane] : -3.0e38f, v1 = lane + 32 < G ? gs[lane + 32] : -3.0e38f;
-    for (int k = 0; k < TG; k++) {
-        float bv = -1e30f;
-        int bi = -1;
-        if (lane < G && !((taken >> lane) & 1ull) && v0 > bv) { bv = v0; bi = lane; }
-        if (lane + 32 < G && !((taken >> (lane + 32)) & 1ull) && v1 > bv) { bv = v1; bi = lane + 32; }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (oi >= 0 && (ov > bv || (ov == bv && (bi < 0 || oi < bi)))) { bv = ov; bi = oi; }
+    for (int half = 0; half < 2; half++) {
+        const int g = lane + 32 * half;
+        bool take = false;
+        if (g < G) {
+            const float v = gs[g];
+            int rank = 0;
+            for (int h = 0; h < G; h++) {
+                const float u = gs[h];
+                rank += (u > v || (u == v && h < g)) ? 1 : 0;
+            }
+            take = v > -1e30f && rank < TG;
         }
-        if (bi >= 0) taken |= 1ull << bi;
+        const unsigned bal = __ballot_sync(0xffffffffu, take);
+        taken |= (unsigned long long)bal << (32 * half);
     }
     return taken;
 }
 
+// order-preserving int key of a non-NaN float: a < b exactly when
+// f32_ord(a) < f32_ord(b) (-0.0 below +0.0; the scores here are never -0.0)
+__device__ __forceinline__ int f32_ord(float f) {
+    const int i = __float_as_int(f);
+    return i >= 0 ? i : i ^ 0x7FFFFFFF;
+}
+__device__ __forceinline__ float f32_unord(int o) { return __int_as_float(o >= 0 ? o : o ^ 0x7FFFFFFF); }
+
 // Slot-order top-K of infer.m:966-980 over the experts of the taken groups in
 // ascending order: a candidate strictly greater than the current minimum
-// replaces the first (lowest) slot holding that minimum.  One warp; every
-// lane keeps the same KK slots (K <= KK used) in registers.  Candidates are
-// tested 32 at a time with a ballot; only the first one above the minimum is
-// inserted before the rest of the batch is tested again against the new
-// minimum (the minimum only grows, so earlier lanes stay out).
-template <int KK>
+// replaces the first (lowest) slot holding that minimum.  One warp; lane k < K
+// holds slot k.  Candidates are tested 32 at a time with a ballot; only the
+// first one above the minimum is inserted before the rest of the batch is
+// tested again against the new minimum (the minimum only grows, so earlier
+// lanes stay out).  The new minimum is one warp min-reduction of the slots'
+// ordered keys, its slot the first lane holding it.  On return every lane
+// holds the K slots in key[] / idx[] (slot order).
 __device__ __forceinline__ void topk_slots_warp(const float *choice, unsigned long long taken, int G, int per, int K,
                                                 int lane, float (&key)[MOE_MAX_K], int (&idx)[MOE_MAX_K]) {
-    float kv[KK];
-    int iv[KK];
-#pragma unroll
-    for (int k = 0; k < KK; k++) {
-        kv[k] = k < K ? -1e30f : 3.0e38f;  // unused slots are never the minimum
-        iv[k] = 0;
-    }
-    int mk = 0;
-    float mkey = -1e30f;
+    float sv = lane < K ? -1e30f : 3.0e38f;  // lanes past K never hold the minimum
+    int si = 0;
+    float mkey = -1e30f;  // the current minimum
+    int mk = 0;           // the first slot holding it
     for (int g = 0; g < G; g++) {
         if (!((taken >> g) & 1ull)) continue;
         for (int e0 = g * per; e0 < (g + 1) * per; e0 += 32) {
@@ -697,34 +721,82 @@ __device__ __forceinline__ void topk_slots_warp(const float *choice, unsigned lo
                 if (!bal) break;
                 const int f = __ffs(bal) - 1;
                 const float cf = __shfl_sync(0xffffffffu, c, f);
-#pragma unroll
-                for (int k = 0; k < KK; k++)
-                    if (k == mk) { kv[k] = cf; iv[k] = e0 + f; }
-                float tv[KK];
-                int ti[KK];
-#pragma unroll
-                for (int k = 0; k < KK; k++) { tv[k] = kv[k]; ti[k] = k; }
-#pragma unroll
-                for (int w = 1; w < KK; w <<= 1)
-#pragma unroll
-                    for (int k = 0; k + w < KK; k += 2 * w)
-                        if (tv[k + w] < tv[k]) { tv[k] = tv[k + w]; ti[k] = ti[k + w]; }
-                mkey = tv[0];
-                mk = ti[0];
+                if (lane == mk) { sv = cf; si = e0 + f; }
+                const int o = f32_ord(sv);
+                const int mn = __reduce_min_sync(0xffffffffu, o);
+                mk = __ffs(__ballot_sync(0xffffffffu, o == mn)) - 1;
+                mkey = f32_unord(mn);
                 rem = f == 31 ? 0u : (0xffffffffu << (f + 1));
             }
         }
     }
 #pragma unroll
     for (int k = 0; k < MOE_MAX_K; k++) {
-        key[k] = k < KK ? kv[k < KK ? k : 0] : -1e30f;
-        idx[k] = k < KK ? iv[k < KK ? k : 0] : 0;
+        key[k] = __shfl_sync(0xffffffffu, sv, k);
+        idx[k] = __shfl_sync(0xffffffffu, si, k);
     }
 }
 
-// The last block of the grid to finish builds the plan for all tokens.
-__device__ __forceinline__ void route_plan_finish(const RouteArgs &a, int &is_last) {
+// The plan of one routed token, written by the routing warp from its
+// registers (all lanes hold the K slots and weights): the K experts are
+// distinct, so each gets one pair and one chunk of one token, in ascending
+// expert order, then the shared expert's pair and chunk -- what
+// build_plan_block produces for this input (chunks of equal size may take any
+// order in chunk_order).  Returns false, writing nothing, when an expert
+// repeats (fewer candidates than slots), which build_plan_block handles.
+__device__ __forceinline__ bool plan_one_token(const RouteArgs &a, int lane, const int (&idx)[MOE_MAX_K],
+                                               const float (&w)[MOE_MAX_K]) {
+    const int K = a.d.K, E = a.d.E;
+    int e = 0, rank = 0;
+    float wk = 0.0f;
+    bool dup = false;
+#pragma unroll
+    for (int k = 0; k < MOE_MAX_K; k++)
+        if (k == lane) { e = idx[k]; wk = w[k]; }
+#pragma unroll
+    for (int j = 0; j < MOE_MAX_K; j++)
+        if (j < K) {
+            rank += idx[j] < e ? 1 : 0;
+            dup |= j != lane && idx[j] == e;
+        }
+    if (__any_sync(0xffffffffu, lane < K && (dup || e < 0 || e >= E))) return false;
+    const int n = K + (a.include_shared ? 1 : 0);
+    const MoePlan &p = a.plan;
+    if (lane < K) {
+        p.pair_expert[rank] = e;
+        p.pair_token[rank] = 0;
+        p.pair_w[rank] = wk;
+        p.slot_pair[lane] = rank;
+        p.chunk_expert[rank] = e;
+        p.chunk_pair0[rank] = rank;
+        p.chunk_ntok[rank] = 1;
+    } else if (lane == K && a.include_shared) {
+        p.pair_expert[K] = E;
+        p.pair_token[K] = 0;
+        p.pair_w[K] = 1.0f;
+        p.slot_pair[K] = K;
+        p.chunk_expert[K] = E;
+        p.chunk_pair0[K] = K;
+        p.chunk_ntok[K] = 1;
+    }
+    if (lane < n) p.chunk_order[lane] = lane;
+    // pairs, chunks, routed experts with pairs, tcgen05 chunks (none), the rest 0
+    if (lane < MOE_PLAN_COUNTS) p.counts[lane] = lane == 0 ? n : lane == 1 ? n : lane == 2 ? K : 0;
+    return true;
+}
+
+// The last block of the grid to finish builds the plan for all tokens.  With
+// one token the routing block builds it itself, right after routing (no
+// grid-wide fence and counter hand-off; in routing mode usually straight
+// from its registers, plan_one_token); the operand blocks then just leave.
+__device__ __forceinline__ void route_plan_finish(const RouteArgs &a, int &is_last, const int &plan_done) {
     if (!a.build_plan) return;
+    if (a.T == 1) {
+        if (blockIdx.x != 0) return;
+        __syncthreads();  // the block's own idx / w stores (and plan_done) are visible to its reads
+        if (!plan_done) build_plan_block(a);
+        return;
+    }
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) is_last = (atomicAdd(a.counter, 1) == (int)gridDim.x - 1);
@@ -741,7 +813,8 @@ __device__ __forceinline__ void route_plan_finish(const RouteArgs &a, int &is_la
 __global__ void __launch_bounds__(256) k_route_plan(RouteArgs a) {
     __shared__ float score[1024], choice[1024];
     __shared__ float gs[64];
-    __shared__ int is_last;
+    __shared__ int is_last, plan_done;
+    if (threadIdx.x == 0) plan_done = 0;
     moe_pdl_wait();
     moe_pdl_trigger();
     if ((int)blockIdx.x >= a.T) {
@@ -755,7 +828,7 @@ __global__ void __launch_bounds__(256) k_route_plan(RouteArgs a) {
             build_op_sb(xs, row + (size_t)sb * OPB_SB, 4, threadIdx.x & 31);
             build_opw_sb(xs, row + op_bytes(a.d.H) + (size_t)sb * OPW_SB, 4, threadIdx.x & 31);
         }
-        route_plan_finish(a, is_last);
+        route_plan_finish(a, is_last, plan_done);
         return;
     }
     const int t = blockIdx.x;
@@ -811,9 +884,8 @@ __global__ void __launch_bounds__(256) k_route_plan(RouteArgs a) {
             const unsigned long long taken = top_groups_warp(gs, G, TG, lane);
             float key[MOE_MAX_K];
             int idx[MOE_MAX_K];
-            if (K <= 8) topk_slots_warp<8>(choice, taken, G, per, K, lane, key, idx);
-            else topk_slots_warp<MOE_MAX_K>(choice, taken, G, per, K, lane, key, idx);
-            if (lane != 0) goto routed;
+            topk_slots_warp(choice, taken, G, per, K, lane, key, idx);
+            // the routing weights (every lane, the same values; lane 0 stores them)
             float w[MOE_MAX_K], s = 0.0f;
 #pragma unroll
             for (int k = 0; k < MOE_MAX_K; k++)
@@ -821,18 +893,26 @@ __global__ void __launch_bounds__(256) k_route_plan(RouteArgs a) {
             const float f = s > 0.0f ? a.d.scale / s : 1.0f;
 #pragma unroll
             for (int k = 0; k < MOE_MAX_K; k++)
-                if (k < K) {
-                    a.idx_out[t * K + k] = idx[k];
-                    a.w_out[t * K + k] = s > 0.0f ? w[k] * f : w[k];
-                }
+                if (k < K) w[k] = s > 0.0f ? w[k] * f : w[k];
+            if (lane == 0) {
+#pragma unroll
+                for (int k = 0; k < MOE_MAX_K; k++)
+                    if (k < K) {
+                        a.idx_out[t * K + k] = idx[k];
+                        a.w_out[t * K + k] = w[k];
+                    }
+            }
+            if (a.build_plan && a.T == 1) {
+                const bool done = plan_one_token(a, lane, idx, w);
+                if (lane == 0) plan_done = done ? 1 : 0;
+            }
         }
-    routed:;
     } else if (a.mode == 1 && threadIdx.x < K) {
         a.idx_out[t * K + threadIdx.x] = a.idx_in[t * K + threadIdx.x];
         a.w_out[t * K + threadIdx.x] = a.w_in[t * K + threadIdx.x];
     }
 
-    route_plan_finish(a, is_last);
+    route_plan_finish(a, is_last, plan_done);
 }
 
 void moe_launch_route_and_plan(const MoeDims &d, const float *part, int n_split, const float *logits,
