@@ -453,17 +453,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PF_THREADS, 1)
         // activation producer: this CTA's half of the tile's pairs (16-row
         // boxes), PF_NSB atoms ahead.  The copies of both CTAs complete on the
         // leader's b_full, where the leader expects the bytes of both halves.
+        // Only the boxes that reach the tile's pairs are loaded: the rows of a
+        // half past them (N is rounded up to 32) keep stale values, which
+        // reach only accumulator columns that are never stored (column n of
+        // D depends on row n of B alone).
         const uint32_t leader = elect_one();
         int gb = 0;  // atoms issued
         for (int item = cl; item < n_items && ok; item += ncl) {
             PfItem it;
             if (!pf_item<MODE>(d, L, plan, item, PR, rank, it)) continue;
-            const int nbox = it.npair / 32, y0 = it.p0 + (int)rank * (it.npair / 2);
+            const int nhalf = it.npair / 2, y0 = it.p0 + (int)rank * nhalf;
+            // 16-row boxes of each half that hold pairs of the tile
+            const int real0 = min(it.ntile, nhalf), real1 = max(it.ntile - nhalf, 0);
+            const int nb0 = (real0 + 15) / 16, nb1 = (real1 + 15) / 16, nbox = rank ? nb1 : nb0;
             for (int i = 0; i < n_atoms; i++, gb++) {
                 const int st = gb % PF_NSB;
                 if (!tc_wait_warp(&b_empty[st], ((gb / PF_NSB) & 1) ^ 1)) { ok = false; break; }
                 if (leader) {
-                    if (rank == 0) tc_expect(&b_full[st], 2 * nbox * PF_BOX16);
+                    if (rank == 0) tc_expect(&b_full[st], (nb0 + nb1) * PF_BOX16);
                     const uint32_t bar = cluster_map(&b_full[st], 0);
                     for (int bx = 0; bx < nbox; bx++)
                         tc_tma2_pair(sb + st * PF_BST + bx * PF_BOX16, &tmB, 64 * i, y0 + 16 * bx, bar);
