@@ -737,9 +737,9 @@ __device__ __forceinline__ void topk_slots_warp(const float *choice, unsigned lo
     }
 }
 
-// The plan of one routed token, written by the routing warp from its
-// registers (all lanes hold the K slots and weights): the K experts are
-// distinct, so each gets one pair and one chunk of one token, in ascending
+// The plan of one token, written by warp 0 from its registers (all lanes hold
+// the K slots and weights, routed or given): when the K experts are
+// distinct, each gets one pair and one chunk of one token, in ascending
 // expert order, then the shared expert's pair and chunk -- what
 // build_plan_block produces for this input (chunks of equal size may take any
 // order in chunk_order).  Returns false, writing nothing, when an expert
@@ -787,8 +787,8 @@ __device__ __forceinline__ bool plan_one_token(const RouteArgs &a, int lane, con
 
 // The last block of the grid to finish builds the plan for all tokens.  With
 // one token the routing block builds it itself, right after routing (no
-// grid-wide fence and counter hand-off; in routing mode usually straight
-// from its registers, plan_one_token); the operand blocks then just leave.
+// grid-wide fence and counter hand-off; usually straight from warp 0's
+// registers, plan_one_token); the operand blocks then just leave.
 __device__ __forceinline__ void route_plan_finish(const RouteArgs &a, int &is_last, const int &plan_done) {
     if (!a.build_plan) return;
     if (a.T == 1) {
@@ -907,9 +907,28 @@ __global__ void __launch_bounds__(256) k_route_plan(RouteArgs a) {
                 if (lane == 0) plan_done = done ? 1 : 0;
             }
         }
-    } else if (a.mode == 1 && threadIdx.x < K) {
-        a.idx_out[t * K + threadIdx.x] = a.idx_in[t * K + threadIdx.x];
-        a.w_out[t * K + threadIdx.x] = a.w_in[t * K + threadIdx.x];
+    } else if (a.mode == 1 && threadIdx.x < 32) {
+        // routing given: copied through; with one token warp 0 also writes the plan
+        const int lane = threadIdx.x;
+        int ie = 0;
+        float iw = 0.0f;
+        if (lane < K) {
+            ie = a.idx_in[t * K + lane];
+            iw = a.w_in[t * K + lane];
+            a.idx_out[t * K + lane] = ie;
+            a.w_out[t * K + lane] = iw;
+        }
+        if (a.build_plan && a.T == 1) {
+            int idx[MOE_MAX_K];
+            float w[MOE_MAX_K];
+#pragma unroll
+            for (int k = 0; k < MOE_MAX_K; k++) {
+                idx[k] = __shfl_sync(0xffffffffu, ie, k);
+                w[k] = __shfl_sync(0xffffffffu, iw, k);
+            }
+            const bool done = plan_one_token(a, lane, idx, w);
+            if (lane == 0) plan_done = done ? 1 : 0;
+        }
     }
 
     route_plan_finish(a, is_last, plan_done);
