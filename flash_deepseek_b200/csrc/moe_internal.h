@@ -40,6 +40,10 @@ struct MoeLayerDev {
     CUtensorMap tm_d6s;     // Q6_K down, S plane, box 16 B x 128 rows
     CUtensorMap tm_d6d;     // Q6_K down, D plane, box 2 nb_pad B x 128 rows
     CUtensorMap tm_pf6q;    // Q6_K down, Q plane, box 208 B x 128 rows (prefill: rows 208 B apart in shared memory)
+    // the router weights x 2^8 as fp16 hi / lo (decode tensor-core router), rows
+    // padded with zeros to a multiple of 128; box 64 columns x 128 rows
+    __half *rwh, *rwl;
+    CUtensorMap tm_rwh, tm_rwl;
 };
 
 struct MoeDims {
@@ -142,6 +146,7 @@ __host__ __device__ __forceinline__ void moe_chunk(int n, int c, int tc, int &st
 // chunks, [4] gate/up, [5] Q6_K down, [6] Q4_K down work counters (zeroed by
 // the plan builder)
 #define MOE_PLAN_COUNTS 8
+#define MOE_ROUTER_SIMT_T 4  // decode tokens up to which the SIMT router (k_router_small) runs
 
 #ifdef __CUDACC__
 // Block-wide, after the block has written the plan's n_chunks chunks:
@@ -243,6 +248,14 @@ void moe_launch_pfe_experts(const MoeDims &d, const MoeLayerDev &L, MoePrefillWs
                             uint64_t *launches);
 void moe_launch_pfe_final(const MoeDims &d, MoePrefillWs &ws, int T, float *out, cudaStream_t s, uint64_t *launches);
 void moe_prefill_free(MoePrefillWs &ws);
+// the router weights' fp16 hi/lo split kept per layer (decode tensor-core router)
+void moe_launch_router_split(const float *Wr, int E, int H, __half *wh, __half *wl, cudaStream_t s,
+                             uint64_t *launches);
+// decode router logits of T (5..64) tokens on the tensor cores into logits[T][E]
+void moe_launch_router_tc(const MoeDims &d, const CUtensorMap &tm_wh, const CUtensorMap &tm_wl, const float *x,
+                          int T, __half *xh, __half *xl, const CUtensorMap &tm_xh, const CUtensorMap &tm_xl,
+                          float *part, int max_split, float *logits, int *error, cudaStream_t s,
+                          uint64_t *launches);
 // router logits of T tokens into ws.logits (tensor cores, fp16 hi/lo splits)
 void moe_launch_prefill_router(const MoeDims &d, const float *Wr, MoePrefillWs &ws, const float *x, int T,
                                cudaStream_t s, uint64_t *launches);

@@ -464,7 +464,7 @@ __global__ void __launch_bounds__(256) k_router_logits(const float *__restrict__
 // router row (H fp32, all loads in flight at once) and reduces in a fixed
 // order, so there is no second pass over partials.  Same fp32 dot product as
 // the reference's sgemv (infer.m:1881) up to summation order.
-#define RS_MAX_T 4
+#define RS_MAX_T MOE_ROUTER_SIMT_T
 #define RS_U 8  // float4 loads in flight per thread
 __global__ void __launch_bounds__(256) k_router_small(const float *__restrict__ Wr, const float *__restrict__ x, int T,
                                                       int H, int E, float *__restrict__ logits) {

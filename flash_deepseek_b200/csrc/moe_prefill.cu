@@ -837,6 +837,43 @@ void moe_launch_prefill_router(const MoeDims &d, const float *Wr, MoePrefillWs &
     if (launches) *launches += 4;
 }
 
+// The router weights' fp16 hi/lo split (x 2^8, the same split as the
+// prefill router's), kept per layer for the decode path: wh / wl hold E rows
+// of H (rows up to the 128-row box padded with zeros by the caller).
+void moe_launch_router_split(const float *Wr, int E, int H, __half *wh, __half *wl, cudaStream_t s,
+                             uint64_t *launches) {
+    const size_t nw = (size_t)E * H;
+    k_pf_split<<<(unsigned)((nw / 4 + 255) / 256), 256, 0, s>>>(Wr, nw, RT_SCALE, wh, wl);
+    LAUNCH_COUNT(launches);
+}
+
+// Decode router logits of 5..64 tokens on the tensor cores: x split into fp16
+// hi/lo (xh / xl: 128 rows, tm_xh / tm_xl over them), the three-MMA router
+// against the layer's kept split, K slices summed in a fixed order into
+// logits[T][E].  max_split bounds the slices (the part buffer holds
+// max_split x T x E); the slice count is the largest divisor of H / 64 within
+// it, so that the router CTAs cover more SMs.
+void moe_launch_router_tc(const MoeDims &d, const CUtensorMap &tm_wh, const CUtensorMap &tm_wl, const float *x,
+                          int T, __half *xh, __half *xl, const CUtensorMap &tm_xh, const CUtensorMap &tm_xl,
+                          float *part, int max_split, float *logits, int *error, cudaStream_t s,
+                          uint64_t *launches) {
+    const size_t nx = (size_t)T * d.H;
+    const size_t gx = (nx / 4 + 255) / 256;
+    k_pf_split<<<(unsigned)(gx < 148 * 16 ? gx : 148 * 16), 256, 0, s>>>(x, nx, 1.0f, xh, xl);
+    const size_t smem = 1024 + (size_t)RT_NS * 4 * PF_ATOM;
+    static size_t attr[MOE_MAX_DEVICES];
+    moe_smem_limit(k_pf_router, smem, attr);
+    const int na = d.H / 64;
+    int nsplit = 1;
+    for (int k = max_split < na ? max_split : na; k >= 1; k--)
+        if (na % k == 0) { nsplit = k; break; }
+    k_pf_router<<<dim3((d.E + 127) / 128, (T + 127) / 128, nsplit), RT_THREADS, smem, s>>>(
+        T, d.H, d.E, nsplit, tm_wh, tm_wl, tm_xh, tm_xl, part, error);
+    const size_t nl = (size_t)T * d.E;
+    k_pf_router_sum<<<(unsigned)((nl + 255) / 256), 256, 0, s>>>(part, nl, nsplit, logits);
+    if (launches) *launches += 3;
+}
+
 // ===========================================================================
 // expert parallelism for prefill (one process per GPU, experts sharded
 // n_experts / world per rank, router and shared expert replicated).  Row
