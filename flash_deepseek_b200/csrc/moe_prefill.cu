@@ -812,7 +812,16 @@ __global__ void __launch_bounds__(256) k_pf_router_sum(const float *__restrict__
                                                        float *__restrict__ logits) {
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         float a = part[i];
-        for (int k = 1; k < nsplit; k++) a += part[(size_t)k * n + i];
+        // the partials loaded 8 at a time (one L2 round trip per 8 slices),
+        // added one by one in slice order
+        for (int k = 1; k < nsplit; k += 8) {
+            float v[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) v[u] = k + u < nsplit ? part[(size_t)(k + u) * n + i] : 0.0f;
+#pragma unroll
+            for (int u = 0; u < 8; u++)
+                if (k + u < nsplit) a += v[u];
+        }
         logits[i] = a * (1.0f / RT_SCALE);
     }
 }
