@@ -241,8 +241,11 @@ int moe_prefill(moe_ctx *ctx, int layer, const float *h_post, int n_tokens, floa
 
 /* Routing from hidden states with no allocation: router logits
  * (d_h x d_router_w^T, fp32) then the grouped top-k of moe_route(), writing
- * d_idx / d_w [n_tokens x top_k] -- the same kernels and arithmetic as the
- * routing inside moe_forward().  For callers that cannot call cudaMalloc (a
+ * d_idx / d_w [n_tokens x top_k] -- the routing of moe_forward(): the same
+ * kernels and arithmetic up to 4 tokens; for more, moe_forward's logits come
+ * from the tensor-core router (fp32 accuracy, another summation order), so
+ * the two agree except where two experts' choice scores are within ~1e-6 of
+ * each other.  For callers that cannot call cudaMalloc (a
  * fixed memory pool, or a latency-critical decode loop where an allocation
  * may synchronize the device): all scratch lives in a fixed array inside the
  * library (2 MiB per GPU, held until exit).  Limits: n_tokens <= 64,

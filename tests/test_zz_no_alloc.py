@@ -1,7 +1,9 @@
 """GPU: moe_route_hidden_noalloc -- routing for callers that cannot allocate
 device memory (a fixed memory pool, or a decode loop where cudaMalloc may
 synchronize the device) -- gives the same routing as moe_forward, through the
-C ABI, at DeepSeek-V3 shapes.  Calls follow each other on one shared scratch
+C ABI, at DeepSeek-V3 shapes (above 4 tokens moe_forward's logits come from
+the tensor-core router, fp32-accurate in another summation order; these
+seeded inputs hold no near tie, so indices match exactly and weights to 1e-6).  Calls follow each other on one shared scratch
 array that keeps the last call's contents: 3 tokens (one-pass router kernel,
 no scratch), then 5 and 64 tokens (split-K router: partial sums and
 completion counters in the array), then 64 tokens again with other inputs.
