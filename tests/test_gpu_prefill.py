@@ -87,6 +87,28 @@ def test_prefill_matches_oracle(cuda_lib, oracle, down_type):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("T", [1, 2, 17])
+def test_prefill_short_prompts_match_oracle(cuda_lib, oracle, T):
+    """Ragged tiny tiles: one to a few pairs per expert, so the pair MMA's N
+    (rounded up to 32) is mostly padding and the peer CTA of a pair holds no
+    pair of the tile (it loads no activation box); the same call object is
+    reused across sizes by the workspace."""
+    from test_gpu_moe import check_routing, oracle_layer, rel_err, router_of, small_cfg
+    cfg = small_cfg(intermediate=2048)
+    m = cuda_lib.MoE(cfg)
+    m.init_layer_synthetic(0, seed=13, down_type=14)
+    router, bias = router_of(oracle, 13, 0, cfg)
+    h = oracle.normal(30 + T, oracle.stream(0, 0, oracle.KIND_ACT), T * cfg.hidden, 1.0).reshape(T, cfg.hidden)
+    out, idx, w = m.prefill(0, h)
+    logits = (h.astype(np.float64) @ router.astype(np.float64).T).astype(np.float32)
+    check_routing(oracle, cfg, logits, bias, idx, w)
+    ref = oracle_layer(oracle, m, cfg, 0, 14, h, idx, w, router, bias)
+    e = rel_err(out, ref)
+    assert e < PREFILL_TOL, (T, e)
+    m.close()
+
+
+@pytest.mark.gpu
 def test_prefill_matches_decode_path_full_size(cuda_lib, oracle):
     """DeepSeek shapes: the tensor-core prefill (tensor-core router with fp16
     hi/lo splits, tcgen05 expert GEMMs) agrees with the exact decode path on
