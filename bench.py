@@ -56,7 +56,10 @@ EXTRA = {
     "stack_b8": dict(B=8, name="config4_stack58_b8"),
     "stack_b32": dict(B=32, name="config4_stack58_b32"),
     "prefill4096": dict(B=4096, name="config5_prefill4096_1layer"),
+    "dense_b1": dict(B=1, name="dense_ffn_layers0to2_b1"),
 }
+DENSE_I = 18432             # DENSE_INTERMEDIATE (infer.m:59)
+DENSE_LAYERS = 3            # FIRST_MOE_LAYER (infer.m:46)
 Q4_DOWN_BYTES = H * (I // 256) * 144         # 8,257,536
 
 
@@ -480,7 +483,9 @@ def run_extra(args):
                    20 + 20 + 18 times; every layer's weights exceed L2, so the
                    re-use changes nothing but the memory needed
       prefill4096  4096 tokens through one layer per moe_prefill_device call
-                   (tcgen05 GEMMs over fp16-dequantized weight tiles)"""
+                   (tcgen05 GEMMs over fp16-dequantized weight tiles)
+      dense_b1     one token through the three dense FFN layers (0-2) per
+                   step, moe_dense_forward_device per layer"""
     import torch
     import flash_deepseek_b200 as F
     W = EXTRA[args.workload]
@@ -648,6 +653,60 @@ def run_extra(args):
             clk.__exit__(None, None, None)
             moe.close()
             return None
+    elif args.workload == "dense_b1":
+        # the three dense FFN layers of one decode token (infer.m:1852-1868):
+        # fp16 weights, 792.7 MB per layer, 2.38 GB per step (> L2: no flush)
+        cfg = F.MoeConfig(n_layers=DENSE_LAYERS, max_tokens=1)
+        moe = F.MoE(cfg, device=local)
+        for l in range(DENSE_LAYERS):
+            moe.init_dense_synthetic(l, DENSE_I, seed=0, w_sigma=0.02)
+        xs = [torch.randn(1, H, generator=g).to(dev) for _ in range(N_POOL)]
+        out = torch.empty(1, H, device=dev)
+        stream = torch.cuda.ExternalStream(moe.stream, device=dev)
+
+        def step(i):
+            for l in range(DENSE_LAYERS):
+                moe.dense_forward_device(l, xs[i % N_POOL], 1, out, stream=moe.stream)
+        with torch.cuda.stream(stream):
+            for i in range(args.warmup):
+                step(i)
+        torch.cuda.synchronize()
+        n = args.steps
+        l0 = moe.kernel_launches
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            a.record(stream)
+            for i in range(n):
+                step(i)
+            b.record(stream)
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b)
+        launches = moe.kernel_launches - l0
+        ms_step = ms / n
+        value = n / (ms / 1e3)
+        unit = "tokens/s"
+        bytes_step = DENSE_LAYERS * 3 * DENSE_I * H * 2 + DENSE_LAYERS * (2 * H * 4 + 2 * DENSE_I * 4)
+        roof = {"bound": "hbm", "kernel": "whole step (3 layers x k_dense_gateup + k_dense_down)",
+                "achieved": round(bytes_step / (ms_step / 1e3) / 1e9, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(bytes_step / (ms_step / 1e3) / 1e9 / peak, 4), "peak_source": peak_kind,
+                "algorithmic_bytes_per_step": bytes_step, "traffic": None}
+        # end to end: moe_dense_forward per layer from pinned host memory
+        h_pin = xs[0].cpu().pin_memory().numpy()
+        o_pin = torch.empty(1, H).pin_memory().numpy()
+        lib = moe.lib
+        for l in range(DENSE_LAYERS):
+            lib.moe_dense_forward(moe.ctx, l, h_pin.ctypes.data, 1, o_pin.ctypes.data)
+        n_e2e = max(2, n // 4)
+        t_0 = time.perf_counter()
+        for i in range(n_e2e):
+            for l in range(DENSE_LAYERS):
+                if lib.moe_dense_forward(moe.ctx, l, h_pin.ctypes.data, 1, o_pin.ctypes.data) != 0:
+                    raise RuntimeError(lib.moe_last_error(moe.ctx))
+        e2e_s = time.perf_counter() - t_0
+        e2e = {"value": round(n_e2e / e2e_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": DENSE_LAYERS * H * 4,
+               "d2h_bytes_per_step": DENSE_LAYERS * H * 4, "timer": "host wall clock (synchronous calls)"}
+        extra = {"intermediate": DENSE_I, "layers": DENSE_LAYERS, "experts": 0,
+                 "l2": "not flushed: 2.38 GB of weights per step cycle through the 126 MB L2"}
     else:  # prefill4096: one moe_prefill_device call (tcgen05 GEMMs) per step and rank
         from flash_deepseek_b200 import ep
         world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -724,9 +783,12 @@ def run_extra(args):
             "scaling": "strong", "vs_baseline": None,
             "dtype": ("fp16 operands (dequantized weights, activations) on tcgen05, fp32 accumulation"
                       if args.workload == "prefill4096" else
+                      "fp16 weights, fp32 activations, fp32 accumulation" if args.workload == "dense_b1" else
                       "int8 tensor-core products of Q4_K/Q6_K integers and 21-bit activation planes (exact), fp32 "
                       "accumulation"),
-            "data": "synthetic: random-init N(0,0.02) weights quantized on device, N(0,1) tokens",
+            "data": ("synthetic: random-init N(0,0.02) weights rounded to fp16 on device, N(0,1) tokens"
+                     if args.workload == "dense_b1" else
+                     "synthetic: random-init N(0,0.02) weights quantized on device, N(0,1) tokens"),
             "config": dict({"workload": W["name"], "global_batch": W["B"], "hidden": H, "intermediate": I,
                             "experts": E, "parallelism": "ep1"}, **extra),
             "roofline": roof, "e2e": e2e, "gpu_launches": int(launches), "clocks": clk.summary()}
@@ -796,12 +858,13 @@ def other_configs(args):
     GPU after the default one (each in its own context, with its own warm-up,
     timed loop, L2 handling and clock sampling, as its --workload line would
     be): config 2 (one token), config 1 (one expert per call), config 5 (4096-
-    token prefill) and config 4 (the 58-layer stack at batch 1)."""
+    token prefill), config 4 (the 58-layer stack at batch 1) and the dense FFN
+    layers 0-2 at batch 1."""
     keep = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "dtype", "roofline", "roofline_down",
             "roofline_tc", "roofline_phases",
             "phase_ms", "e2e", "gpu_launches", "clocks", "config")
     out = {}
-    for wl, steps in (("decode_b1", 100), ("expert1", 256), ("prefill4096", 3), ("stack_b1", 3)):
+    for wl, steps in (("decode_b1", 100), ("expert1", 256), ("prefill4096", 3), ("stack_b1", 3), ("dense_b1", 100)):
         a = argparse.Namespace(**vars(args))
         a.workload, a.steps, a.warmup, a.no_cpu = wl, steps, 3, True
         try:

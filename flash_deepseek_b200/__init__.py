@@ -24,8 +24,11 @@ import numpy as np
 
 from ._lib import MoeConfigC, load as load_library
 
+TYPE_F32 = 0  # GGML_TYPE_F32
+TYPE_F16 = 1  # GGML_TYPE_F16
 TYPE_Q4_K = 12  # GGML_TYPE_Q4_K (gguf.h:59)
 TYPE_Q6_K = 14  # GGML_TYPE_Q6_K (gguf.h:61)
+TYPE_BF16 = 30  # GGML_TYPE_BF16
 QK_K = 256
 BLOCK_BYTES = {TYPE_Q4_K: 144, TYPE_Q6_K: 210}
 
@@ -229,6 +232,38 @@ class MoE:
         self._check(self.lib.moe_read_expert(self.ctx, layer, expert, _ptr(out), n), "moe_read_expert")
         return out
 
+    # ------------------------------------------------------ dense FFN layers
+    def load_dense_layer(self, layer: int, gate, gate_type: int, up, up_type: int, down, down_type: int,
+                         intermediate: int):
+        """The dense FFN of a first layer (infer.m:1786-1793) from GGUF bytes
+        (numpy arrays of any dtype, read as raw bytes)."""
+        bufs = [np.ascontiguousarray(b).view(np.uint8) for b in (gate, up, down)]
+        self._check(self.lib.moe_load_dense_layer(self.ctx, layer, intermediate, _ptr(bufs[0]), gate_type,
+                                                  _ptr(bufs[1]), up_type, _ptr(bufs[2]), down_type),
+                    "moe_load_dense_layer")
+
+    def init_dense_synthetic(self, layer: int, intermediate: int, seed: int = 0, w_sigma: float = 0.02):
+        self._check(self.lib.moe_init_dense_synthetic(self.ctx, layer, intermediate, seed, w_sigma),
+                    "moe_init_dense_synthetic")
+
+    def read_dense_weight(self, layer: int, which: int, intermediate: int) -> np.ndarray:
+        """Matrix `which` (0 gate, 1 up, 2 down) as fp16 bits (uint16)."""
+        out = np.empty(intermediate * self.cfg.hidden, np.uint16)
+        self._check(self.lib.moe_read_dense_weight(self.ctx, layer, which, _ptr(out), out.nbytes),
+                    "moe_read_dense_weight")
+        return out.reshape((intermediate, self.cfg.hidden) if which < 2 else (self.cfg.hidden, intermediate))
+
+    def dense_forward(self, layer: int, h_post):
+        h = _f32(h_post).reshape(-1, self.cfg.hidden)
+        out = np.empty_like(h)
+        self._check(self.lib.moe_dense_forward(self.ctx, layer, _ptr(h), h.shape[0], _ptr(out)),
+                    "moe_dense_forward")
+        return out
+
+    def dense_forward_device(self, layer: int, d_h, n_tokens: int, d_out, stream=None):
+        self._check(self.lib.moe_dense_forward_device(self.ctx, layer, _ptr(d_h), n_tokens, _ptr(d_out),
+                                                      _ptr(stream)), "moe_dense_forward_device")
+
     # --------------------------------------------------------------- forward
     def forward(self, layer: int, h_post):
         """MoE block on host arrays: returns (out [T,H], idx [T,K], w [T,K])."""
@@ -327,5 +362,5 @@ def dequantize_row_q6_K(src, n: int) -> np.ndarray:
     return out
 
 
-__all__ = ["MoE", "MoeConfig", "MoeError", "TYPE_Q4_K", "TYPE_Q6_K", "dequantize_row_q4_K", "dequantize_row_q6_K",
+__all__ = ["MoE", "MoeConfig", "MoeError", "TYPE_BF16", "TYPE_F16", "TYPE_F32", "TYPE_Q4_K", "TYPE_Q6_K", "dequantize_row_q4_K", "dequantize_row_q6_K",
            "get_unique_id", "load_library", "row_bytes"]

@@ -44,6 +44,11 @@ SIGNATURES = {
     "moe_read_expert": (C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_size_t]),
     "moe_expert_bytes": (C.c_size_t, [_vp, C.c_int]),
     "moe_write_layer_packed": (C.c_int, [_vp, C.c_int, C.c_char_p]),
+    "moe_load_dense_layer": (C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_int, _vp, C.c_int, _vp, C.c_int]),
+    "moe_init_dense_synthetic": (C.c_int, [_vp, C.c_int, C.c_int, C.c_uint64, C.c_double]),
+    "moe_read_dense_weight": (C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_size_t]),
+    "moe_dense_forward": (C.c_int, [_vp, C.c_int, _vp, C.c_int, _vp]),
+    "moe_dense_forward_device": (C.c_int, [_vp, C.c_int, _vp, C.c_int, _vp, _vp]),
     "moe_forward": (C.c_int, [_vp, C.c_int, _vp, C.c_int, _vp, _vp, _vp]),
     "moe_forward_device": (C.c_int, [_vp, C.c_int, _vp, C.c_int, _vp, _vp, _vp, _vp]),
     "moe_check_error": (C.c_int, [_vp]),

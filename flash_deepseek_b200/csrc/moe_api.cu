@@ -74,6 +74,14 @@ struct moe_ctx {
     int n_split = 0;
     std::vector<MoeLayerDev> layers;
     std::vector<size_t> layer_down_bytes;
+    // dense FFN layers (moe_dense.cu): [gate][up][down] fp16, intermediate Id
+    struct DenseDev {
+        __half *w = nullptr;
+        int Id = 0;
+    };
+    std::vector<DenseDev> dense;
+    float *dense_act = nullptr;  // [max_tok x Id] of the widest dense layer
+    size_t dense_act_n = 0;
     // workspace
     float *part = nullptr, *logits = nullptr, *d_in = nullptr, *d_out = nullptr, *h_post = nullptr;
     int *rl_counters = nullptr;
@@ -426,6 +434,7 @@ moe_ctx *moe_create(const moe_config *cfg, int device, int rank, int world_size,
     c->max_tok = k.max_tokens;
     c->max_rows = world_size * k.max_tokens;
     c->layers.assign(k.n_layers, MoeLayerDev{});
+    c->dense.assign(k.n_layers, moe_ctx::DenseDev{});
     c->layer_down_bytes.assign(k.n_layers, 0);
     if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess || ctx_alloc(c) != MOE_OK) {
         fprintf(stderr, "[moe_cuda] ERROR: moe_create: allocation failed: %s\n", c->err.c_str());
@@ -480,6 +489,8 @@ void moe_destroy(moe_ctx *c) {
         cudaFree(L.logit_bias);
         cudaFree(L.norm);
     }
+    for (auto &D : c->dense) cudaFree(D.w);
+    cudaFree(c->dense_act);
     void *bufs[] = {c->part, c->logits, c->rl_counters, c->d_in, c->d_out, c->h_post, c->idx, c->wts, c->idx_given, c->w_given, c->bias_tmp, c->xop, c->plan.counts,
                     c->plan.pair_expert, c->plan.pair_token, c->plan.pair_w, c->plan.chunk_expert,
                     c->plan.chunk_pair0, c->plan.chunk_ntok, c->plan.chunk_order, c->plan.slot_pair, c->plan.error, c->counter, c->act,
@@ -511,6 +522,8 @@ static int layer_alloc(moe_ctx *c, int layer, int down_type, int sh_down_type) {
     CK(cudaSetDevice(c->device));
     MoeLayerDev &L = c->layers[layer];
     const int H = c->d.H, I = c->d.I, E = c->d.E;
+    cudaFree(c->dense[layer].w);  // a slot holds a MoE block or a dense FFN
+    c->dense[layer] = moe_ctx::DenseDev{};
     L.gate_bytes = row_bytes(MOE_TYPE_Q4_K, H) * I;
     const size_t db = row_bytes(down_type, I) * H, sdb = row_bytes(sh_down_type, I) * H;
     const size_t stride = (2 * L.gate_bytes + (db > sdb ? db : sdb) + 255) & ~(size_t)255;
@@ -732,6 +745,129 @@ int moe_set_norm_weight(moe_ctx *c, int layer, const float *w) {
     MoeLayerDev &L = c->layers[layer];
     if (!L.norm) CK(cudaMalloc((void **)&L.norm, sizeof(float) * c->d.H));
     CK(upload_sync(c, L.norm, w, sizeof(float) * c->d.H));
+    return MOE_OK;
+}
+
+// ------------------------------------------------------------ dense layers
+static size_t type_bytes(int type, size_t n) {
+    switch (type) {
+    case MOE_TYPE_F32: return n * 4;
+    case MOE_TYPE_F16:
+    case MOE_TYPE_BF16: return n * 2;
+    case MOE_TYPE_Q4_K: return n / MOE_QK * MOE_Q4K_BYTES;
+    case MOE_TYPE_Q6_K: return n / MOE_QK * MOE_Q6K_BYTES;
+    default: return 0;
+    }
+}
+
+// fp16 storage and activation scratch of dense layer `layer`; frees the
+// slot's MoE experts
+static int dense_alloc(moe_ctx *c, int layer, int Id) {
+    if (layer < 0 || layer >= (int)c->layers.size()) return fail(c, MOE_ERR_ARG, "layer %d out of range", layer);
+    if (!moe_dense_shape_ok(c->d.H, Id))
+        return fail(c, MOE_ERR_ARG, "dense FFN needs hidden %% 256 == 0, intermediate %% 256 == 0 and %zu bytes of "
+                                    "activations per pass within shared memory (hidden %d, intermediate %d)",
+                    moe_dense_smem_need(c->d.H, Id), c->d.H, Id);
+    CK(cudaStreamSynchronize(c->stream));
+    drop_graphs(c);
+    MoeLayerDev &L = c->layers[layer];
+    cudaFree(L.experts);
+    L.experts = nullptr;
+    moe_ctx::DenseDev &D = c->dense[layer];
+    if (!D.w || D.Id != Id) {
+        cudaFree(D.w);
+        D.w = nullptr;
+        CK(cudaMalloc((void **)&D.w, 3 * (size_t)Id * c->d.H * sizeof(__half)));
+    }
+    D.Id = Id;
+    const size_t act_n = (size_t)c->max_tok * Id;
+    if (act_n > c->dense_act_n) {
+        cudaFree(c->dense_act);
+        c->dense_act = nullptr;
+        c->dense_act_n = 0;
+        CK(cudaMalloc((void **)&c->dense_act, act_n * sizeof(float)));
+        c->dense_act_n = act_n;
+    }
+    return MOE_OK;
+}
+
+int moe_load_dense_layer(moe_ctx *c, int layer, int Id, const void *gate, int gate_type, const void *up, int up_type,
+                         const void *down, int down_type) {
+    if (!c || !gate || !up || !down) return MOE_ERR_ARG;
+    DeviceScope ds(c->device);
+    const size_t n = (size_t)Id * c->d.H;
+    const int types[3] = {gate_type, up_type, down_type};
+    for (int t : types)
+        if (!type_bytes(t, 256) || Id <= 0)
+            return fail(c, MOE_ERR_ARG, "dense matrices must be F32 (0), F16 (1), BF16 (30), Q4_K (12) or Q6_K (14)");
+    int rc = dense_alloc(c, layer, Id);
+    if (rc) return rc;
+    const void *src[3] = {gate, up, down};
+    size_t raw = 0;
+    bool quant = false;
+    for (int t : types) {
+        raw = std::max(raw, type_bytes(t, n));
+        quant |= t == MOE_TYPE_Q4_K || t == MOE_TYPE_Q6_K;
+    }
+    uint8_t *tmp = nullptr;
+    float *tf = nullptr;
+    CK(cudaMalloc((void **)&tmp, raw));
+    if (quant && cudaMalloc((void **)&tf, n * sizeof(float)) != cudaSuccess) {
+        cudaFree(tmp);
+        return fail(c, MOE_ERR_CUDA, "dense layer %d: no room for the dequant scratch", layer);
+    }
+    cudaError_t e = cudaSuccess;
+    for (int m = 0; m < 3 && e == cudaSuccess; m++) {
+        e = cudaMemcpyAsync(tmp, src[m], type_bytes(types[m], n), cudaMemcpyHostToDevice, c->stream);
+        if (e == cudaSuccess) {
+            moe_launch_to_f16(types[m], tmp, c->dense[layer].w + m * n, n, tf, c->stream, &c->launches);
+            e = cudaGetLastError();
+        }
+        if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);  // tmp is reused by the next matrix
+    }
+    cudaFree(tmp);
+    cudaFree(tf);
+    if (e != cudaSuccess) return fail(c, MOE_ERR_CUDA, "dense layer %d: %s", layer, cudaGetErrorString(e));
+    return MOE_OK;
+}
+
+int moe_init_dense_synthetic(moe_ctx *c, int layer, int Id, uint64_t seed, double w_sigma) {
+    if (!c) return MOE_ERR_ARG;
+    DeviceScope ds(c->device);
+    int rc = dense_alloc(c, layer, Id);
+    if (rc) return rc;
+    const size_t n = (size_t)Id * c->d.H;
+    float *tf = nullptr;
+    CK(cudaMalloc((void **)&tf, n * sizeof(float)));
+    const int kinds[3] = {SYN_GATE, SYN_UP, SYN_DOWN};
+    cudaError_t e = cudaSuccess;
+    for (int m = 0; m < 3 && e == cudaSuccess; m++) {
+        moe_launch_synth_f32(seed, synth_stream(layer, c->d.E + 1, kinds[m]), n, w_sigma, tf, c->stream,
+                             &c->launches);
+        moe_launch_to_f16(MOE_TYPE_F32, tf, c->dense[layer].w + m * n, n, nullptr, c->stream, &c->launches);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    cudaFree(tf);
+    if (e != cudaSuccess) return fail(c, MOE_ERR_CUDA, "synthetic dense layer %d: %s", layer, cudaGetErrorString(e));
+    return MOE_OK;
+}
+
+static int check_dense(moe_ctx *c, int layer) {
+    if (layer < 0 || layer >= (int)c->dense.size() || !c->dense[layer].w)
+        return fail(c, MOE_ERR_STATE, "dense layer %d not loaded", layer);
+    return MOE_OK;
+}
+
+int moe_read_dense_weight(moe_ctx *c, int layer, int which, void *dst, size_t dst_size) {
+    if (!c || !dst || which < 0 || which > 2) return MOE_ERR_ARG;
+    DeviceScope ds(c->device);
+    int rc = check_dense(c, layer);
+    if (rc) return rc;
+    const size_t n = (size_t)c->dense[layer].Id * c->d.H;
+    if (dst_size < n * sizeof(__half)) return fail(c, MOE_ERR_ARG, "dst_size %zu < %zu", dst_size, n * 2);
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaMemcpy(dst, c->dense[layer].w + which * n, n * sizeof(__half), cudaMemcpyDeviceToHost));
     return MOE_OK;
 }
 
@@ -1272,6 +1408,38 @@ int moe_shared_forward(moe_ctx *c, int layer, const float *h, int T, float *sd) 
     return finish_sync(c);
 }
 
+int moe_dense_forward_device(moe_ctx *c, int layer, const float *d_h, int T, float *d_out, void *stream) {
+    if (!c) return MOE_ERR_ARG;
+    DeviceScope ds(c->device);
+    int rc = check_dense(c, layer);
+    if (rc) return rc;
+    if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
+    if (T > 0 && (!d_h || !d_out || ((uintptr_t)d_h & 15) || ((uintptr_t)d_out & 15)))
+        return fail(c, MOE_ERR_ARG, "moe_dense_forward_device: null or not 16-byte aligned buffer");
+    cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    const moe_ctx::DenseDev &D = c->dense[layer];
+    moe_launch_dense_ffn(D.w, c->d.H, D.Id, d_h, T, c->dense_act, nullptr, d_out, s, &c->launches);
+    CK(cudaGetLastError());
+    return MOE_OK;
+}
+
+int moe_dense_forward(moe_ctx *c, int layer, const float *h, int T, float *out) {
+    if (!c) return MOE_ERR_ARG;
+    if (T > 0 && (!h || !out)) return fail(c, MOE_ERR_ARG, "moe_dense_forward: null pointer");
+    int rc = check_dense(c, layer);
+    if (rc) return rc;
+    if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
+    if (T == 0) return MOE_OK;
+    DeviceScope ds(c->device);
+    const size_t n = (size_t)T * c->d.H;
+    CK(cudaMemcpyAsync(c->d_in, h, n * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    rc = moe_dense_forward_device(c, layer, c->d_in, T, c->d_out, c->stream);
+    if (rc) return rc;
+    rc = copy_out(c, c->stream, false, {{out, c->d_out, n * sizeof(float)}});
+    if (rc) return rc;
+    return finish_sync(c);
+}
+
 int moe_route(moe_ctx *c, const float *logits, const float *bias, int T, int *idx, float *w) {
     if (!c) return MOE_ERR_ARG;
     if (T > 0 && (!logits || !idx || !w)) return fail(c, MOE_ERR_ARG, "moe_route: null pointer");
@@ -1430,11 +1598,15 @@ int moe_forward_stack_device(moe_ctx *c, int first, int n_layers, float *d_hidde
     if (T > 0 && !d_hidden) return fail(c, MOE_ERR_ARG, "moe_forward_stack_device: null hidden");
     if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
     cudaStream_t s = stream ? (cudaStream_t)stream : c->stream;
+    if (T > 0 && ((uintptr_t)d_hidden & 15)) return fail(c, MOE_ERR_ARG, "hidden buffer not 16-byte aligned");
+    bool any_moe = false;
     for (int l = first; l < first + n_layers; l++) {
-        const int rc = check_layer(c, l);
+        const bool dense = l >= 0 && l < (int)c->dense.size() && c->dense[l].w;
+        const int rc = dense ? MOE_OK : check_layer(c, l);
         if (rc) return rc;
+        any_moe |= !dense;
     }
-    int rc = ep_usable(c);
+    int rc = any_moe ? ep_usable(c) : MOE_OK;
     if (rc) return rc;
     // the whole stack is one launch sequence (one graph once replayed)
     const moe_ctx::GraphSig sig{1, first, n_layers, T, d_hidden, nullptr, s};
@@ -1444,6 +1616,12 @@ int moe_forward_stack_device(moe_ctx *c, int first, int n_layers, float *d_hidde
             if (T > 0)
                 moe_launch_rmsnorm(d_hidden, c->layers[l].norm, c->h_post, T, c->d.H, c->cfg.rms_eps, s,
                                    &c->launches);
+            if (c->dense[l].w) {  // every rank runs its own tokens on its copy of the layer
+                moe_launch_dense_ffn(c->dense[l].w, c->d.H, c->dense[l].Id, c->h_post, T, c->dense_act, d_hidden,
+                                     d_hidden, s, &c->launches);
+                if (c->hits) CK(cudaMemsetAsync(c->hits + l, 0, sizeof(int), s));
+                continue;
+            }
             if (c->world > 1) r = run_ep(c, l, c->h_post, T, nullptr, nullptr, d_hidden, d_hidden, s);
             else if (T > 0) r = run_local(c, l, c->h_post, T, nullptr, nullptr, 1, 1, d_hidden, d_hidden, s);
             if (r) return r;

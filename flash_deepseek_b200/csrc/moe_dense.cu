@@ -1,0 +1,267 @@
+// moe_dense.cu -- the dense FFN of DeepSeek-V3's first layers (0-2), the
+// other FFN half of a decoder layer next to the MoE block (infer.m:1852-1868).
+//
+// Weights are kept as fp16 in HBM, rounded from whatever the GGUF holds
+// (F32, F16, BF16, Q4_K, Q6_K) the way the reference's dequant_tensor_f16
+// does (infer.m:314-348, 519-538); activations stay fp32 and the products
+// accumulate in fp32, as mv_f16 (infer.m:459-516) and silu_mul
+// (infer.m:378-383) do.
+//
+//   k_dense_gateup  g = Wg x, u = Wu x, act = silu(g) * u   (fp32 [T x Id])
+//   k_dense_down    out = Wd act (+ residual)               (fp32 [T x H])
+//
+// Decode is a pass over 3 * Id * H * 2 bytes of weights (DeepSeek-V3:
+// 792.7 MB per layer), so both kernels are HBM streams: one warp per output
+// row, 16-byte non-allocating weight loads, several in flight per lane, the
+// tokens' activations staged once per CTA in shared memory, persistent CTAs
+// sized by occupancy over all SMs.  Up to DN_TT_GU (gate/up) and DN_TT_D
+// (down) tokens share one weight pass; larger batches take more passes.
+#include <cuda_fp16.h>
+#include <math.h>
+
+#include "../../include/moe_cuda.h"
+#include "moe_common.cuh"
+#include "moe_internal.h"
+
+#define LAUNCH_COUNT(p) \
+    do {                \
+        if (p) (*(p))++; \
+    } while (0)
+
+namespace {
+
+constexpr int DN_WARPS = 8;
+constexpr int DN_THREADS = DN_WARPS * 32;
+constexpr int DN_TT_GU = 4;   // tokens per weight pass, gate/up
+constexpr int DN_TT_D = 2;    // tokens per weight pass, down
+constexpr int DN_U_GU = 4;    // 16-byte loads in flight per lane and matrix, gate/up
+constexpr int DN_U_D = 8;     // the same, down
+
+__device__ __forceinline__ uint4 ld_weight16(const uint4 *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+// acc += sum over the 8 halves of w times xs[0..8)
+__device__ __forceinline__ float dot8(const uint4 &w, const float *xs, float acc) {
+    const float4 x0 = *reinterpret_cast<const float4 *>(xs);
+    const float4 x1 = *reinterpret_cast<const float4 *>(xs + 4);
+    const float2 w0 = __half22float2(*reinterpret_cast<const __half2 *>(&w.x));
+    const float2 w1 = __half22float2(*reinterpret_cast<const __half2 *>(&w.y));
+    const float2 w2 = __half22float2(*reinterpret_cast<const __half2 *>(&w.z));
+    const float2 w3 = __half22float2(*reinterpret_cast<const __half2 *>(&w.w));
+    acc = fmaf(w0.x, x0.x, acc);
+    acc = fmaf(w0.y, x0.y, acc);
+    acc = fmaf(w1.x, x0.z, acc);
+    acc = fmaf(w1.y, x0.w, acc);
+    acc = fmaf(w2.x, x1.x, acc);
+    acc = fmaf(w2.y, x1.y, acc);
+    acc = fmaf(w3.x, x1.z, acc);
+    acc = fmaf(w3.y, x1.w, acc);
+    return acc;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// the tokens [t0, t0 + tt) of x [T x cols] into shared memory (cols % 4 == 0)
+__device__ __forceinline__ void stage_rows(float *xs, const float *__restrict__ x, int t0, int tt, int cols) {
+    const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)t0 * cols);
+    float4 *dst = reinterpret_cast<float4 *>(xs);
+    const int n4 = tt * cols / 4;
+    for (int i = threadIdx.x; i < n4; i += blockDim.x) dst[i] = src[i];
+}
+
+// One warp per intermediate row r: g = Wg[r] . x, u = Wu[r] . x for up to
+// DN_TT_GU tokens per pass, act[t][r] = g / (1 + exp(-g)) * u (infer.m:378-383).
+// Lane l reads the 16-byte vectors l, l + 32, ... of both rows (H % 256 == 0).
+__global__ void __launch_bounds__(DN_THREADS, 2) k_dense_gateup(const __half *__restrict__ Wg,
+                                                             const __half *__restrict__ Wu,
+                                                             const float *__restrict__ x, int T, int H, int Id,
+                                                             float *__restrict__ act) {
+    extern __shared__ float4 dn_smem[];
+    float *xs = reinterpret_cast<float *>(dn_smem);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nv = H >> 8;
+    for (int t0 = 0; t0 < T; t0 += DN_TT_GU) {
+        const int tt = min(DN_TT_GU, T - t0);
+        __syncthreads();
+        stage_rows(xs, x, t0, tt, H);
+        __syncthreads();
+        for (int r = blockIdx.x * DN_WARPS + warp; r < Id; r += gridDim.x * DN_WARPS) {
+            float ag[DN_TT_GU], au[DN_TT_GU];
+#pragma unroll
+            for (int t = 0; t < DN_TT_GU; t++) ag[t] = au[t] = 0.0f;
+            const uint4 *pg = reinterpret_cast<const uint4 *>(Wg + (size_t)r * H) + lane;
+            const uint4 *pu = reinterpret_cast<const uint4 *>(Wu + (size_t)r * H) + lane;
+            const float *xl = xs + lane * 8;
+            int i = 0;
+            for (; i + DN_U_GU <= nv; i += DN_U_GU) {
+                uint4 g[DN_U_GU], u[DN_U_GU];
+#pragma unroll
+                for (int j = 0; j < DN_U_GU; j++) {
+                    g[j] = ld_weight16(pg + (i + j) * 32);
+                    u[j] = ld_weight16(pu + (i + j) * 32);
+                }
+#pragma unroll
+                for (int j = 0; j < DN_U_GU; j++)
+#pragma unroll
+                    for (int t = 0; t < DN_TT_GU; t++)
+                        if (t < tt) {
+                            const float *xp = xl + (size_t)t * H + (i + j) * 256;
+                            ag[t] = dot8(g[j], xp, ag[t]);
+                            au[t] = dot8(u[j], xp, au[t]);
+                        }
+            }
+            for (; i < nv; i++) {
+                const uint4 g = ld_weight16(pg + i * 32), u = ld_weight16(pu + i * 32);
+#pragma unroll
+                for (int t = 0; t < DN_TT_GU; t++)
+                    if (t < tt) {
+                        const float *xp = xl + (size_t)t * H + i * 256;
+                        ag[t] = dot8(g, xp, ag[t]);
+                        au[t] = dot8(u, xp, au[t]);
+                    }
+            }
+#pragma unroll
+            for (int t = 0; t < DN_TT_GU; t++)
+                if (t < tt) {
+                    const float gs = warp_sum(ag[t]), us = warp_sum(au[t]);
+                    if (lane == 0) act[(size_t)(t0 + t) * Id + r] = (gs / (1.0f + expf(-gs))) * us;
+                }
+        }
+    }
+}
+
+// One warp per hidden row r: out[t][r] = (residual[t][r]) + Wd[r] . act[t]
+// for up to DN_TT_D tokens per pass (Id % 256 == 0).  residual may be out
+// itself (the layer stack's hidden state): each element is read and written
+// by the same lane.
+__global__ void __launch_bounds__(DN_THREADS) k_dense_down(const __half *__restrict__ Wd,
+                                                           const float *__restrict__ act, int T, int H, int Id,
+                                                           const float *residual, float *out) {
+    extern __shared__ float4 dn_smem[];
+    float *as = reinterpret_cast<float *>(dn_smem);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nv = Id >> 8;
+    for (int t0 = 0; t0 < T; t0 += DN_TT_D) {
+        const int tt = min(DN_TT_D, T - t0);
+        __syncthreads();
+        stage_rows(as, act, t0, tt, Id);
+        __syncthreads();
+        for (int r = blockIdx.x * DN_WARPS + warp; r < H; r += gridDim.x * DN_WARPS) {
+            float acc[DN_TT_D];
+#pragma unroll
+            for (int t = 0; t < DN_TT_D; t++) acc[t] = 0.0f;
+            const uint4 *pw = reinterpret_cast<const uint4 *>(Wd + (size_t)r * Id) + lane;
+            const float *al = as + lane * 8;
+            int i = 0;
+            for (; i + DN_U_D <= nv; i += DN_U_D) {
+                uint4 w[DN_U_D];
+#pragma unroll
+                for (int j = 0; j < DN_U_D; j++) w[j] = ld_weight16(pw + (i + j) * 32);
+#pragma unroll
+                for (int j = 0; j < DN_U_D; j++)
+#pragma unroll
+                    for (int t = 0; t < DN_TT_D; t++)
+                        if (t < tt) acc[t] = dot8(w[j], al + (size_t)t * Id + (i + j) * 256, acc[t]);
+            }
+            for (; i < nv; i++) {
+                const uint4 w = ld_weight16(pw + i * 32);
+#pragma unroll
+                for (int t = 0; t < DN_TT_D; t++)
+                    if (t < tt) acc[t] = dot8(w, al + (size_t)t * Id + i * 256, acc[t]);
+            }
+#pragma unroll
+            for (int t = 0; t < DN_TT_D; t++)
+                if (t < tt) {
+                    const float s = warp_sum(acc[t]);
+                    if (lane == 0) {
+                        const size_t o = (size_t)(t0 + t) * H + r;
+                        out[o] = residual ? residual[o] + s : s;
+                    }
+                }
+        }
+    }
+}
+
+// GGUF tensor values to fp16 (RNE): F32 / BF16 sources, or fp32 from the
+// Q4_K / Q6_K dequant twins
+__global__ void k_f32_to_f16(const float *__restrict__ src, __half *__restrict__ dst, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        dst[i] = __float2half_rn(src[i]);
+}
+__global__ void k_bf16_to_f16(const uint16_t *__restrict__ src, __half *__restrict__ dst, size_t n) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        dst[i] = __float2half_rn(__uint_as_float((uint32_t)src[i] << 16));
+}
+
+int dense_sms() {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+}
+
+// persistent CTAs: as many as fit on every SM with this much shared memory
+int dense_ctas(const void *fn, size_t smem) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, DN_THREADS, smem) != cudaSuccess || per_sm < 1)
+        per_sm = 1;
+    return per_sm * dense_sms();
+}
+
+}  // namespace
+
+size_t moe_dense_smem_need(int H, int Id) {
+    const size_t a = (size_t)DN_TT_GU * H * sizeof(float), b = (size_t)DN_TT_D * Id * sizeof(float);
+    return a > b ? a : b;
+}
+
+int moe_dense_shape_ok(int H, int Id) {
+    return H > 0 && Id > 0 && H % 256 == 0 && Id % 256 == 0 && moe_dense_smem_need(H, Id) <= MOE_DENSE_SMEM_MAX;
+}
+
+void moe_launch_dense_ffn(const __half *w, int H, int Id, const float *x, int T, float *act, const float *residual,
+                          float *out, cudaStream_t s, uint64_t *launches) {
+    if (T <= 0) return;
+    const __half *Wg = w, *Wu = w + (size_t)Id * H, *Wd = w + 2 * (size_t)Id * H;
+    const size_t sg = (size_t)min(T, DN_TT_GU) * H * sizeof(float);
+    const size_t sd = (size_t)min(T, DN_TT_D) * Id * sizeof(float);
+    static size_t done_gu[MOE_MAX_DEVICES], done_d[MOE_MAX_DEVICES];
+    moe_smem_limit(k_dense_gateup, sg, done_gu);
+    moe_smem_limit(k_dense_down, sd, done_d);
+    const int gg = min(dense_ctas((const void *)k_dense_gateup, sg), (Id + DN_WARPS - 1) / DN_WARPS);
+    const int gd = min(dense_ctas((const void *)k_dense_down, sd), (H + DN_WARPS - 1) / DN_WARPS);
+    k_dense_gateup<<<gg, DN_THREADS, sg, s>>>(Wg, Wu, x, T, H, Id, act);
+    LAUNCH_COUNT(launches);
+    k_dense_down<<<gd, DN_THREADS, sd, s>>>(Wd, act, T, H, Id, residual, out);
+    LAUNCH_COUNT(launches);
+}
+
+void moe_launch_to_f16(int type, const void *src, __half *dst, size_t n, float *tmp, cudaStream_t s,
+                       uint64_t *launches) {
+    const int grid = 4 * dense_sms();
+    if (type == MOE_TYPE_F16) {
+        cudaMemcpyAsync(dst, src, n * sizeof(__half), cudaMemcpyDeviceToDevice, s);
+        return;
+    }
+    if (type == MOE_TYPE_BF16) {
+        k_bf16_to_f16<<<grid, 256, 0, s>>>((const uint16_t *)src, dst, n);
+        LAUNCH_COUNT(launches);
+        return;
+    }
+    const float *f = (const float *)src;
+    if (type == MOE_TYPE_Q4_K || type == MOE_TYPE_Q6_K) {
+        moe_launch_dequant(type, (const uint8_t *)src, tmp, n, s, launches);
+        f = tmp;
+    }
+    k_f32_to_f16<<<grid, 256, 0, s>>>(f, dst, n);
+    LAUNCH_COUNT(launches);
+}

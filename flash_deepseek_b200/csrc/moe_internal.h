@@ -276,6 +276,17 @@ void moe_launch_synth_quant(int type, uint64_t seed, uint64_t stream, int rows, 
                             uint8_t *dst, cudaStream_t s, uint64_t *launches);
 void moe_launch_synth_f32(uint64_t seed, uint64_t stream, size_t n, double sigma, float *dst, cudaStream_t s,
                           uint64_t *launches);
+// dense FFN layers (moe_dense.cu): w = [gate Id x H][up Id x H][down H x Id]
+// fp16; act [T x Id] fp32 scratch; out = residual (may be null) + FFN(x)
+#define MOE_DENSE_SMEM_MAX (227 * 1024)
+size_t moe_dense_smem_need(int H, int Id);
+int moe_dense_shape_ok(int H, int Id);
+void moe_launch_dense_ffn(const __half *w, int H, int Id, const float *x, int T, float *act, const float *residual,
+                          float *out, cudaStream_t s, uint64_t *launches);
+// n values of a GGUF tensor of `type` (device memory) to fp16; tmp holds n
+// floats for Q4_K / Q6_K
+void moe_launch_to_f16(int type, const void *src, __half *dst, size_t n, float *tmp, cudaStream_t s,
+                       uint64_t *launches);
 void moe_launch_prep_rows(const float *recv, const int *meta, int meta_w, int R, const float *local, int T, int H,
                           uint8_t *xop, cudaStream_t s, uint64_t *launches);
 // expert parallel (moe_ep.cu)

@@ -42,8 +42,11 @@
 extern "C" {
 #endif
 
+#define MOE_TYPE_F32 0   /* GGML_TYPE_F32 */
+#define MOE_TYPE_F16 1   /* GGML_TYPE_F16 */
 #define MOE_TYPE_Q4_K 12 /* GGML_TYPE_Q4_K, gguf.h:59 */
 #define MOE_TYPE_Q6_K 14 /* GGML_TYPE_Q6_K, gguf.h:61 */
+#define MOE_TYPE_BF16 30 /* GGML_TYPE_BF16 */
 
 #define MOE_OK 0
 #define MOE_ERR_ARG (-1)      /* bad argument / shape */
@@ -168,6 +171,35 @@ size_t moe_expert_bytes(const moe_ctx *ctx, int layer);
  * file. */
 int moe_write_layer_packed(moe_ctx *ctx, int layer, const char *path);
 
+/* ------------------------------------------------------- dense FFN layers */
+/* The dense FFN of the first layers (L < 3 in DeepSeek-V3: FIRST_MOE_LAYER,
+ * infer.m:46), which take the place of the MoE block there.  The three
+ * matrices (GGUF blk.L.ffn_gate / ffn_up [intermediate x H], ffn_down
+ * [H x intermediate]; DENSE_INTERMEDIATE 18432, infer.m:59) are given as
+ * host bytes of GGUF type F32, F16, BF16, Q4_K or Q6_K and kept on the GPU as
+ * fp16, rounded as the reference's dequant_tensor_f16 does (infer.m:530-538,
+ * loaded at infer.m:1786-1793).  Needs hidden % 256 == 0 and
+ * intermediate % 256 == 0.  A layer slot holds either a MoE block or a dense
+ * FFN; loading one frees the other. */
+int moe_load_dense_layer(moe_ctx *ctx, int layer, int intermediate,
+                         const void *gate, int gate_type, const void *up, int up_type,
+                         const void *down, int down_type);
+/* Synthetic dense layer: fp16 of N(0, w_sigma) values from the generator of
+ * moe_init_layer_synthetic (gate / up / down streams of expert id
+ * n_experts + 1), reproducible by the oracle. */
+int moe_init_dense_synthetic(moe_ctx *ctx, int layer, int intermediate, uint64_t seed, double w_sigma);
+/* Copies matrix `which` (0 gate, 1 up, 2 down) of a dense layer back as fp16
+ * bits; dst_size >= intermediate * H * 2 bytes. */
+int moe_read_dense_weight(moe_ctx *ctx, int layer, int which, void *dst, size_t dst_size);
+/* The dense FFN of n_tokens tokens without the residual (infer.m:1855-1865,
+ * mv_f16 + silu_mul): out[t] = Wd (silu(Wg h[t]) * (Wu h[t])), fp32
+ * [n_tokens x H].  Every rank of an expert-parallel context holds the whole
+ * layer and runs its own tokens (no exchange). */
+int moe_dense_forward(moe_ctx *ctx, int layer, const float *h_post, int n_tokens, float *out);
+/* Same on device buffers (16-byte aligned), asynchronous on `stream`. */
+int moe_dense_forward_device(moe_ctx *ctx, int layer, const float *d_h_post, int n_tokens,
+                             float *d_out, void *stream);
+
 /* ---------------------------------------------------------------- forward */
 /* The full MoE block for n_tokens tokens held by this rank (host buffers):
  * out[t] = sum_k w_k E_{idx_k}(h[t]) + shared(h[t]), fp32 [n_tokens x H].
@@ -210,8 +242,9 @@ int moe_route(moe_ctx *ctx, const float *logits, const float *bias, int n_tokens
               float *exp_w);
 
 /* Stack of layers [first, first + n_layers): per layer
- *   h_post = RMSNorm(hidden) * norm_w;  hidden = hidden + MoE(h_post)
- * (infer.m:1850, 1922 with attention as identity).  hidden is updated in
+ *   h_post = RMSNorm(hidden) * norm_w;  hidden = hidden + FFN(h_post)
+ * (infer.m:1850, 1864 / 1922 with attention as identity), FFN the dense FFN
+ * of a slot loaded by moe_load_dense_layer, else the MoE block.  hidden is updated in
  * place, device buffer [n_tokens x H]. */
 int moe_forward_stack_device(moe_ctx *ctx, int first_layer, int n_layers, float *d_hidden,
                              int n_tokens, void *stream);

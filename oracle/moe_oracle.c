@@ -572,3 +572,73 @@ void or_moe_layer_given(const or_layer_cfg *cfg, const void *const *experts, con
     }
     free(pairs); free(gs); free(xs); free(g); free(eo);
 }
+
+/* ------------------------------------------------------------------------ */
+/* dense FFN layers 0-2 (infer.m:1786-1793, 1852-1868)                       */
+/* ------------------------------------------------------------------------ */
+/* dequant_tensor_full (infer.m:314-348) followed by the fp16 rounding of
+ * dequant_tensor_f16 / f32_to_f16_alloc (infer.m:519-538). */
+int or_to_f16(int type, const void *src, uint16_t *dst, size_t n) {
+    const uint16_t *h = (const uint16_t *)src;
+    const float *f = (const float *)src;
+    if (type == OR_TYPE_F16) {
+        for (size_t i = 0; i < n; i++) dst[i] = or_fp32_to_fp16(or_fp16_to_fp32(h[i]));
+        return 0;
+    }
+    if (type == OR_TYPE_F32) {
+        for (size_t i = 0; i < n; i++) dst[i] = or_fp32_to_fp16(f[i]);
+        return 0;
+    }
+    if (type == OR_TYPE_BF16) {
+        for (size_t i = 0; i < n; i++) dst[i] = or_fp32_to_fp16(bits_f((uint32_t)h[i] << 16));
+        return 0;
+    }
+    if ((type != OR_TYPE_Q4_K && type != OR_TYPE_Q6_K) || n % OR_QK) return -1;
+    float *tmp = (float *)malloc(sizeof(float) * OR_QK);
+    const size_t bb = type == OR_TYPE_Q6_K ? OR_Q6K_BYTES : OR_Q4K_BYTES;
+    for (size_t b = 0; b < n / OR_QK; b++) {
+        if (type == OR_TYPE_Q6_K) or_dequant_q6k((const uint8_t *)src + b * bb, tmp, OR_QK);
+        else or_dequant_q4k((const uint8_t *)src + b * bb, tmp, OR_QK);
+        for (int i = 0; i < OR_QK; i++) dst[b * OR_QK + i] = or_fp32_to_fp16(tmp[i]);
+    }
+    free(tmp);
+    return 0;
+}
+
+typedef struct { const uint16_t *A; const float *x; float *y; int n, dbl; } mvh_ctx;
+static void mvh_rows(void *c, long lo, long hi) {
+    mvh_ctx *m = (mvh_ctx *)c;
+    for (long r = lo; r < hi; r++) {
+        const uint16_t *row = m->A + (size_t)r * m->n;
+        if (m->dbl) {
+            double a = 0.0;
+            for (int k = 0; k < m->n; k++) a += (double)or_fp16_to_fp32(row[k]) * (double)m->x[k];
+            m->y[r] = (float)a;
+        } else {
+            float a = 0.0f;
+            for (int k = 0; k < m->n; k++) a += or_fp16_to_fp32(row[k]) * m->x[k];
+            m->y[r] = a;
+        }
+    }
+}
+/* infer.m:459-516 (NEON fp16 -> fp32 widening, fp32 FMA; rows split over
+ * worker threads) */
+void or_mv_f16(const uint16_t *A, const float *x, float *y, int m, int n, int acc_double, int n_threads) {
+    mvh_ctx c = {A, x, y, n, acc_double};
+    parallel_for(m, n_threads, mvh_rows, &c);
+}
+
+/* infer.m:1855-1865 without the residual add of 1864 */
+void or_dense_ffn(const uint16_t *gate, const uint16_t *up, const uint16_t *down, int H, int Id,
+                  const float *x, int T, float *out, int acc_double, int n_threads) {
+    float *g = (float *)malloc(sizeof(float) * (size_t)Id * 3);
+    float *u = g + Id, *a = u + Id;
+    for (int t = 0; t < T; t++) {
+        const float *xt = x + (size_t)t * H;
+        or_mv_f16(gate, xt, g, Id, H, acc_double, n_threads);
+        or_mv_f16(up, xt, u, Id, H, acc_double, n_threads);
+        or_silu_mul(g, u, a, Id);
+        or_mv_f16(down, a, out + (size_t)t * H, H, Id, acc_double, n_threads);
+    }
+    free(g);
+}

@@ -103,6 +103,26 @@ void or_moe_layer_given(const or_layer_cfg *cfg, const void *const *experts,
 
 size_t or_expert_bytes(int H, int I, int down_type);
 
+/* ---- dense FFN layers (infer.m:1786-1793, 1852-1868) ---- */
+#define OR_TYPE_F32 0
+#define OR_TYPE_F16 1
+#define OR_TYPE_BF16 30
+/* dequant_tensor_f16 (infer.m:314-348 + 530-538): n values of a GGUF tensor
+ * of `type` (F32, F16, BF16, Q4_K, Q6_K) to fp32, then each rounded to fp16
+ * (RNE, f32_to_f16_alloc infer.m:519-527).  Returns 0, or -1 on a type it
+ * does not decode (n must be a multiple of 256 for Q4_K / Q6_K). */
+int  or_to_f16(int type, const void *src, uint16_t *dst, size_t n);
+/* mv_f16 (infer.m:459-516): y = A x, A fp16 [m x n] row-major widened to
+ * fp32, fp64 (acc_double) or left-to-right fp32 accumulation. */
+void or_mv_f16(const uint16_t *A, const float *x, float *y, int m, int n,
+               int acc_double, int n_threads);
+/* The dense FFN of T tokens without the residual (infer.m:1855-1865):
+ * out[t] = Wd (silu(Wg x[t]) * (Wu x[t])); Wg, Wu fp16 [Id x H], Wd fp16
+ * [H x Id]. */
+void or_dense_ffn(const uint16_t *gate, const uint16_t *up, const uint16_t *down,
+                  int H, int Id, const float *x, int T, float *out,
+                  int acc_double, int n_threads);
+
 #ifdef __cplusplus
 }
 #endif

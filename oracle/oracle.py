@@ -17,6 +17,9 @@ LIB_PATH = os.path.join(HERE, "liboracle.so")
 REF_PATH = os.path.join(HERE, "_ref", "libref_moe.so")
 REF_GGUF_PATH = os.path.join(HERE, "_ref", "libref_gguf.so")
 
+TYPE_F32 = 0
+TYPE_F16 = 1
+TYPE_BF16 = 30
 TYPE_Q4_K = 12
 TYPE_Q6_K = 14
 QK = 256
@@ -84,6 +87,11 @@ def lib():
                                    C.c_int, C.c_int]
         L.or_moe_layer_given.argtypes = [C.POINTER(LayerCfg), C.POINTER(C.c_void_p), _f32p, C.c_int, _i32p, _f32p,
                                          _f32p, C.c_int, C.c_int]
+        _u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
+        L.or_to_f16.restype = C.c_int
+        L.or_to_f16.argtypes = [C.c_int, C.c_void_p, _u16p, C.c_size_t]
+        L.or_mv_f16.argtypes = [_u16p, _f32p, _f32p, C.c_int, C.c_int, C.c_int, C.c_int]
+        L.or_dense_ffn.argtypes = [_u16p, _u16p, _u16p, C.c_int, C.c_int, _f32p, C.c_int, _f32p, C.c_int, C.c_int]
         _lib = L
     return _lib
 
@@ -232,6 +240,34 @@ def expert_forward(blob, H, I, down_type, x, acc_double=True, threads=8):
     lib().or_expert_forward(blob[:gb], blob[gb:2 * gb], blob[2 * gb:], down_type,
                             np.ascontiguousarray(x, np.float32), H, I, eo, int(acc_double), threads)
     return eo
+
+
+def to_f16(blob, qtype: int, n: int) -> np.ndarray:
+    """A GGUF tensor of n values (F32, F16, BF16, Q4_K, Q6_K) as fp16 bits,
+    the way the reference keeps its dense FFN weights."""
+    b = np.ascontiguousarray(blob).view(np.uint8).reshape(-1)
+    out = np.empty(n, np.uint16)
+    if lib().or_to_f16(qtype, b.ctypes.data_as(C.c_void_p), out, n) != 0:
+        raise ValueError(f"type {qtype} not decodable to fp16")
+    return out
+
+
+def mv_f16(A, x, acc_double=True, threads=8):
+    A = np.ascontiguousarray(A, np.uint16)
+    m, n = A.shape
+    y = np.empty(m, np.float32)
+    lib().or_mv_f16(A, np.ascontiguousarray(x, np.float32), y, m, n, int(acc_double), threads)
+    return y
+
+
+def dense_ffn(gate, up, down, x, acc_double=True, threads=8):
+    """gate, up: fp16 bits [Id x H]; down: fp16 bits [H x Id]; x [T x H]."""
+    Id, H = gate.shape
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, H)
+    out = np.empty_like(x)
+    lib().or_dense_ffn(np.ascontiguousarray(gate, np.uint16), np.ascontiguousarray(up, np.uint16),
+                       np.ascontiguousarray(down, np.uint16), H, Id, x, x.shape[0], out, int(acc_double), threads)
+    return out
 
 
 def moe_layer(cfg: dict, experts: dict, router_w, bias, x, force_idx=None, force_w=None,

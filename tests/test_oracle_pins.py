@@ -148,3 +148,45 @@ def test_grouped_layer_equals_per_token_layer(oracle, down_type):
         ref, _, _, _ = O.moe_layer(cfg, experts, router, None, x, force_idx=idx, force_w=w, acc_double=dbl)
         got = O.moe_layer_given(cfg, experts, x, idx, w, acc_double=dbl)
         assert np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+
+
+def test_to_f16_pins(oracle):
+    """dequant_tensor_f16 (infer.m:314-348, 519-538): the fp32 value of each
+    GGUF type, rounded to fp16 to nearest even -- against numpy's float16
+    cast (IEEE RNE, subnormals and overflow included) and the gguf-py
+    golden dequant of the Q4_K / Q6_K blocks."""
+    rng = np.random.default_rng(4)
+    v = np.concatenate([rng.standard_normal(4096) * s for s in (1e-7, 1e-4, 1.0, 3e4, 1e5)]).astype(np.float32)
+    assert np.array_equal(oracle.to_f16(v, oracle.TYPE_F32, v.size), v.astype(np.float16).view(np.uint16))
+    bf = (v.view(np.uint32) >> 16).astype(np.uint16)
+    want = (bf.astype(np.uint32) << 16).view(np.float32).astype(np.float16).view(np.uint16)
+    assert np.array_equal(oracle.to_f16(bf, oracle.TYPE_BF16, bf.size), want)
+    h = v[(np.abs(v) < 6e4)].astype(np.float16)
+    assert np.array_equal(oracle.to_f16(h, oracle.TYPE_F16, h.size), h.view(np.uint16))
+    for name, qtype in (("dequant_q4k.npz", oracle.TYPE_Q4_K), ("dequant_q6k.npz", oracle.TYPE_Q6_K)):
+        g = gold(name)
+        blob, ref = g["blocks"].reshape(-1), g["expected"].reshape(-1)
+        n = ref.size
+        assert np.array_equal(oracle.to_f16(blob, qtype, n), ref.astype(np.float32).astype(np.float16).view(np.uint16))
+
+
+def test_dense_ffn_composition(oracle):
+    """infer.m:1855-1865 (mv_f16, silu_mul, mv_f16) against a float64 numpy
+    composition of the same fp16 weights; silu_mul on the fp32 projections is
+    the pinned or_silu_mul."""
+    rng = np.random.default_rng(8)
+    H, Id, T = 512, 768, 3
+    g = (rng.standard_normal((Id, H)) * 0.05).astype(np.float16)
+    u = (rng.standard_normal((Id, H)) * 0.05).astype(np.float16)
+    d = (rng.standard_normal((H, Id)) * 0.05).astype(np.float16)
+    x = rng.standard_normal((T, H)).astype(np.float32)
+    out = oracle.dense_ffn(g.view(np.uint16), u.view(np.uint16), d.view(np.uint16), x)
+    G = (x.astype(np.float64) @ g.astype(np.float64).T).astype(np.float32)
+    U = (x.astype(np.float64) @ u.astype(np.float64).T).astype(np.float32)
+    A = np.empty_like(G)
+    for t in range(T):
+        oracle.lib().or_silu_mul(np.ascontiguousarray(G[t]), np.ascontiguousarray(U[t]), A[t], Id)
+    ref = (A.astype(np.float64) @ d.astype(np.float64).T).astype(np.float32)
+    assert np.array_equal(out, ref) or float(np.max(np.abs(out - ref)) / np.max(np.abs(ref))) < 1e-6
+    y = oracle.mv_f16(g.view(np.uint16), x[0], acc_double=False)
+    assert float(np.max(np.abs(y - G[0])) / np.max(np.abs(G[0]))) < 1e-5
