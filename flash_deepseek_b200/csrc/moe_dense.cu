@@ -14,7 +14,8 @@
 // 792.7 MB per layer), so both kernels are HBM streams: one warp per output
 // row, 16-byte non-allocating weight loads, several in flight per lane, the
 // tokens' activations staged once per CTA in shared memory, persistent CTAs
-// sized by occupancy over all SMs.  Up to DN_TT_GU (gate/up) and DN_TT_D
+// sized by occupancy over all SMs; each CTA issues its first weight loads
+// before it stages the activations.  Up to DN_TT_GU (gate/up) and DN_TT_D
 // (down) tokens share one weight pass; larger batches take more passes.
 #include <cuda_fp16.h>
 #include <math.h>
@@ -35,7 +36,8 @@ constexpr int DN_THREADS = DN_WARPS * 32;
 constexpr int DN_TT_GU = 4;   // tokens per weight pass, gate/up
 constexpr int DN_TT_D = 2;    // tokens per weight pass, down
 constexpr int DN_U_GU = 4;    // 16-byte loads in flight per lane and matrix, gate/up
-constexpr int DN_U_D = 8;     // the same, down
+constexpr int DN_VD = 9;      // 16-byte loads in flight per lane, down (one row's share when Id <= 18432)
+constexpr int DN_RPC_MAX = 128;  // hidden rows per CTA of the down kernel, at most
 
 __device__ __forceinline__ uint4 ld_weight16(const uint4 *p) {
     uint4 v;
@@ -70,12 +72,22 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
-// the tokens [t0, t0 + tt) of x [T x cols] into shared memory (cols % 4 == 0)
+// the tokens [t0, t0 + tt) of x [T x cols] into shared memory (cols % 4 == 0),
+// DN_STAGE loads in flight per thread
+constexpr int DN_STAGE = 4;
 __device__ __forceinline__ void stage_rows(float *xs, const float *__restrict__ x, int t0, int tt, int cols) {
     const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)t0 * cols);
     float4 *dst = reinterpret_cast<float4 *>(xs);
     const int n4 = tt * cols / 4;
-    for (int i = threadIdx.x; i < n4; i += blockDim.x) dst[i] = src[i];
+    for (int i0 = threadIdx.x; i0 < n4; i0 += DN_STAGE * blockDim.x) {
+        float4 v[DN_STAGE];
+#pragma unroll
+        for (int j = 0; j < DN_STAGE; j++)
+            if (i0 + j * (int)blockDim.x < n4) v[j] = src[i0 + j * blockDim.x];
+#pragma unroll
+        for (int j = 0; j < DN_STAGE; j++)
+            if (i0 + j * (int)blockDim.x < n4) dst[i0 + j * blockDim.x] = v[j];
+    }
 }
 
 // One warp per intermediate row r: g = Wg[r] . x, u = Wu[r] . x for up to
@@ -89,12 +101,23 @@ __global__ void __launch_bounds__(DN_THREADS, 2) k_dense_gateup(const __half *__
     float *xs = reinterpret_cast<float *>(dn_smem);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nv = H >> 8;
+    const int r_first = blockIdx.x * DN_WARPS + warp;
     for (int t0 = 0; t0 < T; t0 += DN_TT_GU) {
         const int tt = min(DN_TT_GU, T - t0);
+        // the first row's first vectors are in flight while x is staged
+        uint4 g[DN_U_GU], u[DN_U_GU];
+        const bool pre = r_first < Id && nv >= DN_U_GU;
+        if (pre) {
+#pragma unroll
+            for (int j = 0; j < DN_U_GU; j++) {
+                g[j] = ld_weight16(reinterpret_cast<const uint4 *>(Wg + (size_t)r_first * H) + lane + j * 32);
+                u[j] = ld_weight16(reinterpret_cast<const uint4 *>(Wu + (size_t)r_first * H) + lane + j * 32);
+            }
+        }
         __syncthreads();
         stage_rows(xs, x, t0, tt, H);
         __syncthreads();
-        for (int r = blockIdx.x * DN_WARPS + warp; r < Id; r += gridDim.x * DN_WARPS) {
+        for (int r = r_first; r < Id; r += gridDim.x * DN_WARPS) {
             float ag[DN_TT_GU], au[DN_TT_GU];
 #pragma unroll
             for (int t = 0; t < DN_TT_GU; t++) ag[t] = au[t] = 0.0f;
@@ -103,11 +126,12 @@ __global__ void __launch_bounds__(DN_THREADS, 2) k_dense_gateup(const __half *__
             const float *xl = xs + lane * 8;
             int i = 0;
             for (; i + DN_U_GU <= nv; i += DN_U_GU) {
-                uint4 g[DN_U_GU], u[DN_U_GU];
+                if (!(pre && r == r_first && i == 0)) {
 #pragma unroll
-                for (int j = 0; j < DN_U_GU; j++) {
-                    g[j] = ld_weight16(pg + (i + j) * 32);
-                    u[j] = ld_weight16(pu + (i + j) * 32);
+                    for (int j = 0; j < DN_U_GU; j++) {
+                        g[j] = ld_weight16(pg + (i + j) * 32);
+                        u[j] = ld_weight16(pu + (i + j) * 32);
+                    }
                 }
 #pragma unroll
                 for (int j = 0; j < DN_U_GU; j++)
@@ -139,54 +163,74 @@ __global__ void __launch_bounds__(DN_THREADS, 2) k_dense_gateup(const __half *__
     }
 }
 
-// One warp per hidden row r: out[t][r] = (residual[t][r]) + Wd[r] . act[t]
-// for up to DN_TT_D tokens per pass (Id % 256 == 0).  residual may be out
-// itself (the layer stack's hidden state): each element is read and written
-// by the same lane.
-__global__ void __launch_bounds__(DN_THREADS) k_dense_down(const __half *__restrict__ Wd,
+// CTA b owns the hidden rows [H b / G, H (b + 1) / G) (G CTAs, at most
+// DN_RPC_MAX rows each); warp w covers the 16-byte vectors w * 32 + lane +
+// 256 i of every one of them, so that the rows divide evenly over the CTAs
+// whatever H / (warps on the GPU) is.  Partial sums meet in shared memory and
+// are added in warp order: out[t][r] = (residual[t][r]) + Wd[r] . act[t] for
+// up to DN_TT_D tokens per pass (Id % 256 == 0).  residual may be out itself
+// (the layer stack's hidden state): each element is read and written by the
+// same thread.
+__global__ void __launch_bounds__(DN_THREADS, 3) k_dense_down(const __half *__restrict__ Wd,
                                                            const float *__restrict__ act, int T, int H, int Id,
-                                                           const float *residual, float *out) {
+                                                           int rpc, const float *residual, float *out) {
     extern __shared__ float4 dn_smem[];
-    float *as = reinterpret_cast<float *>(dn_smem);
+    const int tt_max = min(T, DN_TT_D);
+    float *part = reinterpret_cast<float *>(dn_smem);        // [DN_WARPS][rpc][tt_max]
+    float *as = part + DN_WARPS * rpc * tt_max;              // [tt][Id], 16-byte aligned (rpc * tt_max * 32 B)
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int nv = Id >> 8;
+    const int r0 = (int)((long long)H * blockIdx.x / gridDim.x);
+    const int r1 = (int)((long long)H * (blockIdx.x + 1) / gridDim.x);
+    const int nv32 = Id >> 3;                      // 16-byte vectors per row
+    const int base = warp * 32 + lane;
+    const int cnt = nv32 > base ? (nv32 - base + 255) >> 8 : 0;   // this lane's vectors per row (warp-uniform)
     for (int t0 = 0; t0 < T; t0 += DN_TT_D) {
         const int tt = min(DN_TT_D, T - t0);
+        // the first row's weights are in flight while the activations are staged
+        uint4 w[DN_VD];
+        if (r0 < r1) {
+            const uint4 *pw = reinterpret_cast<const uint4 *>(Wd + (size_t)r0 * Id) + base;
+#pragma unroll
+            for (int j = 0; j < DN_VD; j++)
+                if (j < cnt) w[j] = ld_weight16(pw + j * 256);
+        }
         __syncthreads();
         stage_rows(as, act, t0, tt, Id);
         __syncthreads();
-        for (int r = blockIdx.x * DN_WARPS + warp; r < H; r += gridDim.x * DN_WARPS) {
+        for (int r = r0; r < r1; r++) {
             float acc[DN_TT_D];
 #pragma unroll
             for (int t = 0; t < DN_TT_D; t++) acc[t] = 0.0f;
-            const uint4 *pw = reinterpret_cast<const uint4 *>(Wd + (size_t)r * Id) + lane;
-            const float *al = as + lane * 8;
-            int i = 0;
-            for (; i + DN_U_D <= nv; i += DN_U_D) {
-                uint4 w[DN_U_D];
+            const uint4 *pw = reinterpret_cast<const uint4 *>(Wd + (size_t)r * Id) + base;
+            const float *al = as + base * 8;
+            for (int i0 = 0; i0 < cnt; i0 += DN_VD) {
+                if (r != r0 || i0 != 0) {
 #pragma unroll
-                for (int j = 0; j < DN_U_D; j++) w[j] = ld_weight16(pw + (i + j) * 32);
+                    for (int j = 0; j < DN_VD; j++)
+                        if (i0 + j < cnt) w[j] = ld_weight16(pw + (i0 + j) * 256);
+                }
 #pragma unroll
-                for (int j = 0; j < DN_U_D; j++)
+                for (int j = 0; j < DN_VD; j++)
+                    if (i0 + j < cnt)
 #pragma unroll
-                    for (int t = 0; t < DN_TT_D; t++)
-                        if (t < tt) acc[t] = dot8(w[j], al + (size_t)t * Id + (i + j) * 256, acc[t]);
-            }
-            for (; i < nv; i++) {
-                const uint4 w = ld_weight16(pw + i * 32);
-#pragma unroll
-                for (int t = 0; t < DN_TT_D; t++)
-                    if (t < tt) acc[t] = dot8(w, al + (size_t)t * Id + i * 256, acc[t]);
+                        for (int t = 0; t < DN_TT_D; t++)
+                            if (t < tt) acc[t] = dot8(w[j], al + (size_t)t * Id + (i0 + j) * 2048, acc[t]);
             }
 #pragma unroll
             for (int t = 0; t < DN_TT_D; t++)
                 if (t < tt) {
-                    const float s = warp_sum(acc[t]);
-                    if (lane == 0) {
-                        const size_t o = (size_t)(t0 + t) * H + r;
-                        out[o] = residual ? residual[o] + s : s;
-                    }
+                    const float v = warp_sum(acc[t]);
+                    if (lane == 0) part[(warp * rpc + (r - r0)) * tt_max + t] = v;
                 }
+        }
+        __syncthreads();
+        for (int k = threadIdx.x; k < (r1 - r0) * tt; k += blockDim.x) {
+            const int rl = k / tt, t = k - rl * tt;
+            float v = 0.0f;
+#pragma unroll
+            for (int w = 0; w < DN_WARPS; w++) v += part[(w * rpc + rl) * tt_max + t];
+            const size_t o = (size_t)(t0 + t) * H + r0 + rl;
+            out[o] = residual ? residual[o] + v : v;
         }
     }
 }
@@ -220,7 +264,9 @@ int dense_ctas(const void *fn, size_t smem) {
 }  // namespace
 
 size_t moe_dense_smem_need(int H, int Id) {
-    const size_t a = (size_t)DN_TT_GU * H * sizeof(float), b = (size_t)DN_TT_D * Id * sizeof(float);
+    (void)H;
+    const size_t a = (size_t)DN_TT_GU * H * sizeof(float);
+    const size_t b = (size_t)DN_TT_D * Id * sizeof(float) + (size_t)DN_WARPS * DN_RPC_MAX * DN_TT_D * sizeof(float);
     return a > b ? a : b;
 }
 
@@ -232,16 +278,30 @@ void moe_launch_dense_ffn(const __half *w, int H, int Id, const float *x, int T,
                           float *out, cudaStream_t s, uint64_t *launches) {
     if (T <= 0) return;
     const __half *Wg = w, *Wu = w + (size_t)Id * H, *Wd = w + 2 * (size_t)Id * H;
-    const size_t sg = (size_t)min(T, DN_TT_GU) * H * sizeof(float);
-    const size_t sd = (size_t)min(T, DN_TT_D) * Id * sizeof(float);
+    const int ttg = min(T, DN_TT_GU), ttd = min(T, DN_TT_D);
+    const size_t sg = (size_t)ttg * H * sizeof(float);
     static size_t done_gu[MOE_MAX_DEVICES], done_d[MOE_MAX_DEVICES];
     moe_smem_limit(k_dense_gateup, sg, done_gu);
-    moe_smem_limit(k_dense_down, sd, done_d);
     const int gg = min(dense_ctas((const void *)k_dense_gateup, sg), (Id + DN_WARPS - 1) / DN_WARPS);
-    const int gd = min(dense_ctas((const void *)k_dense_down, sd), (H + DN_WARPS - 1) / DN_WARPS);
+    // down: as many CTAs as fit with their activations and partial sums (the
+    // partials grow as the CTAs get fewer, so settle the count in two rounds)
+    const size_t sd_act = (size_t)ttd * Id * sizeof(float);
+    moe_smem_limit(k_dense_down, sd_act + (size_t)DN_WARPS * DN_RPC_MAX * DN_TT_D * sizeof(float), done_d);
+    int gd = H;
+    size_t sd = 0;
+    int rpc = 1;
+    for (int round = 0; round < 2; round++) {
+        const size_t guess = sd_act + (size_t)DN_WARPS * (round ? rpc : 1) * ttd * sizeof(float);
+        gd = min(dense_ctas((const void *)k_dense_down, guess), H);
+        gd = max(gd, (H + DN_RPC_MAX - 1) / DN_RPC_MAX);
+        rpc = (H + gd - 1) / gd;
+        sd = sd_act + (size_t)DN_WARPS * rpc * ttd * sizeof(float);
+    }
+    // (launched as programmatic dependents, with the first weight loads ahead
+    // of the wait, the step measured 3 % slower: plain launches)
     k_dense_gateup<<<gg, DN_THREADS, sg, s>>>(Wg, Wu, x, T, H, Id, act);
     LAUNCH_COUNT(launches);
-    k_dense_down<<<gd, DN_THREADS, sd, s>>>(Wd, act, T, H, Id, residual, out);
+    k_dense_down<<<gd, DN_THREADS, sd, s>>>(Wd, act, T, H, Id, rpc, residual, out);
     LAUNCH_COUNT(launches);
 }
 
