@@ -264,6 +264,46 @@ class MoE:
         self._check(self.lib.moe_dense_forward_device(self.ctx, layer, _ptr(d_h), n_tokens, _ptr(d_out),
                                                       _ptr(stream)), "moe_dense_forward_device")
 
+    # ------------------------------------------------- output head, sampling
+    def load_lm_head(self, w, qtype: int, vocab: int):
+        b = np.ascontiguousarray(w).view(np.uint8)
+        self._check(self.lib.moe_load_lm_head(self.ctx, vocab, _ptr(b), qtype), "moe_load_lm_head")
+        self.vocab = vocab
+
+    def init_lm_head_synthetic(self, vocab: int, seed: int = 0, w_sigma: float = 0.02):
+        self._check(self.lib.moe_init_lm_head_synthetic(self.ctx, vocab, seed, w_sigma), "moe_init_lm_head_synthetic")
+        self.vocab = vocab
+
+    def read_lm_head(self) -> np.ndarray:
+        out = np.empty((self.vocab, self.cfg.hidden), np.uint16)
+        self._check(self.lib.moe_read_lm_head(self.ctx, _ptr(out), out.nbytes), "moe_read_lm_head")
+        return out
+
+    def lm_head(self, h):
+        h = _f32(h).reshape(-1, self.cfg.hidden)
+        out = np.empty((h.shape[0], self.vocab), np.float32)
+        self._check(self.lib.moe_lm_head(self.ctx, _ptr(h), h.shape[0], _ptr(out)), "moe_lm_head")
+        return out
+
+    def lm_head_device(self, d_h, n_tokens: int, d_logits, stream=None):
+        self._check(self.lib.moe_lm_head_device(self.ctx, _ptr(d_h), n_tokens, _ptr(d_logits), _ptr(stream)),
+                    "moe_lm_head_device")
+
+    def sample(self, logits, temp: float, top_p: float, rng_state: int):
+        """(tokens, next rng_state) for rows of logits, as sample_top_p."""
+        lg = _f32(logits)
+        lg = lg.reshape(-1, lg.shape[-1])
+        st = C.c_uint32(rng_state)
+        out = np.empty(lg.shape[0], np.int32)
+        self._check(self.lib.moe_sample(self.ctx, _ptr(lg), lg.shape[0], lg.shape[1], temp, top_p, C.byref(st),
+                                        _ptr(out)), "moe_sample")
+        return out, st.value
+
+    def sample_device(self, d_logits, n_tokens: int, vocab: int, temp: float, top_p: float, rng_state: int,
+                      d_tokens, stream=None):
+        self._check(self.lib.moe_sample_device(self.ctx, _ptr(d_logits), n_tokens, vocab, temp, top_p, rng_state,
+                                               _ptr(d_tokens), _ptr(stream)), "moe_sample_device")
+
     # --------------------------------------------------------------- forward
     def forward(self, layer: int, h_post):
         """MoE block on host arrays: returns (out [T,H], idx [T,K], w [T,K])."""

@@ -49,6 +49,14 @@ SIGNATURES = {
     "moe_read_dense_weight": (C.c_int, [_vp, C.c_int, C.c_int, _vp, C.c_size_t]),
     "moe_dense_forward": (C.c_int, [_vp, C.c_int, _vp, C.c_int, _vp]),
     "moe_dense_forward_device": (C.c_int, [_vp, C.c_int, _vp, C.c_int, _vp, _vp]),
+    "moe_load_lm_head": (C.c_int, [_vp, C.c_int, _vp, C.c_int]),
+    "moe_init_lm_head_synthetic": (C.c_int, [_vp, C.c_int, C.c_uint64, C.c_double]),
+    "moe_read_lm_head": (C.c_int, [_vp, _vp, C.c_size_t]),
+    "moe_lm_head": (C.c_int, [_vp, _vp, C.c_int, _vp]),
+    "moe_lm_head_device": (C.c_int, [_vp, _vp, C.c_int, _vp, _vp]),
+    "moe_sample": (C.c_int, [_vp, _vp, C.c_int, C.c_int, C.c_float, C.c_float, C.POINTER(C.c_uint32), _vp]),
+    "moe_sample_device": (C.c_int, [_vp, _vp, C.c_int, C.c_int, C.c_float, C.c_float, C.c_uint32, _vp, _vp]),
+    "moe_rng_advance": (C.c_uint32, [C.c_uint32, C.c_int]),
     "moe_forward": (C.c_int, [_vp, C.c_int, _vp, C.c_int, _vp, _vp, _vp]),
     "moe_forward_device": (C.c_int, [_vp, C.c_int, _vp, C.c_int, _vp, _vp, _vp, _vp]),
     "moe_check_error": (C.c_int, [_vp]),

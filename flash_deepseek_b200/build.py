@@ -14,7 +14,7 @@ CSRC = os.path.join(HERE, "csrc")
 ROOT = os.path.dirname(HERE)
 OUT = os.path.join(HERE, "libmoe_cuda.so")
 SOURCES = ["moe_kernels.cu", "moe_experts.cu", "moe_experts_tc.cu", "moe_prefill.cu", "moe_ep.cu", "moe_api.cu",
-           "moe_noalloc.cu", "moe_dense.cu"]
+           "moe_noalloc.cu", "moe_dense.cu", "moe_sample.cu"]
 HEADERS = ["moe_common.cuh", "moe_internal.h", "moe_nccl.h", "moe_umma.cuh", "moe_wait.h"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

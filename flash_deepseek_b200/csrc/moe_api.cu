@@ -82,6 +82,12 @@ struct moe_ctx {
     std::vector<DenseDev> dense;
     float *dense_act = nullptr;  // [max_tok x Id] of the widest dense layer
     size_t dense_act_n = 0;
+    // output head (lm_head, infer.m:1937-1941): fp16 [vocab x H]; sampling scratch
+    __half *head_w = nullptr;
+    int vocab = 0;
+    float *head_logits = nullptr, *sample_p = nullptr;  // [max_tok x n] each
+    int *sample_tok = nullptr;                           // [max_tok]
+    size_t sample_n = 0;
     // workspace
     float *part = nullptr, *logits = nullptr, *d_in = nullptr, *d_out = nullptr, *h_post = nullptr;
     int *rl_counters = nullptr;
@@ -491,6 +497,10 @@ void moe_destroy(moe_ctx *c) {
     }
     for (auto &D : c->dense) cudaFree(D.w);
     cudaFree(c->dense_act);
+    cudaFree(c->head_w);
+    cudaFree(c->head_logits);
+    cudaFree(c->sample_p);
+    cudaFree(c->sample_tok);
     void *bufs[] = {c->part, c->logits, c->rl_counters, c->d_in, c->d_out, c->h_post, c->idx, c->wts, c->idx_given, c->w_given, c->bias_tmp, c->xop, c->plan.counts,
                     c->plan.pair_expert, c->plan.pair_token, c->plan.pair_w, c->plan.chunk_expert,
                     c->plan.chunk_pair0, c->plan.chunk_ntok, c->plan.chunk_order, c->plan.slot_pair, c->plan.error, c->counter, c->act,
@@ -868,6 +878,94 @@ int moe_read_dense_weight(moe_ctx *c, int layer, int which, void *dst, size_t ds
     if (dst_size < n * sizeof(__half)) return fail(c, MOE_ERR_ARG, "dst_size %zu < %zu", dst_size, n * 2);
     CK(cudaStreamSynchronize(c->stream));
     CK(cudaMemcpy(dst, c->dense[layer].w + which * n, n * sizeof(__half), cudaMemcpyDeviceToHost));
+    return MOE_OK;
+}
+
+// ---------------------------------------------------------- output head
+// sampling scratch for rows of n values: logits and probabilities [max_tok x n]
+static int sample_scratch(moe_ctx *c, int n) {
+    if ((size_t)n <= c->sample_n) return MOE_OK;
+    cudaFree(c->head_logits);
+    cudaFree(c->sample_p);
+    cudaFree(c->sample_tok);
+    c->head_logits = c->sample_p = nullptr;
+    c->sample_tok = nullptr;
+    c->sample_n = 0;
+    const size_t m = (size_t)c->max_tok * n;
+    CK(cudaMalloc((void **)&c->head_logits, m * sizeof(float)));
+    CK(cudaMalloc((void **)&c->sample_p, m * sizeof(float)));
+    CK(cudaMalloc((void **)&c->sample_tok, c->max_tok * sizeof(int)));
+    c->sample_n = n;
+    return MOE_OK;
+}
+
+static int head_alloc(moe_ctx *c, int vocab) {
+    if (vocab <= 0 || c->d.H % 256) return fail(c, MOE_ERR_ARG, "lm_head needs vocab > 0 and hidden %% 256 == 0");
+    CK(cudaStreamSynchronize(c->stream));
+    drop_graphs(c);
+    if (!c->head_w || c->vocab != vocab) {
+        cudaFree(c->head_w);
+        c->head_w = nullptr;
+        c->vocab = 0;
+        CK(cudaMalloc((void **)&c->head_w, (size_t)vocab * c->d.H * sizeof(__half)));
+    }
+    c->vocab = vocab;
+    return sample_scratch(c, vocab);
+}
+
+int moe_load_lm_head(moe_ctx *c, int vocab, const void *w, int type) {
+    if (!c || !w) return MOE_ERR_ARG;
+    DeviceScope ds(c->device);
+    const size_t n = (size_t)vocab * c->d.H;
+    if (!type_bytes(type, 256) || vocab <= 0)
+        return fail(c, MOE_ERR_ARG, "lm_head must be F32 (0), F16 (1), BF16 (30), Q4_K (12) or Q6_K (14)");
+    int rc = head_alloc(c, vocab);
+    if (rc) return rc;
+    const bool quant = type == MOE_TYPE_Q4_K || type == MOE_TYPE_Q6_K;
+    uint8_t *tmp = nullptr;
+    float *tf = nullptr;
+    CK(cudaMalloc((void **)&tmp, type_bytes(type, n)));
+    if (quant && cudaMalloc((void **)&tf, n * sizeof(float)) != cudaSuccess) {
+        cudaFree(tmp);
+        return fail(c, MOE_ERR_CUDA, "lm_head: no room for the dequant scratch");
+    }
+    cudaError_t e = cudaMemcpyAsync(tmp, w, type_bytes(type, n), cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) {
+        moe_launch_to_f16(type, tmp, c->head_w, n, tf, c->stream, &c->launches);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    cudaFree(tmp);
+    cudaFree(tf);
+    if (e != cudaSuccess) return fail(c, MOE_ERR_CUDA, "lm_head: %s", cudaGetErrorString(e));
+    return MOE_OK;
+}
+
+int moe_init_lm_head_synthetic(moe_ctx *c, int vocab, uint64_t seed, double w_sigma) {
+    if (!c) return MOE_ERR_ARG;
+    DeviceScope ds(c->device);
+    int rc = head_alloc(c, vocab);
+    if (rc) return rc;
+    const size_t n = (size_t)vocab * c->d.H;
+    float *tf = nullptr;
+    CK(cudaMalloc((void **)&tf, n * sizeof(float)));
+    moe_launch_synth_f32(seed, synth_stream(0, c->d.E + 2, SYN_GATE), n, w_sigma, tf, c->stream, &c->launches);
+    moe_launch_to_f16(MOE_TYPE_F32, tf, c->head_w, n, nullptr, c->stream, &c->launches);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    cudaFree(tf);
+    if (e != cudaSuccess) return fail(c, MOE_ERR_CUDA, "synthetic lm_head: %s", cudaGetErrorString(e));
+    return MOE_OK;
+}
+
+int moe_read_lm_head(moe_ctx *c, void *dst, size_t dst_size) {
+    if (!c || !dst) return MOE_ERR_ARG;
+    if (!c->head_w) return fail(c, MOE_ERR_STATE, "lm_head not loaded");
+    DeviceScope ds(c->device);
+    const size_t bytes = (size_t)c->vocab * c->d.H * sizeof(__half);
+    if (dst_size < bytes) return fail(c, MOE_ERR_ARG, "dst_size %zu < %zu", dst_size, bytes);
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaMemcpy(dst, c->head_w, bytes, cudaMemcpyDeviceToHost));
     return MOE_OK;
 }
 
@@ -1438,6 +1536,78 @@ int moe_dense_forward(moe_ctx *c, int layer, const float *h, int T, float *out) 
     rc = copy_out(c, c->stream, false, {{out, c->d_out, n * sizeof(float)}});
     if (rc) return rc;
     return finish_sync(c);
+}
+
+int moe_lm_head_device(moe_ctx *c, const float *d_h, int T, float *d_logits, void *stream) {
+    if (!c) return MOE_ERR_ARG;
+    if (!c->head_w) return fail(c, MOE_ERR_STATE, "lm_head not loaded");
+    if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
+    if (T > 0 && (!d_h || !d_logits || ((uintptr_t)d_h & 15)))
+        return fail(c, MOE_ERR_ARG, "moe_lm_head_device: null or not 16-byte aligned buffer");
+    DeviceScope ds(c->device);
+    moe_launch_lm_head(c->head_w, c->d.H, c->vocab, d_h, T, d_logits, stream ? (cudaStream_t)stream : c->stream,
+                       &c->launches);
+    CK(cudaGetLastError());
+    return MOE_OK;
+}
+
+int moe_lm_head(moe_ctx *c, const float *h, int T, float *logits) {
+    if (!c) return MOE_ERR_ARG;
+    if (T > 0 && (!h || !logits)) return fail(c, MOE_ERR_ARG, "moe_lm_head: null pointer");
+    if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
+    if (!c->head_w) return fail(c, MOE_ERR_STATE, "lm_head not loaded");
+    if (T == 0) return MOE_OK;
+    DeviceScope ds(c->device);
+    CK(cudaMemcpyAsync(c->d_in, h, (size_t)T * c->d.H * sizeof(float), cudaMemcpyHostToDevice, c->stream));
+    int rc = moe_lm_head_device(c, c->d_in, T, c->head_logits, c->stream);
+    if (rc) return rc;
+    rc = copy_out(c, c->stream, false, {{logits, c->head_logits, (size_t)T * c->vocab * sizeof(float)}});
+    if (rc) return rc;
+    return finish_sync(c);
+}
+
+int moe_sample_device(moe_ctx *c, const float *d_logits, int T, int vocab, float temp, float top_p,
+                      uint32_t rng_state, int *d_tokens, void *stream) {
+    if (!c) return MOE_ERR_ARG;
+    if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
+    if (vocab <= 0 || (T > 0 && (!d_logits || !d_tokens))) return fail(c, MOE_ERR_ARG, "moe_sample_device: bad argument");
+    DeviceScope ds(c->device);
+    int rc = sample_scratch(c, vocab);
+    if (rc) return rc;
+    moe_launch_sample(d_logits, T, vocab, temp, top_p, rng_state, c->sample_p, d_tokens,
+                      stream ? (cudaStream_t)stream : c->stream, &c->launches);
+    CK(cudaGetLastError());
+    return MOE_OK;
+}
+
+uint32_t moe_rng_advance(uint32_t state, int n) {
+    for (int i = 0; i < n; i++) {
+        state ^= state << 13;
+        state ^= state >> 17;
+        state ^= state << 5;
+    }
+    return state;
+}
+
+int moe_sample(moe_ctx *c, const float *logits, int T, int vocab, float temp, float top_p, uint32_t *rng_state,
+               int *tokens) {
+    if (!c) return MOE_ERR_ARG;
+    if (T > 0 && (!logits || !tokens || !rng_state)) return fail(c, MOE_ERR_ARG, "moe_sample: null pointer");
+    if (T < 0 || T > c->max_tok) return fail(c, MOE_ERR_ARG, "n_tokens %d exceeds max_tokens %d", T, c->max_tok);
+    if (T == 0) return MOE_OK;
+    DeviceScope ds(c->device);
+    int rc = sample_scratch(c, vocab);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(c->head_logits, logits, (size_t)T * vocab * sizeof(float), cudaMemcpyHostToDevice,
+                       c->stream));
+    rc = moe_sample_device(c, c->head_logits, T, vocab, temp, top_p, *rng_state, c->sample_tok, c->stream);
+    if (rc) return rc;
+    rc = copy_out(c, c->stream, false, {{tokens, c->sample_tok, (size_t)T * sizeof(int)}});
+    if (rc) return rc;
+    rc = finish_sync(c);
+    if (rc) return rc;
+    if (temp > 0.0f) *rng_state = moe_rng_advance(*rng_state, T);  // one draw per sampled row (infer.m:447)
+    return MOE_OK;
 }
 
 int moe_route(moe_ctx *c, const float *logits, const float *bias, int T, int *idx, float *w) {

@@ -47,10 +47,12 @@ __device__ __forceinline__ uint4 ld_weight16(const uint4 *p) {
     return v;
 }
 
-// acc += sum over the 8 halves of w times xs[0..8)
-__device__ __forceinline__ float dot8(const uint4 &w, const float *xs, float acc) {
-    const float4 x0 = *reinterpret_cast<const float4 *>(xs);
-    const float4 x1 = *reinterpret_cast<const float4 *>(xs + 4);
+// acc += sum over the 8 halves of w times the 8 floats lo[0..4), hi[0..4)
+// (a lane's activations sit in two 16-byte pieces 512 bytes apart; see
+// stage_rows)
+__device__ __forceinline__ float dot8(const uint4 &w, const float *lo, float acc) {
+    const float4 x0 = *reinterpret_cast<const float4 *>(lo);
+    const float4 x1 = *reinterpret_cast<const float4 *>(lo + 128);
     const float2 w0 = __half22float2(*reinterpret_cast<const __half2 *>(&w.x));
     const float2 w1 = __half22float2(*reinterpret_cast<const __half2 *>(&w.y));
     const float2 w2 = __half22float2(*reinterpret_cast<const __half2 *>(&w.z));
@@ -72,8 +74,11 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
-// the tokens [t0, t0 + tt) of x [T x cols] into shared memory (cols % 4 == 0),
-// DN_STAGE loads in flight per thread
+// the tokens [t0, t0 + tt) of x [T x cols] into shared memory (cols % 256 ==
+// 0), DN_STAGE loads in flight per thread.  Within each 256-float chunk the
+// floats 8 l .. 8 l + 3 go to 4 l and 8 l + 4 .. 8 l + 7 to 128 + 4 l, so that
+// lane l of a warp reading its 8 floats touches two 16-byte pieces that sit
+// next to its neighbours' (no bank conflicts).
 constexpr int DN_STAGE = 4;
 __device__ __forceinline__ void stage_rows(float *xs, const float *__restrict__ x, int t0, int tt, int cols) {
     const float4 *src = reinterpret_cast<const float4 *>(x + (size_t)t0 * cols);
@@ -85,18 +90,21 @@ __device__ __forceinline__ void stage_rows(float *xs, const float *__restrict__ 
         for (int j = 0; j < DN_STAGE; j++)
             if (i0 + j * (int)blockDim.x < n4) v[j] = src[i0 + j * blockDim.x];
 #pragma unroll
-        for (int j = 0; j < DN_STAGE; j++)
-            if (i0 + j * (int)blockDim.x < n4) dst[i0 + j * blockDim.x] = v[j];
+        for (int j = 0; j < DN_STAGE; j++) {
+            const int q = i0 + j * blockDim.x;
+            if (q < n4) dst[(q & ~63) | ((q & 1) << 5) | ((q >> 1) & 31)] = v[j];
+        }
     }
 }
 
-// One warp per intermediate row r: g = Wg[r] . x, u = Wu[r] . x for up to
-// DN_TT_GU tokens per pass, act[t][r] = g / (1 + exp(-g)) * u (infer.m:378-383).
-// Lane l reads the 16-byte vectors l, l + 32, ... of both rows (H % 256 == 0).
-__global__ void __launch_bounds__(DN_THREADS, 2) k_dense_gateup(const __half *__restrict__ Wg,
-                                                             const __half *__restrict__ Wu,
-                                                             const float *__restrict__ x, int T, int H, int Id,
-                                                             float *__restrict__ act) {
+// One warp per output row r: g = Wg[r] . x (and u = Wu[r] . x when GLU) for up
+// to DN_TT_GU tokens per pass; GLU writes act[t][r] = g / (1 + exp(-g)) * u
+// (infer.m:378-383), else act[t][r] = g.  Lane l reads the 16-byte vectors
+// l, l + 32, ... of the rows (H % 256 == 0).
+template <bool GLU>
+__device__ __forceinline__ void dense_rows(const __half *__restrict__ Wg, const __half *__restrict__ Wu,
+                                           const float *__restrict__ x, int T, int H, int Id,
+                                           float *__restrict__ act) {
     extern __shared__ float4 dn_smem[];
     float *xs = reinterpret_cast<float *>(dn_smem);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -111,7 +119,7 @@ __global__ void __launch_bounds__(DN_THREADS, 2) k_dense_gateup(const __half *__
 #pragma unroll
             for (int j = 0; j < DN_U_GU; j++) {
                 g[j] = ld_weight16(reinterpret_cast<const uint4 *>(Wg + (size_t)r_first * H) + lane + j * 32);
-                u[j] = ld_weight16(reinterpret_cast<const uint4 *>(Wu + (size_t)r_first * H) + lane + j * 32);
+                if (GLU) u[j] = ld_weight16(reinterpret_cast<const uint4 *>(Wu + (size_t)r_first * H) + lane + j * 32);
             }
         }
         __syncthreads();
@@ -123,14 +131,14 @@ __global__ void __launch_bounds__(DN_THREADS, 2) k_dense_gateup(const __half *__
             for (int t = 0; t < DN_TT_GU; t++) ag[t] = au[t] = 0.0f;
             const uint4 *pg = reinterpret_cast<const uint4 *>(Wg + (size_t)r * H) + lane;
             const uint4 *pu = reinterpret_cast<const uint4 *>(Wu + (size_t)r * H) + lane;
-            const float *xl = xs + lane * 8;
+            const float *xl = xs + lane * 4;
             int i = 0;
             for (; i + DN_U_GU <= nv; i += DN_U_GU) {
                 if (!(pre && r == r_first && i == 0)) {
 #pragma unroll
                     for (int j = 0; j < DN_U_GU; j++) {
                         g[j] = ld_weight16(pg + (i + j) * 32);
-                        u[j] = ld_weight16(pu + (i + j) * 32);
+                        if (GLU) u[j] = ld_weight16(pu + (i + j) * 32);
                     }
                 }
 #pragma unroll
@@ -140,27 +148,48 @@ __global__ void __launch_bounds__(DN_THREADS, 2) k_dense_gateup(const __half *__
                         if (t < tt) {
                             const float *xp = xl + (size_t)t * H + (i + j) * 256;
                             ag[t] = dot8(g[j], xp, ag[t]);
-                            au[t] = dot8(u[j], xp, au[t]);
+                            if (GLU) au[t] = dot8(u[j], xp, au[t]);
                         }
             }
             for (; i < nv; i++) {
-                const uint4 g = ld_weight16(pg + i * 32), u = ld_weight16(pu + i * 32);
+                const uint4 g1 = ld_weight16(pg + i * 32);
+                uint4 u1 = g1;
+                if (GLU) u1 = ld_weight16(pu + i * 32);
 #pragma unroll
                 for (int t = 0; t < DN_TT_GU; t++)
                     if (t < tt) {
                         const float *xp = xl + (size_t)t * H + i * 256;
-                        ag[t] = dot8(g, xp, ag[t]);
-                        au[t] = dot8(u, xp, au[t]);
+                        ag[t] = dot8(g1, xp, ag[t]);
+                        if (GLU) au[t] = dot8(u1, xp, au[t]);
                     }
             }
 #pragma unroll
             for (int t = 0; t < DN_TT_GU; t++)
                 if (t < tt) {
-                    const float gs = warp_sum(ag[t]), us = warp_sum(au[t]);
-                    if (lane == 0) act[(size_t)(t0 + t) * Id + r] = (gs / (1.0f + expf(-gs))) * us;
+                    const float gs = warp_sum(ag[t]);
+                    if (GLU) {
+                        const float us = warp_sum(au[t]);
+                        if (lane == 0) act[(size_t)(t0 + t) * Id + r] = (gs / (1.0f + expf(-gs))) * us;
+                    } else if (lane == 0) {
+                        act[(size_t)(t0 + t) * Id + r] = gs;
+                    }
                 }
         }
     }
+}
+
+__global__ void __launch_bounds__(DN_THREADS, 2) k_dense_gateup(const __half *__restrict__ Wg,
+                                                             const __half *__restrict__ Wu,
+                                                             const float *__restrict__ x, int T, int H, int Id,
+                                                             float *__restrict__ act) {
+    dense_rows<true>(Wg, Wu, x, T, H, Id, act);
+}
+
+// logits[t][v] = W[v] . h[t] over fp16 W [V x H] (lm_head, infer.m:1937-1941)
+__global__ void __launch_bounds__(DN_THREADS, 2) k_lm_head(const __half *__restrict__ W,
+                                                        const float *__restrict__ h, int T, int H, int V,
+                                                        float *__restrict__ logits) {
+    dense_rows<false>(W, nullptr, h, T, H, V, logits);
 }
 
 // CTA b owns the hidden rows [H b / G, H (b + 1) / G) (G CTAs, at most
@@ -202,7 +231,7 @@ __global__ void __launch_bounds__(DN_THREADS, 3) k_dense_down(const __half *__re
 #pragma unroll
             for (int t = 0; t < DN_TT_D; t++) acc[t] = 0.0f;
             const uint4 *pw = reinterpret_cast<const uint4 *>(Wd + (size_t)r * Id) + base;
-            const float *al = as + base * 8;
+            const float *al = as + warp * 256 + lane * 4;   // vector base + 256 i sits in chunk warp + 8 i
             for (int i0 = 0; i0 < cnt; i0 += DN_VD) {
                 if (r != r0 || i0 != 0) {
 #pragma unroll
@@ -302,6 +331,17 @@ void moe_launch_dense_ffn(const __half *w, int H, int Id, const float *x, int T,
     k_dense_gateup<<<gg, DN_THREADS, sg, s>>>(Wg, Wu, x, T, H, Id, act);
     LAUNCH_COUNT(launches);
     k_dense_down<<<gd, DN_THREADS, sd, s>>>(Wd, act, T, H, Id, rpc, residual, out);
+    LAUNCH_COUNT(launches);
+}
+
+void moe_launch_lm_head(const __half *w, int H, int V, const float *h, int T, float *logits, cudaStream_t s,
+                        uint64_t *launches) {
+    if (T <= 0) return;
+    const size_t sg = (size_t)min(T, DN_TT_GU) * H * sizeof(float);
+    static size_t done[MOE_MAX_DEVICES];
+    moe_smem_limit(k_lm_head, sg, done);
+    const int g = min(dense_ctas((const void *)k_lm_head, sg), (V + DN_WARPS - 1) / DN_WARPS);
+    k_lm_head<<<g, DN_THREADS, sg, s>>>(w, h, T, H, V, logits);
     LAUNCH_COUNT(launches);
 }
 

@@ -1,0 +1,267 @@
+// moe_sample.cu -- the next token from the lm_head logits: the reference's
+// sample_top_p (infer.m:419-456: temperature softmax, descending sort,
+// nucleus cut at top_p, one xorshift32 draw scaled by the nucleus mass, walk)
+// and argmax (infer.m:390-394) at temp <= 0.
+//
+// One CTA per token row.  Instead of sorting the vocabulary, the kernel finds
+// the two places where the descending cumulative probability crosses a
+// target (top_p, then the draw) by radix selection over the probabilities'
+// bit patterns (positive floats order like their bits): four passes of 8-bit
+// digits, each a histogram of counts and of 2^40-scaled fixed-point sums
+// (integer atomics: the same sums in any order).  Equal probabilities are
+// taken in index order, the order a stable sort gives.
+#include <math.h>
+#include <stdint.h>
+
+#include "moe_common.cuh"
+#include "moe_internal.h"
+
+#define LAUNCH_COUNT(p) \
+    do {                \
+        if (p) (*(p))++; \
+    } while (0)
+
+namespace {
+
+constexpr int SP_THREADS = 1024;
+constexpr int SP_WARPS = SP_THREADS / 32;
+constexpr int SP_HIST = 8;                  // histograms, each shared by 4 warps (fewer atomic conflicts)
+constexpr float SP_FIX = 1099511627776.0f;  // 2^40
+
+struct SpShared {
+    unsigned int cnt[SP_HIST][256];
+    unsigned long long sum[SP_HIST][256];
+    float fred[SP_WARPS];
+    int ired[SP_WARPS];
+    unsigned int wscan[SP_WARPS];
+    uint32_t pre, msk, last_cnt;
+    unsigned long long above;
+};
+
+__device__ __forceinline__ unsigned long long fx(float p) { return __float2ull_rz(p * SP_FIX); }
+
+__device__ __forceinline__ float block_max(float v, SpShared &sh) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    __syncthreads();
+    if (lane == 0) sh.fred[warp] = v;
+    __syncthreads();
+    v = sh.fred[0];
+    for (int w = 1; w < SP_WARPS; w++) v = fmaxf(v, sh.fred[w]);
+    return v;
+}
+
+// every thread gets the sum, added in warp order
+__device__ __forceinline__ float block_sum(float v, SpShared &sh) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();
+    if (lane == 0) sh.fred[warp] = v;
+    __syncthreads();
+    v = 0.0f;
+    for (int w = 0; w < SP_WARPS; w++) v += sh.fred[w];
+    return v;
+}
+
+// Descending over the probabilities whose key (bit pattern) is in the set
+// (all of them, or those above kmin when gt): the key K at which the
+// cumulative fixed-point sum first reaches `target` (the smallest key when it
+// never does).  Leaves K in sh.pre, the sum over set keys above K in
+// sh.above and the count of set keys equal to K in sh.last_cnt.
+__device__ void radix_select(const float *__restrict__ p, int n, bool gt, uint32_t kmin,
+                             unsigned long long target, SpShared &sh) {
+    const int tid = threadIdx.x, warp = tid >> 5;
+    if (tid == 0) {
+        sh.pre = 0;
+        sh.msk = 0;
+        sh.above = 0;
+    }
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int k = tid; k < SP_HIST * 256; k += SP_THREADS) {
+            (&sh.cnt[0][0])[k] = 0;
+            (&sh.sum[0][0])[k] = 0;
+        }
+        __syncthreads();
+        const uint32_t pre = sh.pre, msk = sh.msk;
+        for (int i = tid; i < n; i += SP_THREADS) {
+            const float v = p[i];
+            const uint32_t k = __float_as_uint(v);
+            if ((gt && k <= kmin) || (k & msk) != pre) continue;
+            const int d = (k >> shift) & 255;
+            atomicAdd(&sh.cnt[warp % SP_HIST][d], 1u);
+            atomicAdd(&sh.sum[warp % SP_HIST][d], fx(v));
+        }
+        __syncthreads();
+        // fold the histograms into the first
+        for (int d = tid; d < 256; d += SP_THREADS) {
+            unsigned int c = 0;
+            unsigned long long s = 0;
+            for (int w = 0; w < SP_HIST; w++) {
+                c += sh.cnt[w][d];
+                s += sh.sum[w][d];
+            }
+            sh.cnt[0][d] = c;
+            sh.sum[0][d] = s;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            unsigned long long acc = sh.above;
+            int pick = -1, lowest = -1;
+            for (int d = 255; d >= 0; d--) {
+                if (!sh.cnt[0][d]) continue;
+                lowest = d;
+                if (acc + sh.sum[0][d] >= target) {
+                    pick = d;
+                    break;
+                }
+                acc += sh.sum[0][d];
+            }
+            if (pick < 0 && lowest >= 0) {  // target not reached: the smallest key
+                pick = lowest;
+                acc -= sh.sum[0][lowest];
+            }
+            if (pick < 0) pick = 0;         // empty set (callers rule it out)
+            sh.above = acc;
+            sh.pre = pre | ((uint32_t)pick << shift);
+            sh.msk = msk | (255u << shift);
+            sh.last_cnt = sh.cnt[0][pick];
+        }
+        __syncthreads();
+    }
+}
+
+// index of the m-th (1-based) element whose key is K, in index order
+__device__ int mth_equal(const float *__restrict__ p, int n, uint32_t K, unsigned int m, SpShared &sh, int *slot) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int chunk = (n + SP_THREADS - 1) / SP_THREADS;
+    const int lo = min(n, tid * chunk), hi = min(n, lo + chunk);
+    unsigned int c = 0;
+    for (int i = lo; i < hi; i++) c += __float_as_uint(p[i]) == K;
+    unsigned int incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) sh.wscan[warp] = incl;
+    __syncthreads();
+    unsigned int before = incl - c;
+    for (int w = 0; w < warp; w++) before += sh.wscan[w];
+    if (c && m > before && m <= before + c) {
+        unsigned int seen = before;
+        for (int i = lo; i < hi; i++)
+            if (__float_as_uint(p[i]) == K && ++seen == m) {
+                *slot = i;
+                break;
+            }
+    }
+    __syncthreads();
+    return *slot;
+}
+
+__device__ __forceinline__ unsigned int need_count(unsigned long long target, unsigned long long above, float pk,
+                                                   unsigned int cap) {
+    const unsigned long long f = fx(pk);
+    if (target <= above) return 1;
+    if (!f) return cap;
+    const unsigned long long m = (target - above + f - 1) / f;
+    return (unsigned int)max(1ull, min((unsigned long long)cap, m));
+}
+
+__global__ void __launch_bounds__(SP_THREADS, 1) k_sample(const float *__restrict__ logits, int V, float temp,
+                                                         float top_p, uint32_t rng, float *__restrict__ pbuf,
+                                                         int *__restrict__ tokens) {
+    __shared__ SpShared sh;
+    __shared__ int slot;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float *l = logits + (size_t)blockIdx.x * V;
+    float *p = pbuf + (size_t)blockIdx.x * V;
+    if (tid == 0) slot = V - 1;
+    if (!(temp > 0.0f)) {
+        // argmax: the first index of the largest logit (infer.m:390-394)
+        float bv = l[0];
+        int bi = 0;
+        for (int i = tid; i < V; i += SP_THREADS)
+            if (l[i] > bv) {
+                bv = l[i];
+                bi = i;
+            }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (lane == 0) {
+            sh.fred[warp] = bv;
+            sh.ired[warp] = bi;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            for (int w = 1; w < SP_WARPS; w++)
+                if (sh.fred[w] > bv || (sh.fred[w] == bv && sh.ired[w] < bi)) {
+                    bv = sh.fred[w];
+                    bi = sh.ired[w];
+                }
+            tokens[blockIdx.x] = bi;
+        }
+        return;
+    }
+    // softmax of logits / temp (infer.m:426-436), no contraction of the scaled subtraction
+    const float inv_t = 1.0f / temp;
+    float mx = -1e30f;
+    for (int i = tid; i < V; i += SP_THREADS) mx = fmaxf(mx, __fmul_rn(l[i], inv_t));
+    mx = block_max(mx, sh);
+    float part = 0.0f;
+    for (int i = tid; i < V; i += SP_THREADS) {
+        const float e = expf(__fsub_rn(__fmul_rn(l[i], inv_t), mx));
+        p[i] = e;
+        part += e;
+    }
+    const float inv_s = 1.0f / block_sum(part, sh);
+    for (int i = tid; i < V; i += SP_THREADS) p[i] = __fmul_rn(p[i], inv_s);
+    __syncthreads();
+    // nucleus (infer.m:440-445): the first key where the cumulative mass reaches top_p
+    const unsigned long long t1 = (unsigned long long)((double)top_p * 1099511627776.0);
+    radix_select(p, V, false, 0, t1, sh);
+    const uint32_t tau = sh.pre;
+    const unsigned long long above1 = sh.above;
+    const unsigned int j1 = need_count(t1, above1, __uint_as_float(tau), sh.last_cnt);
+    const float cum = (float)((double)(above1 + (unsigned long long)j1 * fx(__uint_as_float(tau))) /
+                              1099511627776.0);
+    // the draw of this row (infer.m:412-418): the (row + 1)-th xorshift32 state
+    uint32_t x = rng;
+    for (int t = 0; t <= (int)blockIdx.x; t++) {
+        x ^= x << 13;
+        x ^= x >> 17;
+        x ^= x << 5;
+    }
+    const float r = __fmul_rn((float)(x & 0xFFFFFFu) * (1.0f / (float)0x1000000), cum);
+    const unsigned long long t2 = fx(r);
+    __syncthreads();
+    int pick;
+    if (above1 >= t2 && above1 > 0) {
+        radix_select(p, V, true, tau, t2, sh);
+        const uint32_t kap = sh.pre;
+        const unsigned int m = need_count(t2, sh.above, __uint_as_float(kap), sh.last_cnt);
+        pick = mth_equal(p, V, kap, m, sh, &slot);
+    } else {
+        const unsigned int m = need_count(t2, above1, __uint_as_float(tau), j1);
+        pick = mth_equal(p, V, tau, m, sh, &slot);
+    }
+    if (tid == 0) tokens[blockIdx.x] = pick;
+}
+
+}  // namespace
+
+void moe_launch_sample(const float *logits, int T, int V, float temp, float top_p, uint32_t rng, float *p,
+                       int *tokens, cudaStream_t s, uint64_t *launches) {
+    if (T <= 0) return;
+    k_sample<<<T, SP_THREADS, 0, s>>>(logits, V, temp, top_p, rng, p, tokens);
+    LAUNCH_COUNT(launches);
+}

@@ -200,6 +200,38 @@ int moe_dense_forward(moe_ctx *ctx, int layer, const float *h_post, int n_tokens
 int moe_dense_forward_device(moe_ctx *ctx, int layer, const float *d_h_post, int n_tokens,
                              float *d_out, void *stream);
 
+/* ------------------------------------------------- output head, sampling */
+/* The output projection (lm_head, infer.m:1937-1941; GGUF output.weight
+ * [vocab x H], VOCAB_SIZE 129280) kept as fp16 like the dense layers (any
+ * GGUF type above), and its logits for n_tokens rows of final hidden states
+ * (after the output RMSNorm): logits[t] = W h[t], fp32 [n_tokens x vocab]. */
+int moe_load_lm_head(moe_ctx *ctx, int vocab, const void *w, int type);
+/* Synthetic head: fp16 of N(0, w_sigma) from the generator's stream of
+ * (layer 0, expert id n_experts + 2, gate kind). */
+int moe_init_lm_head_synthetic(moe_ctx *ctx, int vocab, uint64_t seed, double w_sigma);
+/* The kept fp16 weights back (dst_size >= vocab * H * 2). */
+int moe_read_lm_head(moe_ctx *ctx, void *dst, size_t dst_size);
+int moe_lm_head(moe_ctx *ctx, const float *h, int n_tokens, float *logits);
+int moe_lm_head_device(moe_ctx *ctx, const float *d_h, int n_tokens, float *d_logits, void *stream);
+
+/* The next token of each of n_tokens rows of `vocab` logits, as the
+ * reference's sample_top_p (infer.m:419-456): argmax (first index of the
+ * largest logit) when temp <= 0; otherwise softmax(logits / temp), the
+ * smallest prefix of the descending order whose mass reaches top_p, one
+ * xorshift32 draw r = rand_unit() * (that mass), and the first token of the
+ * prefix at which the running mass reaches r.  Probabilities that are equal
+ * are taken in index order.  Row t uses the (t + 1)-th xorshift32 state after
+ * *rng_state; the host entry advances *rng_state by n_tokens when temp > 0
+ * (the reference's generator starts at 0xa1b2c3d4, infer.m:411).  The
+ * cumulative sums are exact (fixed point, 2^-40) where the reference adds in
+ * fp32, so a draw within fp32 rounding of a boundary may pick a neighbour. */
+int moe_sample(moe_ctx *ctx, const float *logits, int n_tokens, int vocab, float temp, float top_p,
+               uint32_t *rng_state, int *tokens);
+int moe_sample_device(moe_ctx *ctx, const float *d_logits, int n_tokens, int vocab, float temp,
+                      float top_p, uint32_t rng_state, int *d_tokens, void *stream);
+/* The xorshift32 state after n draws (rand_unit, infer.m:412-418). */
+uint32_t moe_rng_advance(uint32_t state, int n);
+
 /* ---------------------------------------------------------------- forward */
 /* The full MoE block for n_tokens tokens held by this rank (host buffers):
  * out[t] = sum_k w_k E_{idx_k}(h[t]) + shared(h[t]), fp32 [n_tokens x H].

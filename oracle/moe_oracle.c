@@ -642,3 +642,72 @@ void or_dense_ffn(const uint16_t *gate, const uint16_t *up, const uint16_t *down
     }
     free(g);
 }
+
+/* ------------------------------------------------------------------------ */
+/* next-token choice (infer.m:390-394, 405-456)                              */
+/* ------------------------------------------------------------------------ */
+/* infer.m:390-394: the first index of the largest value */
+int or_argmax(const float *x, int n) {
+    int b = 0;
+    float v = x[0];
+    for (int i = 1; i < n; i++)
+        if (x[i] > v) { v = x[i]; b = i; }
+    return b;
+}
+
+/* infer.m:412-418 */
+float or_rand_unit(uint32_t *state) {
+    uint32_t x = *state;
+    x ^= x << 13; x ^= x >> 17; x ^= x << 5;
+    *state = x;
+    return (x & 0xFFFFFFu) * (1.0f / (float)0x1000000);
+}
+
+typedef struct { float p; int idx; } or_pi;
+/* descending by p; equal p in index order (qsort's order for ties is
+ * unspecified in the reference; this is the order a stable sort gives) */
+static int or_cmp_pi(const void *a, const void *b) {
+    const or_pi *x = (const or_pi *)a, *y = (const or_pi *)b;
+    if (x->p != y->p) return x->p < y->p ? 1 : -1;
+    return (x->idx > y->idx) - (x->idx < y->idx);
+}
+
+/* infer.m:419-456 (sample_top_p), the draw taken from and written back to
+ * *state; cum_out / r_out (may be NULL) return the nucleus mass and the draw */
+int or_sample_top_p(const float *logits, int n, float temp, float top_p, uint32_t *state, float *cum_out,
+                    float *r_out) {
+    if (temp <= 0.0f) return or_argmax(logits, n);
+    or_pi *buf = (or_pi *)malloc(sizeof(or_pi) * (size_t)n);
+    float inv_t = 1.0f / temp;
+    float maxv = -1e30f;
+    for (int i = 0; i < n; i++) {
+        float v = logits[i] * inv_t;
+        if (v > maxv) maxv = v;
+    }
+    float sum = 0;
+    for (int i = 0; i < n; i++) {
+        float v = logits[i] * inv_t;
+        float p = expf(v - maxv);
+        buf[i].p = p; buf[i].idx = i; sum += p;
+    }
+    float inv_s = 1.0f / sum;
+    for (int i = 0; i < n; i++) buf[i].p *= inv_s;
+    qsort(buf, (size_t)n, sizeof(or_pi), or_cmp_pi);
+    float cum = 0;
+    int cutoff = n;
+    for (int i = 0; i < n; i++) {
+        cum += buf[i].p;
+        if (cum >= top_p) { cutoff = i + 1; break; }
+    }
+    float r = or_rand_unit(state) * cum;
+    if (cum_out) *cum_out = cum;
+    if (r_out) *r_out = r;
+    float c = 0;
+    int tok = buf[cutoff - 1].idx;
+    for (int i = 0; i < cutoff; i++) {
+        c += buf[i].p;
+        if (r <= c) { tok = buf[i].idx; break; }
+    }
+    free(buf);
+    return tok;
+}

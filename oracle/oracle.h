@@ -123,6 +123,12 @@ void or_dense_ffn(const uint16_t *gate, const uint16_t *up, const uint16_t *down
                   int H, int Id, const float *x, int T, float *out,
                   int acc_double, int n_threads);
 
+/* ---- next-token choice (infer.m:390-394, 405-456) ---- */
+int   or_argmax(const float *x, int n);
+float or_rand_unit(uint32_t *state);
+int   or_sample_top_p(const float *logits, int n, float temp, float top_p,
+                      uint32_t *state, float *cum_out, float *r_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -92,6 +92,13 @@ def lib():
         L.or_to_f16.argtypes = [C.c_int, C.c_void_p, _u16p, C.c_size_t]
         L.or_mv_f16.argtypes = [_u16p, _f32p, _f32p, C.c_int, C.c_int, C.c_int, C.c_int]
         L.or_dense_ffn.argtypes = [_u16p, _u16p, _u16p, C.c_int, C.c_int, _f32p, C.c_int, _f32p, C.c_int, C.c_int]
+        L.or_argmax.restype = C.c_int
+        L.or_argmax.argtypes = [_f32p, C.c_int]
+        L.or_rand_unit.restype = C.c_float
+        L.or_rand_unit.argtypes = [C.POINTER(C.c_uint32)]
+        L.or_sample_top_p.restype = C.c_int
+        L.or_sample_top_p.argtypes = [_f32p, C.c_int, C.c_float, C.c_float, C.POINTER(C.c_uint32),
+                                      C.POINTER(C.c_float), C.POINTER(C.c_float)]
         _lib = L
     return _lib
 
@@ -101,7 +108,8 @@ def ref_available() -> bool:
 
 
 def ref():
-    """The reference's own quant.c / route() / silu_mul / rms_norm."""
+    """The reference's own quant.c / route() / silu_mul / rms_norm / argmax /
+    sample_top_p."""
     global _ref
     if _ref is None:
         R = C.CDLL(REF_PATH)
@@ -117,6 +125,10 @@ def ref():
         R.ref_moe_token_cpu.restype = C.c_int
         R.ref_moe_token_cpu.argtypes = [C.POINTER(C.c_void_p), C.c_int, _f32p, _f32p, _f32p, _f32p, C.c_int,
                                         _f32p, C.c_void_p, C.c_void_p, C.c_int]
+        R.ref_argmax.restype = C.c_int
+        R.ref_argmax.argtypes = [_f32p, C.c_int]
+        R.ref_sample_top_p.restype = C.c_int
+        R.ref_sample_top_p.argtypes = [_f32p, C.c_int, C.c_float, C.c_float, C.POINTER(C.c_uint32)]
         _ref = R
     return _ref
 
@@ -268,6 +280,15 @@ def dense_ffn(gate, up, down, x, acc_double=True, threads=8):
     lib().or_dense_ffn(np.ascontiguousarray(gate, np.uint16), np.ascontiguousarray(up, np.uint16),
                        np.ascontiguousarray(down, np.uint16), H, Id, x, x.shape[0], out, int(acc_double), threads)
     return out
+
+
+def sample_top_p(logits, temp: float, top_p: float, state: int):
+    """(token, next state, nucleus mass, draw) of one row, as infer.m:419-456."""
+    st = C.c_uint32(state)
+    cum, r = C.c_float(0), C.c_float(0)
+    lg = np.ascontiguousarray(logits, np.float32)
+    tok = lib().or_sample_top_p(lg, lg.size, temp, top_p, C.byref(st), C.byref(cum), C.byref(r))
+    return tok, st.value, cum.value, r.value
 
 
 def moe_layer(cfg: dict, experts: dict, router_w, bias, x, force_idx=None, force_w=None,

@@ -4,8 +4,8 @@
  *
  * oracle/Makefile compiles this file together with the reference's quant.c
  * (unmodified, from where it lies) and with rms_norm / sigmoidf / silu_mul /
- * route extracted verbatim from the reference's infer.m into a temporary file
- * (REF_SNIPPET).  Nothing of the reference is written into this repository;
+ * route / argmax / rand_unit / sample_top_p extracted verbatim from the
+ * reference's infer.m into a temporary file (REF_SNIPPET).  Nothing of the reference is written into this repository;
  * the only output is oracle/_ref/libref_moe.so.
  *
  * infer.m itself cannot be compiled on Linux (Objective-C, Metal, Accelerate),
@@ -37,6 +37,15 @@ void ref_silu_mul(const float *g, const float *u, float *o, int d) { silu_mul(g,
 void ref_rms_norm(const float *x, const float *w, float *o, int d) { rms_norm(x, w, o, d); }
 void ref_route(const float *logits, const float *bias, int K, int *exp_idx, float *exp_w) {
     route(logits, bias, K, exp_idx, exp_w);
+}
+/* argmax / rand_unit / sample_top_p (infer.m:390-456), the generator state
+ * handed in and out */
+int ref_argmax(const float *x, int n) { return argmax(x, n); }
+int ref_sample_top_p(const float *logits, int n, float temp, float top_p, uint32_t *state) {
+    g_rng = *state;
+    int t = sample_top_p(logits, n, temp, top_p);
+    *state = g_rng;
+    return t;
 }
 
 /* ------------------------------------------------------------------------ */

@@ -1,0 +1,146 @@
+"""The output head through the C ABI against the oracle: lm_head
+(infer.m:1937-1941) over fp16 weights kept from GGUF bytes, at a small
+vocabulary and at DeepSeek-V3's (129280 x 7168); the next-token choice
+(sample_top_p / argmax, infer.m:390-456) on rows of logits with successive
+generator states, against the oracle restatement that is itself pinned to the
+reference's own sample_top_p."""
+import numpy as np
+import pytest
+
+HEAD_TOL = 1e-5   # fp16 weights x fp32 activations, fp32 accumulation vs the oracle's fp64
+REF_STATE = 0xA1B2C3D4   # the reference generator's start (infer.m:411)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("qtype,T", [(1, 1), (1, 3), (14, 5), (0, 2)])
+def test_lm_head_matches_oracle(cuda_lib, oracle, qtype, T):
+    from test_gpu_moe import rel_err, small_cfg
+    cfg = small_cfg()
+    H, V = cfg.hidden, 3000
+    rng = np.random.default_rng(qtype * 10 + T)
+    w = (rng.standard_normal(V * H) * 0.05).astype(np.float32)
+    blob = {0: w, 1: w.astype(np.float16), 14: oracle.quantize(w, oracle.TYPE_Q6_K)}[qtype]
+    bits = oracle.to_f16(blob, qtype, V * H).reshape(V, H)
+    m = cuda_lib.MoE(cfg)
+    m.load_lm_head(blob, qtype, V)
+    assert np.array_equal(m.read_lm_head(), bits)
+    h = oracle.normal(50 + T, oracle.stream(0, 0, oracle.KIND_ACT), T * H, 1.0).reshape(T, H)
+    got = m.lm_head(h)
+    ref = np.stack([oracle.mv_f16(bits, h[t]) for t in range(T)])
+    assert rel_err(got, ref) < HEAD_TOL
+    m.close()
+
+
+@pytest.mark.gpu
+def test_lm_head_full_size(cuda_lib, oracle):
+    """DeepSeek-V3's head (vocab 129280, hidden 7168) on the synthetic
+    generator: sampled weight rows against the oracle's generator, the logits
+    of one token against the oracle on the weights read back."""
+    from test_gpu_moe import rel_err
+    cfg = cuda_lib.MoeConfig(n_layers=1, max_tokens=2)
+    H, V = cfg.hidden, 129280
+    m = cuda_lib.MoE(cfg)
+    m.init_lm_head_synthetic(V, seed=4, w_sigma=0.02)
+    W = m.read_lm_head()
+    for r in (0, 1, V // 2, V - 1):
+        v = oracle.normal(4, oracle.stream(0, cfg.n_experts + 2, oracle.KIND_GATE), H, 0.02, first=r * H)
+        assert np.array_equal(W[r], oracle.to_f16(v, oracle.TYPE_F32, H)), r
+    h = oracle.normal(13, oracle.stream(0, 0, oracle.KIND_ACT), H, 1.0).reshape(1, H)
+    got = m.lm_head(h)
+    ref = oracle.mv_f16(W, h[0])[None]
+    assert rel_err(got, ref) < HEAD_TOL
+    m.close()
+
+
+def _oracle_rows(oracle, lg, temp, top_p, state):
+    toks = []
+    for row in lg:
+        t, state, _, _ = oracle.sample_top_p(row, temp, top_p, state)
+        toks.append(t)
+    return np.array(toks), state
+
+
+def _exact_rows(lg, temp, top_p, state):
+    """The kernel's semantics in numpy: fp32 probabilities as the reference
+    forms them, cumulative sums in float64 (the kernel's are exact to 2^-40),
+    equal probabilities in index order.  Returns tokens, the next state and
+    each row's rank of every token."""
+    toks, ranks = [], []
+    for l in lg:
+        inv_t = np.float32(1.0) / np.float32(temp)
+        v = (l * inv_t).astype(np.float32)
+        e = np.exp((v - v.max()).astype(np.float32)).astype(np.float32)
+        p = (e * (np.float32(1.0) / np.float32(e.astype(np.float64).sum()))).astype(np.float32)
+        order = np.lexsort((np.arange(p.size), -p.astype(np.float64)))
+        c = np.cumsum(p[order].astype(np.float64))
+        k = min(int(np.searchsorted(c, np.float64(np.float32(top_p)), "left")), p.size - 1)
+        state ^= (state << 13) & 0xFFFFFFFF
+        state ^= state >> 17
+        state ^= (state << 5) & 0xFFFFFFFF
+        r = np.float32(np.float32((state & 0xFFFFFF) * (1.0 / 0x1000000)) * np.float32(c[k]))
+        toks.append(order[min(int(np.searchsorted(c[:k + 1], np.float64(r), "left")), k)])
+        rank = np.empty(p.size, np.int64)
+        rank[order] = np.arange(p.size)
+        ranks.append(rank)
+    return np.array(toks), state, ranks
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("V,scale,temp,top_p,peaked", [(129280, 2.0, 0.6, 0.95, False),
+                                                       (129280, 0.3, 1.0, 0.95, False),
+                                                       (1000, 3.0, 0.6, 0.95, True), (1000, 1.0, 1.5, 0.5, True),
+                                                       (4096, 2.0, 0.8, 1.0, True)])
+def test_sample_matches_oracle(cuda_lib, oracle, V, scale, temp, top_p, peaked):
+    """16 rows per call, 4 calls with the state carried over.  The kernel adds
+    probabilities exactly where the reference adds them in fp32, left to right
+    over the sorted vocabulary; with a nucleus of thousands of tokens that
+    rounding moves the reference's pick by up to ~10 ranks (the oracle, which
+    is the reference's own arithmetic, and an exact-sum model agree on 42 of
+    64 draws at V = 129280, temp 0.6).  So: the tokens of the exact-sum model
+    up to 2 draws whose pick moves by at most 2 ranks (expf ulps), the same
+    generator states as the reference, and the reference's own tokens where
+    the nucleus is small (peaked rows)."""
+    from test_gpu_moe import small_cfg
+    cfg = small_cfg(max_tokens=16)
+    m = cuda_lib.MoE(cfg)
+    rng = np.random.default_rng(V + int(scale * 10))
+    state, ostate, estate = REF_STATE, REF_STATE, REF_STATE
+    miss_exact = miss_ref = 0
+    for call in range(4):
+        lg = (rng.standard_normal((16, V)) * scale).astype(np.float32)
+        got, state = m.sample(lg, temp, top_p, state)
+        want, ostate = _oracle_rows(oracle, lg, temp, top_p, ostate)
+        exact, estate, ranks = _exact_rows(lg, temp, top_p, estate)
+        assert state == ostate == estate
+        for g, e, rk in zip(got, exact, ranks):
+            assert abs(int(rk[g]) - int(rk[e])) <= 2, (g, e)
+        miss_exact += int(np.sum(got != exact))
+        miss_ref += int(np.sum(got != want))
+    assert miss_exact <= 2, miss_exact
+    if peaked:
+        assert miss_ref <= 1, miss_ref
+    m.close()
+
+
+@pytest.mark.gpu
+def test_sample_argmax_and_ties(cuda_lib, oracle):
+    """temp <= 0 is argmax (first index of the largest logit, no draw); equal
+    probabilities are taken in index order; the state does not move."""
+    from test_gpu_moe import small_cfg
+    cfg = small_cfg(max_tokens=8)
+    m = cuda_lib.MoE(cfg)
+    rng = np.random.default_rng(3)
+    lg = rng.standard_normal((8, 5000)).astype(np.float32)
+    lg[1, [17, 4000]] = 9.0           # a tie for the maximum: the first index
+    lg[2, :] = 0.0                    # all equal
+    got, st = m.sample(lg, 0.0, 0.95, 77)
+    assert st == 77
+    assert got.tolist() == [oracle.lib().or_argmax(np.ascontiguousarray(r), r.size) for r in lg]
+    # ties inside the nucleus: a block of equal top logits
+    lg2 = np.full((4, 3000), -20.0, np.float32)
+    lg2[:, 100:110] = 5.0
+    lg2[:, 2000:2010] = 5.0
+    got, st = m.sample(lg2, 0.7, 0.9, 12345)
+    want, ost = _oracle_rows(oracle, lg2, 0.7, 0.9, 12345)
+    assert st == ost and np.array_equal(got, want)
+    m.close()

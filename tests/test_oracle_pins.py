@@ -2,6 +2,7 @@
 golden fixtures made by tests/golden/make_golden.py from gguf-py and from the
 reference's quant.c / route() built in place -- and, where the reference
 build is present, against it directly."""
+import ctypes as C
 import os
 
 import numpy as np
@@ -190,3 +191,24 @@ def test_dense_ffn_composition(oracle):
     assert np.array_equal(out, ref) or float(np.max(np.abs(out - ref)) / np.max(np.abs(ref))) < 1e-6
     y = oracle.mv_f16(g.view(np.uint16), x[0], acc_double=False)
     assert float(np.max(np.abs(y - G[0])) / np.max(np.abs(G[0]))) < 1e-5
+
+
+def test_sampler_vs_reference(oracle):
+    """or_sample_top_p / or_argmax against the reference's own sample_top_p
+    and argmax (infer.m:390-456, built in place): the same token and the same
+    generator state over many draws, logits without equal probabilities (the
+    reference's qsort leaves their order open)."""
+    if not oracle.ref_available():
+        pytest.skip("reference build not present")
+    R = oracle.ref()
+    rng = np.random.default_rng(12)
+    for n, scale in ((1000, 3.0), (129280, 2.0), (50, 0.5)):
+        for trial in range(6):
+            lg = (rng.standard_normal(n) * scale).astype(np.float32)
+            assert R.ref_argmax(lg, n) == oracle.lib().or_argmax(lg, n)
+            for temp, top_p in ((0.6, 0.95), (1.0, 0.5), (0.0, 0.9), (2.0, 1.0)):
+                s0 = int(rng.integers(1, 2**32))
+                st = C.c_uint32(s0)
+                want = R.ref_sample_top_p(lg, n, temp, top_p, C.byref(st))
+                tok, s1, _, _ = oracle.sample_top_p(lg, temp, top_p, s0)
+                assert (tok, s1) == (want, st.value), (n, trial, temp, top_p)
