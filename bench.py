@@ -57,7 +57,9 @@ EXTRA = {
     "stack_b32": dict(B=32, name="config4_stack58_b32"),
     "prefill4096": dict(B=4096, name="config5_prefill4096_1layer"),
     "dense_b1": dict(B=1, name="dense_ffn_layers0to2_b1"),
+    "head_b1": dict(B=1, name="lm_head_sample_b1"),
 }
+VOCAB = 129280              # VOCAB_SIZE of DeepSeek-V3
 DENSE_I = 18432             # DENSE_INTERMEDIATE (infer.m:59)
 DENSE_LAYERS = 3            # FIRST_MOE_LAYER (infer.m:46)
 Q4_DOWN_BYTES = H * (I // 256) * 144         # 8,257,536
@@ -485,7 +487,9 @@ def run_extra(args):
       prefill4096  4096 tokens through one layer per moe_prefill_device call
                    (tcgen05 GEMMs over fp16-dequantized weight tiles)
       dense_b1     one token through the three dense FFN layers (0-2) per
-                   step, moe_dense_forward_device per layer"""
+                   step, moe_dense_forward_device per layer
+      head_b1      one token through lm_head (129280 x 7168 fp16) and the
+                   top-p sampler (temp 0.6, top_p 0.95)"""
     import torch
     import flash_deepseek_b200 as F
     W = EXTRA[args.workload]
@@ -707,6 +711,70 @@ def run_extra(args):
                "d2h_bytes_per_step": DENSE_LAYERS * H * 4, "timer": "host wall clock (synchronous calls)"}
         extra = {"intermediate": DENSE_I, "layers": DENSE_LAYERS, "experts": 0,
                  "l2": "not flushed: 2.38 GB of weights per step cycle through the 126 MB L2"}
+    elif args.workload == "head_b1":
+        # one decode token through the output head and the sampler
+        # (infer.m:1937-1941, 419-456): fp16 [129280 x 7168] = 1.85 GB per step
+        cfg = F.MoeConfig(n_layers=1, max_tokens=1)
+        moe = F.MoE(cfg, device=local)
+        moe.init_lm_head_synthetic(VOCAB, seed=0, w_sigma=0.02)
+        xs = [torch.randn(1, H, generator=g).to(dev) for _ in range(N_POOL)]
+        logits = torch.empty(1, VOCAB, device=dev)
+        tok = torch.empty(1, dtype=torch.int32, device=dev)
+        stream = torch.cuda.ExternalStream(moe.stream, device=dev)
+        state = 0xA1B2C3D4
+
+        def step(i):
+            moe.lm_head_device(xs[i % N_POOL], 1, logits, stream=moe.stream)
+            moe.sample_device(logits, 1, VOCAB, 0.6, 0.95, (state + i) & 0xFFFFFFFF, tok, stream=moe.stream)
+        with torch.cuda.stream(stream):
+            for i in range(args.warmup):
+                step(i)
+        torch.cuda.synchronize()
+        n = args.steps
+        l0 = moe.kernel_launches
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(n)]
+        with torch.cuda.stream(stream):
+            for i in range(n):
+                ev[i][0].record(stream)
+                moe.lm_head_device(xs[i % N_POOL], 1, logits, stream=moe.stream)
+                ev[i][1].record(stream)
+                moe.sample_device(logits, 1, VOCAB, 0.6, 0.95, (state + i) & 0xFFFFFFFF, tok, stream=moe.stream)
+                ev[i][2].record(stream)
+        torch.cuda.synchronize()
+        head_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / n
+        samp_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / n
+        ms = sum(e[0].elapsed_time(e[2]) for e in ev)
+        launches = moe.kernel_launches - l0
+        ms_step = ms / n
+        value = n / (ms / 1e3)
+        unit = "tokens/s"
+        head_bytes = VOCAB * H * 2 + H * 4 + VOCAB * 4
+        roof = {"bound": "hbm", "kernel": "k_lm_head (the sampler, k_sample, is latency-bound: see phase_ms)",
+                "achieved": round(head_bytes / (head_ms / 1e3) / 1e9, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(head_bytes / (head_ms / 1e3) / 1e9 / peak, 4), "peak_source": peak_kind,
+                "algorithmic_bytes_per_launch": head_bytes, "traffic": None}
+        extra = {"vocab": VOCAB, "temp": 0.6, "top_p": 0.95, "experts": 0,
+                 "l2": "not flushed: 1.85 GB of weights per step", "phase_ms": {"lm_head": round(head_ms, 4),
+                                                                                 "sample": round(samp_ms, 4)}}
+        # end to end: moe_lm_head (hidden in, logits out) then moe_sample (logits in, token out)
+        import ctypes as C
+        h_pin = xs[0].cpu().pin_memory().numpy()
+        lg_pin = torch.empty(1, VOCAB).pin_memory().numpy()
+        t_pin = np.empty(1, np.int32)
+        lib = moe.lib
+        st = C.c_uint32(state)
+        n_e2e = max(2, n // 4)
+        t_0 = None
+        for i in range(n_e2e + 1):
+            if i == 1:
+                t_0 = time.perf_counter()
+            if (lib.moe_lm_head(moe.ctx, h_pin.ctypes.data, 1, lg_pin.ctypes.data) != 0 or
+                    lib.moe_sample(moe.ctx, lg_pin.ctypes.data, 1, VOCAB, 0.6, 0.95, C.byref(st),
+                                   t_pin.ctypes.data) != 0):
+                raise RuntimeError(lib.moe_last_error(moe.ctx))
+        e2e_s = time.perf_counter() - t_0
+        e2e = {"value": round(n_e2e / e2e_s, 2), "unit": "tokens/s", "h2d_bytes_per_step": H * 4 + VOCAB * 4,
+               "d2h_bytes_per_step": VOCAB * 4 + 4, "timer": "host wall clock (synchronous calls)"}
     else:  # prefill4096: one moe_prefill_device call (tcgen05 GEMMs) per step and rank
         from flash_deepseek_b200 import ep
         world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -783,11 +851,12 @@ def run_extra(args):
             "scaling": "strong", "vs_baseline": None,
             "dtype": ("fp16 operands (dequantized weights, activations) on tcgen05, fp32 accumulation"
                       if args.workload == "prefill4096" else
-                      "fp16 weights, fp32 activations, fp32 accumulation" if args.workload == "dense_b1" else
+                      "fp16 weights, fp32 activations, fp32 accumulation" if args.workload in ("dense_b1", "head_b1")
+                      else
                       "int8 tensor-core products of Q4_K/Q6_K integers and 21-bit activation planes (exact), fp32 "
                       "accumulation"),
             "data": ("synthetic: random-init N(0,0.02) weights rounded to fp16 on device, N(0,1) tokens"
-                     if args.workload == "dense_b1" else
+                     if args.workload in ("dense_b1", "head_b1") else
                      "synthetic: random-init N(0,0.02) weights quantized on device, N(0,1) tokens"),
             "config": dict({"workload": W["name"], "global_batch": W["B"], "hidden": H, "intermediate": I,
                             "experts": E, "parallelism": "ep1"}, **extra),
@@ -858,13 +927,14 @@ def other_configs(args):
     GPU after the default one (each in its own context, with its own warm-up,
     timed loop, L2 handling and clock sampling, as its --workload line would
     be): config 2 (one token), config 1 (one expert per call), config 5 (4096-
-    token prefill), config 4 (the 58-layer stack at batch 1) and the dense FFN
-    layers 0-2 at batch 1."""
+    token prefill), config 4 (the 58-layer stack at batch 1), the dense FFN
+    layers 0-2 and the output head with the sampler at batch 1."""
     keep = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "dtype", "roofline", "roofline_down",
             "roofline_tc", "roofline_phases",
             "phase_ms", "e2e", "gpu_launches", "clocks", "config")
     out = {}
-    for wl, steps in (("decode_b1", 100), ("expert1", 256), ("prefill4096", 3), ("stack_b1", 3), ("dense_b1", 100)):
+    for wl, steps in (("decode_b1", 100), ("expert1", 256), ("prefill4096", 3), ("stack_b1", 3), ("dense_b1", 100),
+                      ("head_b1", 100)):
         a = argparse.Namespace(**vars(args))
         a.workload, a.steps, a.warmup, a.no_cpu = wl, steps, 3, True
         try:

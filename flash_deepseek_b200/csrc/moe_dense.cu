@@ -105,6 +105,7 @@ template <bool GLU>
 __device__ __forceinline__ void dense_rows(const __half *__restrict__ Wg, const __half *__restrict__ Wu,
                                            const float *__restrict__ x, int T, int H, int Id,
                                            float *__restrict__ act) {
+    constexpr int U = GLU ? DN_U_GU : 7;   // 16-byte loads in flight per lane (7 divides H / 256 = 28)
     extern __shared__ float4 dn_smem[];
     float *xs = reinterpret_cast<float *>(dn_smem);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -113,13 +114,13 @@ __device__ __forceinline__ void dense_rows(const __half *__restrict__ Wg, const 
     for (int t0 = 0; t0 < T; t0 += DN_TT_GU) {
         const int tt = min(DN_TT_GU, T - t0);
         // the first row's first vectors are in flight while x is staged
-        uint4 g[DN_U_GU], u[DN_U_GU];
-        const bool pre = r_first < Id && nv >= DN_U_GU;
+        uint4 g[U], u[GLU ? U : 1];
+        const bool pre = r_first < Id && nv >= U;
         if (pre) {
 #pragma unroll
-            for (int j = 0; j < DN_U_GU; j++) {
+            for (int j = 0; j < U; j++) {
                 g[j] = ld_weight16(reinterpret_cast<const uint4 *>(Wg + (size_t)r_first * H) + lane + j * 32);
-                if (GLU) u[j] = ld_weight16(reinterpret_cast<const uint4 *>(Wu + (size_t)r_first * H) + lane + j * 32);
+                if constexpr (GLU) u[j] = ld_weight16(reinterpret_cast<const uint4 *>(Wu + (size_t)r_first * H) + lane + j * 32);
             }
         }
         __syncthreads();
@@ -133,22 +134,22 @@ __device__ __forceinline__ void dense_rows(const __half *__restrict__ Wg, const 
             const uint4 *pu = reinterpret_cast<const uint4 *>(Wu + (size_t)r * H) + lane;
             const float *xl = xs + lane * 4;
             int i = 0;
-            for (; i + DN_U_GU <= nv; i += DN_U_GU) {
+            for (; i + U <= nv; i += U) {
                 if (!(pre && r == r_first && i == 0)) {
 #pragma unroll
-                    for (int j = 0; j < DN_U_GU; j++) {
+                    for (int j = 0; j < U; j++) {
                         g[j] = ld_weight16(pg + (i + j) * 32);
-                        if (GLU) u[j] = ld_weight16(pu + (i + j) * 32);
+                        if constexpr (GLU) u[j] = ld_weight16(pu + (i + j) * 32);
                     }
                 }
 #pragma unroll
-                for (int j = 0; j < DN_U_GU; j++)
+                for (int j = 0; j < U; j++)
 #pragma unroll
                     for (int t = 0; t < DN_TT_GU; t++)
                         if (t < tt) {
                             const float *xp = xl + (size_t)t * H + (i + j) * 256;
                             ag[t] = dot8(g[j], xp, ag[t]);
-                            if (GLU) au[t] = dot8(u[j], xp, au[t]);
+                            if constexpr (GLU) au[t] = dot8(u[j], xp, au[t]);
                         }
             }
             for (; i < nv; i++) {
