@@ -87,6 +87,7 @@ struct moe_ctx {
     int vocab = 0;
     float *head_logits = nullptr, *sample_p = nullptr;  // [max_tok x n] each
     int *sample_tok = nullptr;                           // [max_tok]
+    void *sample_ws = nullptr;                           // moe_sample_ws_bytes(max_tok)
     size_t sample_n = 0;
     // workspace
     float *part = nullptr, *logits = nullptr, *d_in = nullptr, *d_out = nullptr, *h_post = nullptr;
@@ -501,6 +502,7 @@ void moe_destroy(moe_ctx *c) {
     cudaFree(c->head_logits);
     cudaFree(c->sample_p);
     cudaFree(c->sample_tok);
+    cudaFree(c->sample_ws);
     void *bufs[] = {c->part, c->logits, c->rl_counters, c->d_in, c->d_out, c->h_post, c->idx, c->wts, c->idx_given, c->w_given, c->bias_tmp, c->xop, c->plan.counts,
                     c->plan.pair_expert, c->plan.pair_token, c->plan.pair_w, c->plan.chunk_expert,
                     c->plan.chunk_pair0, c->plan.chunk_ntok, c->plan.chunk_order, c->plan.slot_pair, c->plan.error, c->counter, c->act,
@@ -895,6 +897,7 @@ static int sample_scratch(moe_ctx *c, int n) {
     CK(cudaMalloc((void **)&c->head_logits, m * sizeof(float)));
     CK(cudaMalloc((void **)&c->sample_p, m * sizeof(float)));
     CK(cudaMalloc((void **)&c->sample_tok, c->max_tok * sizeof(int)));
+    if (!c->sample_ws) CK(cudaMalloc(&c->sample_ws, moe_sample_ws_bytes(c->max_tok)));
     c->sample_n = n;
     return MOE_OK;
 }
@@ -1574,7 +1577,7 @@ int moe_sample_device(moe_ctx *c, const float *d_logits, int T, int vocab, float
     DeviceScope ds(c->device);
     int rc = sample_scratch(c, vocab);
     if (rc) return rc;
-    moe_launch_sample(d_logits, T, vocab, temp, top_p, rng_state, c->sample_p, d_tokens,
+    moe_launch_sample(d_logits, T, vocab, temp, top_p, rng_state, c->sample_p, c->sample_ws, d_tokens,
                       stream ? (cudaStream_t)stream : c->stream, &c->launches);
     CK(cudaGetLastError());
     return MOE_OK;

@@ -286,11 +286,12 @@ void moe_launch_dense_ffn(const __half *w, int H, int Id, const float *x, int T,
 // logits [T x V] = W [V x H] fp16 . h [T x H] (moe_dense.cu)
 void moe_launch_lm_head(const __half *w, int H, int V, const float *h, int T, float *logits, cudaStream_t s,
                         uint64_t *launches);
-// temperature + top-p sampling (or argmax at temp <= 0) of T rows of V logits,
-// one CTA per row (moe_sample.cu); p: [T x V] fp32 scratch; row t draws the
-// (t + 1)-th xorshift32 state after `rng`
+// temperature + top-p sampling (or argmax at temp <= 0) of T rows of V logits
+// (moe_sample.cu); p: [T x V] fp32 scratch; ws: moe_sample_ws_bytes(T) bytes;
+// row t draws the (t + 1)-th xorshift32 state after `rng`
+size_t moe_sample_ws_bytes(int rows);
 void moe_launch_sample(const float *logits, int T, int V, float temp, float top_p, uint32_t rng, float *p,
-                       int *tokens, cudaStream_t s, uint64_t *launches);
+                       void *ws, int *tokens, cudaStream_t s, uint64_t *launches);
 // n values of a GGUF tensor of `type` (device memory) to fp16; tmp holds n
 // floats for Q4_K / Q6_K
 void moe_launch_to_f16(int type, const void *src, __half *dst, size_t n, float *tmp, cudaStream_t s,

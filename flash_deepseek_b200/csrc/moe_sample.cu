@@ -257,11 +257,307 @@ __global__ void __launch_bounds__(SP_THREADS, 1) k_sample(const float *__restric
     if (tid == 0) tokens[blockIdx.x] = pick;
 }
 
+// ---------------------------------------------------------------------------
+// Many-CTA form of the same selection (temp > 0): SG_CTAS CTAs per row, each
+// over one slice of the vocabulary, one small kernel per pass; the per-row
+// state between passes lives in global memory (SmpRow), the histograms in
+// global memory with integer atomics (order-independent sums).
+constexpr int SG_CTAS = 128;
+constexpr int SG_THREADS = 256;
+
+struct SmpRow {
+    uint32_t pre, msk, last_cnt, tau, j1, key, m;
+    int sel2;                       // the draw lies above tau: select 2 runs
+    unsigned long long above, above1, t2;
+};
+
+struct SmpWs {
+    float *part_max, *part_sum;     // [T][SG_CTAS]
+    unsigned int *hcnt;             // [T][256]
+    unsigned long long *hsum;       // [T][256]
+    unsigned int *cnt;              // [T][SG_CTAS]
+    SmpRow *row;                    // [T]
+};
+
+__device__ __forceinline__ void slice_of(int V, int &s0, int &s1) {
+    s0 = (int)((long long)V * blockIdx.x / gridDim.x);
+    s1 = (int)((long long)V * (blockIdx.x + 1) / gridDim.x);
+}
+
+// CTA-wide reductions for SG_THREADS threads; every thread gets the result
+__device__ __forceinline__ float sg_max(float v, float *red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    v = red[0];
+    for (int w = 1; w < SG_THREADS / 32; w++) v = fmaxf(v, red[w]);
+    return v;
+}
+__device__ __forceinline__ float sg_sum(float v, float *red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    v = 0.0f;
+    for (int w = 0; w < SG_THREADS / 32; w++) v += red[w];
+    return v;
+}
+
+// pass 0: per-slice max of logits / temp; CTA 0 of a row clears its histogram,
+// state and token
+__global__ void __launch_bounds__(SG_THREADS) k_sg_max(const float *__restrict__ logits, int V, float inv_t, SmpWs w,
+                                                      int *__restrict__ tokens) {
+    __shared__ float red[SG_THREADS / 32];
+    const int t = blockIdx.y;
+    const float *l = logits + (size_t)t * V;
+    int s0, s1;
+    slice_of(V, s0, s1);
+    float mx = -1e30f;
+    for (int i = s0 + threadIdx.x; i < s1; i += SG_THREADS) mx = fmaxf(mx, __fmul_rn(l[i], inv_t));
+    mx = sg_max(mx, red);
+    if (threadIdx.x == 0) w.part_max[t * SG_CTAS + blockIdx.x] = mx;
+    if (blockIdx.x == 0) {
+        for (int d = threadIdx.x; d < 256; d += SG_THREADS) {
+            w.hcnt[t * 256 + d] = 0;
+            w.hsum[t * 256 + d] = 0;
+        }
+        if (threadIdx.x == 0) {
+            SmpRow r = {};
+            w.row[t] = r;
+            tokens[t] = V - 1;   // replaced by k_sg_final
+        }
+    }
+}
+
+// pass 1: exp(logit / temp - max) into p, per-slice sums
+__global__ void __launch_bounds__(SG_THREADS) k_sg_exp(const float *__restrict__ logits, int V, float inv_t, SmpWs w,
+                                                      float *__restrict__ pbuf) {
+    __shared__ float red[SG_THREADS / 32];
+    const int t = blockIdx.y;
+    const float *l = logits + (size_t)t * V;
+    float *p = pbuf + (size_t)t * V;
+    float mx = -1e30f;
+    for (int g = 0; g < SG_CTAS; g++) mx = fmaxf(mx, w.part_max[t * SG_CTAS + g]);
+    int s0, s1;
+    slice_of(V, s0, s1);
+    float part = 0.0f;
+    for (int i = s0 + threadIdx.x; i < s1; i += SG_THREADS) {
+        const float e = expf(__fsub_rn(__fmul_rn(l[i], inv_t), mx));
+        p[i] = e;
+        part += e;
+    }
+    part = sg_sum(part, red);
+    if (threadIdx.x == 0) w.part_sum[t * SG_CTAS + blockIdx.x] = part;
+}
+
+// a histogram pass of selection `sel` (1: all keys, 2: keys above tau, only
+// when the draw lies there); `norm` first scales the slice to probabilities
+__global__ void __launch_bounds__(SG_THREADS) k_sg_hist(int V, SmpWs w, float *__restrict__ pbuf, int shift, int sel,
+                                                       int norm) {
+    __shared__ unsigned int hc[256];
+    __shared__ unsigned long long hs[256];
+    const int t = blockIdx.y;
+    const SmpRow r = w.row[t];
+    if (sel == 2 && !r.sel2) return;
+    float *p = pbuf + (size_t)t * V;
+    for (int d = threadIdx.x; d < 256; d += SG_THREADS) {
+        hc[d] = 0;
+        hs[d] = 0;
+    }
+    float inv_s = 0.0f;
+    if (norm) {
+        float sum = 0.0f;
+        for (int g = 0; g < SG_CTAS; g++) sum += w.part_sum[t * SG_CTAS + g];
+        inv_s = 1.0f / sum;
+    }
+    __syncthreads();
+    int s0, s1;
+    slice_of(V, s0, s1);
+    for (int i = s0 + threadIdx.x; i < s1; i += SG_THREADS) {
+        float v = p[i];
+        if (norm) {
+            v = __fmul_rn(v, inv_s);
+            p[i] = v;
+        }
+        const uint32_t k = __float_as_uint(v);
+        if ((sel == 2 && k <= r.tau) || (k & r.msk) != r.pre) continue;
+        const int d = (k >> shift) & 255;
+        atomicAdd(&hc[d], 1u);
+        atomicAdd(&hs[d], fx(v));
+    }
+    __syncthreads();
+    for (int d = threadIdx.x; d < 256; d += SG_THREADS)
+        if (hc[d]) {
+            atomicAdd(&w.hcnt[t * 256 + d], hc[d]);
+            atomicAdd(&w.hsum[t * 256 + d], hs[d]);
+        }
+}
+
+// resolves one digit of selection `sel` from the row's histogram (and clears
+// it); after the last digit of selection 1 it forms the nucleus, the draw and
+// which selection finds the token; after the last of selection 2, the token's key
+__global__ void __launch_bounds__(256) k_sg_pick(SmpWs w, int shift, int sel, float top_p, uint32_t rng) {
+    __shared__ unsigned int hc[256];
+    __shared__ unsigned long long hs[256];
+    const int t = blockIdx.x;
+    if (sel == 2 && !w.row[t].sel2) return;   // CTA-uniform
+    for (int d = threadIdx.x; d < 256; d += blockDim.x) {
+        hc[d] = w.hcnt[t * 256 + d];
+        hs[d] = w.hsum[t * 256 + d];
+        w.hcnt[t * 256 + d] = 0;
+        w.hsum[t * 256 + d] = 0;
+    }
+    __syncthreads();
+    if (threadIdx.x) return;
+    SmpRow r = w.row[t];
+    const unsigned long long target = sel == 1 ? (unsigned long long)((double)top_p * 1099511627776.0) : r.t2;
+    unsigned long long acc = r.above;
+    int pick = -1, lowest = -1;
+    for (int d = 255; d >= 0; d--) {
+        if (!hc[d]) continue;
+        lowest = d;
+        if (acc + hs[d] >= target) {
+            pick = d;
+            break;
+        }
+        acc += hs[d];
+    }
+    if (pick < 0 && lowest >= 0) {
+        pick = lowest;
+        acc -= hs[lowest];
+    }
+    if (pick < 0) pick = 0;
+    r.above = acc;
+    r.pre |= (uint32_t)pick << shift;
+    r.msk |= 255u << shift;
+    r.last_cnt = hc[pick];
+    if (shift == 0 && sel == 1) {
+        r.tau = r.pre;
+        r.above1 = r.above;
+        r.j1 = need_count(target, r.above1, __uint_as_float(r.tau), r.last_cnt);
+        const float cum = (float)((double)(r.above1 + (unsigned long long)r.j1 * fx(__uint_as_float(r.tau))) /
+                                  1099511627776.0);
+        uint32_t x = rng;
+        for (int i = 0; i <= t; i++) {
+            x ^= x << 13;
+            x ^= x >> 17;
+            x ^= x << 5;
+        }
+        const float rr = __fmul_rn((float)(x & 0xFFFFFFu) * (1.0f / (float)0x1000000), cum);
+        r.t2 = fx(rr);
+        r.sel2 = r.above1 >= r.t2 && r.above1 > 0;
+        if (!r.sel2) {
+            r.key = r.tau;
+            r.m = need_count(r.t2, r.above1, __uint_as_float(r.tau), r.j1);
+        }
+        r.pre = r.msk = 0;
+        r.above = 0;
+    } else if (shift == 0 && sel == 2) {
+        r.key = r.pre;
+        r.m = need_count(r.t2, r.above, __uint_as_float(r.pre), r.last_cnt);
+    }
+    w.row[t] = r;
+}
+
+// per-slice count of the token's key
+__global__ void __launch_bounds__(SG_THREADS) k_sg_count(int V, SmpWs w, const float *__restrict__ pbuf) {
+    __shared__ float red[SG_THREADS / 32];
+    const int t = blockIdx.y;
+    const uint32_t key = w.row[t].key;
+    const float *p = pbuf + (size_t)t * V;
+    int s0, s1;
+    slice_of(V, s0, s1);
+    float c = 0.0f;   // counts below 2^24: exact in fp32
+    for (int i = s0 + threadIdx.x; i < s1; i += SG_THREADS) c += __float_as_uint(p[i]) == key ? 1.0f : 0.0f;
+    c = sg_sum(c, red);
+    if (threadIdx.x == 0) w.cnt[t * SG_CTAS + blockIdx.x] = (unsigned int)c;
+}
+
+// the slice that holds the m-th element of the key (in index order) finds it
+__global__ void __launch_bounds__(SG_THREADS) k_sg_final(int V, SmpWs w, const float *__restrict__ pbuf,
+                                                        int *__restrict__ tokens) {
+    __shared__ unsigned int wsum[SG_THREADS / 32];
+    const int t = blockIdx.y;
+    const uint32_t key = w.row[t].key;
+    const unsigned int m = w.row[t].m;
+    unsigned int before = 0;
+    for (int g = 0; g < (int)blockIdx.x; g++) before += w.cnt[t * SG_CTAS + g];
+    const unsigned int mine = w.cnt[t * SG_CTAS + blockIdx.x];
+    if (!(m > before && m <= before + mine)) return;   // CTA-uniform
+    const float *p = pbuf + (size_t)t * V;
+    int s0, s1;
+    slice_of(V, s0, s1);
+    const int per = (s1 - s0 + SG_THREADS - 1) / SG_THREADS;
+    const int lo = min(s1, s0 + (int)threadIdx.x * per), hi = min(s1, lo + per);
+    unsigned int c = 0;
+    for (int i = lo; i < hi; i++) c += __float_as_uint(p[i]) == key;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    unsigned int incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) wsum[warp] = incl;
+    __syncthreads();
+    unsigned int b = before + incl - c;
+    for (int k = 0; k < warp; k++) b += wsum[k];
+    if (c && m > b && m <= b + c) {
+        for (int i = lo; i < hi; i++)
+            if (__float_as_uint(p[i]) == key && ++b == m) {
+                tokens[t] = i;
+                break;
+            }
+    }
+}
+
 }  // namespace
 
+size_t moe_sample_ws_bytes(int rows) {
+    return (size_t)rows * (2 * SG_CTAS * sizeof(float) + 256 * (sizeof(unsigned int) + sizeof(unsigned long long)) +
+                           SG_CTAS * sizeof(unsigned int) + sizeof(SmpRow)) + 64;
+}
+
 void moe_launch_sample(const float *logits, int T, int V, float temp, float top_p, uint32_t rng, float *p,
-                       int *tokens, cudaStream_t s, uint64_t *launches) {
+                       void *ws, int *tokens, cudaStream_t s, uint64_t *launches) {
     if (T <= 0) return;
-    k_sample<<<T, SP_THREADS, 0, s>>>(logits, V, temp, top_p, rng, p, tokens);
-    LAUNCH_COUNT(launches);
+    if (!(temp > 0.0f) || V < 4 * SG_CTAS) {   // argmax, or a small vocabulary: one CTA per row
+        k_sample<<<T, SP_THREADS, 0, s>>>(logits, V, temp, top_p, rng, p, tokens);
+        LAUNCH_COUNT(launches);
+        return;
+    }
+    // carve the workspace: 8-byte arrays first
+    uint8_t *b = reinterpret_cast<uint8_t *>(ws);
+    SmpWs w;
+    w.hsum = reinterpret_cast<unsigned long long *>(b);
+    b += (size_t)T * 256 * sizeof(unsigned long long);
+    w.row = reinterpret_cast<SmpRow *>(b);
+    b += (size_t)T * sizeof(SmpRow);
+    w.part_max = reinterpret_cast<float *>(b);
+    b += (size_t)T * SG_CTAS * sizeof(float);
+    w.part_sum = reinterpret_cast<float *>(b);
+    b += (size_t)T * SG_CTAS * sizeof(float);
+    w.hcnt = reinterpret_cast<unsigned int *>(b);
+    b += (size_t)T * 256 * sizeof(unsigned int);
+    w.cnt = reinterpret_cast<unsigned int *>(b);
+    const float inv_t = 1.0f / temp;
+    const dim3 grid(SG_CTAS, T);
+    k_sg_max<<<grid, SG_THREADS, 0, s>>>(logits, V, inv_t, w, tokens);
+    k_sg_exp<<<grid, SG_THREADS, 0, s>>>(logits, V, inv_t, w, p);
+    int n = 2;
+    for (int sel = 1; sel <= 2; sel++)
+        for (int shift = 24; shift >= 0; shift -= 8) {
+            k_sg_hist<<<grid, SG_THREADS, 0, s>>>(V, w, p, shift, sel, sel == 1 && shift == 24);
+            k_sg_pick<<<T, 256, 0, s>>>(w, shift, sel, top_p, rng);
+            n += 2;
+        }
+    k_sg_count<<<grid, SG_THREADS, 0, s>>>(V, w, p);
+    k_sg_final<<<grid, SG_THREADS, 0, s>>>(V, w, p, tokens);
+    n += 2;
+    if (launches) *launches += n;
 }

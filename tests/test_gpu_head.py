@@ -89,7 +89,7 @@ def _exact_rows(lg, temp, top_p, state):
 @pytest.mark.parametrize("V,scale,temp,top_p,peaked", [(129280, 2.0, 0.6, 0.95, False),
                                                        (129280, 0.3, 1.0, 0.95, False),
                                                        (1000, 3.0, 0.6, 0.95, True), (1000, 1.0, 1.5, 0.5, True),
-                                                       (4096, 2.0, 0.8, 1.0, True)])
+                                                       (4096, 2.0, 0.8, 1.0, True), (300, 2.0, 0.7, 0.9, True)])
 def test_sample_matches_oracle(cuda_lib, oracle, V, scale, temp, top_p, peaked):
     """16 rows per call, 4 calls with the state carried over.  The kernel adds
     probabilities exactly where the reference adds them in fp32, left to right
