@@ -259,9 +259,10 @@ __global__ void __launch_bounds__(SP_THREADS, 1) k_sample(const float *__restric
 
 // ---------------------------------------------------------------------------
 // Many-CTA form of the same selection (temp > 0): SG_CTAS CTAs per row, each
-// over one slice of the vocabulary, one small kernel per pass; the per-row
-// state between passes lives in global memory (SmpRow), the histograms in
-// global memory with integer atomics (order-independent sums).
+// over one slice of the vocabulary, one small kernel per histogram pass; each
+// pass resolves the previous pass's digit itself (every CTA the same way) and
+// CTA 0 records the state for the next launch; the histograms live in global
+// memory, one per pass, with integer atomics (order-independent sums).
 constexpr int SG_CTAS = 128;
 constexpr int SG_THREADS = 256;
 
@@ -271,12 +272,15 @@ struct SmpRow {
     unsigned long long above, above1, t2;
 };
 
+constexpr int SG_PASSES = 8;     // four digits per selection, two selections
+
 struct SmpWs {
     float *part_max, *part_sum;     // [T][SG_CTAS]
-    unsigned int *hcnt;             // [T][256]
-    unsigned long long *hsum;       // [T][256]
+    unsigned int *hcnt;             // [SG_PASSES][T][256]
+    unsigned long long *hsum;       // [SG_PASSES][T][256]
     unsigned int *cnt;              // [T][SG_CTAS]
-    SmpRow *row;                    // [T]
+    SmpRow *row;                    // [SG_PASSES + 1][T]: the state after 0..8 digits
+    int T;
 };
 
 __device__ __forceinline__ void slice_of(int V, int &s0, int &s1) {
@@ -322,13 +326,14 @@ __global__ void __launch_bounds__(SG_THREADS) k_sg_max(const float *__restrict__
     mx = sg_max(mx, red);
     if (threadIdx.x == 0) w.part_max[t * SG_CTAS + blockIdx.x] = mx;
     if (blockIdx.x == 0) {
-        for (int d = threadIdx.x; d < 256; d += SG_THREADS) {
-            w.hcnt[t * 256 + d] = 0;
-            w.hsum[t * 256 + d] = 0;
+        for (int k = threadIdx.x; k < SG_PASSES * 256; k += SG_THREADS) {
+            const size_t o = ((size_t)(k >> 8) * w.T + t) * 256 + (k & 255);
+            w.hcnt[o] = 0;
+            w.hsum[o] = 0;
         }
         if (threadIdx.x == 0) {
-            SmpRow r = {};
-            w.row[t] = r;
+            const SmpRow r = {};
+            for (int j = 0; j <= SG_PASSES; j++) w.row[(size_t)j * w.T + t] = r;
             tokens[t] = V - 1;   // replaced by k_sg_final
         }
     }
@@ -355,66 +360,16 @@ __global__ void __launch_bounds__(SG_THREADS) k_sg_exp(const float *__restrict__
     if (threadIdx.x == 0) w.part_sum[t * SG_CTAS + blockIdx.x] = part;
 }
 
-// a histogram pass of selection `sel` (1: all keys, 2: keys above tau, only
-// when the draw lies there); `norm` first scales the slice to probabilities
-__global__ void __launch_bounds__(SG_THREADS) k_sg_hist(int V, SmpWs w, float *__restrict__ pbuf, int shift, int sel,
-                                                       int norm) {
-    __shared__ unsigned int hc[256];
-    __shared__ unsigned long long hs[256];
-    const int t = blockIdx.y;
-    const SmpRow r = w.row[t];
-    if (sel == 2 && !r.sel2) return;
-    float *p = pbuf + (size_t)t * V;
-    for (int d = threadIdx.x; d < 256; d += SG_THREADS) {
-        hc[d] = 0;
-        hs[d] = 0;
-    }
-    float inv_s = 0.0f;
-    if (norm) {
-        float sum = 0.0f;
-        for (int g = 0; g < SG_CTAS; g++) sum += w.part_sum[t * SG_CTAS + g];
-        inv_s = 1.0f / sum;
-    }
-    __syncthreads();
-    int s0, s1;
-    slice_of(V, s0, s1);
-    for (int i = s0 + threadIdx.x; i < s1; i += SG_THREADS) {
-        float v = p[i];
-        if (norm) {
-            v = __fmul_rn(v, inv_s);
-            p[i] = v;
-        }
-        const uint32_t k = __float_as_uint(v);
-        if ((sel == 2 && k <= r.tau) || (k & r.msk) != r.pre) continue;
-        const int d = (k >> shift) & 255;
-        atomicAdd(&hc[d], 1u);
-        atomicAdd(&hs[d], fx(v));
-    }
-    __syncthreads();
-    for (int d = threadIdx.x; d < 256; d += SG_THREADS)
-        if (hc[d]) {
-            atomicAdd(&w.hcnt[t * 256 + d], hc[d]);
-            atomicAdd(&w.hsum[t * 256 + d], hs[d]);
-        }
-}
-
-// resolves one digit of selection `sel` from the row's histogram (and clears
-// it); after the last digit of selection 1 it forms the nucleus, the draw and
-// which selection finds the token; after the last of selection 2, the token's key
-__global__ void __launch_bounds__(256) k_sg_pick(SmpWs w, int shift, int sel, float top_p, uint32_t rng) {
-    __shared__ unsigned int hc[256];
-    __shared__ unsigned long long hs[256];
-    const int t = blockIdx.x;
-    if (sel == 2 && !w.row[t].sel2) return;   // CTA-uniform
-    for (int d = threadIdx.x; d < 256; d += blockDim.x) {
-        hc[d] = w.hcnt[t * 256 + d];
-        hs[d] = w.hsum[t * 256 + d];
-        w.hcnt[t * 256 + d] = 0;
-        w.hsum[t * 256 + d] = 0;
-    }
-    __syncthreads();
-    if (threadIdx.x) return;
-    SmpRow r = w.row[t];
+// The digit of pass `pass` (0..7: selection pass / 4 + 1, shift 24 - 8 (pass
+// % 4)) resolved from its histogram, on top of the state after the earlier
+// digits.  After the last digit of selection 1 it forms the nucleus, the draw
+// and which selection finds the token; after the last of selection 2, the
+// token's key.  Every CTA that needs it computes it (the same data, the same
+// result); one thread of the caller runs it on the histogram in shared memory.
+__device__ SmpRow sg_resolve(SmpRow r, int pass, const unsigned int *hc, const unsigned long long *hs, float top_p,
+                             uint32_t rng, int t) {
+    const int sel = pass / 4 + 1, shift = 24 - 8 * (pass % 4);
+    if (sel == 2 && !r.sel2) return r;
     const unsigned long long target = sel == 1 ? (unsigned long long)((double)top_p * 1099511627776.0) : r.t2;
     unsigned long long acc = r.above;
     int pick = -1, lowest = -1;
@@ -461,14 +416,92 @@ __global__ void __launch_bounds__(256) k_sg_pick(SmpWs w, int shift, int sel, fl
         r.key = r.pre;
         r.m = need_count(r.t2, r.above, __uint_as_float(r.pre), r.last_cnt);
     }
-    w.row[t] = r;
+    return r;
 }
 
-// per-slice count of the token's key
-__global__ void __launch_bounds__(SG_THREADS) k_sg_count(int V, SmpWs w, const float *__restrict__ pbuf) {
+// The state after `npass` digits, in shared memory for the whole CTA: the
+// state after npass - 1 (written by CTA 0 of the previous launch) and the
+// digit of pass npass - 1 from its finished histogram.  CTA 0 stores it for
+// the next launch.
+__device__ void sg_state(const SmpWs &w, int npass, float top_p, uint32_t rng, SmpRow &st, unsigned int *hc,
+                         unsigned long long *hs) {
+    const int t = blockIdx.y;
+    if (npass == 0) {
+        if (threadIdx.x == 0) st = w.row[t];
+        __syncthreads();
+        return;
+    }
+    const size_t hb = ((size_t)(npass - 1) * w.T + t) * 256;
+    for (int d = threadIdx.x; d < 256; d += blockDim.x) {
+        hc[d] = w.hcnt[hb + d];
+        hs[d] = w.hsum[hb + d];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        st = sg_resolve(w.row[(size_t)(npass - 1) * w.T + t], npass - 1, hc, hs, top_p, rng, t);
+        if (blockIdx.x == 0) w.row[(size_t)npass * w.T + t] = st;
+    }
+    __syncthreads();
+}
+
+// histogram pass `pass` (0..7) over this CTA's slice; pass 0 first scales the
+// slice to probabilities; the passes of selection 2 run only when the draw
+// lies above tau
+__global__ void __launch_bounds__(SG_THREADS) k_sg_hist(int V, SmpWs w, float *__restrict__ pbuf, int pass,
+                                                       float top_p, uint32_t rng) {
+    __shared__ unsigned int hc[256];
+    __shared__ unsigned long long hs[256];
+    __shared__ SmpRow st;
+    const int t = blockIdx.y;
+    sg_state(w, pass, top_p, rng, st, hc, hs);
+    const SmpRow r = st;
+    const int sel = pass / 4 + 1, shift = 24 - 8 * (pass % 4);
+    if (sel == 2 && !r.sel2) return;   // CTA-uniform
+    float *p = pbuf + (size_t)t * V;
+    for (int d = threadIdx.x; d < 256; d += SG_THREADS) {
+        hc[d] = 0;
+        hs[d] = 0;
+    }
+    float inv_s = 0.0f;
+    if (pass == 0) {
+        float sum = 0.0f;
+        for (int g = 0; g < SG_CTAS; g++) sum += w.part_sum[t * SG_CTAS + g];
+        inv_s = 1.0f / sum;
+    }
+    __syncthreads();
+    int s0, s1;
+    slice_of(V, s0, s1);
+    for (int i = s0 + threadIdx.x; i < s1; i += SG_THREADS) {
+        float v = p[i];
+        if (pass == 0) {
+            v = __fmul_rn(v, inv_s);
+            p[i] = v;
+        }
+        const uint32_t k = __float_as_uint(v);
+        if ((sel == 2 && k <= r.tau) || (k & r.msk) != r.pre) continue;
+        const int d = (k >> shift) & 255;
+        atomicAdd(&hc[d], 1u);
+        atomicAdd(&hs[d], fx(v));
+    }
+    __syncthreads();
+    const size_t hb = ((size_t)pass * w.T + t) * 256;
+    for (int d = threadIdx.x; d < 256; d += SG_THREADS)
+        if (hc[d]) {
+            atomicAdd(&w.hcnt[hb + d], hc[d]);
+            atomicAdd(&w.hsum[hb + d], hs[d]);
+        }
+}
+
+// the last digit resolved, then the per-slice count of the token's key
+__global__ void __launch_bounds__(SG_THREADS) k_sg_count(int V, SmpWs w, const float *__restrict__ pbuf, float top_p,
+                                                        uint32_t rng) {
+    __shared__ unsigned int hc[256];
+    __shared__ unsigned long long hs[256];
+    __shared__ SmpRow st;
     __shared__ float red[SG_THREADS / 32];
     const int t = blockIdx.y;
-    const uint32_t key = w.row[t].key;
+    sg_state(w, SG_PASSES, top_p, rng, st, hc, hs);
+    const uint32_t key = st.key;
     const float *p = pbuf + (size_t)t * V;
     int s0, s1;
     slice_of(V, s0, s1);
@@ -483,8 +516,9 @@ __global__ void __launch_bounds__(SG_THREADS) k_sg_final(int V, SmpWs w, const f
                                                         int *__restrict__ tokens) {
     __shared__ unsigned int wsum[SG_THREADS / 32];
     const int t = blockIdx.y;
-    const uint32_t key = w.row[t].key;
-    const unsigned int m = w.row[t].m;
+    const SmpRow &r = w.row[(size_t)SG_PASSES * w.T + t];
+    const uint32_t key = r.key;
+    const unsigned int m = r.m;
     unsigned int before = 0;
     for (int g = 0; g < (int)blockIdx.x; g++) before += w.cnt[t * SG_CTAS + g];
     const unsigned int mine = w.cnt[t * SG_CTAS + blockIdx.x];
@@ -519,8 +553,9 @@ __global__ void __launch_bounds__(SG_THREADS) k_sg_final(int V, SmpWs w, const f
 }  // namespace
 
 size_t moe_sample_ws_bytes(int rows) {
-    return (size_t)rows * (2 * SG_CTAS * sizeof(float) + 256 * (sizeof(unsigned int) + sizeof(unsigned long long)) +
-                           SG_CTAS * sizeof(unsigned int) + sizeof(SmpRow)) + 64;
+    return (size_t)rows * (2 * SG_CTAS * sizeof(float) +
+                           SG_PASSES * 256 * (sizeof(unsigned int) + sizeof(unsigned long long)) +
+                           SG_CTAS * sizeof(unsigned int) + (SG_PASSES + 1) * sizeof(SmpRow)) + 64;
 }
 
 void moe_launch_sample(const float *logits, int T, int V, float temp, float top_p, uint32_t rng, float *p,
@@ -534,30 +569,25 @@ void moe_launch_sample(const float *logits, int T, int V, float temp, float top_
     // carve the workspace: 8-byte arrays first
     uint8_t *b = reinterpret_cast<uint8_t *>(ws);
     SmpWs w;
+    w.T = T;
     w.hsum = reinterpret_cast<unsigned long long *>(b);
-    b += (size_t)T * 256 * sizeof(unsigned long long);
+    b += (size_t)SG_PASSES * T * 256 * sizeof(unsigned long long);
     w.row = reinterpret_cast<SmpRow *>(b);
-    b += (size_t)T * sizeof(SmpRow);
+    b += (size_t)(SG_PASSES + 1) * T * sizeof(SmpRow);
     w.part_max = reinterpret_cast<float *>(b);
     b += (size_t)T * SG_CTAS * sizeof(float);
     w.part_sum = reinterpret_cast<float *>(b);
     b += (size_t)T * SG_CTAS * sizeof(float);
     w.hcnt = reinterpret_cast<unsigned int *>(b);
-    b += (size_t)T * 256 * sizeof(unsigned int);
+    b += (size_t)SG_PASSES * T * 256 * sizeof(unsigned int);
     w.cnt = reinterpret_cast<unsigned int *>(b);
     const float inv_t = 1.0f / temp;
     const dim3 grid(SG_CTAS, T);
     k_sg_max<<<grid, SG_THREADS, 0, s>>>(logits, V, inv_t, w, tokens);
     k_sg_exp<<<grid, SG_THREADS, 0, s>>>(logits, V, inv_t, w, p);
-    int n = 2;
-    for (int sel = 1; sel <= 2; sel++)
-        for (int shift = 24; shift >= 0; shift -= 8) {
-            k_sg_hist<<<grid, SG_THREADS, 0, s>>>(V, w, p, shift, sel, sel == 1 && shift == 24);
-            k_sg_pick<<<T, 256, 0, s>>>(w, shift, sel, top_p, rng);
-            n += 2;
-        }
-    k_sg_count<<<grid, SG_THREADS, 0, s>>>(V, w, p);
+    for (int pass = 0; pass < SG_PASSES; pass++) k_sg_hist<<<grid, SG_THREADS, 0, s>>>(V, w, p, pass, top_p, rng);
+    k_sg_count<<<grid, SG_THREADS, 0, s>>>(V, w, p, top_p, rng);
     k_sg_final<<<grid, SG_THREADS, 0, s>>>(V, w, p, tokens);
-    n += 2;
+    const int n = 4 + SG_PASSES;
     if (launches) *launches += n;
 }
