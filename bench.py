@@ -12,7 +12,8 @@ Weights are random-init N(0, 0.02) quantized to Q4_K gate/up and Q6_K down on
 the device; inputs N(0, 1) from a fixed seed.  Between timed steps a 256 MiB
 buffer is written to flush the 126 MB L2.  On one GPU the default run then
 measures the other configs too (one expert per call, one token, the 4096-token
-prefill, the 58-layer stack at batch 1) and reports them under "configs";
+prefill, the 58-layer stack at batch 1, the dense FFN layers 0-2 and the output
+head with the top-p sampler at one token) and reports them under "configs";
 --no-extra skips them.
 
 --impl reference times the reference's own CPU path (quant.c dequant + fp32
