@@ -711,3 +711,148 @@ int or_sample_top_p(const float *logits, int n, float temp, float top_p, uint32_
     free(buf);
     return tok;
 }
+
+/* ------------------------------------------------------------------------ */
+/* MLA attention of one decode token (infer.m:545-903)                       */
+/* ------------------------------------------------------------------------ */
+/* YaRN band (yarn_init_once, infer.m:591-610): the frequency indices between
+ * which the rotary frequencies ramp from extrapolated to interpolated. */
+void or_yarn_band(const or_mla_cfg *c, int *lo_out, int *hi_out) {
+    const int dim = c->qk_rope;
+    const float twopi = 2.0f * (float)M_PI;
+    float lo_f = ((float)dim * logf(c->rope_orig_ctx / (32.0f * twopi))) / (2.0f * logf(c->rope_theta));
+    float hi_f = ((float)dim * logf(c->rope_orig_ctx / (1.0f * twopi))) / (2.0f * logf(c->rope_theta));
+    int lo = (int)floorf(lo_f), hi = (int)ceilf(hi_f);
+    if (lo < 0) lo = 0;
+    if (hi > dim / 2 - 1) hi = dim / 2 - 1;
+    if (hi <= lo) hi = lo + 1;
+    *lo_out = lo;
+    *hi_out = hi;
+}
+
+/* yarn_freq (infer.m:612-624): blend of base^(-2i/dim) and the same / scale */
+float or_yarn_freq(const or_mla_cfg *c, int i) {
+    int lo, hi;
+    or_yarn_band(c, &lo, &hi);
+    const int dim = c->qk_rope;
+    float freq_extra = 1.0f / powf(c->rope_theta, (float)(2 * i) / (float)dim);
+    float freq_inter = freq_extra / c->rope_scale;
+    float denom = (float)(hi - lo);
+    if (denom < 1e-3f) denom = 1e-3f;
+    float ramp = ((float)i - (float)lo) / denom;
+    if (ramp < 0.0f) ramp = 0.0f;
+    if (ramp > 1.0f) ramp = 1.0f;
+    float mask = 1.0f - ramp;
+    return freq_inter * (1.0f - mask) + freq_extra * mask;
+}
+
+/* apply_rope_q / apply_rope_k (infer.m:628-656): interleaved pairs
+ * (x[2i], x[2i+1]) of each head rotated by pos * freq(i) */
+void or_rope(const or_mla_cfg *c, float *x, int n_heads, int pos) {
+    const int half = c->qk_rope / 2;
+    for (int h = 0; h < n_heads; h++) {
+        float *xh = x + (size_t)h * c->qk_rope;
+        for (int i = 0; i < half; i++) {
+            float ang = (float)pos * or_yarn_freq(c, i);
+            float cs = cosf(ang), sn = sinf(ang);
+            float a = xh[2 * i], b = xh[2 * i + 1];
+            xh[2 * i] = a * cs - b * sn;
+            xh[2 * i + 1] = a * sn + b * cs;
+        }
+    }
+}
+
+/* softmax (infer.m:384-388) */
+void or_softmax(float *x, int n) {
+    float m = x[0];
+    for (int i = 1; i < n; i++) if (x[i] > m) m = x[i];
+    float s = 0;
+    for (int i = 0; i < n; i++) { x[i] = expf(x[i] - m); s += x[i]; }
+    float inv = 1.0f / s;
+    for (int i = 0; i < n; i++) x[i] *= inv;
+}
+
+static float dot_h(const uint16_t *a, const float *x, int n, int dbl) {
+    if (dbl) {
+        double s = 0.0;
+        for (int k = 0; k < n; k++) s += (double)or_fp16_to_fp32(a[k]) * (double)x[k];
+        return (float)s;
+    }
+    float s = 0.0f;
+    for (int k = 0; k < n; k++) s += or_fp16_to_fp32(a[k]) * x[k];
+    return s;
+}
+
+static float dot_f(const float *a, const float *x, int n, int dbl) {
+    if (dbl) {
+        double s = 0.0;
+        for (int k = 0; k < n; k++) s += (double)a[k] * (double)x[k];
+        return (float)s;
+    }
+    float s = 0.0f;
+    for (int k = 0; k < n; k++) s += a[k] * x[k];
+    return s;
+}
+
+/* mla_forward (infer.m:766-903) for the token at position pos: RMSNorm,
+ * q_a -> RMSNorm -> q_b (per head [nope | rope]), kv_a -> RMSNorm on the
+ * latent part, RoPE on q_rope and k_rope, append (c_kv, k_rope) to the cache
+ * at *len, absorbed attention (Q_abs = k_b q_nope; scores = scale (Q_abs .
+ * c_kv + q_rope . k_rope), scale = (0.1 ln(rope_scale) + 1)^2 / sqrt(qk_nope +
+ * qk_rope); softmax; wc = sum_s p_s c_kv[s]; out_h = v_b wc), o_proj, and
+ * hidden += o. */
+void or_mla_decode(const or_mla_cfg *c, const or_mla_weights *w, float *hidden, float *c_kv, float *k_rope_cache,
+                   int *len, int pos, int acc_double) {
+    const int H = c->H, NH = c->n_heads, QL = c->q_lora, KL = c->kv_lora, NP = c->qk_nope, RP = c->qk_rope,
+              VH = c->v_head, QK = NP + RP, dbl = acc_double;
+    float *normed = (float *)malloc(sizeof(float) * (size_t)H);
+    float *qa = (float *)malloc(sizeof(float) * (size_t)QL), *qan = (float *)malloc(sizeof(float) * (size_t)QL);
+    float *qf = (float *)malloc(sizeof(float) * (size_t)NH * QK);
+    float *qn = (float *)malloc(sizeof(float) * (size_t)NH * NP), *qr = (float *)malloc(sizeof(float) * (size_t)NH * RP);
+    float *kva = (float *)malloc(sizeof(float) * (size_t)(KL + RP));
+    or_rms_norm(hidden, w->attn_norm, normed, H, c->eps);
+    for (int r = 0; r < QL; r++) qa[r] = dot_h(w->q_a + (size_t)r * H, normed, H, dbl);
+    or_rms_norm(qa, w->q_a_norm, qan, QL, c->eps);
+    for (int r = 0; r < NH * QK; r++) qf[r] = dot_h(w->q_b + (size_t)r * QL, qan, QL, dbl);
+    for (int h = 0; h < NH; h++) {
+        memcpy(qn + (size_t)h * NP, qf + (size_t)h * QK, sizeof(float) * (size_t)NP);
+        memcpy(qr + (size_t)h * RP, qf + (size_t)h * QK + NP, sizeof(float) * (size_t)RP);
+    }
+    for (int r = 0; r < KL + RP; r++) kva[r] = dot_h(w->kv_a + (size_t)r * H, normed, H, dbl);
+    const int S = *len + 1;
+    float *ckv_new = c_kv + (size_t)(*len) * KL, *kr_new = k_rope_cache + (size_t)(*len) * RP;
+    or_rms_norm(kva, w->kv_a_norm, ckv_new, KL, c->eps);
+    memcpy(kr_new, kva + KL, sizeof(float) * (size_t)RP);
+    or_rope(c, qr, NH, pos);
+    or_rope(c, kr_new, 1, pos);
+    *len = S;
+    const float ms = 0.1f * logf(c->rope_scale) + 1.0f;
+    const float scale = (ms * ms) / sqrtf((float)QK);
+    float *qabs = (float *)malloc(sizeof(float) * (size_t)KL), *sc = (float *)malloc(sizeof(float) * (size_t)S);
+    float *wc = (float *)malloc(sizeof(float) * (size_t)KL), *att = (float *)malloc(sizeof(float) * (size_t)NH * VH);
+    for (int h = 0; h < NH; h++) {
+        const uint16_t *kb = w->k_b + (size_t)h * KL * NP, *vb = w->v_b + (size_t)h * VH * KL;
+        for (int j = 0; j < KL; j++) qabs[j] = dot_h(kb + (size_t)j * NP, qn + (size_t)h * NP, NP, dbl);
+        for (int s = 0; s < S; s++) {
+            const float a = dot_f(qabs, c_kv + (size_t)s * KL, KL, dbl);
+            const float b = dot_f(qr + (size_t)h * RP, k_rope_cache + (size_t)s * RP, RP, dbl);
+            sc[s] = scale * a + scale * b;
+        }
+        or_softmax(sc, S);
+        for (int j = 0; j < KL; j++) {
+            if (dbl) {
+                double a = 0.0;
+                for (int s = 0; s < S; s++) a += (double)sc[s] * (double)c_kv[(size_t)s * KL + j];
+                wc[j] = (float)a;
+            } else {
+                float a = 0.0f;
+                for (int s = 0; s < S; s++) a += sc[s] * c_kv[(size_t)s * KL + j];
+                wc[j] = a;
+            }
+        }
+        for (int v = 0; v < VH; v++) att[(size_t)h * VH + v] = dot_h(vb + (size_t)v * KL, wc, KL, dbl);
+    }
+    for (int r = 0; r < H; r++) hidden[r] += dot_h(w->o_proj + (size_t)r * NH * VH, att, NH * VH, dbl);
+    free(normed); free(qa); free(qan); free(qf); free(qn); free(qr); free(kva);
+    free(qabs); free(sc); free(wc); free(att);
+}

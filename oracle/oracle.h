@@ -14,6 +14,10 @@
  *   - The expert / layer composition (dequant + dot in place of Accelerate's
  *     cblas_sgemv, which does not exist on Linux) is a restatement of
  *     infer.m:1069-1114 and 1915-1922 built from the pinned pieces.
+ *   - dense FFN fp16 rounding, sample_top_p / argmax, softmax and the YaRN
+ *     RoPE: against the reference's own functions built in place (the MLA
+ *     decode step itself, which calls Metal and Accelerate, is restated from
+ *     infer.m:766-903 on those pinned pieces).
  *   - The quantizer and the counter-based RNG have no counterpart in the
  *     reference (it ships neither); they define the synthetic inputs.
  */
@@ -128,6 +132,28 @@ int   or_argmax(const float *x, int n);
 float or_rand_unit(uint32_t *state);
 int   or_sample_top_p(const float *logits, int n, float temp, float top_p,
                       uint32_t *state, float *cum_out, float *r_out);
+
+/* ---- MLA attention, one decode token (infer.m:545-903) ---- */
+typedef struct {
+    int H, n_heads, q_lora, kv_lora, qk_nope, qk_rope, v_head;
+    float rope_theta, rope_scale, rope_orig_ctx, eps;
+} or_mla_cfg;
+/* fp16 bits: q_a [q_lora x H], q_b [n_heads * (qk_nope + qk_rope) x q_lora],
+ * kv_a [(kv_lora + qk_rope) x H], k_b [n_heads][kv_lora x qk_nope],
+ * v_b [n_heads][v_head x kv_lora], o_proj [H x n_heads * v_head];
+ * fp32 norms attn_norm [H], q_a_norm [q_lora], kv_a_norm [kv_lora] */
+typedef struct {
+    const uint16_t *q_a, *q_b, *kv_a, *k_b, *v_b, *o_proj;
+    const float *attn_norm, *q_a_norm, *kv_a_norm;
+} or_mla_weights;
+void  or_yarn_band(const or_mla_cfg *c, int *lo, int *hi);
+float or_yarn_freq(const or_mla_cfg *c, int i);
+void  or_rope(const or_mla_cfg *c, float *x, int n_heads, int pos);
+void  or_softmax(float *x, int n);
+/* hidden [H] += attention output; the cache (c_kv [. x kv_lora], k_rope
+ * [. x qk_rope]) gains row *len, which then grows by one */
+void  or_mla_decode(const or_mla_cfg *c, const or_mla_weights *w, float *hidden,
+                    float *c_kv, float *k_rope, int *len, int pos, int acc_double);
 
 #ifdef __cplusplus
 }

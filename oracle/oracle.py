@@ -43,6 +43,21 @@ class LayerCfg(C.Structure):
                 ("down_type", C.c_int)]
 
 
+class MlaCfg(C.Structure):
+    _fields_ = [("H", C.c_int), ("n_heads", C.c_int), ("q_lora", C.c_int), ("kv_lora", C.c_int),
+                ("qk_nope", C.c_int), ("qk_rope", C.c_int), ("v_head", C.c_int), ("rope_theta", C.c_float),
+                ("rope_scale", C.c_float), ("rope_orig_ctx", C.c_float), ("eps", C.c_float)]
+
+
+class MlaWeights(C.Structure):
+    _fields_ = [(k, C.c_void_p) for k in ("q_a", "q_b", "kv_a", "k_b", "v_b", "o_proj", "attn_norm", "q_a_norm",
+                                          "kv_a_norm")]
+
+
+# DeepSeek-V3 / R1 attention shapes (infer.m:44-65)
+MLA_DEEPSEEK = dict(H=7168, n_heads=128, q_lora=1536, kv_lora=512, qk_nope=128, qk_rope=64, v_head=128,
+                    rope_theta=10000.0, rope_scale=40.0, rope_orig_ctx=4096.0, eps=1e-6)
+
 _lib = None
 _ref = None
 
@@ -99,6 +114,13 @@ def lib():
         L.or_sample_top_p.restype = C.c_int
         L.or_sample_top_p.argtypes = [_f32p, C.c_int, C.c_float, C.c_float, C.POINTER(C.c_uint32),
                                       C.POINTER(C.c_float), C.POINTER(C.c_float)]
+        L.or_yarn_band.argtypes = [C.POINTER(MlaCfg), C.POINTER(C.c_int), C.POINTER(C.c_int)]
+        L.or_yarn_freq.restype = C.c_float
+        L.or_yarn_freq.argtypes = [C.POINTER(MlaCfg), C.c_int]
+        L.or_rope.argtypes = [C.POINTER(MlaCfg), _f32p, C.c_int, C.c_int]
+        L.or_softmax.argtypes = [_f32p, C.c_int]
+        L.or_mla_decode.argtypes = [C.POINTER(MlaCfg), C.POINTER(MlaWeights), _f32p, _f32p, _f32p,
+                                    C.POINTER(C.c_int), C.c_int, C.c_int]
         _lib = L
     return _lib
 
@@ -129,6 +151,12 @@ def ref():
         R.ref_argmax.argtypes = [_f32p, C.c_int]
         R.ref_sample_top_p.restype = C.c_int
         R.ref_sample_top_p.argtypes = [_f32p, C.c_int, C.c_float, C.c_float, C.POINTER(C.c_uint32)]
+        R.ref_softmax.argtypes = [_f32p, C.c_int]
+        R.ref_yarn_freq.restype = C.c_float
+        R.ref_yarn_freq.argtypes = [C.c_int]
+        R.ref_yarn_band.argtypes = [C.POINTER(C.c_int), C.POINTER(C.c_int)]
+        R.ref_rope_q.argtypes = [_f32p, C.c_int, C.c_int]
+        R.ref_rope_k.argtypes = [_f32p, C.c_int]
         _ref = R
     return _ref
 
@@ -289,6 +317,35 @@ def sample_top_p(logits, temp: float, top_p: float, state: int):
     lg = np.ascontiguousarray(logits, np.float32)
     tok = lib().or_sample_top_p(lg, lg.size, temp, top_p, C.byref(st), C.byref(cum), C.byref(r))
     return tok, st.value, cum.value, r.value
+
+
+def mla_cfg(**kw) -> MlaCfg:
+    d = dict(MLA_DEEPSEEK)
+    d.update(kw)
+    return MlaCfg(**d)
+
+
+class MlaCache:
+    """The per-layer latent cache of mla_forward (MLACache, infer.m:665-675)."""
+
+    def __init__(self, cfg: MlaCfg, max_seq: int):
+        self.c_kv = np.zeros((max_seq, cfg.kv_lora), np.float32)
+        self.k_rope = np.zeros((max_seq, cfg.qk_rope), np.float32)
+        self.len = 0
+
+
+def mla_decode(cfg: MlaCfg, w: dict, hidden, cache: MlaCache, pos: int, acc_double=True):
+    """hidden + attention of one token (infer.m:766-903); w holds fp16-bit
+    matrices q_a, q_b, kv_a, k_b, v_b, o_proj and fp32 norms attn_norm,
+    q_a_norm, kv_a_norm; the cache gains one row."""
+    arrs = {k: np.ascontiguousarray(w[k], np.uint16) for k in ("q_a", "q_b", "kv_a", "k_b", "v_b", "o_proj")}
+    arrs.update({k: np.ascontiguousarray(w[k], np.float32) for k in ("attn_norm", "q_a_norm", "kv_a_norm")})
+    ws = MlaWeights(**{k: a.ctypes.data for k, a in arrs.items()})
+    h = np.array(hidden, np.float32, copy=True).reshape(-1)
+    n = C.c_int(cache.len)
+    lib().or_mla_decode(C.byref(cfg), C.byref(ws), h, cache.c_kv, cache.k_rope, C.byref(n), pos, int(acc_double))
+    cache.len = n.value
+    return h
 
 
 def moe_layer(cfg: dict, experts: dict, router_w, bias, x, force_idx=None, force_w=None,

@@ -4,8 +4,9 @@
  *
  * oracle/Makefile compiles this file together with the reference's quant.c
  * (unmodified, from where it lies) and with rms_norm / sigmoidf / silu_mul /
- * route / argmax / rand_unit / sample_top_p extracted verbatim from the
- * reference's infer.m into a temporary file (REF_SNIPPET).  Nothing of the reference is written into this repository;
+ * route / argmax / rand_unit / sample_top_p / softmax and the YaRN RoPE
+ * functions extracted verbatim from the reference's infer.m into a temporary
+ * file (REF_SNIPPET).  Nothing of the reference is written into this repository;
  * the only output is oracle/_ref/libref_moe.so.
  *
  * infer.m itself cannot be compiled on Linux (Objective-C, Metal, Accelerate),
@@ -14,6 +15,7 @@
  * dot and cblas_saxpy (infer.m:1915-1917) a plain fp32 loop.
  */
 #include <math.h>
+#include <stdio.h>
 #include <pthread.h>
 #include <stdint.h>
 #include <stdlib.h>
@@ -29,6 +31,10 @@
 #define ROUTED_SCALE 2.5f
 #define RMS_NORM_EPS 1e-6f
 #define MAX_K 16
+#define QK_ROPE_HEAD_DIM 64
+#define ROPE_THETA 10000.0f
+#define ROPE_SCALE 40.0f
+#define ROPE_ORIG_CTX 4096.0f
 
 #include REF_SNIPPET
 
@@ -41,6 +47,12 @@ void ref_route(const float *logits, const float *bias, int K, int *exp_idx, floa
 /* argmax / rand_unit / sample_top_p (infer.m:390-456), the generator state
  * handed in and out */
 int ref_argmax(const float *x, int n) { return argmax(x, n); }
+/* softmax / yarn_freq / apply_rope_q / apply_rope_k (infer.m:384-388, 586-656) */
+void ref_softmax(float *x, int n) { softmax(x, n); }
+float ref_yarn_freq(int i) { yarn_init_once(); return yarn_freq(i); }
+void ref_yarn_band(int *lo, int *hi) { yarn_init_once(); *lo = g_yarn_low; *hi = g_yarn_high; }
+void ref_rope_q(float *x, int n_heads, int pos) { apply_rope_q(x, n_heads, pos); }
+void ref_rope_k(float *x, int pos) { apply_rope_k(x, pos); }
 int ref_sample_top_p(const float *logits, int n, float temp, float top_p, uint32_t *state) {
     g_rng = *state;
     int t = sample_top_p(logits, n, temp, top_p);
