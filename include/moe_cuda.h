@@ -224,7 +224,10 @@ int moe_lm_head_device(moe_ctx *ctx, const float *d_h, int n_tokens, float *d_lo
  * *rng_state; the host entry advances *rng_state by n_tokens when temp > 0
  * (the reference's generator starts at 0xa1b2c3d4, infer.m:411).  The
  * cumulative sums are exact (fixed point, 2^-40) where the reference adds in
- * fp32, so a draw within fp32 rounding of a boundary may pick a neighbour. */
+ * fp32, so a draw within fp32 rounding of a boundary may pick a neighbour.
+ * Scratch for max_tokens rows of `vocab` values is allocated by
+ * moe_load_lm_head / moe_init_lm_head_synthetic, or by the first call with a
+ * larger vocabulary; make that call before any stream capture. */
 int moe_sample(moe_ctx *ctx, const float *logits, int n_tokens, int vocab, float temp, float top_p,
                uint32_t *rng_state, int *tokens);
 int moe_sample_device(moe_ctx *ctx, const float *d_logits, int n_tokens, int vocab, float temp,
